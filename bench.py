@@ -1,0 +1,388 @@
+"""Benchmark of the frame path: SPAN x2 1080p -> 2160p on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: frames shard across GPUs, no collective)
+
+A step is one batch of 8 synthetic 1080p frames through the engine (the contract's configs[1]:
+FP16, batch 8, 240 frames per GPU by default = 30 steps). `value` is whole-job frames/s with the
+inputs resident in HBM; `e2e` is the same through the public C ABI with pinned host frames, the
+host->device copy and the device->host read of every output inside the timed region. `roofline`
+times the dominant kernel with CUDA events on its launching stream during the timed steps.
+`--impl reference` times the reference's own FP32 CPU implementation (its IR interpreter, compiled
+from the reference sources into oracle/_ref) on the host cores, on bounded crops of the same frames.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "ultimate-anime-videoplayer_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+FRAME_H, FRAME_W = 1080, 1920
+FLOP_PER_PX = 777888.0  # canonical SPAN x2: 388,944 MACs per input pixel
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["span16", "span8"], default="span16")
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--height", type=int, default=FRAME_H)
+    ap.add_argument("--width", type=int, default=FRAME_W)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region (started before, stopped after)."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------------------------------------------
+# reference CPU implementation (the oracle/_ref build of the reference's own interpreter)
+# ------------------------------------------------------------------------------------------------
+CROP_H, CROP_W = 24, 48
+
+
+def reference_sample(threads, frame, flat, crops_per_thread=1):
+    """Each host thread runs the reference's FP32 SPAN on its own crop of the frame (the interpreter
+    is single-threaded per call); returns (frames processed, seconds)."""
+    from oracle import ref_lib
+    import numpy as np
+
+    H, W = frame.shape[1:]
+    rng = np.random.default_rng(0)
+    jobs = []
+    for t in range(threads):
+        for _ in range(crops_per_thread):
+            y = int(rng.integers(0, H - CROP_H))
+            x = int(rng.integers(0, W - CROP_W))
+            jobs.append((t, np.ascontiguousarray(frame[None, :, y:y + CROP_H, x:x + CROP_W])))
+    done = [0] * threads
+
+    def work(t):
+        for tt, crop in jobs:
+            if tt == t:
+                ref_lib.span_forward(crop, flat)
+                done[t] += 1
+
+    ts = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    t0 = time.perf_counter()
+    for th in ts:
+        th.start()
+    for th in ts:
+        th.join()
+    dt = time.perf_counter() - t0
+    return sum(done) * CROP_H * CROP_W / float(FRAME_H * FRAME_W), dt
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(frame, flat, budget_s=12.0):
+    from oracle import ref_lib
+    if not ref_lib.available():
+        return None
+    cores = host_cores()
+    frames, dt = reference_sample(cores, frame, flat)
+    reps = max(1, int(budget_s / max(dt, 1e-3)))
+    if reps > 1:
+        frames, dt = reference_sample(cores, frame, flat, crops_per_thread=reps)
+    return {"value": frames / dt, "unit": "frames/s", "cores": cores, "kind": "reference",
+            "sample": f"{cores} threads x {reps} crops of {CROP_H}x{CROP_W} px of a synthetic 1080p frame, "
+                      f"reference FP32 IR interpreter (oracle/_ref), scaled by pixels to 1920x1080 frames"}
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import nets, ref_lib
+    from synth import anime_frame
+
+    config = {"workload": "span_x2 1080p->2160p (configs[1] network), reference FP32 CPU path",
+              "height": args.height, "width": args.width, "batch": args.batch}
+    if not ref_lib.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
+        return
+    frame = anime_frame(args.height, args.width, 0).astype(np.float32)
+    flat = nets.span_flat(nets.span_init(1))
+    cores = host_cores()
+    for _ in range(args.warmup):
+        reference_sample(cores, frame, flat)
+    total_frames, total_s = 0.0, 0.0
+    for _ in range(args.steps):
+        f, dt = reference_sample(cores, frame, flat)
+        total_frames += f
+        total_s += dt
+    value = total_frames / total_s
+    line = {"metric": "SPAN x2 1080p->2160p frames/s", "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference", "config": config,
+            "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cores, "kind": "reference",
+                             "sample": f"per step: {cores} threads x 1 crop of {CROP_H}x{CROP_W} px, "
+                                       "scaled by pixels to 1920x1080 frames"},
+            "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------------------------------------------
+# this library
+# ------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import kirari_b200 as kb
+    from oracle import nets
+    from synth import anime_frames
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+
+    def barrier():
+        if world > 1:
+            t = torch.ones(1, device="cuda")
+            dist.all_reduce(t)
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B, H, W = args.batch, args.height, args.width
+    p = nets.span_init(1)
+    flat = nets.span_flat(p)
+    blob = kb.make_blob(kb.MODEL_SPAN_X2, flat)
+    frames = anime_frames(B, H, W, seed=10 + rank)
+    fp8 = args.workload == "span8"
+    scales = None
+    if fp8:
+        calib = torch.from_numpy(anime_frames(16, H, W, seed=1000).astype(np.float16)).cuda()
+        e16 = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B, device=local_rank)
+        peaks = e16.calibrate(calib)
+        e16.close()
+        del calib
+        scales = nets.span_scales_from_peaks(peaks, floor=2.0 ** -14)
+    eng = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B, precision=kb.PREC_FP8 if fp8 else kb.PREC_FP16,
+                    act_scales=scales, device=local_rank)
+    d_in = torch.from_numpy(frames.astype(np.float16)).cuda()
+    d_out = torch.empty((B, 3, 2 * H, 2 * W), dtype=torch.float16, device="cuda")
+    stream = torch.cuda.Stream()
+    sh = kb.ctypes.c_void_p(stream.cuda_stream)
+    ins = (kb.Tensor * 1)(kb.to_kb2_tensor(d_in))
+    outs = (kb.Tensor * 1)(kb.to_kb2_tensor(d_out))
+
+    # ---- device-resident timing
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            eng.enqueue_raw(ins, outs, sh)
+    stream.synchronize()
+    eng.check_device(stream)
+    eng.read_profile()
+    eng.set_profiling(True)
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        eng.enqueue_raw(ins, outs, sh)
+    stop.record(stream)
+    stop.synchronize()
+    barrier()
+    clk = clocks.stop()
+    eng.set_profiling(False)
+    eng.check_device(stream)
+    ms = max_over_ranks(start.elapsed_time(stop))
+    profile = eng.read_profile()
+    value = world * B * args.steps / (ms / 1e3)
+
+    # ---- roofline of the dominant kernel (measured inside the timed region)
+    peaks_json, peak_kind = measured_peaks()
+    top_name, top = max(profile.items(), key=lambda kv: kv[1]["total_ms"])
+    avg_ms = top["total_ms"] / max(1, top["launches"])
+    tflops = top["flops"] / (avg_ms / 1e3) / 1e12
+    peak = float(peaks_json["bf16_tflops_sustained"]) * (2.0 if top_name.endswith(".fp8") else 1.0)
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get(top_name, {}).get(f"{B}x{H}x{W}")
+    except (OSError, ValueError):
+        pass
+    roofline = {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
+                "traffic": traffic, "kernel": top_name, "launches": top["launches"],
+                "avg_launch_ms": avg_ms, "flops_per_launch": top["flops"],
+                "algorithmic_bytes_per_launch": top["bytes"],
+                "peak_source": f"{peak_kind} bf16_tflops_sustained" + (" x2 (E4M3)" if top_name.endswith(".fp8") else ""),
+                "network_tflops": FLOP_PER_PX * H * W * B * args.steps / (ms / 1e3) / 1e12}
+    layers = {k: {"launches": v["launches"], "ms_per_launch": v["total_ms"] / max(1, v["launches"]),
+                  "share": v["total_ms"] / max(1e-9, sum(x["total_ms"] for x in profile.values()))}
+              for k, v in profile.items()}
+
+    # ---- end to end through the C ABI with host frames (pinned), copies in the timed region
+    e2e = None
+    if not args.no_e2e:
+        h_in = torch.from_numpy(frames.astype(np.float16)).pin_memory()
+        h_out = [torch.empty((B, 3, 2 * H, 2 * W), dtype=torch.float16).pin_memory() for _ in range(2)]
+        d_ins = [torch.empty_like(d_in) for _ in range(2)]
+        d_outs = [d_out, torch.empty_like(d_out)]
+        s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        ins2 = [(kb.Tensor * 1)(kb.to_kb2_tensor(t)) for t in d_ins]
+        outs2 = [(kb.Tensor * 1)(kb.to_kb2_tensor(t)) for t in d_outs]
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_done = [torch.cuda.Event() for _ in range(2)]
+        ev_free = [torch.cuda.Event() for _ in range(2)]
+
+        def pipeline(n_steps):
+            for i in range(n_steps):
+                k = i % 2
+                with torch.cuda.stream(s_h2d):
+                    s_h2d.wait_event(ev_free[k]) if i >= 2 else None
+                    d_ins[k].copy_(h_in, non_blocking=True)
+                    ev_in[k].record(s_h2d)
+                stream.wait_event(ev_in[k])
+                if i >= 2:
+                    stream.wait_event(ev_free[k])
+                eng.enqueue_raw(ins2[k], outs2[k], sh)
+                ev_done[k].record(stream)
+                with torch.cuda.stream(s_d2h):
+                    s_d2h.wait_event(ev_done[k])
+                    h_out[k].copy_(d_outs[k], non_blocking=True)
+                    ev_free[k].record(s_d2h)
+            torch.cuda.synchronize()
+
+        pipeline(min(2, args.warmup))
+        barrier()
+        t0 = time.perf_counter()
+        pipeline(args.steps)
+        barrier()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        e2e = {"value": world * B * args.steps / e2e_s, "unit": "frames/s",
+               "h2d_bytes_per_step": int(h_in.numel() * 2), "d2h_bytes_per_step": int(h_out[0].numel() * 2),
+               "path": "kb2_enqueue with pinned host frames: H2D copy, enqueue, D2H of every output frame, "
+                       "double-buffered across three streams"}
+        eng.check_device(stream)
+
+    launches = args.steps * eng.launches_per_enqueue()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(frames[0], flat)
+    eng.close()
+    if rank == 0:
+        line = {"metric": "SPAN x2 1080p->2160p frames/s", "value": value, "unit": "frames/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "e4m3+f16" if fp8 else "f16", "data": "synthetic (seeded anime-like frames, seeded weights)",
+                "config": {"workload": ("configs[2] SPAN x2 FP8 E4M3" if fp8 else "configs[1] SPAN x2 FP16")
+                           + f", batch {B}, {H}x{W} -> {2 * H}x{2 * W}",
+                           "global_batch": B * world, "frames_per_gpu": B * args.steps,
+                           "parallelism": f"frame-sharded x{world}, no collective",
+                           "l2": "working set > L2: each layer reads and writes 8 x 199 MB activations"},
+                "roofline": roofline, "layers": layers, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+                "cpu_baseline": cpu}
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,139 @@
+/* kirari_b200.h -- C ABI of the B200-native frame path (SPAN x2 upscaler, IFNet interpolator).
+ *
+ * Drop-in for the reference's upscaler / interpolator engine boundary
+ * (Ta2b/Ultimate-Anime-VideoPlayer). The reference boundary is C++-typed -- `gpu::Backend::enqueue
+ * (Engine&, span<const Tensor>, span<Tensor>) -> expected<void, Refusal>` (src/gpu/backend.h:438),
+ * engines created by `Backend::load` (backend.h:446) and module entry points
+ * `kirari_backend_create/destroy` (backend.h:584-587) -- so this header restates it with plain C
+ * types: device frame in, device frame out, per-model weights and scales, an int status in place of
+ * the named refusal. Nothing here throws, exits or traps; out-of-contract shapes are refused before
+ * any launch.
+ *
+ * Threading: one engine per stream / thread (as the reference's engines, backend.h:445); enqueue is
+ * asynchronous on the stream given and never synchronises the host, so it may be captured into a
+ * CUDA graph by the caller.
+ */
+#ifndef KIRARI_B200_H
+#define KIRARI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KB2_ABI_VERSION 1
+
+/* Status codes: the reference's RefusalCode values that can cross this boundary
+ * (src/core/types.h:21-116), plus KB2_KERNEL_TIMEOUT for a bounded device wait that gave up. */
+typedef enum kb2_status {
+  KB2_OK = 0,
+  KB2_SHAPE_INVALID = 1,        /* RefusalCode::ShapeInvalid: size out of contract */
+  KB2_INPUT_MISMATCH = 2,       /* RefusalCode::InputMismatch: wrong tensor count / type / shape */
+  KB2_FORMAT_UNSUPPORTED = 3,   /* RefusalCode::FormatUnsupported: model / precision / GPU refused */
+  KB2_GPU_MEMORY_EXHAUSTED = 4, /* RefusalCode::GpuMemoryExhausted */
+  KB2_VENDOR_CALL_FAILED = 5,   /* RefusalCode::VendorCallFailed: a CUDA call failed */
+  KB2_WEIGHTS_INVALID = 6,      /* RefusalCode::HashMismatch / FormatVersion on the weight blob */
+  KB2_KERNEL_TIMEOUT = 7,       /* a device-side wait gave up (the kernel returned, context usable) */
+  KB2_INVALID_ARGUMENT = 8      /* null pointer or negative count */
+} kb2_status;
+
+/* TensorType of src/gpu/tensor.h:10. */
+typedef enum kb2_tensor_type { KB2_F32 = 0, KB2_F16 = 1, KB2_U8 = 2, KB2_I8 = 3 } kb2_tensor_type;
+
+/* Tensor of src/gpu/tensor.h:45-50: NCHW shape, device address = handle + offset. */
+typedef struct kb2_tensor {
+  int32_t type;     /* kb2_tensor_type */
+  int64_t dims[4];  /* N, C, H, W */
+  uint64_t handle;  /* CUdeviceptr */
+  uint64_t offset;  /* bytes */
+} kb2_tensor;
+
+typedef enum kb2_model { KB2_MODEL_SPAN_X2 = 1, KB2_MODEL_IFNET = 2 } kb2_model;
+typedef enum kb2_precision { KB2_PREC_FP16 = 1, KB2_PREC_FP8_E4M3 = 2 } kb2_precision;
+
+typedef struct kb2_engine kb2_engine;
+
+/* Engine creation parameters (the reference's Artifact + shape set, backend.h:446). */
+typedef struct kb2_engine_desc {
+  int32_t model;        /* kb2_model */
+  int32_t precision;    /* kb2_precision (IFNet: FP16 only) */
+  int32_t max_batch;    /* frames (SPAN) or frame pairs (IFNet) per enqueue, >= 1 */
+  int32_t height;       /* input frame height */
+  int32_t width;        /* input frame width */
+  int32_t device;       /* CUDA device ordinal */
+  const void* weights;  /* weight blob (kb2 blob v1), host memory */
+  uint64_t weights_bytes;
+  const float* act_scales; /* FP8: per-tensor E4M3 activation scales (SPAN: 19), host memory */
+  int32_t act_scale_count;
+} kb2_engine_desc;
+
+/* Module identity (replaces kirari_backend_abi, src/gpu/backend.h:584). */
+int kb2_abi_version(void);
+
+/* Creates an engine: validates the blob (magic, version, CRC-32, parameter count), packs the weights
+ * for the tensor cores, allocates the activation workspace. Replaces Backend::load
+ * (src/gpu/backend.h:446) for SpanFp8Engine (src/gpu/cuda/backend/span_fp8_engine.h:45) and
+ * RifeFusedEngine (rife_fused_engine.h:41). On failure *out is null and the status says why;
+ * kb2_create_error() returns the message. */
+int kb2_create(const kb2_engine_desc* desc, kb2_engine** out);
+const char* kb2_create_error(void);
+
+/* Destroys an engine (waits for its device work). Replaces the Engine destructor. */
+int kb2_destroy(kb2_engine* engine);
+
+/* Last refusal message of this engine ("" if none). */
+const char* kb2_last_error(const kb2_engine* engine);
+
+/* Device bytes the engine owns (weights + workspace), as SpanFp8Net::workspace_bytes
+ * (src/gpu/cuda/backend/span_fp8_net.h:136). */
+int kb2_workspace_bytes(const kb2_engine* engine, uint64_t* bytes);
+
+/* Enqueues one pass on `stream` (a cudaStream_t; 0 = legacy default stream). Replaces
+ * Backend::enqueue (src/gpu/backend.h:438) -> TensorRtBackend::enqueue_span_fp8 / enqueue_rife_fused
+ * (src/gpu/cuda/backend/tensorrt_backend.cpp:527-548).
+ *   SPAN:  inputs[0] = F16 [n,3,H,W];              outputs[0] = F16 [n,3,2H,2W]
+ *   IFNet: inputs[0] = F16 [n,3,H,W] (frame A), inputs[1] = F16 [n,3,H,W] (frame B);
+ *          outputs[0] = F16 [n,3,H,W] (the frame at the engine's timestep)
+ * n <= max_batch, H and W the engine's. Device pointers must be 16-byte aligned. */
+int kb2_enqueue(kb2_engine* engine, void* stream, const kb2_tensor* inputs, int32_t n_inputs,
+                const kb2_tensor* outputs, int32_t n_outputs);
+
+/* IFNet: timestep of the following enqueues, in (0, 1) (the time planes of the reference's
+ * 11-plane input, src/kernels/spec/rife.h:60; Engine::next_times_only, backend.h:391). */
+int kb2_set_timestep(kb2_engine* engine, float timestep);
+
+/* Reads and clears the engine's device error word after synchronising `stream`: KB2_OK, or
+ * KB2_KERNEL_TIMEOUT with the code in *code (which wait gave up). */
+int kb2_check_device(kb2_engine* engine, void* stream, int32_t* code);
+
+/* SPAN FP16 engine only: runs the frames through the FP16 network and returns, per quantised tensor,
+ * the maximum |value| seen (19 peaks: [3b] block b input, [3b+1] / [3b+2] its two activations,
+ * [18] last block output), the calibration of span_fp8::derive (src/gpu/span_fp8/derive.h:42-46).
+ * Synchronous on `stream`. Scales are then peak * 1.25 / 448. */
+int kb2_span_calibrate(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks,
+                       int32_t n_peaks);
+
+/* Per-layer device timing, the role of the reference's GpuTiming event pairs
+ * (src/gpu/cuda/backend/gpu_timing.h:1-40): while enabled, every kernel launch of an enqueue is
+ * bracketed by CUDA events on the enqueue's stream; kb2_read_profile synchronises the engine's last
+ * stream and returns one record per layer kind, accumulated since profiling was enabled. */
+typedef struct kb2_layer_profile {
+  char name[48];         /* layer kind, e.g. "span.block_conv.fp16.silu" */
+  uint64_t launches;     /* launches timed */
+  double total_ms;       /* summed device time */
+  double flops;          /* algorithmic FLOPs per launch at the last batch (direct-conv MACs x 2) */
+  double bytes;          /* algorithmic HBM bytes per launch at the last batch (inputs + outputs once) */
+} kb2_layer_profile;
+
+int kb2_set_profiling(kb2_engine* engine, int32_t enable);
+int kb2_read_profile(kb2_engine* engine, kb2_layer_profile* records, int32_t capacity, int32_t* count);
+/* Kernel launches one enqueue issues (all of them this library's own kernels). */
+int kb2_launches_per_enqueue(const kb2_engine* engine, int32_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KIRARI_B200_H */

@@ -1,0 +1,458 @@
+"""CPU restatement (numpy, float32) of the frame path's two networks — TEST INFRASTRUCTURE ONLY.
+
+This module is the parity checker. Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s
+CPU-baseline leg may import it; the product path (the CUDA library behind ``include/kirari_b200.h``)
+never does. Its results are pinned against the reference's own FP32 interpreter (``oracle/_ref``,
+built by ``oracle/Makefile`` from Ta2b/Ultimate-Anime-VideoPlayer's ``src/gpu/ir``) by the committed
+fixtures in ``tests/golden/`` (``tests/golden/make_golden.py``).
+
+Operator semantics follow the reference file by file:
+
+* Conv, zero padding, FP32 sums: ``src/gpu/ir/op_window.cpp:227-288``.
+* ConvTranspose, scatter form: ``src/gpu/ir/op_window.cpp:309-335``.
+* Resize linear / half-pixel, clamp then lerp: ``src/gpu/ir/op_sample.cpp:88-170``.
+* DepthToSpace CRD (PyTorch pixel_shuffle order): ``src/gpu/ir/op_pixel.cpp:78``.
+* Backward warp: the tap of ``src/gpu/cuda/backend/warp_lib.cuh:45-58`` (``ix = x + fx`` rounded
+  to FP32, clamped to the window, truncated, right/bottom neighbour clamped) and the bilinear
+  blend of ``warp_lib.cuh:61-69`` / ``src/kernels/spec/warp.h:44-49``.
+* E4M3 rounding (RNE, saturate to +-448): ``src/gpu/span_fp8/quantize.h:14-18``.
+* FP8 scales ``max * 1.25 / 448``: ``src/gpu/span_fp8/derive.h:42-46``.
+
+The network definitions are the contract's canonical SPAN x2 and classic IFNet 4.x; the concat
+order of SPAN's conv_cat follows the reference's ``span_fp8::forward``
+(``src/gpu/span_fp8/forward.cpp:158-160``: conv_1 output, last block output, first block output,
+the last block's first activation).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+SPAN_C = 48
+SPAN_BLOCKS = 6
+IFNET_CHANNELS = (192, 128, 96, 64)
+IFNET_SCALES = (8, 4, 2, 1)
+IFNET_RES = 8
+E4M3_MAX = 448.0
+SCALE_HEADROOM = 1.25
+
+
+# --------------------------------------------------------------------------------------------
+# Parameter layouts (flat float32, the order oracle/ref_graphs.cpp and the C ABI read)
+# --------------------------------------------------------------------------------------------
+def span_param_shapes():
+    """[(name, shape)] of canonical SPAN: OIHW weights, then bias, per conv."""
+    c = SPAN_C
+    out = [("conv_1.w", (c, 3, 3, 3)), ("conv_1.b", (c,))]
+    for b in range(SPAN_BLOCKS):
+        for k in range(3):
+            out += [(f"block{b}.c{k + 1}.w", (c, c, 3, 3)), (f"block{b}.c{k + 1}.b", (c,))]
+    out += [("conv_cat.w", (c, 4 * c, 1, 1)), ("conv_cat.b", (c,))]
+    out += [("upsampler.w", (12, c, 3, 3)), ("upsampler.b", (12,))]
+    return out
+
+
+def ifnet_param_shapes():
+    """[(name, shape)] of classic IFNet: per block conv0a/conv0b (+PReLU), 8 residual convs,
+    the 4x4 stride-2 transposed conv (ConvTranspose weights are [Cin, Cout, kh, kw])."""
+    out = []
+    for k, c in enumerate(IFNET_CHANNELS):
+        cin = 7 if k == 0 else 12
+        out += [(f"b{k}.conv0a.w", (c // 2, cin, 3, 3)), (f"b{k}.conv0a.b", (c // 2,)),
+                (f"b{k}.conv0a.slope", (c // 2,))]
+        out += [(f"b{k}.conv0b.w", (c, c // 2, 3, 3)), (f"b{k}.conv0b.b", (c,)),
+                (f"b{k}.conv0b.slope", (c,))]
+        for j in range(IFNET_RES):
+            out += [(f"b{k}.res{j}.w", (c, c, 3, 3)), (f"b{k}.res{j}.b", (c,)),
+                    (f"b{k}.res{j}.slope", (c,))]
+        out += [(f"b{k}.last.w", (c, 5, 4, 4)), (f"b{k}.last.b", (5,))]
+    return out
+
+
+def _flat(params, shapes):
+    return np.concatenate([np.asarray(params[n], np.float32).reshape(-1) for n, _ in shapes])
+
+
+def span_flat(params):
+    return _flat(params, span_param_shapes())
+
+
+def ifnet_flat(params):
+    return _flat(params, ifnet_param_shapes())
+
+
+def unflatten(flat, shapes):
+    out, at = {}, 0
+    for n, s in shapes:
+        k = int(np.prod(s))
+        out[n] = np.asarray(flat[at:at + k], np.float32).reshape(s)
+        at += k
+    assert at == flat.size, "parameter count mismatch"
+    return out
+
+
+def kaiming(rng, shape, fan_in, gain=math.sqrt(2.0)):
+    return (rng.standard_normal(shape) * (gain / math.sqrt(fan_in))).astype(np.float32)
+
+
+def span_init(seed=1):
+    """Kaiming-normal weights (fan_in, gain sqrt 2), zero biases (the contract's config 1)."""
+    rng = np.random.default_rng(seed)
+    p = {}
+    for name, shape in span_param_shapes():
+        if name.endswith(".b"):
+            p[name] = np.zeros(shape, np.float32)
+        else:
+            p[name] = kaiming(rng, shape, int(np.prod(shape[1:])))
+    return p
+
+
+def ifnet_init(seed=2, res_gain=0.2, last_gain=0.05):
+    """Seeded IFNet weights: Kaiming-normal for the entry convs, a damped Kaiming for the eight
+    residual convs (x + res_gain * conv, so the residual stack neither vanishes nor explodes),
+    a small gain on the transposed conv (flows of a few pixels), zero biases, PReLU slopes 0.25."""
+    rng = np.random.default_rng(seed)
+    p = {}
+    for name, shape in ifnet_param_shapes():
+        if name.endswith(".b"):
+            p[name] = np.zeros(shape, np.float32)
+        elif name.endswith(".slope"):
+            p[name] = np.full(shape, 0.25, np.float32)
+        elif ".last." in name:
+            p[name] = kaiming(rng, shape, shape[0] * 4, gain=last_gain)
+        elif ".res" in name:
+            p[name] = kaiming(rng, shape, int(np.prod(shape[1:])), gain=res_gain)
+        else:
+            p[name] = kaiming(rng, shape, int(np.prod(shape[1:])))
+    return p
+
+
+# --------------------------------------------------------------------------------------------
+# Operators
+# --------------------------------------------------------------------------------------------
+def conv2d(x, w, b=None, stride=1, pad=1):
+    """Cross-correlation with zero padding, FP32 (op_window.cpp:227-288 semantics)."""
+    x = np.asarray(x, np.float32)
+    n, c, h, wd = x.shape
+    o, ci, kh, kw = w.shape
+    assert ci == c
+    xp = np.pad(x, ((0, 0), (0, 0), (pad, pad), (pad, pad)))
+    ho = (h + 2 * pad - kh) // stride + 1
+    wo = (wd + 2 * pad - kw) // stride + 1
+    out = np.zeros((n, o, ho, wo), np.float32)
+    wm = w.reshape(o, c * kh * kw).T.astype(np.float32)
+    # rows of output at a time keep the im2col buffer bounded
+    rows = max(1, int(2 ** 25 // max(1, wo * c * kh * kw)))
+    for i in range(n):
+        for y0 in range(0, ho, rows):
+            y1 = min(ho, y0 + rows)
+            win = np.lib.stride_tricks.sliding_window_view(
+                xp[i, :, y0 * stride:(y1 - 1) * stride + kh, :], (kh, kw), axis=(1, 2))
+            win = win[:, ::stride, ::stride]  # c, rows, wo, kh, kw
+            cols = win.transpose(1, 2, 0, 3, 4).reshape((y1 - y0) * wo, c * kh * kw)
+            out[i, :, y0:y1, :] = (cols @ wm).reshape(y1 - y0, wo, o).transpose(2, 0, 1)
+    if b is not None:
+        out += np.asarray(b, np.float32)[None, :, None, None]
+    return out
+
+
+def conv_transpose_4x4s2(x, w, b):
+    """ConvTranspose kernel 4, stride 2, pad 1 (op_window.cpp:309-335, scatter form)."""
+    n, c, h, wd = x.shape
+    co = w.shape[1]
+    out = np.zeros((n, co, 2 * h + 2, 2 * wd + 2), np.float32)  # 1-px margin each side
+    for ky in range(4):
+        for kx in range(4):
+            contrib = np.einsum("nchw,co->nohw", x, w[:, :, ky, kx], optimize=True).astype(np.float32)
+            out[:, :, ky:ky + 2 * h:2, kx:kx + 2 * wd:2] += contrib
+    out = out[:, :, 1:2 * h + 1, 1:2 * wd + 1]
+    return out + np.asarray(b, np.float32)[None, :, None, None]
+
+
+def sigmoid(x):
+    x = np.asarray(x, np.float32)
+    return (1.0 / (1.0 + np.exp(-x))).astype(np.float32)
+
+
+def silu(x):
+    return (x * sigmoid(x)).astype(np.float32)
+
+
+def prelu(x, slope):
+    s = np.asarray(slope, np.float32)[None, :, None, None]
+    return np.where(x >= 0, x, x * s).astype(np.float32)
+
+
+def pixel_shuffle(x, r=2):
+    """DepthToSpace CRD: channel c*r*r + i*r + j goes to pixel (r*y + i, r*x + j) of plane c."""
+    n, c, h, w = x.shape
+    oc = c // (r * r)
+    return x.reshape(n, oc, r, r, h, w).transpose(0, 1, 4, 2, 5, 3).reshape(n, oc, h * r, w * r)
+
+
+def resize_axis_taps(n_in, n_out):
+    """Half-pixel linear taps of the reference Resize (op_sample.cpp:88-170): float32 position
+    (o + 0.5) / scale - 0.5 with scale = n_out / n_in, clamped to [0, n_in - 1], truncated."""
+    scale = np.float32(n_out) / np.float32(n_in)
+    o = np.arange(n_out, dtype=np.float32)
+    pos = (o + np.float32(0.5)) / scale - np.float32(0.5)
+    pos = np.clip(pos, np.float32(0.0), np.float32(n_in - 1)).astype(np.float32)
+    lo = pos.astype(np.int64)
+    hi = np.minimum(lo + 1, n_in - 1)
+    t = (pos - lo.astype(np.float32)).astype(np.float32)
+    return lo, hi, t
+
+
+def resize_bilinear(x, h_out, w_out):
+    n, c, h, w = x.shape
+    ylo, yhi, ty = resize_axis_taps(h, h_out)
+    xlo, xhi, tx = resize_axis_taps(w, w_out)
+    tx = tx[None, None, None, :]
+    ty = ty[None, None, :, None]
+    one = np.float32(1.0)
+    top = (one - tx) * x[:, :, ylo][:, :, :, xlo] + tx * x[:, :, ylo][:, :, :, xhi]
+    bot = (one - tx) * x[:, :, yhi][:, :, :, xlo] + tx * x[:, :, yhi][:, :, :, xhi]
+    return ((one - ty) * top + ty * bot).astype(np.float32)
+
+
+def warp_taps(fx, fy, left, top, right, bottom):
+    """Bilinear tap of warp_lib.cuh:45-58 for every pixel of a flow plane pair [h, w]:
+    ix = fl32(x + fx), clamped to [left, right - 1], x0 = trunc(ix), x1 = min(x0 + 1, right - 1).
+    Returns (x0, x1, y0, y1, wx, wy)."""
+    h, w = fx.shape
+    xs = np.arange(w, dtype=np.float32)[None, :]
+    ys = np.arange(h, dtype=np.float32)[:, None]
+    ix = (xs + fx.astype(np.float32)).astype(np.float32)
+    iy = (ys + fy.astype(np.float32)).astype(np.float32)
+    # fmaxf/fminf: a NaN position goes to the lower bound (fmaxf(NaN, lo) = lo)
+    ix = np.where(np.isnan(ix), np.float32(left), ix)
+    iy = np.where(np.isnan(iy), np.float32(top), iy)
+    ix = np.minimum(np.maximum(ix, np.float32(left)), np.float32(right - 1))
+    iy = np.minimum(np.maximum(iy, np.float32(top)), np.float32(bottom - 1))
+    x0 = ix.astype(np.int32)
+    y0 = iy.astype(np.int32)
+    x1 = np.minimum(x0 + 1, right - 1)
+    y1 = np.minimum(y0 + 1, bottom - 1)
+    wx = (ix - x0.astype(np.float32)).astype(np.float32)
+    wy = (iy - y0.astype(np.float32)).astype(np.float32)
+    return x0, x1, y0, y1, wx, wy
+
+
+def warp(img, flow2, window=None):
+    """Backward warp of img [n,c,h,w] by flow2 [n,2,h,w] (bilinear, border clamp to the window,
+    by default the whole plane)."""
+    n, c, h, w = img.shape
+    left, top, right, bottom = window if window is not None else (0, 0, w, h)
+    out = np.empty_like(img, dtype=np.float32)
+    one = np.float32(1.0)
+    for i in range(n):
+        x0, x1, y0, y1, wx, wy = warp_taps(flow2[i, 0], flow2[i, 1], left, top, right, bottom)
+        for ch in range(c):
+            p = img[i, ch].astype(np.float32)
+            a, b_, d, e = p[y0, x0], p[y0, x1], p[y1, x0], p[y1, x1]
+            out[i, ch] = (a * (one - wx) + b_ * wx) * (one - wy) + (d * (one - wx) + e * wx) * wy
+    return out
+
+
+# --------------------------------------------------------------------------------------------
+# FP8 E4M3 (host rounding of the reference, quantize.h:14-18)
+# --------------------------------------------------------------------------------------------
+def _e4m3_grid():
+    vals = [0.0]
+    for e in range(16):
+        for m in range(8):
+            if e == 15 and m == 7:
+                continue  # NaN encoding
+            v = (m / 8.0) * 2.0 ** -6 if e == 0 else (1.0 + m / 8.0) * 2.0 ** (e - 7)
+            vals.append(v)
+    return np.array(sorted(set(vals)), np.float64)
+
+
+_E4M3 = _e4m3_grid()
+
+
+def e4m3_round(x):
+    """Round to nearest E4M3, ties to even mantissa, saturating to +-448 (NaN -> NaN)."""
+    x = np.asarray(x, np.float32)
+    a = np.abs(x.astype(np.float64))
+    a = np.minimum(a, E4M3_MAX)
+    idx = np.searchsorted(_E4M3, a)
+    idx = np.clip(idx, 1, _E4M3.size - 1)
+    lo, hi = _E4M3[idx - 1], _E4M3[idx]
+    dlo, dhi = a - lo, hi - a
+    # ties: pick the even mantissa (codes alternate even/odd along the sorted grid)
+    pick_hi = (dhi < dlo) | ((dhi == dlo) & ((idx % 2) == 0))
+    r = np.where(pick_hi, hi, lo)
+    r = np.where(a >= _E4M3[-1], E4M3_MAX, r)
+    out = (np.sign(x) * r).astype(np.float32)
+    return np.where(np.isnan(x), np.float32(np.nan), out)
+
+
+def fake_quant(x, scale):
+    return (e4m3_round(np.asarray(x, np.float32) / np.float32(scale)) * np.float32(scale)).astype(np.float32)
+
+
+# --------------------------------------------------------------------------------------------
+# Networks
+# --------------------------------------------------------------------------------------------
+def span_forward(x, p, act_scales=None, store=None, taps=None):
+    """Canonical SPAN x2: x [n,3,h,w] -> [n,3,2h,2w].
+
+    act_scales: 19 per-tensor E4M3 scales of the block conv inputs ([3b] c1, [1+3b] c2, [2+3b] c3;
+      [18] the last block output), the fake-quantised FP8 network (block conv inputs rounded to E4M3).
+    store: optional rounding applied to every stored activation (e.g. FP16 storage emulation).
+    taps: optional dict that receives the block conv inputs (calibration peaks)."""
+    st = store if store is not None else (lambda v: v)
+    q = (lambda v, i: fake_quant(v, act_scales[i])) if act_scales is not None else (lambda v, i: v)
+    s0 = st(conv2d(x, p["conv_1.w"], p["conv_1.b"]))
+    xb = s0
+    first_block = last_act = None
+    for b in range(SPAN_BLOCKS):
+        if taps is not None:
+            taps.setdefault(3 * b, []).append(float(np.abs(xb).max()))
+        a1 = st(silu(conv2d(q(xb, 3 * b), p[f"block{b}.c1.w"], p[f"block{b}.c1.b"])))
+        if taps is not None:
+            taps.setdefault(3 * b + 1, []).append(float(np.abs(a1).max()))
+        a2 = st(silu(conv2d(q(a1, 3 * b + 1), p[f"block{b}.c2.w"], p[f"block{b}.c2.b"])))
+        if taps is not None:
+            taps.setdefault(3 * b + 2, []).append(float(np.abs(a2).max()))
+        c3 = conv2d(q(a2, 3 * b + 2), p[f"block{b}.c3.w"], p[f"block{b}.c3.b"])
+        xb = st(((c3 + xb) * (sigmoid(c3) - np.float32(0.5))).astype(np.float32))
+        if b == 0:
+            first_block = xb
+        if b == SPAN_BLOCKS - 1:
+            last_act = a1
+    if taps is not None:
+        taps.setdefault(3 * SPAN_BLOCKS, []).append(float(np.abs(xb).max()))
+    cat = np.concatenate([s0, xb, first_block, last_act], axis=1)
+    fused = st(conv2d(cat, p["conv_cat.w"], p["conv_cat.b"], pad=0))
+    up = conv2d(fused, p["upsampler.w"], p["upsampler.b"])
+    return pixel_shuffle(up, 2)
+
+
+def quantize_weights_per_channel(w, in_scale=None):
+    """E4M3 weights at one scale per output channel (max |w| / 448, quantize.h:1-5), with the input
+    activation scale folded in first; returns the dequantised weights the kernel effectively uses."""
+    w = np.asarray(w, np.float32)
+    if in_scale is not None:
+        w = (w * np.asarray(in_scale, np.float32)).astype(np.float32)
+    flat = w.reshape(w.shape[0], -1)
+    mx = np.abs(flat).max(axis=1)
+    ws = np.where(mx > 0, mx / np.float32(E4M3_MAX), np.float32(1.0)).astype(np.float32)
+    q = (e4m3_round(flat / ws[:, None]) * ws[:, None]).reshape(w.shape)
+    if in_scale is not None:
+        q = q / np.asarray(in_scale, np.float32)
+    return q.astype(np.float32)
+
+
+def span_forward_fp8_pipeline(x, p, scales):
+    """Emulation of this library's FP8 SPAN data path (test aid): conv_1, block 0, conv_cat and the
+    upsampler in FP16 (FP16 storage); blocks 1..5 with E4M3 per-output-channel weights on E4M3
+    activations, the SPAN gate reading the E4M3 block input; every conv_cat source in FP16."""
+    f16 = lambda v: np.asarray(v, np.float16).astype(np.float32)  # noqa: E731
+    q = lambda v, i: fake_quant(v, scales[i])  # noqa: E731
+    s0 = f16(conv2d(f16(x), f16(p["conv_1.w"]), p["conv_1.b"]))
+    xb16, first_block, last_act = s0, None, None
+    for b in range(SPAN_BLOCKS):
+        if b == 0:
+            a1 = f16(silu(conv2d(s0, f16(p["block0.c1.w"]), p["block0.c1.b"])))
+            a2 = f16(silu(conv2d(a1, f16(p["block0.c2.w"]), p["block0.c2.b"])))
+            c3 = conv2d(a2, f16(p["block0.c3.w"]), p["block0.c3.b"])
+            xr = (c3 + s0) * (sigmoid(c3) - np.float32(0.5))
+            xb16, xq = f16(xr), q(xr, 3)
+            first_block = xb16
+            continue
+        w = [quantize_weights_per_channel(p[f"block{b}.c{k + 1}.w"]) for k in range(3)]
+        a1r = silu(conv2d(xq, w[0], p[f"block{b}.c1.b"]))
+        a1 = q(a1r, 3 * b + 1)
+        a2 = q(silu(conv2d(a1, w[1], p[f"block{b}.c2.b"])), 3 * b + 2)
+        c3 = conv2d(a2, w[2], p[f"block{b}.c3.b"])
+        xr = ((c3 + xq) * (sigmoid(c3) - np.float32(0.5))).astype(np.float32)
+        if b == SPAN_BLOCKS - 1:
+            last_act = f16(a1r)
+            xb16 = f16(xr)
+        else:
+            xq = q(xr, 3 * b + 3)
+    cat = np.concatenate([s0, xb16, first_block, last_act], axis=1)
+    fused = f16(conv2d(cat, f16(p["conv_cat.w"]), p["conv_cat.b"], pad=0))
+    up = conv2d(fused, f16(p["upsampler.w"]), p["upsampler.b"])
+    return pixel_shuffle(up, 2)
+
+
+def span_scales_from_peaks(peaks, floor=None):
+    """max * 1.25 / 448 per tensor (derive.h:42-46); a non-finite peak is refused, and so is a
+    zero peak unless ``floor`` is given (the seeded canonical SPAN's deep blocks decay to exact
+    zeros in FP32, so its calibration floors their peaks instead of refusing them)."""
+    peaks = np.asarray(peaks, np.float64)
+    if floor is not None:
+        peaks = np.maximum(peaks, floor)
+    if not np.all(np.isfinite(peaks)) or np.any(peaks <= 0):
+        raise ValueError("unusable calibration peak")
+    return (peaks * SCALE_HEADROOM / E4M3_MAX).astype(np.float32)
+
+
+def ifnet_block(x, flow, scale, p, k):
+    c = IFNET_CHANNELS[k]
+    n, _, h, w = x.shape
+    if scale != 1:
+        x = resize_bilinear(x, h // scale, w // scale)
+    if flow is not None:
+        f = flow
+        if scale != 1:
+            f = resize_bilinear(flow, h // scale, w // scale)
+        f = (f * np.float32(1.0 / scale)).astype(np.float32)
+        x = np.concatenate([x, f], axis=1)
+    hdn = prelu(conv2d(x, p[f"b{k}.conv0a.w"], p[f"b{k}.conv0a.b"], stride=2), p[f"b{k}.conv0a.slope"])
+    hdn = prelu(conv2d(hdn, p[f"b{k}.conv0b.w"], p[f"b{k}.conv0b.b"], stride=2), p[f"b{k}.conv0b.slope"])
+    for j in range(IFNET_RES):
+        r = conv2d(hdn, p[f"b{k}.res{j}.w"], p[f"b{k}.res{j}.b"])
+        hdn = prelu((r + hdn).astype(np.float32), p[f"b{k}.res{j}.slope"])
+    tmp = conv_transpose_4x4s2(hdn, p[f"b{k}.last.w"], p[f"b{k}.last.b"])
+    tmp = resize_bilinear(tmp, h, w)
+    fd = (tmp[:, :4] * np.float32(scale * 2)).astype(np.float32)
+    md = tmp[:, 4:5]
+    del c
+    return fd, md
+
+
+def ifnet_forward(img0, img1, timestep, p, return_flow=False):
+    """Classic IFNet 4.x on img0, img1 [n,3,h,w] (h, w multiples of 32) -> [n,3,h,w]."""
+    n, _, h, w = img0.shape
+    t = np.full((n, 1, h, w), np.float32(timestep), np.float32)
+    flow = mask = None
+    w0, w1 = img0, img1
+    for k, s in enumerate(IFNET_SCALES):
+        if k == 0:
+            xin = np.concatenate([img0, img1, t], axis=1)
+            flow, mask = ifnet_block(xin, None, s, p, k)
+        else:
+            xin = np.concatenate([w0, w1, t, mask], axis=1)
+            fd, md = ifnet_block(xin, flow, s, p, k)
+            flow = (flow + fd).astype(np.float32)
+            mask = (mask + md).astype(np.float32)
+        w0 = warp(img0, flow[:, 0:2])
+        w1 = warp(img1, flow[:, 2:4])
+    m = sigmoid(mask)
+    out = (w0 * m + w1 * (np.float32(1.0) - m)).astype(np.float32)
+    if return_flow:
+        return out, flow, mask
+    return out
+
+
+# --------------------------------------------------------------------------------------------
+# Metrics (span_fp8/metrics.cpp semantics: PSNR over [0, 1] after clamp)
+# --------------------------------------------------------------------------------------------
+def clamp01(x):
+    return np.clip(np.asarray(x, np.float32), 0.0, 1.0)
+
+
+def psnr(a, b):
+    a = clamp01(a).astype(np.float64)
+    b = clamp01(b).astype(np.float64)
+    mse = float(np.mean((a - b) ** 2))
+    return float("inf") if mse == 0 else 10.0 * math.log10(1.0 / mse)
+
+
+def max_abs_clamped(a, b):
+    return float(np.max(np.abs(clamp01(a) - clamp01(b))))

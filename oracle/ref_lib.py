@@ -1,0 +1,70 @@
+"""ctypes binding of oracle/_ref/libkirari_ref.so — TEST INFRASTRUCTURE ONLY.
+
+The library is the reference's own FP32 CPU interpreter (Ta2b/Ultimate-Anime-VideoPlayer
+``src/gpu/ir``, compiled in place by ``oracle/Makefile``) driving the in-code graphs of
+``oracle/ref_graphs.cpp``. It is used to pin the numpy restatement (``oracle/nets.py``) and as the
+timed reference CPU implementation in ``bench.py``. Nothing in the product path loads it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_ref", "libkirari_ref.so")
+_lib = None
+_fp = ctypes.POINTER(ctypes.c_float)
+
+
+def available() -> bool:
+    return os.path.exists(LIB_PATH)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not available():
+            raise FileNotFoundError(f"{LIB_PATH} missing: run `make -C oracle` where the reference exists")
+        L = ctypes.CDLL(LIB_PATH)
+        L.kref_last_error.restype = ctypes.c_char_p
+        L.kref_span_forward.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp, ctypes.c_long,
+                                        _fp, _fp]
+        L.kref_span_forward.restype = ctypes.c_int
+        L.kref_ifnet_forward.argtypes = [_fp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                         _fp, ctypes.c_long, _fp]
+        L.kref_ifnet_forward.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return a.ctypes.data_as(_fp)
+
+
+def span_forward(x, flat_params, act_scales=None):
+    """Reference FP32 SPAN x2 on x [n,3,h,w]; act_scales (19) selects the E4M3 fake-quant graph."""
+    x = np.ascontiguousarray(x, np.float32)
+    flat = np.ascontiguousarray(flat_params, np.float32)
+    n, _, h, w = x.shape
+    out = np.zeros((n, 3, 2 * h, 2 * w), np.float32)
+    sc = None if act_scales is None else np.ascontiguousarray(act_scales, np.float32)
+    rc = lib().kref_span_forward(_ptr(x), n, h, w, _ptr(flat), flat.size,
+                                 None if sc is None else _ptr(sc), _ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"kref_span_forward: {rc} {lib().kref_last_error().decode(errors='replace')}")
+    return out
+
+
+def ifnet_forward(img0, img1, timestep, flat_params):
+    """Reference FP32 classic IFNet on img0, img1 [n,3,h,w] (h, w multiples of 32)."""
+    a = np.ascontiguousarray(img0, np.float32)
+    b = np.ascontiguousarray(img1, np.float32)
+    flat = np.ascontiguousarray(flat_params, np.float32)
+    n, _, h, w = a.shape
+    out = np.zeros((n, 3, h, w), np.float32)
+    rc = lib().kref_ifnet_forward(_ptr(a), _ptr(b), n, h, w, float(timestep), _ptr(flat), flat.size, _ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"kref_ifnet_forward: {rc} {lib().kref_last_error().decode(errors='replace')}")
+    return out

@@ -1,0 +1,169 @@
+// The C ABI of include/kirari_b200.h over the C++ engines. Every entry point catches everything:
+// nothing throws across the boundary (the reference's rule for its module entry points,
+// src/gpu/backend.h:575-587).
+#include <memory>
+#include <new>
+#include <string>
+
+#include "../../include/kirari_b200.h"
+#include "engine.h"
+
+namespace {
+thread_local std::string g_create_error;
+
+int set_error(kb2_engine* e, const kb2::Status& s);
+}  // namespace
+
+struct kb2_engine {
+  std::unique_ptr<kb2::Engine> impl;
+  std::string error;
+};
+
+namespace {
+int set_error(kb2_engine* e, const kb2::Status& s) {
+  if (e != nullptr) e->error = s.ok() ? std::string() : s.detail;
+  return s.code;
+}
+
+kb2::Status tensor_ptr(const kb2_tensor& t, int type, const int64_t (&dims)[4], void** out) {
+  if (t.type != type) return kb2::refuse(KB2_INPUT_MISMATCH, "tensor type mismatch");
+  for (int i = 0; i < 4; ++i)
+    if (t.dims[i] != dims[i]) return kb2::refuse(KB2_INPUT_MISMATCH, "tensor shape mismatch");
+  const uint64_t addr = t.handle + t.offset;
+  if (addr == 0 || (addr & 15u) != 0) return kb2::refuse(KB2_INPUT_MISMATCH, "tensor address null or not 16-byte aligned");
+  *out = reinterpret_cast<void*>(addr);
+  return kb2::Status::Ok();
+}
+}  // namespace
+
+namespace kb2 {
+Status Engine::frame_io(const kb2_tensor* inputs, int n_in, const kb2_tensor* outputs, int n_out, int n_frames_in,
+                        int out_scale, void** in_ptrs, void** out_ptr, int* batch) const {
+  if (inputs == nullptr || outputs == nullptr || n_in != n_frames_in || n_out != 1)
+    return refuse(KB2_INPUT_MISMATCH, "wrong number of input / output tensors");
+  const int64_t n = inputs[0].dims[0];
+  if (n < 1 || n > max_batch()) return refuse(KB2_SHAPE_INVALID, "batch out of contract");
+  const int64_t din[4] = {n, 3, height(), width()};
+  for (int i = 0; i < n_in; ++i) KB2_TRY(tensor_ptr(inputs[i], KB2_F16, din, &in_ptrs[i]));
+  const int64_t dout[4] = {n, 3, height() * out_scale, width() * out_scale};
+  KB2_TRY(tensor_ptr(outputs[0], KB2_F16, dout, out_ptr));
+  *batch = static_cast<int>(n);
+  return Status::Ok();
+}
+}  // namespace kb2
+
+extern "C" {
+
+int kb2_abi_version(void) { return KB2_ABI_VERSION; }
+
+const char* kb2_create_error(void) { return g_create_error.c_str(); }
+
+int kb2_create(const kb2_engine_desc* desc, kb2_engine** out) {
+  try {
+    g_create_error.clear();
+    if (out == nullptr || desc == nullptr) {
+      g_create_error = "null argument";
+      return KB2_INVALID_ARGUMENT;
+    }
+    *out = nullptr;
+    std::unique_ptr<kb2::Engine> impl;
+    const kb2::Status st = kb2::make_engine(*desc, impl);
+    if (!st.ok()) {
+      g_create_error = st.detail;
+      return st.code;
+    }
+    auto* e = new (std::nothrow) kb2_engine;
+    if (e == nullptr) {
+      g_create_error = "host allocation failed";
+      return KB2_GPU_MEMORY_EXHAUSTED;
+    }
+    e->impl = std::move(impl);
+    *out = e;
+    return KB2_OK;
+  } catch (const std::exception& ex) {
+    g_create_error = ex.what();
+    return KB2_VENDOR_CALL_FAILED;
+  } catch (...) {
+    g_create_error = "unknown failure";
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
+int kb2_destroy(kb2_engine* engine) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    cudaDeviceSynchronize();
+    delete engine;
+    return KB2_OK;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
+const char* kb2_last_error(const kb2_engine* engine) { return engine == nullptr ? "" : engine->error.c_str(); }
+
+int kb2_workspace_bytes(const kb2_engine* engine, uint64_t* bytes) {
+  if (engine == nullptr || bytes == nullptr) return KB2_INVALID_ARGUMENT;
+  *bytes = engine->impl->device_bytes();
+  return KB2_OK;
+}
+
+int kb2_enqueue(kb2_engine* engine, void* stream, const kb2_tensor* inputs, int32_t n_inputs,
+                const kb2_tensor* outputs, int32_t n_outputs) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    return set_error(engine, engine->impl->enqueue(static_cast<cudaStream_t>(stream), inputs, n_inputs, outputs,
+                                                   n_outputs));
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
+int kb2_set_timestep(kb2_engine* engine, float timestep) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  return set_error(engine, engine->impl->set_timestep(timestep));
+}
+
+int kb2_check_device(kb2_engine* engine, void* stream, int32_t* code) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    return set_error(engine, engine->impl->check_device(static_cast<cudaStream_t>(stream), code));
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
+int kb2_span_calibrate(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks, int32_t n_peaks) {
+  if (engine == nullptr || frames == nullptr || peaks == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    return set_error(engine, engine->impl->calibrate(static_cast<cudaStream_t>(stream), *frames, peaks, n_peaks));
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
+int kb2_set_profiling(kb2_engine* engine, int32_t enable) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  return set_error(engine, engine->impl->set_profiling(enable != 0));
+}
+
+int kb2_read_profile(kb2_engine* engine, kb2_layer_profile* records, int32_t capacity, int32_t* count) {
+  if (engine == nullptr || count == nullptr || (records == nullptr && capacity > 0) || capacity < 0)
+    return KB2_INVALID_ARGUMENT;
+  try {
+    int n = 0;
+    const int rc = set_error(engine, engine->impl->read_profile(records, capacity, &n));
+    *count = n;
+    return rc;
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
+int kb2_launches_per_enqueue(const kb2_engine* engine, int32_t* launches) {
+  if (engine == nullptr || launches == nullptr) return KB2_INVALID_ARGUMENT;
+  *launches = engine->impl->launches_per_enqueue();
+  return KB2_OK;
+}
+
+}  // extern "C"

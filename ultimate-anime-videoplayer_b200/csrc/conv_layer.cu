@@ -1,0 +1,274 @@
+// Host side of the tensor-core convolution: the K-step table (which input row, pixel shift and
+// channel chunk each 32-byte K step of an MMA reads), the matching weight packing (FP16, or E4M3 with
+// per-output-channel scales as span_fp8::channel_scales, src/gpu/span_fp8/quantize.h:1-5), the TMA
+// tensor maps and the persistent launch.
+#include <array>
+#include <cstdio>
+
+#include "conv_layer.h"
+
+namespace kb2 {
+
+namespace {
+
+struct Half {
+  int src, dy, dx, chunk;
+  bool zero;  // pads the instruction: weights are zero, the data read is in bounds and finite
+};
+
+std::vector<std::array<Half, 2>> make_ksteps(const ConvSpec& s, int chunks) {
+  std::vector<std::array<Half, 2>> steps;
+  if (s.taps == 1) {
+    std::vector<Half> seq;
+    for (int src = 0; src < s.n_sources; ++src)
+      for (int c = 0; c < chunks; ++c) seq.push_back({src, 0, 0, c, false});
+    if (seq.size() % 2 != 0) {
+      const Half last = seq.back();
+      seq.push_back({last.src, 0, 1, last.chunk, true});
+    }
+    for (size_t i = 0; i < seq.size(); i += 2) steps.push_back({seq[i], seq[i + 1]});
+    return steps;
+  }
+  for (int dy = -1; dy <= 1; ++dy) {
+    for (int dx = -1; dx <= 1; ++dx)
+      for (int c = 0; c + 1 < chunks; c += 2) steps.push_back({Half{0, dy, dx, c, false}, Half{0, dy, dx, c + 1, false}});
+    if (chunks % 2 != 0) {
+      const int cl = chunks - 1;
+      // the odd chunk of horizontally adjacent taps: one pixel (16 bytes) apart in the slot
+      steps.push_back({Half{0, dy, -1, cl, false}, Half{0, dy, 0, cl, false}});
+      steps.push_back({Half{0, dy, 1, cl, false}, Half{0, dy, 2, cl, true}});
+    }
+  }
+  return steps;
+}
+
+using LaunchFn = void (*)(dim3, size_t, cudaStream_t, const CUtensorMap*, const ConvArgs&);
+using Kernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, ConvArgs);
+
+template <bool F8, int N, int E, int O>
+void launch_impl(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap* m, const ConvArgs& a) {
+  conv_tc_kernel<F8, N, E, O><<<grid, 192, smem, s>>>(m[0], m[1], m[2], m[3], a);
+}
+
+struct KernelEntry {
+  bool fp8;
+  int n, epi, out;
+  LaunchFn launch;
+  const void* fn;
+};
+
+#define KB2_KERNEL(F8, N, E, O) \
+  KernelEntry { F8, N, E, O, &launch_impl<F8, N, E, O>, reinterpret_cast<const void*>(&conv_tc_kernel<F8, N, E, O>) }
+
+// The instantiations the SPAN engines use (FP16 engine: the first four; FP8 engine: all).
+const KernelEntry kKernels[] = {
+    KB2_KERNEL(false, 48, kEpiBias, kOutF16Chunk),     KB2_KERNEL(false, 48, kEpiSilu, kOutF16Chunk),
+    KB2_KERNEL(false, 48, kEpiSpanAttn, kOutF16Chunk), KB2_KERNEL(false, 16, kEpiBias, kOutPixShuf2),
+    KB2_KERNEL(false, 48, kEpiSpanAttn, kOutF16E4m3),  KB2_KERNEL(true, 48, kEpiSilu, kOutE4m3Chunk),
+    KB2_KERNEL(true, 48, kEpiSilu, kOutF16E4m3),       KB2_KERNEL(true, 48, kEpiSpanAttn, kOutE4m3Chunk),
+    KB2_KERNEL(true, 48, kEpiSpanAttn, kOutF16Chunk),
+};
+
+const KernelEntry* find_kernel(const ConvSpec& s) {
+  for (const KernelEntry& k : kKernels)
+    if (k.fp8 == s.fp8 && k.n == s.n_pad && k.epi == s.epi && k.out == s.out) return &k;
+  return nullptr;
+}
+
+uint32_t tmem_cols(int n) {
+  const uint32_t stride = n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : 256));
+  return 2 * stride;
+}
+
+uint16_t f32_to_f16_bits(float f) {
+  const __half h = __float2half_rn(f);
+  return *reinterpret_cast<const uint16_t*>(&h);
+}
+
+}  // namespace
+
+int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const float* prelu_slope,
+                        const float* act_scales, const ChunkedTensor* const* inputs, int* err_word) {
+  spec = s;
+  const KernelEntry* k = find_kernel(s);
+  if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this layer shape");
+  const ChunkedTensor& in0 = *inputs[0];
+  for (int i = 0; i < s.n_sources; ++i) {
+    const ChunkedTensor& t = *inputs[i];
+    if (t.fp8 != s.fp8 || t.chunks != in0.chunks || t.H != in0.H || t.W != in0.W || t.batch != in0.batch)
+      return refuse(KB2_INPUT_MISMATCH, "conv sources of different geometry");
+  }
+  const int chunks = in0.chunks;
+  const int epc = s.fp8 ? 16 : 8;
+  const int halo = s.taps == 9 ? 1 : 0;
+  if (chunks * epc < s.cin) return refuse(KB2_INPUT_MISMATCH, "input tensor narrower than the conv");
+
+  const auto steps = make_ksteps(s, chunks);
+  if (static_cast<int>(steps.size()) > kMaxKSteps) return refuse(KB2_FORMAT_UNSUPPORTED, "too many K steps");
+  int dx_max = 0;
+  for (const auto& st : steps)
+    for (const Half& h : st) dx_max = h.dx > dx_max ? h.dx : dx_max;
+  int px = dx_max + halo + kTileM;
+  px = (px + 7) / 8 * 8;
+  const uint32_t src_bytes = static_cast<uint32_t>(chunks) * px * 16;
+  const uint32_t slot_bytes = src_bytes * static_cast<uint32_t>(s.n_sources);
+
+  ConvArgs& a = args;
+  a = ConvArgs{};
+  a.batch = in0.batch;
+  a.H = in0.H;
+  a.W = in0.W;
+  a.strips = (in0.W + kTileM - 1) / kTileM;
+  a.n_sources = s.n_sources;
+  a.chunks = chunks;
+  a.px = px;
+  a.halo = halo;
+  a.in_rows = s.taps == 9 ? 3 : 1;
+  a.row_off = s.taps == 9 ? -1 : 0;
+  a.src_bytes = src_bytes;
+  a.slot_bytes = slot_bytes;
+  a.ring = s.taps == 9 ? 4 : 3;
+  a.n_ksteps = static_cast<int>(steps.size());
+  for (size_t j = 0; j < steps.size(); ++j) {
+    auto addr = [&](const Half& h) {
+      return static_cast<int64_t>(h.src) * src_bytes + static_cast<int64_t>(h.chunk) * px * 16 +
+             static_cast<int64_t>(h.dx + halo) * 16;
+    };
+    const int64_t a0 = addr(steps[j][0]);
+    const int64_t a1 = addr(steps[j][1]);
+    if (steps[j][0].dy != steps[j][1].dy || a1 <= a0 || (a1 - a0) % 16 != 0 || (a1 - a0) >= (1 << 18))
+      return refuse(KB2_FORMAT_UNSUPPORTED, "K step halves not expressible as one descriptor");
+    a.ks[j].a_off = static_cast<uint32_t>(a0);
+    a.ks[j].lbo = static_cast<uint32_t>(a1 - a0);
+    a.ks[j].row = s.taps == 9 ? steps[j][0].dy + 1 : 0;
+  }
+  a.idesc = make_idesc(kTileM, s.n_pad);
+
+  // ---- weights
+  const int kk = s.taps == 9 ? 3 : 1;
+  const int cin_total = s.n_sources * s.cin;
+  auto w_at = [&](int co, int ci_total, int ky, int kx) {
+    return W[((static_cast<size_t>(co) * cin_total + ci_total) * kk + ky) * kk + kx];
+  };
+  std::vector<float> wscale(static_cast<size_t>(s.n_pad), 1.0f);
+  auto src_scale = [&](int src) { return act_scales != nullptr ? act_scales[src] : 1.0f; };
+  if (s.fp8) {
+    for (int co = 0; co < s.n_real; ++co) {
+      float mx = 0.0f;
+      for (int src = 0; src < s.n_sources; ++src)
+        for (int ci = 0; ci < s.cin; ++ci)
+          for (int ky = 0; ky < kk; ++ky)
+            for (int kx = 0; kx < kk; ++kx)
+              mx = std::fmax(mx, std::fabs(w_at(co, src * s.cin + ci, ky, kx) * src_scale(src)));
+      wscale[co] = mx > 0.0f ? mx / 448.0f : 1.0f;
+    }
+  }
+  const size_t step_bytes = 2u * static_cast<size_t>(s.n_pad) * 16u;
+  std::vector<uint8_t> packed(steps.size() * step_bytes, 0);
+  for (size_t j = 0; j < steps.size(); ++j) {
+    for (int h = 0; h < 2; ++h) {
+      const Half& hf = steps[j][h];
+      for (int co = 0; co < s.n_real; ++co) {
+        for (int e = 0; e < epc; ++e) {
+          const int ci = hf.chunk * epc + e;
+          float v = 0.0f;
+          if (!hf.zero && ci < s.cin) {
+            const int ky = s.taps == 9 ? hf.dy + 1 : 0;
+            const int kx = s.taps == 9 ? hf.dx + 1 : 0;
+            v = w_at(co, hf.src * s.cin + ci, ky, kx);
+          }
+          uint8_t* dst = packed.data() + j * step_bytes + static_cast<size_t>(h) * s.n_pad * 16 +
+                         static_cast<size_t>(co) * 16;
+          if (s.fp8) {
+            dst[e] = e4m3_encode(v * src_scale(hf.src) / wscale[co]);
+          } else {
+            const uint16_t bits = f32_to_f16_bits(v);
+            std::memcpy(dst + 2 * e, &bits, 2);
+          }
+        }
+      }
+    }
+  }
+  KB2_TRY(wpack.alloc(packed.size()));
+  KB2_CUDA(cudaMemcpy(wpack.ptr, packed.data(), packed.size(), cudaMemcpyHostToDevice));
+  std::vector<float> bias_h(static_cast<size_t>(s.n_pad), 0.0f), slope_h(static_cast<size_t>(s.n_pad), 0.0f);
+  for (int co = 0; co < s.n_real; ++co) {
+    bias_h[co] = b != nullptr ? b[co] : 0.0f;
+    slope_h[co] = prelu_slope != nullptr ? prelu_slope[co] : 0.0f;
+  }
+  KB2_TRY(bias.alloc(bias_h.size() * 4));
+  KB2_CUDA(cudaMemcpy(bias.ptr, bias_h.data(), bias_h.size() * 4, cudaMemcpyHostToDevice));
+  KB2_TRY(slope.alloc(slope_h.size() * 4));
+  KB2_CUDA(cudaMemcpy(slope.ptr, slope_h.data(), slope_h.size() * 4, cudaMemcpyHostToDevice));
+  if (s.fp8) {
+    KB2_TRY(scale.alloc(wscale.size() * 4));
+    KB2_CUDA(cudaMemcpy(scale.ptr, wscale.data(), wscale.size() * 4, cudaMemcpyHostToDevice));
+  }
+  a.wpack = wpack.as<uint8_t>();
+  a.wbytes = static_cast<uint32_t>(packed.size());
+  a.w_smem = (a.wbytes + 1023u) / 1024u * 1024u;
+  a.bias = bias.as<float>();
+  a.slope = slope.as<float>();
+  a.chan_scale = s.fp8 ? scale.as<float>() : nullptr;
+  a.out_chunks = s.out_chunks;
+  a.out2_chunks = s.out2_chunks;
+  a.err = err_word;
+
+  // ---- tensor maps (single-source layers repeat map 0)
+  for (int i = 0; i < 4; ++i) KB2_TRY(encode_row_map(&maps[i], *inputs[i < s.n_sources ? i : 0], px));
+
+  // ---- launch shape
+  smem = 1024 + a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (2 * a.ring + 6) * 8 + 16;
+  int dev = 0;
+  KB2_CUDA(cudaGetDevice(&dev));
+  int optin = 0;
+  KB2_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (smem > static_cast<size_t>(optin)) return refuse(KB2_FORMAT_UNSUPPORTED, "layer needs too much shared memory");
+  KB2_CUDA(cudaFuncSetAttribute(k->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+  int per_sm = 0;
+  KB2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k->fn, 192, smem));
+  if (per_sm < 1) return refuse(KB2_FORMAT_UNSUPPORTED, "layer does not fit on an SM");
+  const int tmem_cap = static_cast<int>(512u / tmem_cols(s.n_pad));
+  if (per_sm > tmem_cap) per_sm = tmem_cap;
+  const int slots = num_sms() * per_sm;
+  // bands: about 16 work items per resident block, 4..64 rows each
+  const long long rows_total = static_cast<long long>(a.batch) * a.H * a.strips;
+  int band = static_cast<int>(rows_total / (16LL * slots));
+  band = band < 4 ? 4 : (band > 64 ? 64 : band);
+  a.band_rows = band;
+  a.bands = (a.H + band - 1) / band;
+  a.items = a.batch * a.bands * a.strips;
+  grid = a.items < slots ? a.items : slots;
+  return Status::Ok();
+}
+
+Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
+                         float res_scale, void* out2) const {
+  const KernelEntry* k = find_kernel(spec);
+  if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no kernel");
+  ConvArgs a = args;
+  a.batch = batch;
+  a.items = batch * a.bands * a.strips;
+  a.out = static_cast<uint8_t*>(out);
+  a.out2 = static_cast<uint8_t*>(out2);
+  a.residual = static_cast<const uint8_t*>(residual);
+  a.res_fp8 = spec.fp8 ? 1 : 0;
+  a.out_inv_scale = out_inv_scale;
+  a.res_scale = res_scale;
+  const int g = a.items < grid ? a.items : grid;
+  k->launch(dim3(static_cast<unsigned>(g)), smem, stream, maps, a);
+  return cuda_status(cudaGetLastError(), "conv_tc_kernel launch");
+}
+
+}  // namespace kb2

@@ -1,0 +1,107 @@
+// Engine implementations: SPAN x2 (FP16 / FP8) and the factory.
+#include <cstring>
+
+#include "engine.h"
+#include "span_net.h"
+
+namespace kb2 {
+
+Status Engine::check_device(cudaStream_t stream, int32_t* code) {
+  KB2_CUDA(cudaStreamSynchronize(stream));
+  int word = 0;
+  KB2_CUDA(cudaMemcpy(&word, err_word(), sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != nullptr) *code = word;
+  if (word != 0) {
+    KB2_CUDA(cudaMemset(err_word(), 0, sizeof(int)));
+    return refuse(KB2_KERNEL_TIMEOUT, "a device-side wait gave up (code " + std::to_string(word) + ")");
+  }
+  return Status::Ok();
+}
+
+namespace {
+
+class SpanEngine final : public Engine {
+ public:
+  Status init(const kb2_engine_desc& d, const std::vector<float>& params) {
+    return net_.create(params, d.precision, d.max_batch, d.height, d.width, d.act_scales, d.act_scale_count);
+  }
+  std::vector<std::string> input_names() const override { return {"input"}; }
+  std::vector<std::string> output_names() const override { return {"output"}; }
+  int max_batch() const override { return net_.max_batch(); }
+  int height() const override { return net_.height(); }
+  int width() const override { return net_.width(); }
+  size_t device_bytes() const override { return net_.device_bytes(); }
+  Status enqueue(cudaStream_t stream, const kb2_tensor* inputs, int n_inputs, const kb2_tensor* outputs,
+                 int n_outputs) override {
+    void* in = nullptr;
+    void* out = nullptr;
+    int batch = 0;
+    KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 1, 2, &in, &out, &batch));
+    return net_.run(stream, in, out, batch);
+  }
+  Status calibrate(cudaStream_t stream, const kb2_tensor& frames, float* peaks, int n_peaks) override {
+    if (n_peaks != kSpanScales) return refuse(KB2_INPUT_MISMATCH, "SPAN calibration returns 19 peaks");
+    if (frames.type != KB2_F16 || frames.dims[1] != 3 || frames.dims[2] != height() || frames.dims[3] != width() ||
+        frames.dims[0] < 1)
+      return refuse(KB2_INPUT_MISMATCH, "calibration frames: F16 [n,3,H,W] expected");
+    const uint64_t addr = frames.handle + frames.offset;
+    if (addr == 0 || (addr & 15u) != 0) return refuse(KB2_INPUT_MISMATCH, "calibration frames misaligned");
+    return net_.calibrate(stream, reinterpret_cast<const void*>(addr), static_cast<int>(frames.dims[0]), peaks);
+  }
+  Status set_profiling(bool on) override {
+    net_.set_profiling(on);
+    return Status::Ok();
+  }
+  Status read_profile(kb2_layer_profile* records, int capacity, int* count) override {
+    std::vector<SpanNet::Profile> kinds;
+    KB2_TRY(net_.read_profile(kinds));
+    *count = static_cast<int>(kinds.size());
+    for (int i = 0; i < *count && i < capacity; ++i) {
+      kb2_layer_profile& r = records[i];
+      std::memset(&r, 0, sizeof(r));
+      std::strncpy(r.name, kinds[i].name.c_str(), sizeof(r.name) - 1);
+      r.launches = kinds[i].launches;
+      r.total_ms = kinds[i].ms;
+      r.flops = kinds[i].flops;
+      r.bytes = kinds[i].bytes;
+    }
+    return Status::Ok();
+  }
+  int launches_per_enqueue() const override { return net_.launches_per_run(); }
+
+ protected:
+  int* err_word() const override { return net_.err_word(); }
+
+ private:
+  SpanNet net_;
+};
+
+}  // namespace
+
+Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
+  // Everything that needs no device is checked first: the blob and the shapes.
+  if (d.model != KB2_MODEL_SPAN_X2 && d.model != KB2_MODEL_IFNET) return refuse(KB2_FORMAT_UNSUPPORTED, "unknown model");
+  std::vector<float> params;
+  KB2_TRY(parse_blob(d.weights, d.weights_bytes, d.model, params));
+  if (d.max_batch < 1 || d.height < 1 || d.width < 1 || d.height > 8192 || d.width > 8192)
+    return refuse(KB2_SHAPE_INVALID, "frame size or batch out of contract");
+  int count = 0;
+  KB2_CUDA(cudaGetDeviceCount(&count));
+  if (d.device < 0 || d.device >= count) return refuse(KB2_INPUT_MISMATCH, "no such CUDA device");
+  KB2_CUDA(cudaSetDevice(d.device));
+  int major = 0, minor = 0;
+  KB2_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d.device));
+  KB2_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, d.device));
+  if (major != 10 || minor != 0)
+    return refuse(KB2_FORMAT_UNSUPPORTED, "this library runs on sm_100 (B200) only");
+  if (d.model == KB2_MODEL_SPAN_X2) {
+    auto e = std::make_unique<SpanEngine>();
+    KB2_TRY(e->init(d, params));
+    out = std::move(e);
+    return Status::Ok();
+  }
+  if (d.model == KB2_MODEL_IFNET) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet engine not built in this library");
+  return refuse(KB2_FORMAT_UNSUPPORTED, "unknown model");
+}
+
+}  // namespace kb2

@@ -1,0 +1,46 @@
+// C++ engines behind the C ABI: the shape of the reference's gpu::Engine (src/gpu/backend.h:381-413)
+// with the per-model enqueue of TensorRtBackend (tensorrt_backend.cpp:527-548) folded in.
+#pragma once
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "host_util.h"
+
+namespace kb2 {
+
+class Engine {
+ public:
+  virtual ~Engine() = default;
+  virtual std::vector<std::string> input_names() const = 0;   // Engine::input_names (backend.h:385)
+  virtual std::vector<std::string> output_names() const = 0;  // Engine::output_names (backend.h:386)
+  virtual int max_batch() const = 0;
+  virtual int height() const = 0;
+  virtual int width() const = 0;
+  virtual size_t device_bytes() const = 0;
+  virtual Status enqueue(cudaStream_t stream, const kb2_tensor* inputs, int n_inputs, const kb2_tensor* outputs,
+                         int n_outputs) = 0;
+  virtual Status set_timestep(float) { return refuse(KB2_FORMAT_UNSUPPORTED, "this engine has no timestep"); }
+  virtual Status calibrate(cudaStream_t, const kb2_tensor&, float*, int) {
+    return refuse(KB2_FORMAT_UNSUPPORTED, "this engine does not calibrate");
+  }
+  Status check_device(cudaStream_t stream, int32_t* code);
+  virtual Status set_profiling(bool) { return refuse(KB2_FORMAT_UNSUPPORTED, "no profiling"); }
+  virtual Status read_profile(kb2_layer_profile*, int, int* count) {
+    *count = 0;
+    return refuse(KB2_FORMAT_UNSUPPORTED, "no profiling");
+  }
+  virtual int launches_per_enqueue() const = 0;
+
+ protected:
+  // Validates the frame tensors of an enqueue: n_frames_in inputs F16 [n,3,H,W], one output
+  // F16 [n,3,H*out_scale,W*out_scale], n <= max_batch, 16-byte aligned.
+  Status frame_io(const kb2_tensor* inputs, int n_in, const kb2_tensor* outputs, int n_out, int n_frames_in,
+                  int out_scale, void** in_ptrs, void** out_ptr, int* batch) const;
+  virtual int* err_word() const = 0;
+};
+
+Status make_engine(const kb2_engine_desc& desc, std::unique_ptr<Engine>& out);
+
+}  // namespace kb2

@@ -1,0 +1,362 @@
+// Canonical SPAN x2 on the tensor-core conv layers: the network driver that replaces the reference's
+// SpanFp8Net facade (src/gpu/cuda/backend/span_fp8_net.h:107-175) and its native16 / FP8 bodies
+// (span_native16.cu, span_fp8_body.cuh).
+//
+// Launch sequence (all batch-wide):
+//   pack      NCHW F16 frame -> row-chunked [n][y][2][x][8] (channels 3..15 zero)
+//   conv_1    3x3 3->48                                                     -> S0
+//   block b   c1 3x3 + SiLU -> T1; c2 3x3 + SiLU -> T2;
+//             c3 3x3 then (c3 + x)(sigmoid(c3) - 0.5), x the block input    -> X(b+1)
+//   conv_cat  1x1 over the four sources [S0, X6, X1, T1 of the last block], no concat buffer
+//   upsampler 3x3 48->12 + PixelShuffle(2) in the epilogue                  -> NCHW F16 [n][3][2H][2W]
+// The concat order is the reference's span_fp8::forward (src/gpu/span_fp8/forward.cpp:158-160).
+//
+// Precision. FP16 engine: FP16 operands and activations, FP32 accumulation. FP8 engine: blocks 1..5
+// run E4M3 x E4M3 -> FP32 (per-tensor activation scales, per-output-channel weight scales); conv_1,
+// block 0, conv_cat and the upsampler stay FP16, and every conv_cat source is kept in FP16 (layers
+// whose output feeds both an E4M3 conv and conv_cat write both copies). The reference keeps the same
+// FP16 ends (conv_1, conv_cat, to_pixel; src/gpu/span_fp8/package.h:12-16); block 0 is added to
+// them because with the seeded weights the deep blocks decay to ~0 and the output is carried by
+// conv_1 and block 0, whose E4M3 rounding alone would cost the 45 dB bar.
+#include <cuda_fp16.h>
+
+#include "span_net.h"
+
+namespace kb2 {
+
+namespace {
+
+// NCHW half [n][3][H][W] -> [n][H][2][W][8] half (16 channels, 3 real).
+__global__ void pack_frame_kernel(const __half* __restrict__ in, uint8_t* __restrict__ out, int batch, int H,
+                                  int W) {
+  const long long total = static_cast<long long>(batch) * H * W;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int x = static_cast<int>(i % W);
+    const long long t = i / W;
+    const int y = static_cast<int>(t % H);
+    const int n = static_cast<int>(t / H);
+    const size_t plane = static_cast<size_t>(H) * W;
+    const __half* src = in + static_cast<size_t>(n) * 3 * plane + static_cast<size_t>(y) * W + x;
+    const __half z = __float2half_rn(0.0f);
+    __half v[8] = {src[0], src[plane], src[2 * plane], z, z, z, z, z};
+    uint8_t* row = out + (static_cast<size_t>(n) * H + y) * 2 * W * 16;
+    *reinterpret_cast<uint4*>(row + static_cast<size_t>(x) * 16) = *reinterpret_cast<const uint4*>(v);
+    *reinterpret_cast<uint4*>(row + (static_cast<size_t>(W) + x) * 16) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// max |v| over an F16 chunked tensor -> atomicMax on the float bits (non-negative floats order as
+// unsigned integers).
+__global__ void absmax_f16_kernel(const __half2* __restrict__ v, size_t n2, unsigned int* out) {
+  float m = 0.0f;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n2;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float2 f = __half22float2(v[i]);
+    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+}  // namespace
+
+Status SpanNet::make_tensor(std::unique_ptr<Tensor>& t, int chunks, bool fp8) {
+  t = std::make_unique<Tensor>();
+  t->t.batch = max_batch_;
+  t->t.H = H_;
+  t->t.W = W_;
+  t->t.chunks = chunks;
+  t->t.fp8 = fp8;
+  KB2_TRY(t->buf.alloc(t->t.bytes()));
+  KB2_CUDA(cudaMemset(t->buf.ptr, 0, t->t.bytes()));
+  t->t.ptr = t->buf.as<uint8_t>();
+  return Status::Ok();
+}
+
+Status SpanNet::create(const std::vector<float>& params, int precision, int max_batch, int H, int W,
+                       const float* act_scales, int n_scales) {
+  if (params.size() != kSpanParams) return refuse(KB2_WEIGHTS_INVALID, "SPAN: parameter count mismatch");
+  if (max_batch < 1 || H < 1 || W < 1 || H > 8192 || W > 8192)
+    return refuse(KB2_SHAPE_INVALID, "SPAN: frame size out of contract");
+  if (precision != KB2_PREC_FP16 && precision != KB2_PREC_FP8_E4M3)
+    return refuse(KB2_FORMAT_UNSUPPORTED, "SPAN: unknown precision");
+  fp8_ = precision == KB2_PREC_FP8_E4M3;
+  scales_.assign(kSpanScales, 1.0f);
+  if (fp8_) {
+    if (act_scales == nullptr || n_scales != kSpanScales)
+      return refuse(KB2_INPUT_MISMATCH, "SPAN FP8: 19 activation scales required");
+    for (int i = 0; i < kSpanScales; ++i)
+      if (!(act_scales[i] > 0.0f) || !std::isfinite(act_scales[i]))
+        return refuse(KB2_INPUT_MISMATCH, "SPAN FP8: scales must be positive and finite");
+    scales_.assign(act_scales, act_scales + kSpanScales);
+  }
+  max_batch_ = max_batch;
+  H_ = H;
+  W_ = W;
+  KB2_TRY(err_.alloc(sizeof(int)));
+  KB2_CUDA(cudaMemset(err_.ptr, 0, sizeof(int)));
+  KB2_TRY(peaks_.alloc(kSpanScales * sizeof(unsigned int)));
+
+  auto tensor = [&](int chunks, bool fp8, const ChunkedTensor** out) -> Status {
+    std::unique_ptr<Tensor> t;
+    KB2_TRY(make_tensor(t, chunks, fp8));
+    *out = &t->t;
+    tensors_.push_back(std::move(t));
+    return Status::Ok();
+  };
+  const ChunkedTensor *s0, *t1h, *t2h, *x1, *x1q = nullptr, *t1q = nullptr, *t2q = nullptr, *xa, *xb;
+  const ChunkedTensor *t1l, *t1lq = nullptr, *x6 = nullptr, *cat;
+  KB2_TRY(tensor(2, false, &img_));
+  KB2_TRY(tensor(6, false, &s0));
+  KB2_TRY(tensor(6, false, &t1h));
+  KB2_TRY(tensor(6, false, &t2h));
+  KB2_TRY(tensor(6, false, &x1));
+  KB2_TRY(tensor(6, false, &t1l));
+  KB2_TRY(tensor(6, false, &cat));
+  if (fp8_) {
+    KB2_TRY(tensor(3, true, &x1q));
+    KB2_TRY(tensor(3, true, &t1q));
+    KB2_TRY(tensor(3, true, &t2q));
+    KB2_TRY(tensor(3, true, &xa));
+    KB2_TRY(tensor(3, true, &xb));
+    KB2_TRY(tensor(3, true, &t1lq));
+    KB2_TRY(tensor(6, false, &x6));
+  } else {
+    KB2_TRY(tensor(6, false, &xa));
+    KB2_TRY(tensor(6, false, &xb));
+  }
+
+  // parameter offsets (oracle/nets.py span_param_shapes order)
+  const int c = 48;
+  const float* w1 = params.data();
+  const float* b1 = w1 + c * 3 * 9;
+  const float* blk = b1 + c;
+  const size_t conv48 = static_cast<size_t>(c) * c * 9 + c;
+  const float* wcat = blk + kSpanBlocks * 3 * conv48;
+  const float* bcat = wcat + c * 4 * c;
+  const float* wup = bcat + c;
+  const float* bup = wup + 12 * c * 9;
+
+  int* err = err_.as<int>();
+  auto add = [&](const ConvSpec& s, const float* w, const float* b, const float* in_scales,
+                 std::vector<const ChunkedTensor*> inputs, Step step) -> Status {
+    layers_.push_back(std::make_unique<ConvLayer>());
+    step.layer = layers_.back().get();
+    KB2_TRY(step.layer->build(s, w, b, nullptr, in_scales, inputs.data(), err));
+    // algorithmic work per output pixel: direct-conv MACs x 2; bytes = every input and output once
+    step.flops_px = 2.0 * s.n_sources * s.cin * s.n_real * s.taps;
+    double bytes = 0.0;
+    for (const ChunkedTensor* t : inputs) bytes += t->chunks * 16.0;
+    if (step.residual != nullptr) bytes += step.residual->chunks * 16.0;
+    bytes += step.out != nullptr ? step.out->chunks * 16.0 : s.n_real * 2.0;
+    if (step.out2 != nullptr) bytes += step.out2->chunks * 16.0;
+    step.bytes_px = bytes;
+    const char* precision = s.fp8 ? "fp8" : "fp16";
+    std::string name;
+    if (s.n_sources == 4) name = "span.conv_cat.fp16";
+    else if (s.out == kOutPixShuf2) name = "span.upsampler.fp16";
+    else if (s.cin == 3) name = "span.conv_1.fp16";
+    else if (s.epi == kEpiSpanAttn) name = std::string("span.block_gate.") + precision;
+    else name = std::string("span.block_conv.") + precision;
+    step.kind = kind_index(name.c_str());
+    steps_.push_back(step);
+    return Status::Ok();
+  };
+  auto spec = [&](int taps, bool fp8, int cin, int epi, int out) {
+    ConvSpec s;
+    s.taps = taps;
+    s.fp8 = fp8;
+    s.cin = cin;
+    s.n_real = c;
+    s.n_pad = c;
+    s.epi = epi;
+    s.out = out;
+    s.out_chunks = out == kOutE4m3Chunk ? 3 : 6;
+    s.out2_chunks = 3;
+    return s;
+  };
+  const int pk = fp8_ ? -1 : 0;  // calibration taps exist on the FP16 engine only
+  auto peak = [&](int i) { return pk < 0 ? -1 : i; };
+
+  // conv_1
+  KB2_TRY(add(spec(9, false, 3, kEpiBias, kOutF16Chunk), w1, b1, nullptr, {img_},
+              Step{nullptr, s0, nullptr, nullptr, 1.0f, 1.0f, peak(0)}));
+  // blocks
+  const ChunkedTensor* x_in = s0;
+  for (int b = 0; b < kSpanBlocks; ++b) {
+    const bool q = block_fp8(b);
+    const bool last = b == kSpanBlocks - 1;
+    const float* wk[3];
+    for (int k = 0; k < 3; ++k) wk[k] = blk + (static_cast<size_t>(b) * 3 + k) * conv48;
+    auto bias = [&](int k) { return wk[k] + static_cast<size_t>(c) * c * 9; };
+    const float sc_in = scales_[3 * b], sc_a1 = scales_[3 * b + 1], sc_a2 = scales_[3 * b + 2];
+    // c1 -> T1 (the last block's T1 is a conv_cat source: kept in FP16, plus its E4M3 copy)
+    const ChunkedTensor* t1 = q ? (last ? t1lq : t1q) : (last ? t1l : t1h);
+    if (q && last) {
+      KB2_TRY(add(spec(9, true, c, kEpiSilu, kOutF16E4m3), wk[0], bias(0), &sc_in, {x_in},
+                  Step{nullptr, t1l, t1lq, nullptr, 1.0f / sc_a1, 1.0f, -1}));
+    } else {
+      KB2_TRY(add(spec(9, q, c, kEpiSilu, q ? kOutE4m3Chunk : kOutF16Chunk), wk[0], bias(0), q ? &sc_in : nullptr,
+                  {x_in}, Step{nullptr, t1, nullptr, nullptr, q ? 1.0f / sc_a1 : 1.0f, 1.0f, peak(3 * b + 1)}));
+    }
+    // c2 -> T2
+    const ChunkedTensor* t2 = q ? t2q : t2h;
+    KB2_TRY(add(spec(9, q, c, kEpiSilu, q ? kOutE4m3Chunk : kOutF16Chunk), wk[1], bias(1), q ? &sc_a1 : nullptr,
+                {t1}, Step{nullptr, t2, nullptr, nullptr, q ? 1.0f / sc_a2 : 1.0f, 1.0f, peak(3 * b + 2)}));
+    // c3 + gate -> block output
+    const float res_scale = q ? sc_in : 1.0f;
+    if (!fp8_) {
+      const ChunkedTensor* xo = b == 0 ? x1 : (b % 2 == 1 ? xa : xb);
+      KB2_TRY(add(spec(9, false, c, kEpiSpanAttn, kOutF16Chunk), wk[2], bias(2), nullptr, {t2},
+                  Step{nullptr, xo, nullptr, x_in, 1.0f, 1.0f, peak(3 * b + 3)}));
+      x6 = xo;
+      x_in = xo;
+    } else if (b == 0) {  // FP16 block 0: X1 in FP16 for conv_cat, E4M3 copy for block 1
+      KB2_TRY(add(spec(9, false, c, kEpiSpanAttn, kOutF16E4m3), wk[2], bias(2), nullptr, {t2},
+                  Step{nullptr, x1, x1q, x_in, 1.0f / scales_[3], 1.0f, -1}));
+      x_in = x1q;
+    } else if (!last) {
+      const ChunkedTensor* xo = b % 2 == 1 ? xa : xb;
+      KB2_TRY(add(spec(9, true, c, kEpiSpanAttn, kOutE4m3Chunk), wk[2], bias(2), &sc_a2, {t2},
+                  Step{nullptr, xo, nullptr, x_in, 1.0f / scales_[3 * b + 3], res_scale, -1}));
+      x_in = xo;
+    } else {
+      KB2_TRY(add(spec(9, true, c, kEpiSpanAttn, kOutF16Chunk), wk[2], bias(2), &sc_a2, {t2},
+                  Step{nullptr, x6, nullptr, x_in, 1.0f, res_scale, -1}));
+    }
+  }
+  {  // conv_cat: FP16 1x1 over four FP16 sources
+    ConvSpec s = spec(1, false, c, kEpiBias, kOutF16Chunk);
+    s.n_sources = 4;
+    KB2_TRY(add(s, wcat, bcat, nullptr, {s0, x6, x1, t1l}, Step{nullptr, cat, nullptr, nullptr, 1.0f, 1.0f, -1}));
+  }
+  {  // upsampler + PixelShuffle(2)
+    ConvSpec s = spec(9, false, c, kEpiBias, kOutPixShuf2);
+    s.n_real = 12;
+    s.n_pad = 16;
+    KB2_TRY(add(s, wup, bup, nullptr, {cat}, Step{nullptr, nullptr, nullptr, nullptr, 1.0f, 1.0f, -1}));
+  }
+  return Status::Ok();
+}
+
+size_t SpanNet::device_bytes() const {
+  size_t total = 0;
+  for (const auto& t : tensors_) total += t->buf.bytes;
+  for (const auto& l : layers_) total += l->wpack.bytes + l->bias.bytes + l->scale.bytes + l->slope.bytes;
+  return total;
+}
+
+Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, bool capture_peaks) {
+  if (batch < 1 || batch > max_batch_) return refuse(KB2_SHAPE_INVALID, "SPAN: batch out of contract");
+  {
+    const long long px = static_cast<long long>(batch) * H_ * W_;
+    long long blocks = (px + 255) / 256;
+    if (blocks > 65535LL * 16) blocks = 65535LL * 16;
+    const double px_b = static_cast<double>(px);
+    if (profiling_) KB2_TRY(timed(kind_index("span.pack"), 0.0, 0.0, stream, true));
+    pack_frame_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const __half*>(in),
+                                                                       img_->ptr, batch, H_, W_);
+    KB2_CUDA(cudaGetLastError());
+    if (profiling_) KB2_TRY(timed(kind_index("span.pack"), 0.0, px_b * (6.0 + 32.0), stream, false));
+  }
+  const double pixels = static_cast<double>(batch) * H_ * W_;
+  unsigned int* peaks = peaks_.as<unsigned int>();
+  for (const Step& s : steps_) {
+    void* dst = s.out != nullptr ? static_cast<void*>(s.out->ptr) : out;
+    if (profiling_) KB2_TRY(timed(s.kind, 0.0, 0.0, stream, true));
+    KB2_TRY(s.layer->launch(stream, batch, dst, s.residual != nullptr ? s.residual->ptr : nullptr, s.out_inv_scale,
+                            s.res_scale, s.out2 != nullptr ? s.out2->ptr : nullptr));
+    if (profiling_) KB2_TRY(timed(s.kind, s.flops_px * pixels, s.bytes_px * pixels, stream, false));
+    if (capture_peaks && s.peak >= 0) {
+      const size_t n2 = static_cast<size_t>(batch) * H_ * s.out->chunks * W_ * 4;  // 4 half2 per chunk
+      absmax_f16_kernel<<<4 * num_sms(), 256, 0, stream>>>(reinterpret_cast<const __half2*>(s.out->ptr), n2,
+                                                          peaks + s.peak);
+      KB2_CUDA(cudaGetLastError());
+    }
+  }
+  return Status::Ok();
+}
+
+int SpanNet::kind_index(const char* name) {
+  for (size_t i = 0; i < kinds_.size(); ++i)
+    if (kinds_[i].name == name) return static_cast<int>(i);
+  kinds_.push_back(Profile{name});
+  return static_cast<int>(kinds_.size()) - 1;
+}
+
+Status SpanNet::timed(int kind, double flops, double bytes, cudaStream_t stream, bool begin) {
+  auto take = [&](cudaEvent_t* e) -> Status {
+    if (!event_pool_.empty()) {
+      *e = event_pool_.back();
+      event_pool_.pop_back();
+      return Status::Ok();
+    }
+    return cuda_status(cudaEventCreate(e), "cudaEventCreate");
+  };
+  if (begin) {
+    KB2_TRY(take(&open_start_));
+    return cuda_status(cudaEventRecord(open_start_, stream), "cudaEventRecord");
+  }
+  cudaEvent_t stop = nullptr;
+  KB2_TRY(take(&stop));
+  KB2_CUDA(cudaEventRecord(stop, stream));
+  pending_.push_back(Pending{kind, open_start_, stop, flops, bytes});
+  open_start_ = nullptr;
+  return Status::Ok();
+}
+
+Status SpanNet::read_profile(std::vector<Profile>& out) {
+  for (const Pending& p : pending_) {
+    KB2_CUDA(cudaEventSynchronize(p.stop));
+    float ms = 0.0f;
+    KB2_CUDA(cudaEventElapsedTime(&ms, p.start, p.stop));
+    Profile& k = kinds_[p.kind];
+    k.launches += 1;
+    k.ms += ms;
+    k.flops = p.flops;
+    k.bytes = p.bytes;
+    event_pool_.push_back(p.start);
+    event_pool_.push_back(p.stop);
+  }
+  pending_.clear();
+  out = kinds_;
+  for (Profile& k : kinds_) {
+    k.launches = 0;
+    k.ms = 0.0;
+  }
+  return Status::Ok();
+}
+
+SpanNet::~SpanNet() {
+  for (const Pending& p : pending_) {
+    cudaEventDestroy(p.start);
+    cudaEventDestroy(p.stop);
+  }
+  for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
+}
+
+Status SpanNet::calibrate(cudaStream_t stream, const void* frames, int n, float* peaks_out) {
+  if (fp8_) return refuse(KB2_FORMAT_UNSUPPORTED, "calibration runs on the FP16 engine");
+  std::vector<float> best(kSpanScales, 0.0f);
+  DeviceBuffer scratch;
+  KB2_TRY(scratch.alloc(static_cast<size_t>(max_batch_) * 3 * 4 * H_ * W_ * 2));
+  for (int i = 0; i < n; i += max_batch_) {
+    const int batch = n - i < max_batch_ ? n - i : max_batch_;
+    KB2_CUDA(cudaMemsetAsync(peaks_.ptr, 0, kSpanScales * sizeof(unsigned int), stream));
+    const uint8_t* src = static_cast<const uint8_t*>(frames) + static_cast<size_t>(i) * 3 * H_ * W_ * 2;
+    KB2_TRY(run(stream, src, scratch.ptr, batch, true));
+    unsigned int bits[kSpanScales];
+    KB2_CUDA(cudaMemcpyAsync(bits, peaks_.ptr, sizeof(bits), cudaMemcpyDeviceToHost, stream));
+    KB2_CUDA(cudaStreamSynchronize(stream));
+    for (int k = 0; k < kSpanScales; ++k) {
+      float f;
+      std::memcpy(&f, &bits[k], 4);
+      best[k] = std::fmax(best[k], f);
+    }
+  }
+  std::memcpy(peaks_out, best.data(), kSpanScales * sizeof(float));
+  return Status::Ok();
+}
+
+}  // namespace kb2

@@ -1,0 +1,202 @@
+"""Python mirror of the C ABI in include/kirari_b200.h (ctypes), with torch for device memory.
+
+This is the host-side interface the tests and the benchmark use: the same calls a C++ player makes
+through the header (create with a weight blob, enqueue device frames on a stream, read refusals).
+The library it loads is the in-tree libkirari_b200.so; there is no other backend and no CPU
+fallback: if the library is missing, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import struct
+import zlib
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkirari_b200.so")
+
+KB2_OK = 0
+KB2_SHAPE_INVALID = 1
+KB2_INPUT_MISMATCH = 2
+KB2_FORMAT_UNSUPPORTED = 3
+KB2_GPU_MEMORY_EXHAUSTED = 4
+KB2_VENDOR_CALL_FAILED = 5
+KB2_WEIGHTS_INVALID = 6
+KB2_KERNEL_TIMEOUT = 7
+KB2_INVALID_ARGUMENT = 8
+
+KB2_F32, KB2_F16, KB2_U8, KB2_I8 = 0, 1, 2, 3
+MODEL_SPAN_X2 = 1
+MODEL_IFNET = 2
+PREC_FP16 = 1
+PREC_FP8 = 2
+
+# every entry point of include/kirari_b200.h
+EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "kb2_last_error",
+           "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
+           "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue")
+
+
+class KB2Error(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"kb2 status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_int32), ("dims", ctypes.c_int64 * 4), ("handle", ctypes.c_uint64),
+                ("offset", ctypes.c_uint64)]
+
+
+class EngineDesc(ctypes.Structure):
+    _fields_ = [("model", ctypes.c_int32), ("precision", ctypes.c_int32), ("max_batch", ctypes.c_int32),
+                ("height", ctypes.c_int32), ("width", ctypes.c_int32), ("device", ctypes.c_int32),
+                ("weights", ctypes.c_void_p), ("weights_bytes", ctypes.c_uint64),
+                ("act_scales", ctypes.POINTER(ctypes.c_float)), ("act_scale_count", ctypes.c_int32)]
+
+
+class LayerProfile(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 48), ("launches", ctypes.c_uint64), ("total_ms", ctypes.c_double),
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
+
+
+_lib = None
+
+
+def lib():
+    """Loads libkirari_b200.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} not built: run `python ultimate-anime-videoplayer_b200/build.py`")
+        L = ctypes.CDLL(LIB_PATH)
+        L.kb2_abi_version.restype = ctypes.c_int
+        L.kb2_create.argtypes = [ctypes.POINTER(EngineDesc), ctypes.POINTER(ctypes.c_void_p)]
+        L.kb2_create_error.restype = ctypes.c_char_p
+        L.kb2_destroy.argtypes = [ctypes.c_void_p]
+        L.kb2_last_error.argtypes = [ctypes.c_void_p]
+        L.kb2_last_error.restype = ctypes.c_char_p
+        L.kb2_workspace_bytes.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
+        L.kb2_enqueue.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.c_int32,
+                                  ctypes.POINTER(Tensor), ctypes.c_int32]
+        L.kb2_set_timestep.argtypes = [ctypes.c_void_p, ctypes.c_float]
+        L.kb2_check_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
+        L.kb2_span_calibrate.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Tensor),
+                                         ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
+        L.kb2_set_profiling.argtypes = [ctypes.c_void_p, ctypes.c_int32]
+        L.kb2_read_profile.argtypes = [ctypes.c_void_p, ctypes.POINTER(LayerProfile), ctypes.c_int32,
+                                       ctypes.POINTER(ctypes.c_int32)]
+        L.kb2_launches_per_enqueue.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
+        _lib = L
+    return _lib
+
+
+def make_blob(model: int, flat_params) -> bytes:
+    """Weight blob v1: 'KB2WGT01', u32 version 1, u32 model, u64 count, u32 CRC-32, u32 0, floats."""
+    payload = np.ascontiguousarray(flat_params, dtype="<f4").tobytes()
+    header = b"KB2WGT01" + struct.pack("<IIQII", 1, model, len(payload) // 4, zlib.crc32(payload) & 0xFFFFFFFF, 0)
+    return header + payload
+
+
+def to_kb2_tensor(t) -> Tensor:
+    """torch CUDA tensor -> kb2_tensor (NCHW, contiguous)."""
+    import torch
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    dtype = {torch.float16: KB2_F16, torch.float32: KB2_F32, torch.uint8: KB2_U8, torch.int8: KB2_I8}[t.dtype]
+    dims = list(t.shape) + [1] * (4 - t.dim())
+    return Tensor(dtype, (ctypes.c_int64 * 4)(*dims), t.data_ptr(), 0)
+
+
+def _stream_handle(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+class Engine:
+    """An engine of the C ABI (SPAN x2 or IFNet)."""
+
+    def __init__(self, model, blob: bytes, height, width, max_batch=1, precision=PREC_FP16, act_scales=None,
+                 device=0):
+        self._blob = ctypes.create_string_buffer(blob, len(blob))
+        self._scales = None
+        n_scales = 0
+        if act_scales is not None:
+            arr = np.ascontiguousarray(act_scales, np.float32)
+            self._scales = (ctypes.c_float * arr.size)(*arr.tolist())
+            n_scales = arr.size
+        desc = EngineDesc(model, precision, max_batch, height, width, device,
+                          ctypes.cast(self._blob, ctypes.c_void_p), len(blob),
+                          ctypes.cast(self._scales, ctypes.POINTER(ctypes.c_float)) if self._scales else None,
+                          n_scales)
+        h = ctypes.c_void_p()
+        rc = lib().kb2_create(ctypes.byref(desc), ctypes.byref(h))
+        if rc != KB2_OK:
+            raise KB2Error(rc, lib().kb2_create_error().decode(errors="replace"))
+        self.h = h
+        self.height, self.width, self.max_batch = height, width, max_batch
+
+    def _check(self, rc):
+        if rc != KB2_OK:
+            raise KB2Error(rc, lib().kb2_last_error(self.h).decode(errors="replace"))
+
+    def enqueue(self, inputs, outputs, stream=None):
+        ins = (Tensor * len(inputs))(*[to_kb2_tensor(t) for t in inputs])
+        outs = (Tensor * len(outputs))(*[to_kb2_tensor(t) for t in outputs])
+        self._check(lib().kb2_enqueue(self.h, _stream_handle(stream), ins, len(inputs), outs, len(outputs)))
+
+    def enqueue_raw(self, ins, outs, stream_handle):
+        """Pre-built kb2_tensor arrays (no per-call marshalling), for timing loops."""
+        self._check(lib().kb2_enqueue(self.h, stream_handle, ins, len(ins), outs, len(outs)))
+
+    def set_timestep(self, t):
+        self._check(lib().kb2_set_timestep(self.h, float(t)))
+
+    def check_device(self, stream=None):
+        code = ctypes.c_int32(0)
+        rc = lib().kb2_check_device(self.h, _stream_handle(stream), ctypes.byref(code))
+        if rc != KB2_OK:
+            raise KB2Error(rc, f"device error word {code.value:#x}")
+
+    def workspace_bytes(self):
+        v = ctypes.c_uint64(0)
+        self._check(lib().kb2_workspace_bytes(self.h, ctypes.byref(v)))
+        return v.value
+
+    def calibrate(self, frames, stream=None):
+        peaks = (ctypes.c_float * 19)()
+        t = to_kb2_tensor(frames)
+        self._check(lib().kb2_span_calibrate(self.h, _stream_handle(stream), ctypes.byref(t), peaks, 19))
+        return np.array(peaks[:], np.float32)
+
+    def set_profiling(self, on=True):
+        self._check(lib().kb2_set_profiling(self.h, 1 if on else 0))
+
+    def read_profile(self):
+        """{name: dict(launches, total_ms, flops, bytes)} since profiling was enabled / last read."""
+        recs = (LayerProfile * 64)()
+        n = ctypes.c_int32(0)
+        self._check(lib().kb2_read_profile(self.h, recs, 64, ctypes.byref(n)))
+        return {recs[i].name.decode(): dict(launches=recs[i].launches, total_ms=recs[i].total_ms,
+                                            flops=recs[i].flops, bytes=recs[i].bytes) for i in range(min(n.value, 64))}
+
+    def launches_per_enqueue(self):
+        n = ctypes.c_int32(0)
+        self._check(lib().kb2_launches_per_enqueue(self.h, ctypes.byref(n)))
+        return n.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().kb2_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
