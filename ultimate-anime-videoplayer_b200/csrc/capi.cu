@@ -5,7 +5,7 @@
 #include <new>
 #include <string>
 
-#include "../../include/kirari_b200.h"
+#include "kirari_b200.h"
 #include "engine.h"
 
 namespace {

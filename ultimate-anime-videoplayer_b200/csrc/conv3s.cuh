@@ -1,0 +1,289 @@
+// 3x3 convolution with the kernel rows stacked along N (sm_100a, tcgen05 + TMEM + TMA).
+//
+// Why: a tcgen05.mma of M = 128 costs at least ~45 cycles whatever N is below ~96 (measured on
+// B200; at N >= 128 it runs at the tensor rate, N / 2 cycles for K = 16). SPAN's convolutions have
+// 48 output channels, so the plain implicit GEMM (conv_tc.cuh) spends half of each instruction idle.
+// Here every input row is multiplied once by the three kernel rows at the same time:
+//
+//     B = [ W(dy = +1) | W(dy = 0) | W(dy = -1) ]      (N = 3 x 48 = 144 rows of weights)
+//
+// and the three 48-column results land in the accumulators of the three output rows that input row
+// feeds (o = t - 2, t - 1, t for input row index t of a band), which sit side by side in a TMEM
+// ring of output-row slots. An output row is complete after its third input row; the epilogue then
+// reads it and releases the slot. Per input row the work is kx * channel steps = 9 (FP16) or 5 (E4M3) instructions of N = 144,
+// tensor-bound, and each input row is read from shared memory exactly once. The first K step is
+// issued per 48-row block so that the block opening a fresh output row can overwrite its slot
+// (every other instruction accumulates), which spares zeroing the slots. Band edges use the one- or
+// two-block sub-ranges of B (N = 48 / 96), and an instruction whose three slots would wrap around
+// the end of the ring is split in two.
+//
+// Roles as in conv_tc.cuh: warp 0 = TMA producer (same row slots), warp 1 = TMEM owner + MMA issuer,
+// warps 2.. = epilogue (4 per kStackEpiCols output channels) with the same fused epilogues.
+#pragma once
+
+#include "conv_tc.cuh"
+
+namespace kb2 {
+
+// One block per SM owning all 512 TMEM columns, with one epilogue warp per 32 lanes x 8 output
+// columns. Measured on 8 x 1080p: two blocks per SM (256 columns and 16-column epilogue warps
+// each) made the plain conv 7% faster but the gated conv 55% slower (the wider epilogue warps
+// spill and serialise the residual reads), so the single-block shape is kept.
+constexpr int kStackBlocksPerSm = 1;
+constexpr int kStackEpiCols = 8;
+constexpr uint32_t kStackTmemCols = 512 / kStackBlocksPerSm;
+
+template <int kCoutPad>
+struct StackShape {
+  static constexpr int epi_warps = 4 * (kCoutPad / kStackEpiCols);  // 4 quadrants x column groups
+  static constexpr int threads = 64 + 32 * epi_warps;
+  static constexpr int max_slots = static_cast<int>(kStackTmemCols) / kCoutPad < 24
+                                       ? static_cast<int>(kStackTmemCols) / kCoutPad
+                                       : 24;
+};
+
+constexpr int kRowMaxK = 12;  // K steps per input row (FP16 48 channels: 9; E4M3: 5; conv_1: 3)
+
+constexpr uint32_t kStackSmemExtra = 1024 + 128 * 8 + (kMaxKSteps + 1) * 8 + 3 * kMaxN * 4 + 64;
+
+template <bool kFp8, int kCoutPad, int kEpi, int kOut>
+__global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPerSm)
+    conv3s_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
+  static_assert(kCoutPad == 16 || kCoutPad == 48, "stacked kernel: 16 or 48 output channels");
+  constexpr int kEpiWarps = StackShape<kCoutPad>::epi_warps;
+  constexpr int kN = 3 * kCoutPad;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sw = smem;
+  uint8_t* ring = smem + a.w_smem;
+  const uint32_t R = static_cast<uint32_t>(a.acc_slots);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + a.ring * a.slot_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + a.ring;
+  uint64_t* acc_full = bars + 2 * a.ring;
+  uint64_t* slot_free = acc_full + R;
+  uint64_t* wbar = slot_free + R;
+  uint64_t* drain = wbar + 1;
+  uint64_t* s_k = bars + 128;  // per K step of a row: (a_off >> 4) | (lbo >> 4) << 16
+  float* s_bias = reinterpret_cast<float*>(s_k + kMaxKSteps + 1);
+  float* s_scale = s_bias + kMaxN;
+  float* s_slope = s_scale + kMaxN;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_slope + kMaxN);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < a.ring; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (uint32_t i = 0; i < R; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&slot_free[i], kEpiWarps);
+    }
+    mbar_init(wbar, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
+    s_bias[j] = j < kCoutPad ? a.bias[j] : 0.0f;
+    s_scale[j] = (a.chan_scale != nullptr && j < kCoutPad) ? a.chan_scale[j] : 1.0f;
+    s_slope[j] = (a.slope != nullptr && j < kCoutPad) ? a.slope[j] : 0.0f;
+  }
+  for (int j = threadIdx.x; j <= kMaxKSteps; j += blockDim.x)
+    s_k[j] = j < a.n_ksteps
+                 ? (static_cast<uint64_t>(a.ks[j].a_off >> 4) | (static_cast<uint64_t>(a.ks[j].lbo >> 4) << 16))
+                 : 0;
+  if (warp == 0 && lane == 0) prefetch_tmap(&maps.m[0]);
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kStackTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ producer (rows y0-1 .. y1)
+      bool ok = true;
+      mbar_arrive_expect_tx(wbar, a.wbytes);
+      for (uint32_t off = 0; off < a.wbytes; off += 32768u) {
+        const uint32_t len = a.wbytes - off < 32768u ? a.wbytes - off : 32768u;
+        bulk_load(sw + off, a.wpack + off, len, wbar);
+      }
+      // ring positions are carried as (slot, phase) counters: an integer division by a runtime
+      // divisor costs this single thread hundreds of cycles per row
+      RingPos in{0, 0};
+      uint32_t issued = 0;
+      for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
+        const int strip = item % a.strips;
+        const int t = item / a.strips;
+        const int band = t % a.bands;
+        const int n = t / a.bands;
+        const int y0 = band * a.band_rows;
+        const int y1 = min(a.H, y0 + a.band_rows);
+        const int x0 = strip * a.strip_w;
+        for (int r = y0 - 1; r <= y1; ++r) {
+          if (!wait_bar(&empty[in.idx], in.phase ^ 1u, a.err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[in.idx], a.slot_bytes);
+          // one box: 128 pixels from x0 - 1 (zero fill left of the image), all chunks
+          tma_load_4d(ring + in.idx * a.slot_bytes, &maps.m[0], &full[in.idx], (x0 - 1) * 2, 0, r, n);
+          in.advance(a.ring);
+          ++issued;
+        }
+      }
+      // every copy issued has landed before the block may exit: wait for the last ring's worth
+      RingPos back = in;
+      for (uint32_t k = 0; k < a.ring && k < issued; ++k) {
+        back.retreat(a.ring);
+        wait_bar(&full[back.idx], back.phase, a.err, kErrWaitDrain);
+      }
+      wait_bar(wbar, 0, a.err, kErrWaitDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      bool ok = wait_bar(wbar, 0, a.err, kErrWaitMma);
+      const uint32_t ring_base = smem_u32(ring);
+      const uint64_t desc_hi = make_sdesc(0, 0, 128);
+      const uint64_t b_desc0 = make_sdesc(smem_u32(sw), kN * 16, 128);
+      constexpr uint64_t kBStep16 = (2u * kN * 16u) >> 4;   // one K step of B
+      constexpr uint64_t kBlock16 = (kCoutPad * 16u) >> 4;  // one kernel-row block of B
+      const int n_k = a.n_ksteps;
+      uint64_t kd[kRowMaxK];  // per-row K-step deltas, in registers
+#pragma unroll
+      for (int j = 0; j < kRowMaxK; ++j) kd[j] = s_k[j];
+      const uint32_t id_n[3] = {a.idesc_n[0], a.idesc_n[1], a.idesc_n[2]};
+      RingPos in{0, 0};
+      RingPos acc{0, 0};  // accumulator slot (and phase) of output row t, the row first touched by input t
+      for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
+        const int t0 = item / a.strips;
+        const int band = t0 % a.bands;
+        const int y0 = band * a.band_rows;
+        const int y1 = min(a.H, y0 + a.band_rows);
+        const int rows = y1 - y0;
+        for (int t = 0; t <= rows + 1; ++t) {
+          if (!wait_bar(&full[in.idx], in.phase, a.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          // blocks [b0, b1) of B feed output rows t - 2 + b0 .. t - 2 + b1 - 1 of the band
+          const int b0 = t >= 2 ? 0 : 2 - t;
+          const int b1 = t <= rows - 1 ? 3 : (t == rows ? 2 : 1);
+          if (b1 == 3) {  // output row t is touched for the first time: its slot must have been read
+            if (!wait_bar(&slot_free[acc.idx], acc.phase, a.err, kErrWaitMma)) {
+              ok = false;
+              break;
+            }
+          }
+          tc_fence_after();
+          // slot of output t - 2 + b0 (acc.idx is the slot of output t)
+          const uint32_t back = static_cast<uint32_t>(2 - b0);
+          const uint32_t s_first = acc.idx >= back ? acc.idx - back : acc.idx + R - back;
+          const uint32_t nb = static_cast<uint32_t>(b1 - b0);
+          const uint32_t nb1 = nb < R - s_first ? nb : R - s_first;  // blocks before the ring wraps
+          const uint32_t nb2 = nb - nb1;
+          const uint64_t a_row = desc_hi | static_cast<uint64_t>((ring_base + in.idx * a.slot_bytes) >> 4);
+          const uint64_t b_first = b_desc0 + static_cast<uint64_t>(b0) * kBlock16;
+          const uint32_t d1 = tmem_base + s_first * kCoutPad;
+          const uint32_t id1 = nb1 == 3 ? id_n[2] : (nb1 == 2 ? id_n[1] : id_n[0]);
+          // K step 0, one instruction per block: the block of a fresh output row (b1 == 3, block
+          // 2) overwrites its slot, the others accumulate -- so slots never need zeroing
+          {
+            uint32_t slot = s_first;
+            for (int blk = b0; blk < b1; ++blk) {
+              const uint32_t fresh = (b1 == 3 && blk == 2) ? 1u : 0u;
+              mma_ss<kFp8>(tmem_base + slot * kCoutPad, a_row + kd[0], b_desc0 + static_cast<uint64_t>(blk) * kBlock16,
+                           id_n[0], fresh ^ 1u);
+              slot = slot + 1 == R ? 0 : slot + 1;
+            }
+          }
+#pragma unroll
+          for (int j = 1; j < kRowMaxK; ++j)
+            if (j < n_k) mma_ss<kFp8>(d1, a_row + kd[j], b_first + static_cast<uint64_t>(j) * kBStep16, id1, 1u);
+          if (nb2 > 0) {  // the blocks past the end of the ring go to slot 0
+            const uint32_t id2 = nb2 == 2 ? id_n[1] : id_n[0];
+            const uint64_t b_second = b_first + static_cast<uint64_t>(nb1) * kBlock16;
+#pragma unroll
+            for (int j = 1; j < kRowMaxK; ++j)
+              if (j < n_k) mma_ss<kFp8>(tmem_base, a_row + kd[j], b_second + static_cast<uint64_t>(j) * kBStep16, id2, 1u);
+          }
+          mma_commit(&empty[in.idx]);  // the input row is no longer needed
+          if (t >= 2) mma_commit(&acc_full[acc.idx >= 2 ? acc.idx - 2 : acc.idx + R - 2]);  // output t-2 done
+          in.advance(a.ring);
+          acc.advance(R);  // acc tracks output row t + 1 (virtual past the band's last row)
+        }
+        if (!ok) break;
+        // inputs rows and rows + 1 advanced past the band's last output: step back to the next
+        // band's first output row
+        acc.retreat(R);
+        acc.retreat(R);
+      }
+      mma_commit(drain);
+      wait_bar(drain, 0, a.err, kErrWaitDrain);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const int col0 = ((warp - 2) >> 2) * kStackEpiCols;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    // this warp's per-channel constants, held in registers for the whole kernel (reading them from
+    // shared memory on every row cost ~9% of the plain conv)
+    float r_bias[kStackEpiCols], r_scale[kStackEpiCols], r_slope[kStackEpiCols];
+#pragma unroll
+    for (int j = 0; j < kStackEpiCols; ++j) {
+      r_bias[j] = s_bias[col0 + j];
+      r_scale[j] = s_scale[col0 + j];
+      r_slope[j] = s_slope[col0 + j];
+    }
+    // every slot starts free (phase 0 of slot_free)
+    if (lane == 0)
+      for (uint32_t s = 0; s < R; ++s) mbar_arrive(&slot_free[s]);
+    RingPos acc{0, 0};
+    bool ok = true;
+    for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
+      const int strip = item % a.strips;
+      const int t = item / a.strips;
+      const int band = t % a.bands;
+      const int n = t / a.bands;
+      const int y0 = band * a.band_rows;
+      const int y1 = min(a.H, y0 + a.band_rows);
+      const int m = quad * 32 + lane;
+      const int x = strip * a.strip_w + m;
+      const bool store = m < a.strip_w && x < a.W;
+      for (int y = y0; y < y1; ++y, acc.advance(R)) {
+        const uint32_t s = acc.idx;
+        const bool got = wait_bar(&acc_full[s], acc.phase, a.err, kErrWaitEpilogue);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float v[kStackEpiCols];
+        const uint32_t taddr = tmem_base + lane_addr + s * kCoutPad + static_cast<uint32_t>(col0);
+        if constexpr (kStackEpiCols == 16) tmem_ld16(taddr, v); else tmem_ld8(taddr, v);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&slot_free[s]);
+        if (store) epilogue_cols<kEpi, kOut, kStackEpiCols>(a, r_bias, r_scale, r_slope, v, 0, n, y, x, col0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kStackTmemCols);
+  }
+}
+
+}  // namespace kb2

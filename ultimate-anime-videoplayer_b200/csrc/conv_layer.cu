@@ -2,9 +2,11 @@
 // channel chunk each 32-byte K step of an MMA reads), the matching weight packing (FP16, or E4M3 with
 // per-output-channel scales as span_fp8::channel_scales, src/gpu/span_fp8/quantize.h:1-5), the TMA
 // tensor maps and the persistent launch.
+#include <algorithm>
 #include <array>
 #include <cstdio>
 
+#include "conv3s.cuh"
 #include "conv_layer.h"
 
 namespace kb2 {
@@ -42,36 +44,58 @@ std::vector<std::array<Half, 2>> make_ksteps(const ConvSpec& s, int chunks) {
   return steps;
 }
 
-using LaunchFn = void (*)(dim3, size_t, cudaStream_t, const CUtensorMap*, const ConvArgs&);
-using Kernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, ConvArgs);
+using LaunchFn = void (*)(dim3, size_t, cudaStream_t, const ConvMaps&, const ConvArgs&);
 
 template <bool F8, int N, int E, int O>
-void launch_impl(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap* m, const ConvArgs& a) {
-  conv_tc_kernel<F8, N, E, O><<<grid, 192, smem, s>>>(m[0], m[1], m[2], m[3], a);
+void launch_impl(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
+  conv_tc_kernel<F8, N, E, O><<<grid, ConvShape<N>::threads, smem, s>>>(m, a);
+}
+template <bool F8, int N, int E, int O>
+void launch_stacked(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
+  conv3s_kernel<F8, N, E, O><<<grid, StackShape<N>::threads, smem, s>>>(m, a);
 }
 
 struct KernelEntry {
+  bool stacked;  // 3x3 single-source layer on the stacked-kernel-row kernel (conv3s.cuh)
   bool fp8;
   int n, epi, out;
   LaunchFn launch;
   const void* fn;
+  int threads;
 };
 
-#define KB2_KERNEL(F8, N, E, O) \
-  KernelEntry { F8, N, E, O, &launch_impl<F8, N, E, O>, reinterpret_cast<const void*>(&conv_tc_kernel<F8, N, E, O>) }
+#define KB2_KERNEL(F8, N, E, O)                                                                            \
+  KernelEntry {                                                                                            \
+    false, F8, N, E, O, &launch_impl<F8, N, E, O>, reinterpret_cast<const void*>(&conv_tc_kernel<F8, N, E, O>), \
+        ConvShape<N>::threads                                                                              \
+  }
+#define KB2_STACKED(F8, N, E, O)                                                                              \
+  KernelEntry {                                                                                               \
+    true, F8, N, E, O, &launch_stacked<F8, N, E, O>, reinterpret_cast<const void*>(&conv3s_kernel<F8, N, E, O>), \
+        StackShape<N>::threads                                                                                \
+  }
 
-// The instantiations the SPAN engines use (FP16 engine: the first four; FP8 engine: all).
+// The instantiations the SPAN engines use: 3x3 layers on the stacked kernel, the 1x1 conv_cat on
+// the generic one.
 const KernelEntry kKernels[] = {
-    KB2_KERNEL(false, 48, kEpiBias, kOutF16Chunk),     KB2_KERNEL(false, 48, kEpiSilu, kOutF16Chunk),
-    KB2_KERNEL(false, 48, kEpiSpanAttn, kOutF16Chunk), KB2_KERNEL(false, 16, kEpiBias, kOutPixShuf2),
-    KB2_KERNEL(false, 48, kEpiSpanAttn, kOutF16E4m3),  KB2_KERNEL(true, 48, kEpiSilu, kOutE4m3Chunk),
-    KB2_KERNEL(true, 48, kEpiSilu, kOutF16E4m3),       KB2_KERNEL(true, 48, kEpiSpanAttn, kOutE4m3Chunk),
-    KB2_KERNEL(true, 48, kEpiSpanAttn, kOutF16Chunk),
+    KB2_KERNEL(false, 48, kEpiBias, kOutF16Chunk),
+    KB2_STACKED(false, 48, kEpiBias, kOutF16Chunk),
+    KB2_STACKED(false, 48, kEpiSilu, kOutF16Chunk),
+    KB2_STACKED(false, 48, kEpiSpanAttn, kOutF16Chunk),
+    KB2_STACKED(false, 16, kEpiBias, kOutPixShuf2),
+    KB2_STACKED(false, 48, kEpiSpanAttn, kOutF16E4m3),
+    KB2_STACKED(true, 48, kEpiSilu, kOutE4m3Chunk),
+    KB2_STACKED(true, 48, kEpiSilu, kOutF16E4m3),
+    KB2_STACKED(true, 48, kEpiSpanAttn, kOutE4m3Chunk),
+    KB2_STACKED(true, 48, kEpiSpanAttn, kOutF16Chunk),
 };
+
+bool wants_stacked(const ConvSpec& s) { return s.taps == 9 && s.n_sources == 1 && (s.n_pad == 48 || s.n_pad == 16); }
 
 const KernelEntry* find_kernel(const ConvSpec& s) {
+  const bool st = wants_stacked(s);
   for (const KernelEntry& k : kKernels)
-    if (k.fp8 == s.fp8 && k.n == s.n_pad && k.epi == s.epi && k.out == s.out) return &k;
+    if (k.stacked == st && k.fp8 == s.fp8 && k.n == s.n_pad && k.epi == s.epi && k.out == s.out) return &k;
   return nullptr;
 }
 
@@ -114,13 +138,26 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   const int halo = s.taps == 9 ? 1 : 0;
   if (chunks * epc < s.cin) return refuse(KB2_INPUT_MISMATCH, "input tensor narrower than the conv");
 
-  const auto steps = make_ksteps(s, chunks);
+  const bool stacked = k->stacked;
+  auto steps = make_ksteps(s, chunks);
+  if (stacked) {
+    // one input row per instruction group: the dy = 0 steps (every dy uses the same pixel shifts
+    // and channel pairs); the three kernel rows go into N instead
+    std::vector<std::array<Half, 2>> row_steps;
+    for (const auto& st : steps)
+      if (st[0].dy == 0) row_steps.push_back(st);
+    steps = row_steps;
+  }
   if (static_cast<int>(steps.size()) > kMaxKSteps) return refuse(KB2_FORMAT_UNSUPPORTED, "too many K steps");
-  int dx_max = 0;
+  // the row slot is one 128-pixel TMA box starting at x0 - halo; an A tile shifted by dx reads slot
+  // pixels m + halo + dx (+1 for the second half of a zero-partnered step) for MMA row m, so the
+  // strip keeps only the rows whose reads stay inside the box
+  int reach = 0;  // furthest slot pixel an A half reads for MMA row 0
   for (const auto& st : steps)
-    for (const Half& h : st) dx_max = h.dx > dx_max ? h.dx : dx_max;
-  int px = dx_max + halo + kTileM;
-  px = (px + 7) / 8 * 8;
+    for (const Half& h : st) reach = std::max(reach, h.dx + halo);
+  const int px = kRowBoxPx;
+  const int strip_w = px - reach;
+  if (strip_w < 64) return refuse(KB2_FORMAT_UNSUPPORTED, "row slot too narrow for the taps");
   const uint32_t src_bytes = static_cast<uint32_t>(chunks) * px * 16;
   const uint32_t slot_bytes = src_bytes * static_cast<uint32_t>(s.n_sources);
 
@@ -129,7 +166,8 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   a.batch = in0.batch;
   a.H = in0.H;
   a.W = in0.W;
-  a.strips = (in0.W + kTileM - 1) / kTileM;
+  a.strip_w = strip_w;
+  a.strips = (in0.W + strip_w - 1) / strip_w;
   a.n_sources = s.n_sources;
   a.chunks = chunks;
   a.px = px;
@@ -138,7 +176,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   a.row_off = s.taps == 9 ? -1 : 0;
   a.src_bytes = src_bytes;
   a.slot_bytes = slot_bytes;
-  a.ring = s.taps == 9 ? 4 : 3;
+  a.ring = 0;  // sized below from the shared memory left for two blocks per SM
   a.n_ksteps = static_cast<int>(steps.size());
   for (size_t j = 0; j < steps.size(); ++j) {
     auto addr = [&](const Half& h) {
@@ -152,8 +190,31 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     a.ks[j].a_off = static_cast<uint32_t>(a0);
     a.ks[j].lbo = static_cast<uint32_t>(a1 - a0);
     a.ks[j].row = s.taps == 9 ? steps[j][0].dy + 1 : 0;
+    // the distinct (offset, LBO) pairs of a row are the A tiles copied to TMEM once per input row
+    int tile = -1;
+    for (int t = 0; t < a.n_tiles; ++t)
+      if (a.tile_off[t] == a.ks[j].a_off && a.tile_lbo[t] == a.ks[j].lbo) tile = t;
+    if (tile < 0 && a.n_tiles < kMaxTiles) {
+      tile = a.n_tiles++;
+      a.tile_off[tile] = a.ks[j].a_off;
+      a.tile_lbo[tile] = a.ks[j].lbo;
+    }
+    a.ks[j].tile = tile < 0 ? 0 : tile;
   }
+  // A from TMEM for 3x3 layers (rows reused by three output rows) when the tiles of four input
+  // rows fit beside the accumulators in the 512 TMEM columns
+  a.tmem_a = (s.taps == 9 && a.n_tiles <= kMaxTiles &&
+              kTmemRegionBase + kTmemRegions * 8u * static_cast<uint32_t>(a.n_tiles) <= 512u)
+                 ? 1
+                 : 0;
   a.idesc = make_idesc(kTileM, s.n_pad);
+  if (stacked) {
+    a.tmem_a = 0;
+    a.n_tiles = 0;
+    for (int i = 0; i < 3; ++i) a.idesc_n[i] = make_idesc(kTileM, (i + 1) * s.n_pad);
+    a.acc_slots = s.n_pad == 48 ? StackShape<48>::max_slots : StackShape<16>::max_slots;
+  }
+  const int n_rows_b = stacked ? 3 * s.n_pad : s.n_pad;  // rows of B per K step
 
   // ---- weights
   const int kk = s.taps == 9 ? 3 : 1;
@@ -174,22 +235,27 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
       wscale[co] = mx > 0.0f ? mx / 448.0f : 1.0f;
     }
   }
-  const size_t step_bytes = 2u * static_cast<size_t>(s.n_pad) * 16u;
+  // B of K step j: [half][row][16 bytes]; stacked layers have 3 row blocks, block b holding the
+  // kernel row ky = 2 - b (dy = +1, 0, -1) so that its results land on output rows o = t - 2 + b
+  const size_t step_bytes = 2u * static_cast<size_t>(n_rows_b) * 16u;
   std::vector<uint8_t> packed(steps.size() * step_bytes, 0);
   for (size_t j = 0; j < steps.size(); ++j) {
     for (int h = 0; h < 2; ++h) {
       const Half& hf = steps[j][h];
-      for (int co = 0; co < s.n_real; ++co) {
+      for (int row = 0; row < n_rows_b; ++row) {
+        const int blk = row / s.n_pad;
+        const int co = row % s.n_pad;
+        if (co >= s.n_real) continue;
         for (int e = 0; e < epc; ++e) {
           const int ci = hf.chunk * epc + e;
           float v = 0.0f;
           if (!hf.zero && ci < s.cin) {
-            const int ky = s.taps == 9 ? hf.dy + 1 : 0;
+            const int ky = stacked ? 2 - blk : (s.taps == 9 ? hf.dy + 1 : 0);
             const int kx = s.taps == 9 ? hf.dx + 1 : 0;
             v = w_at(co, hf.src * s.cin + ci, ky, kx);
           }
-          uint8_t* dst = packed.data() + j * step_bytes + static_cast<size_t>(h) * s.n_pad * 16 +
-                         static_cast<size_t>(co) * 16;
+          uint8_t* dst = packed.data() + j * step_bytes + static_cast<size_t>(h) * n_rows_b * 16 +
+                         static_cast<size_t>(row) * 16;
           if (s.fp8) {
             dst[e] = e4m3_encode(v * src_scale(hf.src) / wscale[co]);
           } else {
@@ -226,26 +292,53 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   a.err = err_word;
 
   // ---- tensor maps (single-source layers repeat map 0)
-  for (int i = 0; i < 4; ++i) KB2_TRY(encode_row_map(&maps[i], *inputs[i < s.n_sources ? i : 0], px));
+  for (int i = 0; i < 4; ++i) KB2_TRY(encode_row_map(&maps.m[i], *inputs[i < s.n_sources ? i : 0]));
 
   // ---- launch shape
-  smem = 1024 + a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (2 * a.ring + 6) * 8 + 16;
+  // ring: as many row slots as fit beside the weights with two blocks per SM (at least the window
+  // plus one row of prefetch, at most 12)
+  // TMEM-A layers own all 512 TMEM columns: one block per SM, and a ring as deep as shared memory
+  // allows (slots are released as soon as copied, so the producer runs that many rows ahead);
+  // stacked layers run kStackBlocksPerSm blocks per SM, each with its share of TMEM
+  const bool one_per_sm = a.tmem_a != 0 || (stacked && kStackBlocksPerSm == 1);
+  {
+    const size_t fixed = a.w_smem + (stacked ? kStackSmemExtra : kConvSmemExtra);
+    const int min_ring = a.in_rows + 1;
+    auto fit = [&](size_t per_block) {
+      return per_block > fixed ? static_cast<int>((per_block - fixed) / slot_bytes) : 0;
+    };
+    int ring = one_per_sm ? fit(200u * 1024u) : fit((228u * 1024u) / 2 - 2048u);
+    if (!one_per_sm && !stacked && ring < min_ring + 2) ring = fit(227u * 1024u);  // wide slots: one block per SM
+    ring = std::min(ring, 12);
+    a.ring = static_cast<uint32_t>(std::max(ring, min_ring));
+  }
+  smem = a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (stacked ? kStackSmemExtra : kConvSmemExtra);
+  // a block that allocates all 512 TMEM columns asks for more than half the SM's shared memory, so
+  // two of them are never co-resident (the second would only wait in tcgen05.alloc)
+  if (one_per_sm) smem = std::max<size_t>(smem, 120u * 1024u);
   int dev = 0;
   KB2_CUDA(cudaGetDevice(&dev));
   int optin = 0;
   KB2_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
   if (smem > static_cast<size_t>(optin)) return refuse(KB2_FORMAT_UNSUPPORTED, "layer needs too much shared memory");
   KB2_CUDA(cudaFuncSetAttribute(k->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+  KB2_CUDA(cudaFuncSetAttribute(k->fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   int per_sm = 0;
-  KB2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k->fn, 192, smem));
+  KB2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k->fn, k->threads, smem));
   if (per_sm < 1) return refuse(KB2_FORMAT_UNSUPPORTED, "layer does not fit on an SM");
-  const int tmem_cap = static_cast<int>(512u / tmem_cols(s.n_pad));
-  if (per_sm > tmem_cap) per_sm = tmem_cap;
+  // resident blocks per SM: shared memory (228 KB per SM, 1 KB reserved per block) and TMEM
+  // (512 columns; a TMEM-A block takes them all) permitting
+  const int smem_fit = static_cast<int>((228u * 1024u) / (smem + 1024u));
+  const int tmem_fit = a.tmem_a ? 1 : (stacked ? kStackBlocksPerSm : static_cast<int>(512u / tmem_cols(s.n_pad)));
+  per_sm = std::min({per_sm, smem_fit, tmem_fit});
+  if (per_sm < 1) per_sm = 1;
   const int slots = num_sms() * per_sm;
-  // bands: about 16 work items per resident block, 4..64 rows each
+  // bands: about 16 work items per resident block, 4..64 rows each (8.. for the stacked kernel,
+  // whose two halo rows per band are extra MMA work)
   const long long rows_total = static_cast<long long>(a.batch) * a.H * a.strips;
   int band = static_cast<int>(rows_total / (16LL * slots));
-  band = band < 4 ? 4 : (band > 64 ? 64 : band);
+  const int band_min = stacked ? 8 : 4;
+  band = band < band_min ? band_min : (band > 64 ? 64 : band);
   a.band_rows = band;
   a.bands = (a.H + band - 1) / band;
   a.items = a.batch * a.bands * a.strips;
@@ -254,7 +347,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
 }
 
 Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
-                         float res_scale, void* out2) const {
+                         float res_scale, void* out2, int res_chunks) const {
   const KernelEntry* k = find_kernel(spec);
   if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no kernel");
   ConvArgs a = args;
@@ -264,6 +357,7 @@ Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* 
   a.out2 = static_cast<uint8_t*>(out2);
   a.residual = static_cast<const uint8_t*>(residual);
   a.res_fp8 = spec.fp8 ? 1 : 0;
+  a.res_chunks = res_chunks;
   a.out_inv_scale = out_inv_scale;
   a.res_scale = res_scale;
   const int g = a.items < grid ? a.items : grid;

@@ -25,7 +25,7 @@ struct ConvSpec {
 struct ConvLayer {
   ConvSpec spec;
   ConvArgs args{};
-  CUtensorMap maps[4]{};
+  ConvMaps maps{};
   DeviceBuffer wpack, bias, scale, slope;
   size_t smem = 0;
   int grid = 0;
@@ -36,7 +36,7 @@ struct ConvLayer {
                const float* act_scales, const ChunkedTensor* const* inputs, int* err_word);
   // residual / out: device pointers for this launch (residual may be null).
   Status launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
-                float res_scale, void* out2 = nullptr) const;
+                float res_scale, void* out2 = nullptr, int res_chunks = 0) const;
 };
 
 int num_sms();

@@ -5,20 +5,26 @@
 // (span_fp8_kernels.cuh:304-330) with one B200-native kernel:
 //
 //  * Activations live in HBM as row-chunked NHWC: [n][y][chunk][x][16 bytes], a chunk being 8 FP16
-//    or 16 E4M3 channels. One TMA box brings one input row of one source into shared memory as
-//    [chunk][pixel][16 B]: pixels sit at a 16-byte pitch, which is exactly the row pitch of the UMMA
-//    no-swizzle K-major core matrix, so the A operand of tap (dy, dx) is the row slot of dy shifted
-//    by dx pixels -- a descriptor start-address offset, no im2col copy. Zero padding comes from the
-//    TMA out-of-bounds fill.
-//  * M = 128 output pixels of one row, N = output channels (<= 64 here), K = taps x channels in
-//    steps of 32 bytes (two 16-byte halves, LBO apart). A host-built K-step table says, per
-//    instruction, which input row slot, byte offset and LBO the A operand uses; the packed weights
-//    (B, resident in shared memory) follow the same table.
-//  * Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + single-thread MMA issuer, warps 2-5 =
-//    epilogue (TMEM -> registers -> fused bias / SiLU / SPAN attention / PReLU / pixel shuffle /
-//    E4M3 requantisation -> global). The accumulator is double-buffered in TMEM so the epilogue of
-//    row y overlaps the MMAs of row y+1; input rows stream through a ring of slots, each output row
-//    loading one new input row.
+//    or 16 E4M3 channels. TMA brings one input row of one source into a shared-memory slot as
+//    [chunk][pixel][16 B] (1 KB boxes of 64 pixels): pixels sit at a 16-byte pitch, the row pitch of
+//    the UMMA no-swizzle K-major core matrix, so the A operand of tap (dy, dx) is the row of dy
+//    shifted by dx pixels -- a descriptor start-address offset, no im2col. Zero padding comes from
+//    the TMA out-of-bounds fill.
+//  * M = 128 output pixels of one row, N = output channels (16..64), K = taps x channels in steps
+//    of 32 bytes (two 16-byte halves, LBO apart). A host-built K-step table says which input row and
+//    which A tile each instruction uses; the packed weights (B, resident in shared memory) follow it.
+//  * A operand from TMEM (3x3 layers). With N = 48 an MMA whose A (128 x 32 B) is read from shared
+//    memory is bound by the 128 B/clk shared-memory read, not by the tensor pipe (measured on B200:
+//    ~44 clk per M128 N48 K16 instruction instead of 24). So each input row is copied once into
+//    TMEM (tcgen05.cp) as the few distinct (dx, channel-pair) tiles the K steps use, into a ring of
+//    four row regions, and the three output rows that need that input row read it from TMEM; the
+//    shared-memory slot is released as soon as the copy is done. 1x1 layers (no reuse across rows)
+//    read A from shared memory.
+//  * Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + single-thread MMA / copy issuer,
+//    warps 2.. = epilogue, 4 per 16 accumulator columns. An epilogue warp reads the 32 TMEM lanes
+//    of its quadrant (warp id mod 4) and 16 columns, and applies the fused epilogue (bias, SiLU,
+//    SPAN gate, PReLU, pixel shuffle, E4M3 requantisation). The accumulator is double-buffered so
+//    the epilogue of row y overlaps the MMAs of row y+1.
 //  * Persistent CTAs walk work items (image, band of rows, 128-pixel strip).
 #pragma once
 
@@ -27,7 +33,18 @@
 namespace kb2 {
 
 constexpr int kMaxKSteps = 40;
+constexpr int kMaxTiles = 16;
 constexpr int kTileM = 128;
+constexpr int kMaxN = 64;
+constexpr uint32_t kTmemRegions = 4;       // TMEM ring of input rows (A operand)
+constexpr uint32_t kTmemRegionBase = 128;  // columns [0, 128) hold the two accumulators
+
+template <int kN>
+struct ConvShape {
+  static constexpr int epi_warps = 4 * (kN / 16);
+  static constexpr int threads = 64 + 32 * epi_warps;
+  static constexpr uint32_t col_stride = kN <= 32 ? 32 : 64;  // accumulator buffer stride
+};
 
 enum Epi : int {
   kEpiBias = 0,      // acc*scale + bias
@@ -40,7 +57,7 @@ enum Epi : int {
 enum OutFmt : int {
   kOutF16Chunk = 0,   // [n][y][C/8][x][8] half
   kOutE4m3Chunk = 1,  // [n][y][C/16][x][16] e4m3, value * out_inv_scale
-  kOutPixShuf2 = 2,   // NCHW half [n][n_real/4][2H][2W], DepthToSpace(2, CRD)
+  kOutPixShuf2 = 2,   // NCHW half [n][3][2H][2W], DepthToSpace(2, CRD) of 12 channels
   kOutF16E4m3 = 3,    // both: half chunks to `out`, E4M3 chunks (value * out_inv_scale) to `out2`
 };
 
@@ -48,17 +65,24 @@ struct KStep {
   uint32_t a_off;  // byte offset of the first K half inside the input row slot
   uint32_t lbo;    // byte distance to the second K half
   int32_t row;     // input row of the window (0 .. in_rows-1)
-  int32_t pad_;
+  int32_t tile;    // TMEM tile of this (a_off, lbo) pair within a row region (TMEM-A mode)
 };
 
 struct ConvArgs {
-  int batch, H, W;        // output rows / columns (input has the same size: stride 1)
+  int batch, H, W;  // output rows / columns (input has the same size: stride 1)
   int strips, bands, band_rows, items;
+  int strip_w;  // output pixels per strip (128 minus the pixels the shifted A tiles read past the slot)
   int n_sources, chunks, px, halo, in_rows, row_off;
   uint32_t src_bytes, slot_bytes, ring, w_smem;
   int n_ksteps;
   KStep ks[kMaxKSteps];
+  int tmem_a;                    // 1: A from TMEM (3x3 layers)
+  int n_tiles;                   // distinct A tiles per input row (TMEM-A mode)
+  uint32_t tile_off[kMaxTiles];  // slot byte offset of tile t
+  uint32_t tile_lbo[kMaxTiles];  // its K-half distance
   uint32_t idesc;
+  uint32_t idesc_n[3];  // stacked 3x3 kernel: instruction descriptors for 1, 2, 3 row blocks
+  int acc_slots;        // stacked 3x3 kernel: TMEM ring of output-row accumulators
   const uint8_t* wpack;  // n_ksteps * 2 * N * 16 bytes
   uint32_t wbytes;
   const float* bias;        // N entries (zero padded)
@@ -66,8 +90,9 @@ struct ConvArgs {
   const float* slope;       // N entries (PReLU) or null
   float out_inv_scale;      // E4M3 output: 1 / scale
   float res_scale;          // E4M3 residual dequantisation scale
-  const uint8_t* residual;  // same geometry as the output, chunked
+  const uint8_t* residual;  // same pixels and channels as the output, chunked
   int res_fp8;              // residual chunk format: 0 = f16, 1 = e4m3
+  int res_chunks;           // chunks per residual pixel
   uint8_t* out;
   int out_chunks;  // chunks per output pixel (chunked formats)
   uint8_t* out2;   // kOutF16E4m3: the E4M3 copy
@@ -75,84 +100,89 @@ struct ConvArgs {
   int* err;
 };
 
+// Tensor maps of the sources (one 128-pixel row box each, host_util.h encode_row_map).
+struct ConvMaps {
+  CUtensorMap m[4];
+};
+
+// Shared-memory bytes besides the weights and the ring: alignment slack, barriers, K-step and tile
+// tables, per-channel constants, TMEM address.
+constexpr uint32_t kConvSmemExtra = 1024 + 64 * 8 + (kMaxKSteps + 1) * 8 + kMaxTiles * 8 + 3 * kMaxN * 4 + 64;
+
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t{1023});
 }
 
-template <int kN>
-struct TmemCols {
-  static constexpr uint32_t stride = kN <= 32 ? 32 : (kN <= 64 ? 64 : (kN <= 128 ? 128 : 256));
-  static constexpr uint32_t total = 2 * stride;
-};
-
-template <int kEpi, int kOut, int kN>
-__device__ __forceinline__ void epilogue_store(const ConvArgs& a, float* v, int n, int y, int x) {
-  // scale, bias, activation
-#pragma unroll
-  for (int j = 0; j < kN; ++j) {
-    float s = a.chan_scale != nullptr ? __ldg(a.chan_scale + j) : 1.0f;
-    v[j] = fmaf(v[j], s, __ldg(a.bias + j));
-  }
+// Epilogue of kCols accumulator columns [col0, col0 + kCols) of one pixel, in groups of 8 columns.
+// Per-channel constants are read at kc0 + j; the output channel of column j is col0 + j (col0
+// defaults to kc0; a caller holding its constants in a register array passes kc0 = 0).
+template <int kEpi, int kOut, int kCols>
+__device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_bias, const float* s_scale,
+                                              const float* s_slope, float* v, int kc0, int n, int y, int x,
+                                              int col0_override = -1) {
+  const int col0 = col0_override >= 0 ? col0_override : kc0;
   const size_t pix_row = static_cast<size_t>(n) * a.H + y;
+#pragma unroll
+  for (int j = 0; j < kCols; ++j) v[j] = fmaf(v[j], s_scale[kc0 + j], s_bias[kc0 + j]);
   if constexpr (kEpi == kEpiSilu) {
 #pragma unroll
-    for (int j = 0; j < kN; ++j) v[j] = v[j] * sigmoidf_fast(v[j]);
+    for (int j = 0; j < kCols; ++j) v[j] = v[j] * sigmoidf_fast(v[j]);
   } else if constexpr (kEpi == kEpiPrelu) {
 #pragma unroll
-    for (int j = 0; j < kN; ++j) v[j] = v[j] >= 0.0f ? v[j] : v[j] * __ldg(a.slope + j);
+    for (int j = 0; j < kCols; ++j) v[j] = v[j] >= 0.0f ? v[j] : v[j] * s_slope[kc0 + j];
   } else if constexpr (kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu) {
-    float r[kN];
-    if (a.res_fp8) {
+    // residual: same pixel and channels, in the block input's format
 #pragma unroll
-      for (int c = 0; c < kN / 16; ++c) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(
-            a.residual + ((pix_row * (kN / 16) + c) * a.W + x) * 16));
-        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+    for (int g = 0; g < kCols / 8; ++g) {
+      const int c = col0 + 8 * g;
+      float r[8];
+      if (a.res_fp8) {
+        const uint2 q = __ldg(reinterpret_cast<const uint2*>(
+            a.residual + ((pix_row * a.res_chunks + c / 16) * a.W + x) * 16 + (c % 16)));
+        const uint32_t w2[2] = {q.x, q.y};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 lo = unpack_e4m3x2(static_cast<uint16_t>(w4[k] & 0xFFFFu));
-          const float2 hi = unpack_e4m3x2(static_cast<uint16_t>(w4[k] >> 16));
-          r[c * 16 + 4 * k + 0] = lo.x * a.res_scale;
-          r[c * 16 + 4 * k + 1] = lo.y * a.res_scale;
-          r[c * 16 + 4 * k + 2] = hi.x * a.res_scale;
-          r[c * 16 + 4 * k + 3] = hi.y * a.res_scale;
+        for (int k = 0; k < 2; ++k) {
+          const float2 lo = unpack_e4m3x2(static_cast<uint16_t>(w2[k] & 0xFFFFu));
+          const float2 hi = unpack_e4m3x2(static_cast<uint16_t>(w2[k] >> 16));
+          r[4 * k + 0] = lo.x * a.res_scale;
+          r[4 * k + 1] = lo.y * a.res_scale;
+          r[4 * k + 2] = hi.x * a.res_scale;
+          r[4 * k + 3] = hi.y * a.res_scale;
         }
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < kN / 8; ++c) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(
-            a.residual + ((pix_row * (kN / 8) + c) * a.W + x) * 16));
+      } else {
+        const uint4 q = __ldg(
+            reinterpret_cast<const uint4*>(a.residual + ((pix_row * a.res_chunks + c / 8) * a.W + x) * 16));
         const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float2 f = unpack_half2(w4[k]);
-          r[c * 8 + 2 * k] = f.x;
-          r[c * 8 + 2 * k + 1] = f.y;
+          r[2 * k] = f.x;
+          r[2 * k + 1] = f.y;
         }
       }
-    }
-    if constexpr (kEpi == kEpiSpanAttn) {
 #pragma unroll
-      for (int j = 0; j < kN; ++j) v[j] = (v[j] + r[j]) * (sigmoidf_fast(v[j]) - 0.5f);
-    } else {
-#pragma unroll
-      for (int j = 0; j < kN; ++j) {
-        const float t = v[j] + r[j];
-        v[j] = t >= 0.0f ? t : t * __ldg(a.slope + j);
+      for (int k = 0; k < 8; ++k) {
+        float& t = v[8 * g + k];
+        if constexpr (kEpi == kEpiSpanAttn) {
+          t = (t + r[k]) * sigmoid_centered(t);
+        } else {
+          const float u = t + r[k];
+          t = u >= 0.0f ? u : u * s_slope[kc0 + 8 * g + k];
+        }
       }
     }
   }
 
   if constexpr (kOut == kOutF16Chunk || kOut == kOutF16E4m3) {
 #pragma unroll
-    for (int c = 0; c < kN / 8; ++c) {
+    for (int g = 0; g < kCols / 8; ++g) {
+      const float* f = v + 8 * g;
       uint4 q;
-      q.x = pack_half2(v[c * 8 + 0], v[c * 8 + 1]);
-      q.y = pack_half2(v[c * 8 + 2], v[c * 8 + 3]);
-      q.z = pack_half2(v[c * 8 + 4], v[c * 8 + 5]);
-      q.w = pack_half2(v[c * 8 + 6], v[c * 8 + 7]);
-      *reinterpret_cast<uint4*>(a.out + ((pix_row * a.out_chunks + c) * a.W + x) * 16) = q;
+      q.x = pack_half2(f[0], f[1]);
+      q.y = pack_half2(f[2], f[3]);
+      q.z = pack_half2(f[4], f[5]);
+      q.w = pack_half2(f[6], f[7]);
+      *reinterpret_cast<uint4*>(a.out + ((pix_row * a.out_chunks + (col0 + 8 * g) / 8) * a.W + x) * 16) = q;
     }
   }
   if constexpr (kOut == kOutE4m3Chunk || kOut == kOutF16E4m3) {
@@ -160,39 +190,42 @@ __device__ __forceinline__ void epilogue_store(const ConvArgs& a, float* v, int 
     const int dst_chunks = kOut == kOutE4m3Chunk ? a.out_chunks : a.out2_chunks;
     const float is = a.out_inv_scale;
 #pragma unroll
-    for (int c = 0; c < kN / 16; ++c) {
-      uint32_t w4[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float* f = v + c * 16 + 4 * k;
-        w4[k] = static_cast<uint32_t>(pack_e4m3x2(f[0] * is, f[1] * is)) |
-                (static_cast<uint32_t>(pack_e4m3x2(f[2] * is, f[3] * is)) << 16);
-      }
-      *reinterpret_cast<uint4*>(dst + ((pix_row * dst_chunks + c) * a.W + x) * 16) =
-          make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    for (int g = 0; g < kCols / 8; ++g) {
+      const float* f = v + 8 * g;
+      const int c = col0 + 8 * g;
+      uint2 q;
+      q.x = static_cast<uint32_t>(pack_e4m3x2(f[0] * is, f[1] * is)) |
+            (static_cast<uint32_t>(pack_e4m3x2(f[2] * is, f[3] * is)) << 16);
+      q.y = static_cast<uint32_t>(pack_e4m3x2(f[4] * is, f[5] * is)) |
+            (static_cast<uint32_t>(pack_e4m3x2(f[6] * is, f[7] * is)) << 16);
+      *reinterpret_cast<uint2*>(dst + ((pix_row * dst_chunks + c / 16) * a.W + x) * 16 + (c % 16)) = q;
     }
   }
-  if constexpr (kOut == kOutPixShuf2) {  // channel 4c + 2i + j -> pixel (2y + i, 2x + j) of plane c
-    const int planes = kN / 4 < 3 ? kN / 4 : 3;
+  if constexpr (kOut == kOutPixShuf2) {
+    // channel 4p + 2i + j -> pixel (2y + i, 2x + j) of plane p (p < 3)
     const size_t W2 = static_cast<size_t>(a.W) * 2;
     const size_t H2 = static_cast<size_t>(a.H) * 2;
 #pragma unroll
-    for (int c = 0; c < planes; ++c) {
+    for (int q = 0; q < kCols / 4; ++q) {
+      const int plane = (col0 + 4 * q) / 4;
+      if (plane < 3) {
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const size_t at = ((static_cast<size_t>(n) * 3 + c) * H2 + 2 * static_cast<size_t>(y) + i) * W2 + 2 * x;
-        *reinterpret_cast<uint32_t*>(a.out + at * 2) = pack_half2(v[4 * c + 2 * i], v[4 * c + 2 * i + 1]);
+        for (int i = 0; i < 2; ++i) {
+          const size_t at =
+              ((static_cast<size_t>(n) * 3 + plane) * H2 + 2 * static_cast<size_t>(y) + i) * W2 + 2 * x;
+          *reinterpret_cast<uint32_t*>(a.out + at * 2) = pack_half2(v[4 * q + 2 * i], v[4 * q + 2 * i + 1]);
+        }
       }
     }
   }
 }
 
 template <bool kFp8, int kN, int kEpi, int kOut>
-__global__ void __launch_bounds__(192, 2)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
-                   const __grid_constant__ CUtensorMap map2, const __grid_constant__ CUtensorMap map3,
-                   const __grid_constant__ ConvArgs a) {
-  static_assert(kN % 16 == 0 && kN >= 16 && kN <= 64, "N must be 16..64 in steps of 16");
+__global__ void __launch_bounds__(ConvShape<kN>::threads, 1)
+    conv_tc_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
+  static_assert(kN % 16 == 0 && kN >= 16 && kN <= kMaxN, "N must be 16..64 in steps of 16");
+  constexpr int kEpiWarps = ConvShape<kN>::epi_warps;
+  constexpr uint32_t kColStride = ConvShape<kN>::col_stride;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sw = smem;
@@ -204,12 +237,18 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* wbar = acc_empty + 2;
   uint64_t* drain = wbar + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  // per K step: (a_off >> 4) | (lbo >> 4) << 16 | row << 56 | tile << 58 (bits 56-63 are not part
+  // of the descriptor fields the delta is added to, and are masked off before use)
+  uint64_t* s_kstep = bars + 64;
+  uint64_t* s_tile = s_kstep + kMaxKSteps + 1;  // per A tile: (off >> 4) | (lbo >> 4) << 16
+  float* s_bias = reinterpret_cast<float*>(s_tile + kMaxTiles);
+  float* s_scale = s_bias + kMaxN;
+  float* s_slope = s_scale + kMaxN;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_slope + kMaxN);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr uint32_t kColStride = TmemCols<kN>::stride;
-  constexpr uint32_t kTmemCols = TmemCols<kN>::total;
+  const uint32_t tmem_cols = a.tmem_a ? 512u : 2u * kColStride;
 
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < a.ring; ++i) {
@@ -218,22 +257,33 @@ __global__ void __launch_bounds__(192, 2)
     }
     mbar_init(&acc_full[0], 1);
     mbar_init(&acc_full[1], 1);
-    mbar_init(&acc_empty[0], 4);
-    mbar_init(&acc_empty[1], 4);
+    mbar_init(&acc_empty[0], kEpiWarps);
+    mbar_init(&acc_empty[1], kEpiWarps);
     mbar_init(wbar, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
-    prefetch_tmap(&map0);
-    if (a.n_sources > 1) {
-      prefetch_tmap(&map1);
-      prefetch_tmap(&map2);
-      prefetch_tmap(&map3);
-    }
+  for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
+    s_bias[j] = j < kN ? a.bias[j] : 0.0f;
+    s_scale[j] = (a.chan_scale != nullptr && j < kN) ? a.chan_scale[j] : 1.0f;
+    s_slope[j] = (a.slope != nullptr && j < kN) ? a.slope[j] : 0.0f;
   }
+  for (int j = threadIdx.x; j <= kMaxKSteps; j += blockDim.x) {
+    uint64_t e = 0;
+    if (j < a.n_ksteps) {
+      const KStep& s = a.ks[j];
+      e = static_cast<uint64_t>(s.a_off >> 4) | (static_cast<uint64_t>(s.lbo >> 4) << 16) |
+          (static_cast<uint64_t>(s.row & 3) << 56) | (static_cast<uint64_t>(s.tile & 15) << 58);
+    }
+    s_kstep[j] = e;
+  }
+  for (int t = threadIdx.x; t < kMaxTiles; t += blockDim.x)
+    s_tile[t] = t < a.n_tiles
+                    ? (static_cast<uint64_t>(a.tile_off[t] >> 4) | (static_cast<uint64_t>(a.tile_lbo[t] >> 4) << 16))
+                    : 0;
+  if (warp == 0 && lane < a.n_sources) prefetch_tmap(&maps.m[lane]);
   if (warp == 1) {
-    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_alloc(tmem_holder, tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -258,7 +308,7 @@ __global__ void __launch_bounds__(192, 2)
         const int n = t / a.bands;
         const int y0 = band * a.band_rows;
         const int y1 = min(a.H, y0 + a.band_rows);
-        const int x0 = strip * kTileM;
+        const int x0 = strip * a.strip_w;
         const int r_end = (y1 - 1) + a.row_off + a.in_rows;
         for (int r = y0 + a.row_off; r < r_end; ++r, ++cnt) {
           const uint32_t slot = cnt % a.ring;
@@ -269,12 +319,10 @@ __global__ void __launch_bounds__(192, 2)
           }
           mbar_arrive_expect_tx(&full[slot], a.slot_bytes);
           uint8_t* dst = ring + slot * a.slot_bytes;
-          tma_load_5d(dst, &map0, &full[slot], 0, x0 - a.halo, 0, r, n);
-          if (a.n_sources > 1) {
-            tma_load_5d(dst + a.src_bytes, &map1, &full[slot], 0, x0 - a.halo, 0, r, n);
-            tma_load_5d(dst + 2 * a.src_bytes, &map2, &full[slot], 0, x0 - a.halo, 0, r, n);
-            tma_load_5d(dst + 3 * a.src_bytes, &map3, &full[slot], 0, x0 - a.halo, 0, r, n);
-          }
+          // one box per source: 128 pixels from x0 - halo (a 16-byte-aligned word coordinate,
+          // negative at the left edge: zero fill), all chunks
+          for (int s = 0; s < a.n_sources; ++s)
+            tma_load_4d(dst + s * a.src_bytes, &maps.m[s], &full[slot], (x0 - a.halo) * 2, 0, r, n);
         }
       }
       // every copy issued has landed before the block may exit
@@ -284,11 +332,18 @@ __global__ void __launch_bounds__(192, 2)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ------------------------------------------------------------------ MMA issuer
+      // ------------------------------------------------------------------ MMA / copy issuer
       bool ok = wait_bar(wbar, 0, a.err, kErrWaitMma);
       const uint32_t ring_base = smem_u32(ring);
-      const uint32_t w_base = smem_u32(sw);
-      constexpr uint32_t kBStep = 2u * kN * 16u;
+      // descriptor template: SBO = 128 B (8 rows x 16 B), version 1, no swizzle; the start address
+      // and LBO fields are added per K step (the fields cannot carry into each other)
+      const uint64_t desc_hi = make_sdesc(0, 0, 128);
+      const uint64_t b_desc0 = make_sdesc(smem_u32(sw), kN * 16, 128);
+      constexpr uint64_t kBStep16 = (2u * kN * 16u) >> 4;
+      const int n_ksteps = a.n_ksteps;
+      const int n_tiles = a.n_tiles;
+      const uint32_t region_cols = static_cast<uint32_t>(n_tiles) * 8u;
+      const uint32_t tmem_a_base = tmem_base + kTmemRegionBase;
       uint32_t in_cnt = 0;
       uint32_t acc_cnt = 0;
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
@@ -297,41 +352,75 @@ __global__ void __launch_bounds__(192, 2)
         const int y0 = band * a.band_rows;
         const int y1 = min(a.H, y0 + a.band_rows);
         const uint32_t base = in_cnt;
-        uint32_t waited = 0;
+        uint32_t ready = 0;  // rows of this item available (loaded, and copied to TMEM in TMEM-A mode)
         for (int y = y0; y < y1; ++y) {
           const uint32_t rel = static_cast<uint32_t>(y - y0);
-          for (; waited < rel + static_cast<uint32_t>(a.in_rows); ++waited) {
-            const uint32_t k = base + waited;
-            if (!wait_bar(&full[k % a.ring], (k / a.ring) & 1u, a.err, kErrWaitMma)) {
-              ok = false;
-              break;
-            }
-          }
-          if (!ok) break;
+          // Wait for the accumulator first: its release by the epilogue also proves that the MMAs
+          // of two rows ago are complete, so the TMEM region the copies below overwrite (the input
+          // row four rows back, last read by those MMAs) is no longer in use.
           const uint32_t buf = acc_cnt & 1u;
           const uint32_t use = acc_cnt >> 1;
           if (!wait_bar(&acc_empty[buf], (use & 1u) ^ 1u, a.err, kErrWaitMma)) {
             ok = false;
             break;
           }
+          for (; ready < rel + static_cast<uint32_t>(a.in_rows); ++ready) {
+            const uint32_t k = base + ready;
+            const uint32_t slot = k % a.ring;
+            if (!wait_bar(&full[slot], (k / a.ring) & 1u, a.err, kErrWaitMma)) {
+              ok = false;
+              break;
+            }
+            if (a.tmem_a) {
+              tc_fence_after();
+              const uint64_t row_desc = desc_hi | static_cast<uint64_t>((ring_base + slot * a.slot_bytes) >> 4);
+              const uint32_t dst = tmem_a_base + (k % kTmemRegions) * region_cols;
+              for (int tt = 0; tt < n_tiles; ++tt) tmem_cp_128x256b(dst + 8u * tt, row_desc + s_tile[tt]);
+              mma_commit(&empty[slot]);  // the slot is free once copied
+            }
+          }
+          if (!ok) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + buf * kColStride;
-          for (int j = 0; j < a.n_ksteps; ++j) {
-            const KStep& s = a.ks[j];
-            const uint32_t slot = (base + rel + static_cast<uint32_t>(s.row)) % a.ring;
-            const uint32_t a_addr = ring_base + slot * a.slot_bytes + s.a_off;
-            const uint64_t adesc = make_sdesc(a_addr, s.lbo, 128);
-            const uint64_t bdesc = make_sdesc(w_base + static_cast<uint32_t>(j) * kBStep, kN * 16, 128);
-            mma_ss<kFp8>(d_tmem, adesc, bdesc, a.idesc, j > 0 ? 1u : 0u);
+          uint64_t bdesc = b_desc0;
+          uint64_t e = s_kstep[0];
+          if (a.tmem_a) {
+            const uint32_t r0 = tmem_a_base + ((base + rel) % kTmemRegions) * region_cols;
+            const uint32_t r1 = tmem_a_base + ((base + rel + 1) % kTmemRegions) * region_cols;
+            const uint32_t r2 = tmem_a_base + ((base + rel + 2) % kTmemRegions) * region_cols;
+            for (int j = 0; j < n_ksteps; ++j) {
+              const uint64_t next = s_kstep[j + 1];  // prefetched (the table is padded by one entry)
+              const uint32_t row = static_cast<uint32_t>(e >> 56) & 3u;
+              const uint32_t tile = static_cast<uint32_t>(e >> 58) & 15u;
+              const uint32_t a_tmem = (row == 0 ? r0 : (row == 1 ? r1 : r2)) + 8u * tile;
+              mma_ts<kFp8>(d_tmem, a_tmem, bdesc, a.idesc, j > 0 ? 1u : 0u);
+              bdesc += kBStep16;
+              e = next;
+            }
+          } else {
+            auto row_desc = [&](uint32_t r) {
+              const uint32_t slot = (base + rel + r) % a.ring;
+              return desc_hi | static_cast<uint64_t>((ring_base + slot * a.slot_bytes) >> 4);
+            };
+            const uint64_t d0 = row_desc(0), d1 = row_desc(1), d2 = row_desc(2);
+            for (int j = 0; j < n_ksteps; ++j) {
+              const uint64_t next = s_kstep[j + 1];
+              const uint32_t row = static_cast<uint32_t>(e >> 56) & 3u;
+              const uint64_t adesc = (row == 0 ? d0 : (row == 1 ? d1 : d2)) + (e & 0x3FFF3FFFull);
+              mma_ss<kFp8>(d_tmem, adesc, bdesc, a.idesc, j > 0 ? 1u : 0u);
+              bdesc += kBStep16;
+              e = next;
+            }
           }
           mma_commit(&acc_full[buf]);
-          mma_commit(&empty[(base + rel) % a.ring]);  // the oldest row of this window is done
+          if (!a.tmem_a) mma_commit(&empty[(base + rel) % a.ring]);  // the oldest row of this window is done
           ++acc_cnt;
         }
         if (!ok) break;
         const uint32_t rows_out = static_cast<uint32_t>(y1 - y0);
         const uint32_t total = rows_out - 1 + static_cast<uint32_t>(a.in_rows);
-        for (uint32_t r = rows_out; r < total; ++r) mma_commit(&empty[(base + r) % a.ring]);
+        if (!a.tmem_a)
+          for (uint32_t r = rows_out; r < total; ++r) mma_commit(&empty[(base + r) % a.ring]);
         in_cnt = base + total;
       }
       mma_commit(drain);
@@ -339,8 +428,9 @@ __global__ void __launch_bounds__(192, 2)
     }
     __syncwarp();
   } else {
-    // -------------------------------------------------------------------- epilogue (warps 2..5)
+    // -------------------------------------------------------------------- epilogue
     const int quad = warp & 3;
+    const int col0 = ((warp - 2) >> 2) * 16;
     uint32_t acc_cnt = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
@@ -350,7 +440,9 @@ __global__ void __launch_bounds__(192, 2)
       const int n = t / a.bands;
       const int y0 = band * a.band_rows;
       const int y1 = min(a.H, y0 + a.band_rows);
-      const int x = strip * kTileM + quad * 32 + lane;
+      const int m = quad * 32 + lane;
+      const int x = strip * a.strip_w + m;
+      const bool store = m < a.strip_w && x < a.W;
       for (int y = y0; y < y1; ++y) {
         const uint32_t buf = acc_cnt & 1u;
         const uint32_t use = acc_cnt >> 1;
@@ -360,15 +452,14 @@ __global__ void __launch_bounds__(192, 2)
           break;
         }
         tc_fence_after();
-        float v[kN];
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * kColStride;
-#pragma unroll
-        for (int c = 0; c < kN; c += 16) tmem_ld16(taddr + c, v + c);
+        float v[16];
+        tmem_ld16(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * kColStride + static_cast<uint32_t>(col0),
+                  v);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        if (x < a.W) epilogue_store<kEpi, kOut, kN>(a, v, n, y, x);
+        if (store) epilogue_cols<kEpi, kOut, 16>(a, s_bias, s_scale, s_slope, v, col0, n, y, x);
         ++acc_cnt;
       }
     }
@@ -378,7 +469,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, tmem_cols);
   }
 }
 

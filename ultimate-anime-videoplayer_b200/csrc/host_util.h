@@ -11,7 +11,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/kirari_b200.h"
+#include "kirari_b200.h"
 
 namespace kb2 {
 
@@ -64,22 +64,27 @@ struct ChunkedTensor {
   size_t bytes() const { return static_cast<size_t>(batch) * H * chunks * W * 16; }
 };
 
-// Box = one row of `box_px` pixels x all chunks of one image.
-inline Status encode_row_map(CUtensorMap* map, const ChunkedTensor& t, int box_px) {
+// One row of one image: kRowBoxPx consecutive pixels x all channel chunks, as ONE TMA box. The
+// tensor is viewed as 64-bit words ([n][y][chunk][2 * x]) so that 128 pixels (2 KB per chunk) fit
+// the 256-element box limit; the box lands in shared memory as [chunk][128 px][16 B], the row slot
+// layout of the conv kernels. One request per row matters: issuing a TMA instruction costs the
+// producer ~170 cycles, so many small boxes per row starve the MMAs. Tile mode copies bytes, so the
+// word type does not change the FP16 / E4M3 payload.
+constexpr int kRowBoxPx = 128;
+
+inline Status encode_row_map(CUtensorMap* map, const ChunkedTensor& t) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (fn == nullptr) return refuse(KB2_VENDOR_CALL_FAILED, "cuTensorMapEncodeTiled unavailable");
-  const int epc = t.fp8 ? 16 : 8;
-  const cuuint64_t dims[5] = {static_cast<cuuint64_t>(epc), static_cast<cuuint64_t>(t.W),
-                              static_cast<cuuint64_t>(t.chunks), static_cast<cuuint64_t>(t.H),
-                              static_cast<cuuint64_t>(t.batch)};
+  if (t.chunks < 1 || t.chunks > 256) return refuse(KB2_FORMAT_UNSUPPORTED, "row box: 1..256 chunks");
   const cuuint64_t row = static_cast<cuuint64_t>(t.W) * 16;
-  const cuuint64_t strides[4] = {16, row, row * static_cast<cuuint64_t>(t.chunks),
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(t.W) * 2, static_cast<cuuint64_t>(t.chunks),
+                              static_cast<cuuint64_t>(t.H), static_cast<cuuint64_t>(t.batch)};
+  const cuuint64_t strides[3] = {row, row * static_cast<cuuint64_t>(t.chunks),
                                  row * static_cast<cuuint64_t>(t.chunks) * static_cast<cuuint64_t>(t.H)};
-  const cuuint32_t box[5] = {static_cast<cuuint32_t>(epc), static_cast<cuuint32_t>(box_px),
-                             static_cast<cuuint32_t>(t.chunks), 1, 1};
-  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  const CUresult r = fn(map, t.fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, t.ptr,
-                        dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(kRowBoxPx) * 2, static_cast<cuuint32_t>(t.chunks), 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, t.ptr, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return refuse(KB2_VENDOR_CALL_FAILED, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
   return Status::Ok();

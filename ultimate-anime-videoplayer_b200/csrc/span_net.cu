@@ -266,7 +266,8 @@ Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, b
     void* dst = s.out != nullptr ? static_cast<void*>(s.out->ptr) : out;
     if (profiling_) KB2_TRY(timed(s.kind, 0.0, 0.0, stream, true));
     KB2_TRY(s.layer->launch(stream, batch, dst, s.residual != nullptr ? s.residual->ptr : nullptr, s.out_inv_scale,
-                            s.res_scale, s.out2 != nullptr ? s.out2->ptr : nullptr));
+                            s.res_scale, s.out2 != nullptr ? s.out2->ptr : nullptr,
+                            s.residual != nullptr ? s.residual->chunks : 0));
     if (profiling_) KB2_TRY(timed(s.kind, s.flops_px * pixels, s.bytes_px * pixels, stream, false));
     if (capture_peaks && s.peak >= 0) {
       const size_t n2 = static_cast<size_t>(batch) * H_ * s.out->chunks * W_ * 4;  // 4 half2 per chunk
