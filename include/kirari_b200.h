@@ -63,7 +63,9 @@ typedef struct kb2_engine_desc {
   int32_t height;       /* input frame height */
   int32_t width;        /* input frame width */
   int32_t device;       /* CUDA device ordinal */
-  const void* weights;  /* weight blob (kb2 blob v1), host memory */
+  const void* weights;  /* weight blob v1, host memory: 32-byte header ("KB2WGT01", u32 version 1,
+                           u32 model, u64 float count, u32 CRC-32 of the payload, u32 0), then the
+                           float32 parameters in the model's order */
   uint64_t weights_bytes;
   const float* act_scales; /* FP8: per-tensor E4M3 activation scales (SPAN: 19), host memory */
   int32_t act_scale_count;
