@@ -117,6 +117,23 @@ int kb2_check_device(kb2_engine* engine, void* stream, int32_t* code);
 int kb2_span_calibrate(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks,
                        int32_t n_peaks);
 
+/* kb2_span_calibrate without any device allocation. This entry point has no counterpart in the
+ * reference: it exists for callers that reserve all their device memory up front and cannot let a
+ * call allocate. kb2_span_calibrate allocates scratch for the discarded x2 output frames on every
+ * call; this variant takes it, and the 19 peak words, from a 64 MiB __device__ array compiled into
+ * the library (one per device, shared by all engines on it).
+ *   - Same arguments, checks and result as kb2_span_calibrate. Peaks are bit-identical.
+ *   - Limit: one x2 output frame (24 * H * W bytes) plus 256 bytes must fit in 64 MiB, i.e.
+ *     H * W <= 2,796,192 pixels (1920x1080 fits, 2560x1440 does not); larger engines are refused
+ *     with KB2_SHAPE_INVALID. Frames run min(max_batch, what fits) at a time.
+ *   - The engine's device must be the current device. The first call on a device looks up the
+ *     array (cudaGetSymbolAddress), which makes the driver load and reserve it there: make that
+ *     first call before any stream capture begins. The call is synchronous on `stream`.
+ *   - Profiling must be off (its timing events would be created on demand).
+ *   - Overlapping calls on one device race on the shared array: serialise them. */
+int kb2_span_calibrate_static(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks,
+                              int32_t n_peaks);
+
 /* Per-layer device timing, the role of the reference's GpuTiming event pairs
  * (src/gpu/cuda/backend/gpu_timing.h:1-40): while enabled, every kernel launch of an enqueue is
  * bracketed by CUDA events on the enqueue's stream; kb2_read_profile synchronises the engine's last

@@ -142,6 +142,17 @@ int kb2_span_calibrate(kb2_engine* engine, void* stream, const kb2_tensor* frame
   }
 }
 
+int kb2_span_calibrate_static(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks,
+                              int32_t n_peaks) {
+  if (engine == nullptr || frames == nullptr || peaks == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    return set_error(engine,
+                     engine->impl->calibrate_static(static_cast<cudaStream_t>(stream), *frames, peaks, n_peaks));
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
 int kb2_set_profiling(kb2_engine* engine, int32_t enable) {
   if (engine == nullptr) return KB2_INVALID_ARGUMENT;
   return set_error(engine, engine->impl->set_profiling(enable != 0));

@@ -3,6 +3,7 @@
 
 #include "engine.h"
 #include "span_net.h"
+#include "static_scratch.h"
 
 namespace kb2 {
 
@@ -47,6 +48,25 @@ class SpanEngine final : public Engine {
     const uint64_t addr = frames.handle + frames.offset;
     if (addr == 0 || (addr & 15u) != 0) return refuse(KB2_INPUT_MISMATCH, "calibration frames misaligned");
     return net_.calibrate(stream, reinterpret_cast<const void*>(addr), static_cast<int>(frames.dims[0]), peaks);
+  }
+  Status calibrate_static(cudaStream_t stream, const kb2_tensor& frames, float* peaks, int n_peaks) override {
+    if (n_peaks != kSpanScales) return refuse(KB2_INPUT_MISMATCH, "SPAN calibration returns 19 peaks");
+    if (frames.type != KB2_F16 || frames.dims[1] != 3 || frames.dims[2] != height() || frames.dims[3] != width() ||
+        frames.dims[0] < 1)
+      return refuse(KB2_INPUT_MISMATCH, "calibration frames: F16 [n,3,H,W] expected");
+    const uint64_t addr = frames.handle + frames.offset;
+    if (addr == 0 || (addr & 15u) != 0) return refuse(KB2_INPUT_MISMATCH, "calibration frames misaligned");
+    // the scratch must be looked up on the engine's device, so that device has to be the current one
+    cudaPointerAttributes attr{};
+    KB2_CUDA(cudaPointerGetAttributes(&attr, err_word()));
+    int cur = -1;
+    KB2_CUDA(cudaGetDevice(&cur));
+    if (cur != attr.device)
+      return refuse(KB2_INPUT_MISMATCH, "static calibration: make the engine's device the current device");
+    void* scratch = nullptr;
+    KB2_TRY(static_scratch(&scratch));
+    return net_.calibrate_in(stream, reinterpret_cast<const void*>(addr), static_cast<int>(frames.dims[0]), peaks,
+                             static_cast<uint8_t*>(scratch), kStaticScratchBytes);
   }
   Status set_profiling(bool on) override {
     net_.set_profiling(on);

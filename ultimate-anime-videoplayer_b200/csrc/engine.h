@@ -25,6 +25,10 @@ class Engine {
   virtual Status calibrate(cudaStream_t, const kb2_tensor&, float*, int) {
     return refuse(KB2_FORMAT_UNSUPPORTED, "this engine does not calibrate");
   }
+  // calibrate() with its scratch in the library's static device array (kb2_span_calibrate_static)
+  virtual Status calibrate_static(cudaStream_t, const kb2_tensor&, float*, int) {
+    return refuse(KB2_FORMAT_UNSUPPORTED, "this engine does not calibrate");
+  }
   Status check_device(cudaStream_t stream, int32_t* code);
   virtual Status set_profiling(bool) { return refuse(KB2_FORMAT_UNSUPPORTED, "no profiling"); }
   virtual Status read_profile(kb2_layer_profile*, int, int* count) {

@@ -20,6 +20,8 @@
 // conv_1 and block 0, whose E4M3 rounding alone would cost the 45 dB bar.
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "span_net.h"
 
 namespace kb2 {
@@ -247,7 +249,8 @@ size_t SpanNet::device_bytes() const {
   return total;
 }
 
-Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, bool capture_peaks) {
+Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, bool capture_peaks,
+                    unsigned int* peaks_dst) {
   if (batch < 1 || batch > max_batch_) return refuse(KB2_SHAPE_INVALID, "SPAN: batch out of contract");
   {
     const long long px = static_cast<long long>(batch) * H_ * W_;
@@ -261,7 +264,7 @@ Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, b
     if (profiling_) KB2_TRY(timed(kind_index("span.pack"), 0.0, px_b * (6.0 + 32.0), stream, false));
   }
   const double pixels = static_cast<double>(batch) * H_ * W_;
-  unsigned int* peaks = peaks_.as<unsigned int>();
+  unsigned int* peaks = peaks_dst != nullptr ? peaks_dst : peaks_.as<unsigned int>();
   for (const Step& s : steps_) {
     void* dst = s.out != nullptr ? static_cast<void*>(s.out->ptr) : out;
     if (profiling_) KB2_TRY(timed(s.kind, 0.0, 0.0, stream, true));
@@ -349,6 +352,41 @@ Status SpanNet::calibrate(cudaStream_t stream, const void* frames, int n, float*
     KB2_TRY(run(stream, src, scratch.ptr, batch, true));
     unsigned int bits[kSpanScales];
     KB2_CUDA(cudaMemcpyAsync(bits, peaks_.ptr, sizeof(bits), cudaMemcpyDeviceToHost, stream));
+    KB2_CUDA(cudaStreamSynchronize(stream));
+    for (int k = 0; k < kSpanScales; ++k) {
+      float f;
+      std::memcpy(&f, &bits[k], 4);
+      best[k] = std::fmax(best[k], f);
+    }
+  }
+  std::memcpy(peaks_out, best.data(), kSpanScales * sizeof(float));
+  return Status::Ok();
+}
+
+Status SpanNet::calibrate_in(cudaStream_t stream, const void* frames, int n, float* peaks_out, uint8_t* scratch,
+                            size_t scratch_bytes) {
+  if (fp8_) return refuse(KB2_FORMAT_UNSUPPORTED, "calibration runs on the FP16 engine");
+  // with profiling on, run() may create timing events, which allocates
+  if (profiling_) return refuse(KB2_INVALID_ARGUMENT, "static calibration: turn profiling off first");
+  constexpr size_t kPeakBytes = 256;  // the 19 peak words, padded so the frames start 256-aligned
+  const size_t frame_bytes = static_cast<size_t>(3) * 4 * H_ * W_ * 2;
+  const size_t fit = scratch_bytes > kPeakBytes ? (scratch_bytes - kPeakBytes) / frame_bytes : 0;
+  if (fit < 1)
+    return refuse(KB2_SHAPE_INVALID, "static calibration: one x2 output frame of " + std::to_string(H_) + "x" +
+                                         std::to_string(W_) + " needs " + std::to_string(frame_bytes + kPeakBytes) +
+                                         " bytes of scratch, the static scratch holds " +
+                                         std::to_string(scratch_bytes));
+  const int chunk = static_cast<int>(std::min<size_t>(fit, static_cast<size_t>(max_batch_)));
+  unsigned int* peak_words = reinterpret_cast<unsigned int*>(scratch);
+  std::vector<float> best(kSpanScales, 0.0f);
+  for (int i = 0; i < n; i += chunk) {
+    const int batch = n - i < chunk ? n - i : chunk;
+    // atomicMax only raises the peak words: they must be zero before every chunk
+    KB2_CUDA(cudaMemsetAsync(peak_words, 0, kSpanScales * sizeof(unsigned int), stream));
+    const uint8_t* src = static_cast<const uint8_t*>(frames) + static_cast<size_t>(i) * 3 * H_ * W_ * 2;
+    KB2_TRY(run(stream, src, scratch + kPeakBytes, batch, true, peak_words));
+    unsigned int bits[kSpanScales];
+    KB2_CUDA(cudaMemcpyAsync(bits, peak_words, sizeof(bits), cudaMemcpyDeviceToHost, stream));
     KB2_CUDA(cudaStreamSynchronize(stream));
     for (int k = 0; k < kSpanScales; ++k) {
       float f;

@@ -18,8 +18,14 @@ class SpanNet {
   Status create(const std::vector<float>& params, int precision, int max_batch, int H, int W,
                 const float* act_scales, int n_scales);
   // in: NCHW F16 [batch][3][H][W]; out: NCHW F16 [batch][3][2H][2W] (device pointers).
-  Status run(cudaStream_t stream, const void* in, void* out, int batch, bool capture_peaks = false);
+  // peaks_dst: where capture_peaks collects the 19 peak words (null: the engine's own words).
+  Status run(cudaStream_t stream, const void* in, void* out, int batch, bool capture_peaks = false,
+             unsigned int* peaks_dst = nullptr);
   Status calibrate(cudaStream_t stream, const void* frames, int n, float* peaks_out);
+  // calibrate() with the caller's device scratch in place of its per-call allocation: the peak
+  // words at the start of `scratch`, the discarded x2 frames after them (kb2_span_calibrate_static).
+  Status calibrate_in(cudaStream_t stream, const void* frames, int n, float* peaks_out, uint8_t* scratch,
+                      size_t scratch_bytes);
   size_t device_bytes() const;
   int* err_word() const { return err_.as<int>(); }
   int height() const { return H_; }

@@ -36,7 +36,7 @@ PREC_FP8 = 2
 # every entry point of include/kirari_b200.h
 EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "kb2_last_error",
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
-           "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue")
+           "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static")
 
 
 class KB2Error(RuntimeError):
@@ -86,6 +86,8 @@ def lib():
         L.kb2_check_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
         L.kb2_span_calibrate.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Tensor),
                                          ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
+        L.kb2_span_calibrate_static.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Tensor),
+                                                ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
         L.kb2_set_profiling.argtypes = [ctypes.c_void_p, ctypes.c_int32]
         L.kb2_read_profile.argtypes = [ctypes.c_void_p, ctypes.POINTER(LayerProfile), ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_int32)]
@@ -172,6 +174,13 @@ class Engine:
         peaks = (ctypes.c_float * 19)()
         t = to_kb2_tensor(frames)
         self._check(lib().kb2_span_calibrate(self.h, _stream_handle(stream), ctypes.byref(t), peaks, 19))
+        return np.array(peaks[:], np.float32)
+
+    def calibrate_static(self, frames, stream=None):
+        """calibrate() with its scratch in the library's static device array: no device allocation."""
+        peaks = (ctypes.c_float * 19)()
+        t = to_kb2_tensor(frames)
+        self._check(lib().kb2_span_calibrate_static(self.h, _stream_handle(stream), ctypes.byref(t), peaks, 19))
         return np.array(peaks[:], np.float32)
 
     def set_profiling(self, on=True):
