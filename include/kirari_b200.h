@@ -134,6 +134,15 @@ int kb2_span_calibrate(kb2_engine* engine, void* stream, const kb2_tensor* frame
 int kb2_span_calibrate_static(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks,
                               int32_t n_peaks);
 
+/* The warp tap rule of the IFNet path, on the device, for callers and tests that need the exact
+ * sample positions: for a flow field [n][2][h][w] (FP32, device memory; plane 0 = x, plane 1 = y)
+ * writes x0, x1, y0, y1 as int32 planes [n][4][h][w] and the weights wx, wy as FP32 planes
+ * [n][2][h][w] of the bilinear backward warp over the whole h x w plane. The rule is the reference's
+ * tap_at (src/gpu/cuda/backend/warp_lib.cuh:45-58, src/kernels/spec/warp.h:44-49): ix = x + fx in
+ * FP32 round-to-nearest, clamped to [0, w - 1] (NaN to 0), x0 = trunc(ix), x1 = min(x0 + 1, w - 1),
+ * wx = ix - x0; the same along y. Asynchronous on `stream`. */
+int kb2_warp_taps(void* stream, const float* flow, int32_t n, int32_t h, int32_t w, int32_t* taps, float* weights);
+
 /* Per-layer device timing, the role of the reference's GpuTiming event pairs
  * (src/gpu/cuda/backend/gpu_timing.h:1-40): while enabled, every kernel launch of an enqueue is
  * bracketed by CUDA events on the enqueue's stream; kb2_read_profile synchronises the engine's last

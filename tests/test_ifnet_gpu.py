@@ -1,0 +1,155 @@
+"""IFNet (RIFE) on the B200 through the C ABI, against the CPU oracle (pinned to the reference).
+
+Tolerances (the contract's): FP16 path max-abs <= 2/255 after clamp to [0, 1] vs the FP32 oracle;
+warp taps bit-exact against the CPU restatement of the reference's tap_at."""
+import numpy as np
+import pytest
+
+import kirari_b200 as kb
+from oracle import nets
+from util import ensure_built, golden
+
+pytestmark = pytest.mark.gpu
+
+FP16_MAX_ABS = 2.0 / 255.0
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ensure_built()
+
+
+@pytest.fixture(scope="module")
+def params():
+    return nets.ifnet_init(2)
+
+
+def run_ifnet(a, b, t, p, max_batch=None):
+    import torch
+    n, _, h, w = a.shape
+    eng = kb.Engine(kb.MODEL_IFNET, kb.make_blob(kb.MODEL_IFNET, nets.ifnet_flat(p)), h, w, max_batch=max_batch or n)
+    eng.set_timestep(t)
+    ta = torch.from_numpy(np.ascontiguousarray(a, np.float16)).cuda()
+    tb = torch.from_numpy(np.ascontiguousarray(b, np.float16)).cuda()
+    out = torch.full((n, 3, h, w), float("nan"), dtype=torch.float16, device="cuda")
+    eng.enqueue([ta, tb], [out])
+    eng.check_device()
+    res = out.float().cpu().numpy()
+    eng.close()
+    return res
+
+
+def padded_oracle(a, b, t, p):
+    """The oracle on the engine's zero padded plane (multiples of 32, window of the reference's
+    rife_window), cropped back to the frame."""
+    n, c, h, w = a.shape
+    hp, wp = -(-h // 32) * 32, -(-w // 32) * 32
+    top, left = ((hp - h) // 2) & ~1, ((wp - w) // 2) & ~1
+
+    def pad(x):
+        z = np.zeros((n, c, hp, wp), np.float32)
+        z[:, :, top:top + h, left:left + w] = x
+        return z
+
+    out = nets.ifnet_forward(pad(a), pad(b), t, p)
+    return out[:, :, top:top + h, left:left + w]
+
+
+def f16(x):
+    return np.asarray(x, np.float16).astype(np.float32)
+
+
+def test_warp_taps_bit_exact():
+    import torch
+    rng = np.random.default_rng(5)
+    n, h, w = 2, 37, 53
+    flow = (rng.standard_normal((n, 2, h, w)) * 6.0).astype(np.float32)
+    flow[0, 0, 0, :8] = [1e9, -1e9, np.inf, -np.inf, np.nan, 0.5, -0.5, 52.9999]
+    flow[1, 1, 3, :4] = [np.nan, 1e-30, -1e-30, 36.5]
+    flow[1, :, 5, 5] = [0.1, 0.2]
+    taps, weights = kb.warp_taps(torch.from_numpy(flow).cuda())
+    taps, weights = taps.cpu().numpy(), weights.cpu().numpy()
+    for i in range(n):
+        x0, x1, y0, y1, wx, wy = nets.warp_taps(flow[i, 0], flow[i, 1], 0, 0, w, h)
+        np.testing.assert_array_equal(taps[i, 0], x0)
+        np.testing.assert_array_equal(taps[i, 1], x1)
+        np.testing.assert_array_equal(taps[i, 2], y0)
+        np.testing.assert_array_equal(taps[i, 3], y1)
+        np.testing.assert_array_equal(weights[i, 0], wx)
+        np.testing.assert_array_equal(weights[i, 1], wy)
+
+
+@pytest.mark.parametrize("name", ["ifnet_64x96_t05.npz", "ifnet_64x96_t03.npz"])
+def test_ifnet_matches_reference_golden(name, params):
+    g = golden(name)
+    out = run_ifnet(g["a"], g["b"], float(g["t"]), params)
+    err = nets.max_abs_clamped(out, g["out"])
+    assert err <= FP16_MAX_ABS, f"max-abs {err * 255:.3f}/255"
+
+
+@pytest.mark.parametrize("shape,t", [((1, 64, 128), 0.5), ((2, 128, 192), 0.25), ((1, 72, 100), 0.5),
+                                     ((1, 130, 66), 0.7)])
+def test_ifnet_fp16_parity(shape, t, params):
+    from synth import shifted_pair
+    n, h, w = shape
+    pairs = [shifted_pair(h, w, seed=30 + i) for i in range(n)]
+    a = f16(np.stack([p[0] for p in pairs]))
+    b = f16(np.stack([p[1] for p in pairs]))
+    out = run_ifnet(a, b, t, params)
+    ref = padded_oracle(a, b, t, params)
+    assert np.isfinite(out).all()
+    err = nets.max_abs_clamped(out, ref)
+    assert err <= FP16_MAX_ABS, f"{shape} t={t}: max-abs {err * 255:.3f}/255"
+
+
+def test_zero_network_is_the_plain_blend():
+    """All-zero weights: zero flow, zero mask, so the output is 0.5 * img0 + 0.5 * img1 exactly
+    (the reference's zero-flow identity case, tests/unit/gpu_cuda/rife_fused_test.cpp:131-179)."""
+    p = {k: np.zeros(s, np.float32) for k, s in nets.ifnet_param_shapes()}
+    rng = np.random.default_rng(3)
+    a = f16(rng.random((1, 3, 64, 64), dtype=np.float32))
+    b = f16(rng.random((1, 3, 64, 64), dtype=np.float32))
+    out = run_ifnet(a, b, 0.5, p)
+    np.testing.assert_array_equal(out, f16(a * np.float32(0.5) + b * np.float32(0.5)))
+
+
+def test_batch_is_independent_per_pair(params):
+    from synth import shifted_pair
+    pairs = [shifted_pair(64, 96, seed=50 + i) for i in range(3)]
+    a = f16(np.stack([p[0] for p in pairs]))
+    b = f16(np.stack([p[1] for p in pairs]))
+    together = run_ifnet(a, b, 0.5, params)
+    for i in range(3):
+        alone = run_ifnet(a[i:i + 1], b[i:i + 1], 0.5, params, max_batch=3)
+        np.testing.assert_array_equal(together[i:i + 1], alone)
+
+
+def test_ifnet_refusals(params):
+    import torch
+    blob = kb.make_blob(kb.MODEL_IFNET, nets.ifnet_flat(params))
+    with pytest.raises(kb.KB2Error) as e:
+        kb.Engine(kb.MODEL_IFNET, blob, 64, 64, precision=kb.PREC_FP8)
+    assert e.value.status == kb.KB2_FORMAT_UNSUPPORTED
+    eng = kb.Engine(kb.MODEL_IFNET, blob, 64, 64, max_batch=1)
+    try:
+        for bad in (0.0, 1.0, 1.5, float("nan")):
+            with pytest.raises(kb.KB2Error) as e:
+                eng.set_timestep(bad)
+            assert e.value.status == kb.KB2_INVALID_ARGUMENT
+        x = torch.zeros((1, 3, 64, 64), dtype=torch.float16, device="cuda")
+        out = torch.zeros((1, 3, 64, 64), dtype=torch.float16, device="cuda")
+        with pytest.raises(kb.KB2Error) as e:
+            eng.enqueue([x], [out])  # one frame instead of two
+        assert e.value.status == kb.KB2_INPUT_MISMATCH
+        with pytest.raises(kb.KB2Error) as e:
+            eng.enqueue([x, torch.zeros((1, 3, 64, 32), dtype=torch.float16, device="cuda")], [out])
+        assert e.value.status == kb.KB2_INPUT_MISMATCH
+        big = torch.zeros((2, 3, 64, 64), dtype=torch.float16, device="cuda")
+        with pytest.raises(kb.KB2Error) as e:
+            eng.enqueue([big, big], [torch.zeros_like(big)])
+        assert e.value.status == kb.KB2_SHAPE_INVALID
+    finally:
+        eng.close()

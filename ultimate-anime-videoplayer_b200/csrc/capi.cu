@@ -7,6 +7,7 @@
 
 #include "kirari_b200.h"
 #include "engine.h"
+#include "ifnet_net.h"
 
 namespace {
 thread_local std::string g_create_error;
@@ -150,6 +151,14 @@ int kb2_span_calibrate_static(kb2_engine* engine, void* stream, const kb2_tensor
                      engine->impl->calibrate_static(static_cast<cudaStream_t>(stream), *frames, peaks, n_peaks));
   } catch (const std::exception& ex) {
     return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
+int kb2_warp_taps(void* stream, const float* flow, int32_t n, int32_t h, int32_t w, int32_t* taps, float* weights) {
+  try {
+    return kb2::warp_taps(static_cast<cudaStream_t>(stream), flow, n, h, w, taps, weights).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
   }
 }
 

@@ -2,6 +2,7 @@
 #include <cstring>
 
 #include "engine.h"
+#include "ifnet_net.h"
 #include "span_net.h"
 #include "static_scratch.h"
 
@@ -96,6 +97,56 @@ class SpanEngine final : public Engine {
   SpanNet net_;
 };
 
+class IfnetEngine final : public Engine {
+ public:
+  Status init(const kb2_engine_desc& d, const std::vector<float>& params) {
+    if (d.precision != KB2_PREC_FP16) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet runs in FP16 only");
+    return net_.create(params, d.max_batch, d.height, d.width);
+  }
+  std::vector<std::string> input_names() const override { return {"img0", "img1"}; }
+  std::vector<std::string> output_names() const override { return {"output"}; }
+  int max_batch() const override { return net_.max_batch(); }
+  int height() const override { return net_.height(); }
+  int width() const override { return net_.width(); }
+  size_t device_bytes() const override { return net_.device_bytes(); }
+  Status enqueue(cudaStream_t stream, const kb2_tensor* inputs, int n_inputs, const kb2_tensor* outputs,
+                 int n_outputs) override {
+    void* in[2] = {nullptr, nullptr};
+    void* out = nullptr;
+    int batch = 0;
+    KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 2, 1, in, &out, &batch));
+    if (inputs[1].dims[0] != inputs[0].dims[0]) return refuse(KB2_INPUT_MISMATCH, "IFNet: frame counts differ");
+    return net_.run(stream, in[0], in[1], out, batch);
+  }
+  Status set_timestep(float t) override { return net_.set_timestep(t); }
+  Status set_profiling(bool on) override {
+    net_.timer().enable(on);
+    return Status::Ok();
+  }
+  Status read_profile(kb2_layer_profile* records, int capacity, int* count) override {
+    std::vector<LayerTimer::Record> kinds;
+    KB2_TRY(net_.timer().read(kinds));
+    *count = static_cast<int>(kinds.size());
+    for (int i = 0; i < *count && i < capacity; ++i) {
+      kb2_layer_profile& r = records[i];
+      std::memset(&r, 0, sizeof(r));
+      std::strncpy(r.name, kinds[i].name.c_str(), sizeof(r.name) - 1);
+      r.launches = kinds[i].launches;
+      r.total_ms = kinds[i].ms;
+      r.flops = kinds[i].flops;
+      r.bytes = kinds[i].bytes;
+    }
+    return Status::Ok();
+  }
+  int launches_per_enqueue() const override { return net_.launches_per_run(); }
+
+ protected:
+  int* err_word() const override { return net_.err_word(); }
+
+ private:
+  IfnetNet net_;
+};
+
 }  // namespace
 
 Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
@@ -120,7 +171,12 @@ Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
     out = std::move(e);
     return Status::Ok();
   }
-  if (d.model == KB2_MODEL_IFNET) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet engine not built in this library");
+  if (d.model == KB2_MODEL_IFNET) {
+    auto e = std::make_unique<IfnetEngine>();
+    KB2_TRY(e->init(d, params));
+    out = std::move(e);
+    return Status::Ok();
+  }
   return refuse(KB2_FORMAT_UNSUPPORTED, "unknown model");
 }
 

@@ -1,0 +1,59 @@
+// Classic IFNet (RIFE 4.x, four blocks at 1/8 .. 1/1) on the tensor-core IFNet convs and the glue
+// kernels (see ifnet_net.cu).
+#pragma once
+
+#include <memory>
+#include <vector>
+
+#include "layer_timer.h"
+
+namespace kb2 {
+
+constexpr size_t kIfnetParams = 5160980;  // oracle/nets.py ifnet_param_shapes
+// Padded frame: multiples of 32, what the network needs (its coarsest level is 1/32 of the frame).
+// The reference pads to 64 for its RIFE 4.x models (src/kernels/spec/rife.h:33); for 1920x1080 both
+// give 1920x1088.
+constexpr int kIfnetAlign = 32;
+
+struct IfLayer;
+
+class IfnetNet {
+ public:
+  IfnetNet();
+  ~IfnetNet();
+  Status create(const std::vector<float>& params, int max_batch, int H, int W);
+  // img0 / img1: NCHW F16 [batch][3][H][W]; out: NCHW F16 [batch][3][H][W] (device pointers).
+  Status run(cudaStream_t stream, const void* img0, const void* img1, void* out, int batch);
+  Status set_timestep(float t);
+  size_t device_bytes() const;
+  int* err_word() const { return err_.as<int>(); }
+  int height() const { return H_; }
+  int width() const { return W_; }
+  int max_batch() const { return max_batch_; }
+  int launches_per_run() const;
+  LayerTimer& timer() { return timer_; }
+
+ private:
+  struct Tensor {
+    uint8_t* ptr = nullptr;
+    int H = 0, W = 0, chunks = 0;
+    DeviceBuffer buf;
+  };
+  Status tensor(std::unique_ptr<Tensor>& t, int H, int W, int chunks);
+
+  int max_batch_ = 0, H_ = 0, W_ = 0, Hp_ = 0, Wp_ = 0, top_ = 0, left_ = 0;
+  float timestep_ = 0.5f;
+  DeviceBuffer err_;
+  std::vector<std::unique_ptr<Tensor>> tensors_;
+  std::vector<std::unique_ptr<IfLayer>> layers_;  // per block: conv0a, conv0b, 8 residual, convT
+  const Tensor* x_[4] = {};                       // block inputs
+  DeviceBuffer flows_[4];                         // transposed-conv outputs, FP32 [n][5][Hp/2s][Wp/2s]
+  LayerTimer timer_;
+  int k_glue_ = 0, k_blend_ = 0;
+};
+
+// Bilinear backward-warp taps of a flow field [n][2][h][w] (FP32, device): x0, x1, y0, y1 as int32
+// planes [n][4][h][w] and wx, wy as FP32 planes [n][2][h][w] (kb2_warp_taps).
+Status warp_taps(cudaStream_t stream, const float* flow, int n, int h, int w, int32_t* taps, float* weights);
+
+}  // namespace kb2

@@ -36,7 +36,8 @@ PREC_FP8 = 2
 # every entry point of include/kirari_b200.h
 EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "kb2_last_error",
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
-           "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static")
+           "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
+           "kb2_warp_taps")
 
 
 class KB2Error(RuntimeError):
@@ -88,6 +89,8 @@ def lib():
                                          ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
         L.kb2_span_calibrate_static.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Tensor),
                                                 ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
+        L.kb2_warp_taps.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                    ctypes.c_void_p, ctypes.c_void_p]
         L.kb2_set_profiling.argtypes = [ctypes.c_void_p, ctypes.c_int32]
         L.kb2_read_profile.argtypes = [ctypes.c_void_p, ctypes.POINTER(LayerProfile), ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_int32)]
@@ -209,3 +212,18 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+def warp_taps(flow, stream=None):
+    """Device warp taps of a flow field (torch float32 CUDA tensor [n, 2, h, w]):
+    returns (taps int32 [n, 4, h, w] = x0, x1, y0, y1; weights float32 [n, 2, h, w] = wx, wy)."""
+    import torch
+    n, two, h, w = flow.shape
+    assert two == 2 and flow.dtype == torch.float32 and flow.is_cuda and flow.is_contiguous()
+    taps = torch.empty((n, 4, h, w), dtype=torch.int32, device=flow.device)
+    weights = torch.empty((n, 2, h, w), dtype=torch.float32, device=flow.device)
+    rc = lib().kb2_warp_taps(_stream_handle(stream), ctypes.c_void_p(flow.data_ptr()), n, h, w,
+                             ctypes.c_void_p(taps.data_ptr()), ctypes.c_void_p(weights.data_ptr()))
+    if rc != KB2_OK:
+        raise KB2Error(rc, "kb2_warp_taps")
+    return taps, weights
