@@ -1,10 +1,12 @@
 """Benchmark of the frame path: SPAN x2 1080p -> 2160p on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8|rife] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: frames shard across GPUs, no collective)
 
 A step is one batch of 8 synthetic 1080p frames through the engine (the contract's configs[1]:
-FP16, batch 8, 240 frames per GPU by default = 30 steps). `value` is whole-job frames/s with the
+FP16, batch 8, 240 frames per GPU by default = 30 steps); `--workload span8` is configs[2] (FP8
+E4M3), `--workload rife` is configs[3] (IFNet FP16, 8 frame pairs per step at t = 0.5;
+`--height 2160 --width 3840` for the 4K interpolation rate). `value` is whole-job frames/s with the
 inputs resident in HBM; `e2e` is the same through the public C ABI with pinned host frames, the
 host->device copy and the device->host read of every output inside the timed region. `roofline`
 times the dominant kernel with CUDA events on its launching stream during the timed steps.
@@ -38,10 +40,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["span16", "span8"], default="span16")
+    ap.add_argument("--workload", choices=["span16", "span8", "rife"], default="span16")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--height", type=int, default=FRAME_H)
     ap.add_argument("--width", type=int, default=FRAME_W)
+    ap.add_argument("--timestep", type=float, default=0.5)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -120,26 +123,37 @@ class ClockSampler:
 CROP_H, CROP_W = 24, 48
 
 
-def reference_sample(threads, frame, flat, crops_per_thread=1):
-    """Each host thread runs the reference's FP32 SPAN on its own crop of the frame (the interpreter
-    is single-threaded per call); returns (frames processed, seconds)."""
+RIFE_CROP_H, RIFE_CROP_W = 64, 96  # IFNet needs multiples of 32
+
+
+def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, timestep=0.5, full=None):
+    """Each host thread runs the reference's FP32 network on its own crop of the frame (the
+    interpreter is single-threaded per call); returns (frames processed, seconds). SPAN when
+    frame_b is None, else IFNet on the crop pair."""
     from oracle import ref_lib
     import numpy as np
 
+    rife = frame_b is not None
+    ch, cw = (RIFE_CROP_H, RIFE_CROP_W) if rife else (CROP_H, CROP_W)
     H, W = frame.shape[1:]
     rng = np.random.default_rng(0)
     jobs = []
     for t in range(threads):
         for _ in range(crops_per_thread):
-            y = int(rng.integers(0, H - CROP_H))
-            x = int(rng.integers(0, W - CROP_W))
-            jobs.append((t, np.ascontiguousarray(frame[None, :, y:y + CROP_H, x:x + CROP_W])))
+            y = int(rng.integers(0, H - ch))
+            x = int(rng.integers(0, W - cw))
+            a = np.ascontiguousarray(frame[None, :, y:y + ch, x:x + cw])
+            b = np.ascontiguousarray(frame_b[None, :, y:y + ch, x:x + cw]) if rife else None
+            jobs.append((t, a, b))
     done = [0] * threads
 
     def work(t):
-        for tt, crop in jobs:
+        for tt, a, b in jobs:
             if tt == t:
-                ref_lib.span_forward(crop, flat)
+                if rife:
+                    ref_lib.ifnet_forward(a, b, timestep, flat)
+                else:
+                    ref_lib.span_forward(a, flat)
                 done[t] += 1
 
     ts = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
@@ -149,7 +163,8 @@ def reference_sample(threads, frame, flat, crops_per_thread=1):
     for th in ts:
         th.join()
     dt = time.perf_counter() - t0
-    return sum(done) * CROP_H * CROP_W / float(FRAME_H * FRAME_W), dt
+    fh, fw = full if full is not None else (FRAME_H, FRAME_W)
+    return sum(done) * ch * cw / float(fh * fw), dt
 
 
 def host_cores():
@@ -159,18 +174,42 @@ def host_cores():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(frame, flat, budget_s=12.0):
+def cpu_baseline(frame, flat, budget_s=12.0, frame_b=None, timestep=0.5, full=None):
     from oracle import ref_lib
     if not ref_lib.available():
         return None
     cores = host_cores()
-    frames, dt = reference_sample(cores, frame, flat)
+    kw = dict(frame_b=frame_b, timestep=timestep, full=full)
+    frames, dt = reference_sample(cores, frame, flat, **kw)
     reps = max(1, int(budget_s / max(dt, 1e-3)))
     if reps > 1:
-        frames, dt = reference_sample(cores, frame, flat, crops_per_thread=reps)
+        frames, dt = reference_sample(cores, frame, flat, crops_per_thread=reps, **kw)
+    ch, cw = (RIFE_CROP_H, RIFE_CROP_W) if frame_b is not None else (CROP_H, CROP_W)
+    fh, fw = full if full is not None else (FRAME_H, FRAME_W)
+    net = "IFNet pairs" if frame_b is not None else "SPAN"
     return {"value": frames / dt, "unit": "frames/s", "cores": cores, "kind": "reference",
-            "sample": f"{cores} threads x {reps} crops of {CROP_H}x{CROP_W} px of a synthetic 1080p frame, "
-                      f"reference FP32 IR interpreter (oracle/_ref), scaled by pixels to 1920x1080 frames"}
+            "sample": f"{cores} threads x {reps} {net} crops of {ch}x{cw} px of synthetic {fw}x{fh} frames, "
+                      f"reference FP32 IR interpreter (oracle/_ref), scaled by pixels to {fw}x{fh} frames"}
+
+
+def workload_desc(args, world=1):
+    """metric, unit, dtype, config of the workload (shared by both arms)."""
+    B, H, W = args.batch, args.height, args.width
+    if args.workload == "rife":
+        metric = f"RIFE IFNet {W}x{H} interpolated frames/s"
+        config = {"workload": f"configs[3] IFNet FP16, {B} frame pairs per step, {W}x{H}, t={args.timestep}",
+                  "global_batch": B * world, "frames_per_gpu": B * args.steps,
+                  "parallelism": f"pair-sharded x{world}, no collective",
+                  "l2": "working set > L2: block 3 reads and writes 8 x 67 MB inputs and 8 x 33 MB activations"}
+        return metric, "f16", config
+    fp8 = args.workload == "span8"
+    metric = "SPAN x2 1080p->2160p frames/s" if (H, W) == (FRAME_H, FRAME_W) else f"SPAN x2 {W}x{H} frames/s"
+    config = {"workload": ("configs[2] SPAN x2 FP8 E4M3" if fp8 else "configs[1] SPAN x2 FP16")
+                          + f", batch {B}, {H}x{W} -> {2 * H}x{2 * W}",
+              "global_batch": B * world, "frames_per_gpu": B * args.steps,
+              "parallelism": f"frame-sharded x{world}, no collective",
+              "l2": "working set > L2: each layer reads and writes 8 x 199 MB activations"}
+    return metric, ("e4m3+f16" if fp8 else "f16"), config
 
 
 def run_reference(args):
@@ -179,31 +218,39 @@ def run_reference(args):
         return
     import numpy as np
     from oracle import nets, ref_lib
-    from synth import anime_frame
+    from synth import anime_frame, shifted_pair
 
-    config = {"workload": "span_x2 1080p->2160p (configs[1] network), reference FP32 CPU path",
-              "height": args.height, "width": args.width, "batch": args.batch}
+    metric, _, config = workload_desc(args, world)
+    config = dict(config, workload=config["workload"] + ", reference FP32 CPU path")
     if not ref_lib.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
         return
-    frame = anime_frame(args.height, args.width, 0).astype(np.float32)
-    flat = nets.span_flat(nets.span_init(1))
+    rife = args.workload == "rife"
+    if rife:
+        fa, fb = shifted_pair(args.height, args.width, 0)
+        frame, frame_b = np.ascontiguousarray(fa, np.float32), np.ascontiguousarray(fb, np.float32)
+        flat = nets.ifnet_flat(nets.ifnet_init(2))
+    else:
+        frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
+        flat = nets.span_flat(nets.span_init(1))
+    kw = dict(frame_b=frame_b, timestep=args.timestep, full=(args.height, args.width))
     cores = host_cores()
     for _ in range(args.warmup):
-        reference_sample(cores, frame, flat)
+        reference_sample(cores, frame, flat, **kw)
     total_frames, total_s = 0.0, 0.0
     for _ in range(args.steps):
-        f, dt = reference_sample(cores, frame, flat)
+        f, dt = reference_sample(cores, frame, flat, **kw)
         total_frames += f
         total_s += dt
     value = total_frames / total_s
-    line = {"metric": "SPAN x2 1080p->2160p frames/s", "value": value, "unit": "frames/s", "n_gpus": world,
+    ch, cw = (RIFE_CROP_H, RIFE_CROP_W) if rife else (CROP_H, CROP_W)
+    line = {"metric": metric, "value": value, "unit": "frames/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference", "config": config,
             "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cores, "kind": "reference",
-                             "sample": f"per step: {cores} threads x 1 crop of {CROP_H}x{CROP_W} px, "
-                                       "scaled by pixels to 1920x1080 frames"},
+                             "sample": f"per step: {cores} threads x 1 crop of {ch}x{cw} px, "
+                                       f"scaled by pixels to {args.width}x{args.height} frames"},
             "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -218,7 +265,7 @@ def run_ours(args):
 
     import kirari_b200 as kb
     from oracle import nets
-    from synth import anime_frames
+    from synth import anime_frames, shifted_pair
 
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)
@@ -241,26 +288,43 @@ def run_ours(args):
         return float(t.item())
 
     B, H, W = args.batch, args.height, args.width
-    p = nets.span_init(1)
-    flat = nets.span_flat(p)
-    blob = kb.make_blob(kb.MODEL_SPAN_X2, flat)
-    frames = anime_frames(B, H, W, seed=10 + rank)
+    rife = args.workload == "rife"
     fp8 = args.workload == "span8"
-    scales = None
-    if fp8:
-        calib = torch.from_numpy(anime_frames(16, H, W, seed=1000).astype(np.float16)).cuda()
-        e16 = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B, device=local_rank)
-        peaks = e16.calibrate(calib)
-        e16.close()
-        del calib
-        scales = nets.span_scales_from_peaks(peaks, floor=2.0 ** -14)
-    eng = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B, precision=kb.PREC_FP8 if fp8 else kb.PREC_FP16,
-                    act_scales=scales, device=local_rank)
-    d_in = torch.from_numpy(frames.astype(np.float16)).cuda()
-    d_out = torch.empty((B, 3, 2 * H, 2 * W), dtype=torch.float16, device="cuda")
+    metric, dtype, config = workload_desc(args, world)
+    if rife:
+        p = nets.ifnet_init(2)
+        flat = nets.ifnet_flat(p)
+        blob = kb.make_blob(kb.MODEL_IFNET, flat)
+        pairs = [shifted_pair(H, W, seed=10 + 97 * rank + i) for i in range(B)]
+        frames = np.ascontiguousarray(np.stack([q[0] for q in pairs]), np.float16)
+        frames_b = np.ascontiguousarray(np.stack([q[1] for q in pairs]), np.float16)
+        eng = kb.Engine(kb.MODEL_IFNET, blob, H, W, max_batch=B, device=local_rank)
+        eng.set_timestep(args.timestep)
+        host_in = [frames, frames_b]
+        out_shape = (B, 3, H, W)
+    else:
+        p = nets.span_init(1)
+        flat = nets.span_flat(p)
+        blob = kb.make_blob(kb.MODEL_SPAN_X2, flat)
+        frames = anime_frames(B, H, W, seed=10 + rank).astype(np.float16)
+        frames_b = None
+        scales = None
+        if fp8:
+            calib = torch.from_numpy(anime_frames(16, H, W, seed=1000).astype(np.float16)).cuda()
+            e16 = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B, device=local_rank)
+            peaks = e16.calibrate(calib)
+            e16.close()
+            del calib
+            scales = nets.span_scales_from_peaks(peaks, floor=2.0 ** -14)
+        eng = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B, precision=kb.PREC_FP8 if fp8 else kb.PREC_FP16,
+                        act_scales=scales, device=local_rank)
+        host_in = [frames]
+        out_shape = (B, 3, 2 * H, 2 * W)
+    d_in = [torch.from_numpy(x).cuda() for x in host_in]
+    d_out = torch.empty(out_shape, dtype=torch.float16, device="cuda")
     stream = torch.cuda.Stream()
     sh = kb.ctypes.c_void_p(stream.cuda_stream)
-    ins = (kb.Tensor * 1)(kb.to_kb2_tensor(d_in))
+    ins = (kb.Tensor * len(d_in))(*[kb.to_kb2_tensor(t) for t in d_in])
     outs = (kb.Tensor * 1)(kb.to_kb2_tensor(d_out))
 
     # ---- device-resident timing
@@ -300,12 +364,14 @@ def run_ours(args):
             traffic = json.load(f).get(top_name, {}).get(f"{B}x{H}x{W}")
     except (OSError, ValueError):
         pass
+    total_flops = sum(v["flops"] * v["launches"] for v in profile.values())
     roofline = {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
                 "traffic": traffic, "kernel": top_name, "launches": top["launches"],
                 "avg_launch_ms": avg_ms, "flops_per_launch": top["flops"],
                 "algorithmic_bytes_per_launch": top["bytes"],
                 "peak_source": f"{peak_kind} bf16_tflops_sustained" + (" x2 (E4M3)" if top_name.endswith(".fp8") else ""),
-                "network_tflops": FLOP_PER_PX * H * W * B * args.steps / (ms / 1e3) / 1e12}
+                "network_tflops": (total_flops / (ms / 1e3) / 1e12) if rife else
+                FLOP_PER_PX * H * W * B * args.steps / (ms / 1e3) / 1e12}
     layers = {k: {"launches": v["launches"], "ms_per_launch": v["total_ms"] / max(1, v["launches"]),
                   "share": v["total_ms"] / max(1e-9, sum(x["total_ms"] for x in profile.values()))}
               for k, v in profile.items()}
@@ -313,12 +379,12 @@ def run_ours(args):
     # ---- end to end through the C ABI with host frames (pinned), copies in the timed region
     e2e = None
     if not args.no_e2e:
-        h_in = torch.from_numpy(frames.astype(np.float16)).pin_memory()
-        h_out = [torch.empty((B, 3, 2 * H, 2 * W), dtype=torch.float16).pin_memory() for _ in range(2)]
-        d_ins = [torch.empty_like(d_in) for _ in range(2)]
+        h_in = [torch.from_numpy(x).pin_memory() for x in host_in]
+        h_out = [torch.empty(out_shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+        d_ins = [[torch.empty_like(t) for t in d_in] for _ in range(2)]
         d_outs = [d_out, torch.empty_like(d_out)]
         s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
-        ins2 = [(kb.Tensor * 1)(kb.to_kb2_tensor(t)) for t in d_ins]
+        ins2 = [(kb.Tensor * len(d_in))(*[kb.to_kb2_tensor(t) for t in ts]) for ts in d_ins]
         outs2 = [(kb.Tensor * 1)(kb.to_kb2_tensor(t)) for t in d_outs]
         ev_in = [torch.cuda.Event() for _ in range(2)]
         ev_done = [torch.cuda.Event() for _ in range(2)]
@@ -329,7 +395,8 @@ def run_ours(args):
                 k = i % 2
                 with torch.cuda.stream(s_h2d):
                     s_h2d.wait_event(ev_free[k]) if i >= 2 else None
-                    d_ins[k].copy_(h_in, non_blocking=True)
+                    for dst, src in zip(d_ins[k], h_in):
+                        dst.copy_(src, non_blocking=True)
                     ev_in[k].record(s_h2d)
                 stream.wait_event(ev_in[k])
                 if i >= 2:
@@ -349,7 +416,8 @@ def run_ours(args):
         barrier()
         e2e_s = max_over_ranks(time.perf_counter() - t0)
         e2e = {"value": world * B * args.steps / e2e_s, "unit": "frames/s",
-               "h2d_bytes_per_step": int(h_in.numel() * 2), "d2h_bytes_per_step": int(h_out[0].numel() * 2),
+               "h2d_bytes_per_step": int(sum(t.numel() * 2 for t in h_in)),
+               "d2h_bytes_per_step": int(h_out[0].numel() * 2),
                "path": "kb2_enqueue with pinned host frames: H2D copy, enqueue, D2H of every output frame, "
                        "double-buffered across three streams"}
         eng.check_device(stream)
@@ -357,20 +425,17 @@ def run_ours(args):
     launches = args.steps * eng.launches_per_enqueue()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(frames[0], flat)
+        cpu = cpu_baseline(frames[0].astype(np.float32), flat,
+                           frame_b=frames_b[0].astype(np.float32) if rife else None,
+                           timestep=args.timestep, full=(H, W))
     eng.close()
     if rank == 0:
-        line = {"metric": "SPAN x2 1080p->2160p frames/s", "value": value, "unit": "frames/s", "n_gpus": world,
+        line = {"metric": metric, "value": value, "unit": "frames/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "e4m3+f16" if fp8 else "f16", "data": "synthetic (seeded anime-like frames, seeded weights)",
-                "config": {"workload": ("configs[2] SPAN x2 FP8 E4M3" if fp8 else "configs[1] SPAN x2 FP16")
-                           + f", batch {B}, {H}x{W} -> {2 * H}x{2 * W}",
-                           "global_batch": B * world, "frames_per_gpu": B * args.steps,
-                           "parallelism": f"frame-sharded x{world}, no collective",
-                           "l2": "working set > L2: each layer reads and writes 8 x 199 MB activations"},
-                "roofline": roofline, "layers": layers, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
-                "cpu_baseline": cpu}
+                "dtype": dtype, "data": "synthetic (seeded anime-like frames, seeded weights)",
+                "config": config, "roofline": roofline, "layers": layers, "e2e": e2e, "gpu_launches": launches,
+                "clocks": clk, "cpu_baseline": cpu}
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

@@ -151,8 +151,8 @@ typedef struct kb2_layer_profile {
   char name[48];         /* layer kind, e.g. "span.block_conv.fp16.silu" */
   uint64_t launches;     /* launches timed */
   double total_ms;       /* summed device time */
-  double flops;          /* algorithmic FLOPs per launch at the last batch (direct-conv MACs x 2) */
-  double bytes;          /* algorithmic HBM bytes per launch at the last batch (inputs + outputs once) */
+  double flops;          /* algorithmic FLOPs per launch (direct-conv MACs x 2), averaged over the launches */
+  double bytes;          /* algorithmic HBM bytes per launch (inputs + outputs once), averaged likewise */
 } kb2_layer_profile;
 
 int kb2_set_profiling(kb2_engine* engine, int32_t enable);

@@ -8,10 +8,10 @@
 //    the whole padded plane, as the reference IR's GridSample (border, align_corners = 0);
 //  * half-pixel linear resize (src/gpu/ir/op_sample.cpp:88-170): position (o + 0.5) / scale - 0.5
 //    in FP32 with scale = n_out / n_in, clamped to [0, n_in - 1], truncated;
-//  * the flow and mask of the network are never stored at full resolution. The transposed conv of
-//    block j leaves a small FP32 tensor (5 planes at 1/(2 s_j) of the frame). The flow at a pixel
-//    is the sum, in block order, of those tensors resized to the pixel and scaled by 2 s_j, which
-//    is what the sequential `flow = flow + resize(...)` of the network computes.
+//  * the transposed conv of block j leaves a small FP32 tensor (5 planes at 1/(2 s_j) of the
+//    frame). After each block, one pass adds it, resized to full resolution and scaled by 2 s_j,
+//    to the full-resolution FP32 flow / mask planes: the network's sequential
+//    `flow = flow + resize(...)`, in the same order.
 //
 // Every product and sum is written with the _rn intrinsics, in the order the network states it,
 // so that no multiply-add contraction changes a warp position.
@@ -74,33 +74,63 @@ __device__ __forceinline__ AxisTap warp_tap(int p, float f, int n) {
   return r;
 }
 
-// Flow (4) and mask after blocks [0, k) at padded pixel (Y, X) of frame n.
-__device__ __forceinline__ void flow_at(const IfFlowLevels& L, int k, int n, int Y, int X, int Hp, int Wp,
-                                        float f[4], float* mask) {
-  for (int j = 0; j < k; ++j) {
-    const AxisTap ty = resize_tap(Y, L.h[j], Hp);
-    const AxisTap tx = resize_tap(X, L.w[j], Wp);
-    const size_t plane = static_cast<size_t>(L.h[j]) * L.w[j];
-    const float* base = L.t[j] + static_cast<size_t>(n) * 5 * plane;
-    float v[5];
+// Adds block j's contribution at padded pixel (Y, X) of frame n to the flow (4) and mask; block 0
+// sets them.
+__device__ __forceinline__ void flow_step(const IfFlowLevels& L, int j, int n, int Y, int X, int Hp, int Wp,
+                                          float f[4], float* mask) {
+  const AxisTap ty = resize_tap(Y, L.h[j], Hp);
+  const AxisTap tx = resize_tap(X, L.w[j], Wp);
+  const size_t plane = static_cast<size_t>(L.h[j]) * L.w[j];
+  const float* base = L.t[j] + static_cast<size_t>(n) * 5 * plane;
+  float v[5];
 #pragma unroll
-    for (int c = 0; c < 5; ++c) {
-      const float* p = base + c * plane;
-      const float a = __ldg(p + static_cast<size_t>(ty.lo) * L.w[j] + tx.lo);
-      const float b = __ldg(p + static_cast<size_t>(ty.lo) * L.w[j] + tx.hi);
-      const float d = __ldg(p + static_cast<size_t>(ty.hi) * L.w[j] + tx.lo);
-      const float e = __ldg(p + static_cast<size_t>(ty.hi) * L.w[j] + tx.hi);
-      v[c] = lerp_rn(lerp_rn(a, b, tx.t), lerp_rn(d, e, tx.t), ty.t);
+  for (int c = 0; c < 5; ++c) {
+    const float* p = base + c * plane;
+    const float a = __ldg(p + static_cast<size_t>(ty.lo) * L.w[j] + tx.lo);
+    const float b = __ldg(p + static_cast<size_t>(ty.lo) * L.w[j] + tx.hi);
+    const float d = __ldg(p + static_cast<size_t>(ty.hi) * L.w[j] + tx.lo);
+    const float e = __ldg(p + static_cast<size_t>(ty.hi) * L.w[j] + tx.hi);
+    v[c] = lerp_rn(lerp_rn(a, b, tx.t), lerp_rn(d, e, tx.t), ty.t);
+  }
+  if (j == 0) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) f[c] = __fmul_rn(v[c], L.mul[j]);
+    *mask = v[4];
+  } else {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) f[c] = __fadd_rn(f[c], __fmul_rn(v[c], L.mul[j]));
+    *mask = __fadd_rn(*mask, v[4]);
+  }
+}
+
+// Full-resolution flow (planes 0-3) and mask (plane 4) after the blocks so far: FP32 [n][5][Hp][Wp].
+struct IfFlowField {
+  float* f;
+  int Hp, Wp;
+  __device__ __forceinline__ size_t at(int n, int c, int Y, int X) const {
+    return ((static_cast<size_t>(n) * 5 + c) * Hp + Y) * Wp + X;
+  }
+};
+
+// flow / mask += block k's transposed-conv output resized to full resolution (flow x 2 s); block 0
+// sets them.
+__global__ void ifnet_flow_update_kernel(IfFlowLevels L, int k, int batch, IfFlowField F) {
+  const long long total = static_cast<long long>(batch) * F.Hp * F.Wp;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int X = static_cast<int>(i % F.Wp);
+    const int Y = static_cast<int>((i / F.Wp) % F.Hp);
+    const int n = static_cast<int>(i / (static_cast<long long>(F.Wp) * F.Hp));
+    float f[4], mask;
+    if (k > 0) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) f[c] = F.f[F.at(n, c, Y, X)];
+      mask = F.f[F.at(n, 4, Y, X)];
     }
-    if (j == 0) {
+    flow_step(L, k, n, Y, X, F.Hp, F.Wp, f, &mask);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) f[c] = __fmul_rn(v[c], L.mul[j]);
-      *mask = v[4];
-    } else {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) f[c] = __fadd_rn(f[c], __fmul_rn(v[c], L.mul[j]));
-      *mask = __fadd_rn(*mask, v[4]);
-    }
+    for (int c = 0; c < 4; ++c) F.f[F.at(n, c, Y, X)] = f[c];
+    F.f[F.at(n, 4, Y, X)] = mask;
   }
 }
 
@@ -132,10 +162,12 @@ __device__ __forceinline__ void warp3(const __half* img, const IfFrames& F, int 
 
 // The 12 input planes of block k >= 1 at padded full-resolution pixel (Y, X): warped frames (6),
 // timestep, mask, flow (4, not yet divided by the block scale).
-__device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowLevels& L, int k, int n, int Y, int X,
+__device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowField& FF, int n, int Y, int X,
                                              float timestep, float v[12]) {
-  float f[4], mask;
-  flow_at(L, k, n, Y, X, F.Hp, F.Wp, f, &mask);
+  float f[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) f[c] = __ldg(FF.f + FF.at(n, c, Y, X));
+  const float mask = __ldg(FF.f + FF.at(n, 4, Y, X));
   warp3(F.img0, F, n, Y, X, f[0], f[1], v);
   warp3(F.img1, F, n, Y, X, f[2], f[3], v + 3);
   v[6] = timestep;
@@ -146,7 +178,7 @@ __device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowLeve
 
 // Input of block k as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used):
 // the block's planes resized to 1/s (not for s = 1), the flow planes then divided by s.
-__global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, int k, int batch, float timestep,
+__global__ void ifnet_block_input_kernel(IfFrames F, IfFlowField FF, int k, int batch, float timestep,
                                          uint8_t* __restrict__ out) {
   const int s = if_scale(k);
   const int ho = F.Hp / s, wo = F.Wp / s;
@@ -161,7 +193,7 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, int k, int 
     for (int c = 0; c < 16; ++c) v[c] = 0.0f;
     const int nc = k == 0 ? 7 : 12;
     if (s == 1) {
-      block_planes(F, L, k, n, oy, ox, timestep, v);
+      block_planes(F, FF, n, oy, ox, timestep, v);
     } else {
       const AxisTap ty = resize_tap(oy, F.Hp, ho);
       const AxisTap tx = resize_tap(ox, F.Wp, wo);
@@ -179,7 +211,7 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, int k, int 
             }
             p[6] = timestep;
           } else {
-            block_planes(F, L, k, n, ys[yy], xs[xx], timestep, p);
+            block_planes(F, FF, n, ys[yy], xs[xx], timestep, p);
           }
         }
       for (int c = 0; c < nc; ++c)
@@ -209,7 +241,7 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, int k, int 
 
 // The interpolated frame: warp both frames by the final flow, blend with sigmoid(mask), crop the
 // window: out = w0 * m + w1 * (1 - m), NCHW FP16 [n][3][H][W].
-__global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, int batch, __half* __restrict__ out) {
+__global__ void ifnet_blend_kernel(IfFrames F, IfFlowField FF, int batch, __half* __restrict__ out) {
   const long long total = static_cast<long long>(batch) * F.H * F.W;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -217,8 +249,10 @@ __global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, int batch, __half
     const int y = static_cast<int>((i / F.W) % F.H);
     const int n = static_cast<int>(i / (static_cast<long long>(F.W) * F.H));
     const int Y = y + F.top, X = x + F.left;
-    float f[4], mask;
-    flow_at(L, kIfBlocks, n, Y, X, F.Hp, F.Wp, f, &mask);
+    float f[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) f[c] = __ldg(FF.f + FF.at(n, c, Y, X));
+    const float mask = __ldg(FF.f + FF.at(n, 4, Y, X));
     float w0[3], w1[3];
     warp3(F.img0, F, n, Y, X, f[0], f[1], w0);
     warp3(F.img1, F, n, Y, X, f[2], f[3], w1);

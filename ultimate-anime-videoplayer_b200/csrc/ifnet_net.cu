@@ -228,6 +228,9 @@ Status IfnetNet::create(const std::vector<float>& params, int max_batch, int H, 
   const int k_c0a = timer_.kind("ifnet.conv0a"), k_c0b = timer_.kind("ifnet.conv0b");
   const int k_res = timer_.kind("ifnet.res"), k_ct = timer_.kind("ifnet.convt");
   k_blend_ = timer_.kind("ifnet.blend");
+  k_flow_ = timer_.kind("ifnet.flow");
+  KB2_TRY(flow_full_.alloc(static_cast<size_t>(max_batch_) * 5 * Hp_ * Wp_ * sizeof(float)));
+  KB2_CUDA(cudaMemset(flow_full_.ptr, 0, flow_full_.bytes));
 
   const float* p = params.data();
   for (int k = 0; k < kIfBlocks; ++k) {
@@ -328,12 +331,13 @@ Status IfnetNet::set_timestep(float t) {
   return Status::Ok();
 }
 
-int IfnetNet::launches_per_run() const { return kIfBlocks + static_cast<int>(layers_.size()) + 1; }
+int IfnetNet::launches_per_run() const { return 2 * kIfBlocks + static_cast<int>(layers_.size()) + 1; }
 
 size_t IfnetNet::device_bytes() const {
   size_t total = err_.bytes;
   for (const auto& t : tensors_) total += t->buf.bytes;
   for (const auto& f : flows_) total += f.bytes;
+  total += flow_full_.bytes;
   for (const auto& l : layers_) total += l->wpack.bytes + l->bias.bytes + l->slope.bytes;
   return total;
 }
@@ -349,13 +353,16 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
     L.w[k] = Wp_ / (2 * s);
     L.mul[k] = static_cast<float>(2 * s);
   }
+  const IfFlowField FF{flow_full_.as<float>(), Hp_, Wp_};
+  const long long full_px = static_cast<long long>(batch) * Hp_ * Wp_;
+  const int full_blocks = static_cast<int>(std::min<long long>((full_px + 255) / 256, 32LL * num_sms()));
   const int per_block = 2 + kIfRes + 1;
   for (int k = 0; k < kIfBlocks; ++k) {
     const int s = if_scale(k);
     const long long px = static_cast<long long>(batch) * (Hp_ / s) * (Wp_ / s);
     const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
     KB2_TRY(timer_.begin(stream));
-    ifnet_block_input_kernel<<<blocks, 256, 0, stream>>>(F, L, k, batch, timestep_, x_[k]->ptr);
+    ifnet_block_input_kernel<<<blocks, 256, 0, stream>>>(F, FF, k, batch, timestep_, x_[k]->ptr);
     KB2_CUDA(cudaGetLastError());
     KB2_TRY(timer_.end(k_glue_, 0.0, px * 32.0, stream));
     for (int i = 0; i < per_block; ++i) {
@@ -365,13 +372,17 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
       KB2_TRY(l.launch(stream, batch));
       KB2_TRY(timer_.end(l.kind, l.flops_px * opx, l.bytes_px * opx, stream));
     }
+    KB2_TRY(timer_.begin(stream));
+    ifnet_flow_update_kernel<<<full_blocks, 256, 0, stream>>>(L, k, batch, FF);
+    KB2_CUDA(cudaGetLastError());
+    KB2_TRY(timer_.end(k_flow_, 0.0, full_px * (k == 0 ? 20.0 : 40.0), stream));
   }
   const long long px = static_cast<long long>(batch) * H_ * W_;
   const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
   KB2_TRY(timer_.begin(stream));
-  ifnet_blend_kernel<<<blocks, 256, 0, stream>>>(F, L, batch, static_cast<__half*>(out));
+  ifnet_blend_kernel<<<blocks, 256, 0, stream>>>(F, FF, batch, static_cast<__half*>(out));
   KB2_CUDA(cudaGetLastError());
-  KB2_TRY(timer_.end(k_blend_, 0.0, px * (12.0 + 6.0), stream));
+  KB2_TRY(timer_.end(k_blend_, 0.0, px * (20.0 + 12.0 + 6.0), stream));
   return Status::Ok();
 }
 

@@ -53,16 +53,24 @@ class LayerTimer {
       Record& k = kinds_[p.kind];
       k.launches += 1;
       k.ms += ms;
-      k.flops = p.flops;
-      k.bytes = p.bytes;
+      k.flops += p.flops;  // sums here; averaged per launch below
+      k.bytes += p.bytes;
       pool_.push_back(p.start);
       pool_.push_back(p.stop);
     }
     pending_.clear();
     out = kinds_;
+    for (Record& r : out) {
+      if (r.launches > 0) {
+        r.flops /= static_cast<double>(r.launches);
+        r.bytes /= static_cast<double>(r.launches);
+      }
+    }
     for (Record& k : kinds_) {
       k.launches = 0;
       k.ms = 0.0;
+      k.flops = 0.0;
+      k.bytes = 0.0;
     }
     return Status::Ok();
   }
