@@ -274,18 +274,13 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
 
+    import shard
+
     def barrier():
-        if world > 1:
-            t = torch.ones(1, device="cuda")
-            dist.all_reduce(t)
-        torch.cuda.synchronize()
+        shard.barrier("cuda")
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(v, "cuda")
 
     B, H, W = args.batch, args.height, args.width
     rife = args.workload == "rife"
@@ -295,7 +290,7 @@ def run_ours(args):
         p = nets.ifnet_init(2)
         flat = nets.ifnet_flat(p)
         blob = kb.make_blob(kb.MODEL_IFNET, flat)
-        pairs = [shifted_pair(H, W, seed=10 + 97 * rank + i) for i in range(B)]
+        pairs = [shifted_pair(H, W, seed=shard.frame_seed(10, rank, i)) for i in range(B)]
         frames = np.ascontiguousarray(np.stack([q[0] for q in pairs]), np.float16)
         frames_b = np.ascontiguousarray(np.stack([q[1] for q in pairs]), np.float16)
         eng = kb.Engine(kb.MODEL_IFNET, blob, H, W, max_batch=B, device=local_rank)
@@ -306,7 +301,7 @@ def run_ours(args):
         p = nets.span_init(1)
         flat = nets.span_flat(p)
         blob = kb.make_blob(kb.MODEL_SPAN_X2, flat)
-        frames = anime_frames(B, H, W, seed=10 + rank).astype(np.float16)
+        frames = anime_frames(B, H, W, seed=shard.frame_seed(10, rank, 0)).astype(np.float16)
         frames_b = None
         scales = None
         if fp8:
@@ -350,7 +345,7 @@ def run_ours(args):
     eng.check_device(stream)
     ms = max_over_ranks(start.elapsed_time(stop))
     profile = eng.read_profile()
-    value = world * B * args.steps / (ms / 1e3)
+    value = shard.whole_job_rate(B * args.steps, world, ms / 1e3)
 
     # ---- roofline of the dominant kernel (measured inside the timed region)
     peaks_json, peak_kind = measured_peaks()
@@ -415,7 +410,7 @@ def run_ours(args):
         pipeline(args.steps)
         barrier()
         e2e_s = max_over_ranks(time.perf_counter() - t0)
-        e2e = {"value": world * B * args.steps / e2e_s, "unit": "frames/s",
+        e2e = {"value": shard.whole_job_rate(B * args.steps, world, e2e_s), "unit": "frames/s",
                "h2d_bytes_per_step": int(sum(t.numel() * 2 for t in h_in)),
                "d2h_bytes_per_step": int(h_out[0].numel() * 2),
                "path": "kb2_enqueue with pinned host frames: H2D copy, enqueue, D2H of every output frame, "
