@@ -8,22 +8,27 @@
 //     B = [ W(dy = +1) | W(dy = 0) | W(dy = -1) ]      (N = 3 x 48 = 144 rows of weights)
 //
 // and the three 48-column results land in the accumulators of the three output rows that input row
-// feeds (o = t - 2, t - 1, t for input row index t of a band), which sit side by side in a TMEM
-// ring of output-row slots. An output row is complete after its third input row; the epilogue then
-// reads it and releases the slot. Per input row the work is kx * channel steps = 9 (FP16) or 5 (E4M3) instructions of N = 144,
-// tensor-bound, and each input row is read from shared memory exactly once. The first K step is
-// issued per 48-row block so that the block opening a fresh output row can overwrite its slot
-// (every other instruction accumulates), which spares zeroing the slots. Band edges use the one- or
-// two-block sub-ranges of B (N = 48 / 96), and an instruction whose three slots would wrap around
-// the end of the ring is split in two.
+// feeds (o = t - 2, t - 1, t for input row index t of a band). An output row is complete after its
+// third input row; the epilogue then reads it.
 //
-// Each input row step covers two neighbouring 126-pixel strips: two TMA boxes in one ring slot, and
-// two TMEM rings of output-row slots, so the per-row synchronisation of the single issuing thread
-// (barrier waits, commits, fences: ~600 cycles measured with no MMA at all) is paid once for twice
-// the MMA work. Measured on 8 x 1080p: 4-9% faster per layer than one strip per step.
+// Issue rate. The single issuing thread is the bottleneck of this kernel: measured on B200, nine
+// MMAs issued from one asm block with precomputed descriptors run at the tensor rate (73 cycles
+// each for N = 144), while any instruction between two MMAs (a branch, a descriptor update) costs
+// ~60 cycles more per MMA. So every input row is exactly n_k MMAs of N = 144 into one contiguous
+// 144-column accumulator window (mma_ss_row, one asm block), all accumulating:
+//  * output rows cycle through 6 slots; slot s owns the 48-column TMEM block s, and slots 0 and 1
+//    also own blocks 6 and 7. The window of input row t starts at the block of slot(t - 2), so it
+//    never wraps: its third block lands in block 6 or 7 when the ring would wrap, and the epilogue
+//    adds the two blocks of a slot (8 blocks = 384 columns);
+//  * when an output row is first touched, its block(s) are cleared by an MMA with an all-zero B tile
+//    and enable-input-d off (issued in order just before the row's accumulating MMAs), so the
+//    row's n_k MMAs all accumulate;
+//  * a slot is reused every 6 output rows, which leaves the epilogue 3 rows of slack;
+//  * band edges use the one- or two-block sub-ranges of B (N = 48 / 96) in the same asm block.
 //
-// Roles as in conv_tc.cuh: warp 0 = TMA producer (same row slots), warp 1 = TMEM owner + MMA issuer,
-// warps 2.. = epilogue (4 per kStackEpiCols output channels) with the same fused epilogues.
+// Roles: warp 0 = TMA producer (one 128-pixel box of all channel chunks per input row), warp 1 =
+// TMEM owner + MMA issuer, warps 2.. = epilogue (4 per kStackEpiCols output channels) with the fused
+// epilogues of conv_tc.cuh.
 #pragma once
 
 #include "conv_tc.cuh"
@@ -36,21 +41,26 @@ namespace kb2 {
 // spill and serialise the residual reads), so the single-block shape is kept.
 constexpr int kStackBlocksPerSm = 1;
 constexpr int kStackEpiCols = 8;
-constexpr uint32_t kStackTmemCols = 512 / kStackBlocksPerSm;
+constexpr uint32_t kStackTmemCols = 512;
+constexpr uint32_t kStackSlots = 6;   // output-row slots (TMEM reuse period, in output rows)
+constexpr uint32_t kStackBlocks = 8;  // 48-column TMEM blocks: one per slot, plus 6 and 7 for slots 0, 1
 
 template <int kCoutPad>
 struct StackShape {
   static constexpr int epi_warps = 4 * (kCoutPad / kStackEpiCols);  // 4 quadrants x column groups
   static constexpr int threads = 64 + 32 * epi_warps;
-  // output-row slots per strip: two strips share the TMEM columns
-  static constexpr int max_slots = static_cast<int>(kStackTmemCols) / (2 * kCoutPad) < 16
-                                       ? static_cast<int>(kStackTmemCols) / (2 * kCoutPad)
-                                       : 16;
+  static constexpr int max_slots = static_cast<int>(kStackSlots);
+  static_assert(kStackBlocks * kCoutPad <= kStackTmemCols, "TMEM blocks");
 };
 
-constexpr int kRowMaxK = 12;  // K steps per input row (FP16 48 channels: 9; E4M3: 5; conv_1: 3)
+constexpr int kRowMaxK = 9;  // K steps per input row (FP16 48 channels: 9; E4M3: 5; conv_1: 2)
 
-constexpr uint32_t kStackSmemExtra = 1024 + 128 * 8 + (kMaxKSteps + 1) * 8 + 3 * kMaxN * 4 + 64;
+// shared memory after the input ring: barriers (128 x 8 B), K-step table, per-channel constants, TMEM
+// address, then (at kStackZeroOff) the all-zero B tile of the clearing MMA (48 rows x 32 B)
+constexpr uint32_t kStackZeroOff = 2176;
+constexpr uint32_t kStackZeroBytes = 48 * 32;
+constexpr uint32_t kStackSmemExtra = 1024 + kStackZeroOff + kStackZeroBytes + 64;
+static_assert(128 * 8 + (kMaxKSteps + 1) * 8 + 3 * kMaxN * 4 + 4 <= kStackZeroOff, "shared layout");
 
 template <bool kFp8, int kCoutPad, int kEpi, int kOut>
 __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPerSm)
@@ -58,11 +68,11 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
   static_assert(kCoutPad == 16 || kCoutPad == 48, "stacked kernel: 16 or 48 output channels");
   constexpr int kEpiWarps = StackShape<kCoutPad>::epi_warps;
   constexpr int kN = 3 * kCoutPad;
+  constexpr uint32_t R = kStackSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sw = smem;
   uint8_t* ring = smem + a.w_smem;
-  const uint32_t R = static_cast<uint32_t>(a.acc_slots);
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + a.ring * a.slot_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + a.ring;
@@ -75,9 +85,13 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
   float* s_scale = s_bias + kMaxN;
   float* s_slope = s_scale + kMaxN;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_slope + kMaxN);
+  uint8_t* zero_b = reinterpret_cast<uint8_t*>(bars) + kStackZeroOff;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  for (uint32_t j = threadIdx.x; j < kStackZeroBytes / 16; j += blockDim.x)
+    reinterpret_cast<uint4*>(zero_b)[j] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();  // the zero tile is read by the tensor core (async proxy)
 
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < a.ring; ++i) {
@@ -125,23 +139,21 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
       RingPos in{0, 0};
       uint32_t issued = 0;
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
-        const int pair = item % a.strips;
+        const int strip = item % a.strips;
         const int t = item / a.strips;
         const int band = t % a.bands;
         const int n = t / a.bands;
         const int y0 = band * a.band_rows;
         const int y1 = min(a.H, y0 + a.band_rows);
-        const int x0 = pair * 2 * a.strip_w;
+        const int x0 = strip * a.strip_w;
         for (int r = y0 - 1; r <= y1; ++r) {
           if (!wait_bar(&empty[in.idx], in.phase ^ 1u, a.err, kErrWaitProducer)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[in.idx], a.slot_bytes);
-          // one box per strip: 128 pixels from the strip's x - 1 (zero fill outside the image), all chunks
-          uint8_t* dst = ring + in.idx * a.slot_bytes;
-          tma_load_4d(dst, &maps.m[0], &full[in.idx], (x0 - 1) * 2, 0, r, n);
-          tma_load_4d(dst + a.src_bytes, &maps.m[0], &full[in.idx], (x0 + a.strip_w - 1) * 2, 0, r, n);
+          // one box: 128 pixels from x0 - 1 (zero fill left of the image), all chunks
+          tma_load_4d(ring + in.idx * a.slot_bytes, &maps.m[0], &full[in.idx], (x0 - 1) * 2, 0, r, n);
           in.advance(a.ring);
           ++issued;
         }
@@ -161,6 +173,7 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
       const uint32_t ring_base = smem_u32(ring);
       const uint64_t desc_hi = make_sdesc(0, 0, 128);
       const uint64_t b_desc0 = make_sdesc(smem_u32(sw), kN * 16, 128);
+      const uint64_t zero_desc = make_sdesc(smem_u32(zero_b), kCoutPad * 16, 128);
       constexpr uint64_t kBStep16 = (2u * kN * 16u) >> 4;   // one K step of B
       constexpr uint64_t kBlock16 = (kCoutPad * 16u) >> 4;  // one kernel-row block of B
       const int n_k = a.n_ksteps;
@@ -169,7 +182,7 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
       for (int j = 0; j < kRowMaxK; ++j) kd[j] = s_k[j];
       const uint32_t id_n[3] = {a.idesc_n[0], a.idesc_n[1], a.idesc_n[2]};
       RingPos in{0, 0};
-      RingPos acc{0, 0};  // accumulator slot (and phase) of output row t, the row first touched by input t
+      RingPos acc{0, 0};  // slot (and phase) of output row t, the row first touched by input t
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
         const int t0 = item / a.strips;
         const int band = t0 % a.bands;
@@ -184,51 +197,33 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
           // blocks [b0, b1) of B feed output rows t - 2 + b0 .. t - 2 + b1 - 1 of the band
           const int b0 = t >= 2 ? 0 : 2 - t;
           const int b1 = t <= rows - 1 ? 3 : (t == rows ? 2 : 1);
+          const uint64_t a_row = desc_hi | static_cast<uint64_t>((ring_base + in.idx * a.slot_bytes) >> 4);
           if (b1 == 3) {  // output row t is touched for the first time: its slot must have been read
             if (!wait_bar(&slot_free[acc.idx], acc.phase, a.err, kErrWaitMma)) {
               ok = false;
               break;
             }
+            tc_fence_after();
+            // clear its block(s): (any finite A) x (zero B), enable-input-d off
+            mma_ss<kFp8>(tmem_base + acc.idx * kCoutPad, a_row + kd[0], zero_desc, id_n[0], 0u);
+            if (acc.idx < 2) mma_ss<kFp8>(tmem_base + (acc.idx + 6) * kCoutPad, a_row + kd[0], zero_desc, id_n[0], 0u);
           }
           tc_fence_after();
-          // slot of output t - 2 + b0 (acc.idx is the slot of output t)
-          const uint32_t back = static_cast<uint32_t>(2 - b0);
-          const uint32_t s_first = acc.idx >= back ? acc.idx - back : acc.idx + R - back;
-          const uint32_t nb = static_cast<uint32_t>(b1 - b0);
-          const uint32_t nb1 = nb < R - s_first ? nb : R - s_first;  // blocks before the ring wraps
-          const uint32_t nb2 = nb - nb1;
+          // the window starts at the TMEM block of slot(t - 2) = acc.idx - 2 (mod 6); block k of B
+          // (output t - 2 + k) lands in TMEM block start + k, never past block 7
+          const uint32_t start = acc.idx >= 2 ? acc.idx - 2 : acc.idx + R - 2;
           const uint64_t b_first = b_desc0 + static_cast<uint64_t>(b0) * kBlock16;
-          const uint32_t id1 = nb1 == 3 ? id_n[2] : (nb1 == 2 ? id_n[1] : id_n[0]);
+          uint64_t ad[kRowMaxK], bd[kRowMaxK];
 #pragma unroll
-          for (uint32_t h = 0; h < 2; ++h) {  // the two strips: A box h, TMEM ring h
-            const uint32_t ring_h = tmem_base + h * R * kCoutPad;
-            const uint64_t a_row =
-                desc_hi | static_cast<uint64_t>((ring_base + in.idx * a.slot_bytes + h * a.src_bytes) >> 4);
-            const uint32_t d1 = ring_h + s_first * kCoutPad;
-            // K step 0, one instruction per block: the block of a fresh output row (b1 == 3, block
-            // 2) overwrites its slot, the others accumulate -- so slots never need zeroing
-            {
-              uint32_t slot = s_first;
-              for (int blk = b0; blk < b1; ++blk) {
-                const uint32_t fresh = (b1 == 3 && blk == 2) ? 1u : 0u;
-                mma_ss<kFp8>(ring_h + slot * kCoutPad, a_row + kd[0], b_desc0 + static_cast<uint64_t>(blk) * kBlock16,
-                             id_n[0], fresh ^ 1u);
-                slot = slot + 1 == R ? 0 : slot + 1;
-              }
-            }
-#pragma unroll
-            for (int j = 1; j < kRowMaxK; ++j)
-              if (j < n_k) mma_ss<kFp8>(d1, a_row + kd[j], b_first + static_cast<uint64_t>(j) * kBStep16, id1, 1u);
-            if (nb2 > 0) {  // the blocks past the end of the ring go to slot 0
-              const uint32_t id2 = nb2 == 2 ? id_n[1] : id_n[0];
-              const uint64_t b_second = b_first + static_cast<uint64_t>(nb1) * kBlock16;
-#pragma unroll
-              for (int j = 1; j < kRowMaxK; ++j)
-                if (j < n_k) mma_ss<kFp8>(ring_h, a_row + kd[j], b_second + static_cast<uint64_t>(j) * kBStep16, id2, 1u);
-            }
+          for (int j = 0; j < kRowMaxK; ++j) {
+            ad[j] = a_row + kd[j];
+            bd[j] = b_first + static_cast<uint64_t>(j) * kBStep16;
           }
+          const int nb = b1 - b0;
+          const uint32_t idesc = nb == 3 ? id_n[2] : (nb == 2 ? id_n[1] : id_n[0]);
+          mma_ss_row<kFp8>(tmem_base + (start + static_cast<uint32_t>(b0)) * kCoutPad, ad, bd, idesc, n_k);
           mma_commit(&empty[in.idx]);  // the input row is no longer needed
-          if (t >= 2) mma_commit(&acc_full[acc.idx >= 2 ? acc.idx - 2 : acc.idx + R - 2]);  // output t-2 done
+          if (t >= 2) mma_commit(&acc_full[start]);  // output t - 2 done
           in.advance(a.ring);
           acc.advance(R);  // acc tracks output row t + 1 (virtual past the band's last row)
         }
@@ -247,6 +242,7 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
     const int quad = warp & 3;
     const int col0 = ((warp - 2) >> 2) * kStackEpiCols;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
     // this warp's per-channel constants, held in registers for the whole kernel (reading them from
     // shared memory on every row cost ~9% of the plain conv)
     float r_bias[kStackEpiCols], r_scale[kStackEpiCols], r_slope[kStackEpiCols];
@@ -262,17 +258,15 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
     RingPos acc{0, 0};
     bool ok = true;
     for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
-      const int pair = item % a.strips;
+      const int strip = item % a.strips;
       const int t = item / a.strips;
       const int band = t % a.bands;
       const int n = t / a.bands;
       const int y0 = band * a.band_rows;
       const int y1 = min(a.H, y0 + a.band_rows);
       const int m = quad * 32 + lane;
-      const int xa = pair * 2 * a.strip_w + m;  // pixel of TMEM lane m in the first strip
-      const int xb = xa + a.strip_w;             // ... and in the second
-      const bool store_a = m < a.strip_w && xa < a.W;
-      const bool store_b = m < a.strip_w && xb < a.W;
+      const int x = strip * a.strip_w + m;
+      const bool store = m < a.strip_w && x < a.W;
       for (int y = y0; y < y1; ++y, acc.advance(R)) {
         const uint32_t s = acc.idx;
         const bool got = wait_bar(&acc_full[s], acc.phase, a.err, kErrWaitEpilogue);
@@ -281,22 +275,21 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
           break;
         }
         tc_fence_after();
-        float va[kStackEpiCols], vb[kStackEpiCols];
-        const uint32_t taddr = tmem_base + lane_addr + s * kCoutPad + static_cast<uint32_t>(col0);
-        const uint32_t taddr_b = taddr + R * kCoutPad;
-        if constexpr (kStackEpiCols == 16) {
-          tmem_ld16(taddr, va);
-          tmem_ld16(taddr_b, vb);
+        float v[kStackEpiCols];
+        tmem_ld8(my_cols + s * kCoutPad, v);
+        if (s < 2) {  // slots 0 and 1: the part of the sum that landed in block 6 or 7
+          float w[kStackEpiCols];
+          tmem_ld8(my_cols + (s + 6) * kCoutPad, w);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < kStackEpiCols; ++j) v[j] += w[j];
         } else {
-          tmem_ld8(taddr, va);
-          tmem_ld8(taddr_b, vb);
+          tmem_ld_wait();
         }
-        tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&slot_free[s]);
-        if (store_a) epilogue_cols<kEpi, kOut, kStackEpiCols>(a, r_bias, r_scale, r_slope, va, 0, n, y, xa, col0);
-        if (store_b) epilogue_cols<kEpi, kOut, kStackEpiCols>(a, r_bias, r_scale, r_slope, vb, 0, n, y, xb, col0);
+        if (store) epilogue_cols<kEpi, kOut, kStackEpiCols>(a, r_bias, r_scale, r_slope, v, 0, n, y, x, col0);
       }
     }
   }

@@ -159,8 +159,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   const int strip_w = px - reach;
   if (strip_w < 64) return refuse(KB2_FORMAT_UNSUPPORTED, "row slot too narrow for the taps");
   const uint32_t src_bytes = static_cast<uint32_t>(chunks) * px * 16;
-  // the stacked kernel stages two strips per input row (one box each), the generic one one box per source
-  const uint32_t slot_bytes = src_bytes * static_cast<uint32_t>(stacked ? 2 : s.n_sources);
+  const uint32_t slot_bytes = src_bytes * static_cast<uint32_t>(s.n_sources);
 
   ConvArgs& a = args;
   a = ConvArgs{};
@@ -169,7 +168,6 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   a.W = in0.W;
   a.strip_w = strip_w;
   a.strips = (in0.W + strip_w - 1) / strip_w;
-  if (stacked) a.strips = (a.strips + 1) / 2;  // work items cover strip pairs
   a.n_sources = s.n_sources;
   a.chunks = chunks;
   a.px = px;
@@ -214,7 +212,8 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     a.tmem_a = 0;
     a.n_tiles = 0;
     for (int i = 0; i < 3; ++i) a.idesc_n[i] = make_idesc(kTileM, (i + 1) * s.n_pad);
-    a.acc_slots = s.n_pad == 48 ? StackShape<48>::max_slots : StackShape<16>::max_slots;
+    a.acc_slots = static_cast<int>(kStackSlots);
+    if (static_cast<int>(steps.size()) > kRowMaxK) return refuse(KB2_FORMAT_UNSUPPORTED, "stacked: too many K steps per row");
   }
   const int n_rows_b = stacked ? 3 * s.n_pad : s.n_pad;  // rows of B per K step
 
@@ -335,10 +334,10 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   per_sm = std::min({per_sm, smem_fit, tmem_fit});
   if (per_sm < 1) per_sm = 1;
   const int slots = num_sms() * per_sm;
-  // bands: about 16 work items per resident block (8 for the stacked kernel, whose items are strip
-  // pairs), 4..64 rows each (8.. for the stacked kernel, whose two halo rows per band are extra MMA work)
+  // bands: about 16 work items per resident block, 4..64 rows each (8.. for the stacked kernel,
+  // whose two halo rows per band are extra MMA work)
   const long long rows_total = static_cast<long long>(a.batch) * a.H * a.strips;
-  int band = static_cast<int>(rows_total / ((stacked ? 8LL : 16LL) * slots));
+  int band = static_cast<int>(rows_total / (16LL * slots));
   const int band_min = stacked ? 8 : 4;
   band = band < band_min ? band_min : (band > 64 ? 64 : band);
   a.band_rows = band;

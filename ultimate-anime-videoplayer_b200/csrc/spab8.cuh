@@ -1,0 +1,382 @@
+// One SPAN block (SPAB) in one kernel, E4M3: conv1 + SiLU -> conv2 + SiLU -> conv3 + gate, with the
+// two intermediate activations kept in shared memory (sm_100a, tcgen05 + TMEM + TMA).
+//
+// The three convolutions are the stacked-kernel-row convolutions of conv3s.cuh (B = the three kernel
+// rows side by side, N = 144, one instruction group per input row), chained through shared-memory
+// row rings instead of HBM:
+//
+//   input rows (TMA) --conv1--> T1 rows (E4M3, smem) --conv2--> T2 rows (E4M3, smem) --conv3 + gate--> out
+//
+// Per row step s the single MMA issuer runs conv1 on input row s, conv2 on T1 row s - 3 and conv3 on
+// T2 row s - 6 (each written by its epilogue group during the previous step), so the three
+// convolutions overlap and the issuer's per-row synchronisation is paid once for three
+// convolutions. Only the block input is read from HBM and only the block output written: 96 bytes
+// per pixel instead of 3 x 96 (plus the residual re-read) for the three separate launches.
+//
+// Geometry: a work item is 122 output pixels of one band of rows. The input box holds pixels
+// x0 - 3 .. x0 + 124; each 3x3 convolution trims one pixel on each side (T1 is valid for x0 - 2 ..
+// x0 + 123, T2 for x0 - 1 .. x0 + 122). The band reads 3 halo rows above and below. T1 and T2 values
+// outside the frame are written as zeros: they are the zero padding of the next convolution.
+//
+// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2-9 / 10-17 / 18-25 = the epilogues of
+// conv1 / conv2 / conv3 (8 warps each: 4 TMEM lane quadrants x 2 halves of the 48 columns).
+// Arithmetic is that of the separate layers: per-output-channel weight scales with the input scale
+// folded in, FP32 accumulation, SiLU / gate in FP32, E4M3 rounding with saturation.
+#pragma once
+
+#include "conv3s.cuh"
+
+namespace kb2 {
+
+constexpr int kSpabThreads = 64 + 32 * 24;
+constexpr int kSpabStrip = 122;
+constexpr uint32_t kSpabInRing = 6;
+constexpr uint32_t kSpabTRing = 3;
+constexpr uint32_t kSpabRowBytes = 3 * 128 * 16;  // 48 E4M3 channels x 128 pixels
+constexpr uint32_t kSpabChunkBytes = 128 * 16;
+
+struct SpabArgs {
+  int batch, H, W;
+  int strips, bands, band_rows, items;
+  int n_k;                  // K steps per input row
+  uint64_t ks[kRowMaxK];    // per K step: (a_off >> 4) | (lbo >> 4) << 16 (A tile of the row slot)
+  uint32_t idesc_n[3];      // instruction descriptors for 1, 2, 3 row blocks (N = 48, 96, 144)
+  const uint8_t* wpack[3];  // stacked B of conv1..3
+  uint32_t wbytes;          // bytes of one conv's B
+  uint32_t wstride;         // wbytes rounded up to 1 KB (shared-memory layout)
+  const float* bias[3];
+  const float* scale[3];    // per-output-channel dequantisation scale (input scale folded in)
+  float inv1, inv2, inv3;   // 1 / E4M3 scale of T1, T2 and (not the last block) the block output
+  float res_scale;          // E4M3 scale of the block input (the gate's residual)
+  const uint8_t* x_in;      // block input, chunked E4M3 [n][H][3][W][16]
+  uint8_t* out;             // block output: chunked E4M3 (3 chunks) or, last block, FP16 (6 chunks)
+  uint8_t* t1_f16;          // last block: FP16 copy of T1 (a conv_cat source, 6 chunks), else null
+  int* err;
+};
+
+// TMEM: per conv a ring of R output-row slots of 48 columns.
+__host__ __device__ constexpr uint32_t spab_slots(int c) { return c == 2 ? 4u : 3u; }
+__host__ __device__ constexpr uint32_t spab_tmem_base(int c) { return c == 0 ? 0u : (c == 1 ? 144u : 288u); }
+
+constexpr uint32_t kSpabSmemExtra = 1024 + 64 * 8 + 2 * 3 * 48 * 4 + 64;
+
+template <bool kLast>
+__global__ void __launch_bounds__(kSpabThreads, 1)
+    spab8_kernel(const __grid_constant__ CUtensorMap map_in, const __grid_constant__ SpabArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sw = smem;                                  // 3 x wstride
+  uint8_t* in_ring = sw + 3 * a.wstride;               // kSpabInRing rows
+  uint8_t* t_ring = in_ring + kSpabInRing * kSpabRowBytes;  // T1 then T2, kSpabTRing rows each
+  uint64_t* bars = reinterpret_cast<uint64_t*>(t_ring + 2 * kSpabTRing * kSpabRowBytes);
+  uint64_t* full = bars;                        // [kSpabInRing]
+  uint64_t* empty = full + kSpabInRing;         // [kSpabInRing]
+  uint64_t* t_ready = empty + kSpabInRing;      // [2][kSpabTRing]
+  uint64_t* t_free = t_ready + 2 * kSpabTRing;  // [2][kSpabTRing]
+  uint64_t* acc_full = t_free + 2 * kSpabTRing;  // [3][4]
+  uint64_t* acc_free = acc_full + 12;            // [3][4]
+  uint64_t* wbar = acc_free + 12;
+  uint64_t* drain = wbar + 1;
+  float* s_bias = reinterpret_cast<float*>(bars + 64);  // [3][48]
+  float* s_scale = s_bias + 3 * 48;                     // [3][48]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_scale + 3 * 48);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < kSpabInRing; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (uint32_t i = 0; i < 2 * kSpabTRing; ++i) {
+      mbar_init(&t_ready[i], 8);
+      mbar_init(&t_free[i], 1);
+    }
+    for (int c = 0; c < 3; ++c)
+      for (uint32_t i = 0; i < spab_slots(c); ++i) {
+        mbar_init(&acc_full[4 * c + i], 1);
+        mbar_init(&acc_free[4 * c + i], 8);
+      }
+    mbar_init(wbar, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  for (int j = threadIdx.x; j < 3 * 48; j += blockDim.x) {
+    s_bias[j] = a.bias[j / 48][j % 48];
+    s_scale[j] = a.scale[j / 48][j % 48];
+  }
+  if (warp == 0 && lane == 0) prefetch_tmap(&map_in);
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ producer
+      mbar_arrive_expect_tx(wbar, 3 * a.wbytes);
+      for (int c = 0; c < 3; ++c)
+        for (uint32_t off = 0; off < a.wbytes; off += 32768u) {
+          const uint32_t len = a.wbytes - off < 32768u ? a.wbytes - off : 32768u;
+          bulk_load(sw + c * a.wstride + off, a.wpack[c] + off, len, wbar);
+        }
+      bool ok = true;
+      RingPos in{0, 0};
+      uint32_t issued = 0;
+      for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
+        const int strip = item % a.strips;
+        const int t = item / a.strips;
+        const int band = t % a.bands;
+        const int n = t / a.bands;
+        const int y0 = band * a.band_rows;
+        const int rows = min(a.H, y0 + a.band_rows) - y0;
+        const int x0 = strip * kSpabStrip;
+        for (int i = 0; i < rows + 6; ++i) {
+          if (!wait_bar(&empty[in.idx], in.phase ^ 1u, a.err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[in.idx], kSpabRowBytes);
+          tma_load_4d(in_ring + in.idx * kSpabRowBytes, &map_in, &full[in.idx], (x0 - 3) * 2, 0, y0 - 3 + i, n);
+          in.advance(kSpabInRing);
+          ++issued;
+        }
+      }
+      RingPos back = in;
+      for (uint32_t k = 0; k < kSpabInRing && k < issued; ++k) {
+        back.retreat(kSpabInRing);
+        wait_bar(&full[back.idx], back.phase, a.err, kErrWaitDrain);
+      }
+      wait_bar(wbar, 0, a.err, kErrWaitDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      bool ok = wait_bar(wbar, 0, a.err, kErrWaitMma);
+      const uint64_t desc_hi = make_sdesc(0, 0, 128);
+      constexpr uint64_t kBStep16 = (2u * 144u * 16u) >> 4;  // one K step of B
+      constexpr uint64_t kBlock16 = (48u * 16u) >> 4;        // one kernel-row block of B
+      uint64_t bdesc[3];
+      for (int c = 0; c < 3; ++c) bdesc[c] = make_sdesc(smem_u32(sw + c * a.wstride), 144 * 16, 128);
+      const int n_k = a.n_k;
+      uint64_t kd[kRowMaxK];
+#pragma unroll
+      for (int j = 0; j < kRowMaxK; ++j) kd[j] = a.ks[j];
+      const uint32_t id_n[3] = {a.idesc_n[0], a.idesc_n[1], a.idesc_n[2]};
+      const uint32_t in_base = smem_u32(in_ring);
+      const uint32_t t_base = smem_u32(t_ring);
+      RingPos in{0, 0}, tc[2] = {{0, 0}, {0, 0}};
+      RingPos acc[3] = {{0, 0}, {0, 0}, {0, 0}};
+
+      // one input row of conv c: input index t of n_out + 2, feeding outputs t - 2 .. t
+      auto conv_row = [&](int c, int t, int n_out, uint64_t a_row) -> bool {
+        const uint32_t R = spab_slots(c);
+        const uint32_t tb = tmem_base + spab_tmem_base(c);
+        RingPos& ac = acc[c];
+        const int b0 = t >= 2 ? 0 : 2 - t;
+        const int b1 = t <= n_out - 1 ? 3 : (t == n_out ? 2 : 1);
+        if (b1 == 3 && !wait_bar(&acc_free[4 * c + ac.idx], ac.phase, a.err, kErrWaitMma)) return false;
+        tc_fence_after();
+        const uint32_t back = static_cast<uint32_t>(2 - b0);
+        const uint32_t s_first = ac.idx >= back ? ac.idx - back : ac.idx + R - back;
+        const uint32_t nb = static_cast<uint32_t>(b1 - b0);
+        const uint32_t nb1 = nb < R - s_first ? nb : R - s_first;
+        const uint32_t nb2 = nb - nb1;
+        const uint64_t b_first = bdesc[c] + static_cast<uint64_t>(b0) * kBlock16;
+        uint32_t slot = s_first;
+        for (int blk = b0; blk < b1; ++blk) {
+          const uint32_t fresh = (b1 == 3 && blk == 2) ? 1u : 0u;
+          mma_ss<true>(tb + slot * 48u, a_row + kd[0], bdesc[c] + static_cast<uint64_t>(blk) * kBlock16, id_n[0],
+                       fresh ^ 1u);
+          slot = slot + 1 == R ? 0 : slot + 1;
+        }
+        const uint32_t id1 = id_n[nb1 - 1];
+#pragma unroll
+        for (int j = 1; j < kRowMaxK; ++j)
+          if (j < n_k)
+            mma_ss<true>(tb + s_first * 48u, a_row + kd[j], b_first + static_cast<uint64_t>(j) * kBStep16, id1, 1u);
+        if (nb2 > 0) {
+          const uint32_t id2 = id_n[nb2 - 1];
+          const uint64_t b_second = b_first + static_cast<uint64_t>(nb1) * kBlock16;
+#pragma unroll
+          for (int j = 1; j < kRowMaxK; ++j)
+            if (j < n_k) mma_ss<true>(tb, a_row + kd[j], b_second + static_cast<uint64_t>(j) * kBStep16, id2, 1u);
+        }
+        if (t >= 2) mma_commit(&acc_full[4 * c + (ac.idx >= 2 ? ac.idx - 2 : ac.idx + R - 2)]);
+        ac.advance(R);
+        return true;
+      };
+
+      for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
+        const int t = item / a.strips;
+        const int band = t % a.bands;
+        const int y0 = band * a.band_rows;
+        const int rows = min(a.H, y0 + a.band_rows) - y0;
+        for (int s = 0; s < rows + 8 && ok; ++s) {
+          if (s <= rows + 5) {  // conv1 on input row s
+            if (!wait_bar(&full[in.idx], in.phase, a.err, kErrWaitMma)) { ok = false; break; }
+            const uint64_t a_row = desc_hi | static_cast<uint64_t>((in_base + in.idx * kSpabRowBytes) >> 4);
+            if (!conv_row(0, s, rows + 4, a_row)) { ok = false; break; }
+            mma_commit(&empty[in.idx]);
+            in.advance(kSpabInRing);
+          }
+          for (int c = 1; c < 3; ++c) {  // conv2 on T1 row s - 3, conv3 on T2 row s - 6
+            const int r = s - 3 * c;
+            const int n_out = rows + 4 - 2 * c;
+            if (r < 0 || r > n_out + 1) continue;
+            RingPos& q = tc[c - 1];
+            const uint32_t ti = static_cast<uint32_t>(c - 1) * kSpabTRing + q.idx;
+            if (!wait_bar(&t_ready[ti], q.phase, a.err, kErrWaitMma)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t a_row = desc_hi | static_cast<uint64_t>((t_base + ti * kSpabRowBytes) >> 4);
+            if (!conv_row(c, r, n_out, a_row)) { ok = false; break; }
+            mma_commit(&t_free[ti]);
+            q.advance(kSpabTRing);
+          }
+        }
+        if (!ok) break;
+        for (int c = 0; c < 3; ++c) {  // past the band's last output: back to the next band's first
+          acc[c].retreat(spab_slots(c));
+          acc[c].retreat(spab_slots(c));
+        }
+      }
+      mma_commit(drain);
+      wait_bar(drain, 0, a.err, kErrWaitDrain);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------------------- epilogues
+    const int g = (warp - 2) >> 3;  // conv 0, 1, 2
+    const int ew = (warp - 2) & 7;
+    const int quad = warp & 3;
+    const int col0 = (ew >> 2) * 24;
+    const uint32_t R = spab_slots(g);
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tb = tmem_base + spab_tmem_base(g);
+    const float* bias = s_bias + 48 * g;
+    const float* scale = s_scale + 48 * g;
+    const float inv = g == 0 ? a.inv1 : (g == 1 ? a.inv2 : a.inv3);
+    if (lane == 0)
+      for (uint32_t s = 0; s < R; ++s) mbar_arrive(&acc_free[4 * g + s]);
+    RingPos ap{0, 0}, tw{0, 0};
+    bool ok = true;
+    const int m = quad * 32 + lane;
+    for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
+      const int strip = item % a.strips;
+      const int t = item / a.strips;
+      const int band = t % a.bands;
+      const int n = t / a.bands;
+      const int y0 = band * a.band_rows;
+      const int rows = min(a.H, y0 + a.band_rows) - y0;
+      const int x0 = strip * kSpabStrip;
+      const int n_rows = rows + 4 - 2 * g;  // T1: rows + 4, T2: rows + 2, out: rows
+      const int yb = y0 - 2 + g;
+      const int x = x0 - 2 + g + m;
+      for (int r = 0; r < n_rows; ++r) {
+        const int y = yb + r;
+        const bool got = wait_bar(&acc_full[4 * g + ap.idx], ap.phase, a.err, kErrWaitEpilogue);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float v[24];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) tmem_ld8(tb + lane_addr + ap.idx * 48u + static_cast<uint32_t>(col0 + 8 * k), v + 8 * k);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_free[4 * g + ap.idx]);
+        ap.advance(R);
+#pragma unroll
+        for (int j = 0; j < 24; ++j) v[j] = fmaf(v[j], scale[col0 + j], bias[col0 + j]);
+        if (g < 2) {
+          // SiLU, E4M3, into the T ring row; zeros outside the frame (the next conv's padding)
+          const uint32_t ti = static_cast<uint32_t>(g) * kSpabTRing + tw.idx;
+          const bool got_free = wait_bar(&t_free[ti], tw.phase ^ 1u, a.err, kErrWaitEpilogue);
+          if (!__all_sync(0xffffffffu, got_free)) {
+            ok = false;
+            break;
+          }
+          const bool valid = m < (g == 0 ? 126 : 124) && y >= 0 && y < a.H && x >= 0 && x < a.W;
+          uint8_t* row = t_ring + ti * kSpabRowBytes + static_cast<uint32_t>(m) * 16u;
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            const int c = col0 + 8 * k;
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = valid ? v[8 * k + j] * sigmoidf_fast(v[8 * k + j]) : 0.0f;
+            uint2 q;
+            q.x = static_cast<uint32_t>(pack_e4m3x2(f[0] * inv, f[1] * inv)) |
+                  (static_cast<uint32_t>(pack_e4m3x2(f[2] * inv, f[3] * inv)) << 16);
+            q.y = static_cast<uint32_t>(pack_e4m3x2(f[4] * inv, f[5] * inv)) |
+                  (static_cast<uint32_t>(pack_e4m3x2(f[6] * inv, f[7] * inv)) << 16);
+            *reinterpret_cast<uint2*>(row + (c / 16) * kSpabChunkBytes + (c % 16)) = q;
+            if constexpr (kLast) {
+              // the FP16 copy of T1 for conv_cat, for the pixels this item owns
+              if (g == 0 && valid && r >= 2 && r < rows + 2 && m >= 2 && m < 2 + kSpabStrip) {
+                uint4 h;
+                h.x = pack_half2(f[0], f[1]);
+                h.y = pack_half2(f[2], f[3]);
+                h.z = pack_half2(f[4], f[5]);
+                h.w = pack_half2(f[6], f[7]);
+                const size_t pix = ((static_cast<size_t>(n) * a.H + y) * 6 + c / 8) * a.W + x;
+                *reinterpret_cast<uint4*>(a.t1_f16 + pix * 16) = h;
+              }
+            }
+          }
+          fence_proxy_async_smem();  // the tensor core reads the row through the async proxy
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&t_ready[ti]);
+          tw.advance(kSpabTRing);
+        } else if (m < kSpabStrip && x < a.W) {
+          // gate with the block input: (v + x) * (sigmoid(v) - 0.5), to E4M3 or (last block) FP16
+          const size_t pix_row = static_cast<size_t>(n) * a.H + y;
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            const int c = col0 + 8 * k;
+            const uint2 rq = __ldg(reinterpret_cast<const uint2*>(a.x_in + ((pix_row * 3 + c / 16) * a.W + x) * 16 + (c % 16)));
+            const uint16_t rh[4] = {static_cast<uint16_t>(rq.x & 0xFFFFu), static_cast<uint16_t>(rq.x >> 16),
+                                    static_cast<uint16_t>(rq.y & 0xFFFFu), static_cast<uint16_t>(rq.y >> 16)};
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 rr = unpack_e4m3x2(rh[j]);
+              const float v0 = v[8 * k + 2 * j], v1 = v[8 * k + 2 * j + 1];
+              f[2 * j] = (v0 + rr.x * a.res_scale) * sigmoid_centered(v0);
+              f[2 * j + 1] = (v1 + rr.y * a.res_scale) * sigmoid_centered(v1);
+            }
+            if constexpr (kLast) {
+              uint4 h;
+              h.x = pack_half2(f[0], f[1]);
+              h.y = pack_half2(f[2], f[3]);
+              h.z = pack_half2(f[4], f[5]);
+              h.w = pack_half2(f[6], f[7]);
+              *reinterpret_cast<uint4*>(a.out + ((pix_row * 6 + c / 8) * a.W + x) * 16) = h;
+            } else {
+              uint2 q;
+              q.x = static_cast<uint32_t>(pack_e4m3x2(f[0] * inv, f[1] * inv)) |
+                    (static_cast<uint32_t>(pack_e4m3x2(f[2] * inv, f[3] * inv)) << 16);
+              q.y = static_cast<uint32_t>(pack_e4m3x2(f[4] * inv, f[5] * inv)) |
+                    (static_cast<uint32_t>(pack_e4m3x2(f[6] * inv, f[7] * inv)) << 16);
+              *reinterpret_cast<uint2*>(a.out + ((pix_row * 3 + c / 16) * a.W + x) * 16 + (c % 16)) = q;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace kb2

@@ -133,6 +133,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy (TMA, tensor core).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMEM / tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
@@ -170,6 +175,290 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+  }
+}
+
+// kN accumulating MMAs into one accumulator, issued from a single asm block: MMA j multiplies A
+// descriptor a[j] by B descriptor b[j]. The issuing thread executes nothing between consecutive
+// tcgen05.mma instructions; measured on B200 (M = 128, N = 144, K = 16), 9 MMAs issued this way run
+// at the tensor rate (73 cycles each), while a loop with one branch per MMA costs 132.
+template <bool kFp8, int kN>
+__device__ __forceinline__ void mma_ss_block(uint32_t d_tmem, const uint64_t (&a)[9], const uint64_t (&b)[9],
+                                             uint32_t idesc) {
+  static_assert(kN >= 1 && kN <= 9, "1..9 MMAs");
+  if constexpr (kFp8) {
+      if constexpr (kN == 1) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 2) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 3) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %12, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 4) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %13, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 5) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %5, %14, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 6) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %6, %15, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 7) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %6, %15, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %7, %16, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 8) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %6, %15, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %7, %16, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %8, %17, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 9) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %6, %15, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %7, %16, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %8, %17, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %9, %18, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      }
+  } else {
+      if constexpr (kN == 1) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 2) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 3) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %12, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 4) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %13, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 5) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %14, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 6) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %15, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 7) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %15, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %16, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 8) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %15, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %16, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %17, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      } else if constexpr (kN == 9) {
+        asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, %20, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %10, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %11, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %12, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %13, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %14, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %15, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %16, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %17, %19, acc;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %9, %18, %19, acc;\n\t"
+          "}\n" ::"r"(d_tmem),
+          "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+          "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8]),
+          "r"(idesc), "r"(1u)
+          : "memory");
+      }
+  }
+}
+
+// n (1..9, runtime) accumulating MMAs: one branch to the matching block, none between MMAs.
+template <bool kFp8>
+__device__ __forceinline__ void mma_ss_row(uint32_t d_tmem, const uint64_t (&a)[9], const uint64_t (&b)[9],
+                                           uint32_t idesc, int n) {
+  switch (n) {
+    case 1: mma_ss_block<kFp8, 1>(d_tmem, a, b, idesc); break;
+    case 2: mma_ss_block<kFp8, 2>(d_tmem, a, b, idesc); break;
+    case 3: mma_ss_block<kFp8, 3>(d_tmem, a, b, idesc); break;
+    case 4: mma_ss_block<kFp8, 4>(d_tmem, a, b, idesc); break;
+    case 5: mma_ss_block<kFp8, 5>(d_tmem, a, b, idesc); break;
+    case 6: mma_ss_block<kFp8, 6>(d_tmem, a, b, idesc); break;
+    case 7: mma_ss_block<kFp8, 7>(d_tmem, a, b, idesc); break;
+    case 8: mma_ss_block<kFp8, 8>(d_tmem, a, b, idesc); break;
+    default: mma_ss_block<kFp8, 9>(d_tmem, a, b, idesc); break;
   }
 }
 
