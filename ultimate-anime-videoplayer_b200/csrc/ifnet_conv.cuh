@@ -19,7 +19,7 @@
 //  * Warp 0: producer. Warp 1: TMEM owner + MMA issuer. Warps 2..9: epilogue, two per TMEM lane
 //    quadrant, each half of the columns. The accumulator is double-buffered in TMEM. Fused
 //    epilogues: bias + PReLU; bias + residual + PReLU; transposed-conv phases scattered as FP32
-//    planes (+ bias).
+//    pixels of 8 floats (+ bias; 5 used).
 #pragma once
 
 #include "tc_common.cuh"
@@ -54,7 +54,7 @@ struct IfConvArgs {
   const uint8_t* residual;  // kIfResPrelu: chunked FP16 like out
   uint8_t* out;             // chunked FP16 [n][h_out][out_chunks][w_out][16 B]
   int out_chunks;
-  float* out_f32;  // kIfConvT: FP32 planes [n][5][2 h_out][2 w_out]
+  float* out_f32;  // kIfConvT: FP32 [n][2 h_out][2 w_out][8] (5 used: flow x0 y0 x1 y1, mask)
   int* err;
 };
 
@@ -247,11 +247,9 @@ __global__ void __launch_bounds__(kIfThreads, 1)
         for (int j = 0; j < 8; ++j) v[j] += s_bias[cg * 8 + j];
         if constexpr (kEpi == kIfConvT) {
           const int py = cg >> 1, px = cg & 1;
-          const size_t plane = static_cast<size_t>(2 * a.h_out) * (2 * a.w_out);
-          float* dst = a.out_f32 + static_cast<size_t>(n) * 5 * plane +
-                       static_cast<size_t>(2 * oy + py) * (2 * a.w_out) + (2 * x + px);
-#pragma unroll
-          for (int j = 0; j < 5; ++j) dst[j * plane] = v[j];
+          float* dst = a.out_f32 + ((static_cast<size_t>(n) * (2 * a.h_out) + 2 * oy + py) * (2 * a.w_out) + (2 * x + px)) * 8;
+          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], 0.0f, 0.0f, 0.0f);
         } else {
           const size_t pix = ((static_cast<size_t>(n) * a.h_out + oy) * a.out_chunks + cg) * a.w_out + x;
           if constexpr (kEpi == kIfResPrelu) {

@@ -9,9 +9,12 @@
 //  * half-pixel linear resize (src/gpu/ir/op_sample.cpp:88-170): position (o + 0.5) / scale - 0.5
 //    in FP32 with scale = n_out / n_in, clamped to [0, n_in - 1], truncated;
 //  * the transposed conv of block j leaves a small FP32 tensor (5 planes at 1/(2 s_j) of the
-//    frame). After each block, one pass adds it, resized to full resolution and scaled by 2 s_j,
-//    to the full-resolution FP32 flow / mask planes: the network's sequential
-//    `flow = flow + resize(...)`, in the same order.
+//    frame). The flow at a pixel is the sum, in block order, of those tensors resized to the pixel
+//    and scaled by 2 s_j: the network's sequential `flow = flow + resize(...)`. Blocks 1 and 2 need
+//    it only at their resize sample points and compute it there; block 3 computes it at every pixel
+//    and leaves it in FP32 planes, to which the blend adds block 3's own part;
+//  * every resize of this network has a power-of-two scale (the padded frame is a multiple of 32),
+//    so the position (o + 0.5) / scale is computed as (o + 0.5) * (1 / scale): exact, the same value.
 //
 // Every product and sum is written with the _rn intrinsics, in the order the network states it,
 // so that no multiply-add contraction changes a warp position.
@@ -26,20 +29,50 @@ constexpr int kIfBlocks = 4;
 // Scale of block k: the block works on the frame at 1/8, 1/4, 1/2, 1/1.
 __host__ __device__ constexpr int if_scale(int k) { return 8 >> k; }
 
-// The outputs of the transposed convs so far, FP32 planes [n][5][h][w] at 1/(2 s) of the padded frame.
+// The outputs of the transposed convs so far, FP32 [n][h][w][8] (5 used) at 1/(2 s) of the padded frame.
 struct IfFlowLevels {
   const float* t[kIfBlocks];
   int h[kIfBlocks], w[kIfBlocks];
   float mul[kIfBlocks];  // 2 s: flow scale of block j
+  float inv[kIfBlocks];  // 1 / (2 s): resize position factor from the frame to block j's tensor
 };
 
-// Input frames: caller's NCHW FP16 [n][3][H][W], placed at (top, left) in a zero padded
-// Hp x Wp plane.
+// Input frames: caller's NCHW FP16 [n][3][H][W], placed at (top, left) in a zero padded Hp x Wp
+// plane. `pad0` / `pad1`: the same frames padded, one 8-byte RGBx FP16 pixel each
+// ([n][Hp][Wp] uint2, filled by ifnet_pad_frames_kernel), so that a warp tap is one load.
 struct IfFrames {
   const __half* img0;
   const __half* img1;
   int H, W, Hp, Wp, top, left;
+  uint2* pad0;
+  uint2* pad1;
 };
+
+// NCHW frames -> padded RGBx pixels (zeros outside the window).
+__global__ void ifnet_pad_frames_kernel(IfFrames F, int batch) {
+  const long long total = static_cast<long long>(batch) * F.Hp * F.Wp;
+  const size_t plane = static_cast<size_t>(F.H) * F.W;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int X = static_cast<int>(i % F.Wp);
+    const int Y = static_cast<int>((i / F.Wp) % F.Hp);
+    const int n = static_cast<int>(i / (static_cast<long long>(F.Wp) * F.Hp));
+    const int y = Y - F.top, x = X - F.left;
+    uint2 p0 = make_uint2(0, 0), p1 = make_uint2(0, 0);
+    if (y >= 0 && y < F.H && x >= 0 && x < F.W) {
+      const size_t at = static_cast<size_t>(n) * 3 * plane + static_cast<size_t>(y) * F.W + x;
+      const __half z = __float2half_rn(0.0f);
+      const __half2 a01 = __halves2half2(F.img0[at], F.img0[at + plane]);
+      const __half2 a2 = __halves2half2(F.img0[at + 2 * plane], z);
+      const __half2 b01 = __halves2half2(F.img1[at], F.img1[at + plane]);
+      const __half2 b2 = __halves2half2(F.img1[at + 2 * plane], z);
+      p0 = make_uint2(*reinterpret_cast<const uint32_t*>(&a01), *reinterpret_cast<const uint32_t*>(&a2));
+      p1 = make_uint2(*reinterpret_cast<const uint32_t*>(&b01), *reinterpret_cast<const uint32_t*>(&b2));
+    }
+    F.pad0[i] = p0;
+    F.pad1[i] = p1;
+  }
+}
 
 __device__ __forceinline__ float lerp_rn(float a, float b, float t) {
   // (1 - t) * a + t * b
@@ -51,10 +84,10 @@ struct AxisTap {
   float t;
 };
 
-// Half-pixel resize tap of output index o along an axis of n_in -> n_out samples.
-__device__ __forceinline__ AxisTap resize_tap(int o, int n_in, int n_out) {
-  const float scale = __fdiv_rn(static_cast<float>(n_out), static_cast<float>(n_in));
-  float pos = __fsub_rn(__fdiv_rn(__fadd_rn(static_cast<float>(o), 0.5f), scale), 0.5f);
+// Half-pixel resize tap of output index o along an axis of n_in -> n_out samples, inv = n_in / n_out
+// a power of two (so that the division by the scale n_out / n_in is this exact product).
+__device__ __forceinline__ AxisTap resize_tap(int o, float inv, int n_in) {
+  float pos = __fsub_rn(__fmul_rn(__fadd_rn(static_cast<float>(o), 0.5f), inv), 0.5f);
   pos = fminf(fmaxf(pos, 0.0f), static_cast<float>(n_in - 1));
   AxisTap r;
   r.lo = static_cast<int>(pos);
@@ -78,20 +111,25 @@ __device__ __forceinline__ AxisTap warp_tap(int p, float f, int n) {
 // sets them.
 __device__ __forceinline__ void flow_step(const IfFlowLevels& L, int j, int n, int Y, int X, int Hp, int Wp,
                                           float f[4], float* mask) {
-  const AxisTap ty = resize_tap(Y, L.h[j], Hp);
-  const AxisTap tx = resize_tap(X, L.w[j], Wp);
-  const size_t plane = static_cast<size_t>(L.h[j]) * L.w[j];
-  const float* base = L.t[j] + static_cast<size_t>(n) * 5 * plane;
+  const AxisTap ty = resize_tap(Y, L.inv[j], L.h[j]);
+  const AxisTap tx = resize_tap(X, L.inv[j], L.w[j]);
+  const float* base = L.t[j] + static_cast<size_t>(n) * L.h[j] * L.w[j] * 8;
+  const float* ra = base + static_cast<size_t>(ty.lo) * L.w[j] * 8;
+  const float* rb = base + static_cast<size_t>(ty.hi) * L.w[j] * 8;
+  float q[4][5];
+  const float* px[4] = {ra + tx.lo * 8, ra + tx.hi * 8, rb + tx.lo * 8, rb + tx.hi * 8};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 u = __ldg(reinterpret_cast<const float4*>(px[k]));
+    q[k][0] = u.x;
+    q[k][1] = u.y;
+    q[k][2] = u.z;
+    q[k][3] = u.w;
+    q[k][4] = __ldg(px[k] + 4);
+  }
   float v[5];
 #pragma unroll
-  for (int c = 0; c < 5; ++c) {
-    const float* p = base + c * plane;
-    const float a = __ldg(p + static_cast<size_t>(ty.lo) * L.w[j] + tx.lo);
-    const float b = __ldg(p + static_cast<size_t>(ty.lo) * L.w[j] + tx.hi);
-    const float d = __ldg(p + static_cast<size_t>(ty.hi) * L.w[j] + tx.lo);
-    const float e = __ldg(p + static_cast<size_t>(ty.hi) * L.w[j] + tx.hi);
-    v[c] = lerp_rn(lerp_rn(a, b, tx.t), lerp_rn(d, e, tx.t), ty.t);
-  }
+  for (int c = 0; c < 5; ++c) v[c] = lerp_rn(lerp_rn(q[0][c], q[1][c], tx.t), lerp_rn(q[2][c], q[3][c], tx.t), ty.t);
   if (j == 0) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) f[c] = __fmul_rn(v[c], L.mul[j]);
@@ -103,7 +141,8 @@ __device__ __forceinline__ void flow_step(const IfFlowLevels& L, int j, int n, i
   }
 }
 
-// Full-resolution flow (planes 0-3) and mask (plane 4) after the blocks so far: FP32 [n][5][Hp][Wp].
+// Full-resolution flow (planes 0-3) and mask (plane 4) after blocks 0-2: FP32 [n][5][Hp][Wp],
+// written by block 3's input kernel, read by the blend.
 struct IfFlowField {
   float* f;
   int Hp, Wp;
@@ -112,64 +151,54 @@ struct IfFlowField {
   }
 };
 
-// flow / mask += block k's transposed-conv output resized to full resolution (flow x 2 s); block 0
-// sets them.
-__global__ void ifnet_flow_update_kernel(IfFlowLevels L, int k, int batch, IfFlowField F) {
-  const long long total = static_cast<long long>(batch) * F.Hp * F.Wp;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int X = static_cast<int>(i % F.Wp);
-    const int Y = static_cast<int>((i / F.Wp) % F.Hp);
-    const int n = static_cast<int>(i / (static_cast<long long>(F.Wp) * F.Hp));
-    float f[4], mask;
-    if (k > 0) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) f[c] = F.f[F.at(n, c, Y, X)];
-      mask = F.f[F.at(n, 4, Y, X)];
-    }
-    flow_step(L, k, n, Y, X, F.Hp, F.Wp, f, &mask);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) F.f[F.at(n, c, Y, X)] = f[c];
-    F.f[F.at(n, 4, Y, X)] = mask;
-  }
+// Flow (4) and mask after blocks [0, k) at padded pixel (Y, X) of frame n (k >= 1).
+__device__ __forceinline__ void flow_at(const IfFlowLevels& L, int k, int n, int Y, int X, int Hp, int Wp,
+                                        float f[4], float* mask) {
+  for (int j = 0; j < k; ++j) flow_step(L, j, n, Y, X, Hp, Wp, f, mask);
 }
 
-// Frame pixel (Y, X) of the zero padded plane, channel c.
-__device__ __forceinline__ float frame_px(const __half* img, const IfFrames& F, int n, int c, int Y, int X) {
-  const int y = Y - F.top, x = X - F.left;
-  if (y < 0 || y >= F.H || x < 0 || x >= F.W) return 0.0f;
-  return __half2float(img[((static_cast<size_t>(n) * 3 + c) * F.H + y) * F.W + x]);
+// The three channels of padded pixel (Y, X) of one padded frame.
+__device__ __forceinline__ void frame_rgb(const uint2* pad, const IfFrames& F, int n, int Y, int X, float c[3]) {
+  const uint2 q = __ldg(pad + (static_cast<size_t>(n) * F.Hp + Y) * F.Wp + X);
+  const float2 rg = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
+  c[0] = rg.x;
+  c[1] = rg.y;
+  c[2] = __low2float(*reinterpret_cast<const __half2*>(&q.y));
 }
 
-// Backward warp of the 3 channels of `img` at padded pixel (Y, X) by flow (fx, fy).
-__device__ __forceinline__ void warp3(const __half* img, const IfFrames& F, int n, int Y, int X, float fx, float fy,
+// Backward warp of the 3 channels of a padded frame at pixel (Y, X) by flow (fx, fy).
+__device__ __forceinline__ void warp3(const uint2* pad, const IfFrames& F, int n, int Y, int X, float fx, float fy,
                                       float out[3]) {
   const AxisTap tx = warp_tap(X, fx, F.Wp);
   const AxisTap ty = warp_tap(Y, fy, F.Hp);
   const float wx1 = __fsub_rn(1.0f, tx.t), wy1 = __fsub_rn(1.0f, ty.t);
+  float a[3], b[3], d[3], e[3];
+  frame_rgb(pad, F, n, ty.lo, tx.lo, a);
+  frame_rgb(pad, F, n, ty.lo, tx.hi, b);
+  frame_rgb(pad, F, n, ty.hi, tx.lo, d);
+  frame_rgb(pad, F, n, ty.hi, tx.hi, e);
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
-    const float a = frame_px(img, F, n, c, ty.lo, tx.lo);
-    const float b = frame_px(img, F, n, c, ty.lo, tx.hi);
-    const float d = frame_px(img, F, n, c, ty.hi, tx.lo);
-    const float e = frame_px(img, F, n, c, ty.hi, tx.hi);
     // (a (1 - wx) + b wx) (1 - wy) + (d (1 - wx) + e wx) wy
-    const float top = __fadd_rn(__fmul_rn(a, wx1), __fmul_rn(b, tx.t));
-    const float bot = __fadd_rn(__fmul_rn(d, wx1), __fmul_rn(e, tx.t));
+    const float top = __fadd_rn(__fmul_rn(a[c], wx1), __fmul_rn(b[c], tx.t));
+    const float bot = __fadd_rn(__fmul_rn(d[c], wx1), __fmul_rn(e[c], tx.t));
     out[c] = __fadd_rn(__fmul_rn(top, wy1), __fmul_rn(bot, ty.t));
   }
 }
 
 // The 12 input planes of block k >= 1 at padded full-resolution pixel (Y, X): warped frames (6),
-// timestep, mask, flow (4, not yet divided by the block scale).
-__device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowField& FF, int n, int Y, int X,
-                                             float timestep, float v[12]) {
-  float f[4];
+// timestep, mask, flow (4, not yet divided by the block scale). Block 3 also stores the flow.
+__device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowLevels& L, const IfFlowField& FF, int k,
+                                             int n, int Y, int X, float timestep, float v[12]) {
+  float f[4], mask;
+  flow_at(L, k, n, Y, X, F.Hp, F.Wp, f, &mask);
+  if (k == kIfBlocks - 1) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) f[c] = __ldg(FF.f + FF.at(n, c, Y, X));
-  const float mask = __ldg(FF.f + FF.at(n, 4, Y, X));
-  warp3(F.img0, F, n, Y, X, f[0], f[1], v);
-  warp3(F.img1, F, n, Y, X, f[2], f[3], v + 3);
+    for (int c = 0; c < 4; ++c) FF.f[FF.at(n, c, Y, X)] = f[c];
+    FF.f[FF.at(n, 4, Y, X)] = mask;
+  }
+  warp3(F.pad0, F, n, Y, X, f[0], f[1], v);
+  warp3(F.pad1, F, n, Y, X, f[2], f[3], v + 3);
   v[6] = timestep;
   v[7] = mask;
 #pragma unroll
@@ -178,8 +207,8 @@ __device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowFiel
 
 // Input of block k as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used):
 // the block's planes resized to 1/s (not for s = 1), the flow planes then divided by s.
-__global__ void ifnet_block_input_kernel(IfFrames F, IfFlowField FF, int k, int batch, float timestep,
-                                         uint8_t* __restrict__ out) {
+__global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int k, int batch,
+                                         float timestep, uint8_t* __restrict__ out) {
   const int s = if_scale(k);
   const int ho = F.Hp / s, wo = F.Wp / s;
   const long long total = static_cast<long long>(batch) * ho * wo;
@@ -193,10 +222,10 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowField FF, int k, int 
     for (int c = 0; c < 16; ++c) v[c] = 0.0f;
     const int nc = k == 0 ? 7 : 12;
     if (s == 1) {
-      block_planes(F, FF, n, oy, ox, timestep, v);
+      block_planes(F, L, FF, k, n, oy, ox, timestep, v);
     } else {
-      const AxisTap ty = resize_tap(oy, F.Hp, ho);
-      const AxisTap tx = resize_tap(ox, F.Wp, wo);
+      const AxisTap ty = resize_tap(oy, static_cast<float>(s), F.Hp);
+      const AxisTap tx = resize_tap(ox, static_cast<float>(s), F.Wp);
       float q[4][12];
       const int ys[2] = {ty.lo, ty.hi}, xs[2] = {tx.lo, tx.hi};
 #pragma unroll
@@ -205,13 +234,11 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowField FF, int k, int 
         for (int xx = 0; xx < 2; ++xx) {
           float* p = q[yy * 2 + xx];
           if (k == 0) {
-            for (int c = 0; c < 3; ++c) {
-              p[c] = frame_px(F.img0, F, n, c, ys[yy], xs[xx]);
-              p[3 + c] = frame_px(F.img1, F, n, c, ys[yy], xs[xx]);
-            }
+            frame_rgb(F.pad0, F, n, ys[yy], xs[xx], p);
+            frame_rgb(F.pad1, F, n, ys[yy], xs[xx], p + 3);
             p[6] = timestep;
           } else {
-            block_planes(F, FF, n, ys[yy], xs[xx], timestep, p);
+            block_planes(F, L, FF, k, n, ys[yy], xs[xx], timestep, p);
           }
         }
       for (int c = 0; c < nc; ++c)
@@ -241,7 +268,7 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowField FF, int k, int 
 
 // The interpolated frame: warp both frames by the final flow, blend with sigmoid(mask), crop the
 // window: out = w0 * m + w1 * (1 - m), NCHW FP16 [n][3][H][W].
-__global__ void ifnet_blend_kernel(IfFrames F, IfFlowField FF, int batch, __half* __restrict__ out) {
+__global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, __half* __restrict__ out) {
   const long long total = static_cast<long long>(batch) * F.H * F.W;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -249,13 +276,14 @@ __global__ void ifnet_blend_kernel(IfFrames F, IfFlowField FF, int batch, __half
     const int y = static_cast<int>((i / F.W) % F.H);
     const int n = static_cast<int>(i / (static_cast<long long>(F.W) * F.H));
     const int Y = y + F.top, X = x + F.left;
-    float f[4];
+    float f[4], mask;
 #pragma unroll
     for (int c = 0; c < 4; ++c) f[c] = __ldg(FF.f + FF.at(n, c, Y, X));
-    const float mask = __ldg(FF.f + FF.at(n, 4, Y, X));
+    mask = __ldg(FF.f + FF.at(n, 4, Y, X));
+    flow_step(L, kIfBlocks - 1, n, Y, X, F.Hp, F.Wp, f, &mask);
     float w0[3], w1[3];
-    warp3(F.img0, F, n, Y, X, f[0], f[1], w0);
-    warp3(F.img1, F, n, Y, X, f[2], f[3], w1);
+    warp3(F.pad0, F, n, Y, X, f[0], f[1], w0);
+    warp3(F.pad1, F, n, Y, X, f[2], f[3], w1);
     const float m = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-mask)));
     const float m1 = __fsub_rn(1.0f, m);
 #pragma unroll

@@ -183,7 +183,7 @@ struct IfLayer {
     // algorithmic work per output pixel of this conv grid (the transposed conv: 16 taps x 5 outputs
     // per input pixel, whatever the phase layout)
     flops_px = epi == kIfConvT ? 2.0 * 16.0 * cin * 5.0 : 2.0 * 9.0 * cin * cout;
-    bytes_px = (epi == kIfConvT ? 4.0 * 20.0 : out_chunks * 16.0) + (epi == kIfResPrelu ? out_chunks * 16.0 : 0.0) +
+    bytes_px = (epi == kIfConvT ? 4.0 * 32.0 : out_chunks * 16.0) + (epi == kIfResPrelu ? out_chunks * 16.0 : 0.0) +
                in_chunks * 16.0 * stride * stride;
     return Status::Ok();
   }
@@ -228,9 +228,10 @@ Status IfnetNet::create(const std::vector<float>& params, int max_batch, int H, 
   const int k_c0a = timer_.kind("ifnet.conv0a"), k_c0b = timer_.kind("ifnet.conv0b");
   const int k_res = timer_.kind("ifnet.res"), k_ct = timer_.kind("ifnet.convt");
   k_blend_ = timer_.kind("ifnet.blend");
-  k_flow_ = timer_.kind("ifnet.flow");
   KB2_TRY(flow_full_.alloc(static_cast<size_t>(max_batch_) * 5 * Hp_ * Wp_ * sizeof(float)));
   KB2_CUDA(cudaMemset(flow_full_.ptr, 0, flow_full_.bytes));
+  KB2_TRY(pad_.alloc(static_cast<size_t>(max_batch_) * 2 * Hp_ * Wp_ * sizeof(uint2)));
+  k_pad_ = timer_.kind("ifnet.pad");
 
   const float* p = params.data();
   for (int k = 0; k < kIfBlocks; ++k) {
@@ -244,7 +245,7 @@ Status IfnetNet::create(const std::vector<float>& params, int max_batch, int H, 
     KB2_TRY(tensor(a0, h1, w1, c / 16));
     KB2_TRY(tensor(r0, h2, w2, c / 8));
     KB2_TRY(tensor(r1, h2, w2, c / 8));
-    KB2_TRY(flows_[k].alloc(static_cast<size_t>(max_batch_) * 5 * h1 * w1 * sizeof(float)));
+    KB2_TRY(flows_[k].alloc(static_cast<size_t>(max_batch_) * h1 * w1 * 8 * sizeof(float)));
     KB2_CUDA(cudaMemset(flows_[k].ptr, 0, flows_[k].bytes));
     int* err = err_.as<int>();
 
@@ -331,20 +332,30 @@ Status IfnetNet::set_timestep(float t) {
   return Status::Ok();
 }
 
-int IfnetNet::launches_per_run() const { return 2 * kIfBlocks + static_cast<int>(layers_.size()) + 1; }
+int IfnetNet::launches_per_run() const { return 1 + kIfBlocks + static_cast<int>(layers_.size()) + 1; }
 
 size_t IfnetNet::device_bytes() const {
   size_t total = err_.bytes;
   for (const auto& t : tensors_) total += t->buf.bytes;
   for (const auto& f : flows_) total += f.bytes;
-  total += flow_full_.bytes;
+  total += flow_full_.bytes + pad_.bytes;
   for (const auto& l : layers_) total += l->wpack.bytes + l->bias.bytes + l->slope.bytes;
   return total;
 }
 
 Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, void* out, int batch) {
   if (batch < 1 || batch > max_batch_) return refuse(KB2_SHAPE_INVALID, "IFNet: batch out of contract");
-  IfFrames F{static_cast<const __half*>(img0), static_cast<const __half*>(img1), H_, W_, Hp_, Wp_, top_, left_};
+  uint2* pad0 = pad_.as<uint2>();
+  IfFrames F{static_cast<const __half*>(img0), static_cast<const __half*>(img1), H_, W_, Hp_, Wp_, top_, left_, pad0,
+             pad0 + static_cast<size_t>(max_batch_) * Hp_ * Wp_};
+  {
+    const long long px = static_cast<long long>(batch) * Hp_ * Wp_;
+    const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
+    KB2_TRY(timer_.begin(stream));
+    ifnet_pad_frames_kernel<<<blocks, 256, 0, stream>>>(F, batch);
+    KB2_CUDA(cudaGetLastError());
+    KB2_TRY(timer_.end(k_pad_, 0.0, px * (12.0 + 16.0), stream));
+  }
   IfFlowLevels L{};
   for (int k = 0; k < kIfBlocks; ++k) {
     const int s = if_scale(k);
@@ -352,17 +363,16 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
     L.h[k] = Hp_ / (2 * s);
     L.w[k] = Wp_ / (2 * s);
     L.mul[k] = static_cast<float>(2 * s);
+    L.inv[k] = 1.0f / static_cast<float>(2 * s);
   }
   const IfFlowField FF{flow_full_.as<float>(), Hp_, Wp_};
-  const long long full_px = static_cast<long long>(batch) * Hp_ * Wp_;
-  const int full_blocks = static_cast<int>(std::min<long long>((full_px + 255) / 256, 32LL * num_sms()));
   const int per_block = 2 + kIfRes + 1;
   for (int k = 0; k < kIfBlocks; ++k) {
     const int s = if_scale(k);
     const long long px = static_cast<long long>(batch) * (Hp_ / s) * (Wp_ / s);
     const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
     KB2_TRY(timer_.begin(stream));
-    ifnet_block_input_kernel<<<blocks, 256, 0, stream>>>(F, FF, k, batch, timestep_, x_[k]->ptr);
+    ifnet_block_input_kernel<<<blocks, 256, 0, stream>>>(F, L, FF, k, batch, timestep_, x_[k]->ptr);
     KB2_CUDA(cudaGetLastError());
     KB2_TRY(timer_.end(k_glue_, 0.0, px * 32.0, stream));
     for (int i = 0; i < per_block; ++i) {
@@ -372,15 +382,11 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
       KB2_TRY(l.launch(stream, batch));
       KB2_TRY(timer_.end(l.kind, l.flops_px * opx, l.bytes_px * opx, stream));
     }
-    KB2_TRY(timer_.begin(stream));
-    ifnet_flow_update_kernel<<<full_blocks, 256, 0, stream>>>(L, k, batch, FF);
-    KB2_CUDA(cudaGetLastError());
-    KB2_TRY(timer_.end(k_flow_, 0.0, full_px * (k == 0 ? 20.0 : 40.0), stream));
   }
   const long long px = static_cast<long long>(batch) * H_ * W_;
   const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
   KB2_TRY(timer_.begin(stream));
-  ifnet_blend_kernel<<<blocks, 256, 0, stream>>>(F, FF, batch, static_cast<__half*>(out));
+  ifnet_blend_kernel<<<blocks, 256, 0, stream>>>(F, L, FF, batch, static_cast<__half*>(out));
   KB2_CUDA(cudaGetLastError());
   KB2_TRY(timer_.end(k_blend_, 0.0, px * (20.0 + 12.0 + 6.0), stream));
   return Status::Ok();

@@ -47,10 +47,11 @@ class IfnetNet {
   std::vector<std::unique_ptr<Tensor>> tensors_;
   std::vector<std::unique_ptr<IfLayer>> layers_;  // per block: conv0a, conv0b, 8 residual, convT
   const Tensor* x_[4] = {};                       // block inputs
-  DeviceBuffer flows_[4];                         // transposed-conv outputs, FP32 [n][5][Hp/2s][Wp/2s]
-  DeviceBuffer flow_full_;                        // flow / mask so far, FP32 [n][5][Hp][Wp]
+  DeviceBuffer flows_[4];                         // transposed-conv outputs, FP32 [n][Hp/2s][Wp/2s][8]
+  DeviceBuffer flow_full_;                        // flow / mask after blocks 0-2, FP32 [n][5][Hp][Wp]
+  DeviceBuffer pad_;                              // both frames, padded RGBx FP16 pixels [2][n][Hp][Wp]
   LayerTimer timer_;
-  int k_glue_ = 0, k_blend_ = 0, k_flow_ = 0;
+  int k_glue_ = 0, k_blend_ = 0, k_pad_ = 0;
 };
 
 // Bilinear backward-warp taps of a flow field [n][2][h][w] (FP32, device): x0, x1, y0, y1 as int32
