@@ -71,9 +71,37 @@ struct IfShape {
   static constexpr int groups_per_warp = kN / 16;  // 8-column groups per epilogue warp (half of N)
 };
 
-template <int kN, int kStride, int kEpi>
+// Accumulating MMAs kFrom .. kCount - 1 of a stage's descriptor lists, from one or two asm blocks
+// (at most 9 MMAs per block).
+template <int kFrom, int kCount>
+__device__ __forceinline__ void if_issue(uint32_t d, const uint64_t (&ad)[12], const uint64_t (&bd)[12], uint32_t idesc) {
+  constexpr int n = kCount - kFrom;
+  constexpr int n1 = n < 9 ? n : 9;
+  uint64_t a1[9], b1[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) {
+    a1[i] = i < n1 ? ad[kFrom + i] : 0;
+    b1[i] = i < n1 ? bd[kFrom + i] : 0;
+  }
+  mma_ss_block<false, n1>(d, a1, b1, idesc);
+  if constexpr (n > 9) {
+    uint64_t a2[9], b2[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) {
+      a2[i] = i < n - 9 ? ad[kFrom + 9 + i] : 0;
+      b2[i] = i < n - 9 ? bd[kFrom + 9 + i] : 0;
+    }
+    mma_ss_block<false, (n > 9 ? n - 9 : 1)>(d, a2, b2, idesc);
+  }
+}
+
+// kG: input chunks per K group (2, 4, 6 or 8), so that a stage's 3 x kG / 2 MMAs are known at
+// compile time and issue from asm blocks with nothing in between (an instruction between two MMAs
+// costs the single issuing thread ~60 cycles).
+template <int kN, int kStride, int kEpi, int kG>
 __global__ void __launch_bounds__(kIfThreads, 1)
     ifconv_kernel(const __grid_constant__ IfMaps maps, const __grid_constant__ IfConvArgs a) {
+  static_assert(kG == 2 || kG == 4 || kG == 6 || kG == 8, "group of 2..8 chunks");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
   uint8_t* ring = smem;
@@ -169,14 +197,15 @@ __global__ void __launch_bounds__(kIfThreads, 1)
       constexpr uint32_t kStep = 2u * kN * 16u;  // B bytes per K step
       RingPos st{0, 0}, acc{0, 0};
       bool ok = true;
-      const int half_steps = a.g >> 1;
+      constexpr int kHs = kG / 2;     // K steps per tap (chunk pairs)
+      constexpr int kNm = 3 * kHs;    // MMAs per stage
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
         const int t = item / a.strips;
         const int oy = t % a.h_out;
         if (!wait_bar(&acc_empty[acc.idx], acc.phase ^ 1u, a.err, kErrWaitMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc.idx * kN;
-        uint32_t accumulate = 0;
+        bool first = true;
         for (int dy = 0; dy < 3 && ok; ++dy) {
           const int iy = oy * kStride + dy - 1;
           if (iy < 0 || iy >= a.h_in) continue;
@@ -188,6 +217,7 @@ __global__ void __launch_bounds__(kIfThreads, 1)
             tc_fence_after();
             const uint32_t a_base = smem_u32(ring + st.idx * a.stage_bytes);
             const uint32_t b_base = a_base + a.a_bytes;
+            uint64_t ad[12], bd[12];
 #pragma unroll
             for (int dx = 0; dx < 3; ++dx) {
               // tap dx: which staged box and how many pixels into it
@@ -195,16 +225,23 @@ __global__ void __launch_bounds__(kIfThreads, 1)
               if constexpr (kStride == 1) {
                 tile = a_base + static_cast<uint32_t>(dx) * 16u;
               } else {
-                const uint32_t odd = a_base + static_cast<uint32_t>(a.g) * kIfChunkBytes;
+                const uint32_t odd = a_base + static_cast<uint32_t>(kG) * kIfChunkBytes;
                 tile = dx == 0 ? odd : (dx == 1 ? a_base + 16u : odd + 16u);
               }
-              for (int j = 0; j < half_steps; ++j) {
-                const uint64_t adesc = make_sdesc(tile + static_cast<uint32_t>(2 * j) * kIfChunkBytes, kIfChunkBytes, 128);
-                const uint64_t bdesc =
-                    make_sdesc(b_base + static_cast<uint32_t>(dx * half_steps + j) * kStep, kN * 16u, 128);
-                mma_ss<false>(d_tmem, adesc, bdesc, idesc, accumulate);
-                accumulate = 1;
+#pragma unroll
+              for (int j = 0; j < kHs; ++j) {
+                ad[dx * kHs + j] = make_sdesc(tile + static_cast<uint32_t>(2 * j) * kIfChunkBytes, kIfChunkBytes, 128);
+                bd[dx * kHs + j] = make_sdesc(b_base + static_cast<uint32_t>(dx * kHs + j) * kStep, kN * 16u, 128);
               }
+            }
+#pragma unroll
+            for (int i = kNm; i < 12; ++i) ad[i] = bd[i] = 0;
+            if (first) {  // the item's first MMA overwrites the accumulator, the rest accumulate
+              mma_ss<false>(d_tmem, ad[0], bd[0], idesc, 0u);
+              if_issue<1, kNm>(d_tmem, ad, bd, idesc);
+              first = false;
+            } else {
+              if_issue<0, kNm>(d_tmem, ad, bd, idesc);
             }
             mma_commit(&empty[st.idx]);
             st.advance(a.stages);

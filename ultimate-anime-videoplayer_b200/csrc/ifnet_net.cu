@@ -27,35 +27,37 @@ constexpr int kIfRes = 8;
 
 using IfLaunchFn = void (*)(dim3, size_t, cudaStream_t, const IfMaps&, const IfConvArgs&);
 
-template <int N, int S, int E>
+template <int N, int S, int E, int G>
 void if_launch(dim3 grid, size_t smem, cudaStream_t s, const IfMaps& m, const IfConvArgs& a) {
-  ifconv_kernel<N, S, E><<<grid, kIfThreads, smem, s>>>(m, a);
+  ifconv_kernel<N, S, E, G><<<grid, kIfThreads, smem, s>>>(m, a);
 }
 
 struct IfKernel {
-  int n, stride, epi;
+  int n, stride, epi, g;
   IfLaunchFn launch;
   const void* fn;
 };
 
-#define KB2_IFK(N, S, E) \
-  IfKernel { N, S, E, &if_launch<N, S, E>, reinterpret_cast<const void*>(&ifconv_kernel<N, S, E>) }
+#define KB2_IFK(N, S, E, G) \
+  IfKernel { N, S, E, G, &if_launch<N, S, E, G>, reinterpret_cast<const void*>(&ifconv_kernel<N, S, E, G>) }
 
+// the classic IFNet's layers: (N, stride, epilogue, input chunks per K group)
 const IfKernel kIfKernels[] = {
     // conv0a: 12 (7) channels -> C/2, stride 2
-    KB2_IFK(96, 2, kIfPrelu), KB2_IFK(64, 2, kIfPrelu), KB2_IFK(48, 2, kIfPrelu), KB2_IFK(32, 2, kIfPrelu),
+    KB2_IFK(96, 2, kIfPrelu, 2), KB2_IFK(64, 2, kIfPrelu, 2), KB2_IFK(48, 2, kIfPrelu, 2), KB2_IFK(32, 2, kIfPrelu, 2),
     // conv0b: C/2 -> C, stride 2
-    KB2_IFK(192, 2, kIfPrelu), KB2_IFK(128, 2, kIfPrelu),
+    KB2_IFK(192, 2, kIfPrelu, 6), KB2_IFK(128, 2, kIfPrelu, 8), KB2_IFK(96, 2, kIfPrelu, 6),
+    KB2_IFK(64, 2, kIfPrelu, 4),
     // residual convs: C -> C
-    KB2_IFK(192, 1, kIfResPrelu), KB2_IFK(128, 1, kIfResPrelu), KB2_IFK(96, 1, kIfResPrelu),
-    KB2_IFK(64, 1, kIfResPrelu),
+    KB2_IFK(192, 1, kIfResPrelu, 8), KB2_IFK(128, 1, kIfResPrelu, 8), KB2_IFK(96, 1, kIfResPrelu, 6),
+    KB2_IFK(64, 1, kIfResPrelu, 8),
     // transposed conv: C -> 4 phases x 8
-    KB2_IFK(32, 1, kIfConvT),
+    KB2_IFK(32, 1, kIfConvT, 8), KB2_IFK(32, 1, kIfConvT, 6),
 };
 
-const IfKernel* find_if_kernel(int n, int stride, int epi) {
+const IfKernel* find_if_kernel(int n, int stride, int epi, int g) {
   for (const IfKernel& k : kIfKernels)
-    if (k.n == n && k.stride == stride && k.epi == epi) return &k;
+    if (k.n == n && k.stride == stride && k.epi == epi && k.g == g) return &k;
   return nullptr;
 }
 
@@ -91,10 +93,10 @@ struct IfLayer {
   Status build(int n_pad, int stride, int epi, W w, int cout, int cin, const float* b, const float* prelu,
                uint8_t* in, int batch, int h_in, int w_in, int in_chunks, int h_out, int w_out, uint8_t* out,
                int out_chunks, float* out_f32, int* err) {
-    k = find_if_kernel(n_pad, stride, epi);
-    if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet: no conv kernel for this layer shape");
     const int g = group_chunks(in_chunks);
     if (g == 0 || in_chunks * 8 < cin) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet: input channel layout");
+    k = find_if_kernel(n_pad, stride, epi, g);
+    if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet: no conv kernel for this layer shape");
     IfConvArgs& a = args;
     a.h_in = h_in;
     a.w_in = w_in;
