@@ -58,7 +58,11 @@ struct SpabArgs {
 __host__ __device__ constexpr uint32_t spab_slots(int c) { return c == 2 ? 4u : 3u; }
 __host__ __device__ constexpr uint32_t spab_tmem_base(int c) { return c == 0 ? 0u : (c == 1 ? 144u : 288u); }
 
-constexpr uint32_t kSpabSmemExtra = 1024 + 64 * 8 + 2 * 3 * 48 * 4 + 64;
+// after the rings: 64 barriers, per-conv constants, TMEM address, then (at kSpabZeroOff) the
+// all-zero B tile of the clearing MMA (48 rows x 32 B)
+constexpr uint32_t kSpabZeroOff = 1792;
+constexpr uint32_t kSpabSmemExtra = 1024 + kSpabZeroOff + 48 * 32 + 64;
+static_assert(64 * 8 + 2 * 3 * 48 * 4 + 4 <= kSpabZeroOff, "shared layout");
 
 template <bool kLast>
 __global__ void __launch_bounds__(kSpabThreads, 1)
@@ -80,9 +84,12 @@ __global__ void __launch_bounds__(kSpabThreads, 1)
   float* s_bias = reinterpret_cast<float*>(bars + 64);  // [3][48]
   float* s_scale = s_bias + 3 * 48;                     // [3][48]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_scale + 3 * 48);
+  uint8_t* zero_b = reinterpret_cast<uint8_t*>(bars) + kSpabZeroOff;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  for (uint32_t j = threadIdx.x; j < 48 * 32 / 16; j += blockDim.x) reinterpret_cast<uint4*>(zero_b)[j] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();  // the zero tile is read by the tensor core (async proxy)
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kSpabInRing; ++i) {
       mbar_init(&full[i], 1);
@@ -173,13 +180,23 @@ __global__ void __launch_bounds__(kSpabThreads, 1)
       RingPos acc[3] = {{0, 0}, {0, 0}, {0, 0}};
 
       // one input row of conv c: input index t of n_out + 2, feeding outputs t - 2 .. t
+      const uint64_t zero_desc = make_sdesc(smem_u32(zero_b), 48 * 16, 128);
+      // one input row of conv c: input index t of n_out + 2, feeding outputs t - 2 .. t. A fresh
+      // output row's slot is cleared by an MMA against the zero B tile; then every MMA accumulates,
+      // n_k per group of contiguous slots, each group from one asm block (an instruction between
+      // two MMAs costs the issuing thread ~60 cycles). A window that wraps around the 3- or 4-slot
+      // ring is split in two groups.
       auto conv_row = [&](int c, int t, int n_out, uint64_t a_row) -> bool {
         const uint32_t R = spab_slots(c);
         const uint32_t tb = tmem_base + spab_tmem_base(c);
         RingPos& ac = acc[c];
         const int b0 = t >= 2 ? 0 : 2 - t;
         const int b1 = t <= n_out - 1 ? 3 : (t == n_out ? 2 : 1);
-        if (b1 == 3 && !wait_bar(&acc_free[4 * c + ac.idx], ac.phase, a.err, kErrWaitMma)) return false;
+        if (b1 == 3) {
+          if (!wait_bar(&acc_free[4 * c + ac.idx], ac.phase, a.err, kErrWaitMma)) return false;
+          tc_fence_after();
+          mma_ss<true>(tb + ac.idx * 48u, a_row + kd[0], zero_desc, id_n[0], 0u);
+        }
         tc_fence_after();
         const uint32_t back = static_cast<uint32_t>(2 - b0);
         const uint32_t s_first = ac.idx >= back ? ac.idx - back : ac.idx + R - back;
@@ -187,24 +204,18 @@ __global__ void __launch_bounds__(kSpabThreads, 1)
         const uint32_t nb1 = nb < R - s_first ? nb : R - s_first;
         const uint32_t nb2 = nb - nb1;
         const uint64_t b_first = bdesc[c] + static_cast<uint64_t>(b0) * kBlock16;
-        uint32_t slot = s_first;
-        for (int blk = b0; blk < b1; ++blk) {
-          const uint32_t fresh = (b1 == 3 && blk == 2) ? 1u : 0u;
-          mma_ss<true>(tb + slot * 48u, a_row + kd[0], bdesc[c] + static_cast<uint64_t>(blk) * kBlock16, id_n[0],
-                       fresh ^ 1u);
-          slot = slot + 1 == R ? 0 : slot + 1;
+        uint64_t ad[kRowMaxK], bd[kRowMaxK];
+#pragma unroll
+        for (int j = 0; j < kRowMaxK; ++j) {
+          ad[j] = a_row + kd[j];
+          bd[j] = b_first + static_cast<uint64_t>(j) * kBStep16;
         }
-        const uint32_t id1 = id_n[nb1 - 1];
+        const uint32_t id1 = nb1 == 3 ? id_n[2] : (nb1 == 2 ? id_n[1] : id_n[0]);
+        mma_ss_row<true>(tb + s_first * 48u, ad, bd, id1, n_k);
+        if (nb2 > 0) {  // the blocks past the end of the ring go to slot 0
 #pragma unroll
-        for (int j = 1; j < kRowMaxK; ++j)
-          if (j < n_k)
-            mma_ss<true>(tb + s_first * 48u, a_row + kd[j], b_first + static_cast<uint64_t>(j) * kBStep16, id1, 1u);
-        if (nb2 > 0) {
-          const uint32_t id2 = id_n[nb2 - 1];
-          const uint64_t b_second = b_first + static_cast<uint64_t>(nb1) * kBlock16;
-#pragma unroll
-          for (int j = 1; j < kRowMaxK; ++j)
-            if (j < n_k) mma_ss<true>(tb, a_row + kd[j], b_second + static_cast<uint64_t>(j) * kBStep16, id2, 1u);
+          for (int j = 0; j < kRowMaxK; ++j) bd[j] += static_cast<uint64_t>(nb1) * kBlock16;
+          mma_ss_row<true>(tb, ad, bd, nb2 == 2 ? id_n[1] : id_n[0], n_k);
         }
         if (t >= 2) mma_commit(&acc_full[4 * c + (ac.idx >= 2 ? ac.idx - 2 : ac.idx + R - 2)]);
         ac.advance(R);

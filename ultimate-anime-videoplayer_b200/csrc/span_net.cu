@@ -26,10 +26,10 @@
 
 namespace kb2 {
 
-// Fused E4M3 SPAN blocks (spab8.cuh, bit-identical to the three separate launches) are off: with
-// 3 x 3 TMEM slots its issuer still uses per-block MMAs and ring-wrap splits (7-11 instructions per
-// convolution row), and measured on 8 x 1080p one fused block took 4.14 ms against 0.93 + 0.93 +
-// 1.08 ms for the three stacked launches, whose issue is one asm block of 5 MMAs per row.
+// Fused E4M3 SPAN blocks (spab8.cuh, bit-identical to the three separate launches) are off: its
+// three 3-slot accumulator rings wrap on two rows in three, and a wrapped row is issued as two MMA
+// groups. Measured on 8 x 1080p one fused block took 3.71 ms against 0.94 + 0.94 + 1.07 ms for the
+// three stacked launches; a conv row's issue took ~1,000 cycles unwrapped and ~1,700 wrapped.
 constexpr bool kFuseSpab = false;
 
 namespace {
