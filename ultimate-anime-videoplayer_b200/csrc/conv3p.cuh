@@ -1,0 +1,781 @@
+// Paired stacked 3x3 convolution: the stacked-kernel-row scheme of conv3s.cuh with every MMA shared
+// by the two SMs of a cluster (sm_100a, tcgen05 cta_group::2, M = 256).
+//
+// Why: the single issuing thread limits conv3s. Measured on B200, a tcgen05.mma of M = 128 costs its
+// issuing thread ~60 cycles whatever else runs, and each instruction between MMAs costs more, so a
+// row of 9 MMAs plus its bookkeeping took ~1,400-1,800 cycles against ~820 cycles of tensor work. An
+// M = 256 MMA (cta_group::2) runs at the same ~72 cycles per instruction (N = 144, measured) but
+// feeds both SMs of the pair: the issue cost per output pixel halves.
+//
+// Layout of the pair: block r of the cluster owns strip 2p + r of a (frame, band, strip pair) item.
+//  * A (the input row) is split by rows of M: each block copies its own strip's row into its own
+//    ring slot, at the same shared-memory offset in both blocks;
+//  * B (the stacked weights, N = 3 x 48 rows per K step) is split by rows of N: block 0 holds rows
+//    0 .. N/2 - 1, block 1 rows N/2 .. N - 1, each as [K step][K half][N/2 rows][16 bytes], so one
+//    descriptor addresses both halves and D column c is B row c;
+//  * D: each block's TMEM holds its own 128 pixels x all N columns (the 6-slot, 8-block dual-location
+//    window of conv3s.cuh, unchanged).
+// Block 0's thread issues every MMA; its barriers gather the pair: the input row is "full" when both
+// blocks' copies landed (the copies of block 1 complete on block 0's barrier), and an accumulator
+// slot is free when both blocks' epilogues read it (block 1 arrives remotely). Commits multicast to
+// both blocks' "done" barriers.
+//
+// Uniform rows. Every input row t of a band (t = 0 .. rows + 1) is issued alike: clear the block(s)
+// of output entry t, then n_k MMAs of N = 144 into the window of entries t - 2 .. t. A band of
+// `rows` output rows owns rows + 2 consecutive entries; the last two are "virtual" (they collect the
+// out-of-band products of the band's first and last input rows) and the epilogue releases them
+// without reading. The accumulator ring never steps back, and no band-edge MMA variants exist.
+//
+// Roles (both blocks): warp 0 = TMA producer, warp 1 = TMEM allocation (pair-wide) and, in block 0,
+// the MMA issuer, warps 2.. = epilogue of the block's own pixels (conv_tc.cuh epilogues).
+#pragma once
+
+#include <utility>
+
+#include "conv3s.cuh"
+
+namespace kb2 {
+
+constexpr uint16_t kPairMask = 3;  // both blocks of the cluster
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// All threads of both blocks.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of the variable at `local` (a shared::cta address) in block `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Relaxed arrive: orders nothing before it. For releasing an accumulator slot whose TMEM reads have
+// completed (tcgen05.wait::ld): a release at cluster scope would also wait until the epilogue's
+// earlier global stores are visible cluster-wide, which cost ~1,000-1,800 cycles per row (measured).
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// This block's share of a pair copy: its own destination, completion counted on the barrier at
+// `cluster_bar` (block 0's). No multicast.
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint32_t cluster_bar, int c0,
+                                                 int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* holder, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrives on the barrier at this offset in both blocks once every MMA issued so far completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(kPairMask)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- row issue (two asm blocks)
+// The head tests the NEXT row's input and slot barriers (mbarrier.test_wait does not block; its
+// predicates are read only after the head's MMAs), clears the fresh entry's block(s) with an MMA of
+// a zero B and enable-input-d off, and issues the first half of the row's MMAs; the tail issues the
+// rest and the row's commit.
+template <bool kFp8, int kNK, int kClears>
+__device__ __forceinline__ uint32_t pair_row_head(
+    uint32_t d_clear, uint32_t d_clear2, uint64_t zero_desc, uint32_t id_clear, uint32_t d_win, uint32_t idesc,
+    uint32_t nf, uint32_t nf_par, uint32_t ns, uint32_t ns_par, const uint64_t (&a)[9], const uint64_t (&b)[9]) {
+  static_assert(kNK == 2 || kNK == 5 || kNK == 9, "rows of 2, 5 or 9 K steps");
+  static_assert(kClears == 1 || kClears == 2, "one or two cleared blocks");
+  uint32_t ok;
+  if constexpr (kFp8 == false && kNK == 2 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %12, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]),
+            "l"(b[0])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 2 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %12, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]),
+            "l"(b[0])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 5 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 5 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 9 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %16, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %14, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %15, %20, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 9 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %16, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %14, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %15, %20, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 2 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %12, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]),
+            "l"(b[0])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 2 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %12, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]),
+            "l"(b[0])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 5 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 5 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 9 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %16, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %14, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %15, %20, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 9 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %16, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %14, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %15, %20, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4])
+          : "memory");
+  }
+  return ok;
+}
+
+template <bool kFp8, int kNK>
+__device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, uint32_t done,
+                                              const uint64_t (&a)[9], const uint64_t (&b)[9]) {
+  if constexpr (kFp8 == false && kNK == 2) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %5, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[1]),
+            "l"(b[1])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 5) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %6, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %5, %7, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[3]), "l"(a[4]),
+            "l"(b[3]), "l"(b[4])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 9) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %8, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %5, %9, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %6, %10, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %7, %11, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+            "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 2) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %4, %5, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[1]),
+            "l"(b[1])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 5) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %4, %6, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %5, %7, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[3]), "l"(a[4]),
+            "l"(b[3]), "l"(b[4])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 9) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %4, %8, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %5, %9, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %6, %10, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %7, %11, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
+            "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8])
+          : "memory");
+  }
+}
+struct PairIssue {
+  const ConvArgs& a;
+  uint32_t ring_base, w_base, zero_base, tmem_base;
+  const uint64_t* s_k;
+  uint64_t* full;
+  uint64_t* done;
+  uint64_t* slot_free;
+};
+
+// What every row of the issuer needs, set up once.
+struct PairRowCtx {
+  uint64_t ad0[kRowMaxK];  // A descriptors of ring slot 0 (slot k adds k * slot16)
+  uint64_t bs[kRowMaxK];   // B descriptors (all three kernel rows)
+  uint64_t zero_desc;
+  uint64_t slot16;  // one ring slot, in descriptor address units
+  uint32_t tmem;
+  uint32_t full_u32, done_u32, free_u32;  // shared addresses of full[0], done[0], slot_free[0]
+  uint64_t* full;
+  uint64_t* slot_free;
+  int* err;
+};
+
+// Input row k of a 12-row period. The input ring has 12 slots and the accumulator ring 6, so within
+// a period every slot index, TMEM address and accumulator phase is a compile-time constant; only
+// the input ring's phase (one bit per period) is not. The issuing thread then executes little
+// besides its two asm blocks.
+template <bool kFp8, int kCoutPad, int kNK, int kK>
+__device__ __forceinline__ bool pair_row_k(const PairRowCtx& c, uint32_t ph, uint32_t& pre) {
+  constexpr uint32_t kSlot = kK % 6;
+  constexpr uint32_t kAccPh = kK >= 6 ? 1u : 0u;
+  constexpr uint32_t kStart = kSlot >= 2 ? kSlot - 2 : kSlot + 4;
+  constexpr uint32_t kNext = (kK + 1) % 12;
+  constexpr uint32_t kNextSlot = kNext % 6;
+  constexpr uint32_t kNextAccPh = kNext >= 6 ? 1u : 0u;
+  constexpr uint32_t kIdClear = make_idesc(256, kCoutPad);
+  constexpr uint32_t kIdWin = make_idesc(256, 3 * kCoutPad);
+  if (!(pre & 1u) && !wait_bar(c.full + kK, ph, c.err, kErrWaitMma)) return false;
+  if (!(pre & 2u) && !wait_bar(c.slot_free + kSlot, kAccPh, c.err, kErrWaitMma)) return false;
+  tc_fence_after();
+  uint64_t ad[kRowMaxK];
+  const uint64_t off = static_cast<uint64_t>(kK) * c.slot16;
+#pragma unroll
+  for (int j = 0; j < kRowMaxK; ++j) ad[j] = c.ad0[j] + off;
+  const uint32_t d_clear = c.tmem + kSlot * kCoutPad;
+  const uint32_t d_win = c.tmem + kStart * kCoutPad;
+  const uint32_t nf = c.full_u32 + kNext * 8u;
+  const uint32_t nf_par = ph ^ (kK == 11 ? 1u : 0u);
+  const uint32_t ns = c.free_u32 + kNextSlot * 8u;
+  pre = pair_row_head<kFp8, kNK, (kSlot < 2 ? 2 : 1)>(d_clear, d_clear + 6u * kCoutPad, c.zero_desc, kIdClear, d_win,
+                                                        kIdWin, nf, nf_par, ns, kNextAccPh, ad, c.bs);
+  pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + kK * 8u, ad, c.bs);
+  return true;
+}
+
+template <bool kFp8, int kCoutPad, int kNK, int... kKs>
+__device__ __forceinline__ bool pair_period(const PairRowCtx& c, uint32_t ph, uint32_t& pre,
+                                            std::integer_sequence<int, kKs...>) {
+  return (pair_row_k<kFp8, kCoutPad, kNK, kKs>(c, ph, pre) && ...);
+}
+
+// The MMA issuer of the pair (block 0, one thread), for rows of kNK K steps. Every input row is
+// alike (uniform rows), so the issuer only needs the number of input rows of its items.
+template <bool kFp8, int kCoutPad, int kNK>
+__device__ __forceinline__ void pair_issue(const PairIssue& is) {
+  static_assert(kStackSlots == 6, "the 12-row period assumes 6 accumulator slots");
+  const ConvArgs& a = is.a;
+  constexpr int kNHalf = 3 * kCoutPad / 2;                  // B rows per block
+  constexpr uint64_t kBStep16 = (2u * kNHalf * 16u) >> 4;  // one K step of this block's B
+  constexpr uint32_t R = kStackSlots;
+  constexpr uint32_t kIdClear = make_idesc(256, kCoutPad);
+  constexpr uint32_t kIdWin = make_idesc(256, 3 * kCoutPad);
+  PairRowCtx c;
+  const uint64_t a_base = make_sdesc(0, 0, 128) | static_cast<uint64_t>(is.ring_base >> 4);
+  const uint64_t b_desc0 = make_sdesc(is.w_base, kNHalf * 16, 128);
+#pragma unroll
+  for (int j = 0; j < kRowMaxK; ++j) {
+    c.ad0[j] = a_base + is.s_k[j];
+    c.bs[j] = b_desc0 + static_cast<uint64_t>(j) * kBStep16;
+  }
+  c.zero_desc = make_sdesc(is.zero_base, (kCoutPad / 2) * 16, 128);
+  c.slot16 = a.slot_bytes >> 4;
+  c.tmem = is.tmem_base;
+  c.full_u32 = smem_u32(is.full);
+  c.done_u32 = smem_u32(is.done);
+  c.free_u32 = smem_u32(is.slot_free);
+  c.full = is.full;
+  c.slot_free = is.slot_free;
+  c.err = a.err;
+  // input rows of this cluster's items: rows + 2 per band
+  uint32_t total = 0;
+  for (uint32_t item = cluster_id_x(); item < static_cast<uint32_t>(a.items); item += cluster_count_x()) {
+    const int band = (static_cast<int>(item) / a.pairs) % a.bands;
+    const int y0 = band * a.band_rows;
+    total += static_cast<uint32_t>(min(a.H, y0 + a.band_rows) - y0 + 2);
+  }
+  if (a.ring != 12u) return;  // the host sizes every paired ring to 12 slots
+  uint32_t ph = 0;   // input ring phase of the current period
+  uint32_t pre = 0;  // next row's barriers found complete by the previous row: 1 = input, 2 = slot
+  uint32_t g = 0;
+  for (; g + 12u <= total; g += 12u, ph ^= 1u)
+    if (!pair_period<kFp8, kCoutPad, kNK>(c, ph, pre, std::make_integer_sequence<int, 12>{})) return;
+  // the last rows (fewer than a period), with run-time positions
+  RingPos in{0, ph};
+  RingPos acc{0, 0};
+  for (; g < total; ++g) {
+    if (!(pre & 1u) && !wait_bar(&is.full[in.idx], in.phase, a.err, kErrWaitMma)) return;
+    if (!(pre & 2u) && !wait_bar(&is.slot_free[acc.idx], acc.phase, a.err, kErrWaitMma)) return;
+    tc_fence_after();
+    uint64_t ad[kRowMaxK];
+    const uint64_t off = static_cast<uint64_t>(in.idx) * c.slot16;
+#pragma unroll
+    for (int j = 0; j < kRowMaxK; ++j) ad[j] = c.ad0[j] + off;
+    const uint32_t start = acc.idx >= 2 ? acc.idx - 2 : acc.idx + R - 2;
+    const uint32_t d_clear = c.tmem + acc.idx * kCoutPad;
+    const uint32_t d_win = c.tmem + start * kCoutPad;
+    RingPos nin = in;
+    nin.advance(a.ring);
+    RingPos nacc = acc;
+    nacc.advance(R);
+    const uint32_t nf = c.full_u32 + nin.idx * 8u;
+    const uint32_t ns = c.free_u32 + nacc.idx * 8u;
+    if (acc.idx < 2)
+      pre = pair_row_head<kFp8, kNK, 2>(d_clear, d_clear + 6u * kCoutPad, c.zero_desc, kIdClear, d_win, kIdWin, nf,
+                                        nin.phase, ns, nacc.phase, ad, c.bs);
+    else
+      pre = pair_row_head<kFp8, kNK, 1>(d_clear, d_clear, c.zero_desc, kIdClear, d_win, kIdWin, nf, nin.phase, ns,
+                                        nacc.phase, ad, c.bs);
+    pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + in.idx * 8u, ad, c.bs);
+    in.advance(a.ring);
+    acc.advance(R);
+  }
+}
+
+template <bool kFp8, int kCoutPad, int kEpi, int kOut>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>::threads, 1)
+    conv3p_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
+  static_assert(kCoutPad == 16 || kCoutPad == 48, "paired kernel: 16 or 48 output channels");
+  constexpr int kEpiWarps = StackShape<kCoutPad>::epi_warps;
+  constexpr uint32_t R = kStackSlots;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sw = smem;  // this block's half of B
+  uint8_t* ring = smem + a.w_smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + a.ring * a.slot_bytes);
+  uint64_t* full = bars;                    // block 0: both copies of an input row landed
+  uint64_t* done = bars + a.ring;           // both blocks: the input row is consumed
+  uint64_t* slot_free = bars + 2 * a.ring;  // block 0: both epilogues read the slot
+  uint64_t* wbar = slot_free + R;           // this block's weights landed
+  uint64_t* wpeer = wbar + 1;               // block 0: block 1's weights landed
+  uint64_t* drain = wpeer + 1;              // both blocks: every MMA completed
+  uint64_t* s_k = bars + 128;               // per K step of a row: (a_off >> 4) | (lbo >> 4) << 16
+  float* s_bias = reinterpret_cast<float*>(s_k + kMaxKSteps + 1);
+  float* s_scale = s_bias + kMaxN;
+  float* s_slope = s_scale + kMaxN;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_slope + kMaxN);
+  uint8_t* zero_b = reinterpret_cast<uint8_t*>(bars) + kStackZeroOff;
+
+  const uint32_t rank = cluster_rank();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (uint32_t j = threadIdx.x; j < kStackZeroBytes / 16; j += blockDim.x)
+    reinterpret_cast<uint4*>(zero_b)[j] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();  // the zero tile is read by the tensor core (async proxy)
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < a.ring; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&done[i], 1);
+    }
+    for (uint32_t i = 0; i < R; ++i) mbar_init(&slot_free[i], kEpiWarps);  // one group, both blocks
+    mbar_init(wbar, 1);
+    mbar_init(wpeer, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
+    s_bias[j] = j < kCoutPad ? a.bias[j] : 0.0f;
+    s_scale[j] = (a.chan_scale != nullptr && j < kCoutPad) ? a.chan_scale[j] : 1.0f;
+    s_slope[j] = (a.slope != nullptr && j < kCoutPad) ? a.slope[j] : 0.0f;
+  }
+  for (int j = threadIdx.x; j <= kMaxKSteps; j += blockDim.x)
+    s_k[j] = j < a.n_ksteps
+                 ? (static_cast<uint64_t>(a.ks[j].a_off >> 4) | (static_cast<uint64_t>(a.ks[j].lbo >> 4) << 16))
+                 : 0;
+  if (warp == 0 && lane == 0) prefetch_tmap(&maps.m[0]);
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, kStackTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  // both blocks' barriers are initialised before any remote arrive, pair copy or multicast commit
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint32_t half_w = a.wbytes / 2u;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ producer
+      mbar_arrive_expect_tx(wbar, half_w);
+      for (uint32_t off = 0; off < half_w; off += 32768u) {
+        const uint32_t len = half_w - off < 32768u ? half_w - off : 32768u;
+        bulk_load(sw + off, a.wpack + rank * half_w + off, len, wbar);
+      }
+      const uint32_t full0 = cluster_addr(smem_u32(full), 0);  // block 0's full[0]
+      RingPos in{0, 0};
+      bool ok = true;
+      for (uint32_t item = cluster_id_x(); item < static_cast<uint32_t>(a.items) && ok; item += cluster_count_x()) {
+        const int pair = static_cast<int>(item) % a.pairs;
+        const int t = static_cast<int>(item) / a.pairs;
+        const int band = t % a.bands;
+        const int n = t / a.bands;
+        const int y0 = band * a.band_rows;
+        const int y1 = min(a.H, y0 + a.band_rows);
+        const int x0 = (2 * pair + static_cast<int>(rank)) * a.strip_w;
+        for (int r = y0 - 1; r <= y1; ++r) {
+          if (!wait_bar(&done[in.idx], in.phase ^ 1u, a.err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[in.idx], 2u * a.slot_bytes);
+          // one box: 128 pixels from x0 - 1 (zero fill outside the image), all chunks
+          tma_load_4d_pair(ring + in.idx * a.slot_bytes, &maps.m[0], full0 + in.idx * 8u, (x0 - 1) * 2, 0, r, n);
+          in.advance(a.ring);
+        }
+      }
+      // every MMA (and so every copy it read) has completed before the pair may exit
+      wait_bar(drain, 0, a.err, kErrWaitDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      if (rank == 0) {
+        // ---------------------------------------------------------------- MMA issuer (pair)
+        if (wait_bar(wbar, 0, a.err, kErrWaitMma) && wait_bar(wpeer, 0, a.err, kErrWaitMma)) {
+          const PairIssue is{a, smem_u32(ring), smem_u32(sw), smem_u32(zero_b), tmem_base, s_k, full, done, slot_free};
+          switch (a.n_ksteps) {
+            case 9: pair_issue<kFp8, kCoutPad, 9>(is); break;
+            case 5: pair_issue<kFp8, kCoutPad, 5>(is); break;
+            default: pair_issue<kFp8, kCoutPad, 2>(is); break;  // the host admits 2, 5 or 9 K steps
+          }
+        }
+        mma_commit_pair(drain);
+      } else if (wait_bar(wbar, 0, a.err, kErrWaitMma)) {
+        mbar_arrive_remote(cluster_addr(smem_u32(wpeer), 0));  // block 1's half of B is in place
+      }
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------------------- epilogue
+    // Two groups of warps take alternate accumulator entries (group g: entries of parity g, so slots
+    // g, g + 2, g + 4), which puts two rows in the epilogue at once. A warp covers 32 lanes (pixels)
+    // x kEpiCols columns of its group's entries; its residual words are loaded before it waits.
+    constexpr int kGroupWarps = kEpiWarps / 2;
+    constexpr int kEpiCols = 2 * kStackEpiCols;
+    constexpr bool kResidual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
+    const int ew = warp - 2;
+    const uint32_t grp = static_cast<uint32_t>(ew / kGroupWarps);
+    const int quad = warp & 3;
+    const int col0 = ((ew % kGroupWarps) >> 2) * kEpiCols;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
+    const uint32_t free0 = cluster_addr(smem_u32(slot_free), 0);  // block 0's slot_free[0]
+    // the group's slots start free (phase 0 of slot_free)
+    if (lane == 0)
+      for (uint32_t s = grp; s < R; s += 2) mbar_arrive_remote_relaxed(free0 + s * 8u);
+    RingPos acc{0, 0};  // slot of the current entry
+    RingPos in{0, 0};   // input ring position of the row that completes output row y (y + 2 of the band)
+    uint32_t entry = 0;  // entry index (parity selects the group)
+    bool ok = true;
+    for (uint32_t item = cluster_id_x(); item < static_cast<uint32_t>(a.items) && ok; item += cluster_count_x()) {
+      const int pair = static_cast<int>(item) % a.pairs;
+      const int t = static_cast<int>(item) / a.pairs;
+      const int band = t % a.bands;
+      const int n = t / a.bands;
+      const int y0 = band * a.band_rows;
+      const int y1 = min(a.H, y0 + a.band_rows);
+      const int m = quad * 32 + lane;
+      const int x = (2 * pair + static_cast<int>(rank)) * a.strip_w + m;
+      const bool store = m < a.strip_w && x < a.W;
+      in.advance(a.ring);  // the band's input rows y0 - 1 and y0 complete no output row
+      in.advance(a.ring);
+      for (int y = y0; y < y1; ++y, acc.advance(R), in.advance(a.ring), ++entry) {
+        if ((entry & 1u) != grp) continue;
+        const uint32_t s = acc.idx;
+        uint32_t res[kEpiCols / 2];
+        if constexpr (kResidual) {
+          if (store) load_residual_words<kEpiCols>(a, n, y, x, col0, res);
+        }
+        const bool got = wait_bar(&done[in.idx], in.phase, a.err, kErrWaitEpilogue);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float v[kEpiCols];
+        tmem_ld16(my_cols + s * kCoutPad, v);
+        if (s < 2) {  // slots 0 and 1: the part of the sum that landed in block 6 or 7
+          float w[kEpiCols];
+          tmem_ld16(my_cols + (s + 6) * kCoutPad, w);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < kEpiCols; ++j) v[j] += w[j];
+        } else {
+          tmem_ld_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote_relaxed(free0 + s * 8u);
+        if (store)
+          epilogue_cols<kEpi, kOut, kEpiCols>(a, s_bias, s_scale, s_slope, v, col0, n, y, x, col0,
+                                              kResidual ? res : nullptr);
+      }
+      if (!ok) break;
+      // the band's two virtual entries (cleared by its input rows `rows` and `rows + 1`): nothing to
+      // read. The owning group frees each only after that input row is done, i.e. after the issuer
+      // took the slot for it: a release before that would complete a second phase of the slot's
+      // barrier and leave the issuer waiting on the wrong parity.
+      RingPos vin = in;  // input row rows + 2 of the band
+      vin.retreat(a.ring);
+      vin.retreat(a.ring);
+      for (int k = 0; k < 2; ++k, acc.advance(R), vin.advance(a.ring), ++entry) {
+        if ((entry & 1u) != grp) continue;
+        const bool got = wait_bar(&done[vin.idx], vin.phase, a.err, kErrWaitEpilogue);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) mbar_arrive_remote_relaxed(free0 + acc.idx * 8u);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no block leaves while the other's MMAs, copies or arrives may touch it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kStackTmemCols);
+  }
+}
+
+}  // namespace kb2

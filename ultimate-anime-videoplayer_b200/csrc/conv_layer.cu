@@ -6,7 +6,7 @@
 #include <array>
 #include <cstdio>
 
-#include "conv3s.cuh"
+#include "conv3p.cuh"
 #include "conv_layer.h"
 
 namespace kb2 {
@@ -54,9 +54,17 @@ template <bool F8, int N, int E, int O>
 void launch_stacked(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
   conv3s_kernel<F8, N, E, O><<<grid, StackShape<N>::threads, smem, s>>>(m, a);
 }
+template <bool F8, int N, int E, int O>
+void launch_paired(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
+  conv3p_kernel<F8, N, E, O><<<grid, StackShape<N>::threads, smem, s>>>(m, a);  // clusters of 2 (__cluster_dims__)
+}
+
+constexpr int kKindGeneric = 0, kKindStacked = 1, kKindPaired = 2;
+// 3x3 layers whose rows are 2, 5 or 9 K steps run on the pair kernel (conv3p.cuh)
+constexpr bool kPairedStack = true;
 
 struct KernelEntry {
-  bool stacked;  // 3x3 single-source layer on the stacked-kernel-row kernel (conv3s.cuh)
+  int kind;  // kKindGeneric: conv_tc.cuh; kKindStacked: conv3s.cuh; kKindPaired: conv3p.cuh
   bool fp8;
   int n, epi, out;
   LaunchFn launch;
@@ -64,15 +72,20 @@ struct KernelEntry {
   int threads;
 };
 
-#define KB2_KERNEL(F8, N, E, O)                                                                            \
-  KernelEntry {                                                                                            \
-    false, F8, N, E, O, &launch_impl<F8, N, E, O>, reinterpret_cast<const void*>(&conv_tc_kernel<F8, N, E, O>), \
-        ConvShape<N>::threads                                                                              \
+#define KB2_KERNEL(F8, N, E, O)                                                                          \
+  KernelEntry {                                                                                          \
+    kKindGeneric, F8, N, E, O, &launch_impl<F8, N, E, O>,                                                \
+        reinterpret_cast<const void*>(&conv_tc_kernel<F8, N, E, O>), ConvShape<N>::threads               \
   }
-#define KB2_STACKED(F8, N, E, O)                                                                              \
-  KernelEntry {                                                                                               \
-    true, F8, N, E, O, &launch_stacked<F8, N, E, O>, reinterpret_cast<const void*>(&conv3s_kernel<F8, N, E, O>), \
-        StackShape<N>::threads                                                                                \
+#define KB2_STACKED(F8, N, E, O)                                                                         \
+  KernelEntry {                                                                                          \
+    kKindStacked, F8, N, E, O, &launch_stacked<F8, N, E, O>,                                             \
+        reinterpret_cast<const void*>(&conv3s_kernel<F8, N, E, O>), StackShape<N>::threads               \
+  }
+#define KB2_PAIRED(F8, N, E, O)                                                                          \
+  KernelEntry {                                                                                          \
+    kKindPaired, F8, N, E, O, &launch_paired<F8, N, E, O>,                                               \
+        reinterpret_cast<const void*>(&conv3p_kernel<F8, N, E, O>), StackShape<N>::threads               \
   }
 
 // The instantiations the SPAN engines use: 3x3 layers on the stacked kernel, the 1x1 conv_cat on
@@ -88,14 +101,22 @@ const KernelEntry kKernels[] = {
     KB2_STACKED(true, 48, kEpiSilu, kOutF16E4m3),
     KB2_STACKED(true, 48, kEpiSpanAttn, kOutE4m3Chunk),
     KB2_STACKED(true, 48, kEpiSpanAttn, kOutF16Chunk),
+    KB2_PAIRED(false, 48, kEpiBias, kOutF16Chunk),
+    KB2_PAIRED(false, 48, kEpiSilu, kOutF16Chunk),
+    KB2_PAIRED(false, 48, kEpiSpanAttn, kOutF16Chunk),
+    KB2_PAIRED(false, 16, kEpiBias, kOutPixShuf2),
+    KB2_PAIRED(false, 48, kEpiSpanAttn, kOutF16E4m3),
+    KB2_PAIRED(true, 48, kEpiSilu, kOutE4m3Chunk),
+    KB2_PAIRED(true, 48, kEpiSilu, kOutF16E4m3),
+    KB2_PAIRED(true, 48, kEpiSpanAttn, kOutE4m3Chunk),
+    KB2_PAIRED(true, 48, kEpiSpanAttn, kOutF16Chunk),
 };
 
 bool wants_stacked(const ConvSpec& s) { return s.taps == 9 && s.n_sources == 1 && (s.n_pad == 48 || s.n_pad == 16); }
 
-const KernelEntry* find_kernel(const ConvSpec& s) {
-  const bool st = wants_stacked(s);
+const KernelEntry* find_kernel(const ConvSpec& s, int kind) {
   for (const KernelEntry& k : kKernels)
-    if (k.stacked == st && k.fp8 == s.fp8 && k.n == s.n_pad && k.epi == s.epi && k.out == s.out) return &k;
+    if (k.kind == kind && k.fp8 == s.fp8 && k.n == s.n_pad && k.epi == s.epi && k.out == s.out) return &k;
   return nullptr;
 }
 
@@ -125,7 +146,8 @@ int num_sms() {
 Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const float* prelu_slope,
                         const float* act_scales, const ChunkedTensor* const* inputs, int* err_word) {
   spec = s;
-  const KernelEntry* k = find_kernel(s);
+  kind = wants_stacked(s) ? kKindStacked : kKindGeneric;
+  const KernelEntry* k = find_kernel(s, kind);
   if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this layer shape");
   const ChunkedTensor& in0 = *inputs[0];
   for (int i = 0; i < s.n_sources; ++i) {
@@ -138,7 +160,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   const int halo = s.taps == 9 ? 1 : 0;
   if (chunks * epc < s.cin) return refuse(KB2_INPUT_MISMATCH, "input tensor narrower than the conv");
 
-  const bool stacked = k->stacked;
+  const bool stacked = kind != kKindGeneric;
   auto steps = make_ksteps(s, chunks);
   if (stacked) {
     // one input row per instruction group: the dy = 0 steps (every dy uses the same pixel shifts
@@ -147,7 +169,15 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     for (const auto& st : steps)
       if (st[0].dy == 0) row_steps.push_back(st);
     steps = row_steps;
+    // rows of 2, 5 or 9 K steps run on the pair kernel (one MMA for two SMs)
+    const int nk = static_cast<int>(steps.size());
+    const KernelEntry* kp = find_kernel(s, kKindPaired);
+    if (kPairedStack && kp != nullptr && (nk == 2 || nk == 5 || nk == 9)) {
+      kind = kKindPaired;
+      k = kp;
+    }
   }
+  const bool paired = kind == kKindPaired;
   if (static_cast<int>(steps.size()) > kMaxKSteps) return refuse(KB2_FORMAT_UNSUPPORTED, "too many K steps");
   // the row slot is one 128-pixel TMA box starting at x0 - halo; an A tile shifted by dx reads slot
   // pixels m + halo + dx (+1 for the second half of a zero-partnered step) for MMA row m, so the
@@ -255,8 +285,13 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
             const int kx = s.taps == 9 ? hf.dx + 1 : 0;
             v = w_at(co, hf.src * s.cin + ci, ky, kx);
           }
-          uint8_t* dst = packed.data() + j * step_bytes + static_cast<size_t>(h) * n_rows_b * 16 +
-                         static_cast<size_t>(row) * 16;
+          // paired kernel: block r of the pair holds B rows [r N/2, (r + 1) N/2) of every step
+          const int half_rows = n_rows_b / 2;
+          uint8_t* dst = paired ? packed.data() + static_cast<size_t>(row / half_rows) * (packed.size() / 2) +
+                                      j * (step_bytes / 2) + static_cast<size_t>(h) * half_rows * 16 +
+                                      static_cast<size_t>(row % half_rows) * 16
+                                : packed.data() + j * step_bytes + static_cast<size_t>(h) * n_rows_b * 16 +
+                                      static_cast<size_t>(row) * 16;
           if (s.fp8) {
             dst[e] = e4m3_encode(v * src_scale(hf.src) / wscale[co]);
           } else {
@@ -284,7 +319,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   }
   a.wpack = wpack.as<uint8_t>();
   a.wbytes = static_cast<uint32_t>(packed.size());
-  a.w_smem = (a.wbytes + 1023u) / 1024u * 1024u;
+  a.w_smem = ((paired ? a.wbytes / 2u : a.wbytes) + 1023u) / 1024u * 1024u;
   a.bias = bias.as<float>();
   a.slope = slope.as<float>();
   a.chan_scale = s.fp8 ? scale.as<float>() : nullptr;
@@ -311,6 +346,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     int ring = one_per_sm ? fit(200u * 1024u) : fit((228u * 1024u) / 2 - 2048u);
     if (!one_per_sm && !stacked && ring < min_ring + 2) ring = fit(227u * 1024u);  // wide slots: one block per SM
     ring = std::min(ring, 12);
+    if (paired) ring = 12;  // the pair issuer runs 12-row periods (checked against shared memory below)
     a.ring = static_cast<uint32_t>(std::max(ring, min_ring));
   }
   smem = a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (stacked ? kStackSmemExtra : kConvSmemExtra);
@@ -333,27 +369,43 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   const int tmem_fit = a.tmem_a ? 1 : (stacked ? kStackBlocksPerSm : static_cast<int>(512u / tmem_cols(s.n_pad)));
   per_sm = std::min({per_sm, smem_fit, tmem_fit});
   if (per_sm < 1) per_sm = 1;
-  const int slots = num_sms() * per_sm;
-  // bands: about 16 work items per resident block, 4..64 rows each (8.. for the stacked kernel,
-  // whose two halo rows per band are extra MMA work)
-  const long long rows_total = static_cast<long long>(a.batch) * a.H * a.strips;
+  int slots = num_sms() * per_sm;
+  a.pairs = (a.strips + 1) / 2;
+  if (paired) {
+    // resident pairs: clusters need both SMs of a pair free, so ask the runtime instead of
+    // halving the SM count
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * (num_sms() / 2)));
+    cfg.blockDim = dim3(static_cast<unsigned>(k->threads));
+    cfg.dynamicSmemBytes = smem;
+    int clusters = 0;
+    KB2_CUDA(cudaOccupancyMaxActiveClusters(&clusters, k->fn, &cfg));
+    if (clusters < 1) return refuse(KB2_FORMAT_UNSUPPORTED, "paired layer: no cluster of two fits");
+    slots = clusters;
+  }
+  const int units = paired ? a.pairs : a.strips;  // work units across a row band
+  // bands: about 16 work items per resident block (pair), 4..64 rows each (8.. for the stacked
+  // kernels, whose two halo rows per band are extra MMA work)
+  const long long rows_total = static_cast<long long>(a.batch) * a.H * units;
   int band = static_cast<int>(rows_total / (16LL * slots));
   const int band_min = stacked ? 8 : 4;
   band = band < band_min ? band_min : (band > 64 ? 64 : band);
   a.band_rows = band;
   a.bands = (a.H + band - 1) / band;
-  a.items = a.batch * a.bands * a.strips;
+  a.items = a.batch * a.bands * units;
   grid = a.items < slots ? a.items : slots;
+  if (paired) grid *= 2;  // two blocks per item
   return Status::Ok();
 }
 
 Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
                          float res_scale, void* out2, int res_chunks) const {
-  const KernelEntry* k = find_kernel(spec);
+  const KernelEntry* k = find_kernel(spec, kind);
   if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no kernel");
+  const bool paired = kind == kKindPaired;
   ConvArgs a = args;
   a.batch = batch;
-  a.items = batch * a.bands * a.strips;
+  a.items = batch * a.bands * (paired ? a.pairs : a.strips);
   a.out = static_cast<uint8_t*>(out);
   a.out2 = static_cast<uint8_t*>(out2);
   a.residual = static_cast<const uint8_t*>(residual);
@@ -361,7 +413,8 @@ Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* 
   a.res_chunks = res_chunks;
   a.out_inv_scale = out_inv_scale;
   a.res_scale = res_scale;
-  const int g = a.items < grid ? a.items : grid;
+  const int per_item = paired ? 2 : 1;
+  const int g = a.items * per_item < grid ? a.items * per_item : grid;
   k->launch(dim3(static_cast<unsigned>(g)), smem, stream, maps, a);
   return cuda_status(cudaGetLastError(), "conv_tc_kernel launch");
 }

@@ -71,6 +71,7 @@ struct KStep {
 struct ConvArgs {
   int batch, H, W;  // output rows / columns (input has the same size: stride 1)
   int strips, bands, band_rows, items;
+  int pairs;  // paired stacked kernel (conv3p.cuh): strip pairs per row band
   int strip_w;  // output pixels per strip (128 minus the pixels the shifted A tiles read past the slot)
   int n_sources, chunks, px, halo, in_rows, row_off;
   uint32_t src_bytes, slot_bytes, ring, w_smem;
@@ -116,10 +117,36 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // Epilogue of kCols accumulator columns [col0, col0 + kCols) of one pixel, in groups of 8 columns.
 // Per-channel constants are read at kc0 + j; the output channel of column j is col0 + j (col0
 // defaults to kc0; a caller holding its constants in a register array passes kc0 = 0).
+// The residual words of kCols channels [col0, col0 + kCols) of one pixel (same pixel and channels as
+// the output, in the block input's format): 4 words per 8 channels for FP16, 2 for E4M3. Loaded
+// ahead of the accumulator wait by the paired kernel, so the load latency hides behind the wait.
+template <int kCols>
+__device__ __forceinline__ void load_residual_words(const ConvArgs& a, int n, int y, int x, int col0,
+                                                    uint32_t (&w)[kCols / 2]) {
+  const size_t pix_row = static_cast<size_t>(n) * a.H + y;
+#pragma unroll
+  for (int g = 0; g < kCols / 8; ++g) {
+    const int c = col0 + 8 * g;
+    if (a.res_fp8) {
+      const uint2 q = __ldg(reinterpret_cast<const uint2*>(
+          a.residual + ((pix_row * a.res_chunks + c / 16) * a.W + x) * 16 + (c % 16)));
+      w[4 * g] = q.x;
+      w[4 * g + 1] = q.y;
+    } else {
+      const uint4 q =
+          __ldg(reinterpret_cast<const uint4*>(a.residual + ((pix_row * a.res_chunks + c / 8) * a.W + x) * 16));
+      w[4 * g] = q.x;
+      w[4 * g + 1] = q.y;
+      w[4 * g + 2] = q.z;
+      w[4 * g + 3] = q.w;
+    }
+  }
+}
+
 template <int kEpi, int kOut, int kCols>
 __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_bias, const float* s_scale,
                                               const float* s_slope, float* v, int kc0, int n, int y, int x,
-                                              int col0_override = -1) {
+                                              int col0_override = -1, const uint32_t* res_pre = nullptr) {
   const int col0 = col0_override >= 0 ? col0_override : kc0;
   const size_t pix_row = static_cast<size_t>(n) * a.H + y;
 #pragma unroll
@@ -137,8 +164,10 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
       const int c = col0 + 8 * g;
       float r[8];
       if (a.res_fp8) {
-        const uint2 q = __ldg(reinterpret_cast<const uint2*>(
-            a.residual + ((pix_row * a.res_chunks + c / 16) * a.W + x) * 16 + (c % 16)));
+        const uint2 q = res_pre != nullptr ? make_uint2(res_pre[4 * g], res_pre[4 * g + 1])
+                                           : __ldg(reinterpret_cast<const uint2*>(
+                                                 a.residual + ((pix_row * a.res_chunks + c / 16) * a.W + x) * 16 +
+                                                 (c % 16)));
         const uint32_t w2[2] = {q.x, q.y};
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
@@ -150,8 +179,10 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
           r[4 * k + 3] = hi.y * a.res_scale;
         }
       } else {
-        const uint4 q = __ldg(
-            reinterpret_cast<const uint4*>(a.residual + ((pix_row * a.res_chunks + c / 8) * a.W + x) * 16));
+        const uint4 q = res_pre != nullptr
+                            ? make_uint4(res_pre[4 * g], res_pre[4 * g + 1], res_pre[4 * g + 2], res_pre[4 * g + 3])
+                            : __ldg(reinterpret_cast<const uint4*>(
+                                  a.residual + ((pix_row * a.res_chunks + c / 8) * a.W + x) * 16));
         const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {

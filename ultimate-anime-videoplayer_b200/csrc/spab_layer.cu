@@ -20,6 +20,8 @@ Status SpabLayer::build(const ConvLayer& c1, const ConvLayer& c2, const ConvLaye
   for (const ConvLayer* c : cs) {
     if (!c->spec.fp8 || c->spec.taps != 9 || c->spec.n_pad != 48 || c->spec.n_sources != 1)
       return refuse(KB2_FORMAT_UNSUPPORTED, "fused SPAB: E4M3 3x3 48-channel layers only");
+    if (c->kind != 1)  // the fused kernel reads the single-SM stacked packing of B
+      return refuse(KB2_FORMAT_UNSUPPORTED, "fused SPAB: layers packed for the pair kernel");
     if (c->args.n_ksteps != c1.args.n_ksteps || c->args.wbytes != c1.args.wbytes)
       return refuse(KB2_FORMAT_UNSUPPORTED, "fused SPAB: layers of different shapes");
     for (int j = 0; j < c1.args.n_ksteps; ++j)
