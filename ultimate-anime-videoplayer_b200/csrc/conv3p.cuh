@@ -111,7 +111,7 @@ template <bool kFp8, int kNK, int kClears>
 __device__ __forceinline__ uint32_t pair_row_head(
     uint32_t d_clear, uint32_t d_clear2, uint64_t zero_desc, uint32_t id_clear, uint32_t d_win, uint32_t idesc,
     uint32_t nf, uint32_t nf_par, uint32_t ns, uint32_t ns_par, const uint64_t (&a)[9], const uint64_t (&b)[9]) {
-  static_assert(kNK == 2 || kNK == 5 || kNK == 9, "rows of 2, 5 or 9 K steps");
+  static_assert(kNK == 2 || kNK == 3 || kNK == 5 || kNK == 9, "rows of 2, 3, 5 or 9 K steps");
   static_assert(kClears == 1 || kClears == 2, "one or two cleared blocks");
   uint32_t ok;
   if constexpr (kFp8 == false && kNK == 2 && kClears == 1) {
@@ -150,6 +150,45 @@ __device__ __forceinline__ uint32_t pair_row_head(
             "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
             "l"(a[0]),
             "l"(b[0])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 3 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %13, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %14, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]),
+            "l"(b[0]), "l"(b[1])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 3 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %13, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %14, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]),
+            "l"(b[0]), "l"(b[1])
           : "memory");
   } else if constexpr (kFp8 == false && kNK == 5 && kClears == 1) {
     asm volatile(
@@ -274,6 +313,45 @@ __device__ __forceinline__ uint32_t pair_row_head(
             "l"(a[0]),
             "l"(b[0])
           : "memory");
+  } else if constexpr (kFp8 == true && kNK == 3 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %13, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %14, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]),
+            "l"(b[0]), "l"(b[1])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 3 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %13, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %14, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]),
+            "l"(b[0]), "l"(b[1])
+          : "memory");
   } else if constexpr (kFp8 == true && kNK == 5 && kClears == 1) {
     asm volatile(
           "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
@@ -377,6 +455,16 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
             "l"(a[1]),
             "l"(b[1])
           : "memory");
+  } else if constexpr (kFp8 == false && kNK == 3) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %5, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[2]),
+            "l"(b[2])
+          : "memory");
   } else if constexpr (kFp8 == false && kNK == 5) {
     asm volatile(
           "{\n\t.reg .pred acc;\n\t"
@@ -411,6 +499,16 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
             "l"(a[1]),
             "l"(b[1])
           : "memory");
+  } else if constexpr (kFp8 == true && kNK == 3) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %4, %5, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[2]),
+            "l"(b[2])
+          : "memory");
   } else if constexpr (kFp8 == true && kNK == 5) {
     asm volatile(
           "{\n\t.reg .pred acc;\n\t"
@@ -437,6 +535,7 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
           : "memory");
   }
 }
+
 struct PairIssue {
   const ConvArgs& a;
   uint32_t ring_base, w_base, zero_base, tmem_base;
@@ -675,7 +774,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
           switch (a.n_ksteps) {
             case 9: pair_issue<kFp8, kCoutPad, 9>(is); break;
             case 5: pair_issue<kFp8, kCoutPad, 5>(is); break;
-            default: pair_issue<kFp8, kCoutPad, 2>(is); break;  // the host admits 2, 5 or 9 K steps
+            case 3: pair_issue<kFp8, kCoutPad, 3>(is); break;
+            default: pair_issue<kFp8, kCoutPad, 2>(is); break;  // the host admits 2, 3, 5 or 9 K steps
           }
         }
         mma_commit_pair(drain);

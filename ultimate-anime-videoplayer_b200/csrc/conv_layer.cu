@@ -60,7 +60,7 @@ void launch_paired(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, co
 }
 
 constexpr int kKindGeneric = 0, kKindStacked = 1, kKindPaired = 2;
-// 3x3 layers whose rows are 2, 5 or 9 K steps run on the pair kernel (conv3p.cuh)
+// 3x3 layers whose rows are 2, 3, 5 or 9 K steps run on the pair kernel (conv3p.cuh)
 constexpr bool kPairedStack = true;
 
 struct KernelEntry {
@@ -169,10 +169,10 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     for (const auto& st : steps)
       if (st[0].dy == 0) row_steps.push_back(st);
     steps = row_steps;
-    // rows of 2, 5 or 9 K steps run on the pair kernel (one MMA for two SMs)
+    // rows of 2, 3, 5 or 9 K steps run on the pair kernel (one MMA for two SMs)
     const int nk = static_cast<int>(steps.size());
     const KernelEntry* kp = find_kernel(s, kKindPaired);
-    if (kPairedStack && kp != nullptr && (nk == 2 || nk == 5 || nk == 9)) {
+    if (kPairedStack && kp != nullptr && (nk == 2 || nk == 3 || nk == 5 || nk == 9)) {
       kind = kKindPaired;
       k = kp;
     }
