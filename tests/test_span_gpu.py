@@ -117,6 +117,41 @@ def test_fp8_calibrated_psnr():
     assert db >= FP8_MIN_PSNR, f"FP8 PSNR {db:.2f} dB"
 
 
+def live_params(gain=1.2):
+    """The seeded SPAN with its block conv weights scaled by `gain`: at 1.0 the deep blocks'
+    activations decay towards zero (their peaks fall below 1e-5 by block 4), so an E4M3 error there
+    cannot show in the output; at 1.2 every block stays live (peaks 3-10 through block 5)."""
+    p = nets.span_init(1)
+    for k in p:
+        if k.startswith("block") and not k.endswith(".b"):
+            p[k] = p[k] * gain
+    return p
+
+
+def test_fp8_live_blocks_psnr():
+    """FP8 bar on a network whose E4M3 blocks all carry signal, plus FP16 parity on it."""
+    import torch
+    from synth import anime_frames
+    h, w = 48, 160
+    p = live_params()
+    blob = kb.make_blob(kb.MODEL_SPAN_X2, nets.span_flat(p))
+    calib = anime_frames(16, h, w, seed=100)
+    eng16 = kb.Engine(kb.MODEL_SPAN_X2, blob, h, w, max_batch=8)
+    peaks = eng16.calibrate(torch.from_numpy(calib.astype(np.float16)).cuda())
+    eng16.close()
+    assert min(peaks[:19]) > 1.0, "every calibrated tensor should be live"
+    scales = nets.span_scales_from_peaks(peaks, floor=2.0 ** -14)
+    x = f16(anime_frames(2, h, w, seed=7))
+    ref = nets.span_forward(x, p)
+    out8 = run_span(x, p, precision=kb.PREC_FP8, act_scales=scales)
+    assert np.isfinite(out8).all()
+    db = nets.psnr(out8, ref)
+    assert db >= FP8_MIN_PSNR, f"FP8 PSNR {db:.2f} dB"
+    out16 = run_span(x, p)
+    err = nets.max_abs_clamped(out16, ref)
+    assert err <= FP16_MAX_ABS, f"max-abs {err * 255:.3f}/255"
+
+
 def test_enqueue_refusals():
     import torch
     p = nets.span_init(1)
