@@ -799,6 +799,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
     const uint32_t free0 = cluster_addr(smem_u32(slot_free), 0);  // block 0's slot_free[0]
+    // FP16 layers: this warp's biases in registers and no channel scale (re-reading both from shared
+    // memory on every row measured 5-15 % slower); E4M3 layers read bias and scale from shared
+    // memory (in registers they spill)
+    float r_bias[kEpiCols], r_scale[kEpiCols];
+#pragma unroll
+    for (int j = 0; j < kEpiCols; ++j) {
+      r_bias[j] = kFp8 ? 0.0f : s_bias[col0 + j];
+      r_scale[j] = 1.0f;
+    }
+    const float* e_bias = kFp8 ? s_bias + col0 : r_bias;
+    const float* e_scale = kFp8 ? s_scale + col0 : r_scale;
     // the group's slots start free (phase 0 of slot_free)
     if (lane == 0)
       for (uint32_t s = grp; s < R; s += 2) mbar_arrive_remote_relaxed(free0 + s * 8u);
@@ -846,7 +857,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
         __syncwarp();
         if (lane == 0) mbar_arrive_remote_relaxed(free0 + s * 8u);
         if (store)
-          epilogue_cols<kEpi, kOut, kEpiCols>(a, s_bias, s_scale, s_slope, v, col0, n, y, x, col0,
+          epilogue_cols<kEpi, kOut, kEpiCols>(a, e_bias, e_scale, s_slope + col0, v, 0, n, y, x, col0,
                                               kResidual ? res : nullptr);
       }
       if (!ok) break;
