@@ -38,6 +38,25 @@ namespace kb2 {
 
 constexpr uint16_t kPairMask = 3;  // both blocks of the cluster
 
+// Epilogue shape of the pair kernel: `groups` groups of warps take the accumulator entries in turn
+// (entry e goes to group e % groups, so a group owns the slots s with s % groups = g and that many
+// rows are in the epilogue at once); a warp covers 32 pixels x warp_cols channels. Measured on
+// 8 x 1080p (in-process A/B): without a residual, 3 groups of 4 warps x 48 channels beat 2 groups of
+// 12 warps x 16 channels by 5-18 % (fewer epilogue warps disturb the MMA issuer less); the SPAB gate
+// layers, which also hold the residual words, are 20-30 % slower that way and keep 2 x 12 x 16.
+template <int kCoutPad, int kEpi>
+struct PairShape {
+  static constexpr bool residual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
+  static constexpr int groups = residual ? 2 : 3;
+  static constexpr int cols = residual ? 16 : 48;
+  static_assert(kStackSlots % groups == 0, "groups divide the accumulator slots");
+  static constexpr int warp_cols = kCoutPad < cols ? kCoutPad : cols;
+  static_assert(warp_cols % 16 == 0 && kCoutPad % warp_cols == 0, "16-column TMEM loads per warp");
+  static constexpr int group_warps = 4 * (kCoutPad / warp_cols);
+  static constexpr int epi_warps = groups * group_warps;
+  static constexpr int threads = 64 + 32 * epi_warps;
+};
+
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -670,10 +689,10 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
 }
 
 template <bool kFp8, int kCoutPad, int kEpi, int kOut>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>::threads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, kEpi>::threads, 1)
     conv3p_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
   static_assert(kCoutPad == 16 || kCoutPad == 48, "paired kernel: 16 or 48 output channels");
-  constexpr int kEpiWarps = StackShape<kCoutPad>::epi_warps;
+  constexpr int kGroupWarps = PairShape<kCoutPad, kEpi>::group_warps;
   constexpr uint32_t R = kStackSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -704,7 +723,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
       mbar_init(&full[i], 1);
       mbar_init(&done[i], 1);
     }
-    for (uint32_t i = 0; i < R; ++i) mbar_init(&slot_free[i], kEpiWarps);  // one group, both blocks
+    for (uint32_t i = 0; i < R; ++i) mbar_init(&slot_free[i], 2 * kGroupWarps);  // one group, both blocks
     mbar_init(wbar, 1);
     mbar_init(wpeer, 1);
     mbar_init(drain, 1);
@@ -786,25 +805,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
     __syncwarp();
   } else {
     // -------------------------------------------------------------------- epilogue
-    // Two groups of warps take alternate accumulator entries (group g: entries of parity g, so slots
-    // g, g + 2, g + 4), which puts two rows in the epilogue at once. A warp covers 32 lanes (pixels)
-    // x kEpiCols columns of its group's entries; its residual words are loaded before it waits.
-    constexpr int kGroupWarps = kEpiWarps / 2;
-    constexpr int kEpiCols = 2 * kStackEpiCols;
+    // The groups of warps take the accumulator entries in turn (PairShape), so that many
+    // rows are in the epilogue at once. A warp covers 32 lanes (pixels) x kCols columns of its
+    // group's entries in 16-column steps; its residual words are loaded before it waits.
+    constexpr int kCols = PairShape<kCoutPad, kEpi>::warp_cols;
+    constexpr int kSteps = kCols / 16;
+    constexpr uint32_t kG = static_cast<uint32_t>(PairShape<kCoutPad, kEpi>::groups);
     constexpr bool kResidual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
     const int ew = warp - 2;
     const uint32_t grp = static_cast<uint32_t>(ew / kGroupWarps);
     const int quad = warp & 3;
-    const int col0 = ((ew % kGroupWarps) >> 2) * kEpiCols;
+    const int col0 = ((ew % kGroupWarps) >> 2) * kCols;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
     const uint32_t free0 = cluster_addr(smem_u32(slot_free), 0);  // block 0's slot_free[0]
     // FP16 layers: this warp's biases in registers and no channel scale (re-reading both from shared
     // memory on every row measured 5-15 % slower); E4M3 layers read bias and scale from shared
     // memory (in registers they spill)
-    float r_bias[kEpiCols], r_scale[kEpiCols];
+    float r_bias[kCols], r_scale[kCols];
 #pragma unroll
-    for (int j = 0; j < kEpiCols; ++j) {
+    for (int j = 0; j < kCols; ++j) {
       r_bias[j] = kFp8 ? 0.0f : s_bias[col0 + j];
       r_scale[j] = 1.0f;
     }
@@ -812,10 +832,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
     const float* e_scale = kFp8 ? s_scale + col0 : r_scale;
     // the group's slots start free (phase 0 of slot_free)
     if (lane == 0)
-      for (uint32_t s = grp; s < R; s += 2) mbar_arrive_remote_relaxed(free0 + s * 8u);
+      for (uint32_t s = grp; s < R; s += kG) mbar_arrive_remote_relaxed(free0 + s * 8u);
     RingPos acc{0, 0};  // slot of the current entry
     RingPos in{0, 0};   // input ring position of the row that completes output row y (y + 2 of the band)
-    uint32_t entry = 0;  // entry index (parity selects the group)
+    uint32_t eg = 0;     // entry index modulo the group count
     bool ok = true;
     for (uint32_t item = cluster_id_x(); item < static_cast<uint32_t>(a.items) && ok; item += cluster_count_x()) {
       const int pair = static_cast<int>(item) % a.pairs;
@@ -829,12 +849,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
       const bool store = m < a.strip_w && x < a.W;
       in.advance(a.ring);  // the band's input rows y0 - 1 and y0 complete no output row
       in.advance(a.ring);
-      for (int y = y0; y < y1; ++y, acc.advance(R), in.advance(a.ring), ++entry) {
-        if ((entry & 1u) != grp) continue;
+      for (int y = y0; y < y1; ++y, acc.advance(R), in.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1) {
+        if (eg != grp) continue;
         const uint32_t s = acc.idx;
-        uint32_t res[kEpiCols / 2];
+        uint32_t res[kCols / 2];
         if constexpr (kResidual) {
-          if (store) load_residual_words<kEpiCols>(a, n, y, x, col0, res);
+          if (store) load_residual_words<kCols>(a, n, y, x, col0, res);
         }
         const bool got = wait_bar(&done[in.idx], in.phase, a.err, kErrWaitEpilogue);
         if (!__all_sync(0xffffffffu, got)) {
@@ -842,14 +862,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
           break;
         }
         tc_fence_after();
-        float v[kEpiCols];
-        tmem_ld16(my_cols + s * kCoutPad, v);
+        float v[kCols];
+#pragma unroll
+        for (int k = 0; k < kSteps; ++k) tmem_ld16(my_cols + s * kCoutPad + 16u * k, v + 16 * k);
         if (s < 2) {  // slots 0 and 1: the part of the sum that landed in block 6 or 7
-          float w[kEpiCols];
-          tmem_ld16(my_cols + (s + 6) * kCoutPad, w);
+          float w[kCols];
+#pragma unroll
+          for (int k = 0; k < kSteps; ++k) tmem_ld16(my_cols + (s + 6) * kCoutPad + 16u * k, w + 16 * k);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < kEpiCols; ++j) v[j] += w[j];
+          for (int j = 0; j < kCols; ++j) v[j] += w[j];
         } else {
           tmem_ld_wait();
         }
@@ -857,8 +879,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
         __syncwarp();
         if (lane == 0) mbar_arrive_remote_relaxed(free0 + s * 8u);
         if (store)
-          epilogue_cols<kEpi, kOut, kEpiCols>(a, e_bias, e_scale, s_slope + col0, v, 0, n, y, x, col0,
-                                              kResidual ? res : nullptr);
+          epilogue_cols<kEpi, kOut, kCols>(a, e_bias, e_scale, s_slope + col0, v, 0, n, y, x, col0,
+                                           kResidual ? res : nullptr);
       }
       if (!ok) break;
       // the band's two virtual entries (cleared by its input rows `rows` and `rows + 1`): nothing to
@@ -868,8 +890,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(StackShape<kCoutPad>
       RingPos vin = in;  // input row rows + 2 of the band
       vin.retreat(a.ring);
       vin.retreat(a.ring);
-      for (int k = 0; k < 2; ++k, acc.advance(R), vin.advance(a.ring), ++entry) {
-        if ((entry & 1u) != grp) continue;
+      for (int k = 0; k < 2; ++k, acc.advance(R), vin.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1) {
+        if (eg != grp) continue;
         const bool got = wait_bar(&done[vin.idx], vin.phase, a.err, kErrWaitEpilogue);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;

@@ -56,7 +56,7 @@ void launch_stacked(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, c
 }
 template <bool F8, int N, int E, int O>
 void launch_paired(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
-  conv3p_kernel<F8, N, E, O><<<grid, StackShape<N>::threads, smem, s>>>(m, a);  // clusters of 2 (__cluster_dims__)
+  conv3p_kernel<F8, N, E, O><<<grid, PairShape<N, E>::threads, smem, s>>>(m, a);  // clusters of 2 (__cluster_dims__)
 }
 
 constexpr int kKindGeneric = 0, kKindStacked = 1, kKindPaired = 2;
@@ -85,7 +85,7 @@ struct KernelEntry {
 #define KB2_PAIRED(F8, N, E, O)                                                                          \
   KernelEntry {                                                                                          \
     kKindPaired, F8, N, E, O, &launch_paired<F8, N, E, O>,                                               \
-        reinterpret_cast<const void*>(&conv3p_kernel<F8, N, E, O>), StackShape<N>::threads               \
+        reinterpret_cast<const void*>(&conv3p_kernel<F8, N, E, O>), PairShape<N, E>::threads             \
   }
 
 // The instantiations the SPAN engines use: 3x3 layers on the stacked kernel, the 1x1 conv_cat on
