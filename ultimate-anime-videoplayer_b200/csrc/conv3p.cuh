@@ -7,7 +7,7 @@
 // M = 256 MMA (cta_group::2) runs at the same ~72 cycles per instruction (N = 144, measured) but
 // feeds both SMs of the pair: the issue cost per output pixel halves.
 //
-// Layout of the pair: block r of the cluster owns strip 2p + r of a (frame, band, strip pair) item.
+// Layout of the pair: block r of the cluster owns strip 2p + r of its (frame, strip pair) row segments.
 //  * A (the input row) is split by rows of M: each block copies its own strip's row into its own
 //    ring slot, at the same shared-memory offset in both blocks;
 //  * B (the stacked weights, N = 3 x 48 rows per K step) is split by rows of N: block 0 holds rows
@@ -555,6 +555,43 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
   }
 }
 
+// Work split: the output rows of a launch form one row space, unit after unit (unit = frame x strip
+// pair, H rows each); cluster c of nc owns the contiguous range [T c / nc, T (c + 1) / nc) of its T
+// rows, each end rounded down to a multiple of 6 rows within its unit, and walks it as segments
+// inside one unit. A segment of `rows` output rows is issued as rows + 2 + pad input rows and
+// entries (uniform rows; the 2 + pad last entries are virtual), pad making the count a multiple of
+// the 6 accumulator slots. So every segment starts at slot 0 on a row y = 0 mod 6, output row y
+// always lands in slot y mod 6, and the split of its sum between TMEM blocks (slots 0 and 1 use two)
+// is the same whatever the batch and the split: results do not depend on them.
+__device__ __forceinline__ int pair_pad(int rows) { return (6 - (rows + 2) % 6) % 6; }
+
+struct PairSpan {
+  long long r, end;
+  __device__ __forceinline__ static long long align6(const ConvArgs& a, long long b) {
+    const long long u = b / a.H;
+    const long long y = b - u * a.H;
+    return u * a.H + (y - y % 6);
+  }
+  __device__ __forceinline__ PairSpan(const ConvArgs& a, uint32_t c, uint32_t nc) {
+    const long long total = static_cast<long long>(a.batch) * a.pairs * a.H;
+    r = align6(a, total * c / nc);
+    end = c + 1 == nc ? total : align6(a, total * (c + 1) / nc);
+  }
+  // the next segment: frame n, strip pair `pair`, output rows [y0, y1); false when the range is done
+  __device__ __forceinline__ bool next(const ConvArgs& a, int& n, int& pair, int& y0, int& y1) {
+    if (r >= end) return false;
+    const long long u = r / a.H;
+    const long long unit_end = (u + 1) * a.H;
+    const long long stop = end < unit_end ? end : unit_end;
+    y0 = static_cast<int>(r - u * a.H);
+    y1 = static_cast<int>(stop - u * a.H);
+    n = static_cast<int>(u / a.pairs);
+    pair = static_cast<int>(u % a.pairs);
+    r = stop;
+    return true;
+  }
+};
+
 struct PairIssue {
   const ConvArgs& a;
   uint32_t ring_base, w_base, zero_base, tmem_base;
@@ -643,12 +680,12 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
   c.full = is.full;
   c.slot_free = is.slot_free;
   c.err = a.err;
-  // input rows of this cluster's items: rows + 2 per band
+  // input rows of this cluster's segments: rows + 2 each
   uint32_t total = 0;
-  for (uint32_t item = cluster_id_x(); item < static_cast<uint32_t>(a.items); item += cluster_count_x()) {
-    const int band = (static_cast<int>(item) / a.pairs) % a.bands;
-    const int y0 = band * a.band_rows;
-    total += static_cast<uint32_t>(min(a.H, y0 + a.band_rows) - y0 + 2);
+  {
+    PairSpan sp(a, cluster_id_x(), cluster_count_x());
+    int n, pair, y0, y1;
+    while (sp.next(a, n, pair, y0, y1)) total += static_cast<uint32_t>(y1 - y0 + 2 + pair_pad(y1 - y0));
   }
   if (a.ring != 12u) return;  // the host sizes every paired ring to 12 slots
   uint32_t ph = 0;   // input ring phase of the current period
@@ -762,15 +799,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
       const uint32_t full0 = cluster_addr(smem_u32(full), 0);  // block 0's full[0]
       RingPos in{0, 0};
       bool ok = true;
-      for (uint32_t item = cluster_id_x(); item < static_cast<uint32_t>(a.items) && ok; item += cluster_count_x()) {
-        const int pair = static_cast<int>(item) % a.pairs;
-        const int t = static_cast<int>(item) / a.pairs;
-        const int band = t % a.bands;
-        const int n = t / a.bands;
-        const int y0 = band * a.band_rows;
-        const int y1 = min(a.H, y0 + a.band_rows);
+      PairSpan sp(a, cluster_id_x(), cluster_count_x());
+      int n, pair, y0, y1;
+      while (ok && sp.next(a, n, pair, y0, y1)) {
         const int x0 = (2 * pair + static_cast<int>(rank)) * a.strip_w;
-        for (int r = y0 - 1; r <= y1; ++r) {
+        const int last = y1 + pair_pad(y1 - y0);  // rows past y1: the padding entries' inputs
+        for (int r = y0 - 1; r <= last; ++r) {
           if (!wait_bar(&done[in.idx], in.phase ^ 1u, a.err, kErrWaitProducer)) {
             ok = false;
             break;
@@ -837,13 +871,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
     RingPos in{0, 0};   // input ring position of the row that completes output row y (y + 2 of the band)
     uint32_t eg = 0;     // entry index modulo the group count
     bool ok = true;
-    for (uint32_t item = cluster_id_x(); item < static_cast<uint32_t>(a.items) && ok; item += cluster_count_x()) {
-      const int pair = static_cast<int>(item) % a.pairs;
-      const int t = static_cast<int>(item) / a.pairs;
-      const int band = t % a.bands;
-      const int n = t / a.bands;
-      const int y0 = band * a.band_rows;
-      const int y1 = min(a.H, y0 + a.band_rows);
+    PairSpan sp(a, cluster_id_x(), cluster_count_x());
+    int n, pair, y0, y1;
+    while (ok && sp.next(a, n, pair, y0, y1)) {
       const int m = quad * 32 + lane;
       const int x = (2 * pair + static_cast<int>(rank)) * a.strip_w + m;
       const bool store = m < a.strip_w && x < a.W;
@@ -883,14 +913,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
                                            kResidual ? res : nullptr);
       }
       if (!ok) break;
-      // the band's two virtual entries (cleared by its input rows `rows` and `rows + 1`): nothing to
-      // read. The owning group frees each only after that input row is done, i.e. after the issuer
-      // took the slot for it: a release before that would complete a second phase of the slot's
-      // barrier and leave the issuer waiting on the wrong parity.
-      RingPos vin = in;  // input row rows + 2 of the band
+      // the segment's 2 + pad virtual entries (cleared by its input rows rows .. rows + 1 + pad):
+      // nothing to read. The owning group frees each only after that input row is done, i.e. after
+      // the issuer took the slot for it: a release before that would complete a second phase of the
+      // slot's barrier and leave the issuer waiting on the wrong parity.
+      const int virt = 2 + pair_pad(y1 - y0);
+      RingPos vin = in;  // input row rows + 2 of the segment
       vin.retreat(a.ring);
       vin.retreat(a.ring);
-      for (int k = 0; k < 2; ++k, acc.advance(R), vin.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1) {
+      for (int k = 0; k < virt - 2; ++k) in.advance(a.ring);  // past the padding rows as well
+      for (int k = 0; k < virt; ++k, acc.advance(R), vin.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1) {
         if (eg != grp) continue;
         const bool got = wait_bar(&done[vin.idx], vin.phase, a.err, kErrWaitEpilogue);
         if (!__all_sync(0xffffffffu, got)) {

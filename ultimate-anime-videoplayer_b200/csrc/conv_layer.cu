@@ -394,7 +394,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   a.bands = (a.H + band - 1) / band;
   a.items = a.batch * a.bands * units;
   grid = a.items < slots ? a.items : slots;
-  if (paired) grid *= 2;  // two blocks per item
+  if (paired) grid = 2 * slots;  // two blocks per cluster; the launch trims it to the rows
   return Status::Ok();
 }
 
@@ -413,8 +413,13 @@ Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* 
   a.res_chunks = res_chunks;
   a.out_inv_scale = out_inv_scale;
   a.res_scale = res_scale;
-  const int per_item = paired ? 2 : 1;
-  const int g = a.items * per_item < grid ? a.items * per_item : grid;
+  int g = a.items < grid ? a.items : grid;
+  if (paired) {
+    // pair kernel: contiguous row ranges, one per cluster (conv3p.cuh PairSpan)
+    const long long rows = static_cast<long long>(batch) * a.pairs * a.H;
+    const long long clusters = grid / 2;
+    g = 2 * static_cast<int>(rows < clusters ? rows : clusters);
+  }
   k->launch(dim3(static_cast<unsigned>(g)), smem, stream, maps, a);
   return cuda_status(cudaGetLastError(), "conv_tc_kernel launch");
 }
