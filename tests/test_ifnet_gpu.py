@@ -90,8 +90,10 @@ def test_ifnet_matches_reference_golden(name, params):
     assert err <= FP16_MAX_ABS, f"max-abs {err * 255:.3f}/255"
 
 
+# (1, 256, 1056): block 3's residual level is 64 x 264, three 126-pixel strips, so the pair
+# kernel of the 64-channel residual convs runs two strip pairs, one with a strip wholly outside
 @pytest.mark.parametrize("shape,t", [((1, 64, 128), 0.5), ((2, 128, 192), 0.25), ((1, 72, 100), 0.5),
-                                     ((1, 130, 66), 0.7)])
+                                     ((1, 130, 66), 0.7), ((1, 256, 1056), 0.5)])
 def test_ifnet_fp16_parity(shape, t, params):
     from synth import shifted_pair
     n, h, w = shape

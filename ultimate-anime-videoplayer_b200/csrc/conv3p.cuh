@@ -37,6 +37,7 @@
 namespace kb2 {
 
 constexpr uint16_t kPairMask = 3;  // both blocks of the cluster
+constexpr int kPairMaxK = 12;      // K steps per input row: 2, 3 (conv_1), 5, 9 (48 channels), 12 (64)
 
 // Epilogue shape of the pair kernel: `groups` groups of warps take the accumulator entries in turn
 // (entry e goes to group e % groups, so a group owns the slots s with s % groups = g and that many
@@ -48,7 +49,8 @@ template <int kCoutPad, int kEpi>
 struct PairShape {
   static constexpr bool residual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
   static constexpr int groups = residual ? 2 : 3;
-  static constexpr int cols = residual ? 16 : 48;
+  // 64 channels (the IFNet residual convs): 32 columns a warp, 2 x 8 warps (576 threads)
+  static constexpr int cols = residual ? (kCoutPad % 32 == 0 ? 32 : 16) : (kCoutPad % 48 == 0 ? 48 : 32);
   static_assert(kStackSlots % groups == 0, "groups divide the accumulator slots");
   static constexpr int warp_cols = kCoutPad < cols ? kCoutPad : cols;
   static_assert(warp_cols % 16 == 0 && kCoutPad % warp_cols == 0, "16-column TMEM loads per warp");
@@ -129,8 +131,8 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
 template <bool kFp8, int kNK, int kClears>
 __device__ __forceinline__ uint32_t pair_row_head(
     uint32_t d_clear, uint32_t d_clear2, uint64_t zero_desc, uint32_t id_clear, uint32_t d_win, uint32_t idesc,
-    uint32_t nf, uint32_t nf_par, uint32_t ns, uint32_t ns_par, const uint64_t (&a)[9], const uint64_t (&b)[9]) {
-  static_assert(kNK == 2 || kNK == 3 || kNK == 5 || kNK == 9, "rows of 2, 3, 5 or 9 K steps");
+    uint32_t nf, uint32_t nf_par, uint32_t ns, uint32_t ns_par, const uint64_t (&a)[kNK], const uint64_t (&b)[kNK]) {
+  static_assert(kNK == 2 || kNK == 3 || kNK == 5 || kNK == 9 || kNK == 12, "rows of 2, 3, 5, 9 or 12 K steps");
   static_assert(kClears == 1 || kClears == 2, "one or two cleared blocks");
   uint32_t ok;
   if constexpr (kFp8 == false && kNK == 2 && kClears == 1) {
@@ -295,6 +297,53 @@ __device__ __forceinline__ uint32_t pair_row_head(
             "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]),
             "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4])
           : "memory");
+  } else if constexpr (kFp8 == false && kNK == 12 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %14, %20, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %15, %21, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %16, %22, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 12 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %14, %20, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %15, %21, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %16, %22, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5])
+          : "memory");
   } else if constexpr (kFp8 == true && kNK == 2 && kClears == 1) {
     asm volatile(
           "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
@@ -457,13 +506,60 @@ __device__ __forceinline__ uint32_t pair_row_head(
             "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]),
             "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4])
           : "memory");
+  } else if constexpr (kFp8 == true && kNK == 12 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %14, %20, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %15, %21, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %16, %22, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 12 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %17, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %18, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %19, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %14, %20, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %15, %21, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %16, %22, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5])
+          : "memory");
   }
   return ok;
 }
 
 template <bool kFp8, int kNK>
 __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, uint32_t done,
-                                              const uint64_t (&a)[9], const uint64_t (&b)[9]) {
+                                              const uint64_t (&a)[kNK], const uint64_t (&b)[kNK]) {
   if constexpr (kFp8 == false && kNK == 2) {
     asm volatile(
           "{\n\t.reg .pred acc;\n\t"
@@ -508,6 +604,21 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
             "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
             "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8])
           : "memory");
+  } else if constexpr (kFp8 == false && kNK == 12) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %10, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %5, %11, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %6, %12, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %7, %13, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %8, %14, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %9, %15, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[6]), "l"(a[7]), "l"(a[8]), "l"(a[9]), "l"(a[10]), "l"(a[11]),
+            "l"(b[6]), "l"(b[7]), "l"(b[8]), "l"(b[9]), "l"(b[10]), "l"(b[11])
+          : "memory");
   } else if constexpr (kFp8 == true && kNK == 2) {
     asm volatile(
           "{\n\t.reg .pred acc;\n\t"
@@ -551,6 +662,21 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
           ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
             "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(a[8]),
             "l"(b[5]), "l"(b[6]), "l"(b[7]), "l"(b[8])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 12) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %4, %10, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %5, %11, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %6, %12, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %7, %13, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %8, %14, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %9, %15, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[6]), "l"(a[7]), "l"(a[8]), "l"(a[9]), "l"(a[10]), "l"(a[11]),
+            "l"(b[6]), "l"(b[7]), "l"(b[8]), "l"(b[9]), "l"(b[10]), "l"(b[11])
           : "memory");
   }
 }
@@ -602,9 +728,10 @@ struct PairIssue {
 };
 
 // What every row of the issuer needs, set up once.
+template <int kNK>
 struct PairRowCtx {
-  uint64_t ad0[kRowMaxK];  // A descriptors of ring slot 0 (slot k adds k * slot16)
-  uint64_t bs[kRowMaxK];   // B descriptors (all three kernel rows)
+  uint64_t ad0[kNK];  // A descriptors of ring slot 0 (slot k adds k * slot16)
+  uint64_t bs[kNK];   // B descriptors (all three kernel rows)
   uint64_t zero_desc;
   uint64_t slot16;  // one ring slot, in descriptor address units
   uint32_t tmem;
@@ -614,40 +741,54 @@ struct PairRowCtx {
   int* err;
 };
 
-// Input row k of a 12-row period. The input ring has 12 slots and the accumulator ring 6, so within
-// a period every slot index, TMEM address and accumulator phase is a compile-time constant; only
-// the input ring's phase (one bit per period) is not. The issuing thread then executes little
-// besides its two asm blocks.
+// Input ring of the pair kernel: 12 row slots, or 6 for 64-channel layers (twelve 16 KB slots and
+// the weights do not fit in shared memory).
+template <int kCoutPad>
+constexpr uint32_t pair_ring() {
+  return kCoutPad == 64 ? 6u : 12u;
+}
+
+// Input row k of a 12-row period. The accumulator ring has 6 slots and the input ring 12 or 6, so
+// within a period every slot index, TMEM address and accumulator phase is a compile-time constant.
+// With 12 input slots the input phase is one bit per period (`ph`); with 6 it is 0 for rows 0-5 and
+// 1 for rows 6-11 of every period (`ph` stays 0). The issuing thread then executes little besides
+// its two asm blocks.
 template <bool kFp8, int kCoutPad, int kNK, int kK>
-__device__ __forceinline__ bool pair_row_k(const PairRowCtx& c, uint32_t ph, uint32_t& pre) {
+__device__ __forceinline__ bool pair_row_k(const PairRowCtx<kNK>& c, uint32_t ph, uint32_t& pre) {
+  constexpr uint32_t kRing = pair_ring<kCoutPad>();
+  constexpr uint32_t kIn = kK % kRing;
+  constexpr uint32_t kInPh = kRing == 6u && kK >= 6 ? 1u : 0u;
   constexpr uint32_t kSlot = kK % 6;
   constexpr uint32_t kAccPh = kK >= 6 ? 1u : 0u;
   constexpr uint32_t kStart = kSlot >= 2 ? kSlot - 2 : kSlot + 4;
   constexpr uint32_t kNext = (kK + 1) % 12;
+  constexpr uint32_t kNextIn = kNext % kRing;
+  // the next row's input phase: row 0 of the next period when k = 11
+  constexpr uint32_t kNextInPh = kK == 11 ? (kRing == 12u ? 1u : 0u) : (kRing == 6u && kNext >= 6 ? 1u : 0u);
   constexpr uint32_t kNextSlot = kNext % 6;
   constexpr uint32_t kNextAccPh = kNext >= 6 ? 1u : 0u;
   constexpr uint32_t kIdClear = make_idesc(256, kCoutPad);
   constexpr uint32_t kIdWin = make_idesc(256, 3 * kCoutPad);
-  if (!(pre & 1u) && !wait_bar(c.full + kK, ph, c.err, kErrWaitMma)) return false;
+  if (!(pre & 1u) && !wait_bar(c.full + kIn, ph ^ kInPh, c.err, kErrWaitMma)) return false;
   if (!(pre & 2u) && !wait_bar(c.slot_free + kSlot, kAccPh, c.err, kErrWaitMma)) return false;
   tc_fence_after();
-  uint64_t ad[kRowMaxK];
-  const uint64_t off = static_cast<uint64_t>(kK) * c.slot16;
+  uint64_t ad[kNK];
+  const uint64_t off = static_cast<uint64_t>(kIn) * c.slot16;
 #pragma unroll
-  for (int j = 0; j < kRowMaxK; ++j) ad[j] = c.ad0[j] + off;
+  for (int j = 0; j < kNK; ++j) ad[j] = c.ad0[j] + off;
   const uint32_t d_clear = c.tmem + kSlot * kCoutPad;
   const uint32_t d_win = c.tmem + kStart * kCoutPad;
-  const uint32_t nf = c.full_u32 + kNext * 8u;
-  const uint32_t nf_par = ph ^ (kK == 11 ? 1u : 0u);
+  const uint32_t nf = c.full_u32 + kNextIn * 8u;
+  const uint32_t nf_par = ph ^ kNextInPh;
   const uint32_t ns = c.free_u32 + kNextSlot * 8u;
   pre = pair_row_head<kFp8, kNK, (kSlot < 2 ? 2 : 1)>(d_clear, d_clear + 6u * kCoutPad, c.zero_desc, kIdClear, d_win,
                                                         kIdWin, nf, nf_par, ns, kNextAccPh, ad, c.bs);
-  pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + kK * 8u, ad, c.bs);
+  pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + kIn * 8u, ad, c.bs);
   return true;
 }
 
 template <bool kFp8, int kCoutPad, int kNK, int... kKs>
-__device__ __forceinline__ bool pair_period(const PairRowCtx& c, uint32_t ph, uint32_t& pre,
+__device__ __forceinline__ bool pair_period(const PairRowCtx<kNK>& c, uint32_t ph, uint32_t& pre,
                                             std::integer_sequence<int, kKs...>) {
   return (pair_row_k<kFp8, kCoutPad, kNK, kKs>(c, ph, pre) && ...);
 }
@@ -663,11 +804,11 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
   constexpr uint32_t R = kStackSlots;
   constexpr uint32_t kIdClear = make_idesc(256, kCoutPad);
   constexpr uint32_t kIdWin = make_idesc(256, 3 * kCoutPad);
-  PairRowCtx c;
+  PairRowCtx<kNK> c;
   const uint64_t a_base = make_sdesc(0, 0, 128) | static_cast<uint64_t>(is.ring_base >> 4);
   const uint64_t b_desc0 = make_sdesc(is.w_base, kNHalf * 16, 128);
 #pragma unroll
-  for (int j = 0; j < kRowMaxK; ++j) {
+  for (int j = 0; j < kNK; ++j) {
     c.ad0[j] = a_base + is.s_k[j];
     c.bs[j] = b_desc0 + static_cast<uint64_t>(j) * kBStep16;
   }
@@ -687,11 +828,12 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
     int n, pair, y0, y1;
     while (sp.next(a, n, pair, y0, y1)) total += static_cast<uint32_t>(y1 - y0 + 2 + pair_pad(y1 - y0));
   }
-  if (a.ring != 12u) return;  // the host sizes every paired ring to 12 slots
-  uint32_t ph = 0;   // input ring phase of the current period
+  constexpr uint32_t kRing = pair_ring<kCoutPad>();
+  if (a.ring != kRing) return;  // the host sizes the ring by pair_ring
+  uint32_t ph = 0;   // input ring phase of the current period (12 slots; 6 slots: always 0)
   uint32_t pre = 0;  // next row's barriers found complete by the previous row: 1 = input, 2 = slot
   uint32_t g = 0;
-  for (; g + 12u <= total; g += 12u, ph ^= 1u)
+  for (; g + 12u <= total; g += 12u, ph ^= (kRing == 12u ? 1u : 0u))
     if (!pair_period<kFp8, kCoutPad, kNK>(c, ph, pre, std::make_integer_sequence<int, 12>{})) return;
   // the last rows (fewer than a period), with run-time positions
   RingPos in{0, ph};
@@ -700,10 +842,10 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
     if (!(pre & 1u) && !wait_bar(&is.full[in.idx], in.phase, a.err, kErrWaitMma)) return;
     if (!(pre & 2u) && !wait_bar(&is.slot_free[acc.idx], acc.phase, a.err, kErrWaitMma)) return;
     tc_fence_after();
-    uint64_t ad[kRowMaxK];
+    uint64_t ad[kNK];
     const uint64_t off = static_cast<uint64_t>(in.idx) * c.slot16;
 #pragma unroll
-    for (int j = 0; j < kRowMaxK; ++j) ad[j] = c.ad0[j] + off;
+    for (int j = 0; j < kNK; ++j) ad[j] = c.ad0[j] + off;
     const uint32_t start = acc.idx >= 2 ? acc.idx - 2 : acc.idx + R - 2;
     const uint32_t d_clear = c.tmem + acc.idx * kCoutPad;
     const uint32_t d_win = c.tmem + start * kCoutPad;
@@ -728,7 +870,8 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
 template <bool kFp8, int kCoutPad, int kEpi, int kOut>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, kEpi>::threads, 1)
     conv3p_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
-  static_assert(kCoutPad == 16 || kCoutPad == 48, "paired kernel: 16 or 48 output channels");
+  static_assert(kCoutPad == 16 || kCoutPad == 48 || kCoutPad == 64, "paired kernel: 16, 48 or 64 output channels");
+  static_assert(kStackBlocks * kCoutPad <= kStackTmemCols, "TMEM blocks");
   constexpr int kGroupWarps = PairShape<kCoutPad, kEpi>::group_warps;
   constexpr uint32_t R = kStackSlots;
   extern __shared__ uint8_t smem_raw[];
@@ -824,11 +967,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
         // ---------------------------------------------------------------- MMA issuer (pair)
         if (wait_bar(wbar, 0, a.err, kErrWaitMma) && wait_bar(wpeer, 0, a.err, kErrWaitMma)) {
           const PairIssue is{a, smem_u32(ring), smem_u32(sw), smem_u32(zero_b), tmem_base, s_k, full, done, slot_free};
-          switch (a.n_ksteps) {
-            case 9: pair_issue<kFp8, kCoutPad, 9>(is); break;
-            case 5: pair_issue<kFp8, kCoutPad, 5>(is); break;
-            case 3: pair_issue<kFp8, kCoutPad, 3>(is); break;
-            default: pair_issue<kFp8, kCoutPad, 2>(is); break;  // the host admits 2, 3, 5 or 9 K steps
+          if constexpr (kCoutPad == 64) {
+            pair_issue<kFp8, kCoutPad, 12>(is);  // the host admits 12 K steps only (FP16, 64 channels)
+          } else {
+            switch (a.n_ksteps) {
+              case 9: pair_issue<kFp8, kCoutPad, 9>(is); break;
+              case 5: pair_issue<kFp8, kCoutPad, 5>(is); break;
+              case 3: pair_issue<kFp8, kCoutPad, 3>(is); break;
+              default: pair_issue<kFp8, kCoutPad, 2>(is); break;  // the host admits 2, 3, 5 or 9 K steps
+            }
           }
         }
         mma_commit_pair(drain);
@@ -854,16 +1001,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
     const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
     const uint32_t free0 = cluster_addr(smem_u32(slot_free), 0);  // block 0's slot_free[0]
     // FP16 layers: this warp's biases in registers and no channel scale (re-reading both from shared
-    // memory on every row measured 5-15 % slower); E4M3 layers read bias and scale from shared
-    // memory (in registers they spill)
+    // memory on every row measured 5-15 % slower); E4M3 layers and the 64-channel residual shape
+    // (96 registers a thread at 576 threads) read bias and scale from shared memory (in registers
+    // they spill)
+    constexpr bool kRegBias = !kFp8 && kCoutPad != 64;
     float r_bias[kCols], r_scale[kCols];
 #pragma unroll
     for (int j = 0; j < kCols; ++j) {
-      r_bias[j] = kFp8 ? 0.0f : s_bias[col0 + j];
+      r_bias[j] = kRegBias ? s_bias[col0 + j] : 0.0f;
       r_scale[j] = 1.0f;
     }
-    const float* e_bias = kFp8 ? s_bias + col0 : r_bias;
-    const float* e_scale = kFp8 ? s_scale + col0 : r_scale;
+    const float* e_bias = kRegBias ? r_bias : s_bias + col0;
+    const float* e_scale = kRegBias ? r_scale : s_scale + col0;
     // the group's slots start free (phase 0 of slot_free)
     if (lane == 0)
       for (uint32_t s = grp; s < R; s += kG) mbar_arrive_remote_relaxed(free0 + s * 8u);

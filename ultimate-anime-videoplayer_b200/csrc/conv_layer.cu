@@ -110,9 +110,16 @@ const KernelEntry kKernels[] = {
     KB2_PAIRED(true, 48, kEpiSilu, kOutF16E4m3),
     KB2_PAIRED(true, 48, kEpiSpanAttn, kOutE4m3Chunk),
     KB2_PAIRED(true, 48, kEpiSpanAttn, kOutF16Chunk),
+    // the IFNet residual convs of 64 channels (ifnet_net.cu): pair kernel only
+    KB2_PAIRED(false, 64, kEpiResPrelu, kOutF16Chunk),
 };
 
-bool wants_stacked(const ConvSpec& s) { return s.taps == 9 && s.n_sources == 1 && (s.n_pad == 48 || s.n_pad == 16); }
+bool wants_stacked(const ConvSpec& s) {
+  return s.taps == 9 && s.n_sources == 1 && (s.n_pad == 48 || s.n_pad == 16 || s.n_pad == 64);
+}
+
+// K steps per input row the pair kernel runs (conv3p.cuh): 2, 3, 5 or 9 below 64 channels, 12 at 64
+bool pair_admits(int n_pad, int nk) { return n_pad == 64 ? nk == 12 : (nk == 2 || nk == 3 || nk == 5 || nk == 9); }
 
 const KernelEntry* find_kernel(const ConvSpec& s, int kind) {
   for (const KernelEntry& k : kKernels)
@@ -147,8 +154,9 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
                         const float* act_scales, const ChunkedTensor* const* inputs, int* err_word) {
   spec = s;
   kind = wants_stacked(s) ? kKindStacked : kKindGeneric;
-  const KernelEntry* k = find_kernel(s, kind);
-  if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this layer shape");
+  const KernelEntry* k = find_kernel(s, kind);  // stacked shapes may have a pair kernel only (below)
+  if (k == nullptr && (kind != kKindStacked || find_kernel(s, kKindPaired) == nullptr))
+    return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this layer shape");
   const ChunkedTensor& in0 = *inputs[0];
   for (int i = 0; i < s.n_sources; ++i) {
     const ChunkedTensor& t = *inputs[i];
@@ -169,13 +177,14 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     for (const auto& st : steps)
       if (st[0].dy == 0) row_steps.push_back(st);
     steps = row_steps;
-    // rows of 2, 3, 5 or 9 K steps run on the pair kernel (one MMA for two SMs)
+    // rows of 2, 3, 5, 9 (or 12 at 64 channels) K steps run on the pair kernel (one MMA for two SMs)
     const int nk = static_cast<int>(steps.size());
     const KernelEntry* kp = find_kernel(s, kKindPaired);
-    if (kPairedStack && kp != nullptr && (nk == 2 || nk == 3 || nk == 5 || nk == 9)) {
+    if ((kPairedStack || k == nullptr) && kp != nullptr && pair_admits(s.n_pad, nk)) {
       kind = kKindPaired;
       k = kp;
     }
+    if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this row shape");
   }
   const bool paired = kind == kKindPaired;
   if (static_cast<int>(steps.size()) > kMaxKSteps) return refuse(KB2_FORMAT_UNSUPPORTED, "too many K steps");
@@ -243,7 +252,8 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     a.n_tiles = 0;
     for (int i = 0; i < 3; ++i) a.idesc_n[i] = make_idesc(kTileM, (i + 1) * s.n_pad);
     a.acc_slots = static_cast<int>(kStackSlots);
-    if (static_cast<int>(steps.size()) > kRowMaxK) return refuse(KB2_FORMAT_UNSUPPORTED, "stacked: too many K steps per row");
+    if (static_cast<int>(steps.size()) > (paired ? kPairMaxK : kRowMaxK))
+      return refuse(KB2_FORMAT_UNSUPPORTED, "stacked: too many K steps per row");
   }
   const int n_rows_b = stacked ? 3 * s.n_pad : s.n_pad;  // rows of B per K step
 
@@ -346,7 +356,8 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     int ring = one_per_sm ? fit(200u * 1024u) : fit((228u * 1024u) / 2 - 2048u);
     if (!one_per_sm && !stacked && ring < min_ring + 2) ring = fit(227u * 1024u);  // wide slots: one block per SM
     ring = std::min(ring, 12);
-    if (paired) ring = 12;  // the pair issuer runs 12-row periods (checked against shared memory below)
+    // the pair issuer's ring is fixed by its 12-row periods (checked against shared memory below)
+    if (paired) ring = static_cast<int>(s.n_pad == 64 ? pair_ring<64>() : pair_ring<48>());
     a.ring = static_cast<uint32_t>(std::max(ring, min_ring));
   }
   smem = a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (stacked ? kStackSmemExtra : kConvSmemExtra);

@@ -48,15 +48,21 @@ struct IfFrames {
   uint2* pad1;
 };
 
+// The glue kernels run on a grid of rows: blockIdx.x * blockDim.x + threadIdx.x is the column and
+// blockIdx.y walks the rows (frame-major) in steps of gridDim.y, so no thread divides a 64-bit
+// pixel index.
+constexpr int kGlueThreads = 256;
+constexpr int kGlueMaxRowBlocks = 65535;
+
 // NCHW frames -> padded RGBx pixels (zeros outside the window).
 __global__ void ifnet_pad_frames_kernel(IfFrames F, int batch) {
-  const long long total = static_cast<long long>(batch) * F.Hp * F.Wp;
   const size_t plane = static_cast<size_t>(F.H) * F.W;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int X = static_cast<int>(i % F.Wp);
-    const int Y = static_cast<int>((i / F.Wp) % F.Hp);
-    const int n = static_cast<int>(i / (static_cast<long long>(F.Wp) * F.Hp));
+  const int X = blockIdx.x * blockDim.x + threadIdx.x;
+  if (X >= F.Wp) return;
+  for (int r = blockIdx.y; r < batch * F.Hp; r += gridDim.y) {
+    const int n = r / F.Hp;
+    const int Y = r - n * F.Hp;
+    const size_t i = static_cast<size_t>(r) * F.Wp + X;
     const int y = Y - F.top, x = X - F.left;
     uint2 p0 = make_uint2(0, 0), p1 = make_uint2(0, 0);
     if (y >= 0 && y < F.H && x >= 0 && x < F.W) {
@@ -151,10 +157,12 @@ struct IfFlowField {
   }
 };
 
-// Flow (4) and mask after blocks [0, k) at padded pixel (Y, X) of frame n (k >= 1).
-__device__ __forceinline__ void flow_at(const IfFlowLevels& L, int k, int n, int Y, int X, int Hp, int Wp,
-                                        float f[4], float* mask) {
-  for (int j = 0; j < k; ++j) flow_step(L, j, n, Y, X, Hp, Wp, f, mask);
+// Flow (4) and mask after blocks [0, K) at padded pixel (Y, X) of frame n (K >= 1).
+template <int K>
+__device__ __forceinline__ void flow_at(const IfFlowLevels& L, int n, int Y, int X, int Hp, int Wp, float f[4],
+                                        float* mask) {
+#pragma unroll
+  for (int j = 0; j < K; ++j) flow_step(L, j, n, Y, X, Hp, Wp, f, mask);
 }
 
 // The three channels of padded pixel (Y, X) of one padded frame.
@@ -186,13 +194,14 @@ __device__ __forceinline__ void warp3(const uint2* pad, const IfFrames& F, int n
   }
 }
 
-// The 12 input planes of block k >= 1 at padded full-resolution pixel (Y, X): warped frames (6),
+// The 12 input planes of block K >= 1 at padded full-resolution pixel (Y, X): warped frames (6),
 // timestep, mask, flow (4, not yet divided by the block scale). Block 3 also stores the flow.
-__device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowLevels& L, const IfFlowField& FF, int k,
-                                             int n, int Y, int X, float timestep, float v[12]) {
+template <int K>
+__device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowLevels& L, const IfFlowField& FF, int n,
+                                             int Y, int X, float timestep, float v[12]) {
   float f[4], mask;
-  flow_at(L, k, n, Y, X, F.Hp, F.Wp, f, &mask);
-  if (k == kIfBlocks - 1) {
+  flow_at<K>(L, n, Y, X, F.Hp, F.Wp, f, &mask);
+  if constexpr (K == kIfBlocks - 1) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) FF.f[FF.at(n, c, Y, X)] = f[c];
     FF.f[FF.at(n, 4, Y, X)] = mask;
@@ -205,24 +214,26 @@ __device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowLeve
   for (int c = 0; c < 4; ++c) v[8 + c] = f[c];
 }
 
-// Input of block k as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used):
-// the block's planes resized to 1/s (not for s = 1), the flow planes then divided by s.
-__global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int k, int batch,
-                                         float timestep, uint8_t* __restrict__ out) {
-  const int s = if_scale(k);
+// Input of block K as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used):
+// the block's planes resized to 1/s (not for s = 1), the flow planes then divided by s. One
+// instantiation per block, so that every plane array stays in registers.
+template <int K>
+__global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, float timestep,
+                                         uint8_t* __restrict__ out) {
+  constexpr int k = K;
+  constexpr int s = if_scale(K);
   const int ho = F.Hp / s, wo = F.Wp / s;
-  const long long total = static_cast<long long>(batch) * ho * wo;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int ox = static_cast<int>(i % wo);
-    const int oy = static_cast<int>((i / wo) % ho);
-    const int n = static_cast<int>(i / (static_cast<long long>(wo) * ho));
+  const int ox = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ox >= wo) return;
+  for (int r = blockIdx.y; r < batch * ho; r += gridDim.y) {
+    const int n = r / ho;
+    const int oy = r - n * ho;
     float v[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) v[c] = 0.0f;
-    const int nc = k == 0 ? 7 : 12;
-    if (s == 1) {
-      block_planes(F, L, FF, k, n, oy, ox, timestep, v);
+    constexpr int nc = k == 0 ? 7 : 12;
+    if constexpr (s == 1) {
+      block_planes<K>(F, L, FF, n, oy, ox, timestep, v);
     } else {
       const AxisTap ty = resize_tap(oy, static_cast<float>(s), F.Hp);
       const AxisTap tx = resize_tap(ox, static_cast<float>(s), F.Wp);
@@ -233,18 +244,19 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, IfFlowField
 #pragma unroll
         for (int xx = 0; xx < 2; ++xx) {
           float* p = q[yy * 2 + xx];
-          if (k == 0) {
+          if constexpr (k == 0) {
             frame_rgb(F.pad0, F, n, ys[yy], xs[xx], p);
             frame_rgb(F.pad1, F, n, ys[yy], xs[xx], p + 3);
             p[6] = timestep;
           } else {
-            block_planes(F, L, FF, k, n, ys[yy], xs[xx], timestep, p);
+            block_planes<K>(F, L, FF, n, ys[yy], xs[xx], timestep, p);
           }
         }
+#pragma unroll
       for (int c = 0; c < nc; ++c)
         v[c] = lerp_rn(lerp_rn(q[0][c], q[1][c], tx.t), lerp_rn(q[2][c], q[3][c], tx.t), ty.t);
     }
-    if (k > 0) {
+    if constexpr (k > 0) {
       const float inv = __fdiv_rn(1.0f, static_cast<float>(s));
 #pragma unroll
       for (int c = 8; c < 12; ++c) v[c] = __fmul_rn(v[c], inv);
@@ -269,12 +281,11 @@ __global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, IfFlowField
 // The interpolated frame: warp both frames by the final flow, blend with sigmoid(mask), crop the
 // window: out = w0 * m + w1 * (1 - m), NCHW FP16 [n][3][H][W].
 __global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, __half* __restrict__ out) {
-  const long long total = static_cast<long long>(batch) * F.H * F.W;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int x = static_cast<int>(i % F.W);
-    const int y = static_cast<int>((i / F.W) % F.H);
-    const int n = static_cast<int>(i / (static_cast<long long>(F.W) * F.H));
+  const int x = blockIdx.x * blockDim.x + threadIdx.x;
+  if (x >= F.W) return;
+  for (int r = blockIdx.y; r < batch * F.H; r += gridDim.y) {
+    const int n = r / F.H;
+    const int y = r - n * F.H;
     const int Y = y + F.top, X = x + F.left;
     float f[4], mask;
 #pragma unroll

@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cstring>
 
+#include "conv_layer.h"
 #include "ifnet_conv.cuh"
 #include "ifnet_glue.cuh"
 #include "ifnet_net.h"
@@ -24,6 +25,8 @@ namespace {
 
 constexpr int kIfChannels[kIfBlocks] = {192, 128, 96, 64};
 constexpr int kIfRes = 8;
+// block 3's residual convs (64 channels) on the pair kernel (IfLayer::build_paired)
+constexpr bool kIfPairedRes = true;
 
 using IfLaunchFn = void (*)(dim3, size_t, cudaStream_t, const IfMaps&, const IfConvArgs&);
 
@@ -87,6 +90,48 @@ struct IfLayer {
   int per_sm = 1;
   int kind = 0;
   double flops_px = 0.0, bytes_px = 0.0;  // algorithmic work per output pixel
+  // 64-channel residual convs run on the paired stacked kernel (conv3p.cuh) instead: one M = 256
+  // MMA for two SMs, the three kernel rows stacked in N = 192
+  ConvLayer pair;
+  bool paired = false;
+  uint8_t* pair_out = nullptr;
+  const uint8_t* pair_res = nullptr;
+  int pair_res_chunks = 0;
+
+  // The residual conv (PReLU(conv(x) + bias + x), C -> C, stride 1) of `c` = 64 channels on the pair
+  // kernel: the tensors are [n][h][c / 8][w][8] FP16, the ConvLayer row layout.
+  Status build_paired(int c, const float* w, const float* b, const float* prelu, uint8_t* in, int batch, int h,
+                      int wd, uint8_t* out, int* err) {
+    ConvSpec s;
+    s.taps = 9;
+    s.fp8 = false;
+    s.n_sources = 1;
+    s.cin = c;
+    s.n_real = c;
+    s.n_pad = c;
+    s.epi = kEpiResPrelu;
+    s.out = kOutF16Chunk;
+    s.out_chunks = c / 8;
+    ChunkedTensor t;
+    t.ptr = in;
+    t.batch = batch;
+    t.H = h;
+    t.W = wd;
+    t.chunks = c / 8;
+    t.fp8 = false;
+    const ChunkedTensor* inputs[1] = {&t};
+    KB2_TRY(pair.build(s, w, b, prelu, nullptr, inputs, err));
+    if (pair.kind != 2) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet: residual conv did not map to the pair kernel");
+    paired = true;
+    pair_out = out;
+    pair_res = in;
+    pair_res_chunks = c / 8;
+    args.h_out = h;
+    args.w_out = wd;
+    flops_px = 2.0 * 9.0 * c * c;
+    bytes_px = 3.0 * (c / 8) * 16.0;  // input, residual and output: one FP16 pixel each
+    return Status::Ok();
+  }
 
   // w(n, ci, dy, dx): weight of output column n, input channel ci, tap (dy, dx); cout columns used.
   template <class W>
@@ -191,6 +236,7 @@ struct IfLayer {
   }
 
   Status launch(cudaStream_t stream, int batch) {
+    if (paired) return pair.launch(stream, batch, pair_out, pair_res, 1.0f, 1.0f, nullptr, pair_res_chunks);
     IfConvArgs a = args;
     a.batch = batch;
     a.items = batch * a.h_out * a.strips;
@@ -289,8 +335,11 @@ Status IfnetNet::create(const std::vector<float>& params, int max_batch, int H, 
       Tensor* src = j % 2 == 0 ? r0.get() : r1.get();
       Tensor* dst = j % 2 == 0 ? r1.get() : r0.get();
       auto lr = std::make_unique<IfLayer>();
-      KB2_TRY(lr->build(c, 1, kIfResPrelu, conv_w(wr, c), c, c, br, sr, src->ptr, max_batch_, h2, w2, c / 8, h2, w2,
-                        dst->ptr, c / 8, nullptr, err));
+      if (c == 64 && kIfPairedRes)
+        KB2_TRY(lr->build_paired(c, wr, br, sr, src->ptr, max_batch_, h2, w2, dst->ptr, err));
+      else
+        KB2_TRY(lr->build(c, 1, kIfResPrelu, conv_w(wr, c), c, c, br, sr, src->ptr, max_batch_, h2, w2, c / 8, h2,
+                          w2, dst->ptr, c / 8, nullptr, err));
       lr->kind = k_res;
       layers_.push_back(std::move(lr));
     }
@@ -341,7 +390,9 @@ size_t IfnetNet::device_bytes() const {
   for (const auto& t : tensors_) total += t->buf.bytes;
   for (const auto& f : flows_) total += f.bytes;
   total += flow_full_.bytes + pad_.bytes;
-  for (const auto& l : layers_) total += l->wpack.bytes + l->bias.bytes + l->slope.bytes;
+  for (const auto& l : layers_)
+    total += l->wpack.bytes + l->bias.bytes + l->slope.bytes + l->pair.wpack.bytes + l->pair.bias.bytes +
+             l->pair.slope.bytes + l->pair.scale.bytes;
   return total;
 }
 
@@ -350,11 +401,17 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
   uint2* pad0 = pad_.as<uint2>();
   IfFrames F{static_cast<const __half*>(img0), static_cast<const __half*>(img1), H_, W_, Hp_, Wp_, top_, left_, pad0,
              pad0 + static_cast<size_t>(max_batch_) * Hp_ * Wp_};
+  // a grid of rows for the glue kernels (ifnet_glue.cuh): about 16 blocks per SM, each walking rows
+  const int sms = num_sms();
+  auto row_grid = [sms](int width, int rows) {
+    const int bx = (width + kGlueThreads - 1) / kGlueThreads;
+    const int by = std::max(1, std::min({rows, kGlueMaxRowBlocks, (16 * sms + bx - 1) / bx}));
+    return dim3(static_cast<unsigned>(bx), static_cast<unsigned>(by));
+  };
   {
     const long long px = static_cast<long long>(batch) * Hp_ * Wp_;
-    const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
     KB2_TRY(timer_.begin(stream));
-    ifnet_pad_frames_kernel<<<blocks, 256, 0, stream>>>(F, batch);
+    ifnet_pad_frames_kernel<<<row_grid(Wp_, batch * Hp_), kGlueThreads, 0, stream>>>(F, batch);
     KB2_CUDA(cudaGetLastError());
     KB2_TRY(timer_.end(k_pad_, 0.0, px * (12.0 + 16.0), stream));
   }
@@ -372,9 +429,15 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
   for (int k = 0; k < kIfBlocks; ++k) {
     const int s = if_scale(k);
     const long long px = static_cast<long long>(batch) * (Hp_ / s) * (Wp_ / s);
-    const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
+    const dim3 g = row_grid(Wp_ / s, batch * (Hp_ / s));
+    constexpr int T = kGlueThreads;
     KB2_TRY(timer_.begin(stream));
-    ifnet_block_input_kernel<<<blocks, 256, 0, stream>>>(F, L, FF, k, batch, timestep_, x_[k]->ptr);
+    switch (k) {
+      case 0: ifnet_block_input_kernel<0><<<g, T, 0, stream>>>(F, L, FF, batch, timestep_, x_[k]->ptr); break;
+      case 1: ifnet_block_input_kernel<1><<<g, T, 0, stream>>>(F, L, FF, batch, timestep_, x_[k]->ptr); break;
+      case 2: ifnet_block_input_kernel<2><<<g, T, 0, stream>>>(F, L, FF, batch, timestep_, x_[k]->ptr); break;
+      default: ifnet_block_input_kernel<3><<<g, T, 0, stream>>>(F, L, FF, batch, timestep_, x_[k]->ptr); break;
+    }
     KB2_CUDA(cudaGetLastError());
     KB2_TRY(timer_.end(k_glue_, 0.0, px * 32.0, stream));
     for (int i = 0; i < per_block; ++i) {
@@ -386,9 +449,8 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
     }
   }
   const long long px = static_cast<long long>(batch) * H_ * W_;
-  const int blocks = static_cast<int>(std::min<long long>((px + 255) / 256, 32LL * num_sms()));
   KB2_TRY(timer_.begin(stream));
-  ifnet_blend_kernel<<<blocks, 256, 0, stream>>>(F, L, FF, batch, static_cast<__half*>(out));
+  ifnet_blend_kernel<<<row_grid(W_, batch * H_), kGlueThreads, 0, stream>>>(F, L, FF, batch, static_cast<__half*>(out));
   KB2_CUDA(cudaGetLastError());
   KB2_TRY(timer_.end(k_blend_, 0.0, px * (20.0 + 12.0 + 6.0), stream));
   return Status::Ok();
