@@ -730,10 +730,14 @@ struct PairIssue {
 // What every row of the issuer needs, set up once.
 template <int kNK>
 struct PairRowCtx {
-  uint64_t ad0[kNK];  // A descriptors of ring slot 0 (slot k adds k * slot16)
-  uint64_t bs[kNK];   // B descriptors (all three kernel rows)
+  // The descriptors of a row differ only in their low words (start address and LBO fields), so the
+  // context keeps those and one high word each: half the registers of 64-bit arrays (a row of 12 K
+  // steps otherwise spills).
+  uint32_t a_lo[kNK];  // A descriptors of ring slot 0 (slot k adds k * slot16)
+  uint32_t b_lo[kNK];  // B descriptors (all three kernel rows)
+  uint32_t a_hi, b_hi;
   uint64_t zero_desc;
-  uint64_t slot16;  // one ring slot, in descriptor address units
+  uint32_t slot16;  // one ring slot, in descriptor address units
   uint32_t tmem;
   uint32_t full_u32, done_u32, free_u32;  // shared addresses of full[0], done[0], slot_free[0]
   uint64_t* full;
@@ -772,18 +776,21 @@ __device__ __forceinline__ bool pair_row_k(const PairRowCtx<kNK>& c, uint32_t ph
   if (!(pre & 1u) && !wait_bar(c.full + kIn, ph ^ kInPh, c.err, kErrWaitMma)) return false;
   if (!(pre & 2u) && !wait_bar(c.slot_free + kSlot, kAccPh, c.err, kErrWaitMma)) return false;
   tc_fence_after();
-  uint64_t ad[kNK];
-  const uint64_t off = static_cast<uint64_t>(kIn) * c.slot16;
+  uint64_t ad[kNK], bd[kNK];
+  const uint32_t off = kIn * c.slot16;
 #pragma unroll
-  for (int j = 0; j < kNK; ++j) ad[j] = c.ad0[j] + off;
+  for (int j = 0; j < kNK; ++j) {
+    ad[j] = (static_cast<uint64_t>(c.a_hi) << 32) | (c.a_lo[j] + off);
+    bd[j] = (static_cast<uint64_t>(c.b_hi) << 32) | c.b_lo[j];
+  }
   const uint32_t d_clear = c.tmem + kSlot * kCoutPad;
   const uint32_t d_win = c.tmem + kStart * kCoutPad;
   const uint32_t nf = c.full_u32 + kNextIn * 8u;
   const uint32_t nf_par = ph ^ kNextInPh;
   const uint32_t ns = c.free_u32 + kNextSlot * 8u;
   pre = pair_row_head<kFp8, kNK, (kSlot < 2 ? 2 : 1)>(d_clear, d_clear + 6u * kCoutPad, c.zero_desc, kIdClear, d_win,
-                                                        kIdWin, nf, nf_par, ns, kNextAccPh, ad, c.bs);
-  pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + kIn * 8u, ad, c.bs);
+                                                        kIdWin, nf, nf_par, ns, kNextAccPh, ad, bd);
+  pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + kIn * 8u, ad, bd);
   return true;
 }
 
@@ -809,11 +816,13 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
   const uint64_t b_desc0 = make_sdesc(is.w_base, kNHalf * 16, 128);
 #pragma unroll
   for (int j = 0; j < kNK; ++j) {
-    c.ad0[j] = a_base + is.s_k[j];
-    c.bs[j] = b_desc0 + static_cast<uint64_t>(j) * kBStep16;
+    c.a_lo[j] = static_cast<uint32_t>(a_base + is.s_k[j]);
+    c.b_lo[j] = static_cast<uint32_t>(b_desc0 + static_cast<uint64_t>(j) * kBStep16);
   }
   c.zero_desc = make_sdesc(is.zero_base, (kCoutPad / 2) * 16, 128);
   c.slot16 = a.slot_bytes >> 4;
+  c.a_hi = static_cast<uint32_t>(a_base >> 32);
+  c.b_hi = static_cast<uint32_t>(b_desc0 >> 32);
   c.tmem = is.tmem_base;
   c.full_u32 = smem_u32(is.full);
   c.done_u32 = smem_u32(is.done);
@@ -842,10 +851,13 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
     if (!(pre & 1u) && !wait_bar(&is.full[in.idx], in.phase, a.err, kErrWaitMma)) return;
     if (!(pre & 2u) && !wait_bar(&is.slot_free[acc.idx], acc.phase, a.err, kErrWaitMma)) return;
     tc_fence_after();
-    uint64_t ad[kNK];
-    const uint64_t off = static_cast<uint64_t>(in.idx) * c.slot16;
+    uint64_t ad[kNK], bd[kNK];
+    const uint32_t off = in.idx * c.slot16;
 #pragma unroll
-    for (int j = 0; j < kNK; ++j) ad[j] = c.ad0[j] + off;
+    for (int j = 0; j < kNK; ++j) {
+      ad[j] = (static_cast<uint64_t>(c.a_hi) << 32) | (c.a_lo[j] + off);
+      bd[j] = (static_cast<uint64_t>(c.b_hi) << 32) | c.b_lo[j];
+    }
     const uint32_t start = acc.idx >= 2 ? acc.idx - 2 : acc.idx + R - 2;
     const uint32_t d_clear = c.tmem + acc.idx * kCoutPad;
     const uint32_t d_win = c.tmem + start * kCoutPad;
@@ -857,11 +869,11 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
     const uint32_t ns = c.free_u32 + nacc.idx * 8u;
     if (acc.idx < 2)
       pre = pair_row_head<kFp8, kNK, 2>(d_clear, d_clear + 6u * kCoutPad, c.zero_desc, kIdClear, d_win, kIdWin, nf,
-                                        nin.phase, ns, nacc.phase, ad, c.bs);
+                                        nin.phase, ns, nacc.phase, ad, bd);
     else
       pre = pair_row_head<kFp8, kNK, 1>(d_clear, d_clear, c.zero_desc, kIdClear, d_win, kIdWin, nf, nin.phase, ns,
-                                        nacc.phase, ad, c.bs);
-    pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + in.idx * 8u, ad, c.bs);
+                                        nacc.phase, ad, bd);
+    pair_row_tail<kFp8, kNK>(d_win, kIdWin, c.done_u32 + in.idx * 8u, ad, bd);
     in.advance(a.ring);
     acc.advance(R);
   }
