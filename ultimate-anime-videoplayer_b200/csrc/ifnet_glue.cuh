@@ -113,36 +113,61 @@ __device__ __forceinline__ AxisTap warp_tap(int p, float f, int n) {
   return r;
 }
 
-// Adds block j's contribution at padded pixel (Y, X) of frame n to the flow (4) and mask; block 0
-// sets them.
-__device__ __forceinline__ void flow_step(const IfFlowLevels& L, int j, int n, int Y, int X, int Hp, int Wp,
-                                          float f[4], float* mask) {
+// The x half of block j's flow resize at one full-resolution column, cached along a column: the
+// column's x tap (fixed), and for the source row pair last used (lo, hi) both rows' 5 channels
+// interpolated in x. Output rows that resample the same source rows (2, 4 or 8 in a row at
+// scales 2, 4 and 8 of the flow tensor) then only interpolate in y. The arithmetic is that of the
+// resize, x first: lerp(lerp(q00, q01, tx), lerp(q10, q11, tx), ty).
+struct LevelCol {
+  AxisTap tx;
+  int lo, hi;
+  float top[5], bot[5];
+};
+
+__device__ __forceinline__ void level_col_init(const IfFlowLevels& L, int j, int X, LevelCol& c) {
+  c.tx = resize_tap(X, L.inv[j], L.w[j]);
+  c.lo = -1;
+  c.hi = -1;
+}
+
+// Adds block j's contribution at padded row Y of column c (frame n) to the flow (4) and mask;
+// block 0 sets them. The threads of a warp share Y, so the refill branch is uniform.
+__device__ __forceinline__ void flow_step_col(const IfFlowLevels& L, int j, int n, int Y, LevelCol& c, float f[4],
+                                              float* mask) {
   const AxisTap ty = resize_tap(Y, L.inv[j], L.h[j]);
-  const AxisTap tx = resize_tap(X, L.inv[j], L.w[j]);
-  const float* base = L.t[j] + static_cast<size_t>(n) * L.h[j] * L.w[j] * 8;
-  const float* ra = base + static_cast<size_t>(ty.lo) * L.w[j] * 8;
-  const float* rb = base + static_cast<size_t>(ty.hi) * L.w[j] * 8;
-  float q[4][5];
-  const float* px[4] = {ra + tx.lo * 8, ra + tx.hi * 8, rb + tx.lo * 8, rb + tx.hi * 8};
+  if (ty.lo != c.lo || ty.hi != c.hi) {
+    const float* base = L.t[j] + static_cast<size_t>(n) * L.h[j] * L.w[j] * 8;
+    const float* ra = base + static_cast<size_t>(ty.lo) * L.w[j] * 8;
+    const float* rb = base + static_cast<size_t>(ty.hi) * L.w[j] * 8;
+    const float* px[4] = {ra + c.tx.lo * 8, ra + c.tx.hi * 8, rb + c.tx.lo * 8, rb + c.tx.hi * 8};
+    float q[4][5];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float4 u = __ldg(reinterpret_cast<const float4*>(px[k]));
-    q[k][0] = u.x;
-    q[k][1] = u.y;
-    q[k][2] = u.z;
-    q[k][3] = u.w;
-    q[k][4] = __ldg(px[k] + 4);
+    for (int k = 0; k < 4; ++k) {
+      const float4 u = __ldg(reinterpret_cast<const float4*>(px[k]));
+      q[k][0] = u.x;
+      q[k][1] = u.y;
+      q[k][2] = u.z;
+      q[k][3] = u.w;
+      q[k][4] = __ldg(px[k] + 4);
+    }
+#pragma unroll
+    for (int ch = 0; ch < 5; ++ch) {
+      c.top[ch] = lerp_rn(q[0][ch], q[1][ch], c.tx.t);
+      c.bot[ch] = lerp_rn(q[2][ch], q[3][ch], c.tx.t);
+    }
+    c.lo = ty.lo;
+    c.hi = ty.hi;
   }
   float v[5];
 #pragma unroll
-  for (int c = 0; c < 5; ++c) v[c] = lerp_rn(lerp_rn(q[0][c], q[1][c], tx.t), lerp_rn(q[2][c], q[3][c], tx.t), ty.t);
+  for (int ch = 0; ch < 5; ++ch) v[ch] = lerp_rn(c.top[ch], c.bot[ch], ty.t);
   if (j == 0) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) f[c] = __fmul_rn(v[c], L.mul[j]);
+    for (int ch = 0; ch < 4; ++ch) f[ch] = __fmul_rn(v[ch], L.mul[j]);
     *mask = v[4];
   } else {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) f[c] = __fadd_rn(f[c], __fmul_rn(v[c], L.mul[j]));
+    for (int ch = 0; ch < 4; ++ch) f[ch] = __fadd_rn(f[ch], __fmul_rn(v[ch], L.mul[j]));
     *mask = __fadd_rn(*mask, v[4]);
   }
 }
@@ -152,39 +177,33 @@ __device__ __forceinline__ void flow_step(const IfFlowLevels& L, int j, int n, i
 struct IfFlowField {
   float* f;
   int Hp, Wp;
-  __device__ __forceinline__ size_t at(int n, int c, int Y, int X) const {
-    return ((static_cast<size_t>(n) * 5 + c) * Hp + Y) * Wp + X;
+  __device__ __forceinline__ float* pixel(int n, int Y, int X) const {
+    return f + static_cast<size_t>(n) * 5 * Hp * Wp + static_cast<size_t>(Y) * Wp + X;
   }
+  __device__ __forceinline__ size_t plane() const { return static_cast<size_t>(Hp) * Wp; }
 };
 
-// Flow (4) and mask after blocks [0, K) at padded pixel (Y, X) of frame n (K >= 1).
-template <int K>
-__device__ __forceinline__ void flow_at(const IfFlowLevels& L, int n, int Y, int X, int Hp, int Wp, float f[4],
-                                        float* mask) {
-#pragma unroll
-  for (int j = 0; j < K; ++j) flow_step(L, j, n, Y, X, Hp, Wp, f, mask);
-}
-
-// The three channels of padded pixel (Y, X) of one padded frame.
-__device__ __forceinline__ void frame_rgb(const uint2* pad, const IfFrames& F, int n, int Y, int X, float c[3]) {
-  const uint2 q = __ldg(pad + (static_cast<size_t>(n) * F.Hp + Y) * F.Wp + X);
+// The three channels of pixel (Y, X) of one padded frame (`fr`: the frame's first pixel).
+__device__ __forceinline__ void frame_rgb(const uint2* fr, int Wp, int Y, int X, float c[3]) {
+  const uint2 q = __ldg(fr + (Y * Wp + X));
   const float2 rg = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
   c[0] = rg.x;
   c[1] = rg.y;
   c[2] = __low2float(*reinterpret_cast<const __half2*>(&q.y));
 }
 
-// Backward warp of the 3 channels of a padded frame at pixel (Y, X) by flow (fx, fy).
-__device__ __forceinline__ void warp3(const uint2* pad, const IfFrames& F, int n, int Y, int X, float fx, float fy,
+// Backward warp of the 3 channels of a padded frame (`fr`: its first pixel) at pixel (Y, X) by
+// flow (fx, fy).
+__device__ __forceinline__ void warp3(const uint2* fr, const IfFrames& F, int Y, int X, float fx, float fy,
                                       float out[3]) {
   const AxisTap tx = warp_tap(X, fx, F.Wp);
   const AxisTap ty = warp_tap(Y, fy, F.Hp);
   const float wx1 = __fsub_rn(1.0f, tx.t), wy1 = __fsub_rn(1.0f, ty.t);
   float a[3], b[3], d[3], e[3];
-  frame_rgb(pad, F, n, ty.lo, tx.lo, a);
-  frame_rgb(pad, F, n, ty.lo, tx.hi, b);
-  frame_rgb(pad, F, n, ty.hi, tx.lo, d);
-  frame_rgb(pad, F, n, ty.hi, tx.hi, e);
+  frame_rgb(fr, F.Wp, ty.lo, tx.lo, a);
+  frame_rgb(fr, F.Wp, ty.lo, tx.hi, b);
+  frame_rgb(fr, F.Wp, ty.hi, tx.lo, d);
+  frame_rgb(fr, F.Wp, ty.hi, tx.hi, e);
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
     // (a (1 - wx) + b wx) (1 - wy) + (d (1 - wx) + e wx) wy
@@ -194,113 +213,179 @@ __device__ __forceinline__ void warp3(const uint2* pad, const IfFrames& F, int n
   }
 }
 
-// The 12 input planes of block K >= 1 at padded full-resolution pixel (Y, X): warped frames (6),
-// timestep, mask, flow (4, not yet divided by the block scale). Block 3 also stores the flow.
+// The 12 input planes of block K >= 1 at padded full-resolution pixel (Y, X) of frame n: warped
+// frames (6), timestep, mask, flow (4, not yet divided by the block scale), the flow from the
+// column caches of blocks 0 .. K - 1. Block 3 also stores the flow.
 template <int K>
 __device__ __forceinline__ void block_planes(const IfFrames& F, const IfFlowLevels& L, const IfFlowField& FF, int n,
-                                             int Y, int X, float timestep, float v[12]) {
+                                             int Y, int X, LevelCol (&cols)[K], float timestep, float v[12]) {
   float f[4], mask;
-  flow_at<K>(L, n, Y, X, F.Hp, F.Wp, f, &mask);
-  if constexpr (K == kIfBlocks - 1) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) FF.f[FF.at(n, c, Y, X)] = f[c];
-    FF.f[FF.at(n, 4, Y, X)] = mask;
+  for (int j = 0; j < K; ++j) flow_step_col(L, j, n, Y, cols[j], f, &mask);
+  if constexpr (K == kIfBlocks - 1) {
+    float* p = FF.pixel(n, Y, X);
+    const size_t pl = FF.plane();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) p[c * pl] = f[c];
+    p[4 * pl] = mask;
   }
-  warp3(F.pad0, F, n, Y, X, f[0], f[1], v);
-  warp3(F.pad1, F, n, Y, X, f[2], f[3], v + 3);
+  const size_t frame = static_cast<size_t>(n) * F.Hp * F.Wp;
+  warp3(F.pad0 + frame, F, Y, X, f[0], f[1], v);
+  warp3(F.pad1 + frame, F, Y, X, f[2], f[3], v + 3);
   v[6] = timestep;
   v[7] = mask;
 #pragma unroll
   for (int c = 0; c < 4; ++c) v[8 + c] = f[c];
 }
 
+// Output rows per thread in the glue kernels: a thread walks a run of rows down one column (runs
+// never cross frames), so the flow caches are refilled once per source row pair.
+constexpr int kGlueRunRows = 8;
+
+// Block K's input row run: rows per run at the block's scale (8 full-resolution rows).
+template <int K>
+constexpr int glue_run() {
+  return kGlueRunRows / if_scale(K) > 0 ? kGlueRunRows / if_scale(K) : 1;
+}
+
+// Stores the 16 planes of one output pixel as two FP16 chunks.
+__device__ __forceinline__ void store_chunks(uint8_t* row, int wo, int ox, const float v[16]) {
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch) {
+    uint4 o;
+    __half2 h0 = __floats2half2_rn(v[8 * ch + 0], v[8 * ch + 1]);
+    __half2 h1 = __floats2half2_rn(v[8 * ch + 2], v[8 * ch + 3]);
+    __half2 h2 = __floats2half2_rn(v[8 * ch + 4], v[8 * ch + 5]);
+    __half2 h3 = __floats2half2_rn(v[8 * ch + 6], v[8 * ch + 7]);
+    o.x = *reinterpret_cast<uint32_t*>(&h0);
+    o.y = *reinterpret_cast<uint32_t*>(&h1);
+    o.z = *reinterpret_cast<uint32_t*>(&h2);
+    o.w = *reinterpret_cast<uint32_t*>(&h3);
+    *reinterpret_cast<uint4*>(row + (static_cast<size_t>(ch) * wo + ox) * 16) = o;
+  }
+}
+
 // Input of block K as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used):
 // the block's planes resized to 1/s (not for s = 1), the flow planes then divided by s. One
-// instantiation per block, so that every plane array stays in registers.
+// instantiation per block, so that every plane array stays in registers; 64 registers a thread
+// (4 blocks of 256 per SM: measured 19-27 % faster than 80-88 registers at 2-3 blocks, no spills).
+//  * s = 1: one thread per column, walking glue_run<K>() rows;
+//  * s > 1: two threads per output column, one per resize sample column (lo, hi); each computes
+//    the planes at its column for both sample rows, and the pair exchanges them by a shuffle so
+//    that both hold lerp(q(x lo), q(x hi), tx) for each row; the even thread stores.
 template <int K>
-__global__ void ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, float timestep,
-                                         uint8_t* __restrict__ out) {
-  constexpr int k = K;
+__global__ void __launch_bounds__(kGlueThreads, 4)
+    ifnet_block_input_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, float timestep,
+                             uint8_t* __restrict__ out) {
   constexpr int s = if_scale(K);
+  constexpr int R = glue_run<K>();
+  constexpr int nc = K == 0 ? 7 : 12;
   const int ho = F.Hp / s, wo = F.Wp / s;
-  const int ox = blockIdx.x * blockDim.x + threadIdx.x;
-  if (ox >= wo) return;
-  for (int r = blockIdx.y; r < batch * ho; r += gridDim.y) {
-    const int n = r / ho;
-    const int oy = r - n * ho;
-    float v[16];
+  const int runs = (ho + R - 1) / R;
+  if constexpr (s == 1) {
+    const int X = blockIdx.x * blockDim.x + threadIdx.x;
+    if (X >= wo) return;
+    LevelCol cols[K];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) v[c] = 0.0f;
-    constexpr int nc = k == 0 ? 7 : 12;
-    if constexpr (s == 1) {
-      block_planes<K>(F, L, FF, n, oy, ox, timestep, v);
-    } else {
-      const AxisTap ty = resize_tap(oy, static_cast<float>(s), F.Hp);
-      const AxisTap tx = resize_tap(ox, static_cast<float>(s), F.Wp);
-      float q[4][12];
-      const int ys[2] = {ty.lo, ty.hi}, xs[2] = {tx.lo, tx.hi};
+    for (int j = 0; j < K; ++j) level_col_init(L, j, X, cols[j]);
+    for (int r = blockIdx.y; r < batch * runs; r += gridDim.y) {
+      const int n = r / runs;
+      const int y0 = (r - n * runs) * R;
 #pragma unroll
-      for (int yy = 0; yy < 2; ++yy)
+      for (int j = 0; j < K; ++j) cols[j].lo = -1;
+      for (int y = y0; y < y0 + R && y < ho; ++y) {
+        float v[16];
 #pragma unroll
-        for (int xx = 0; xx < 2; ++xx) {
-          float* p = q[yy * 2 + xx];
-          if constexpr (k == 0) {
-            frame_rgb(F.pad0, F, n, ys[yy], xs[xx], p);
-            frame_rgb(F.pad1, F, n, ys[yy], xs[xx], p + 3);
-            p[6] = timestep;
+        for (int c = 12; c < 16; ++c) v[c] = 0.0f;
+        block_planes<K>(F, L, FF, n, y, X, cols, timestep, v);
+        // the flow planes divided by s = 1: unchanged
+        store_chunks(out + (static_cast<size_t>(n) * ho + y) * 2 * wo * 16, wo, X, v);
+      }
+    }
+  } else {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int ox = t >> 1;
+    const int side = t & 1;
+    const bool live = ox < wo;  // both threads of a pair agree; the shuffles need every lane
+    const AxisTap tx = resize_tap(live ? ox : wo - 1, static_cast<float>(s), F.Wp);
+    const int X = side ? tx.hi : tx.lo;
+    LevelCol cols[K > 0 ? K : 1];
+#pragma unroll
+    for (int j = 0; j < K; ++j) level_col_init(L, j, X, cols[j]);
+    const float inv = __fdiv_rn(1.0f, static_cast<float>(s));
+    for (int r = blockIdx.y; r < batch * runs; r += gridDim.y) {
+      const int n = r / runs;
+      const int y0 = (r - n * runs) * R;
+#pragma unroll
+      for (int j = 0; j < K; ++j) cols[j].lo = -1;
+      for (int oy = y0; oy < y0 + R && oy < ho; ++oy) {
+        const AxisTap ty = resize_tap(oy, static_cast<float>(s), F.Hp);
+        float h[2][12];
+#pragma unroll
+        for (int yy = 0; yy < 2; ++yy) {
+          const int Y = yy ? ty.hi : ty.lo;
+          float q[12];
+          if constexpr (K == 0) {
+            const size_t frame = static_cast<size_t>(n) * F.Hp * F.Wp;
+            frame_rgb(F.pad0 + frame, F.Wp, Y, X, q);
+            frame_rgb(F.pad1 + frame, F.Wp, Y, X, q + 3);
+            q[6] = timestep;
           } else {
-            block_planes<K>(F, L, FF, n, ys[yy], xs[xx], timestep, p);
+            block_planes<K>(F, L, FF, n, Y, X, cols, timestep, q);
+          }
+#pragma unroll
+          for (int c = 0; c < nc; ++c) {
+            const float p = __shfl_xor_sync(0xffffffffu, q[c], 1);
+            h[yy][c] = side ? lerp_rn(p, q[c], tx.t) : lerp_rn(q[c], p, tx.t);
           }
         }
+        float v[16];
 #pragma unroll
-      for (int c = 0; c < nc; ++c)
-        v[c] = lerp_rn(lerp_rn(q[0][c], q[1][c], tx.t), lerp_rn(q[2][c], q[3][c], tx.t), ty.t);
-    }
-    if constexpr (k > 0) {
-      const float inv = __fdiv_rn(1.0f, static_cast<float>(s));
+        for (int c = 0; c < 16; ++c) v[c] = c < nc ? lerp_rn(h[0][c], h[1][c], ty.t) : 0.0f;
+        if constexpr (K > 0) {
 #pragma unroll
-      for (int c = 8; c < 12; ++c) v[c] = __fmul_rn(v[c], inv);
-    }
-    uint8_t* row = out + (static_cast<size_t>(n) * ho + oy) * 2 * wo * 16;
-#pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-      uint4 o;
-      __half2 h0 = __floats2half2_rn(v[8 * ch + 0], v[8 * ch + 1]);
-      __half2 h1 = __floats2half2_rn(v[8 * ch + 2], v[8 * ch + 3]);
-      __half2 h2 = __floats2half2_rn(v[8 * ch + 4], v[8 * ch + 5]);
-      __half2 h3 = __floats2half2_rn(v[8 * ch + 6], v[8 * ch + 7]);
-      o.x = *reinterpret_cast<uint32_t*>(&h0);
-      o.y = *reinterpret_cast<uint32_t*>(&h1);
-      o.z = *reinterpret_cast<uint32_t*>(&h2);
-      o.w = *reinterpret_cast<uint32_t*>(&h3);
-      *reinterpret_cast<uint4*>(row + (static_cast<size_t>(ch) * wo + ox) * 16) = o;
+          for (int c = 8; c < 12; ++c) v[c] = __fmul_rn(v[c], inv);
+        }
+        if (live && side == 0) store_chunks(out + (static_cast<size_t>(n) * ho + oy) * 2 * wo * 16, wo, ox, v);
+      }
     }
   }
 }
 
 // The interpolated frame: warp both frames by the final flow, blend with sigmoid(mask), crop the
-// window: out = w0 * m + w1 * (1 - m), NCHW FP16 [n][3][H][W].
+// window: out = w0 * m + w1 * (1 - m), NCHW FP16 [n][3][H][W]. One thread per column walking
+// kGlueRunRows rows, with block 3's flow resize cached along the column.
 __global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, __half* __restrict__ out) {
   const int x = blockIdx.x * blockDim.x + threadIdx.x;
   if (x >= F.W) return;
-  for (int r = blockIdx.y; r < batch * F.H; r += gridDim.y) {
-    const int n = r / F.H;
-    const int y = r - n * F.H;
-    const int Y = y + F.top, X = x + F.left;
-    float f[4], mask;
+  const int X = x + F.left;
+  LevelCol col;
+  level_col_init(L, kIfBlocks - 1, X, col);
+  const int runs = (F.H + kGlueRunRows - 1) / kGlueRunRows;
+  const size_t pl = FF.plane();
+  for (int r = blockIdx.y; r < batch * runs; r += gridDim.y) {
+    const int n = r / runs;
+    const int y0 = (r - n * runs) * kGlueRunRows;
+    col.lo = -1;
+    const size_t frame = static_cast<size_t>(n) * F.Hp * F.Wp;
+    for (int y = y0; y < y0 + kGlueRunRows && y < F.H; ++y) {
+      const int Y = y + F.top;
+      const float* p = FF.pixel(n, Y, X);
+      float f[4], mask;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) f[c] = __ldg(FF.f + FF.at(n, c, Y, X));
-    mask = __ldg(FF.f + FF.at(n, 4, Y, X));
-    flow_step(L, kIfBlocks - 1, n, Y, X, F.Hp, F.Wp, f, &mask);
-    float w0[3], w1[3];
-    warp3(F.pad0, F, n, Y, X, f[0], f[1], w0);
-    warp3(F.pad1, F, n, Y, X, f[2], f[3], w1);
-    const float m = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-mask)));
-    const float m1 = __fsub_rn(1.0f, m);
+      for (int c = 0; c < 4; ++c) f[c] = __ldg(p + c * pl);
+      mask = __ldg(p + 4 * pl);
+      flow_step_col(L, kIfBlocks - 1, n, Y, col, f, &mask);
+      float w0[3], w1[3];
+      warp3(F.pad0 + frame, F, Y, X, f[0], f[1], w0);
+      warp3(F.pad1 + frame, F, Y, X, f[2], f[3], w1);
+      const float m = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-mask)));
+      const float m1 = __fsub_rn(1.0f, m);
+      __half* o = out + (static_cast<size_t>(n) * 3 * F.H + y) * F.W + x;
 #pragma unroll
-    for (int c = 0; c < 3; ++c)
-      out[((static_cast<size_t>(n) * 3 + c) * F.H + y) * F.W + x] =
-          __float2half_rn(__fadd_rn(__fmul_rn(w0[c], m), __fmul_rn(w1[c], m1)));
+      for (int c = 0; c < 3; ++c)
+        o[static_cast<size_t>(c) * F.H * F.W] = __float2half_rn(__fadd_rn(__fmul_rn(w0[c], m), __fmul_rn(w1[c], m1)));
+    }
   }
 }
 

@@ -272,7 +272,7 @@ Status IfnetNet::create(const std::vector<float>& params, int max_batch, int H, 
   left_ = ((Wp_ - W) / 2) & ~1;
   KB2_TRY(err_.alloc(sizeof(int)));
   KB2_CUDA(cudaMemset(err_.ptr, 0, sizeof(int)));
-  k_glue_ = timer_.kind("ifnet.glue");
+  for (int k = 0; k < kIfBlocks; ++k) k_glue_[k] = timer_.kind(("ifnet.glue.b" + std::to_string(k)).c_str());
   const int k_c0a = timer_.kind("ifnet.conv0a"), k_c0b = timer_.kind("ifnet.conv0b");
   const int k_res = timer_.kind("ifnet.res"), k_ct = timer_.kind("ifnet.convt");
   k_blend_ = timer_.kind("ifnet.blend");
@@ -401,7 +401,7 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
   uint2* pad0 = pad_.as<uint2>();
   IfFrames F{static_cast<const __half*>(img0), static_cast<const __half*>(img1), H_, W_, Hp_, Wp_, top_, left_, pad0,
              pad0 + static_cast<size_t>(max_batch_) * Hp_ * Wp_};
-  // a grid of rows for the glue kernels (ifnet_glue.cuh): about 16 blocks per SM, each walking rows
+  // a grid of row runs for the glue kernels (ifnet_glue.cuh): about 16 blocks per SM, each walking runs
   const int sms = num_sms();
   auto row_grid = [sms](int width, int rows) {
     const int bx = (width + kGlueThreads - 1) / kGlueThreads;
@@ -429,7 +429,9 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
   for (int k = 0; k < kIfBlocks; ++k) {
     const int s = if_scale(k);
     const long long px = static_cast<long long>(batch) * (Hp_ / s) * (Wp_ / s);
-    const dim3 g = row_grid(Wp_ / s, batch * (Hp_ / s));
+    // s = 1: a thread per column; s > 1: two per output column (ifnet_glue.cuh); runs of rows
+    const int run = k == 0 ? glue_run<0>() : k == 1 ? glue_run<1>() : k == 2 ? glue_run<2>() : glue_run<3>();
+    const dim3 g = row_grid((s == 1 ? 1 : 2) * (Wp_ / s), batch * ((Hp_ / s + run - 1) / run));
     constexpr int T = kGlueThreads;
     KB2_TRY(timer_.begin(stream));
     switch (k) {
@@ -439,7 +441,7 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
       default: ifnet_block_input_kernel<3><<<g, T, 0, stream>>>(F, L, FF, batch, timestep_, x_[k]->ptr); break;
     }
     KB2_CUDA(cudaGetLastError());
-    KB2_TRY(timer_.end(k_glue_, 0.0, px * 32.0, stream));
+    KB2_TRY(timer_.end(k_glue_[k], 0.0, px * 32.0, stream));
     for (int i = 0; i < per_block; ++i) {
       IfLayer& l = *layers_[k * per_block + i];
       const double opx = static_cast<double>(batch) * l.args.h_out * l.args.w_out;
@@ -450,7 +452,8 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
   }
   const long long px = static_cast<long long>(batch) * H_ * W_;
   KB2_TRY(timer_.begin(stream));
-  ifnet_blend_kernel<<<row_grid(W_, batch * H_), kGlueThreads, 0, stream>>>(F, L, FF, batch, static_cast<__half*>(out));
+  ifnet_blend_kernel<<<row_grid(W_, batch * ((H_ + kGlueRunRows - 1) / kGlueRunRows)), kGlueThreads, 0, stream>>>(
+      F, L, FF, batch, static_cast<__half*>(out));
   KB2_CUDA(cudaGetLastError());
   KB2_TRY(timer_.end(k_blend_, 0.0, px * (20.0 + 12.0 + 6.0), stream));
   return Status::Ok();

@@ -51,7 +51,7 @@ class IfnetNet {
   DeviceBuffer flow_full_;                        // flow / mask after blocks 0-2, FP32 [n][5][Hp][Wp]
   DeviceBuffer pad_;                              // both frames, padded RGBx FP16 pixels [2][n][Hp][Wp]
   LayerTimer timer_;
-  int k_glue_ = 0, k_blend_ = 0, k_pad_ = 0;
+  int k_glue_[4] = {}, k_blend_ = 0, k_pad_ = 0;
 };
 
 // Bilinear backward-warp taps of a flow field [n][2][h][w] (FP32, device): x0, x1, y0, y1 as int32
