@@ -456,3 +456,110 @@ def psnr(a, b):
 
 def max_abs_clamped(a, b):
     return float(np.max(np.abs(clamp01(a) - clamp01(b))))
+
+
+# --------------------------------------------------------------------------------------------
+# AnimeJaNai "unshuffle" SPAN and its .span8 package (the reference's span_fp8 format)
+# --------------------------------------------------------------------------------------------
+# Package layout (src/gpu/span_fp8/package.h:1-17, package.cpp:143-198), little-endian:
+#   header 40 bytes: "AJPSPAN8", version u32 (2), blocks u32 (2..8), stored channels u32 (64),
+#   real channels u32 (48 or 64), payload bytes u64, CRC-32 of the payload u32, flags u32
+#   (bit 0 f16 accumulators outside the blocks, bit 1 FP16 blocks, bit 2 f32 sums with bit 1);
+#   payload: 1 + 3 * blocks f32 activation scales, then conv_1 [64][3][3][16], per block c1, c2,
+#   c3 [64][3][3][64] and the 1x1 attention [64][64], conv_cat [64][256], to_pixel [48][3][3][64];
+#   each conv's FP16 weights ([out][ky][kx][in]) followed by its f32 biases.
+SPAN8_STORED = 64
+SPAN8_IN = 16       # conv_1 reads the 12 unshuffled channels padded to 16
+SPAN8_PIXEL = 48    # 3 planes x 4 x 4 before DepthToSpace(4)
+SPAN8_HEADER = 40
+
+
+def span8_init(blocks=5, real=48, seed=11, gain=0.7, bias_std=0.02, pixel_gain=0.2, pixel_bias=0.5):
+    """Seeded package contents in the stored layout (channels beyond `real` zero, as the
+    reference stores a b5f48 in 64 channels, package.h:11-13): Kaiming-normal weights (damped by
+    `gain`) rounded to FP16, small normal biases, unit scales, the FP16 flag set. to_pixel is scaled
+    by `pixel_gain` around `pixel_bias`, so that most output values fall inside [0, 1] as an
+    image's do and the clamped comparison sees them."""
+    rng = np.random.default_rng(seed)
+
+    def conv(outs, taps, ins_real, ins_stored, groups=1, out_real=None):
+        out_real = outs if out_real is None else out_real
+        w = np.zeros((outs, taps, groups, ins_stored), np.float32)
+        fan = taps * groups * ins_real
+        w[:out_real, :, :, :ins_real] = kaiming(rng, (out_real, taps, groups, ins_real), fan, gain=gain * math.sqrt(2.0))
+        b = np.zeros(outs, np.float32)
+        b[:out_real] = (rng.standard_normal(out_real) * bias_std).astype(np.float32)
+        return {"w": w.reshape(outs, taps, groups * ins_stored).astype(np.float16).astype(np.float32), "b": b}
+
+    p = {"blocks": blocks, "real": real, "flags": 2, "scales": np.ones(1 + 3 * blocks, np.float32)}
+    p["first"] = conv(SPAN8_STORED, 9, 12, SPAN8_IN, out_real=real)
+    p["block"] = []
+    for _ in range(blocks):
+        blk = {k: conv(SPAN8_STORED, 9, real, SPAN8_STORED, out_real=real) for k in ("c1", "c2", "c3")}
+        blk["att"] = conv(SPAN8_STORED, 1, real, SPAN8_STORED, out_real=real)
+        p["block"].append(blk)
+    p["concat"] = conv(SPAN8_STORED, 1, real, SPAN8_STORED, groups=4, out_real=real)
+    p["pixel"] = conv(SPAN8_PIXEL, 9, real, SPAN8_STORED)
+    p["pixel"]["w"] = (p["pixel"]["w"] * np.float32(pixel_gain)).astype(np.float16).astype(np.float32)
+    p["pixel"]["b"] = (p["pixel"]["b"] + np.float32(pixel_bias)).astype(np.float32)
+    return p
+
+
+def _crc32(payload):
+    import zlib
+    return zlib.crc32(payload) & 0xFFFFFFFF
+
+
+def span8_package(p, version=2):
+    """The .span8 bytes of package contents `p` (the writer of package.cpp:200-215)."""
+    import struct
+    body = bytearray()
+    body += np.asarray(p["scales"], "<f4").tobytes()
+
+    def put(c):
+        body.extend(np.asarray(c["w"], np.float32).astype("<f2").tobytes())
+        body.extend(np.asarray(c["b"], "<f4").tobytes())
+
+    put(p["first"])
+    for blk in p["block"]:
+        for k in ("c1", "c2", "c3", "att"):
+            put(blk[k])
+    put(p["concat"])
+    put(p["pixel"])
+    head = b"AJPSPAN8" + struct.pack("<IIIIQII", version, p["blocks"], SPAN8_STORED, p["real"], len(body),
+                                     _crc32(bytes(body)), p["flags"])
+    return bytes(head) + bytes(body)
+
+
+def _span8_conv(x, c, real_in, real_out, side, groups=1, stored=SPAN8_STORED):
+    """One package conv on the real channels: weights [out][ky*kx][groups*stored] -> OIHW."""
+    w = np.asarray(c["w"], np.float32).reshape(c["w"].shape[0], side * side, groups, stored)
+    w = w[:real_out, :, :, :real_in].reshape(real_out, side, side, groups * real_in).transpose(0, 3, 1, 2)
+    return conv2d(x, np.ascontiguousarray(w), c["b"][:real_out], pad=side // 2)
+
+
+def span8_forward(x, p):
+    """FP32 forward of the unshuffle SPAN (src/gpu/span_fp8/forward.cpp:144-166): 2x2 unshuffle
+    (channel c*4 + dy*2 + dx), conv_1, blocks (c1, ReLU, c2, ReLU, c3; out (x + c3) * tanh(att(c3))),
+    conv_cat over (conv_1 out, last block out, first block out, the last block's first ReLU),
+    to_pixel, DepthToSpace(4). x: [n,3,h,w], h and w even; returns [n,3,2h,2w]."""
+    x = np.asarray(x, np.float32)
+    n, _, h, w = x.shape
+    ch = p["real"]
+    u = x.reshape(n, 3, h // 2, 2, w // 2, 2).transpose(0, 1, 3, 5, 2, 4).reshape(n, 12, h // 2, w // 2)
+    first = _span8_conv(u, p["first"], 12, ch, 3, stored=SPAN8_IN)
+    cur = first
+    first_block = last_relu = None
+    for b, blk in enumerate(p["block"]):
+        r1 = np.maximum(_span8_conv(cur, blk["c1"], ch, ch, 3), 0.0).astype(np.float32)
+        r2 = np.maximum(_span8_conv(r1, blk["c2"], ch, ch, 3), 0.0).astype(np.float32)
+        c3 = _span8_conv(r2, blk["c3"], ch, ch, 3)
+        att = _span8_conv(c3, blk["att"], ch, ch, 1)
+        cur = ((cur + c3) * np.tanh(att)).astype(np.float32)
+        if b == 0:
+            first_block = cur
+        if b + 1 == len(p["block"]):
+            last_relu = r1
+    cat = _span8_conv(np.concatenate([first, cur, first_block, last_relu], axis=1), p["concat"], ch, ch, 1, groups=4)
+    pix = _span8_conv(cat, p["pixel"], ch, SPAN8_PIXEL, 3)
+    return pixel_shuffle(pix, 4)

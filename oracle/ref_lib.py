@@ -68,3 +68,46 @@ def ifnet_forward(img0, img1, timestep, flat_params):
     if rc != 0:
         raise RuntimeError(f"kref_ifnet_forward: {rc} {lib().kref_last_error().decode(errors='replace')}")
     return out
+
+
+def _span8_bind(L):
+    if getattr(L, "_span8_bound", False):
+        return L
+    _u8 = ctypes.POINTER(ctypes.c_ubyte)
+    L.kref_span8_last_error.restype = ctypes.c_char_p
+    L.kref_span8_parse.argtypes = [_u8, ctypes.c_long, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                   ctypes.POINTER(ctypes.c_int)]
+    L.kref_span8_parse.restype = ctypes.c_int
+    L.kref_span8_forward.argtypes = [_u8, ctypes.c_long, _fp, ctypes.c_int, ctypes.c_int, _fp]
+    L.kref_span8_forward.restype = ctypes.c_int
+    L._span8_bound = True
+    return L
+
+
+def span8_parse(package: bytes):
+    """The reference's .span8 reader (package.cpp:143): (0, blocks, real, fp16) when it accepts the
+    bytes, else (its refusal code + 1, message)."""
+    L = _span8_bind(lib())
+    buf = (ctypes.c_ubyte * len(package)).from_buffer_copy(package)
+    b, r, f = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    rc = L.kref_span8_parse(buf, len(package), ctypes.byref(b), ctypes.byref(r), ctypes.byref(f))
+    if rc != 0:
+        return rc, L.kref_span8_last_error().decode(errors="replace")
+    return 0, b.value, r.value, f.value
+
+
+def span8_forward(package: bytes, x):
+    """The reference's FP32 unshuffle-SPAN forward (forward.cpp:144) of x [n,3,h,w]."""
+    L = _span8_bind(lib())
+    x = np.ascontiguousarray(x, np.float32)
+    n, _, h, w = x.shape
+    buf = (ctypes.c_ubyte * len(package)).from_buffer_copy(package)
+    out = np.zeros((n, 3, 2 * h, 2 * w), np.float32)
+    for i in range(n):
+        xi = np.ascontiguousarray(x[i])
+        oi = np.zeros((3, 2 * h, 2 * w), np.float32)
+        rc = L.kref_span8_forward(buf, len(package), _ptr(xi), h, w, _ptr(oi))
+        if rc != 0:
+            raise RuntimeError(f"kref_span8_forward: {rc} {L.kref_span8_last_error().decode(errors='replace')}")
+        out[i] = oi
+    return out

@@ -745,11 +745,11 @@ struct PairRowCtx {
   int* err;
 };
 
-// Input ring of the pair kernel: 12 row slots, or 6 for 64-channel layers (twelve 16 KB slots and
-// the weights do not fit in shared memory).
-template <int kCoutPad>
+// Input ring of the pair kernel: 12 row slots, or 6 for rows of 12 K steps (64 FP16 input
+// channels: twelve 16 KB slots and the weights do not fit in shared memory).
+template <int kNK>
 constexpr uint32_t pair_ring() {
-  return kCoutPad == 64 ? 6u : 12u;
+  return kNK == 12 ? 6u : 12u;
 }
 
 // Input row k of a 12-row period. The accumulator ring has 6 slots and the input ring 12 or 6, so
@@ -759,7 +759,7 @@ constexpr uint32_t pair_ring() {
 // its two asm blocks.
 template <bool kFp8, int kCoutPad, int kNK, int kK>
 __device__ __forceinline__ bool pair_row_k(const PairRowCtx<kNK>& c, uint32_t ph, uint32_t& pre) {
-  constexpr uint32_t kRing = pair_ring<kCoutPad>();
+  constexpr uint32_t kRing = pair_ring<kNK>();
   constexpr uint32_t kIn = kK % kRing;
   constexpr uint32_t kInPh = kRing == 6u && kK >= 6 ? 1u : 0u;
   constexpr uint32_t kSlot = kK % 6;
@@ -837,7 +837,7 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
     int n, pair, y0, y1;
     while (sp.next(a, n, pair, y0, y1)) total += static_cast<uint32_t>(y1 - y0 + 2 + pair_pad(y1 - y0));
   }
-  constexpr uint32_t kRing = pair_ring<kCoutPad>();
+  constexpr uint32_t kRing = pair_ring<kNK>();
   if (a.ring != kRing) return;  // the host sizes the ring by pair_ring
   uint32_t ph = 0;   // input ring phase of the current period (12 slots; 6 slots: always 0)
   uint32_t pre = 0;  // next row's barriers found complete by the previous row: 1 = input, 2 = slot
@@ -979,14 +979,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
         // ---------------------------------------------------------------- MMA issuer (pair)
         if (wait_bar(wbar, 0, a.err, kErrWaitMma) && wait_bar(wpeer, 0, a.err, kErrWaitMma)) {
           const PairIssue is{a, smem_u32(ring), smem_u32(sw), smem_u32(zero_b), tmem_base, s_k, full, done, slot_free};
+          // rows of K steps as the host admits them (conv_layer.cu pair_admits): 64 output channels
+          // 12 or 3, FP16 48: 12, 9, 5, 3 or 2 (no 12 for E4M3 or 16 outputs)
           if constexpr (kCoutPad == 64) {
-            pair_issue<kFp8, kCoutPad, 12>(is);  // the host admits 12 K steps only (FP16, 64 channels)
+            if (a.n_ksteps == 12) pair_issue<kFp8, kCoutPad, 12>(is);
+            else pair_issue<kFp8, kCoutPad, 3>(is);
           } else {
             switch (a.n_ksteps) {
+              case 12:
+                if constexpr (!kFp8 && kCoutPad == 48) pair_issue<kFp8, kCoutPad, 12>(is);
+                break;
               case 9: pair_issue<kFp8, kCoutPad, 9>(is); break;
               case 5: pair_issue<kFp8, kCoutPad, 5>(is); break;
               case 3: pair_issue<kFp8, kCoutPad, 3>(is); break;
-              default: pair_issue<kFp8, kCoutPad, 2>(is); break;  // the host admits 2, 3, 5 or 9 K steps
+              default: pair_issue<kFp8, kCoutPad, 2>(is); break;
             }
           }
         }

@@ -112,14 +112,28 @@ const KernelEntry kKernels[] = {
     KB2_PAIRED(true, 48, kEpiSpanAttn, kOutF16Chunk),
     // the IFNet residual convs of 64 channels (ifnet_net.cu): pair kernel only
     KB2_PAIRED(false, 64, kEpiResPrelu, kOutF16Chunk),
+    // the unshuffle SPAN (span8_net.cu): ReLU convs (PReLU, slope 0), c3 and conv_1 at 64
+    // channels, to_pixel with DepthToSpace(4), the 1x1 attention with its tanh gate, conv_cat at 64
+    KB2_PAIRED(false, 48, kEpiPrelu, kOutF16Chunk),
+    KB2_PAIRED(false, 64, kEpiPrelu, kOutF16Chunk),
+    KB2_PAIRED(false, 64, kEpiBias, kOutF16Chunk),
+    KB2_PAIRED(false, 48, kEpiBias, kOutPixShuf4),
+    KB2_KERNEL(false, 48, kEpiTanhGate, kOutF16Chunk),
+    KB2_KERNEL(false, 64, kEpiTanhGate, kOutF16Chunk),
+    KB2_KERNEL(false, 64, kEpiBias, kOutF16Chunk),
 };
 
 bool wants_stacked(const ConvSpec& s) {
   return s.taps == 9 && s.n_sources == 1 && (s.n_pad == 48 || s.n_pad == 16 || s.n_pad == 64);
 }
 
-// K steps per input row the pair kernel runs (conv3p.cuh): 2, 3, 5 or 9 below 64 channels, 12 at 64
-bool pair_admits(int n_pad, int nk) { return n_pad == 64 ? nk == 12 : (nk == 2 || nk == 3 || nk == 5 || nk == 9); }
+// K steps per input row the pair kernel runs (conv3p.cuh): 64 output channels 12 or 3; 48 channels
+// 2, 3, 5, 9, or 12 in FP16 (64 FP16 inputs); 16 channels 2, 3, 5 or 9
+bool pair_admits(const ConvSpec& s, int nk) {
+  if (s.n_pad == 64) return !s.fp8 && (nk == 12 || nk == 3);
+  if (nk == 12) return !s.fp8 && s.n_pad == 48;
+  return nk == 2 || nk == 3 || nk == 5 || nk == 9;
+}
 
 const KernelEntry* find_kernel(const ConvSpec& s, int kind) {
   for (const KernelEntry& k : kKernels)
@@ -180,7 +194,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     // rows of 2, 3, 5, 9 (or 12 at 64 channels) K steps run on the pair kernel (one MMA for two SMs)
     const int nk = static_cast<int>(steps.size());
     const KernelEntry* kp = find_kernel(s, kKindPaired);
-    if ((kPairedStack || k == nullptr) && kp != nullptr && pair_admits(s.n_pad, nk)) {
+    if ((kPairedStack || k == nullptr) && kp != nullptr && pair_admits(s, nk)) {
       kind = kKindPaired;
       k = kp;
     }
@@ -357,7 +371,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     if (!one_per_sm && !stacked && ring < min_ring + 2) ring = fit(227u * 1024u);  // wide slots: one block per SM
     ring = std::min(ring, 12);
     // the pair issuer's ring is fixed by its 12-row periods (checked against shared memory below)
-    if (paired) ring = static_cast<int>(s.n_pad == 64 ? pair_ring<64>() : pair_ring<48>());
+    if (paired) ring = static_cast<int>(steps.size() == 12 ? pair_ring<12>() : pair_ring<9>());
     a.ring = static_cast<uint32_t>(std::max(ring, min_ring));
   }
   smem = a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (stacked ? kStackSmemExtra : kConvSmemExtra);
@@ -410,7 +424,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
 }
 
 Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
-                         float res_scale, void* out2, int res_chunks) const {
+                         float res_scale, void* out2, int res_chunks, const void* residual2) const {
   const KernelEntry* k = find_kernel(spec, kind);
   if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no kernel");
   const bool paired = kind == kKindPaired;
@@ -420,6 +434,7 @@ Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* 
   a.out = static_cast<uint8_t*>(out);
   a.out2 = static_cast<uint8_t*>(out2);
   a.residual = static_cast<const uint8_t*>(residual);
+  a.residual2 = static_cast<const uint8_t*>(residual2);
   a.res_fp8 = spec.fp8 ? 1 : 0;
   a.res_chunks = res_chunks;
   a.out_inv_scale = out_inv_scale;

@@ -35,9 +35,10 @@ struct ConvLayer {
   // the input tensors (FP8 only; folded into the per-output-channel weight scales).
   Status build(const ConvSpec& s, const float* W, const float* b, const float* prelu_slope,
                const float* act_scales, const ChunkedTensor* const* inputs, int* err_word);
-  // residual / out: device pointers for this launch (residual may be null).
+  // residual / out: device pointers for this launch (residual may be null); residual2: the second
+  // addend of kEpiTanhGate.
   Status launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
-                float res_scale, void* out2 = nullptr, int res_chunks = 0) const;
+                float res_scale, void* out2 = nullptr, int res_chunks = 0, const void* residual2 = nullptr) const;
 };
 
 int num_sms();

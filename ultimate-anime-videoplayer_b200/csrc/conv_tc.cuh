@@ -52,6 +52,7 @@ enum Epi : int {
   kEpiSpanAttn = 2,  // (v + x) * (sigmoid(v) - 0.5), x = the block input (residual tensor)
   kEpiPrelu = 3,     // PReLU(v)
   kEpiResPrelu = 4,  // PReLU(v + residual)
+  kEpiTanhGate = 5,  // (residual + residual2) * tanh(v): the unshuffle SPAN's block end (x + c3) * tanh(att)
 };
 
 enum OutFmt : int {
@@ -59,6 +60,7 @@ enum OutFmt : int {
   kOutE4m3Chunk = 1,  // [n][y][C/16][x][16] e4m3, value * out_inv_scale
   kOutPixShuf2 = 2,   // NCHW half [n][3][2H][2W], DepthToSpace(2, CRD) of 12 channels
   kOutF16E4m3 = 3,    // both: half chunks to `out`, E4M3 chunks (value * out_inv_scale) to `out2`
+  kOutPixShuf4 = 4,   // NCHW half [n][3][4H][4W], DepthToSpace(4, CRD) of 48 channels
 };
 
 struct KStep {
@@ -92,6 +94,7 @@ struct ConvArgs {
   float out_inv_scale;      // E4M3 output: 1 / scale
   float res_scale;          // E4M3 residual dequantisation scale
   const uint8_t* residual;  // same pixels and channels as the output, chunked
+  const uint8_t* residual2;  // kEpiTanhGate: the second addend (FP16 chunks like `residual`)
   int res_fp8;              // residual chunk format: 0 = f16, 1 = e4m3
   int res_chunks;           // chunks per residual pixel
   uint8_t* out;
@@ -204,6 +207,25 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
     }
   }
 
+  if constexpr (kEpi == kEpiTanhGate) {
+    // (x + c3) * tanh(att): both addends FP16 chunks of the same pixel and channels
+#pragma unroll
+    for (int g = 0; g < kCols / 8; ++g) {
+      const size_t at = ((pix_row * a.res_chunks + (col0 + 8 * g) / 8) * a.W + x) * 16;
+      const uint4 qa = __ldg(reinterpret_cast<const uint4*>(a.residual + at));
+      const uint4 qb = __ldg(reinterpret_cast<const uint4*>(a.residual2 + at));
+      const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w};
+      const uint32_t wb[4] = {qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 fa = unpack_half2(wa[k]);
+        const float2 fb = unpack_half2(wb[k]);
+        v[8 * g + 2 * k] = (fa.x + fb.x) * tanh_approx(v[8 * g + 2 * k]);
+        v[8 * g + 2 * k + 1] = (fa.y + fb.y) * tanh_approx(v[8 * g + 2 * k + 1]);
+      }
+    }
+  }
+
   if constexpr (kOut == kOutF16Chunk || kOut == kOutF16E4m3) {
 #pragma unroll
     for (int g = 0; g < kCols / 8; ++g) {
@@ -230,6 +252,21 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
       q.y = static_cast<uint32_t>(pack_e4m3x2(f[4] * is, f[5] * is)) |
             (static_cast<uint32_t>(pack_e4m3x2(f[6] * is, f[7] * is)) << 16);
       *reinterpret_cast<uint2*>(dst + ((pix_row * dst_chunks + c / 16) * a.W + x) * 16 + (c % 16)) = q;
+    }
+  }
+  if constexpr (kOut == kOutPixShuf4) {
+    // channel 16p + 4i + j -> pixel (4y + i, 4x + j) of plane p: four adjacent halves per (p, i)
+    const size_t W4 = static_cast<size_t>(a.W) * 4;
+    const size_t H4 = static_cast<size_t>(a.H) * 4;
+#pragma unroll
+    for (int q = 0; q < kCols / 4; ++q) {
+      const int c = col0 + 4 * q;
+      const int plane = c / 16, i = (c % 16) / 4;
+      if (plane < 3) {
+        const size_t at = ((static_cast<size_t>(n) * 3 + plane) * H4 + 4 * static_cast<size_t>(y) + i) * W4 + 4 * x;
+        *reinterpret_cast<uint2*>(a.out + at * 2) =
+            make_uint2(pack_half2(v[4 * q], v[4 * q + 1]), pack_half2(v[4 * q + 2], v[4 * q + 3]));
+      }
     }
   }
   if constexpr (kOut == kOutPixShuf2) {

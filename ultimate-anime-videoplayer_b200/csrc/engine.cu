@@ -1,8 +1,10 @@
-// Engine implementations: SPAN x2 (FP16 / FP8) and the factory.
+// Engine implementations: SPAN x2 (FP16 / FP8), IFNet, the unshuffle SPAN of a .span8 package, and
+// the factory.
 #include <cstring>
 
 #include "engine.h"
 #include "ifnet_net.h"
+#include "span8_net.h"
 #include "span_net.h"
 #include "static_scratch.h"
 
@@ -147,13 +149,68 @@ class IfnetEngine final : public Engine {
   IfnetNet net_;
 };
 
+// The unshuffle SPAN of a .span8 package (KB2_MODEL_SPAN_UNSHUFFLE): FP16.
+class Span8Engine final : public Engine {
+ public:
+  Status init(const kb2_engine_desc& d, const Span8Package& pkg) {
+    if (d.precision != KB2_PREC_FP16)
+      return refuse(KB2_FORMAT_UNSUPPORTED, "unshuffle SPAN runs in FP16 (the package's FP16 weights)");
+    return net_.create(pkg, d.max_batch, d.height, d.width);
+  }
+  std::vector<std::string> input_names() const override { return {"input"}; }
+  std::vector<std::string> output_names() const override { return {"output"}; }
+  int max_batch() const override { return net_.max_batch(); }
+  int height() const override { return net_.height(); }
+  int width() const override { return net_.width(); }
+  size_t device_bytes() const override { return net_.device_bytes(); }
+  Status enqueue(cudaStream_t stream, const kb2_tensor* inputs, int n_inputs, const kb2_tensor* outputs,
+                 int n_outputs) override {
+    void* in = nullptr;
+    void* out = nullptr;
+    int batch = 0;
+    KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 1, 2, &in, &out, &batch));
+    return net_.run(stream, in, out, batch);
+  }
+  Status set_profiling(bool on) override {
+    net_.timer().enable(on);
+    return Status::Ok();
+  }
+  Status read_profile(kb2_layer_profile* records, int capacity, int* count) override {
+    std::vector<LayerTimer::Record> kinds;
+    KB2_TRY(net_.timer().read(kinds));
+    *count = static_cast<int>(kinds.size());
+    for (int i = 0; i < *count && i < capacity; ++i) {
+      kb2_layer_profile& r = records[i];
+      std::memset(&r, 0, sizeof(r));
+      std::strncpy(r.name, kinds[i].name.c_str(), sizeof(r.name) - 1);
+      r.launches = kinds[i].launches;
+      r.total_ms = kinds[i].ms;
+      r.flops = kinds[i].flops;
+      r.bytes = kinds[i].bytes;
+    }
+    return Status::Ok();
+  }
+  int launches_per_enqueue() const override { return net_.launches_per_run(); }
+
+ protected:
+  int* err_word() const override { return net_.err_word(); }
+
+ private:
+  Span8Net net_;
+};
+
 }  // namespace
 
 Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
   // Everything that needs no device is checked first: the blob and the shapes.
-  if (d.model != KB2_MODEL_SPAN_X2 && d.model != KB2_MODEL_IFNET) return refuse(KB2_FORMAT_UNSUPPORTED, "unknown model");
+  if (d.model != KB2_MODEL_SPAN_X2 && d.model != KB2_MODEL_IFNET && d.model != KB2_MODEL_SPAN_UNSHUFFLE)
+    return refuse(KB2_FORMAT_UNSUPPORTED, "unknown model");
   std::vector<float> params;
-  KB2_TRY(parse_blob(d.weights, d.weights_bytes, d.model, params));
+  Span8Package pkg;
+  if (d.model == KB2_MODEL_SPAN_UNSHUFFLE)
+    KB2_TRY(parse_span8(d.weights, d.weights_bytes, pkg));
+  else
+    KB2_TRY(parse_blob(d.weights, d.weights_bytes, d.model, params));
   if (d.max_batch < 1 || d.height < 1 || d.width < 1 || d.height > 8192 || d.width > 8192)
     return refuse(KB2_SHAPE_INVALID, "frame size or batch out of contract");
   int count = 0;
@@ -168,6 +225,12 @@ Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
   if (d.model == KB2_MODEL_SPAN_X2) {
     auto e = std::make_unique<SpanEngine>();
     KB2_TRY(e->init(d, params));
+    out = std::move(e);
+    return Status::Ok();
+  }
+  if (d.model == KB2_MODEL_SPAN_UNSHUFFLE) {
+    auto e = std::make_unique<Span8Engine>();
+    KB2_TRY(e->init(d, pkg));
     out = std::move(e);
     return Status::Ok();
   }

@@ -30,6 +30,7 @@ KB2_INVALID_ARGUMENT = 8
 KB2_F32, KB2_F16, KB2_U8, KB2_I8 = 0, 1, 2, 3
 MODEL_SPAN_X2 = 1
 MODEL_IFNET = 2
+MODEL_SPAN_UNSHUFFLE = 3  # weights: the bytes of a .span8 package
 PREC_FP16 = 1
 PREC_FP8 = 2
 
