@@ -1,12 +1,14 @@
 """Benchmark of the frame path: SPAN x2 1080p -> 2160p on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8|rife] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8|rife|janai] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: frames shard across GPUs, no collective)
 
 A step is one batch of 8 synthetic 1080p frames through the engine (the contract's configs[1]:
 FP16, batch 8, 240 frames per GPU by default = 30 steps); `--workload span8` is configs[2] (FP8
 E4M3), `--workload rife` is configs[3] (IFNet FP16, 8 frame pairs per step at t = 0.5;
-`--height 2160 --width 3840` for the 4K interpolation rate). `value` is whole-job frames/s with the
+`--height 2160 --width 3840` for the 4K interpolation rate), `--workload janai` the AnimeJaNai
+unshuffle SPAN b8f64 (8 blocks x 64 channels at half resolution, FP16) read from a seeded .span8
+package (the first of the contract's "next" rows). `value` is whole-job frames/s with the
 inputs resident in HBM; `e2e` is the same through the public C ABI with pinned host frames, the
 host->device copy and the device->host read of every output inside the timed region. `roofline`
 times the dominant kernel with CUDA events on its launching stream during the timed steps.
@@ -40,7 +42,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["span16", "span8", "rife"], default="span16")
+    ap.add_argument("--workload", choices=["span16", "span8", "rife", "janai"], default="span16")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--height", type=int, default=FRAME_H)
     ap.add_argument("--width", type=int, default=FRAME_W)
@@ -129,7 +131,8 @@ RIFE_CROP_H, RIFE_CROP_W = 64, 96  # IFNet needs multiples of 32
 def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, timestep=0.5, full=None):
     """Each host thread runs the reference's FP32 network on its own crop of the frame (the
     interpreter is single-threaded per call); returns (frames processed, seconds). SPAN when
-    frame_b is None, else IFNet on the crop pair."""
+    frame_b is None, else IFNet on the crop pair; `flat` given as bytes is a .span8 package, run by
+    the reference's unshuffle-SPAN forward (src/gpu/span_fp8/forward.cpp:144)."""
     from oracle import ref_lib
     import numpy as np
 
@@ -152,6 +155,8 @@ def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, tim
             if tt == t:
                 if rife:
                     ref_lib.ifnet_forward(a, b, timestep, flat)
+                elif isinstance(flat, bytes):
+                    ref_lib.span8_forward(flat, a)
                 else:
                     ref_lib.span_forward(a, flat)
                 done[t] += 1
@@ -186,7 +191,7 @@ def cpu_baseline(frame, flat, budget_s=12.0, frame_b=None, timestep=0.5, full=No
         frames, dt = reference_sample(cores, frame, flat, crops_per_thread=reps, **kw)
     ch, cw = (RIFE_CROP_H, RIFE_CROP_W) if frame_b is not None else (CROP_H, CROP_W)
     fh, fw = full if full is not None else (FRAME_H, FRAME_W)
-    net = "IFNet pairs" if frame_b is not None else "SPAN"
+    net = "IFNet pairs" if frame_b is not None else ("unshuffle SPAN b8f64" if isinstance(flat, bytes) else "SPAN")
     return {"value": frames / dt, "unit": "frames/s", "cores": cores, "kind": "reference",
             "sample": f"{cores} threads x {reps} {net} crops of {ch}x{cw} px of synthetic {fw}x{fh} frames, "
                       f"reference FP32 IR interpreter (oracle/_ref), scaled by pixels to {fw}x{fh} frames"}
@@ -201,6 +206,15 @@ def workload_desc(args, world=1):
                   "global_batch": B * world, "frames_per_gpu": B * args.steps,
                   "parallelism": f"pair-sharded x{world}, no collective",
                   "l2": "working set > L2: block 3 reads and writes 8 x 67 MB inputs and 8 x 33 MB activations"}
+        return metric, "f16", config
+    if args.workload == "janai":
+        metric = ("SPAN b8f64 unshuffle x2 1080p->2160p frames/s" if (H, W) == (FRAME_H, FRAME_W)
+                  else f"SPAN b8f64 unshuffle x2 {W}x{H} frames/s")
+        config = {"workload": f"AnimeJaNai unshuffle SPAN b8f64 FP16 (.span8 package, seeded), batch {B}, "
+                              f"{H}x{W} -> {2 * H}x{2 * W}",
+                  "global_batch": B * world, "frames_per_gpu": B * args.steps,
+                  "parallelism": f"frame-sharded x{world}, no collective",
+                  "l2": "working set > L2: each layer reads and writes 8 x 66 MB activations (half resolution)"}
         return metric, "f16", config
     fp8 = args.workload == "span8"
     metric = "SPAN x2 1080p->2160p frames/s" if (H, W) == (FRAME_H, FRAME_W) else f"SPAN x2 {W}x{H} frames/s"
@@ -230,6 +244,9 @@ def run_reference(args):
         fa, fb = shifted_pair(args.height, args.width, 0)
         frame, frame_b = np.ascontiguousarray(fa, np.float32), np.ascontiguousarray(fb, np.float32)
         flat = nets.ifnet_flat(nets.ifnet_init(2))
+    elif args.workload == "janai":
+        frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
+        flat = nets.span8_package(nets.span8_init(8, 64, seed=3))
     else:
         frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
         flat = nets.span_flat(nets.span_init(1))
@@ -285,8 +302,16 @@ def run_ours(args):
     B, H, W = args.batch, args.height, args.width
     rife = args.workload == "rife"
     fp8 = args.workload == "span8"
+    janai = args.workload == "janai"
     metric, dtype, config = workload_desc(args, world)
-    if rife:
+    if janai:
+        flat = nets.span8_package(nets.span8_init(8, 64, seed=3))
+        frames = anime_frames(B, H, W, seed=shard.frame_seed(10, rank, 0)).astype(np.float16)
+        frames_b = None
+        eng = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, flat, H, W, max_batch=B, device=local_rank)
+        host_in = [frames]
+        out_shape = (B, 3, 2 * H, 2 * W)
+    elif rife:
         p = nets.ifnet_init(2)
         flat = nets.ifnet_flat(p)
         blob = kb.make_blob(kb.MODEL_IFNET, flat)
@@ -365,7 +390,7 @@ def run_ours(args):
                 "avg_launch_ms": avg_ms, "flops_per_launch": top["flops"],
                 "algorithmic_bytes_per_launch": top["bytes"],
                 "peak_source": f"{peak_kind} bf16_tflops_sustained" + (" x2 (E4M3)" if top_name.endswith(".fp8") else ""),
-                "network_tflops": (total_flops / (ms / 1e3) / 1e12) if rife else
+                "network_tflops": (total_flops / (ms / 1e3) / 1e12) if (rife or janai) else
                 FLOP_PER_PX * H * W * B * args.steps / (ms / 1e3) / 1e12}
     layers = {k: {"launches": v["launches"], "ms_per_launch": v["total_ms"] / max(1, v["launches"]),
                   "share": v["total_ms"] / max(1e-9, sum(x["total_ms"] for x in profile.values()))}

@@ -308,12 +308,17 @@ Status Span8Net::run(cudaStream_t stream, const void* in, void* out, int batch) 
   for (const Step& s : steps_) {
     const ConvSpec& sp = s.layer->spec;
     const double flops = 2.0 * sp.taps * sp.n_sources * sp.cin * sp.n_real * px;
+    // algorithmic bytes: every FP16 source pixel and residual read once, every output written once
+    const double in_b = 2.0 * sp.n_sources * s.layer->args.chunks * 8;
+    const double res_b = (s.residual != nullptr ? 2.0 * ch_ : 0.0) + (s.residual2 != nullptr ? 2.0 * ch_ : 0.0);
+    const double out_b = 2.0 * sp.n_real;
+    const double bytes = (in_b + res_b + out_b) * px;
     KB2_TRY(timer_.begin(stream));
     KB2_TRY(s.layer->launch(stream, batch, s.out != nullptr ? static_cast<void*>(s.out->ptr) : out,
                             s.residual != nullptr ? s.residual->ptr : nullptr, 1.0f, 1.0f, nullptr,
                             s.residual != nullptr ? s.residual->chunks : 0,
                             s.residual2 != nullptr ? s.residual2->ptr : nullptr));
-    KB2_TRY(timer_.end(s.kind, flops, 0.0, stream));
+    KB2_TRY(timer_.end(s.kind, flops, bytes, stream));
   }
   return Status::Ok();
 }
