@@ -505,6 +505,18 @@ def span8_init(blocks=5, real=48, seed=11, gain=0.7, bias_std=0.02, pixel_gain=0
     return p
 
 
+def span8_fp8_package(p, frames, floor=2.0 ** -14):
+    """An FP8 package (no FP16 flag) of contents `p` whose activation scales are calibrated on
+    `frames` the reference's way: scale = max(peak, floor) * 1.25 / 448 (derive.h:42-62)."""
+    peaks = []
+    span8_forward(frames, p, peaks=peaks)
+    q = dict(p)
+    q["flags"] = 0
+    q["scales"] = (np.maximum(np.asarray(peaks, np.float32), np.float32(floor)) * np.float32(SCALE_HEADROOM)
+                   / np.float32(E4M3_MAX)).astype(np.float32)
+    return q
+
+
 def _crc32(payload):
     import zlib
     return zlib.crc32(payload) & 0xFFFFFFFF
@@ -538,16 +550,22 @@ def _span8_conv(x, c, real_in, real_out, side, groups=1, stored=SPAN8_STORED):
     return conv2d(x, np.ascontiguousarray(w), c["b"][:real_out], pad=side // 2)
 
 
-def span8_forward(x, p):
+def span8_forward(x, p, peaks=None):
     """FP32 forward of the unshuffle SPAN (src/gpu/span_fp8/forward.cpp:144-166): 2x2 unshuffle
     (channel c*4 + dy*2 + dx), conv_1, blocks (c1, ReLU, c2, ReLU, c3; out (x + c3) * tanh(att(c3))),
     conv_cat over (conv_1 out, last block out, first block out, the last block's first ReLU),
-    to_pixel, DepthToSpace(4). x: [n,3,h,w], h and w even; returns [n,3,2h,2w]."""
+    to_pixel, DepthToSpace(4). x: [n,3,h,w], h and w even; returns [n,3,2h,2w]. `peaks`, a list,
+    receives max |v| of the package's 1 + 3 * blocks scaled tensors in their order (package.h:15-17:
+    conv_1 output, then per block its two ReLU outputs and its output)."""
+    def peak(t):
+        if peaks is not None:
+            peaks.append(float(np.max(np.abs(t))))
     x = np.asarray(x, np.float32)
     n, _, h, w = x.shape
     ch = p["real"]
     u = x.reshape(n, 3, h // 2, 2, w // 2, 2).transpose(0, 1, 3, 5, 2, 4).reshape(n, 12, h // 2, w // 2)
     first = _span8_conv(u, p["first"], 12, ch, 3, stored=SPAN8_IN)
+    peak(first)
     cur = first
     first_block = last_relu = None
     for b, blk in enumerate(p["block"]):
@@ -556,6 +574,9 @@ def span8_forward(x, p):
         c3 = _span8_conv(r2, blk["c3"], ch, ch, 3)
         att = _span8_conv(c3, blk["att"], ch, ch, 1)
         cur = ((cur + c3) * np.tanh(att)).astype(np.float32)
+        peak(r1)
+        peak(r2)
+        peak(cur)
         if b == 0:
             first_block = cur
         if b + 1 == len(p["block"]):

@@ -2,7 +2,8 @@
 against the CPU oracle (oracle/nets.py span8_forward, pinned to the reference's own FP32 forward by
 tests/test_span8.py) and against the reference's outputs in the golden fixtures.
 
-Tolerance (the contract's FP16 bar): max-abs <= 2/255 after clamp to [0, 1] vs the FP32 oracle."""
+Tolerances (the contract's): FP16 max-abs <= 2/255 after clamp to [0, 1] vs the FP32 oracle; E4M3
+blocks PSNR >= 45 dB vs the FP32 oracle."""
 import numpy as np
 import pytest
 
@@ -82,6 +83,35 @@ def test_span8_refusals():
     with pytest.raises(kb.KB2Error) as e:
         kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, pkg, 33, 64)  # odd height: the 2x2 unshuffle needs even sides
     assert e.value.status == kb.KB2_SHAPE_INVALID
+
+
+# E4M3 blocks of an FP8 package (scales calibrated on the frames the reference's way), against the
+# FP32 oracle: the contract's FP8 bar, PSNR >= 45 dB
+@pytest.mark.parametrize("blocks,real,n,h,w", [(3, 48, 2, 40, 72), (5, 48, 1, 64, 540), (3, 64, 2, 36, 100),
+                                               (8, 64, 1, 64, 540)])
+def test_span8_fp8_psnr(blocks, real, n, h, w):
+    import torch
+    from synth import anime_frames
+    x = f16(anime_frames(n, h, w, seed=17 + blocks))
+    p = nets.span8_fp8_package(nets.span8_init(blocks, real, seed=50 + blocks), x)
+    pkg = nets.span8_package(p)
+    ref = nets.span8_forward(x, p)
+    eng = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, pkg, h, w, max_batch=n, precision=kb.PREC_FP8)
+    tx = torch.from_numpy(np.ascontiguousarray(x, np.float16)).cuda()
+    out = torch.full((n, 3, 2 * h, 2 * w), float("nan"), dtype=torch.float16, device="cuda")
+    eng.enqueue([tx], [out])
+    eng.check_device()
+    res = out.float().cpu().numpy()
+    eng.close()
+    assert np.isfinite(res).all()
+    db = nets.psnr(res, ref)
+    assert db >= 45.0, f"b{blocks}f{real}: {db:.2f} dB"
+    # the FP16 engine of the same package stays within the FP16 bar
+    assert nets.max_abs_clamped(run_span8(pkg, x), ref) <= FP16_MAX_ABS
+
+
+def test_span8_fp8_refuses_fp16_packages():
+    pkg = nets.span8_package(nets.span8_init(2, 48, seed=4))  # the FP16 flag: unit scales
     with pytest.raises(kb.KB2Error) as e:
         kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, pkg, 32, 64, precision=kb.PREC_FP8)
     assert e.value.status == kb.KB2_FORMAT_UNSUPPORTED

@@ -37,7 +37,7 @@
 namespace kb2 {
 
 constexpr uint16_t kPairMask = 3;  // both blocks of the cluster
-constexpr int kPairMaxK = 12;      // K steps per input row: 2, 3 (conv_1), 5, 9 (48 channels), 12 (64)
+constexpr int kPairMaxK = 12;      // K steps per input row: 2, 3 (conv_1), 5, 6 (E4M3), 9, 12 (FP16 64)
 
 // Epilogue shape of the pair kernel: `groups` groups of warps take the accumulator entries in turn
 // (entry e goes to group e % groups, so a group owns the slots s with s % groups = g and that many
@@ -132,7 +132,7 @@ template <bool kFp8, int kNK, int kClears>
 __device__ __forceinline__ uint32_t pair_row_head(
     uint32_t d_clear, uint32_t d_clear2, uint64_t zero_desc, uint32_t id_clear, uint32_t d_win, uint32_t idesc,
     uint32_t nf, uint32_t nf_par, uint32_t ns, uint32_t ns_par, const uint64_t (&a)[kNK], const uint64_t (&b)[kNK]) {
-  static_assert(kNK == 2 || kNK == 3 || kNK == 5 || kNK == 9 || kNK == 12, "rows of 2, 3, 5, 9 or 12 K steps");
+  static_assert(kNK == 2 || kNK == 3 || kNK == 5 || kNK == 6 || kNK == 9 || kNK == 12, "rows of 2, 3, 5, 6, 9 or 12 K steps");
   static_assert(kClears == 1 || kClears == 2, "one or two cleared blocks");
   uint32_t ok;
   if constexpr (kFp8 == false && kNK == 2 && kClears == 1) {
@@ -232,6 +232,47 @@ __device__ __forceinline__ uint32_t pair_row_head(
             "l"(b[0]), "l"(b[1]), "l"(b[2])
           : "memory");
   } else if constexpr (kFp8 == false && kNK == 5 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 6 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
+  } else if constexpr (kFp8 == false && kNK == 6 && kClears == 2) {
     asm volatile(
           "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
           "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
@@ -461,6 +502,47 @@ __device__ __forceinline__ uint32_t pair_row_head(
             "l"(a[0]), "l"(a[1]), "l"(a[2]),
             "l"(b[0]), "l"(b[1]), "l"(b[2])
           : "memory");
+  } else if constexpr (kFp8 == true && kNK == 6 && kClears == 1) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 6 && kClears == 2) {
+    asm volatile(
+          "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 pf, [%7], %8;\n\t"
+          "mbarrier.test_wait.parity.shared::cta.b64 ps, [%9], %10;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "setp.ne.b32 clr, 0, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%1], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%2], %11, %3, %4, clr;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %11, %14, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %12, %15, %6, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%5], %13, %16, %6, acc;\n\t"
+          "selp.u32 t0, 1, 0, pf;\n\t"
+          "selp.u32 t1, 2, 0, ps;\n\t"
+          "or.b32 %0, t0, t1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(d_clear), "r"(d_clear2), "l"(zero_desc), "r"(id_clear), "r"(d_win), "r"(idesc),
+            "r"(nf), "r"(nf_par), "r"(ns), "r"(ns_par),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]),
+            "l"(b[0]), "l"(b[1]), "l"(b[2])
+          : "memory");
   } else if constexpr (kFp8 == true && kNK == 9 && kClears == 1) {
     asm volatile(
           "{\n\t.reg .pred pf, ps, acc, clr;\n\t.reg .b32 t0, t1;\n\t"
@@ -591,6 +673,18 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
             "l"(a[3]), "l"(a[4]),
             "l"(b[3]), "l"(b[4])
           : "memory");
+  } else if constexpr (kFp8 == false && kNK == 6) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %7, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %5, %8, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %6, %9, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[3]), "l"(a[4]), "l"(a[5]),
+            "l"(b[3]), "l"(b[4]), "l"(b[5])
+          : "memory");
   } else if constexpr (kFp8 == false && kNK == 9) {
     asm volatile(
           "{\n\t.reg .pred acc;\n\t"
@@ -649,6 +743,18 @@ __device__ __forceinline__ void pair_row_tail(uint32_t d_win, uint32_t idesc, ui
           ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
             "l"(a[3]), "l"(a[4]),
             "l"(b[3]), "l"(b[4])
+          : "memory");
+  } else if constexpr (kFp8 == true && kNK == 6) {
+    asm volatile(
+          "{\n\t.reg .pred acc;\n\t"
+          "setp.ne.b32 acc, 1, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %4, %7, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %5, %8, %1, acc;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %6, %9, %1, acc;\n\t"
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%2], %3;\n\t}\n"
+          ::"r"(d_win), "r"(idesc), "r"(done), "h"(kPairMask),
+            "l"(a[3]), "l"(a[4]), "l"(a[5]),
+            "l"(b[3]), "l"(b[4]), "l"(b[5])
           : "memory");
   } else if constexpr (kFp8 == true && kNK == 9) {
     asm volatile(
@@ -980,8 +1086,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
         if (wait_bar(wbar, 0, a.err, kErrWaitMma) && wait_bar(wpeer, 0, a.err, kErrWaitMma)) {
           const PairIssue is{a, smem_u32(ring), smem_u32(sw), smem_u32(zero_b), tmem_base, s_k, full, done, slot_free};
           // rows of K steps as the host admits them (conv_layer.cu pair_admits): 64 output channels
-          // 12 or 3, FP16 48: 12, 9, 5, 3 or 2 (no 12 for E4M3 or 16 outputs)
-          if constexpr (kCoutPad == 64) {
+          // 12 or 3 in FP16, 6 in E4M3 (64 input channels); 48: 12 (FP16), 9, 5, 3 or 2
+          if constexpr (kCoutPad == 64 && kFp8) {
+            pair_issue<kFp8, kCoutPad, 6>(is);
+          } else if constexpr (kCoutPad == 64) {
             if (a.n_ksteps == 12) pair_issue<kFp8, kCoutPad, 12>(is);
             else pair_issue<kFp8, kCoutPad, 3>(is);
           } else {

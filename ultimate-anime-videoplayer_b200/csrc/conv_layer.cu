@@ -121,16 +121,28 @@ const KernelEntry kKernels[] = {
     KB2_KERNEL(false, 48, kEpiTanhGate, kOutF16Chunk),
     KB2_KERNEL(false, 64, kEpiTanhGate, kOutF16Chunk),
     KB2_KERNEL(false, 64, kEpiBias, kOutF16Chunk),
+    // its E4M3 blocks: ReLU convs to E4M3 (the last block's first one to FP16 as well, a conv_cat
+    // source), c3 to FP16, the gate and conv_1 writing FP16 and E4M3 copies of the block input
+    KB2_PAIRED(true, 48, kEpiPrelu, kOutE4m3Chunk),
+    KB2_PAIRED(true, 48, kEpiPrelu, kOutF16E4m3),
+    KB2_PAIRED(true, 48, kEpiBias, kOutF16Chunk),
+    KB2_PAIRED(true, 64, kEpiPrelu, kOutE4m3Chunk),
+    KB2_PAIRED(true, 64, kEpiPrelu, kOutF16E4m3),
+    KB2_PAIRED(true, 64, kEpiBias, kOutF16Chunk),
+    KB2_PAIRED(false, 48, kEpiBias, kOutF16E4m3),
+    KB2_PAIRED(false, 64, kEpiBias, kOutF16E4m3),
+    KB2_KERNEL(false, 48, kEpiTanhGate, kOutF16E4m3),
+    KB2_KERNEL(false, 64, kEpiTanhGate, kOutF16E4m3),
 };
 
 bool wants_stacked(const ConvSpec& s) {
   return s.taps == 9 && s.n_sources == 1 && (s.n_pad == 48 || s.n_pad == 16 || s.n_pad == 64);
 }
 
-// K steps per input row the pair kernel runs (conv3p.cuh): 64 output channels 12 or 3; 48 channels
-// 2, 3, 5, 9, or 12 in FP16 (64 FP16 inputs); 16 channels 2, 3, 5 or 9
+// K steps per input row the pair kernel runs (conv3p.cuh): 64 output channels 12 or 3 in FP16, 6 in
+// E4M3 (64 inputs); 48 channels 2, 3, 5, 9, or 12 in FP16 (64 FP16 inputs); 16 channels 2, 3, 5 or 9
 bool pair_admits(const ConvSpec& s, int nk) {
-  if (s.n_pad == 64) return !s.fp8 && (nk == 12 || nk == 3);
+  if (s.n_pad == 64) return s.fp8 ? nk == 6 : (nk == 12 || nk == 3);
   if (nk == 12) return !s.fp8 && s.n_pad == 48;
   return nk == 2 || nk == 3 || nk == 5 || nk == 9;
 }

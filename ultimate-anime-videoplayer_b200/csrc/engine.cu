@@ -149,13 +149,17 @@ class IfnetEngine final : public Engine {
   IfnetNet net_;
 };
 
-// The unshuffle SPAN of a .span8 package (KB2_MODEL_SPAN_UNSHUFFLE): FP16.
+// The unshuffle SPAN of a .span8 package (KB2_MODEL_SPAN_UNSHUFFLE): FP16, or E4M3 blocks for an FP8
+// package.
 class Span8Engine final : public Engine {
  public:
   Status init(const kb2_engine_desc& d, const Span8Package& pkg) {
-    if (d.precision != KB2_PREC_FP16)
-      return refuse(KB2_FORMAT_UNSUPPORTED, "unshuffle SPAN runs in FP16 (the package's FP16 weights)");
-    return net_.create(pkg, d.max_batch, d.height, d.width);
+    const bool fp8 = d.precision == KB2_PREC_FP8_E4M3;
+    if (!fp8 && d.precision != KB2_PREC_FP16) return refuse(KB2_FORMAT_UNSUPPORTED, "unknown precision");
+    // an FP16-native package carries unit scales that mean nothing for E4M3 (package.h:61-66)
+    if (fp8 && (pkg.flags & 2u) != 0u)
+      return refuse(KB2_FORMAT_UNSUPPORTED, "unshuffle SPAN: an FP16 package has no E4M3 activation scales");
+    return net_.create(pkg, fp8, d.max_batch, d.height, d.width);
   }
   std::vector<std::string> input_names() const override { return {"input"}; }
   std::vector<std::string> output_names() const override { return {"output"}; }

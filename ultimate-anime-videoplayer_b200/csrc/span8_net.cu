@@ -11,8 +11,15 @@
 //              att 1x1 on C3, then (x + C3) * tanh(att), x the block input        -> X(b+1)
 //   conv_cat   1x1 over the four sources [S0, X_last, X1, R1 of the last block], no concat buffer
 //   to_pixel   3x3 C->48 + DepthToSpace(4) in the epilogue                          -> NCHW F16 [n][3][2H][2W]
-// ReLU is the PReLU epilogue with zero slopes. The E4M3 blocks of an FP8 package are not run: every
-// package runs in FP16 (its weights are FP16 in the file; the FP8 scales are read and checked only).
+// ReLU is the PReLU epilogue with zero slopes.
+//
+// Precision. FP16 engine: FP16 operands and activations, FP32 accumulation (any package; its weights
+// are FP16 in the file). E4M3 engine (an FP8 package, without the FP16 flag): the blocks' 3x3 convs
+// run E4M3 x E4M3 -> FP32 with the package's per-tensor activation scales ([0] conv_1 output, [1+3b]
+// and [2+3b] block b's ReLU outputs, [3+3b] its output: span_fp8/package.h:15-17) and per-output-
+// channel weight scales; conv_1 and the gates write FP16 and E4M3 copies of each block input, c3
+// writes FP16, and the attention, conv_cat and to_pixel stay FP16, as the reference keeps its ends
+// in FP16 (package.h:12-16).
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -165,20 +172,20 @@ Status parse_span8(const void* bytes, uint64_t n, Span8Package& out) {
   return Status::Ok();
 }
 
-Status Span8Net::make_tensor(std::unique_ptr<Tensor>& t, int chunks) {
+Status Span8Net::make_tensor(std::unique_ptr<Tensor>& t, int chunks, bool fp8) {
   t = std::make_unique<Tensor>();
   t->t.batch = max_batch_;
   t->t.H = h_;
   t->t.W = w_;
   t->t.chunks = chunks;
-  t->t.fp8 = false;
+  t->t.fp8 = fp8;
   KB2_TRY(t->buf.alloc(t->t.bytes()));
   KB2_CUDA(cudaMemset(t->buf.ptr, 0, t->t.bytes()));
   t->t.ptr = t->buf.as<uint8_t>();
   return Status::Ok();
 }
 
-Status Span8Net::create(const Span8Package& pkg, int max_batch, int H, int W) {
+Status Span8Net::create(const Span8Package& pkg, bool fp8, int max_batch, int H, int W) {
   if (H % 2 != 0 || W % 2 != 0) return refuse(KB2_SHAPE_INVALID, "unshuffle SPAN: even frame height and width");
   if (H < 4 || W < 4) return refuse(KB2_SHAPE_INVALID, "unshuffle SPAN: frame too small");
   max_batch_ = max_batch;
@@ -187,103 +194,128 @@ Status Span8Net::create(const Span8Package& pkg, int max_batch, int H, int W) {
   h_ = H / 2;
   w_ = W / 2;
   ch_ = pkg.real;
-  const int C = ch_, cc = C / 8;
+  fp8_ = fp8;
+  const int C = ch_, cc = C / 8, cq = C / 16;  // FP16 and E4M3 chunks of a C-channel tensor
   KB2_TRY(err_.alloc(sizeof(int)));
   KB2_CUDA(cudaMemset(err_.ptr, 0, sizeof(int)));
   int* err = err_.as<int>();
   k_pack_ = timer_.kind("span8.unshuffle");
-  const int k_first = timer_.kind("span8.conv_1"), k_relu = timer_.kind("span8.block_relu_conv");
-  const int k_c3 = timer_.kind("span8.block_c3"), k_gate = timer_.kind("span8.block_att_gate");
+  const int k_first = timer_.kind("span8.conv_1");
+  const int k_relu = timer_.kind(fp8 ? "span8.block_relu_conv.fp8" : "span8.block_relu_conv");
+  const int k_c3 = timer_.kind(fp8 ? "span8.block_c3.fp8" : "span8.block_c3");
+  const int k_gate = timer_.kind("span8.block_att_gate");
   const int k_cat = timer_.kind("span8.conv_cat"), k_pix = timer_.kind("span8.to_pixel");
 
-  std::unique_ptr<Tensor> u, s0, xa, xb, x1, r1, r1_last, r2, c3, cat;
+  // FP16 tensors: the unshuffled frame, conv_1's output, the block outputs (two alternating, the
+  // first block's kept), the ReLU outputs, c3 and conv_cat's output. The E4M3 engine adds E4M3
+  // copies of every block-conv input: conv_1's and each block's output, the two ReLU outputs.
+  std::unique_ptr<Tensor> u, s0, xa, xb, x1, r1, r1_last, r2, c3, cat, s0q, xaq, xbq, x1q;
   KB2_TRY(make_tensor(u, 2));
   KB2_TRY(make_tensor(s0, cc));
   KB2_TRY(make_tensor(xa, cc));
   KB2_TRY(make_tensor(xb, cc));
   KB2_TRY(make_tensor(x1, cc));
-  KB2_TRY(make_tensor(r1, cc));
   KB2_TRY(make_tensor(r1_last, cc));
-  KB2_TRY(make_tensor(r2, cc));
   KB2_TRY(make_tensor(c3, cc));
   KB2_TRY(make_tensor(cat, cc));
+  KB2_TRY(make_tensor(r1, fp8 ? cq : cc, fp8));
+  KB2_TRY(make_tensor(r2, fp8 ? cq : cc, fp8));
+  if (fp8) {
+    KB2_TRY(make_tensor(s0q, cq, true));
+    KB2_TRY(make_tensor(xaq, cq, true));
+    KB2_TRY(make_tensor(xbq, cq, true));
+    KB2_TRY(make_tensor(x1q, cq, true));
+  }
   unshuffled_ = &u->t;
+  // E4M3 copy of an FP16 block input
+  auto q_of = [&](const ChunkedTensor* t) -> const ChunkedTensor* {
+    if (!fp8) return nullptr;
+    if (t == &s0->t) return &s0q->t;
+    if (t == &xa->t) return &xaq->t;
+    if (t == &xb->t) return &xbq->t;
+    return &x1q->t;
+  };
 
-  auto add = [&](const ConvSpec& s, const std::vector<float>& w, const std::vector<float>& b,
-                 const ChunkedTensor* const* inputs, const ChunkedTensor* out, const ChunkedTensor* res,
-                 const ChunkedTensor* res2, int kind) -> Status {
+  auto add = [&](const ConvSpec& sp, const std::vector<float>& w, const std::vector<float>& b, const float* act_scale,
+                 const ChunkedTensor* const* inputs, const ChunkedTensor* out, const ChunkedTensor* out2, float out_scale,
+                 const ChunkedTensor* res, const ChunkedTensor* res2, int kind) -> Status {
     auto l = std::make_unique<ConvLayer>();
-    KB2_TRY(l->build(s, w.data(), b.data(), nullptr, nullptr, inputs, err));
-    steps_.push_back(Step{l.get(), out, res, res2, kind});
+    KB2_TRY(l->build(sp, w.data(), b.data(), nullptr, act_scale, inputs, err));
+    steps_.push_back(Step{l.get(), out, out2, out2 != nullptr ? 1.0f / out_scale : 1.0f, res, res2, kind});
     layers_.push_back(std::move(l));
     return Status::Ok();
   };
-  auto conv3 = [&](int cin, int n_pad, int epi, int out_fmt, int out_chunks) {
-    ConvSpec s;
-    s.taps = 9;
-    s.cin = cin;
-    s.n_real = n_pad;
-    s.n_pad = n_pad;
-    s.epi = epi;
-    s.out = out_fmt;
-    s.out_chunks = out_chunks;
-    return s;
+  auto spec = [&](int taps, bool q, int cin, int n_pad, int epi, int out_fmt) {
+    ConvSpec sp;
+    sp.taps = taps;
+    sp.fp8 = q;
+    sp.cin = cin;
+    sp.n_real = n_pad;
+    sp.n_pad = n_pad;
+    sp.epi = epi;
+    sp.out = out_fmt;
+    sp.out_chunks = out_fmt == kOutE4m3Chunk ? cq : cc;
+    sp.out2_chunks = cq;
+    return sp;
   };
-  const std::vector<float> bias_c(pkg.first.b.begin(), pkg.first.b.begin() + C);
+  auto bias = [&](const Span8Package::Conv& c, int n) { return std::vector<float>(c.b.begin(), c.b.begin() + n); };
+  const std::vector<float>& sc = pkg.scales;  // [0] conv_1 out; block b: [1+3b] ReLU 1, [2+3b] ReLU 2, [3+3b] out
   {
     const ChunkedTensor* in[1] = {&u->t};
-    KB2_TRY(add(conv3(12, C, kEpiBias, kOutF16Chunk, cc), oihw(pkg.first, C, 3, 1, kFirstIn, 12), bias_c, in, &s0->t,
-                nullptr, nullptr, k_first));
+    KB2_TRY(add(spec(9, false, 12, C, kEpiBias, fp8 ? kOutF16E4m3 : kOutF16Chunk), oihw(pkg.first, C, 3, 1, kFirstIn, 12),
+                bias(pkg.first, C), nullptr, in, &s0->t, q_of(&s0->t), sc[0], nullptr, nullptr, k_first));
   }
   const ChunkedTensor* x = &s0->t;
   for (int b = 0; b < pkg.blocks; ++b) {
     const Span8Package::Block& blk = pkg.block[b];
-    auto bias = [&](const Span8Package::Conv& c) { return std::vector<float>(c.b.begin(), c.b.begin() + C); };
     const bool last = b + 1 == pkg.blocks;
-    const ChunkedTensor* t1 = last ? &r1_last->t : &r1->t;
-    const ChunkedTensor* in_x[1] = {x};
-    KB2_TRY(add(conv3(C, C, kEpiPrelu, kOutF16Chunk, cc), oihw(blk.c[0], C, 3, 1, kStored, C), bias(blk.c[0]), in_x,
-                t1, nullptr, nullptr, k_relu));
-    const ChunkedTensor* in_1[1] = {t1};
-    KB2_TRY(add(conv3(C, C, kEpiPrelu, kOutF16Chunk, cc), oihw(blk.c[1], C, 3, 1, kStored, C), bias(blk.c[1]), in_1,
-                &r2->t, nullptr, nullptr, k_relu));
+    const float s_in = b == 0 ? sc[0] : sc[3 * b];
+    // c1: E4M3 engine -> E4M3 ReLU output (the last block's also in FP16 for conv_cat)
+    const ChunkedTensor* in_x[1] = {fp8 ? q_of(x) : x};
+    if (fp8) {
+      if (last)
+        KB2_TRY(add(spec(9, true, C, C, kEpiPrelu, kOutF16E4m3), oihw(blk.c[0], C, 3, 1, kStored, C), bias(blk.c[0], C),
+                    &s_in, in_x, &r1_last->t, &r1->t, sc[1 + 3 * b], nullptr, nullptr, k_relu));
+      else
+        KB2_TRY(add(spec(9, true, C, C, kEpiPrelu, kOutE4m3Chunk), oihw(blk.c[0], C, 3, 1, kStored, C), bias(blk.c[0], C),
+                    &s_in, in_x, nullptr, &r1->t, sc[1 + 3 * b], nullptr, nullptr, k_relu));
+    } else {
+      KB2_TRY(add(spec(9, false, C, C, kEpiPrelu, kOutF16Chunk), oihw(blk.c[0], C, 3, 1, kStored, C), bias(blk.c[0], C),
+                  nullptr, in_x, last ? &r1_last->t : &r1->t, nullptr, 1.0f, nullptr, nullptr, k_relu));
+    }
+    // c2 reads the E4M3 ReLU output (FP16: the last block's own copy)
+    const ChunkedTensor* in_1[1] = {fp8 || !last ? &r1->t : &r1_last->t};
+    const float s1 = sc[1 + 3 * b], s2 = sc[2 + 3 * b];
+    if (fp8)
+      KB2_TRY(add(spec(9, true, C, C, kEpiPrelu, kOutE4m3Chunk), oihw(blk.c[1], C, 3, 1, kStored, C), bias(blk.c[1], C),
+                  &s1, in_1, nullptr, &r2->t, s2, nullptr, nullptr, k_relu));
+    else
+      KB2_TRY(add(spec(9, false, C, C, kEpiPrelu, kOutF16Chunk), oihw(blk.c[1], C, 3, 1, kStored, C), bias(blk.c[1], C),
+                  nullptr, in_1, &r2->t, nullptr, 1.0f, nullptr, nullptr, k_relu));
     const ChunkedTensor* in_2[1] = {&r2->t};
-    KB2_TRY(add(conv3(C, C, kEpiBias, kOutF16Chunk, cc), oihw(blk.c[2], C, 3, 1, kStored, C), bias(blk.c[2]), in_2,
-                &c3->t, nullptr, nullptr, k_c3));
+    KB2_TRY(add(spec(9, fp8, C, C, kEpiBias, kOutF16Chunk), oihw(blk.c[2], C, 3, 1, kStored, C), bias(blk.c[2], C),
+                fp8 ? &s2 : nullptr, in_2, &c3->t, nullptr, 1.0f, nullptr, nullptr, k_c3));
     // the block output: block 0's is kept for conv_cat; the others alternate between two buffers
     const ChunkedTensor* xo = b == 0 ? &x1->t : (x == &xa->t ? &xb->t : &xa->t);
-    ConvSpec g;
-    g.taps = 1;
-    g.cin = C;
-    g.n_real = C;
-    g.n_pad = C;
-    g.epi = kEpiTanhGate;
-    g.out = kOutF16Chunk;
-    g.out_chunks = cc;
     const ChunkedTensor* in_3[1] = {&c3->t};
-    KB2_TRY(add(g, oihw(blk.att, C, 1, 1, kStored, C), bias(blk.att), in_3, xo, x, &c3->t, k_gate));
+    KB2_TRY(add(spec(1, false, C, C, kEpiTanhGate, fp8 ? kOutF16E4m3 : kOutF16Chunk), oihw(blk.att, C, 1, 1, kStored, C),
+                bias(blk.att, C), nullptr, in_3, xo, q_of(xo), sc[3 + 3 * b], x, &c3->t, k_gate));
     x = xo;
   }
   {
-    ConvSpec s;
-    s.taps = 1;
-    s.n_sources = 4;
-    s.cin = C;
-    s.n_real = C;
-    s.n_pad = C;
-    s.epi = kEpiBias;
-    s.out = kOutF16Chunk;
-    s.out_chunks = cc;
+    ConvSpec sp = spec(1, false, C, C, kEpiBias, kOutF16Chunk);
+    sp.n_sources = 4;
     const ChunkedTensor* in[4] = {&s0->t, x, &x1->t, &r1_last->t};
-    KB2_TRY(add(s, oihw(pkg.concat, C, 1, 4, kStored, C), std::vector<float>(pkg.concat.b.begin(), pkg.concat.b.begin() + C),
-                in, &cat->t, nullptr, nullptr, k_cat));
+    KB2_TRY(add(sp, oihw(pkg.concat, C, 1, 4, kStored, C), bias(pkg.concat, C), nullptr, in, &cat->t, nullptr, 1.0f,
+                nullptr, nullptr, k_cat));
   }
   {
     const ChunkedTensor* in[1] = {&cat->t};
-    KB2_TRY(add(conv3(C, kPixelOut, kEpiBias, kOutPixShuf4, 0), oihw(pkg.pixel, kPixelOut, 3, 1, kStored, C), pkg.pixel.b,
-                in, nullptr, nullptr, nullptr, k_pix));
+    KB2_TRY(add(spec(9, false, C, kPixelOut, kEpiBias, kOutPixShuf4), oihw(pkg.pixel, kPixelOut, 3, 1, kStored, C),
+                pkg.pixel.b, nullptr, in, nullptr, nullptr, 1.0f, nullptr, nullptr, k_pix));
   }
-  for (auto* t : {&u, &s0, &xa, &xb, &x1, &r1, &r1_last, &r2, &c3, &cat}) tensors_.push_back(std::move(*t));
+  for (auto* t : {&u, &s0, &xa, &xb, &x1, &r1, &r1_last, &r2, &c3, &cat, &s0q, &xaq, &xbq, &x1q})
+    if (*t) tensors_.push_back(std::move(*t));
   return Status::Ok();
 }
 
@@ -309,13 +341,16 @@ Status Span8Net::run(cudaStream_t stream, const void* in, void* out, int batch) 
     const ConvSpec& sp = s.layer->spec;
     const double flops = 2.0 * sp.taps * sp.n_sources * sp.cin * sp.n_real * px;
     // algorithmic bytes: every FP16 source pixel and residual read once, every output written once
-    const double in_b = 2.0 * sp.n_sources * s.layer->args.chunks * 8;
+    const double in_b = 16.0 * sp.n_sources * s.layer->args.chunks;
     const double res_b = (s.residual != nullptr ? 2.0 * ch_ : 0.0) + (s.residual2 != nullptr ? 2.0 * ch_ : 0.0);
-    const double out_b = 2.0 * sp.n_real;
+    const double out_b = (sp.out == kOutE4m3Chunk ? 1.0 : 2.0) * sp.n_real + (s.out2 != nullptr ? sp.n_real : 0.0);
     const double bytes = (in_b + res_b + out_b) * px;
     KB2_TRY(timer_.begin(stream));
-    KB2_TRY(s.layer->launch(stream, batch, s.out != nullptr ? static_cast<void*>(s.out->ptr) : out,
-                            s.residual != nullptr ? s.residual->ptr : nullptr, 1.0f, 1.0f, nullptr,
+    // E4M3-only layers write their one output through `out2`'s tensor
+    const ChunkedTensor* o = s.out != nullptr ? s.out : (s.out2 != nullptr && sp.out == kOutE4m3Chunk ? s.out2 : nullptr);
+    void* o2 = s.out != nullptr && s.out2 != nullptr ? static_cast<void*>(s.out2->ptr) : nullptr;
+    KB2_TRY(s.layer->launch(stream, batch, o != nullptr ? static_cast<void*>(o->ptr) : out,
+                            s.residual != nullptr ? s.residual->ptr : nullptr, s.out_inv_scale, 1.0f, o2,
                             s.residual != nullptr ? s.residual->chunks : 0,
                             s.residual2 != nullptr ? s.residual2->ptr : nullptr));
     KB2_TRY(timer_.end(s.kind, flops, bytes, stream));

@@ -36,7 +36,9 @@ Status parse_span8(const void* bytes, uint64_t n, Span8Package& out);
 
 class Span8Net {
  public:
-  Status create(const Span8Package& pkg, int max_batch, int H, int W);
+  // fp8: the blocks' 3x3 convs in E4M3 with the package's activation scales (an FP8 package);
+  // otherwise every layer in FP16.
+  Status create(const Span8Package& pkg, bool fp8, int max_batch, int H, int W);
   // in: NCHW F16 [batch][3][H][W]; out: NCHW F16 [batch][3][2H][2W] (device pointers).
   Status run(cudaStream_t stream, const void* in, void* out, int batch);
   size_t device_bytes() const;
@@ -55,13 +57,16 @@ class Span8Net {
   struct Step {
     ConvLayer* layer;
     const ChunkedTensor* out;  // null: the caller's output frame
+    const ChunkedTensor* out2;  // E4M3 copy (dual-output layers), or null
+    float out_inv_scale;        // 1 / scale of the E4M3 output
     const ChunkedTensor* residual;
     const ChunkedTensor* residual2;
     int kind;
   };
-  Status make_tensor(std::unique_ptr<Tensor>& t, int chunks);
+  Status make_tensor(std::unique_ptr<Tensor>& t, int chunks, bool fp8 = false);
 
   int max_batch_ = 0, H_ = 0, W_ = 0, h_ = 0, w_ = 0, ch_ = 0;
+  bool fp8_ = false;
   DeviceBuffer err_;
   std::vector<std::unique_ptr<Tensor>> tensors_;
   std::vector<std::unique_ptr<ConvLayer>> layers_;
