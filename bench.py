@@ -1,6 +1,6 @@
 """Benchmark of the frame path: SPAN x2 1080p -> 2160p on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8|rife|janai] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8|rife|janai|janai8] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: frames shard across GPUs, no collective)
 
 A step is one batch of 8 synthetic 1080p frames through the engine (the contract's configs[1]:
@@ -8,7 +8,9 @@ FP16, batch 8, 240 frames per GPU by default = 30 steps); `--workload span8` is 
 E4M3), `--workload rife` is configs[3] (IFNet FP16, 8 frame pairs per step at t = 0.5;
 `--height 2160 --width 3840` for the 4K interpolation rate), `--workload janai` the AnimeJaNai
 unshuffle SPAN b8f64 (8 blocks x 64 channels at half resolution, FP16) read from a seeded .span8
-package (the first of the contract's "next" rows). `value` is whole-job frames/s with the
+package (the first of the contract's "next" rows), `--workload janai8` the same model from an FP8
+package (E4M3 blocks, activation scales calibrated on crops of the frames). `value` is whole-job
+frames/s with the
 inputs resident in HBM; `e2e` is the same through the public C ABI with pinned host frames, the
 host->device copy and the device->host read of every output inside the timed region. `roofline`
 times the dominant kernel with CUDA events on its launching stream during the timed steps.
@@ -42,7 +44,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["span16", "span8", "rife", "janai"], default="span16")
+    ap.add_argument("--workload", choices=["span16", "span8", "rife", "janai", "janai8"], default="span16")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--height", type=int, default=FRAME_H)
     ap.add_argument("--width", type=int, default=FRAME_W)
@@ -172,6 +174,20 @@ def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, tim
     return sum(done) * ch * cw / float(fh * fw), dt
 
 
+def janai_package(fp8, H, W):
+    """The seeded b8f64 .span8 package of the janai workloads; FP8: activation scales calibrated by
+    the CPU restatement on four 64x128 crops of seeded frames (the reference derives them offline,
+    derive.h:42-62)."""
+    import numpy as np
+    from oracle import nets
+    from synth import anime_frames
+    p = nets.span8_init(8, 64, seed=3)
+    if fp8:
+        crops = anime_frames(4, min(H, 64), min(W, 128), seed=900).astype(np.float16).astype(np.float32)
+        p = nets.span8_fp8_package(p, crops)
+    return nets.span8_package(p)
+
+
 def host_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -207,15 +223,16 @@ def workload_desc(args, world=1):
                   "parallelism": f"pair-sharded x{world}, no collective",
                   "l2": "working set > L2: block 3 reads and writes 8 x 67 MB inputs and 8 x 33 MB activations"}
         return metric, "f16", config
-    if args.workload == "janai":
+    if args.workload in ("janai", "janai8"):
+        q = args.workload == "janai8"
         metric = ("SPAN b8f64 unshuffle x2 1080p->2160p frames/s" if (H, W) == (FRAME_H, FRAME_W)
                   else f"SPAN b8f64 unshuffle x2 {W}x{H} frames/s")
-        config = {"workload": f"AnimeJaNai unshuffle SPAN b8f64 FP16 (.span8 package, seeded), batch {B}, "
-                              f"{H}x{W} -> {2 * H}x{2 * W}",
+        config = {"workload": f"AnimeJaNai unshuffle SPAN b8f64 {'E4M3 blocks' if q else 'FP16'} "
+                              f"(.span8 package, seeded), batch {B}, {H}x{W} -> {2 * H}x{2 * W}",
                   "global_batch": B * world, "frames_per_gpu": B * args.steps,
                   "parallelism": f"frame-sharded x{world}, no collective",
                   "l2": "working set > L2: each layer reads and writes 8 x 66 MB activations (half resolution)"}
-        return metric, "f16", config
+        return metric, ("e4m3+f16" if q else "f16"), config
     fp8 = args.workload == "span8"
     metric = "SPAN x2 1080p->2160p frames/s" if (H, W) == (FRAME_H, FRAME_W) else f"SPAN x2 {W}x{H} frames/s"
     config = {"workload": ("configs[2] SPAN x2 FP8 E4M3" if fp8 else "configs[1] SPAN x2 FP16")
@@ -244,9 +261,9 @@ def run_reference(args):
         fa, fb = shifted_pair(args.height, args.width, 0)
         frame, frame_b = np.ascontiguousarray(fa, np.float32), np.ascontiguousarray(fb, np.float32)
         flat = nets.ifnet_flat(nets.ifnet_init(2))
-    elif args.workload == "janai":
+    elif args.workload in ("janai", "janai8"):
         frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
-        flat = nets.span8_package(nets.span8_init(8, 64, seed=3))
+        flat = janai_package(args.workload == "janai8", args.height, args.width)
     else:
         frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
         flat = nets.span_flat(nets.span_init(1))
@@ -302,13 +319,15 @@ def run_ours(args):
     B, H, W = args.batch, args.height, args.width
     rife = args.workload == "rife"
     fp8 = args.workload == "span8"
-    janai = args.workload == "janai"
+    janai = args.workload in ("janai", "janai8")
     metric, dtype, config = workload_desc(args, world)
     if janai:
-        flat = nets.span8_package(nets.span8_init(8, 64, seed=3))
+        q = args.workload == "janai8"
+        flat = janai_package(q, H, W)
         frames = anime_frames(B, H, W, seed=shard.frame_seed(10, rank, 0)).astype(np.float16)
         frames_b = None
-        eng = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, flat, H, W, max_batch=B, device=local_rank)
+        eng = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, flat, H, W, max_batch=B, precision=kb.PREC_FP8 if q else kb.PREC_FP16,
+                        device=local_rank)
         host_in = [frames]
         out_shape = (B, 3, 2 * H, 2 * W)
     elif rife:
