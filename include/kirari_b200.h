@@ -53,7 +53,8 @@ typedef struct kb2_tensor {
 /* KB2_MODEL_SPAN_UNSHUFFLE: the AnimeJaNai "unshuffle" SPAN x2 (b5f48, b8f64 ...) of a .span8
  * package (the reference's span_fp8::Package, src/gpu/span_fp8/package.h:1-17, read as
  * span_fp8::parse does, package.cpp:143); `weights` / `weights_bytes` are then the package file's
- * bytes, and the engine runs in FP16. Same frames as KB2_MODEL_SPAN_X2 (even H and W). */
+ * bytes. KB2_PREC_FP16 runs any package in FP16; KB2_PREC_FP8_E4M3 runs an FP8 package's blocks in
+ * E4M3 with its own activation scales. Same frames as KB2_MODEL_SPAN_X2 (even H and W). */
 typedef enum kb2_model { KB2_MODEL_SPAN_X2 = 1, KB2_MODEL_IFNET = 2, KB2_MODEL_SPAN_UNSHUFFLE = 3 } kb2_model;
 typedef enum kb2_precision { KB2_PREC_FP16 = 1, KB2_PREC_FP8_E4M3 = 2 } kb2_precision;
 
