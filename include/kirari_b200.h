@@ -115,6 +115,14 @@ int kb2_set_timestep(kb2_engine* engine, float timestep);
  * KB2_KERNEL_TIMEOUT with the code in *code (which wait gave up). */
 int kb2_check_device(kb2_engine* engine, void* stream, int32_t* code);
 
+/* No counterpart in the reference. Self-test of the bounded device waits behind KB2_KERNEL_TIMEOUT:
+ * on `device`, one thread waits on a barrier that nothing completes, through the same wait every
+ * kernel of this library uses; the wait gives up after its time limit (2 s), records its code and
+ * the kernel ends normally. Returns KB2_KERNEL_TIMEOUT with the code (0x500) in *code and the time
+ * the device waited in *waited_seconds (either may be null); the device stays usable. Blocks the
+ * calling thread for that time; allocates 16 bytes of device memory. */
+int kb2_selftest_bounded_wait(int32_t device, int32_t* code, double* waited_seconds);
+
 /* SPAN FP16 engine only: runs the frames through the FP16 network and returns, per quantised tensor,
  * the maximum |value| seen (19 peaks: [3b] block b input, [3b+1] / [3b+2] its two activations,
  * [18] last block output), the calibration of span_fp8::derive (src/gpu/span_fp8/derive.h:42-46).

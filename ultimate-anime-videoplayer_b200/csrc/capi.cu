@@ -162,6 +162,14 @@ int kb2_warp_taps(void* stream, const float* flow, int32_t n, int32_t h, int32_t
   }
 }
 
+int kb2_selftest_bounded_wait(int32_t device, int32_t* code, double* waited_seconds) {
+  try {
+    return kb2::selftest_bounded_wait(device, code, waited_seconds).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
 int kb2_set_profiling(kb2_engine* engine, int32_t enable) {
   if (engine == nullptr) return KB2_INVALID_ARGUMENT;
   return set_error(engine, engine->impl->set_profiling(enable != 0));

@@ -47,4 +47,8 @@ class Engine {
 
 Status make_engine(const kb2_engine_desc& desc, std::unique_ptr<Engine>& out);
 
+// kb2_selftest_bounded_wait (selftest.cu): KB2_KERNEL_TIMEOUT with the wait's error code and the time
+// the device waited, when the bounded wait gave up as designed.
+Status selftest_bounded_wait(int device, int32_t* code, double* waited_s);
+
 }  // namespace kb2

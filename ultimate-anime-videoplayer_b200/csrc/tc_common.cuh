@@ -19,6 +19,7 @@ enum DeviceError : int {
   kErrWaitMma = 0x200,       // MMA issuer waited too long for data or a free accumulator
   kErrWaitEpilogue = 0x300,  // epilogue waited too long for an accumulator
   kErrWaitDrain = 0x400,     // end-of-kernel drain of copies / MMAs in flight timed out
+  kErrWaitSelftest = 0x500,  // kb2_selftest_bounded_wait: a wait on a barrier that nothing completes
 };
 
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s

@@ -38,7 +38,7 @@ PREC_FP8 = 2
 EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "kb2_last_error",
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
-           "kb2_warp_taps")
+           "kb2_warp_taps", "kb2_selftest_bounded_wait")
 
 
 class KB2Error(RuntimeError):
@@ -90,6 +90,8 @@ def lib():
                                          ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
         L.kb2_span_calibrate_static.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Tensor),
                                                 ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
+        L.kb2_selftest_bounded_wait.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
+                                                ctypes.POINTER(ctypes.c_double)]
         L.kb2_warp_taps.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                     ctypes.c_void_p, ctypes.c_void_p]
         L.kb2_set_profiling.argtypes = [ctypes.c_void_p, ctypes.c_int32]
@@ -228,3 +230,11 @@ def warp_taps(flow, stream=None):
     if rc != KB2_OK:
         raise KB2Error(rc, "kb2_warp_taps")
     return taps, weights
+
+
+def selftest_bounded_wait(device=0):
+    """kb2_selftest_bounded_wait: (status, error code, seconds the device waited)."""
+    code = ctypes.c_int32(0)
+    waited = ctypes.c_double(0.0)
+    rc = lib().kb2_selftest_bounded_wait(device, ctypes.byref(code), ctypes.byref(waited))
+    return rc, code.value, waited.value
