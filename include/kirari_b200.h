@@ -168,6 +168,31 @@ typedef struct kb2_layer_profile {
   double bytes;          /* algorithmic HBM bytes per launch (inputs + outputs once), averaged likewise */
 } kb2_layer_profile;
 
+/* Motion of frame pairs at their middle, as RIFE estimates it (the reference's kernels::ref::Motion,
+ * src/kernels/ref/warp.h:16-28): `flow` device FP32 [n][4][plane_h][plane_w] (f0x, f0y, f1x, f1y:
+ * displacements to frame a and to frame b, in pixels of the window), `mask` device FP32
+ * [n][plane_h][plane_w] (weight of frame a), and the frames' window in those planes. */
+typedef struct kb2_motion {
+  const float* flow;
+  const float* mask;
+  int32_t plane_h, plane_w;
+  int32_t x, y, width, height;
+} kb2_motion;
+
+/* Frames at instant t in (0, 1) from frames a, b (F16 [n,3,H,W], device) and their mid-pair
+ * motion, into out (F16 [n,3,H,W]); asynchronous on `stream`. Replaces warp_blend_at
+ * (src/kernels/ref/warp.cpp:261; its CUDA form k_warp_blend_mid): t = 1/2 reads flow and mask as
+ * they are; other t move each point on a straight line from the middle and weight a by the blend law
+ * logit(m) = logit(mask) + 2.591 ln((1 - t) / t) (src/kernels/spec/warp.h:58-74). Bilinear reads. */
+int kb2_warp_blend_at(void* stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion, float t,
+                      const kb2_tensor* out);
+
+/* Per frame pair, the 99.9th percentile of the largest |flow component| over the window, in pixels of
+ * the window (flow_max, src/kernels/ref/warp.cpp:290: the test for one RIFE pass per calm pair,
+ * src/kernels/spec/warp.h:76-110). bins: the caller's device scratch of n x 256 uint32; out: host
+ * float[n]. Synchronises `stream`. */
+int kb2_flow_max(void* stream, const kb2_motion* motion, int32_t n, uint32_t* bins, float* out);
+
 int kb2_set_profiling(kb2_engine* engine, int32_t enable);
 int kb2_read_profile(kb2_engine* engine, kb2_layer_profile* records, int32_t capacity, int32_t* count);
 /* Kernel launches one enqueue issues (all of them this library's own kernels). */

@@ -584,3 +584,97 @@ def span8_forward(x, p, peaks=None):
     cat = _span8_conv(np.concatenate([first, cur, first_block, last_relu], axis=1), p["concat"], ch, ch, 1, groups=4)
     pix = _span8_conv(cat, p["pixel"], ch, SPAN8_PIXEL, 3)
     return pixel_shuffle(pix, 4)
+
+
+# --------------------------------------------------------------------------------------------
+# Frame synthesis at any instant from one mid-pair motion (the reference's warp_blend_at and
+# flow_max, src/kernels/ref/warp.cpp; law and constants of src/kernels/spec/warp.h:50-110)
+# --------------------------------------------------------------------------------------------
+BLEND_LAW_A, BLEND_LAW_B, BLEND_LAW_C = np.float32(1.0), np.float32(2.591), np.float32(0.0)
+MASK_EPSILON = np.float32(1e-4)
+FLOW_BINS, FLOW_BIN_STEP, FLOW_PERCENTILE = 256, np.float32(0.25), 0.999
+
+
+def _bilinear_window(p, win, x, y):
+    """Bilinear read relative to the corner of window win = (x, y, w, h) of plane p (warp.cpp:18-34):
+    clamp to the window (NaN goes to 0, as fmaxf), truncate, right / bottom neighbour clamped; FP32
+    operations in the reference's order, no contraction."""
+    wx, wy, ww, wh = win
+    f32 = np.float32
+    x = np.fmin(np.fmax(np.asarray(x, f32), f32(0)), f32(ww - 1)).astype(f32)
+    y = np.fmin(np.fmax(np.asarray(y, f32), f32(0)), f32(wh - 1)).astype(f32)
+    x0 = x.astype(np.int32)
+    y0 = y.astype(np.int32)
+    x1 = np.minimum(x0 + 1, ww - 1)
+    y1 = np.minimum(y0 + 1, wh - 1)
+    fx = (x - x0.astype(f32)).astype(f32)
+    fy = (y - y0.astype(f32)).astype(f32)
+    one = f32(1)
+    top = (p[wy + y0, wx + x0] * (one - fx) + p[wy + y0, wx + x1] * fx).astype(f32)
+    bot = (p[wy + y1, wx + x0] * (one - fx) + p[wy + y1, wx + x1] * fx).astype(f32)
+    return (top * (one - fy) + bot * fy).astype(f32)
+
+
+def warp_blend_at(a, b, flow, mask, window, t):
+    """One frame [3,h,w] at instant t in (0, 1) from frames a, b [3,h,w] and the mid-pair motion:
+    flow [4,ph,pw] (f0x, f0y, f1x, f1y), mask [ph,pw], the frame's window (x, y, w, h) in those planes
+    (warp.cpp warp_blend_at:261 with the bilinear filter, no pan lock, the motion estimated at the
+    middle). t = 1/2: flow and mask as they are; else straight-line motion from the middle and the
+    blend law logit(m) = A logit(mm) + B ln((1 - t) / t) + C."""
+    f32 = np.float32
+    a = np.asarray(a, f32)
+    b = np.asarray(b, f32)
+    flow = np.asarray(flow, f32)
+    mask = np.asarray(mask, f32)
+    _, h, w = a.shape
+    ww, wh = window[2], window[3]
+    sx = f32(w) / f32(ww)
+    sy = f32(h) / f32(wh)
+    fy, fx = np.meshgrid(np.arange(h, dtype=f32), np.arange(w, dtype=f32), indexing="ij")
+    u = ((fx + f32(0.5)) / sx - f32(0.5)).astype(f32)
+    v = ((fy + f32(0.5)) / sy - f32(0.5)).astype(f32)
+    t = f32(t)
+    one = f32(1)
+    f = [_bilinear_window(flow[c], window, u, v) for c in range(4)]
+    if t == f32(0.5):
+        ax, ay, bx, by = f
+        wgt = _bilinear_window(mask, window, u, v)
+    else:
+        u2 = (u - ((one - t) * f[0] + t * f[2])).astype(f32)
+        v2 = (v - ((one - t) * f[1] + t * f[3])).astype(f32)
+        g = [_bilinear_window(flow[c], window, u2, v2) for c in range(4)]
+        tx = (g[2] - g[0]).astype(f32)
+        ty = (g[3] - g[1]).astype(f32)
+        mm = np.fmin(np.fmax(_bilinear_window(mask, window, u2, v2), MASK_EPSILON), one - MASK_EPSILON).astype(f32)
+        z = (BLEND_LAW_A * np.log(mm / (one - mm)) + BLEND_LAW_B * np.log((one - t) / t) + BLEND_LAW_C).astype(f32)
+        wgt = (one / (one + np.exp(-z))).astype(f32)
+        ax, ay = (-t * tx).astype(f32), (-t * ty).astype(f32)
+        bx, by = ((one - t) * tx).astype(f32), ((one - t) * ty).astype(f32)
+    full = (0, 0, w, h)
+    out = np.empty_like(a)
+    for c in range(3):
+        va = _bilinear_window(a[c], full, fx + sx * ax, fy + sy * ay)
+        vb = _bilinear_window(b[c], full, fx + sx * bx, fy + sy * by)
+        out[c] = (va * wgt + vb * (one - wgt)).astype(f32)
+    return out
+
+
+def flow_max(flow, window):
+    """The 99.9th percentile of max |f| over the 4 flow planes inside the window, as the lower edge
+    of its histogram bin (256 bins of 0.25 px, the last taking the rest; warp.cpp flow_max:290,
+    spec/warp.h:91-110)."""
+    wx, wy, ww, wh = window
+    m = np.max(np.abs(np.asarray(flow, np.float32)[:, wy:wy + wh, wx:wx + ww]), axis=0)
+    m = np.where(np.isnan(m), np.float32(0), m)
+    scaled = (m / FLOW_BIN_STEP).astype(np.float32)
+    bins = np.where(~(m > 0), 0, np.where(scaled >= FLOW_BINS - 1, FLOW_BINS - 1,
+                                          np.minimum(scaled, FLOW_BINS - 1).astype(np.int64)))
+    hist = np.bincount(bins.ravel(), minlength=FLOW_BINS)
+    points = int(ww) * int(wh)
+    rank = int(float(points) * FLOW_PERCENTILE)
+    if float(rank) < float(points) * FLOW_PERCENTILE:
+        rank += 1
+    rank = max(rank, 1)
+    seen = np.cumsum(hist)
+    i = int(np.argmax(seen >= rank))
+    return float(np.float32(i) * FLOW_BIN_STEP)

@@ -111,3 +111,46 @@ def span8_forward(package: bytes, x):
             raise RuntimeError(f"kref_span8_forward: {rc} {L.kref_span8_last_error().decode(errors='replace')}")
         out[i] = oi
     return out
+
+
+def _warp_bind(L):
+    if getattr(L, "_warp_bound", False):
+        return L
+    i = ctypes.c_int
+    L.kref_warp_last_error.restype = ctypes.c_char_p
+    L.kref_warp_blend_at.argtypes = [_fp, _fp, i, i, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, _fp]
+    L.kref_warp_blend_at.restype = i
+    L.kref_flow_max.argtypes = [_fp, _fp, i, i, i, i, i, i, _fp]
+    L.kref_flow_max.restype = i
+    L._warp_bound = True
+    return L
+
+
+def warp_blend_at(a, b, flow, mask, window, t):
+    """The reference's CPU warp_blend_at (src/kernels/ref/warp.cpp:261): a, b [3,h,w], flow
+    [4,ph,pw], mask [ph,pw], window (x, y, w, h); returns [3,h,w]."""
+    L = _warp_bind(lib())
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    flow = np.ascontiguousarray(flow, np.float32)
+    mask = np.ascontiguousarray(mask, np.float32)
+    _, h, w = a.shape
+    ph, pw = mask.shape
+    out = np.zeros_like(a)
+    rc = L.kref_warp_blend_at(_ptr(a), _ptr(b), h, w, _ptr(flow), _ptr(mask), ph, pw, *window, float(t), _ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"kref_warp_blend_at: {L.kref_warp_last_error().decode(errors='replace')}")
+    return out
+
+
+def flow_max(flow, mask, window):
+    """The reference's CPU flow_max (src/kernels/ref/warp.cpp:290)."""
+    L = _warp_bind(lib())
+    flow = np.ascontiguousarray(flow, np.float32)
+    mask = np.ascontiguousarray(mask, np.float32)
+    ph, pw = mask.shape
+    out = np.zeros(1, np.float32)
+    rc = L.kref_flow_max(_ptr(flow), _ptr(mask), ph, pw, *window, _ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"kref_flow_max: {L.kref_warp_last_error().decode(errors='replace')}")
+    return float(out[0])

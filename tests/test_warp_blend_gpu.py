@@ -1,0 +1,85 @@
+"""kb2_warp_blend_at and kb2_flow_max on the B200, against the reference's own CPU warp_blend_at /
+flow_max (golden fixtures) and the numpy restatement (oracle/nets.py, pinned by
+tests/test_warp_blend.py).
+
+Bars: at t = 1/2 (flow and mask read as they are; no ln / exp) the FP16 output equals the FP16
+rounding of the restatement's FP32 result, bit for bit; at other t CUDA's logf / expf stand for the
+host's, and the output stays within 2e-3 of the FP32 result (FP16 rounding of values up to 1 plus
+that); flow_max is exact."""
+import numpy as np
+import pytest
+
+import kirari_b200 as kb
+from oracle import nets
+from util import ensure_built, golden
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ensure_built()
+
+
+def _dev(x, dtype):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dtype).cuda()
+
+
+def _run(a, b, flow, mask, win, t):
+    import torch
+    out = kb.warp_blend_at(_dev(a, torch.float16), _dev(b, torch.float16), _dev(flow, torch.float32),
+                           _dev(mask, torch.float32), win, t)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ["warp_blend_36x52_win.npz", "warp_blend_64x96_full.npz"])
+def test_warp_blend_matches_reference_golden(name):
+    g = golden(name)
+    win = tuple(int(v) for v in g["window"])
+    for i, t in enumerate(g["times"]):
+        out = _run(g["a"][None], g["b"][None], g["flow"][None], g["mask"][None], win, float(t))[0]
+        assert np.abs(out - g["out"][i]).max() <= 2e-3, f"t={t}"
+    import torch
+    got = kb.flow_max(_dev(g["flow"][None], torch.float32), _dev(g["mask"][None], torch.float32), win)
+    assert got == [float(g["flow_max"])]
+
+
+def test_warp_blend_batch_against_restatement():
+    import torch
+    rng = np.random.default_rng(7)
+    n, h, w, ph, pw = 3, 70, 130, 48, 80
+    win = (5, 3, 66, 40)
+    a = rng.random((n, 3, h, w), dtype=np.float32).astype(np.float16).astype(np.float32)
+    b = rng.random((n, 3, h, w), dtype=np.float32).astype(np.float16).astype(np.float32)
+    flow = (rng.standard_normal((n, 4, ph, pw)) * 5.0).astype(np.float32)
+    flow[1, 0, 4, 9] = np.nan  # NaN reads as 0 in the clamp, as fmaxf
+    mask = rng.random((n, ph, pw), dtype=np.float32)
+    for t in (0.5, 0.3):
+        out = _run(a, b, flow, mask, win, t)
+        for i in range(n):
+            ref = nets.warp_blend_at(a[i], b[i], flow[i], mask[i], win, t)
+            if t == 0.5:
+                np.testing.assert_array_equal(out[i], ref.astype(np.float16).astype(np.float32))
+            else:
+                assert np.abs(out[i] - ref).max() <= 2e-3
+    got = kb.flow_max(_dev(flow, torch.float32), _dev(mask, torch.float32), win)
+    assert got == [nets.flow_max(flow[i], win) for i in range(n)]
+
+
+def test_warp_blend_refusals():
+    import torch
+    a = torch.zeros((1, 3, 8, 8), dtype=torch.float16, device="cuda")
+    flow = torch.zeros((1, 4, 8, 8), dtype=torch.float32, device="cuda")
+    mask = torch.zeros((1, 8, 8), dtype=torch.float32, device="cuda")
+    for t in (0.0, 1.0, float("nan")):
+        with pytest.raises(kb.KB2Error) as e:
+            kb.warp_blend_at(a, a, flow, mask, (0, 0, 8, 8), t)
+        assert e.value.status == kb.KB2_INVALID_ARGUMENT
+    with pytest.raises(kb.KB2Error) as e:
+        kb.warp_blend_at(a, a, flow, mask, (2, 0, 8, 8), 0.5)  # window past the planes
+    assert e.value.status == kb.KB2_SHAPE_INVALID

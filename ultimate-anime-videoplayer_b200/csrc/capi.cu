@@ -162,6 +162,23 @@ int kb2_warp_taps(void* stream, const float* flow, int32_t n, int32_t h, int32_t
   }
 }
 
+int kb2_warp_blend_at(void* stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion, float t,
+                      const kb2_tensor* out) {
+  try {
+    return kb2::warp_blend_at(static_cast<cudaStream_t>(stream), a, b, motion, t, out).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
+int kb2_flow_max(void* stream, const kb2_motion* motion, int32_t n, uint32_t* bins, float* out) {
+  try {
+    return kb2::flow_max(static_cast<cudaStream_t>(stream), motion, n, bins, out).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
 int kb2_selftest_bounded_wait(int32_t device, int32_t* code, double* waited_seconds) {
   try {
     return kb2::selftest_bounded_wait(device, code, waited_seconds).code;

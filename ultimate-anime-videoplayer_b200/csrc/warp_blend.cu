@@ -1,0 +1,242 @@
+// Frames at any instant from one mid-pair motion, and the motion's size: the reference's
+// warp_blend_at and flow_max (src/kernels/ref/warp.cpp:261, :290; the law and its constants in
+// src/kernels/spec/warp.h:50-110), which let the player run RIFE once per calm pair and synthesise
+// the other instants from that one motion.
+//
+// warp_blend_at, per output pixel (x, y) of frame n (H x W), with the motion's window ww x wh:
+//   sx = W / ww, u = (x + 0.5) / sx - 0.5 (the same in y): the pixel's point in the motion grid;
+//   t = 1/2: f = flow(u, v), m = mask(u, v);
+//   other t: (u2, v2) = (u, v) - ((1 - t) f0 + t f1)(u, v); d = f1(u2, v2) - f0(u2, v2);
+//            to a -t d, to b (1 - t) d; mm = clamp(mask(u2, v2), 1e-4, 1 - 1e-4);
+//            m = 1 / (1 + exp(-(A ln(mm / (1 - mm)) + B ln((1 - t) / t) + C)));
+//   out = a(x + sx dax, y + sy day) m + b(x + sx dbx, y + sy dby) (1 - m), bilinear reads clamped to
+//   the window (motion) or the frame (images). FP32 arithmetic in the reference's order with the
+//   _rn intrinsics (no contraction); ln and exp are CUDA's logf / expf.
+// flow_max: per pair, a 256-bin histogram of max |flow component| over the window (bins of 0.25 px,
+// the last taking the rest), then the 99.9th percentile's bin edge.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "engine.h"
+
+namespace kb2 {
+
+namespace {
+
+constexpr float kLawA = 1.0f, kLawB = 2.591f, kLawC = 0.0f, kMaskEps = 1e-4f;
+constexpr int kFlowBins = 256;
+constexpr float kFlowBinStep = 0.25f;
+constexpr double kFlowPercentile = 0.999;
+
+struct MotionView {
+  const float* flow;  // [n][4][ph][pw]
+  const float* mask;  // [n][ph][pw]
+  int ph, pw, wx, wy, ww, wh;
+};
+
+// Bilinear read of plane p (row pitch pw) relative to the corner (wx, wy) of a ww x wh window:
+// clamp (NaN to 0, as fmaxf), truncate, right / bottom neighbour clamped.
+template <class T>
+__device__ __forceinline__ float load_f(const T* p, size_t i);
+template <>
+__device__ __forceinline__ float load_f<float>(const float* p, size_t i) {
+  return __ldg(p + i);
+}
+template <>
+__device__ __forceinline__ float load_f<__half>(const __half* p, size_t i) {
+  return __half2float(p[i]);
+}
+
+template <class T>
+__device__ __forceinline__ float bilinear(const T* p, int pw, int wx, int wy, int ww, int wh, float x, float y) {
+  x = fminf(fmaxf(x, 0.0f), static_cast<float>(ww - 1));
+  y = fminf(fmaxf(y, 0.0f), static_cast<float>(wh - 1));
+  const int x0 = static_cast<int>(x), y0 = static_cast<int>(y);
+  const int x1 = min(x0 + 1, ww - 1), y1 = min(y0 + 1, wh - 1);
+  const float fx = __fsub_rn(x, static_cast<float>(x0));
+  const float fy = __fsub_rn(y, static_cast<float>(y0));
+  const size_t r0 = static_cast<size_t>(wy + y0) * pw + wx, r1 = static_cast<size_t>(wy + y1) * pw + wx;
+  const float gx = __fsub_rn(1.0f, fx), gy = __fsub_rn(1.0f, fy);
+  const float top = __fadd_rn(__fmul_rn(load_f(p, r0 + x0), gx), __fmul_rn(load_f(p, r0 + x1), fx));
+  const float bot = __fadd_rn(__fmul_rn(load_f(p, r1 + x0), gx), __fmul_rn(load_f(p, r1 + x1), fx));
+  return __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy));
+}
+
+template <bool kMiddle>
+__global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half* __restrict__ b, MotionView m,
+                                     int batch, int H, int W, float t, __half* __restrict__ out) {
+  const int x = blockIdx.x * blockDim.x + threadIdx.x;
+  if (x >= W) return;
+  const float sx = __fdiv_rn(static_cast<float>(W), static_cast<float>(m.ww));
+  const float sy = __fdiv_rn(static_cast<float>(H), static_cast<float>(m.wh));
+  const float fx = static_cast<float>(x);
+  const float u = __fsub_rn(__fdiv_rn(__fadd_rn(fx, 0.5f), sx), 0.5f);
+  const size_t plane = static_cast<size_t>(m.ph) * m.pw;
+  const size_t frame = static_cast<size_t>(H) * W;
+  for (int r = blockIdx.y; r < batch * H; r += gridDim.y) {
+    const int n = r / H;
+    const int y = r - n * H;
+    const float fy = static_cast<float>(y);
+    const float v = __fsub_rn(__fdiv_rn(__fadd_rn(fy, 0.5f), sy), 0.5f);
+    const float* fl = m.flow + static_cast<size_t>(n) * 4 * plane;
+    const float* mk = m.mask + static_cast<size_t>(n) * plane;
+    float f[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) f[c] = bilinear(fl + c * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u, v);
+    float dax, day, dbx, dby, wgt;
+    if constexpr (kMiddle) {
+      dax = f[0];
+      day = f[1];
+      dbx = f[2];
+      dby = f[3];
+      wgt = bilinear(mk, m.pw, m.wx, m.wy, m.ww, m.wh, u, v);
+    } else {
+      const float s = __fsub_rn(1.0f, t);
+      const float u2 = __fsub_rn(u, __fadd_rn(__fmul_rn(s, f[0]), __fmul_rn(t, f[2])));
+      const float v2 = __fsub_rn(v, __fadd_rn(__fmul_rn(s, f[1]), __fmul_rn(t, f[3])));
+      float g[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) g[c] = bilinear(fl + c * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2);
+      const float tx = __fsub_rn(g[2], g[0]);
+      const float ty = __fsub_rn(g[3], g[1]);
+      const float mm =
+          fminf(fmaxf(bilinear(mk, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2), kMaskEps), __fsub_rn(1.0f, kMaskEps));
+      const float z = __fadd_rn(__fadd_rn(__fmul_rn(kLawA, logf(__fdiv_rn(mm, __fsub_rn(1.0f, mm)))),
+                                          __fmul_rn(kLawB, logf(__fdiv_rn(s, t)))),
+                                kLawC);
+      wgt = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+      dax = __fmul_rn(-t, tx);
+      day = __fmul_rn(-t, ty);
+      dbx = __fmul_rn(s, tx);
+      dby = __fmul_rn(s, ty);
+    }
+    const float xa = __fadd_rn(fx, __fmul_rn(sx, dax)), ya = __fadd_rn(fy, __fmul_rn(sy, day));
+    const float xb = __fadd_rn(fx, __fmul_rn(sx, dbx)), yb = __fadd_rn(fy, __fmul_rn(sy, dby));
+    const float w1 = __fsub_rn(1.0f, wgt);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const size_t pc = (static_cast<size_t>(n) * 3 + c) * frame;
+      const float va = bilinear(a + pc, W, 0, 0, W, H, xa, ya);
+      const float vb = bilinear(b + pc, W, 0, 0, W, H, xb, yb);
+      out[pc + static_cast<size_t>(y) * W + x] = __float2half_rn(__fadd_rn(__fmul_rn(va, wgt), __fmul_rn(vb, w1)));
+    }
+  }
+}
+
+// Histogram of max |flow component| over each pair's window (block histogram in shared memory).
+__global__ void flow_hist_kernel(MotionView m, int batch, unsigned int* __restrict__ bins) {
+  __shared__ unsigned int h[kFlowBins];
+  for (int i = threadIdx.x; i < kFlowBins; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const size_t plane = static_cast<size_t>(m.ph) * m.pw;
+  const int x = blockIdx.x * blockDim.x + threadIdx.x;
+  // every block keeps to one pair: blockIdx.z
+  const int n = blockIdx.z;
+  if (x < m.ww) {
+    const float* fl = m.flow + static_cast<size_t>(n) * 4 * plane;
+    for (int y = blockIdx.y; y < m.wh; y += gridDim.y) {
+      const size_t at = static_cast<size_t>(m.wy + y) * m.pw + m.wx + x;
+      float mx = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) mx = fmaxf(mx, fabsf(__ldg(fl + c * plane + at)));
+      int bin = 0;
+      if (mx > 0.0f) {
+        const float scaled = __fdiv_rn(mx, kFlowBinStep);
+        bin = scaled >= static_cast<float>(kFlowBins - 1) ? kFlowBins - 1 : static_cast<int>(scaled);
+      }
+      atomicAdd(&h[bin], 1u);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kFlowBins; i += blockDim.x)
+    if (h[i] != 0) atomicAdd(&bins[static_cast<size_t>(n) * kFlowBins + i], h[i]);
+}
+
+Status motion_view(const kb2_motion* motion, MotionView& m) {
+  if (motion == nullptr || motion->flow == nullptr || motion->mask == nullptr)
+    return refuse(KB2_INVALID_ARGUMENT, "motion: null pointer");
+  const kb2_motion& q = *motion;
+  if (q.plane_h < 1 || q.plane_w < 1 || q.plane_h > 16384 || q.plane_w > 16384)
+    return refuse(KB2_SHAPE_INVALID, "motion: plane size out of range");
+  // written without x + width, which could overflow
+  if (q.x < 0 || q.y < 0 || q.width < 1 || q.height < 1 || q.width > q.plane_w - q.x || q.height > q.plane_h - q.y)
+    return refuse(KB2_SHAPE_INVALID, "motion: window outside the planes");
+  m = MotionView{q.flow, q.mask, q.plane_h, q.plane_w, q.x, q.y, q.width, q.height};
+  return Status::Ok();
+}
+
+dim3 rows_grid(int width, int rows) {
+  const int bx = (width + 127) / 128;
+  const int by = std::max(1, std::min({rows, 65535, (16 * 148 + bx - 1) / bx}));
+  return dim3(static_cast<unsigned>(bx), static_cast<unsigned>(by));
+}
+
+}  // namespace
+
+Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion, float t,
+                     const kb2_tensor* out) {
+  if (a == nullptr || b == nullptr || out == nullptr) return refuse(KB2_INVALID_ARGUMENT, "null tensor");
+  if (!(t > 0.0f && t < 1.0f)) return refuse(KB2_INVALID_ARGUMENT, "warp_blend_at: t outside (0, 1)");
+  MotionView m{};
+  KB2_TRY(motion_view(motion, m));
+  for (const kb2_tensor* x : {a, b, out}) {
+    if (x->type != KB2_F16 || x->dims[1] != 3) return refuse(KB2_INPUT_MISMATCH, "warp_blend_at: F16 [n,3,H,W]");
+    if (x->dims[0] != a->dims[0] || x->dims[2] != a->dims[2] || x->dims[3] != a->dims[3])
+      return refuse(KB2_INPUT_MISMATCH, "warp_blend_at: frames of different shapes");
+    if (x->handle + x->offset == 0 || ((x->handle + x->offset) & 1u) != 0)
+      return refuse(KB2_INPUT_MISMATCH, "warp_blend_at: null or misaligned frame");
+  }
+  const long long n = a->dims[0], H = a->dims[2], W = a->dims[3];
+  if (n < 1 || H < 1 || W < 1 || H > 16384 || W > 16384 || n * H > (1LL << 30))
+    return refuse(KB2_SHAPE_INVALID, "warp_blend_at: frame size out of range");
+  const auto* pa = reinterpret_cast<const __half*>(a->handle + a->offset);
+  const auto* pb = reinterpret_cast<const __half*>(b->handle + b->offset);
+  auto* po = reinterpret_cast<__half*>(out->handle + out->offset);
+  const dim3 g = rows_grid(static_cast<int>(W), static_cast<int>(n * H));
+  if (t == 0.5f)
+    warp_blend_at_kernel<true><<<g, 128, 0, stream>>>(pa, pb, m, static_cast<int>(n), static_cast<int>(H),
+                                                      static_cast<int>(W), t, po);
+  else
+    warp_blend_at_kernel<false><<<g, 128, 0, stream>>>(pa, pb, m, static_cast<int>(n), static_cast<int>(H),
+                                                       static_cast<int>(W), t, po);
+  return cuda_status(cudaGetLastError(), "warp_blend_at launch");
+}
+
+Status flow_max(cudaStream_t stream, const kb2_motion* motion, int n, unsigned int* bins, float* out) {
+  if (bins == nullptr || out == nullptr) return refuse(KB2_INVALID_ARGUMENT, "flow_max: null pointer");
+  if (n < 1 || n > 65535) return refuse(KB2_SHAPE_INVALID, "flow_max: pair count out of range");
+  MotionView m{};
+  KB2_TRY(motion_view(motion, m));
+  KB2_CUDA(cudaMemsetAsync(bins, 0, static_cast<size_t>(n) * kFlowBins * sizeof(unsigned int), stream));
+  dim3 g = rows_grid(m.ww, m.wh);
+  g.y = std::max(1u, std::min(g.y, 64u));
+  g.z = static_cast<unsigned>(n);
+  flow_hist_kernel<<<g, 128, 0, stream>>>(m, n, bins);
+  KB2_CUDA(cudaGetLastError());
+  std::vector<unsigned int> h(static_cast<size_t>(n) * kFlowBins);
+  KB2_CUDA(cudaMemcpyAsync(h.data(), bins, h.size() * sizeof(unsigned int), cudaMemcpyDeviceToHost, stream));
+  KB2_CUDA(cudaStreamSynchronize(stream));
+  const unsigned long long points = static_cast<unsigned long long>(m.ww) * static_cast<unsigned long long>(m.wh);
+  for (int i = 0; i < n; ++i) {
+    // the bin of the percentile's rank (spec/warp.h flow_percentile): rank = ceil(points * 0.999), >= 1
+    auto rank = static_cast<unsigned long long>(static_cast<double>(points) * kFlowPercentile);
+    if (static_cast<double>(rank) < static_cast<double>(points) * kFlowPercentile) ++rank;
+    if (rank == 0) rank = 1;
+    unsigned long long seen = 0;
+    float v = static_cast<float>(kFlowBins - 1) * kFlowBinStep;
+    for (int k = 0; k < kFlowBins; ++k) {
+      seen += h[static_cast<size_t>(i) * kFlowBins + k];
+      if (seen >= rank) {
+        v = static_cast<float>(k) * kFlowBinStep;
+        break;
+      }
+    }
+    out[i] = v;
+  }
+  return Status::Ok();
+}
+
+}  // namespace kb2

@@ -38,7 +38,7 @@ PREC_FP8 = 2
 EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "kb2_last_error",
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
-           "kb2_warp_taps", "kb2_selftest_bounded_wait")
+           "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max")
 
 
 class KB2Error(RuntimeError):
@@ -58,6 +58,12 @@ class EngineDesc(ctypes.Structure):
                 ("height", ctypes.c_int32), ("width", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("weights", ctypes.c_void_p), ("weights_bytes", ctypes.c_uint64),
                 ("act_scales", ctypes.POINTER(ctypes.c_float)), ("act_scale_count", ctypes.c_int32)]
+
+
+class Motion(ctypes.Structure):
+    _fields_ = [("flow", ctypes.c_void_p), ("mask", ctypes.c_void_p), ("plane_h", ctypes.c_int32),
+                ("plane_w", ctypes.c_int32), ("x", ctypes.c_int32), ("y", ctypes.c_int32),
+                ("width", ctypes.c_int32), ("height", ctypes.c_int32)]
 
 
 class LayerProfile(ctypes.Structure):
@@ -90,6 +96,10 @@ def lib():
                                          ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
         L.kb2_span_calibrate_static.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Tensor),
                                                 ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
+        L.kb2_warp_blend_at.argtypes = [ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
+                                        ctypes.POINTER(Motion), ctypes.c_float, ctypes.POINTER(Tensor)]
+        L.kb2_flow_max.argtypes = [ctypes.c_void_p, ctypes.POINTER(Motion), ctypes.c_int32, ctypes.c_void_p,
+                                   ctypes.POINTER(ctypes.c_float)]
         L.kb2_selftest_bounded_wait.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
                                                 ctypes.POINTER(ctypes.c_double)]
         L.kb2_warp_taps.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
@@ -238,3 +248,35 @@ def selftest_bounded_wait(device=0):
     waited = ctypes.c_double(0.0)
     rc = lib().kb2_selftest_bounded_wait(device, ctypes.byref(code), ctypes.byref(waited))
     return rc, code.value, waited.value
+
+
+def _motion(flow, mask, window):
+    """kb2_motion over torch device tensors flow [n,4,ph,pw] and mask [n,ph,pw] (FP32, contiguous)."""
+    ph, pw = int(mask.shape[-2]), int(mask.shape[-1])
+    return Motion(flow.data_ptr(), mask.data_ptr(), ph, pw, *[int(v) for v in window])
+
+
+def warp_blend_at(a, b, flow, mask, window, t, stream=None):
+    """kb2_warp_blend_at on torch device tensors: a, b F16 [n,3,H,W]; returns F16 [n,3,H,W]."""
+    import torch
+    out = torch.empty_like(a)
+    m = _motion(flow, mask, window)
+    ta, tb, to = to_kb2_tensor(a), to_kb2_tensor(b), to_kb2_tensor(out)
+    rc = lib().kb2_warp_blend_at(_stream_handle(stream), ctypes.byref(ta), ctypes.byref(tb), ctypes.byref(m),
+                                 float(t), ctypes.byref(to))
+    if rc != KB2_OK:
+        raise KB2Error(rc, "kb2_warp_blend_at")
+    return out
+
+
+def flow_max(flow, mask, window, stream=None):
+    """kb2_flow_max on torch device tensors: one value (pixels of the window) per pair."""
+    import torch
+    n = int(flow.shape[0])
+    bins = torch.empty((n, 256), dtype=torch.int32, device=flow.device)
+    out = (ctypes.c_float * n)()
+    m = _motion(flow, mask, window)
+    rc = lib().kb2_flow_max(_stream_handle(stream), ctypes.byref(m), n, ctypes.c_void_p(bins.data_ptr()), out)
+    if rc != KB2_OK:
+        raise KB2Error(rc, "kb2_flow_max")
+    return list(out)
