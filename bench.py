@@ -1,6 +1,6 @@
 """Benchmark of the frame path: SPAN x2 1080p -> 2160p on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8|rife|janai|janai8] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload span16|span8|rife|janai|janai8|warp] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: frames shard across GPUs, no collective)
 
 A step is one batch of 8 synthetic 1080p frames through the engine (the contract's configs[1]:
@@ -9,8 +9,9 @@ E4M3), `--workload rife` is configs[3] (IFNet FP16, 8 frame pairs per step at t 
 `--height 2160 --width 3840` for the 4K interpolation rate), `--workload janai` the AnimeJaNai
 unshuffle SPAN b8f64 (8 blocks x 64 channels at half resolution, FP16) read from a seeded .span8
 package (the first of the contract's "next" rows), `--workload janai8` the same model from an FP8
-package (E4M3 blocks, activation scales calibrated on crops of the frames). `value` is whole-job
-frames/s with the
+package (E4M3 blocks, activation scales calibrated on crops of the frames), `--workload warp` the
+frames synthesised at t = 1/3 from one mid-pair motion (`kb2_warp_blend_at`, 8 pairs of 1080p with
+a RIFE-shaped motion of 1920x1088 planes). `value` is whole-job frames/s with the
 inputs resident in HBM; `e2e` is the same through the public C ABI with pinned host frames, the
 host->device copy and the device->host read of every output inside the timed region. `roofline`
 times the dominant kernel with CUDA events on its launching stream during the timed steps.
@@ -44,7 +45,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["span16", "span8", "rife", "janai", "janai8"], default="span16")
+    ap.add_argument("--workload", choices=["span16", "span8", "rife", "janai", "janai8", "warp"], default="span16")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--height", type=int, default=FRAME_H)
     ap.add_argument("--width", type=int, default=FRAME_W)
@@ -480,8 +481,223 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------------------
+# frames at any instant from one mid-pair motion (kb2_warp_blend_at)
+# ------------------------------------------------------------------------------------------------
+WARP_T = 1.0 / 3.0
+WARP_CROP = (96, 160)  # reference arm: frame crops (h, w), their motion window the same size
+
+
+def warp_inputs(B, H, W, seed):
+    """Frames a, b [B,3,H,W] FP16 values, and a RIFE-shaped motion: 4 flow planes + mask on the
+    padded plane (multiples of 32) with the frame's window at the rife_window offset; smooth flow
+    of a few pixels plus noise."""
+    import numpy as np
+    from synth import anime_frames
+    Hp, Wp = -(-H // 32) * 32, -(-W // 32) * 32
+    top, left = ((Hp - H) // 2) & ~1, ((Wp - W) // 2) & ~1
+    a = anime_frames(B, H, W, seed=seed).astype(np.float16)
+    b = np.roll(a, 3, axis=3)
+    rng = np.random.default_rng(seed)
+    yy, xx = np.meshgrid(np.linspace(0, 6.28, Hp, dtype=np.float32), np.linspace(0, 6.28, Wp, dtype=np.float32),
+                         indexing="ij")
+    base = np.stack([np.sin(xx) * 3, np.cos(yy) * 2, -np.sin(xx) * 3, -np.cos(yy) * 2]).astype(np.float32)
+    flow = np.ascontiguousarray(np.broadcast_to(base, (B, 4, Hp, Wp)) +
+                                rng.standard_normal((B, 4, Hp, Wp), dtype=np.float32) * 0.25, np.float32)
+    mask = np.ascontiguousarray(0.5 + 0.4 * np.sin(xx + yy)[None].repeat(B, 0), np.float32)
+    return a, b, flow, mask, (left, top, W, H)
+
+
+def run_warp(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import kirari_b200 as kb
+    import shard
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    B, H, W = args.batch, args.height, args.width
+    a, b, flow, mask, win = warp_inputs(B, H, W, shard.frame_seed(10, rank, 0))
+    host = [torch.from_numpy(x) for x in (a, b, flow, mask)]
+    dev = [x.cuda() for x in host]
+    stream = torch.cuda.Stream()
+    out = torch.empty_like(dev[0])
+    m = kb._motion(dev[2], dev[3], win)
+    ta, tb, to = kb.to_kb2_tensor(dev[0]), kb.to_kb2_tensor(dev[1]), kb.to_kb2_tensor(out)
+    sh = kb.ctypes.c_void_p(stream.cuda_stream)
+
+    def step(xa, xb, xo, mm):
+        rc = kb.lib().kb2_warp_blend_at(sh, kb.ctypes.byref(xa), kb.ctypes.byref(xb), kb.ctypes.byref(mm),
+                                        WARP_T, kb.ctypes.byref(xo))
+        if rc != kb.KB2_OK:
+            raise kb.KB2Error(rc, "kb2_warp_blend_at")
+
+    for _ in range(args.warmup):
+        step(ta, tb, to, m)
+    stream.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    shard.barrier("cuda")
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for e0, e1 in ev:
+        e0.record(stream)
+        step(ta, tb, to, m)
+        e1.record(stream)
+    stop.record(stream)
+    stop.synchronize()
+    shard.barrier("cuda")
+    clk = clocks.stop()
+    ms = shard.max_over_ranks(start.elapsed_time(stop), "cuda")
+    avg = float(np.mean([e0.elapsed_time(e1) for e0, e1 in ev]))
+    value = shard.whole_job_rate(B * args.steps, world, ms / 1e3)
+    # algorithmic bytes per launch: both frames and the output once (FP16), the 4 flow planes and the
+    # mask once over the window (FP32)
+    px = B * H * W
+    algo = px * (2 * 3 * 2 + 3 * 2 + 5 * 4)
+    peaks_json, peak_kind = measured_peaks()
+    achieved = algo / (avg / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": float(peaks_json["hbm_gbs"]), "unit": "GB/s",
+                "frac": achieved / float(peaks_json["hbm_gbs"]), "traffic": None, "kernel": "warp_blend_at_kernel",
+                "launches": args.steps, "avg_launch_ms": avg, "algorithmic_bytes_per_launch": algo,
+                "peak_source": f"{peak_kind} hbm_gbs"}
+    e2e = None
+    if not args.no_e2e:
+        pinned = [x.pin_memory() for x in host]
+        h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        d = [torch.empty_like(x) for x in dev]
+        md = kb._motion(d[2], d[3], win)
+        da, db = kb.to_kb2_tensor(d[0]), kb.to_kb2_tensor(d[1])
+        shard.barrier("cuda")
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                for dst, src in zip(d, pinned):
+                    dst.copy_(src, non_blocking=True)
+                step(da, db, to, md)
+                h_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+        shard.barrier("cuda")
+        e2e_s = shard.max_over_ranks(time.perf_counter() - t0, "cuda")
+        e2e = {"value": shard.whole_job_rate(B * args.steps, world, e2e_s), "unit": "frames/s",
+               "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host)),
+               "d2h_bytes_per_step": int(h_out.numel() * 2),
+               "path": "kb2_warp_blend_at with pinned host frames and motion: H2D of both frames, the flow and "
+                       "the mask, the call, D2H of the frames, serial on one stream"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = warp_reference_sample(a, b, flow, mask, win, budget_s=10.0, full=(H, W))
+    if rank == 0:
+        print(json.dumps({"metric": f"frames synthesised at t=1/3 from a mid-pair motion, {W}x{H}, frames/s",
+                          "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f16 frames, f32 motion",
+                          "data": "synthetic (seeded frames, smooth flow + noise)",
+                          "config": {"workload": f"kb2_warp_blend_at, {B} pairs of {W}x{H}, motion planes "
+                                                 f"{flow.shape[3]}x{flow.shape[2]}, t=1/3",
+                                     "global_batch": B * world, "parallelism": f"pair-sharded x{world}, no collective",
+                                     "l2": "working set > L2: 8 x 12 MB frames x 2 + 8 x 42 MB motion"},
+                          "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,
+                          "cpu_baseline": cpu}))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def warp_reference_sample(a, b, flow, mask, win, budget_s, full, threads=None):
+    """The reference's CPU warp_blend_at (oracle/_ref) on 96x160 crops of the pairs (crop motion =
+    the window's same rectangle), one crop per host thread, repeated to about `budget_s` seconds;
+    frames/s scaled by pixels to full frames."""
+    import numpy as np
+    from oracle import ref_lib
+    if not ref_lib.available():
+        return None
+    cores = threads or host_cores()
+    ch, cw = WARP_CROP
+    H, W = full
+    left, top = win[0], win[1]
+    rng = np.random.default_rng(0)
+
+    def one(k):
+        y = int(rng.integers(0, H - ch))
+        x = int(rng.integers(0, W - cw))
+        i = k % a.shape[0]
+        return (a[i, :, y:y + ch, x:x + cw].astype(np.float32), b[i, :, y:y + ch, x:x + cw].astype(np.float32),
+                flow[i][:, top + y:top + y + ch, left + x:left + x + cw], mask[i][top + y:top + y + ch, left + x:left + x + cw])
+
+    def run(reps):
+        jobs = [[one(t * reps + r) for r in range(reps)] for t in range(cores)]
+        done = [0] * cores
+
+        def work(t):
+            for ca, cb, cf, cm in jobs[t]:
+                ref_lib.warp_blend_at(ca, cb, cf, cm, (0, 0, cw, ch), WARP_T)
+                done[t] += 1
+
+        ts = [threading.Thread(target=work, args=(t,)) for t in range(cores)]
+        t0 = time.perf_counter()
+        for th in ts:
+            th.start()
+        for th in ts:
+            th.join()
+        return sum(done) * ch * cw / float(H * W), time.perf_counter() - t0
+
+    frames, dt = run(1)
+    reps = max(1, int(budget_s / max(dt, 1e-3)))
+    if reps > 1:
+        frames, dt = run(reps)
+    return {"value": frames / dt, "unit": "frames/s", "cores": cores, "kind": "reference",
+            "sample": f"{cores} threads x {reps} crops of {ch}x{cw} px (and their motion), the reference's CPU "
+                      f"warp_blend_at (oracle/_ref), scaled by pixels to {W}x{H} frames"}
+
+
+def run_warp_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    from oracle import ref_lib
+    if not ref_lib.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
+        return
+    B, H, W = args.batch, args.height, args.width
+    a, b, flow, mask, win = warp_inputs(min(B, 2), H, W, 10)
+    cores = host_cores()
+    for _ in range(args.warmup):
+        warp_reference_sample(a, b, flow, mask, win, 0.0, (H, W), threads=cores)
+    vals = []
+    total_s = 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        r = warp_reference_sample(a, b, flow, mask, win, 0.0, (H, W), threads=cores)
+        total_s += time.perf_counter() - t0
+        vals.append(r["value"])
+    value = float(statistics.mean(vals))
+    print(json.dumps({"metric": f"frames synthesised at t=1/3 from a mid-pair motion, {W}x{H}, frames/s",
+                      "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                      "impl": "reference",
+                      "config": {"workload": f"warp_blend_at, {W}x{H}, t=1/3, reference CPU path"},
+                      "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cores, "kind": "reference",
+                                       "sample": f"per step: {cores} threads x 1 crop of {WARP_CROP[0]}x{WARP_CROP[1]} "
+                                                 f"px, scaled by pixels to {W}x{H} frames"},
+                      "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
 def main():
     args = parse()
+    if args.workload == "warp":
+        if args.impl == "reference":
+            run_warp_reference(args)
+        else:
+            run_warp(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
