@@ -187,6 +187,13 @@ typedef struct kb2_motion {
 int kb2_warp_blend_at(void* stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion, float t,
                       const kb2_tensor* out);
 
+/* kb2_warp_blend_at that keeps the poses (warp_blend_poses, src/kernels/ref/warp.cpp:270;
+ * src/kernels/spec/poses.h): each pixel's instant is adjusted by the ratio of the distance its point
+ * moved in the previous pair (`previous`, the same planes and window; null for a held pair) to the
+ * one it moves now, so that a character animated on twos keeps its pose over a panning background. */
+int kb2_warp_blend_poses(void* stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion,
+                         const kb2_motion* previous, float t, const kb2_tensor* out);
+
 /* Per frame pair, the 99.9th percentile of the largest |flow component| over the window, in pixels of
  * the window (flow_max, src/kernels/ref/warp.cpp:290: the test for one RIFE pass per calm pair,
  * src/kernels/spec/warp.h:76-110). bins: the caller's device scratch of n x 256 uint32; out: host

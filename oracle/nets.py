@@ -659,6 +659,72 @@ def warp_blend_at(a, b, flow, mask, window, t):
     return out
 
 
+POSE_ITERATIONS, POSE_EPSILON, POSE_TIME_LIMIT = 2, np.float32(0.01), np.float32(1e-3)
+
+
+def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t):
+    """Keep the poses (warp.cpp keeping_poses / warp_blend_poses, spec/poses.h): each pixel's instant
+    tp is adjusted by the ratio of the distance its point moved in the previous pair (prev_flow /
+    prev_mask, None for a held pair) to the one it moves now, two iterations, then warp_blend_at at
+    tp for that pixel."""
+    f32 = np.float32
+    a = np.asarray(a, f32)
+    b = np.asarray(b, f32)
+    flow = np.asarray(flow, f32)
+    mask = np.asarray(mask, f32)
+    _, h, w = a.shape
+    ww, wh = window[2], window[3]
+    sx = f32(w) / f32(ww)
+    sy = f32(h) / f32(wh)
+    fy, fx = np.meshgrid(np.arange(h, dtype=f32), np.arange(w, dtype=f32), indexing="ij")
+    u = ((fx + f32(0.5)) / sx - f32(0.5)).astype(f32)
+    v = ((fy + f32(0.5)) / sy - f32(0.5)).astype(f32)
+    one = f32(1)
+    t = f32(t)
+    tp = np.full(u.shape, t, f32)
+    B = lambda pl, x, y: _bilinear_window(pl, window, x, y)  # noqa: E731
+    for _ in range(POSE_ITERATIONS):
+        u2 = (u - ((one - tp) * B(flow[0], u, v) + tp * B(flow[2], u, v))).astype(f32)
+        v2 = (v - ((one - tp) * B(flow[1], u, v) + tp * B(flow[3], u, v))).astype(f32)
+        dx = (B(flow[2], u2, v2) - B(flow[0], u2, v2)).astype(f32)
+        dy = (B(flow[3], u2, v2) - B(flow[1], u2, v2)).astype(f32)
+        before = np.zeros_like(u)
+        if prev_flow is not None:
+            pf = np.asarray(prev_flow, f32)
+            ax = (u - tp * dx).astype(f32)
+            ay = (v - tp * dy).astype(f32)
+            qx, qy = ax, ay
+            for _step in range(2):
+                nx = (ax - B(pf[2], qx, qy)).astype(f32)
+                ny = (ay - B(pf[3], qx, qy)).astype(f32)
+                qx, qy = nx, ny
+            before = np.hypot((B(pf[2], qx, qy) - B(pf[0], qx, qy)).astype(f32),
+                              (B(pf[3], qx, qy) - B(pf[1], qx, qy)).astype(f32)).astype(f32)
+        now = np.hypot(dx, dy).astype(f32)
+        r = ((before + POSE_EPSILON) / (before + now + f32(2) * POSE_EPSILON)).astype(f32)
+        pt = np.where(t < f32(0.5), f32(2) * t * r, one - f32(2) * (one - t) * r).astype(f32)
+        tp = np.fmin(np.fmax(pt, POSE_TIME_LIMIT), one - POSE_TIME_LIMIT).astype(f32)
+    # from_middle at the per-pixel tp
+    f = [B(flow[c], u, v) for c in range(4)]
+    u2 = (u - ((one - tp) * f[0] + tp * f[2])).astype(f32)
+    v2 = (v - ((one - tp) * f[1] + tp * f[3])).astype(f32)
+    g = [B(flow[c], u2, v2) for c in range(4)]
+    tx = (g[2] - g[0]).astype(f32)
+    ty = (g[3] - g[1]).astype(f32)
+    mm = np.fmin(np.fmax(B(mask, u2, v2), MASK_EPSILON), one - MASK_EPSILON).astype(f32)
+    z = (BLEND_LAW_A * np.log(mm / (one - mm)) + BLEND_LAW_B * np.log((one - tp) / tp) + BLEND_LAW_C).astype(f32)
+    wgt = (one / (one + np.exp(-z))).astype(f32)
+    ax, ay = (-tp * tx).astype(f32), (-tp * ty).astype(f32)
+    bx, by = ((one - tp) * tx).astype(f32), ((one - tp) * ty).astype(f32)
+    full = (0, 0, w, h)
+    out = np.empty_like(a)
+    for c in range(3):
+        va = _bilinear_window(a[c], full, fx + sx * ax, fy + sy * ay)
+        vb = _bilinear_window(b[c], full, fx + sx * bx, fy + sy * by)
+        out[c] = (va * wgt + vb * (one - wgt)).astype(f32)
+    return out
+
+
 def flow_max(flow, window):
     """The 99.9th percentile of max |f| over the 4 flow planes inside the window, as the lower edge
     of its histogram bin (256 bins of 0.25 px, the last taking the rest; warp.cpp flow_max:290,

@@ -121,6 +121,8 @@ def _warp_bind(L):
     L.kref_warp_blend_at.argtypes = [_fp, _fp, i, i, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, _fp]
     L.kref_warp_blend_at.restype = i
     L.kref_flow_max.argtypes = [_fp, _fp, i, i, i, i, i, i, _fp]
+    L.kref_warp_blend_poses.argtypes = [_fp, _fp, i, i, _fp, _fp, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, _fp]
+    L.kref_warp_blend_poses.restype = i
     L.kref_flow_max.restype = i
     L._warp_bound = True
     return L
@@ -154,3 +156,23 @@ def flow_max(flow, mask, window):
     if rc != 0:
         raise RuntimeError(f"kref_flow_max: {L.kref_warp_last_error().decode(errors='replace')}")
     return float(out[0])
+
+
+def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t):
+    """The reference's CPU warp_blend_poses (src/kernels/ref/warp.cpp:270): keep the poses, with the
+    previous pair's motion (or None for a held previous pair)."""
+    L = _warp_bind(lib())
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    flow = np.ascontiguousarray(flow, np.float32)
+    mask = np.ascontiguousarray(mask, np.float32)
+    pf = None if prev_flow is None else np.ascontiguousarray(prev_flow, np.float32)
+    pm = None if prev_mask is None else np.ascontiguousarray(prev_mask, np.float32)
+    _, h, w = a.shape
+    ph, pw = mask.shape
+    out = np.zeros_like(a)
+    rc = L.kref_warp_blend_poses(_ptr(a), _ptr(b), h, w, _ptr(flow), _ptr(mask), None if pf is None else _ptr(pf),
+                                 None if pm is None else _ptr(pm), ph, pw, *window, float(t), _ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"kref_warp_blend_poses: {L.kref_warp_last_error().decode(errors='replace')}")
+    return out

@@ -48,6 +48,31 @@ int kref_warp_blend_at(const float* a, const float* b, int h, int w, const float
   return 0;
 }
 
+// warp_blend_poses (warp.cpp:270): prev_flow / prev_mask the previous pair's motion (same planes and
+// window), or null for a held previous pair.
+int kref_warp_blend_poses(const float* a, const float* b, int h, int w, const float* flow, const float* mask,
+                          const float* prev_flow, const float* prev_mask, int ph, int pw, int wx, int wy, int ww,
+                          int wh, float t, float* out) {
+  using kirari::kernels::RgbImage;
+  RgbImage ia(w, h), ib(w, h);
+  for (int c = 0; c < 3; ++c) {
+    std::memcpy(ia.planes[c].data.data(), a + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
+    std::memcpy(ib.planes[c].data.data(), b + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
+  }
+  const auto m = motion_of(flow, mask, ph, pw, wx, wy, ww, wh);
+  kirari::kernels::ref::Motion prev;
+  const bool has_prev = prev_flow != nullptr && prev_mask != nullptr;
+  if (has_prev) prev = motion_of(prev_flow, prev_mask, ph, pw, wx, wy, ww, wh);
+  auto r = kirari::kernels::ref::warp_blend_poses(ia, ib, m, has_prev ? &prev : nullptr, t);
+  if (!r) {
+    g_error = r.error().detail;
+    return 1;
+  }
+  for (int c = 0; c < 3; ++c)
+    std::memcpy(out + static_cast<size_t>(c) * h * w, r->planes[c].data.data(), sizeof(float) * h * w);
+  return 0;
+}
+
 int kref_flow_max(const float* flow, const float* mask, int ph, int pw, int wx, int wy, int ww, int wh, float* out) {
   auto r = kirari::kernels::ref::flow_max(motion_of(flow, mask, ph, pw, wx, wy, ww, wh));
   if (!r) {

@@ -1,5 +1,5 @@
-"""Generates tests/golden/warp_blend_*.npz from the reference's own CPU warp_blend_at and flow_max
-(src/kernels/ref/warp.cpp:261, :290), built into oracle/_ref/libkirari_ref.so by oracle/Makefile.
+"""Generates tests/golden/warp_*.npz from the reference's own CPU warp_blend_at, warp_blend_poses and
+flow_max (src/kernels/ref/warp.cpp:261, :270, :290), built into oracle/_ref/libkirari_ref.so by oracle/Makefile.
 
     make -C oracle
     python tests/golden/make_warp_golden.py
@@ -43,5 +43,31 @@ def main():
         print(name, outs.shape, fmax)
 
 
+def smooth_motion(ph, pw, amp, phase):
+    """A smooth flow (4 planes) and mask: keeping the poses iterates q = pa - f1'(q), which amplifies
+    rounding differences (the reference build's multiply-add contraction) on rough random fields."""
+    yy, xx = np.meshgrid(np.linspace(0, 3, ph, dtype=np.float32), np.linspace(0, 3, pw, dtype=np.float32),
+                         indexing="ij")
+    flow = np.stack([np.sin(xx + phase) * amp, np.cos(yy) * 0.75 * amp, -np.sin(xx + 1 + phase) * amp,
+                     np.cos(yy + 0.5) * 0.5 * amp]).astype(np.float32)
+    mask = (0.5 + 0.4 * np.sin(xx + yy + phase)).astype(np.float32)
+    return flow, mask
+
+
+def poses():
+    h, w, ph, pw, win = 40, 60, 32, 48, (4, 3, 40, 26)
+    rng = np.random.default_rng(3)
+    a = rng.random((3, h, w), dtype=np.float32).astype(np.float16).astype(np.float32)
+    b = rng.random((3, h, w), dtype=np.float32).astype(np.float16).astype(np.float32)
+    flow, mask = smooth_motion(ph, pw, 2.5, 0.0)
+    pflow, pmask = smooth_motion(ph, pw, 1.0, 0.7)
+    outs = np.stack([ref_lib.warp_blend_poses(a, b, flow, mask, pf, pm, win, t)
+                     for t in TIMES for pf, pm in ((pflow, pmask), (None, None))])
+    np.savez_compressed(os.path.join(OUT, "warp_poses_40x60.npz"), a=a, b=b, flow=flow, mask=mask, prev_flow=pflow,
+                        prev_mask=pmask, window=np.array(win, np.int32), times=np.array(TIMES, np.float32), out=outs)
+    print("warp_poses_40x60", outs.shape)
+
+
 if __name__ == "__main__":
     main()
+    poses()

@@ -31,3 +31,14 @@ def test_flow_max_edges():
     assert nets.flow_max(flow, win) == 0.0
     flow[0, 0, :2] = 50.0  # two points of 1,000 do: rank 999 of 1,000
     assert nets.flow_max(flow, win) == 50.0
+
+
+def test_keep_poses_restatement_matches_reference():
+    g = golden("warp_poses_40x60.npz")
+    win = tuple(int(v) for v in g["window"])
+    k = 0
+    for t in g["times"]:
+        for pf, pm in ((g["prev_flow"], g["prev_mask"]), (None, None)):
+            out = nets.warp_blend_poses(g["a"], g["b"], g["flow"], g["mask"], pf, pm, win, float(t))
+            np.testing.assert_allclose(out, g["out"][k], rtol=0, atol=1e-4)
+            k += 1

@@ -83,3 +83,19 @@ def test_warp_blend_refusals():
     with pytest.raises(kb.KB2Error) as e:
         kb.warp_blend_at(a, a, flow, mask, (2, 0, 8, 8), 0.5)  # window past the planes
     assert e.value.status == kb.KB2_SHAPE_INVALID
+
+
+def test_keep_poses_matches_reference_golden():
+    import torch
+    g = golden("warp_poses_40x60.npz")
+    win = tuple(int(v) for v in g["window"])
+    k = 0
+    for t in g["times"]:
+        for prev in (True, False):
+            out = kb.warp_blend_poses(_dev(g["a"][None], torch.float16), _dev(g["b"][None], torch.float16),
+                                      _dev(g["flow"][None], torch.float32), _dev(g["mask"][None], torch.float32),
+                                      _dev(g["prev_flow"][None], torch.float32) if prev else None,
+                                      _dev(g["prev_mask"][None], torch.float32) if prev else None, win, float(t))
+            torch.cuda.synchronize()
+            assert np.abs(out.float().cpu().numpy()[0] - g["out"][k]).max() <= 2e-3, f"t={t} prev={prev}"
+            k += 1

@@ -171,6 +171,15 @@ int kb2_warp_blend_at(void* stream, const kb2_tensor* a, const kb2_tensor* b, co
   }
 }
 
+int kb2_warp_blend_poses(void* stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion,
+                         const kb2_motion* previous, float t, const kb2_tensor* out) {
+  try {
+    return kb2::warp_blend_at(static_cast<cudaStream_t>(stream), a, b, motion, t, out, true, previous).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
 int kb2_flow_max(void* stream, const kb2_motion* motion, int32_t n, uint32_t* bins, float* out) {
   try {
     return kb2::flow_max(static_cast<cudaStream_t>(stream), motion, n, bins, out).code;

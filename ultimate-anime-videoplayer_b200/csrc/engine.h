@@ -53,7 +53,7 @@ Status selftest_bounded_wait(int device, int32_t* code, double* waited_s);
 
 // kb2_warp_blend_at / kb2_flow_max (warp_blend.cu).
 Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion, float t,
-                     const kb2_tensor* out);
+                     const kb2_tensor* out, bool keep_poses = false, const kb2_motion* previous = nullptr);
 Status flow_max(cudaStream_t stream, const kb2_motion* motion, int n, unsigned int* bins, float* out);
 
 }  // namespace kb2

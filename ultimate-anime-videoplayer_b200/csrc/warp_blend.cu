@@ -12,6 +12,10 @@
 //   out = a(x + sx dax, y + sy day) m + b(x + sx dbx, y + sy dby) (1 - m), bilinear reads clamped to
 //   the window (motion) or the frame (images). FP32 arithmetic in the reference's order with the
 //   _rn intrinsics (no contraction); ln and exp are CUDA's logf / expf.
+// warp_blend_poses (keep the poses, spec/poses.h): per pixel, two iterations of: the point seen at the
+// pixel at instant tp, its displacement D now and D' in the previous pair (q = pa - f1'(q), two steps;
+// D' = 0 for a held pair), r = (|D'| + e) / (|D'| + |D| + 2e), tp = pose_time(t, r) clamped; then the
+// straight-line blend at tp. |.| is CUDA's hypotf.
 // flow_max: per pair, a 256-bin histogram of max |flow component| over the window (bins of 0.25 px,
 // the last taking the rest), then the 99.9th percentile's bin edge.
 #include <cuda_fp16.h>
@@ -27,6 +31,9 @@ namespace kb2 {
 namespace {
 
 constexpr float kLawA = 1.0f, kLawB = 2.591f, kLawC = 0.0f, kMaskEps = 1e-4f;
+// keep the poses (spec/poses.h): iterations, distance epsilon (grid pixels), instant limit
+constexpr int kPoseIterations = 2;
+constexpr float kPoseEps = 0.01f, kPoseTimeLimit = 1e-3f;
 constexpr int kFlowBins = 256;
 constexpr float kFlowBinStep = 0.25f;
 constexpr double kFlowPercentile = 0.999;
@@ -65,9 +72,13 @@ __device__ __forceinline__ float bilinear(const T* p, int pw, int wx, int wy, in
   return __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy));
 }
 
-template <bool kMiddle>
+// kMode 0: t = 1/2, flow and mask as they are; 1: straight-line motion from the middle at t; 2: keep the
+// poses: each pixel's instant adjusted by the distance ratio to the previous pair's motion `pm`
+// (pm.flow null: a held previous pair), then mode 1 at that instant.
+template <int kMode>
 __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half* __restrict__ b, MotionView m,
-                                     int batch, int H, int W, float t, __half* __restrict__ out) {
+                                     MotionView pm, int batch, int H, int W, float t, __half* __restrict__ out) {
+  constexpr bool kMiddle = kMode == 0;
   const int x = blockIdx.x * blockDim.x + threadIdx.x;
   if (x >= W) return;
   const float sx = __fdiv_rn(static_cast<float>(W), static_cast<float>(m.ww));
@@ -86,6 +97,40 @@ __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half*
     float f[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) f[c] = bilinear(fl + c * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u, v);
+    float tq = t;  // the pixel's instant
+    if constexpr (kMode == 2) {
+      const float* pf = pm.flow != nullptr ? pm.flow + static_cast<size_t>(n) * 4 * plane : nullptr;
+      for (int k = 0; k < kPoseIterations; ++k) {
+        const float s = __fsub_rn(1.0f, tq);
+        const float u2 = __fsub_rn(u, __fadd_rn(__fmul_rn(s, f[0]), __fmul_rn(tq, f[2])));
+        const float v2 = __fsub_rn(v, __fadd_rn(__fmul_rn(s, f[1]), __fmul_rn(tq, f[3])));
+        const float dx = __fsub_rn(bilinear(fl + 2 * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2),
+                                   bilinear(fl, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2));
+        const float dy = __fsub_rn(bilinear(fl + 3 * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2),
+                                   bilinear(fl + plane, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2));
+        float before = 0.0f;
+        if (pf != nullptr) {
+          // where the point was in the previous pair: q = pa - f1'(q), two steps from pa
+          const float ax = __fsub_rn(u, __fmul_rn(tq, dx)), ay = __fsub_rn(v, __fmul_rn(tq, dy));
+          float qx = ax, qy = ay;
+          for (int step = 0; step < 2; ++step) {
+            const float nx = __fsub_rn(ax, bilinear(pf + 2 * plane, pm.pw, pm.wx, pm.wy, pm.ww, pm.wh, qx, qy));
+            const float ny = __fsub_rn(ay, bilinear(pf + 3 * plane, pm.pw, pm.wx, pm.wy, pm.ww, pm.wh, qx, qy));
+            qx = nx;
+            qy = ny;
+          }
+          before = hypotf(__fsub_rn(bilinear(pf + 2 * plane, pm.pw, pm.wx, pm.wy, pm.ww, pm.wh, qx, qy),
+                                    bilinear(pf, pm.pw, pm.wx, pm.wy, pm.ww, pm.wh, qx, qy)),
+                          __fsub_rn(bilinear(pf + 3 * plane, pm.pw, pm.wx, pm.wy, pm.ww, pm.wh, qx, qy),
+                                    bilinear(pf + plane, pm.pw, pm.wx, pm.wy, pm.ww, pm.wh, qx, qy)));
+        }
+        const float now = hypotf(dx, dy);
+        const float r = __fdiv_rn(__fadd_rn(before, kPoseEps), __fadd_rn(__fadd_rn(before, now), 2.0f * kPoseEps));
+        const float pt = t < 0.5f ? __fmul_rn(__fmul_rn(2.0f, t), r)
+                                  : __fsub_rn(1.0f, __fmul_rn(__fmul_rn(2.0f, __fsub_rn(1.0f, t)), r));
+        tq = fminf(fmaxf(pt, kPoseTimeLimit), 1.0f - kPoseTimeLimit);
+      }
+    }
     float dax, day, dbx, dby, wgt;
     if constexpr (kMiddle) {
       dax = f[0];
@@ -94,9 +139,9 @@ __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half*
       dby = f[3];
       wgt = bilinear(mk, m.pw, m.wx, m.wy, m.ww, m.wh, u, v);
     } else {
-      const float s = __fsub_rn(1.0f, t);
-      const float u2 = __fsub_rn(u, __fadd_rn(__fmul_rn(s, f[0]), __fmul_rn(t, f[2])));
-      const float v2 = __fsub_rn(v, __fadd_rn(__fmul_rn(s, f[1]), __fmul_rn(t, f[3])));
+      const float s = __fsub_rn(1.0f, tq);
+      const float u2 = __fsub_rn(u, __fadd_rn(__fmul_rn(s, f[0]), __fmul_rn(tq, f[2])));
+      const float v2 = __fsub_rn(v, __fadd_rn(__fmul_rn(s, f[1]), __fmul_rn(tq, f[3])));
       float g[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) g[c] = bilinear(fl + c * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2);
@@ -105,11 +150,11 @@ __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half*
       const float mm =
           fminf(fmaxf(bilinear(mk, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2), kMaskEps), __fsub_rn(1.0f, kMaskEps));
       const float z = __fadd_rn(__fadd_rn(__fmul_rn(kLawA, logf(__fdiv_rn(mm, __fsub_rn(1.0f, mm)))),
-                                          __fmul_rn(kLawB, logf(__fdiv_rn(s, t)))),
+                                          __fmul_rn(kLawB, logf(__fdiv_rn(s, tq)))),
                                 kLawC);
       wgt = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
-      dax = __fmul_rn(-t, tx);
-      day = __fmul_rn(-t, ty);
+      dax = __fmul_rn(-tq, tx);
+      day = __fmul_rn(-tq, ty);
       dbx = __fmul_rn(s, tx);
       dby = __fmul_rn(s, ty);
     }
@@ -177,7 +222,7 @@ dim3 rows_grid(int width, int rows) {
 }  // namespace
 
 Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor* b, const kb2_motion* motion, float t,
-                     const kb2_tensor* out) {
+                     const kb2_tensor* out, bool keep_poses, const kb2_motion* previous) {
   if (a == nullptr || b == nullptr || out == nullptr) return refuse(KB2_INVALID_ARGUMENT, "null tensor");
   if (!(t > 0.0f && t < 1.0f)) return refuse(KB2_INVALID_ARGUMENT, "warp_blend_at: t outside (0, 1)");
   MotionView m{};
@@ -195,13 +240,20 @@ Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor*
   const auto* pa = reinterpret_cast<const __half*>(a->handle + a->offset);
   const auto* pb = reinterpret_cast<const __half*>(b->handle + b->offset);
   auto* po = reinterpret_cast<__half*>(out->handle + out->offset);
+  MotionView pm{};
+  if (keep_poses && previous != nullptr) {
+    KB2_TRY(motion_view(previous, pm));
+    if (pm.ph != m.ph || pm.pw != m.pw || pm.wx != m.wx || pm.wy != m.wy || pm.ww != m.ww || pm.wh != m.wh)
+      return refuse(KB2_INPUT_MISMATCH, "warp_blend_poses: the two pairs' motions differ in size or window");
+  }
   const dim3 g = rows_grid(static_cast<int>(W), static_cast<int>(n * H));
-  if (t == 0.5f)
-    warp_blend_at_kernel<true><<<g, 128, 0, stream>>>(pa, pb, m, static_cast<int>(n), static_cast<int>(H),
-                                                      static_cast<int>(W), t, po);
+  const int nn = static_cast<int>(n), hh = static_cast<int>(H), w = static_cast<int>(W);
+  if (keep_poses)
+    warp_blend_at_kernel<2><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+  else if (t == 0.5f)
+    warp_blend_at_kernel<0><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
   else
-    warp_blend_at_kernel<false><<<g, 128, 0, stream>>>(pa, pb, m, static_cast<int>(n), static_cast<int>(H),
-                                                       static_cast<int>(W), t, po);
+    warp_blend_at_kernel<1><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
   return cuda_status(cudaGetLastError(), "warp_blend_at launch");
 }
 

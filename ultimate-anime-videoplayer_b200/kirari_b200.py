@@ -38,7 +38,8 @@ PREC_FP8 = 2
 EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "kb2_last_error",
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
-           "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max")
+           "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max",
+           "kb2_warp_blend_poses")
 
 
 class KB2Error(RuntimeError):
@@ -98,6 +99,9 @@ def lib():
                                                 ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
         L.kb2_warp_blend_at.argtypes = [ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
                                         ctypes.POINTER(Motion), ctypes.c_float, ctypes.POINTER(Tensor)]
+        L.kb2_warp_blend_poses.argtypes = [ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
+                                           ctypes.POINTER(Motion), ctypes.POINTER(Motion), ctypes.c_float,
+                                           ctypes.POINTER(Tensor)]
         L.kb2_flow_max.argtypes = [ctypes.c_void_p, ctypes.POINTER(Motion), ctypes.c_int32, ctypes.c_void_p,
                                    ctypes.POINTER(ctypes.c_float)]
         L.kb2_selftest_bounded_wait.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
@@ -266,6 +270,20 @@ def warp_blend_at(a, b, flow, mask, window, t, stream=None):
                                  float(t), ctypes.byref(to))
     if rc != KB2_OK:
         raise KB2Error(rc, "kb2_warp_blend_at")
+    return out
+
+
+def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t, stream=None):
+    """kb2_warp_blend_poses on torch device tensors (prev_flow None: a held previous pair)."""
+    import torch
+    out = torch.empty_like(a)
+    m = _motion(flow, mask, window)
+    pm = None if prev_flow is None else _motion(prev_flow, prev_mask, window)
+    ta, tb, to = to_kb2_tensor(a), to_kb2_tensor(b), to_kb2_tensor(out)
+    rc = lib().kb2_warp_blend_poses(_stream_handle(stream), ctypes.byref(ta), ctypes.byref(tb), ctypes.byref(m),
+                                    None if pm is None else ctypes.byref(pm), float(t), ctypes.byref(to))
+    if rc != KB2_OK:
+        raise KB2Error(rc, "kb2_warp_blend_poses")
     return out
 
 
