@@ -200,6 +200,19 @@ int kb2_warp_blend_poses(void* stream, const kb2_tensor* a, const kb2_tensor* b,
  * float[n]. Synchronises `stream`. */
 int kb2_flow_max(void* stream, const kb2_motion* motion, int32_t n, uint32_t* bins, float* out);
 
+/* Display-ring pixel formats (the reference's RingPacking; src/kernels/spec/ring_pack.h). */
+typedef enum kb2_display_format {
+  KB2_DISPLAY_RGBA16 = 1,        /* 4 x u16 UNORM, alpha 65535 (8 bytes a pixel) */
+  KB2_DISPLAY_RGB10A2 = 2,       /* r | g << 10 | b << 20 | 3 << 30, 10-bit UNORM (4 bytes a pixel) */
+  KB2_DISPLAY_RGB10A2_DITHER = 3 /* the same with the pixel's fixed TPDF dither before truncation */
+} kb2_display_format;
+
+/* Packs frames (F16 [n,3,H,W], device, e.g. an engine's output) into display pixels: frame f row y
+ * at out + (f * H + y) * pitch bytes (device). The reference's ring store (store_ring,
+ * src/gpu/cuda/backend/pixel_kernels.cuh:78; contract src/kernels/spec/ring_pack.h and color.h
+ * unorm16): clamp to [0, 1] (NaN to 0), x 65535 or x 1023, + 0.5, truncate. Asynchronous on stream. */
+int kb2_pack_display(void* stream, const kb2_tensor* frames, int32_t format, void* out, int64_t pitch);
+
 int kb2_set_profiling(kb2_engine* engine, int32_t enable);
 int kb2_read_profile(kb2_engine* engine, kb2_layer_profile* records, int32_t capacity, int32_t* count);
 /* Kernel launches one enqueue issues (all of them this library's own kernels). */

@@ -744,3 +744,44 @@ def flow_max(flow, window):
     seen = np.cumsum(hist)
     i = int(np.argmax(seen >= rank))
     return float(np.float32(i) * FLOW_BIN_STEP)
+
+
+# --------------------------------------------------------------------------------------------
+# Display-ring pixels (src/kernels/spec/ring_pack.h, color.h unorm16; no contraction)
+# --------------------------------------------------------------------------------------------
+def _clamp_unit(v):
+    v = np.asarray(v, np.float32)
+    return np.where(np.isnan(v), np.float32(0), np.fmin(np.fmax(v, np.float32(0)), np.float32(1))).astype(np.float32)
+
+
+def _ring_hash(x, y, salt):
+    with np.errstate(over="ignore"):
+        x = np.asarray(x, np.uint32)
+        y = np.asarray(y, np.uint32)
+        v = (x * np.uint32(0x9E3779B1)) ^ (y * np.uint32(0x85EBCA77)) ^ np.uint32((salt * 0xC2B2AE3D) & 0xFFFFFFFF)
+        v = (v * np.uint32(747796405) + np.uint32(2891336453)).astype(np.uint32)
+        v = (((v >> ((v >> np.uint32(28)) + np.uint32(4))) ^ v) * np.uint32(277803737)).astype(np.uint32)
+        return ((v >> np.uint32(22)) ^ v).astype(np.uint32)
+
+
+def pack_display(rgb, fmt):
+    """Display pixels of one frame rgb [3,h,w]: fmt 1 RGBA16 -> uint16 [h,w,4]; 2 RGB10A2, 3 RGB10A2
+    with the pixel's TPDF dither -> uint32 [h,w] (r | g << 10 | b << 20 | 3 << 30)."""
+    f32 = np.float32
+    rgb = np.asarray(rgb, f32)
+    _, h, w = rgb.shape
+    c = _clamp_unit(rgb)
+    if fmt == 1:
+        q = (c * f32(65535) + f32(0.5)).astype(f32).astype(np.uint16)
+        return np.concatenate([q.transpose(1, 2, 0), np.full((h, w, 1), 65535, np.uint16)], axis=2)
+    if fmt == 2:
+        q = (c * f32(1023) + f32(0.5)).astype(f32).astype(np.uint32)
+    else:
+        yy, xx = np.meshgrid(np.arange(h, dtype=np.uint32), np.arange(w, dtype=np.uint32), indexing="ij")
+        u5 = ((_ring_hash(xx, yy, 5) >> np.uint32(8)).astype(f32) * f32(1.0 / 16777216.0)).astype(f32)
+        u6 = ((_ring_hash(xx, yy, 6) >> np.uint32(8)).astype(f32) * f32(1.0 / 16777216.0)).astype(f32)
+        noise = ((u5 + u6).astype(f32) - f32(1)).astype(f32)
+        biased = ((c * f32(1023) + f32(0.5)).astype(f32) + noise[None]).astype(f32)
+        q = np.where(~(biased > 0), 0, np.where(biased >= f32(1023), 1023, np.maximum(biased, 0).astype(np.uint32)))
+        q = q.astype(np.uint32)
+    return (q[0] | (q[1] << np.uint32(10)) | (q[2] << np.uint32(20)) | np.uint32(3 << 30)).astype(np.uint32)

@@ -176,3 +176,19 @@ def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t):
     if rc != 0:
         raise RuntimeError(f"kref_warp_blend_poses: {L.kref_warp_last_error().decode(errors='replace')}")
     return out
+
+
+def pack_display(rgb, fmt):
+    """The reference's display-ring packing (src/kernels/spec/ring_pack.h) of one frame [3,h,w]."""
+    L = lib()
+    if not getattr(L, "_pack_bound", False):
+        L.kref_pack_display.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        L.kref_pack_display.restype = ctypes.c_int
+        L._pack_bound = True
+    rgb = np.ascontiguousarray(rgb, np.float32)
+    _, h, w = rgb.shape
+    out = np.zeros((h, w, 4), np.uint16) if fmt == 1 else np.zeros((h, w), np.uint32)
+    rc = L.kref_pack_display(_ptr(rgb), h, w, int(fmt), out.ctypes.data_as(ctypes.c_void_p))
+    if rc != 0:
+        raise RuntimeError("kref_pack_display: unknown format")
+    return out

@@ -180,6 +180,14 @@ int kb2_warp_blend_poses(void* stream, const kb2_tensor* a, const kb2_tensor* b,
   }
 }
 
+int kb2_pack_display(void* stream, const kb2_tensor* frames, int32_t format, void* out, int64_t pitch) {
+  try {
+    return kb2::pack_display(static_cast<cudaStream_t>(stream), frames, format, out, pitch).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
 int kb2_flow_max(void* stream, const kb2_motion* motion, int32_t n, uint32_t* bins, float* out) {
   try {
     return kb2::flow_max(static_cast<cudaStream_t>(stream), motion, n, bins, out).code;

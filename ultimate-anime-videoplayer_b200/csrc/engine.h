@@ -56,4 +56,7 @@ Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor*
                      const kb2_tensor* out, bool keep_poses = false, const kb2_motion* previous = nullptr);
 Status flow_max(cudaStream_t stream, const kb2_motion* motion, int n, unsigned int* bins, float* out);
 
+// kb2_pack_display (display_pack.cu).
+Status pack_display(cudaStream_t stream, const kb2_tensor* frames, int format, void* out, long long pitch);
+
 }  // namespace kb2

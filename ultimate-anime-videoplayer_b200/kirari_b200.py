@@ -31,6 +31,7 @@ KB2_F32, KB2_F16, KB2_U8, KB2_I8 = 0, 1, 2, 3
 MODEL_SPAN_X2 = 1
 MODEL_IFNET = 2
 MODEL_SPAN_UNSHUFFLE = 3  # weights: the bytes of a .span8 package
+DISPLAY_RGBA16, DISPLAY_RGB10A2, DISPLAY_RGB10A2_DITHER = 1, 2, 3
 PREC_FP16 = 1
 PREC_FP8 = 2
 
@@ -39,7 +40,7 @@ EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
            "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max",
-           "kb2_warp_blend_poses")
+           "kb2_warp_blend_poses", "kb2_pack_display")
 
 
 class KB2Error(RuntimeError):
@@ -102,6 +103,8 @@ def lib():
         L.kb2_warp_blend_poses.argtypes = [ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
                                            ctypes.POINTER(Motion), ctypes.POINTER(Motion), ctypes.c_float,
                                            ctypes.POINTER(Tensor)]
+        L.kb2_pack_display.argtypes = [ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.c_int32, ctypes.c_void_p,
+                                       ctypes.c_int64]
         L.kb2_flow_max.argtypes = [ctypes.c_void_p, ctypes.POINTER(Motion), ctypes.c_int32, ctypes.c_void_p,
                                    ctypes.POINTER(ctypes.c_float)]
         L.kb2_selftest_bounded_wait.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
@@ -298,3 +301,22 @@ def flow_max(flow, mask, window, stream=None):
     if rc != KB2_OK:
         raise KB2Error(rc, "kb2_flow_max")
     return list(out)
+
+
+def pack_display(frames, fmt, stream=None):
+    """kb2_pack_display on an F16 [n,3,H,W] device tensor: uint16 [n,H,W,4] (RGBA16) or uint32
+    [n,H,W] (RGB10A2 forms) as an int32 / int16 torch tensor of the same bytes, rows packed."""
+    import torch
+    n, _, h, w = frames.shape
+    if fmt == DISPLAY_RGBA16:
+        out = torch.empty((n, h, w, 4), dtype=torch.int16, device=frames.device)
+        pitch = w * 8
+    else:
+        out = torch.empty((n, h, w), dtype=torch.int32, device=frames.device)
+        pitch = w * 4
+    t = to_kb2_tensor(frames)
+    rc = lib().kb2_pack_display(_stream_handle(stream), ctypes.byref(t), int(fmt), ctypes.c_void_p(out.data_ptr()),
+                                pitch)
+    if rc != KB2_OK:
+        raise KB2Error(rc, "kb2_pack_display")
+    return out
