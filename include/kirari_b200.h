@@ -177,6 +177,7 @@ typedef struct kb2_motion {
   const float* mask;
   int32_t plane_h, plane_w;
   int32_t x, y, width, height;
+  int32_t warp; /* the filter that reads frames a and b: 0 bilinear, 1 Catmull-Rom (RifeWarp) */
 } kb2_motion;
 
 /* Frames at instant t in (0, 1) from frames a, b (F16 [n,3,H,W], device) and their mid-pair

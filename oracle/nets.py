@@ -615,12 +615,57 @@ def _bilinear_window(p, win, x, y):
     return (top * (one - fy) + bot * fy).astype(f32)
 
 
-def warp_blend_at(a, b, flow, mask, window, t):
+def _cr_weights(t):
+    """Catmull-Rom weights of points -1, 0, 1, 2 for fractions t (spec/warp.h:28-34), FP32."""
+    f32 = np.float32
+    t = np.asarray(t, f32)
+    t2 = (t * t).astype(f32)
+    t3 = (t2 * t).astype(f32)
+    return [((f32(-0.5) * t3 + t2) - f32(0.5) * t).astype(f32),
+            ((f32(1.5) * t3 - f32(2.5) * t2) + f32(1)).astype(f32),
+            ((f32(-1.5) * t3 + f32(2) * t2) + f32(0.5) * t).astype(f32),
+            (f32(0.5) * t3 - f32(0.5) * t2).astype(f32)]
+
+
+def _catmull_rom(p, x, y):
+    """Catmull-Rom read of plane p [h,w] (ref/warp.cpp catmull_rom_at): clamped position, clamped
+    indices, rows then columns, the result clamped to the range of the four central samples."""
+    f32 = np.float32
+    h, w = p.shape
+    x = np.fmin(np.fmax(np.asarray(x, f32), f32(0)), f32(w - 1)).astype(f32)
+    y = np.fmin(np.fmax(np.asarray(y, f32), f32(0)), f32(h - 1)).astype(f32)
+    x0 = x.astype(np.int32)
+    y0 = y.astype(np.int32)
+    wx = _cr_weights((x - x0.astype(f32)).astype(f32))
+    wy = _cr_weights((y - y0.astype(f32)).astype(f32))
+    total = np.zeros(x.shape, f32)
+    lo = np.full(x.shape, np.inf, f32)
+    hi = np.full(x.shape, -np.inf, f32)
+    for j in range(4):
+        yy = np.clip(y0 - 1 + j, 0, h - 1)
+        row = np.zeros(x.shape, f32)
+        for i in range(4):
+            v = p[yy, np.clip(x0 - 1 + i, 0, w - 1)]
+            row = (row + v * wx[i]).astype(f32)
+            if i in (1, 2) and j in (1, 2):
+                lo = np.fmin(lo, v)
+                hi = np.fmax(hi, v)
+        total = (total + row * wy[j]).astype(f32)
+    return np.fmin(np.fmax(total, lo), hi).astype(f32)
+
+
+def _frame_read(p, x, y, warp):
+    h, w = p.shape
+    return _catmull_rom(p, x, y) if warp == 1 else _bilinear_window(p, (0, 0, w, h), x, y)
+
+
+def warp_blend_at(a, b, flow, mask, window, t, warp=0):
     """One frame [3,h,w] at instant t in (0, 1) from frames a, b [3,h,w] and the mid-pair motion:
     flow [4,ph,pw] (f0x, f0y, f1x, f1y), mask [ph,pw], the frame's window (x, y, w, h) in those planes
     (warp.cpp warp_blend_at:261 with the bilinear filter, no pan lock, the motion estimated at the
     middle). t = 1/2: flow and mask as they are; else straight-line motion from the middle and the
-    blend law logit(m) = A logit(mm) + B ln((1 - t) / t) + C."""
+    blend law logit(m) = A logit(mm) + B ln((1 - t) / t) + C. warp: the frames' filter, 0 bilinear,
+    1 Catmull-Rom."""
     f32 = np.float32
     a = np.asarray(a, f32)
     b = np.asarray(b, f32)
@@ -650,11 +695,10 @@ def warp_blend_at(a, b, flow, mask, window, t):
         wgt = (one / (one + np.exp(-z))).astype(f32)
         ax, ay = (-t * tx).astype(f32), (-t * ty).astype(f32)
         bx, by = ((one - t) * tx).astype(f32), ((one - t) * ty).astype(f32)
-    full = (0, 0, w, h)
     out = np.empty_like(a)
     for c in range(3):
-        va = _bilinear_window(a[c], full, fx + sx * ax, fy + sy * ay)
-        vb = _bilinear_window(b[c], full, fx + sx * bx, fy + sy * by)
+        va = _frame_read(a[c], (fx + sx * ax).astype(f32), (fy + sy * ay).astype(f32), warp)
+        vb = _frame_read(b[c], (fx + sx * bx).astype(f32), (fy + sy * by).astype(f32), warp)
         out[c] = (va * wgt + vb * (one - wgt)).astype(f32)
     return out
 
@@ -662,7 +706,7 @@ def warp_blend_at(a, b, flow, mask, window, t):
 POSE_ITERATIONS, POSE_EPSILON, POSE_TIME_LIMIT = 2, np.float32(0.01), np.float32(1e-3)
 
 
-def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t):
+def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t, warp=0):
     """Keep the poses (warp.cpp keeping_poses / warp_blend_poses, spec/poses.h): each pixel's instant
     tp is adjusted by the ratio of the distance its point moved in the previous pair (prev_flow /
     prev_mask, None for a held pair) to the one it moves now, two iterations, then warp_blend_at at
@@ -716,11 +760,10 @@ def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t):
     wgt = (one / (one + np.exp(-z))).astype(f32)
     ax, ay = (-tp * tx).astype(f32), (-tp * ty).astype(f32)
     bx, by = ((one - tp) * tx).astype(f32), ((one - tp) * ty).astype(f32)
-    full = (0, 0, w, h)
     out = np.empty_like(a)
     for c in range(3):
-        va = _bilinear_window(a[c], full, fx + sx * ax, fy + sy * ay)
-        vb = _bilinear_window(b[c], full, fx + sx * bx, fy + sy * by)
+        va = _frame_read(a[c], (fx + sx * ax).astype(f32), (fy + sy * ay).astype(f32), warp)
+        vb = _frame_read(b[c], (fx + sx * bx).astype(f32), (fy + sy * by).astype(f32), warp)
         out[c] = (va * wgt + vb * (one - wgt)).astype(f32)
     return out
 

@@ -118,17 +118,18 @@ def _warp_bind(L):
         return L
     i = ctypes.c_int
     L.kref_warp_last_error.restype = ctypes.c_char_p
-    L.kref_warp_blend_at.argtypes = [_fp, _fp, i, i, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, _fp]
+    L.kref_warp_blend_at.argtypes = [_fp, _fp, i, i, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, i, _fp]
     L.kref_warp_blend_at.restype = i
     L.kref_flow_max.argtypes = [_fp, _fp, i, i, i, i, i, i, _fp]
-    L.kref_warp_blend_poses.argtypes = [_fp, _fp, i, i, _fp, _fp, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, _fp]
+    L.kref_warp_blend_poses.argtypes = [_fp, _fp, i, i, _fp, _fp, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, i,
+                                        _fp]
     L.kref_warp_blend_poses.restype = i
     L.kref_flow_max.restype = i
     L._warp_bound = True
     return L
 
 
-def warp_blend_at(a, b, flow, mask, window, t):
+def warp_blend_at(a, b, flow, mask, window, t, warp=0):
     """The reference's CPU warp_blend_at (src/kernels/ref/warp.cpp:261): a, b [3,h,w], flow
     [4,ph,pw], mask [ph,pw], window (x, y, w, h); returns [3,h,w]."""
     L = _warp_bind(lib())
@@ -139,7 +140,8 @@ def warp_blend_at(a, b, flow, mask, window, t):
     _, h, w = a.shape
     ph, pw = mask.shape
     out = np.zeros_like(a)
-    rc = L.kref_warp_blend_at(_ptr(a), _ptr(b), h, w, _ptr(flow), _ptr(mask), ph, pw, *window, float(t), _ptr(out))
+    rc = L.kref_warp_blend_at(_ptr(a), _ptr(b), h, w, _ptr(flow), _ptr(mask), ph, pw, *window, float(t), int(warp),
+                              _ptr(out))
     if rc != 0:
         raise RuntimeError(f"kref_warp_blend_at: {L.kref_warp_last_error().decode(errors='replace')}")
     return out
@@ -158,7 +160,7 @@ def flow_max(flow, mask, window):
     return float(out[0])
 
 
-def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t):
+def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t, warp=0):
     """The reference's CPU warp_blend_poses (src/kernels/ref/warp.cpp:270): keep the poses, with the
     previous pair's motion (or None for a held previous pair)."""
     L = _warp_bind(lib())
@@ -172,7 +174,7 @@ def warp_blend_poses(a, b, flow, mask, prev_flow, prev_mask, window, t):
     ph, pw = mask.shape
     out = np.zeros_like(a)
     rc = L.kref_warp_blend_poses(_ptr(a), _ptr(b), h, w, _ptr(flow), _ptr(mask), None if pf is None else _ptr(pf),
-                                 None if pm is None else _ptr(pm), ph, pw, *window, float(t), _ptr(out))
+                                 None if pm is None else _ptr(pm), ph, pw, *window, float(t), int(warp), _ptr(out))
     if rc != 0:
         raise RuntimeError(f"kref_warp_blend_poses: {L.kref_warp_last_error().decode(errors='replace')}")
     return out

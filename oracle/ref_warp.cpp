@@ -11,7 +11,7 @@ namespace {
 std::string g_error;
 
 kirari::kernels::ref::Motion motion_of(const float* flow, const float* mask, int ph, int pw, int wx, int wy, int ww,
-                                        int wh) {
+                                        int wh, int filter = 0) {
   kirari::kernels::ref::Motion m;
   for (int c = 0; c < 4; ++c) {
     m.flow[c] = kirari::kernels::PlaneF(pw, ph);
@@ -20,6 +20,7 @@ kirari::kernels::ref::Motion motion_of(const float* flow, const float* mask, int
   m.mask = kirari::kernels::PlaneF(pw, ph);
   std::memcpy(m.mask.data.data(), mask, sizeof(float) * ph * pw);
   m.area = kirari::kernels::Window{.x = wx, .y = wy, .width = ww, .height = wh};
+  m.warp = filter == 1 ? kirari::kernels::RifeWarp::CatmullRom : kirari::kernels::RifeWarp::Bilinear;
   return m;
 }
 }  // namespace
@@ -31,14 +32,14 @@ const char* kref_warp_last_error() { return g_error.c_str(); }
 // a, b, out: 3 FP32 planes of h x w; flow: 4 planes and mask: 1 plane of ph x pw; window (wx, wy,
 // ww, wh) of the frame in the planes.
 int kref_warp_blend_at(const float* a, const float* b, int h, int w, const float* flow, const float* mask, int ph,
-                       int pw, int wx, int wy, int ww, int wh, float t, float* out) {
+                       int pw, int wx, int wy, int ww, int wh, float t, int filter, float* out) {
   using kirari::kernels::RgbImage;
   RgbImage ia(w, h), ib(w, h);
   for (int c = 0; c < 3; ++c) {
     std::memcpy(ia.planes[c].data.data(), a + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
     std::memcpy(ib.planes[c].data.data(), b + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
   }
-  auto r = kirari::kernels::ref::warp_blend_at(ia, ib, motion_of(flow, mask, ph, pw, wx, wy, ww, wh), t);
+  auto r = kirari::kernels::ref::warp_blend_at(ia, ib, motion_of(flow, mask, ph, pw, wx, wy, ww, wh, filter), t);
   if (!r) {
     g_error = r.error().detail;
     return 1;
@@ -52,14 +53,14 @@ int kref_warp_blend_at(const float* a, const float* b, int h, int w, const float
 // window), or null for a held previous pair.
 int kref_warp_blend_poses(const float* a, const float* b, int h, int w, const float* flow, const float* mask,
                           const float* prev_flow, const float* prev_mask, int ph, int pw, int wx, int wy, int ww,
-                          int wh, float t, float* out) {
+                          int wh, float t, int filter, float* out) {
   using kirari::kernels::RgbImage;
   RgbImage ia(w, h), ib(w, h);
   for (int c = 0; c < 3; ++c) {
     std::memcpy(ia.planes[c].data.data(), a + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
     std::memcpy(ib.planes[c].data.data(), b + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
   }
-  const auto m = motion_of(flow, mask, ph, pw, wx, wy, ww, wh);
+  const auto m = motion_of(flow, mask, ph, pw, wx, wy, ww, wh, filter);
   kirari::kernels::ref::Motion prev;
   const bool has_prev = prev_flow != nullptr && prev_mask != nullptr;
   if (has_prev) prev = motion_of(prev_flow, prev_mask, ph, pw, wx, wy, ww, wh);

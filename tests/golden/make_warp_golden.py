@@ -5,6 +5,8 @@ flow_max (src/kernels/ref/warp.cpp:261, :270, :290), built into oracle/_ref/libk
     python tests/golden/make_warp_golden.py
 
 Frames are rounded to FP16 first (the library's frame format), so the GPU path reads the same values.
+Outputs cover both frame filters (bilinear, Catmull-Rom); the reference's kernels/ sources are built
+without multiply-add contraction, as the reference builds them.
 """
 from __future__ import annotations
 
@@ -35,7 +37,9 @@ def main():
         b = rng.random((3, h, w), dtype=np.float32).astype(np.float16).astype(np.float32)
         flow = (rng.standard_normal((4, ph, pw)) * scale).astype(np.float32)
         mask = rng.random((ph, pw), dtype=np.float32)
-        outs = np.stack([ref_lib.warp_blend_at(a, b, flow, mask, win, t) for t in TIMES])
+        # [filter][t]: bilinear, then Catmull-Rom frame reads
+        outs = np.stack([np.stack([ref_lib.warp_blend_at(a, b, flow, mask, win, t, warp) for t in TIMES])
+                         for warp in (0, 1)])
         fmax = ref_lib.flow_max(flow, mask, win)
         np.savez_compressed(os.path.join(OUT, name + ".npz"), a=a, b=b, flow=flow, mask=mask,
                             window=np.array(win, np.int32), times=np.array(TIMES, np.float32), out=outs,
@@ -61,8 +65,8 @@ def poses():
     b = rng.random((3, h, w), dtype=np.float32).astype(np.float16).astype(np.float32)
     flow, mask = smooth_motion(ph, pw, 2.5, 0.0)
     pflow, pmask = smooth_motion(ph, pw, 1.0, 0.7)
-    outs = np.stack([ref_lib.warp_blend_poses(a, b, flow, mask, pf, pm, win, t)
-                     for t in TIMES for pf, pm in ((pflow, pmask), (None, None))])
+    outs = np.stack([ref_lib.warp_blend_poses(a, b, flow, mask, pf, pm, win, t, warp)
+                     for warp in (0, 1) for t in TIMES for pf, pm in ((pflow, pmask), (None, None))])
     np.savez_compressed(os.path.join(OUT, "warp_poses_40x60.npz"), a=a, b=b, flow=flow, mask=mask, prev_flow=pflow,
                         prev_mask=pmask, window=np.array(win, np.int32), times=np.array(TIMES, np.float32), out=outs)
     print("warp_poses_40x60", outs.shape)

@@ -3,7 +3,7 @@ flow_max (golden fixtures) and the numpy restatement (oracle/nets.py, pinned by
 tests/test_warp_blend.py).
 
 Bars: at t = 1/2 (flow and mask read as they are; no ln / exp) the FP16 output equals the FP16
-rounding of the restatement's FP32 result, bit for bit; at other t CUDA's logf / expf stand for the
+rounding of the reference's and the restatement's FP32 result, bit for bit (both frame filters); at other t CUDA's logf / expf stand for the
 host's, and the output stays within 2e-3 of the FP32 result (FP16 rounding of values up to 1 plus
 that); flow_max is exact."""
 import numpy as np
@@ -29,10 +29,10 @@ def _dev(x, dtype):
     return torch.from_numpy(np.ascontiguousarray(x)).to(dtype).cuda()
 
 
-def _run(a, b, flow, mask, win, t):
+def _run(a, b, flow, mask, win, t, warp=0):
     import torch
     out = kb.warp_blend_at(_dev(a, torch.float16), _dev(b, torch.float16), _dev(flow, torch.float32),
-                           _dev(mask, torch.float32), win, t)
+                           _dev(mask, torch.float32), win, t, warp=warp)
     torch.cuda.synchronize()
     return out.float().cpu().numpy()
 
@@ -41,9 +41,13 @@ def _run(a, b, flow, mask, win, t):
 def test_warp_blend_matches_reference_golden(name):
     g = golden(name)
     win = tuple(int(v) for v in g["window"])
-    for i, t in enumerate(g["times"]):
-        out = _run(g["a"][None], g["b"][None], g["flow"][None], g["mask"][None], win, float(t))[0]
-        assert np.abs(out - g["out"][i]).max() <= 2e-3, f"t={t}"
+    for warp in (0, 1):
+        for i, t in enumerate(g["times"]):
+            out = _run(g["a"][None], g["b"][None], g["flow"][None], g["mask"][None], win, float(t), warp)[0]
+            if t == 0.5:
+                np.testing.assert_array_equal(out, g["out"][warp, i].astype(np.float16).astype(np.float32))
+            else:
+                assert np.abs(out - g["out"][warp, i]).max() <= 2e-3, f"t={t} warp={warp}"
     import torch
     got = kb.flow_max(_dev(g["flow"][None], torch.float32), _dev(g["mask"][None], torch.float32), win)
     assert got == [float(g["flow_max"])]
@@ -59,10 +63,10 @@ def test_warp_blend_batch_against_restatement():
     flow = (rng.standard_normal((n, 4, ph, pw)) * 5.0).astype(np.float32)
     flow[1, 0, 4, 9] = np.nan  # NaN reads as 0 in the clamp, as fmaxf
     mask = rng.random((n, ph, pw), dtype=np.float32)
-    for t in (0.5, 0.3):
-        out = _run(a, b, flow, mask, win, t)
+    for t, warp in ((0.5, 0), (0.3, 0), (0.5, 1), (0.7, 1)):
+        out = _run(a, b, flow, mask, win, t, warp)
         for i in range(n):
-            ref = nets.warp_blend_at(a[i], b[i], flow[i], mask[i], win, t)
+            ref = nets.warp_blend_at(a[i], b[i], flow[i], mask[i], win, t, warp)
             if t == 0.5:
                 np.testing.assert_array_equal(out[i], ref.astype(np.float16).astype(np.float32))
             else:
@@ -90,12 +94,15 @@ def test_keep_poses_matches_reference_golden():
     g = golden("warp_poses_40x60.npz")
     win = tuple(int(v) for v in g["window"])
     k = 0
-    for t in g["times"]:
-        for prev in (True, False):
-            out = kb.warp_blend_poses(_dev(g["a"][None], torch.float16), _dev(g["b"][None], torch.float16),
-                                      _dev(g["flow"][None], torch.float32), _dev(g["mask"][None], torch.float32),
-                                      _dev(g["prev_flow"][None], torch.float32) if prev else None,
-                                      _dev(g["prev_mask"][None], torch.float32) if prev else None, win, float(t))
-            torch.cuda.synchronize()
-            assert np.abs(out.float().cpu().numpy()[0] - g["out"][k]).max() <= 2e-3, f"t={t} prev={prev}"
-            k += 1
+    for warp in (0, 1):
+        for t in g["times"]:
+            for prev in (True, False):
+                out = kb.warp_blend_poses(_dev(g["a"][None], torch.float16), _dev(g["b"][None], torch.float16),
+                                          _dev(g["flow"][None], torch.float32), _dev(g["mask"][None], torch.float32),
+                                          _dev(g["prev_flow"][None], torch.float32) if prev else None,
+                                          _dev(g["prev_mask"][None], torch.float32) if prev else None, win, float(t),
+                                          warp=warp)
+                torch.cuda.synchronize()
+                err = np.abs(out.float().cpu().numpy()[0] - g["out"][k]).max()
+                assert err <= 2e-3, f"t={t} prev={prev} warp={warp}"
+                k += 1

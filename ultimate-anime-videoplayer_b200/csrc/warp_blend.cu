@@ -72,10 +72,49 @@ __device__ __forceinline__ float bilinear(const T* p, int pw, int wx, int wy, in
   return __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy));
 }
 
+// Catmull-Rom read of plane p (w x h, row pitch w) at (x, y) (spec/warp.h RifeWarp::CatmullRom): the
+// position clamped to the plane, points -1 .. 2 around the truncation with clamped indices, weights
+// (-0.5 t3 + t2 - 0.5 t, 1.5 t3 - 2.5 t2 + 1, -1.5 t3 + 2 t2 + 0.5 t, 0.5 t3 - 0.5 t2), rows then
+// columns, the result clamped to the four central samples' range (ref/warp.cpp catmull_rom_at).
+__device__ __forceinline__ void cr_weights(float t, float (&w)[4]) {
+  const float t2 = __fmul_rn(t, t), t3 = __fmul_rn(t2, t);
+  w[0] = __fsub_rn(__fadd_rn(__fmul_rn(-0.5f, t3), t2), __fmul_rn(0.5f, t));
+  w[1] = __fadd_rn(__fsub_rn(__fmul_rn(1.5f, t3), __fmul_rn(2.5f, t2)), 1.0f);
+  w[2] = __fadd_rn(__fadd_rn(__fmul_rn(-1.5f, t3), __fmul_rn(2.0f, t2)), __fmul_rn(0.5f, t));
+  w[3] = __fsub_rn(__fmul_rn(0.5f, t3), __fmul_rn(0.5f, t2));
+}
+
+__device__ __forceinline__ float catmull_rom(const __half* p, int w, int h, float x, float y) {
+  x = fminf(fmaxf(x, 0.0f), static_cast<float>(w - 1));
+  y = fminf(fmaxf(y, 0.0f), static_cast<float>(h - 1));
+  const int x0 = static_cast<int>(x), y0 = static_cast<int>(y);
+  float wx[4], wy[4];
+  cr_weights(__fsub_rn(x, static_cast<float>(x0)), wx);
+  cr_weights(__fsub_rn(y, static_cast<float>(y0)), wy);
+  float sum = 0.0f, lo = __int_as_float(0x7f800000), hi = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int yy = min(max(y0 - 1 + j, 0), h - 1);
+    float row = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float v = __half2float(__ldg(p + static_cast<size_t>(yy) * w + min(max(x0 - 1 + i, 0), w - 1)));
+      row = __fadd_rn(row, __fmul_rn(v, wx[i]));
+      if ((i == 1 || i == 2) && (j == 1 || j == 2)) {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+      }
+    }
+    sum = __fadd_rn(sum, __fmul_rn(row, wy[j]));
+  }
+  return fminf(fmaxf(sum, lo), hi);
+}
+
 // kMode 0: t = 1/2, flow and mask as they are; 1: straight-line motion from the middle at t; 2: keep the
 // poses: each pixel's instant adjusted by the distance ratio to the previous pair's motion `pm`
 // (pm.flow null: a held previous pair), then mode 1 at that instant.
-template <int kMode>
+// kCatmull: frames a and b read by Catmull-Rom instead of bilinearly (the motion stays bilinear).
+template <int kMode, bool kCatmull>
 __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half* __restrict__ b, MotionView m,
                                      MotionView pm, int batch, int H, int W, float t, __half* __restrict__ out) {
   constexpr bool kMiddle = kMode == 0;
@@ -164,8 +203,8 @@ __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half*
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
       const size_t pc = (static_cast<size_t>(n) * 3 + c) * frame;
-      const float va = bilinear(a + pc, W, 0, 0, W, H, xa, ya);
-      const float vb = bilinear(b + pc, W, 0, 0, W, H, xb, yb);
+      const float va = kCatmull ? catmull_rom(a + pc, W, H, xa, ya) : bilinear(a + pc, W, 0, 0, W, H, xa, ya);
+      const float vb = kCatmull ? catmull_rom(b + pc, W, H, xb, yb) : bilinear(b + pc, W, 0, 0, W, H, xb, yb);
       out[pc + static_cast<size_t>(y) * W + x] = __float2half_rn(__fadd_rn(__fmul_rn(va, wgt), __fmul_rn(vb, w1)));
     }
   }
@@ -204,6 +243,7 @@ Status motion_view(const kb2_motion* motion, MotionView& m) {
   if (motion == nullptr || motion->flow == nullptr || motion->mask == nullptr)
     return refuse(KB2_INVALID_ARGUMENT, "motion: null pointer");
   const kb2_motion& q = *motion;
+  if (q.warp != 0 && q.warp != 1) return refuse(KB2_INVALID_ARGUMENT, "motion: warp filter 0 or 1");
   if (q.plane_h < 1 || q.plane_w < 1 || q.plane_h > 16384 || q.plane_w > 16384)
     return refuse(KB2_SHAPE_INVALID, "motion: plane size out of range");
   // written without x + width, which could overflow
@@ -248,12 +288,16 @@ Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor*
   }
   const dim3 g = rows_grid(static_cast<int>(W), static_cast<int>(n * H));
   const int nn = static_cast<int>(n), hh = static_cast<int>(H), w = static_cast<int>(W);
-  if (keep_poses)
-    warp_blend_at_kernel<2><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
-  else if (t == 0.5f)
-    warp_blend_at_kernel<0><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
-  else
-    warp_blend_at_kernel<1><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+  const int mode = keep_poses ? 2 : (t == 0.5f ? 0 : 1);
+  if (motion->warp == 1) {
+    if (mode == 2) warp_blend_at_kernel<2, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+    else if (mode == 0) warp_blend_at_kernel<0, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+    else warp_blend_at_kernel<1, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+  } else {
+    if (mode == 2) warp_blend_at_kernel<2, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+    else if (mode == 0) warp_blend_at_kernel<0, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+    else warp_blend_at_kernel<1, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+  }
   return cuda_status(cudaGetLastError(), "warp_blend_at launch");
 }
 
