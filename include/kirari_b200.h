@@ -177,7 +177,10 @@ typedef struct kb2_motion {
   const float* mask;
   int32_t plane_h, plane_w;
   int32_t x, y, width, height;
-  int32_t warp; /* the filter that reads frames a and b: 0 bilinear, 1 Catmull-Rom (RifeWarp) */
+  int32_t warp;     /* the filter that reads frames a and b: 0 bilinear, 1 Catmull-Rom (RifeWarp) */
+  int32_t pan_lock; /* 1: estimate each pair's global translation on a and b and use it where RIFE's flow
+                       is small and close to it, fading to a linear blend under half a pixel of motion
+                       (Motion::pan_lock, spec/warp_pan.h); at most 64 pairs a call; not with keep-poses */
 } kb2_motion;
 
 /* Frames at instant t in (0, 1) from frames a, b (F16 [n,3,H,W], device) and their mid-pair

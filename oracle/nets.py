@@ -659,7 +659,7 @@ def _frame_read(p, x, y, warp):
     return _catmull_rom(p, x, y) if warp == 1 else _bilinear_window(p, (0, 0, w, h), x, y)
 
 
-def warp_blend_at(a, b, flow, mask, window, t, warp=0):
+def warp_blend_at(a, b, flow, mask, window, t, warp=0, pan_lock=0):
     """One frame [3,h,w] at instant t in (0, 1) from frames a, b [3,h,w] and the mid-pair motion:
     flow [4,ph,pw] (f0x, f0y, f1x, f1y), mask [ph,pw], the frame's window (x, y, w, h) in those planes
     (warp.cpp warp_blend_at:261 with the bilinear filter, no pan lock, the motion estimated at the
@@ -681,17 +681,35 @@ def warp_blend_at(a, b, flow, mask, window, t, warp=0):
     t = f32(t)
     one = f32(1)
     f = [_bilinear_window(flow[c], window, u, v) for c in range(4)]
+    g_pan = None
+    if pan_lock:
+        dx, dy, sure = pan_estimate(a, b)
+        sm = f32(0.5)
+        g_pan = [f32(f32(-sm * f32(dx)) / sx), f32(f32(-sm * f32(dy)) / sy), f32(f32((one - sm) * f32(dx)) / sx),
+                 f32(f32((one - sm) * f32(dy)) / sy)]
+        if sure:
+            f = _pan_substitute(f, g_pan)
     if t == f32(0.5):
         ax, ay, bx, by = f
         wgt = _bilinear_window(mask, window, u, v)
+        if pan_lock:
+            mm = np.fmin(np.fmax(wgt, MASK_EPSILON), one - MASK_EPSILON).astype(f32)
+            w = _slow_fade_weight(np.hypot((f[2] - f[0]).astype(f32), (f[3] - f[1]).astype(f32)).astype(f32))
+            z = (w * np.log(mm / (one - mm)) + (one - w) * np.log((one - t) / t)).astype(f32)
+            wgt = (one / (one + np.exp(-z))).astype(f32)
     else:
         u2 = (u - ((one - t) * f[0] + t * f[2])).astype(f32)
         v2 = (v - ((one - t) * f[1] + t * f[3])).astype(f32)
         g = [_bilinear_window(flow[c], window, u2, v2) for c in range(4)]
+        if pan_lock and pan_estimate(a, b)[2]:
+            g = _pan_substitute(g, g_pan)
         tx = (g[2] - g[0]).astype(f32)
         ty = (g[3] - g[1]).astype(f32)
         mm = np.fmin(np.fmax(_bilinear_window(mask, window, u2, v2), MASK_EPSILON), one - MASK_EPSILON).astype(f32)
         z = (BLEND_LAW_A * np.log(mm / (one - mm)) + BLEND_LAW_B * np.log((one - t) / t) + BLEND_LAW_C).astype(f32)
+        if pan_lock:
+            w = _slow_fade_weight(np.hypot(tx, ty).astype(f32))
+            z = (w * z + (one - w) * np.log((one - t) / t)).astype(f32)
         wgt = (one / (one + np.exp(-z))).astype(f32)
         ax, ay = (-t * tx).astype(f32), (-t * ty).astype(f32)
         bx, by = ((one - t) * tx).astype(f32), ((one - t) * ty).astype(f32)
@@ -701,6 +719,72 @@ def warp_blend_at(a, b, flow, mask, window, t, warp=0):
         vb = _frame_read(b[c], (fx + sx * bx).astype(f32), (fy + sy * by).astype(f32), warp)
         out[c] = (va * wgt + vb * (one - wgt)).astype(f32)
     return out
+
+
+PAN_GRID, PAN_ITERATIONS = 32, 3
+PAN_LUMA = (np.float32(0.2126), np.float32(0.7152), np.float32(0.0722))
+PAN_DET_RATIO, PAN_MAX_SHIFT, PAN_FLOW_LIMIT, PAN_AGREEMENT = 1e-6, np.float32(8), np.float32(2), np.float32(1)
+SLOW_FADE_LO, SLOW_FADE_HI = np.float32(0.5), np.float32(2.0)
+
+
+def _luma(img):
+    return ((PAN_LUMA[0] * img[0] + PAN_LUMA[1] * img[1]).astype(np.float32) + PAN_LUMA[2] * img[2]).astype(np.float32)
+
+
+def pan_estimate(a, b):
+    """The pair's global translation (ref/warp_pan.cpp pan_estimate): Lucas-Kanade on the luma at a
+    32 x 32 grid, 3 iterations, double sums in point order; returns (dx, dy, sure)."""
+    f32 = np.float32
+    a = np.asarray(a, f32)
+    b = np.asarray(b, f32)
+    _, h, w = a.shape
+    if w < 16 or h < 16:
+        return 0.0, 0.0, False
+    la_img, lb_img = _luma(a), _luma(b)
+
+    def point(i, n):
+        m = n // 12 if n // 12 > 4 else 4
+        return m + (i * (n - 2 * m)) // PAN_GRID
+
+    q = np.arange(PAN_GRID * PAN_GRID)
+    px = np.array([point(i % PAN_GRID, w) for i in q])
+    py = np.array([point(i // PAN_GRID, h) for i in q])
+    la = la_img[py, px]
+    gx = (f32(0.5) * (la_img[py, px + 1] - la_img[py, px - 1])).astype(f32)
+    gy = (f32(0.5) * (la_img[py + 1, px] - la_img[py - 1, px])).astype(f32)
+    dx = dy = f32(0)
+    valid = False
+    for _ in range(PAN_ITERATIONS):
+        r = (_bilinear_window(lb_img, (0, 0, w, h), px.astype(f32) + dx, py.astype(f32) + dy) - la).astype(f32)
+        sxx = sxy = syy = sxr = syr = 0.0
+        for k in range(q.size):  # the reference's order
+            sxx += float(f32(gx[k] * gx[k]))
+            sxy += float(f32(gx[k] * gy[k]))
+            syy += float(f32(gy[k] * gy[k]))
+            sxr += float(f32(gx[k] * r[k]))
+            syr += float(f32(gy[k] * r[k]))
+        det = sxx * syy - sxy * sxy
+        valid = det > PAN_DET_RATIO * (sxx + syy) * (sxx + syy) and det > 0.0
+        if not valid:
+            break
+        dx = f32(dx - f32((syy * sxr - sxy * syr) / det))
+        dy = f32(dy - f32((sxx * syr - sxy * sxr) / det))
+    sure = valid and float(np.hypot(dx, dy)) < float(PAN_MAX_SHIFT)
+    return float(dx), float(dy), bool(sure)
+
+
+def _slow_fade_weight(d):
+    f32 = np.float32
+    s = ((np.asarray(d, f32) - SLOW_FADE_LO) / (SLOW_FADE_HI - SLOW_FADE_LO)).astype(f32)
+    s = np.where(s < 0, f32(0), np.where(s > 1, f32(1), s)).astype(f32)
+    return ((s * s).astype(f32) * (f32(3) - f32(2) * s)).astype(f32)
+
+
+def _pan_substitute(f, g):
+    m = np.max(np.abs(np.stack(f)), axis=0)
+    e = np.max(np.abs(np.stack([f[c] - g[c] for c in range(4)])), axis=0)
+    use = (m < PAN_FLOW_LIMIT) & (e < PAN_AGREEMENT)
+    return [np.where(use, np.float32(g[c]), f[c]).astype(np.float32) for c in range(4)]
 
 
 POSE_ITERATIONS, POSE_EPSILON, POSE_TIME_LIMIT = 2, np.float32(0.01), np.float32(1e-3)

@@ -11,7 +11,7 @@ namespace {
 std::string g_error;
 
 kirari::kernels::ref::Motion motion_of(const float* flow, const float* mask, int ph, int pw, int wx, int wy, int ww,
-                                        int wh, int filter = 0) {
+                                        int wh, int filter = 0, int pan_lock = 0) {
   kirari::kernels::ref::Motion m;
   for (int c = 0; c < 4; ++c) {
     m.flow[c] = kirari::kernels::PlaneF(pw, ph);
@@ -21,6 +21,7 @@ kirari::kernels::ref::Motion motion_of(const float* flow, const float* mask, int
   std::memcpy(m.mask.data.data(), mask, sizeof(float) * ph * pw);
   m.area = kirari::kernels::Window{.x = wx, .y = wy, .width = ww, .height = wh};
   m.warp = filter == 1 ? kirari::kernels::RifeWarp::CatmullRom : kirari::kernels::RifeWarp::Bilinear;
+  m.pan_lock = pan_lock != 0;
   return m;
 }
 }  // namespace
@@ -32,14 +33,15 @@ const char* kref_warp_last_error() { return g_error.c_str(); }
 // a, b, out: 3 FP32 planes of h x w; flow: 4 planes and mask: 1 plane of ph x pw; window (wx, wy,
 // ww, wh) of the frame in the planes.
 int kref_warp_blend_at(const float* a, const float* b, int h, int w, const float* flow, const float* mask, int ph,
-                       int pw, int wx, int wy, int ww, int wh, float t, int filter, float* out) {
+                       int pw, int wx, int wy, int ww, int wh, float t, int filter, int pan_lock, float* out) {
   using kirari::kernels::RgbImage;
   RgbImage ia(w, h), ib(w, h);
   for (int c = 0; c < 3; ++c) {
     std::memcpy(ia.planes[c].data.data(), a + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
     std::memcpy(ib.planes[c].data.data(), b + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
   }
-  auto r = kirari::kernels::ref::warp_blend_at(ia, ib, motion_of(flow, mask, ph, pw, wx, wy, ww, wh, filter), t);
+  auto r = kirari::kernels::ref::warp_blend_at(ia, ib, motion_of(flow, mask, ph, pw, wx, wy, ww, wh, filter, pan_lock),
+                                                t);
   if (!r) {
     g_error = r.error().detail;
     return 1;
@@ -71,6 +73,21 @@ int kref_warp_blend_poses(const float* a, const float* b, int h, int w, const fl
   }
   for (int c = 0; c < 3; ++c)
     std::memcpy(out + static_cast<size_t>(c) * h * w, r->planes[c].data.data(), sizeof(float) * h * w);
+  return 0;
+}
+
+// The reference's pan estimate of two frames (warp_pan.cpp): dx, dy, sure.
+int kref_pan_estimate(const float* a, const float* b, int h, int w, float* out3) {
+  using kirari::kernels::RgbImage;
+  RgbImage ia(w, h), ib(w, h);
+  for (int c = 0; c < 3; ++c) {
+    std::memcpy(ia.planes[c].data.data(), a + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
+    std::memcpy(ib.planes[c].data.data(), b + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
+  }
+  const auto e = kirari::kernels::ref::pan_estimate(ia, ib);
+  out3[0] = e.dx;
+  out3[1] = e.dy;
+  out3[2] = e.sure ? 1.0f : 0.0f;
   return 0;
 }
 

@@ -72,6 +72,30 @@ def poses():
     print("warp_poses_40x60", outs.shape)
 
 
+def pan():
+    """A pair that moves as a whole by (2, 1) px, RIFE-like flow near it with a smooth error, the pan
+    lock on."""
+    sys.path.insert(0, os.path.join(ROOT, "ultimate-anime-videoplayer_b200"))
+    from synth import anime_frames
+    h, w = 64, 96
+    a = anime_frames(1, h, w, seed=3)[0].astype(np.float16).astype(np.float32)
+    b = np.roll(a, (1, 2), axis=(1, 2))
+    yy, xx = np.meshgrid(np.linspace(0, 3, h, dtype=np.float32), np.linspace(0, 3, w, dtype=np.float32),
+                         indexing="ij")
+    flow = np.stack([-1.0 + 0.3 * np.sin(xx), np.full_like(xx, -0.5), np.full_like(xx, 1.0) + 0.1 * np.sin(yy),
+                     0.5 + 0.2 * np.cos(yy)]).astype(np.float32)
+    flow[:, 40:, 60:] *= 4.0  # a region that moves on its own: its flow stays RIFE's
+    mask = (0.5 + 0.3 * np.sin(xx + yy)).astype(np.float32)
+    win = (0, 0, w, h)
+    times = (0.5, 0.3)
+    outs = np.stack([ref_lib.warp_blend_at(a, b, flow, mask, win, t, 0, 1) for t in times])
+    np.savez_compressed(os.path.join(OUT, "warp_pan_64x96.npz"), a=a, b=b, flow=flow, mask=mask,
+                        window=np.array(win, np.int32), times=np.array(times, np.float32), out=outs,
+                        pan=np.array(ref_lib.pan_estimate(a, b), np.float32))
+    print("warp_pan_64x96", outs.shape, ref_lib.pan_estimate(a, b))
+
+
 if __name__ == "__main__":
     main()
     poses()
+    pan()

@@ -45,3 +45,13 @@ def test_keep_poses_restatement_matches_reference():
                 out = nets.warp_blend_poses(g["a"], g["b"], g["flow"], g["mask"], pf, pm, win, float(t), warp)
                 np.testing.assert_allclose(out, g["out"][k], rtol=0, atol=1e-5)
                 k += 1
+
+
+def test_pan_lock_restatement_matches_reference():
+    g = golden("warp_pan_64x96.npz")
+    win = tuple(int(v) for v in g["window"])
+    dx, dy, sure = nets.pan_estimate(g["a"], g["b"])
+    np.testing.assert_array_equal(np.array([dx, dy, float(sure)], np.float32), g["pan"])
+    for i, t in enumerate(g["times"]):
+        out = nets.warp_blend_at(g["a"], g["b"], g["flow"], g["mask"], win, float(t), 0, 1)
+        np.testing.assert_allclose(out, g["out"][i], rtol=0, atol=2e-6)

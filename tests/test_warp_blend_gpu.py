@@ -106,3 +106,18 @@ def test_keep_poses_matches_reference_golden():
                 err = np.abs(out.float().cpu().numpy()[0] - g["out"][k]).max()
                 assert err <= 2e-3, f"t={t} prev={prev} warp={warp}"
                 k += 1
+
+
+def test_pan_lock_matches_reference_golden():
+    import torch
+    g = golden("warp_pan_64x96.npz")
+    win = tuple(int(v) for v in g["window"])
+    for i, t in enumerate(g["times"]):
+        out = kb.warp_blend_at(_dev(g["a"][None], torch.float16), _dev(g["b"][None], torch.float16),
+                               _dev(g["flow"][None], torch.float32), _dev(g["mask"][None], torch.float32), win,
+                               float(t), pan_lock=1)
+        torch.cuda.synchronize()
+        assert np.abs(out.float().cpu().numpy()[0] - g["out"][i]).max() <= 2e-3, f"t={t}"
+    # the lock changes the result here (a sure pan and sub-2-px flow)
+    plain = _run(g["a"][None], g["b"][None], g["flow"][None], g["mask"][None], win, 0.3)[0]
+    assert np.abs(plain - g["out"][1]).max() > 1e-2

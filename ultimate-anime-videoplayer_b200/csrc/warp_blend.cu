@@ -16,6 +16,10 @@
 // pixel at instant tp, its displacement D now and D' in the previous pair (q = pa - f1'(q), two steps;
 // D' = 0 for a held pair), r = (|D'| + e) / (|D'| + |D| + 2e), tp = pose_time(t, r) clamped; then the
 // straight-line blend at tp. |.| is CUDA's hypotf.
+// The pan lock (spec/warp_pan.h, ref/warp_pan.cpp): per pair, a Lucas-Kanade translation of the luma
+// on a 32 x 32 grid (3 iterations); where it is sure, RIFE's flow is replaced by it where small and
+// close; and the blend weight fades to the linear blend under half a pixel of motion
+// (logit m = w law + (1 - w) ln((1 - t) / t), w = smoothstep(0.5, 2, |d|)).
 // flow_max: per pair, a 256-bin histogram of max |flow component| over the window (bins of 0.25 px,
 // the last taking the rest), then the 99.9th percentile's bin edge.
 #include <cuda_fp16.h>
@@ -34,6 +38,23 @@ constexpr float kLawA = 1.0f, kLawB = 2.591f, kLawC = 0.0f, kMaskEps = 1e-4f;
 // keep the poses (spec/poses.h): iterations, distance epsilon (grid pixels), instant limit
 constexpr int kPoseIterations = 2;
 constexpr float kPoseEps = 0.01f, kPoseTimeLimit = 1e-3f;
+// the pair's global translation (spec/warp_pan.h): grid, iterations, luma, limits, slow fade
+constexpr int kPanGrid = 32, kPanIterations = 3;
+constexpr float kPanLumaR = 0.2126f, kPanLumaG = 0.7152f, kPanLumaB = 0.0722f;
+constexpr float kPanDetRatio = 1e-6f, kPanMaxShift = 8.0f, kPanFlowLimit = 2.0f, kPanAgreement = 1.0f;
+constexpr float kSlowFadeLo = 0.5f, kSlowFadeHi = 2.0f;
+
+// A pair's pan: the flow g that replaces RIFE's where it is small and close to it (on), and the
+// slow fade towards the linear blend (always, with the pan lock).
+struct Pan {
+  float g[4];
+  int on;
+};
+
+// The pairs' pans of a pan-locked call, estimated and read on the call's stream (pan-locked calls
+// that overlap on the GPU race on them).
+constexpr int kMaxPanPairs = 64;
+__device__ Pan g_pan_slots[kMaxPanPairs];
 constexpr int kFlowBins = 256;
 constexpr float kFlowBinStep = 0.25f;
 constexpr double kFlowPercentile = 0.999;
@@ -70,6 +91,117 @@ __device__ __forceinline__ float bilinear(const T* p, int pw, int wx, int wy, in
   const float top = __fadd_rn(__fmul_rn(load_f(p, r0 + x0), gx), __fmul_rn(load_f(p, r0 + x1), fx));
   const float bot = __fadd_rn(__fmul_rn(load_f(p, r1 + x0), gx), __fmul_rn(load_f(p, r1 + x1), fx));
   return __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy));
+}
+
+__device__ __forceinline__ float luma_at(const __half* a, size_t plane, int w, int x, int y) {
+  const size_t i = static_cast<size_t>(y) * w + x;
+  return __fadd_rn(__fadd_rn(__fmul_rn(kPanLumaR, __half2float(a[i])), __fmul_rn(kPanLumaG, __half2float(a[plane + i]))),
+                   __fmul_rn(kPanLumaB, __half2float(a[2 * plane + i])));
+}
+
+__device__ __forceinline__ float luma_bilinear(const __half* a, size_t plane, int w, int h, float x, float y) {
+  x = fminf(fmaxf(x, 0.0f), static_cast<float>(w - 1));
+  y = fminf(fmaxf(y, 0.0f), static_cast<float>(h - 1));
+  const int x0 = static_cast<int>(x), y0 = static_cast<int>(y);
+  const int x1 = min(x0 + 1, w - 1), y1 = min(y0 + 1, h - 1);
+  const float fx = __fsub_rn(x, static_cast<float>(x0)), fy = __fsub_rn(y, static_cast<float>(y0));
+  const float gx = __fsub_rn(1.0f, fx), gy = __fsub_rn(1.0f, fy);
+  const float top = __fadd_rn(__fmul_rn(luma_at(a, plane, w, x0, y0), gx), __fmul_rn(luma_at(a, plane, w, x1, y0), fx));
+  const float bot = __fadd_rn(__fmul_rn(luma_at(a, plane, w, x0, y1), gx), __fmul_rn(luma_at(a, plane, w, x1, y1), fx));
+  return __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy));
+}
+
+__device__ __forceinline__ int pan_point(int i, int n) {
+  const int m = n / 12 > 4 ? n / 12 : 4;
+  return m + (i * (n - 2 * m)) / kPanGrid;
+}
+
+// smoothstep(0.5, 2, d): the weight of the fitted blend law against the linear fade
+__device__ __forceinline__ float slow_fade_weight(float d) {
+  float s = __fdiv_rn(__fsub_rn(d, kSlowFadeLo), kSlowFadeHi - kSlowFadeLo);
+  s = s < 0.0f ? 0.0f : (s > 1.0f ? 1.0f : s);
+  return __fmul_rn(__fmul_rn(s, s), __fsub_rn(3.0f, __fmul_rn(2.0f, s)));
+}
+
+// One block of kPanGrid^2 threads per pair: Lucas-Kanade on the luma of a and b at a 32 x 32 grid
+// (ref/warp_pan.cpp pan_estimate), sums in double (the reference's are sequential, these a tree:
+// a last-bit difference at most), then the pair's g for the flow read at the middle (s = 1/2).
+__global__ void __launch_bounds__(kPanGrid * kPanGrid) pan_estimate_kernel(const __half* __restrict__ a,
+                                                                           const __half* __restrict__ b, int H, int W,
+                                                                           float sx, float sy, Pan* __restrict__ pans) {
+  const int n = blockIdx.x;
+  const int q = threadIdx.x;
+  __shared__ double red[5][kPanGrid * kPanGrid / 32];
+  __shared__ float s_dx, s_dy;
+  __shared__ int s_valid;
+  if (W < 16 || H < 16) {
+    if (q == 0) pans[n] = Pan{{0.0f, 0.0f, 0.0f, 0.0f}, 0};
+    return;
+  }
+  const size_t plane = static_cast<size_t>(H) * W;
+  const __half* fa = a + static_cast<size_t>(n) * 3 * plane;
+  const __half* fb = b + static_cast<size_t>(n) * 3 * plane;
+  const int px = pan_point(q % kPanGrid, W), py = pan_point(q / kPanGrid, H);
+  const float la = luma_at(fa, plane, W, px, py);
+  const float gx = __fmul_rn(0.5f, __fsub_rn(luma_at(fa, plane, W, px + 1, py), luma_at(fa, plane, W, px - 1, py)));
+  const float gy = __fmul_rn(0.5f, __fsub_rn(luma_at(fa, plane, W, px, py + 1), luma_at(fa, plane, W, px, py - 1)));
+  if (q == 0) {
+    s_dx = 0.0f;
+    s_dy = 0.0f;
+    s_valid = 0;
+  }
+  __syncthreads();
+  for (int it = 0; it < kPanIterations; ++it) {
+    const float r = __fsub_rn(luma_bilinear(fb, plane, W, H, __fadd_rn(static_cast<float>(px), s_dx),
+                                            __fadd_rn(static_cast<float>(py), s_dy)),
+                              la);
+    double v[5] = {__fmul_rn(gx, gx), __fmul_rn(gx, gy), __fmul_rn(gy, gy), __fmul_rn(gx, r), __fmul_rn(gy, r)};
+#pragma unroll
+    for (int k = 0; k < 5; ++k)
+      for (int o = 16; o > 0; o >>= 1) v[k] += __shfl_xor_sync(0xffffffffu, v[k], o);
+    if ((q & 31) == 0)
+#pragma unroll
+      for (int k = 0; k < 5; ++k) red[k][q >> 5] = v[k];
+    __syncthreads();
+    if (q == 0) {
+      double sm[5] = {0, 0, 0, 0, 0};
+      for (int w = 0; w < kPanGrid * kPanGrid / 32; ++w)
+#pragma unroll
+        for (int k = 0; k < 5; ++k) sm[k] += red[k][w];
+      const double sxx = sm[0], sxy = sm[1], syy = sm[2], sxr = sm[3], syr = sm[4];
+      const double det = sxx * syy - sxy * sxy;
+      const bool valid = det > static_cast<double>(kPanDetRatio) * (sxx + syy) * (sxx + syy) && det > 0.0;
+      s_valid = valid ? 1 : 0;
+      if (valid) {
+        s_dx = __fsub_rn(s_dx, static_cast<float>((syy * sxr - sxy * syr) / det));
+        s_dy = __fsub_rn(s_dy, static_cast<float>((sxx * syr - sxy * sxr) / det));
+      }
+    }
+    __syncthreads();
+    if (!s_valid) break;
+  }
+  if (q == 0) {
+    const float dx = s_dx, dy = s_dy;
+    const bool sure = s_valid != 0 && hypotf(dx, dy) < kPanMaxShift;
+    const float sm = 0.5f;  // the flow read is RIFE's middle
+    pans[n] = Pan{{__fdiv_rn(__fmul_rn(-sm, dx), sx), __fdiv_rn(__fmul_rn(-sm, dy), sy),
+                   __fdiv_rn(__fmul_rn(__fsub_rn(1.0f, sm), dx), sx), __fdiv_rn(__fmul_rn(__fsub_rn(1.0f, sm), dy), sy)},
+                  sure ? 1 : 0};
+  }
+}
+
+// The flow read f replaced by the pan's g where it is small (max |f| < 2) and close (max |f - g| < 1).
+__device__ __forceinline__ void pan_substitute(float (&f)[4], const Pan& p) {
+  if (!p.on) return;
+  float m = 0.0f, e = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    m = fmaxf(m, fabsf(f[c]));
+    e = fmaxf(e, fabsf(__fsub_rn(f[c], p.g[c])));
+  }
+  if (m < kPanFlowLimit && e < kPanAgreement)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) f[c] = p.g[c];
 }
 
 // Catmull-Rom read of plane p (w x h, row pitch w) at (x, y) (spec/warp.h RifeWarp::CatmullRom): the
@@ -114,9 +246,11 @@ __device__ __forceinline__ float catmull_rom(const __half* p, int w, int h, floa
 // poses: each pixel's instant adjusted by the distance ratio to the previous pair's motion `pm`
 // (pm.flow null: a held previous pair), then mode 1 at that instant.
 // kCatmull: frames a and b read by Catmull-Rom instead of bilinearly (the motion stays bilinear).
+// pans: the pairs' pans with the pan lock (modes 0 and 1), else null.
 template <int kMode, bool kCatmull>
 __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half* __restrict__ b, MotionView m,
-                                     MotionView pm, int batch, int H, int W, float t, __half* __restrict__ out) {
+                                     MotionView pm, int batch, int H, int W, float t, const Pan* __restrict__ pans,
+                                     __half* __restrict__ out) {
   constexpr bool kMiddle = kMode == 0;
   const int x = blockIdx.x * blockDim.x + threadIdx.x;
   if (x >= W) return;
@@ -136,6 +270,12 @@ __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half*
     float f[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) f[c] = bilinear(fl + c * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u, v);
+    Pan pan{};
+    const bool fade = kMode != 2 && pans != nullptr;
+    if (fade) {
+      pan = pans[n];
+      pan_substitute(f, pan);
+    }
     float tq = t;  // the pixel's instant
     if constexpr (kMode == 2) {
       const float* pf = pm.flow != nullptr ? pm.flow + static_cast<size_t>(n) * 4 * plane : nullptr;
@@ -177,6 +317,13 @@ __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half*
       dbx = f[2];
       dby = f[3];
       wgt = bilinear(mk, m.pw, m.wx, m.wy, m.ww, m.wh, u, v);
+      if (fade) {  // under half a pixel of motion the blend slides to the linear fade
+        const float mm = fminf(fmaxf(wgt, kMaskEps), __fsub_rn(1.0f, kMaskEps));
+        const float w = slow_fade_weight(hypotf(__fsub_rn(f[2], f[0]), __fsub_rn(f[3], f[1])));
+        const float z = __fadd_rn(__fmul_rn(w, logf(__fdiv_rn(mm, __fsub_rn(1.0f, mm)))),
+                                  __fmul_rn(__fsub_rn(1.0f, w), logf(__fdiv_rn(__fsub_rn(1.0f, t), t))));
+        wgt = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+      }
     } else {
       const float s = __fsub_rn(1.0f, tq);
       const float u2 = __fsub_rn(u, __fadd_rn(__fmul_rn(s, f[0]), __fmul_rn(tq, f[2])));
@@ -184,13 +331,18 @@ __global__ void warp_blend_at_kernel(const __half* __restrict__ a, const __half*
       float g[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) g[c] = bilinear(fl + c * plane, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2);
+      if (fade) pan_substitute(g, pan);
       const float tx = __fsub_rn(g[2], g[0]);
       const float ty = __fsub_rn(g[3], g[1]);
       const float mm =
           fminf(fmaxf(bilinear(mk, m.pw, m.wx, m.wy, m.ww, m.wh, u2, v2), kMaskEps), __fsub_rn(1.0f, kMaskEps));
-      const float z = __fadd_rn(__fadd_rn(__fmul_rn(kLawA, logf(__fdiv_rn(mm, __fsub_rn(1.0f, mm)))),
-                                          __fmul_rn(kLawB, logf(__fdiv_rn(s, tq)))),
-                                kLawC);
+      float z = __fadd_rn(__fadd_rn(__fmul_rn(kLawA, logf(__fdiv_rn(mm, __fsub_rn(1.0f, mm)))),
+                                    __fmul_rn(kLawB, logf(__fdiv_rn(s, tq)))),
+                          kLawC);
+      if (fade) {
+        const float w = slow_fade_weight(hypotf(tx, ty));
+        z = __fadd_rn(__fmul_rn(w, z), __fmul_rn(__fsub_rn(1.0f, w), logf(__fdiv_rn(s, tq))));
+      }
       wgt = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
       dax = __fmul_rn(-tq, tx);
       day = __fmul_rn(-tq, ty);
@@ -244,6 +396,7 @@ Status motion_view(const kb2_motion* motion, MotionView& m) {
     return refuse(KB2_INVALID_ARGUMENT, "motion: null pointer");
   const kb2_motion& q = *motion;
   if (q.warp != 0 && q.warp != 1) return refuse(KB2_INVALID_ARGUMENT, "motion: warp filter 0 or 1");
+  if (q.pan_lock != 0 && q.pan_lock != 1) return refuse(KB2_INVALID_ARGUMENT, "motion: pan_lock 0 or 1");
   if (q.plane_h < 1 || q.plane_w < 1 || q.plane_h > 16384 || q.plane_w > 16384)
     return refuse(KB2_SHAPE_INVALID, "motion: plane size out of range");
   // written without x + width, which could overflow
@@ -289,14 +442,25 @@ Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor*
   const dim3 g = rows_grid(static_cast<int>(W), static_cast<int>(n * H));
   const int nn = static_cast<int>(n), hh = static_cast<int>(H), w = static_cast<int>(W);
   const int mode = keep_poses ? 2 : (t == 0.5f ? 0 : 1);
+  // the pan lock (not with keep-the-poses): one estimate per pair into the library's pan slots
+  const Pan* pans = nullptr;
+  if (motion->pan_lock != 0 && !keep_poses) {
+    if (n > kMaxPanPairs) return refuse(KB2_SHAPE_INVALID, "warp_blend_at: pan lock on more than 64 pairs");
+    Pan* slots = nullptr;
+    KB2_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&slots), g_pan_slots));
+    const float sx = static_cast<float>(W) / static_cast<float>(m.ww), sy = static_cast<float>(H) / static_cast<float>(m.wh);
+    pan_estimate_kernel<<<nn, kPanGrid * kPanGrid, 0, stream>>>(pa, pb, hh, w, sx, sy, slots);
+    KB2_CUDA(cudaGetLastError());
+    pans = slots;
+  }
   if (motion->warp == 1) {
-    if (mode == 2) warp_blend_at_kernel<2, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
-    else if (mode == 0) warp_blend_at_kernel<0, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
-    else warp_blend_at_kernel<1, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+    if (mode == 2) warp_blend_at_kernel<2, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, pans, po);
+    else if (mode == 0) warp_blend_at_kernel<0, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, pans, po);
+    else warp_blend_at_kernel<1, true><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, pans, po);
   } else {
-    if (mode == 2) warp_blend_at_kernel<2, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
-    else if (mode == 0) warp_blend_at_kernel<0, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
-    else warp_blend_at_kernel<1, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, po);
+    if (mode == 2) warp_blend_at_kernel<2, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, pans, po);
+    else if (mode == 0) warp_blend_at_kernel<0, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, pans, po);
+    else warp_blend_at_kernel<1, false><<<g, 128, 0, stream>>>(pa, pb, m, pm, nn, hh, w, t, pans, po);
   }
   return cuda_status(cudaGetLastError(), "warp_blend_at launch");
 }
