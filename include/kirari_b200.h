@@ -180,7 +180,11 @@ typedef struct kb2_motion {
   int32_t warp;     /* the filter that reads frames a and b: 0 bilinear, 1 Catmull-Rom (RifeWarp) */
   int32_t pan_lock; /* 1: estimate each pair's global translation on a and b and use it where RIFE's flow
                        is small and close to it, fading to a linear blend under half a pixel of motion
-                       (Motion::pan_lock, spec/warp_pan.h); at most 64 pairs a call; not with keep-poses */
+                       (Motion::pan_lock, spec/warp_pan.h); at most 64 pairs a call, whose estimates
+                       share a static device array: pan-locked calls that overlap on the GPU race; not
+                       with keep-poses */
+  int32_t at_instant; /* 1: the motion was estimated at the output instant (RIFE run at t directly):
+                         read as it is at any t, without the straight-line step or the blend law */
 } kb2_motion;
 
 /* Frames at instant t in (0, 1) from frames a, b (F16 [n,3,H,W], device) and their mid-pair

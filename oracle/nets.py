@@ -659,7 +659,7 @@ def _frame_read(p, x, y, warp):
     return _catmull_rom(p, x, y) if warp == 1 else _bilinear_window(p, (0, 0, w, h), x, y)
 
 
-def warp_blend_at(a, b, flow, mask, window, t, warp=0, pan_lock=0):
+def warp_blend_at(a, b, flow, mask, window, t, warp=0, pan_lock=0, at_instant=0):
     """One frame [3,h,w] at instant t in (0, 1) from frames a, b [3,h,w] and the mid-pair motion:
     flow [4,ph,pw] (f0x, f0y, f1x, f1y), mask [ph,pw], the frame's window (x, y, w, h) in those planes
     (warp.cpp warp_blend_at:261 with the bilinear filter, no pan lock, the motion estimated at the
@@ -684,12 +684,12 @@ def warp_blend_at(a, b, flow, mask, window, t, warp=0, pan_lock=0):
     g_pan = None
     if pan_lock:
         dx, dy, sure = pan_estimate(a, b)
-        sm = f32(0.5)
+        sm = t if at_instant else f32(0.5)
         g_pan = [f32(f32(-sm * f32(dx)) / sx), f32(f32(-sm * f32(dy)) / sy), f32(f32((one - sm) * f32(dx)) / sx),
                  f32(f32((one - sm) * f32(dy)) / sy)]
         if sure:
             f = _pan_substitute(f, g_pan)
-    if t == f32(0.5):
+    if t == f32(0.5) or at_instant:
         ax, ay, bx, by = f
         wgt = _bilinear_window(mask, window, u, v)
         if pan_lock:

@@ -118,7 +118,7 @@ def _warp_bind(L):
         return L
     i = ctypes.c_int
     L.kref_warp_last_error.restype = ctypes.c_char_p
-    L.kref_warp_blend_at.argtypes = [_fp, _fp, i, i, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, i, i, _fp]
+    L.kref_warp_blend_at.argtypes = [_fp, _fp, i, i, _fp, _fp, i, i, i, i, i, i, ctypes.c_float, i, i, i, _fp]
     L.kref_pan_estimate.argtypes = [_fp, _fp, i, i, _fp]
     L.kref_pan_estimate.restype = i
     L.kref_warp_blend_at.restype = i
@@ -131,7 +131,7 @@ def _warp_bind(L):
     return L
 
 
-def warp_blend_at(a, b, flow, mask, window, t, warp=0, pan_lock=0):
+def warp_blend_at(a, b, flow, mask, window, t, warp=0, pan_lock=0, at_instant=0):
     """The reference's CPU warp_blend_at (src/kernels/ref/warp.cpp:261): a, b [3,h,w], flow
     [4,ph,pw], mask [ph,pw], window (x, y, w, h); returns [3,h,w]."""
     L = _warp_bind(lib())
@@ -143,7 +143,7 @@ def warp_blend_at(a, b, flow, mask, window, t, warp=0, pan_lock=0):
     ph, pw = mask.shape
     out = np.zeros_like(a)
     rc = L.kref_warp_blend_at(_ptr(a), _ptr(b), h, w, _ptr(flow), _ptr(mask), ph, pw, *window, float(t), int(warp),
-                              int(pan_lock), _ptr(out))
+                              int(pan_lock), int(at_instant), _ptr(out))
     if rc != 0:
         raise RuntimeError(f"kref_warp_blend_at: {L.kref_warp_last_error().decode(errors='replace')}")
     return out

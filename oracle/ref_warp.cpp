@@ -11,7 +11,7 @@ namespace {
 std::string g_error;
 
 kirari::kernels::ref::Motion motion_of(const float* flow, const float* mask, int ph, int pw, int wx, int wy, int ww,
-                                        int wh, int filter = 0, int pan_lock = 0) {
+                                        int wh, int filter = 0, int pan_lock = 0, int at_instant = 0) {
   kirari::kernels::ref::Motion m;
   for (int c = 0; c < 4; ++c) {
     m.flow[c] = kirari::kernels::PlaneF(pw, ph);
@@ -22,6 +22,7 @@ kirari::kernels::ref::Motion motion_of(const float* flow, const float* mask, int
   m.area = kirari::kernels::Window{.x = wx, .y = wy, .width = ww, .height = wh};
   m.warp = filter == 1 ? kirari::kernels::RifeWarp::CatmullRom : kirari::kernels::RifeWarp::Bilinear;
   m.pan_lock = pan_lock != 0;
+  m.at_instant = at_instant != 0;
   return m;
 }
 }  // namespace
@@ -33,15 +34,16 @@ const char* kref_warp_last_error() { return g_error.c_str(); }
 // a, b, out: 3 FP32 planes of h x w; flow: 4 planes and mask: 1 plane of ph x pw; window (wx, wy,
 // ww, wh) of the frame in the planes.
 int kref_warp_blend_at(const float* a, const float* b, int h, int w, const float* flow, const float* mask, int ph,
-                       int pw, int wx, int wy, int ww, int wh, float t, int filter, int pan_lock, float* out) {
+                       int pw, int wx, int wy, int ww, int wh, float t, int filter, int pan_lock, int at_instant,
+                       float* out) {
   using kirari::kernels::RgbImage;
   RgbImage ia(w, h), ib(w, h);
   for (int c = 0; c < 3; ++c) {
     std::memcpy(ia.planes[c].data.data(), a + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
     std::memcpy(ib.planes[c].data.data(), b + static_cast<size_t>(c) * h * w, sizeof(float) * h * w);
   }
-  auto r = kirari::kernels::ref::warp_blend_at(ia, ib, motion_of(flow, mask, ph, pw, wx, wy, ww, wh, filter, pan_lock),
-                                                t);
+  auto r = kirari::kernels::ref::warp_blend_at(
+      ia, ib, motion_of(flow, mask, ph, pw, wx, wy, ww, wh, filter, pan_lock, at_instant), t);
   if (!r) {
     g_error = r.error().detail;
     return 1;

@@ -89,8 +89,11 @@ def pan():
     win = (0, 0, w, h)
     times = (0.5, 0.3)
     outs = np.stack([ref_lib.warp_blend_at(a, b, flow, mask, win, t, 0, 1) for t in times])
+    # the same motion taken as estimated at the output instant (read as it is), without and with the lock
+    instant = np.stack([ref_lib.warp_blend_at(a, b, flow, mask, win, 0.3, 0, lock, 1) for lock in (0, 1)])
     np.savez_compressed(os.path.join(OUT, "warp_pan_64x96.npz"), a=a, b=b, flow=flow, mask=mask,
                         window=np.array(win, np.int32), times=np.array(times, np.float32), out=outs,
+                        out_instant=instant,
                         pan=np.array(ref_lib.pan_estimate(a, b), np.float32))
     print("warp_pan_64x96", outs.shape, ref_lib.pan_estimate(a, b))
 

@@ -55,3 +55,6 @@ def test_pan_lock_restatement_matches_reference():
     for i, t in enumerate(g["times"]):
         out = nets.warp_blend_at(g["a"], g["b"], g["flow"], g["mask"], win, float(t), 0, 1)
         np.testing.assert_allclose(out, g["out"][i], rtol=0, atol=2e-6)
+    for lock in (0, 1):  # a motion estimated at the output instant
+        out = nets.warp_blend_at(g["a"], g["b"], g["flow"], g["mask"], win, 0.3, 0, lock, 1)
+        np.testing.assert_allclose(out, g["out_instant"][lock], rtol=0, atol=2e-6)

@@ -118,6 +118,12 @@ def test_pan_lock_matches_reference_golden():
                                float(t), pan_lock=1)
         torch.cuda.synchronize()
         assert np.abs(out.float().cpu().numpy()[0] - g["out"][i]).max() <= 2e-3, f"t={t}"
+    for lock in (0, 1):  # a motion estimated at the output instant, read as it is
+        out = kb.warp_blend_at(_dev(g["a"][None], torch.float16), _dev(g["b"][None], torch.float16),
+                               _dev(g["flow"][None], torch.float32), _dev(g["mask"][None], torch.float32), win, 0.3,
+                               pan_lock=lock, at_instant=1)
+        torch.cuda.synchronize()
+        assert np.abs(out.float().cpu().numpy()[0] - g["out_instant"][lock]).max() <= 2e-3, f"instant lock={lock}"
     # the lock changes the result here (a sure pan and sub-2-px flow)
     plain = _run(g["a"][None], g["b"][None], g["flow"][None], g["mask"][None], win, 0.3)[0]
     assert np.abs(plain - g["out"][1]).max() > 1e-2

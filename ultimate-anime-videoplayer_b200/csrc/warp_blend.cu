@@ -128,7 +128,8 @@ __device__ __forceinline__ float slow_fade_weight(float d) {
 // a last-bit difference at most), then the pair's g for the flow read at the middle (s = 1/2).
 __global__ void __launch_bounds__(kPanGrid * kPanGrid) pan_estimate_kernel(const __half* __restrict__ a,
                                                                            const __half* __restrict__ b, int H, int W,
-                                                                           float sx, float sy, Pan* __restrict__ pans) {
+                                                                           float sx, float sy, float sm,
+                                                                           Pan* __restrict__ pans) {
   const int n = blockIdx.x;
   const int q = threadIdx.x;
   __shared__ double red[5][kPanGrid * kPanGrid / 32];
@@ -183,7 +184,6 @@ __global__ void __launch_bounds__(kPanGrid * kPanGrid) pan_estimate_kernel(const
   if (q == 0) {
     const float dx = s_dx, dy = s_dy;
     const bool sure = s_valid != 0 && hypotf(dx, dy) < kPanMaxShift;
-    const float sm = 0.5f;  // the flow read is RIFE's middle
     pans[n] = Pan{{__fdiv_rn(__fmul_rn(-sm, dx), sx), __fdiv_rn(__fmul_rn(-sm, dy), sy),
                    __fdiv_rn(__fmul_rn(__fsub_rn(1.0f, sm), dx), sx), __fdiv_rn(__fmul_rn(__fsub_rn(1.0f, sm), dy), sy)},
                   sure ? 1 : 0};
@@ -397,6 +397,7 @@ Status motion_view(const kb2_motion* motion, MotionView& m) {
   const kb2_motion& q = *motion;
   if (q.warp != 0 && q.warp != 1) return refuse(KB2_INVALID_ARGUMENT, "motion: warp filter 0 or 1");
   if (q.pan_lock != 0 && q.pan_lock != 1) return refuse(KB2_INVALID_ARGUMENT, "motion: pan_lock 0 or 1");
+  if (q.at_instant != 0 && q.at_instant != 1) return refuse(KB2_INVALID_ARGUMENT, "motion: at_instant 0 or 1");
   if (q.plane_h < 1 || q.plane_w < 1 || q.plane_h > 16384 || q.plane_w > 16384)
     return refuse(KB2_SHAPE_INVALID, "motion: plane size out of range");
   // written without x + width, which could overflow
@@ -441,7 +442,8 @@ Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor*
   }
   const dim3 g = rows_grid(static_cast<int>(W), static_cast<int>(n * H));
   const int nn = static_cast<int>(n), hh = static_cast<int>(H), w = static_cast<int>(W);
-  const int mode = keep_poses ? 2 : (t == 0.5f ? 0 : 1);
+  // a motion estimated at the output instant is read as it is at any t (ref/warp.cpp:265)
+  const int mode = keep_poses ? 2 : (t == 0.5f || motion->at_instant != 0 ? 0 : 1);
   // the pan lock (not with keep-the-poses): one estimate per pair into the library's pan slots
   const Pan* pans = nullptr;
   if (motion->pan_lock != 0 && !keep_poses) {
@@ -449,7 +451,9 @@ Status warp_blend_at(cudaStream_t stream, const kb2_tensor* a, const kb2_tensor*
     Pan* slots = nullptr;
     KB2_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&slots), g_pan_slots));
     const float sx = static_cast<float>(W) / static_cast<float>(m.ww), sy = static_cast<float>(H) / static_cast<float>(m.wh);
-    pan_estimate_kernel<<<nn, kPanGrid * kPanGrid, 0, stream>>>(pa, pb, hh, w, sx, sy, slots);
+    // the instant of the flow read: RIFE's middle, or t for a motion estimated at the output instant
+    const float s_read = motion->at_instant != 0 ? t : 0.5f;
+    pan_estimate_kernel<<<nn, kPanGrid * kPanGrid, 0, stream>>>(pa, pb, hh, w, sx, sy, s_read, slots);
     KB2_CUDA(cudaGetLastError());
     pans = slots;
   }

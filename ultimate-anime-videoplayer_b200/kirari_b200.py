@@ -66,7 +66,7 @@ class Motion(ctypes.Structure):
     _fields_ = [("flow", ctypes.c_void_p), ("mask", ctypes.c_void_p), ("plane_h", ctypes.c_int32),
                 ("plane_w", ctypes.c_int32), ("x", ctypes.c_int32), ("y", ctypes.c_int32),
                 ("width", ctypes.c_int32), ("height", ctypes.c_int32), ("warp", ctypes.c_int32),
-                ("pan_lock", ctypes.c_int32)]
+                ("pan_lock", ctypes.c_int32), ("at_instant", ctypes.c_int32)]
 
 
 class LayerProfile(ctypes.Structure):
@@ -258,18 +258,19 @@ def selftest_bounded_wait(device=0):
     return rc, code.value, waited.value
 
 
-def _motion(flow, mask, window, warp=0, pan_lock=0):
+def _motion(flow, mask, window, warp=0, pan_lock=0, at_instant=0):
     """kb2_motion over torch device tensors flow [n,4,ph,pw] and mask [n,ph,pw] (FP32, contiguous);
     warp: the frames' filter, 0 bilinear, 1 Catmull-Rom; pan_lock: the pair's global translation."""
     ph, pw = int(mask.shape[-2]), int(mask.shape[-1])
-    return Motion(flow.data_ptr(), mask.data_ptr(), ph, pw, *[int(v) for v in window], int(warp), int(pan_lock))
+    return Motion(flow.data_ptr(), mask.data_ptr(), ph, pw, *[int(v) for v in window], int(warp), int(pan_lock),
+                  int(at_instant))
 
 
-def warp_blend_at(a, b, flow, mask, window, t, stream=None, warp=0, pan_lock=0):
+def warp_blend_at(a, b, flow, mask, window, t, stream=None, warp=0, pan_lock=0, at_instant=0):
     """kb2_warp_blend_at on torch device tensors: a, b F16 [n,3,H,W]; returns F16 [n,3,H,W]."""
     import torch
     out = torch.empty_like(a)
-    m = _motion(flow, mask, window, warp, pan_lock)
+    m = _motion(flow, mask, window, warp, pan_lock, at_instant)
     ta, tb, to = to_kb2_tensor(a), to_kb2_tensor(b), to_kb2_tensor(out)
     rc = lib().kb2_warp_blend_at(_stream_handle(stream), ctypes.byref(ta), ctypes.byref(tb), ctypes.byref(m),
                                  float(t), ctypes.byref(to))
