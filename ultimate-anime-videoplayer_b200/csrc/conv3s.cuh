@@ -503,7 +503,6 @@ __global__ void __launch_bounds__(StackShape<kCoutPad>::threads, kStackBlocksPer
     conv3s_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
   static_assert(kCoutPad == 16 || kCoutPad == 48, "stacked kernel: 16 or 48 output channels");
   constexpr int kEpiWarps = StackShape<kCoutPad>::epi_warps;
-  constexpr int kN = 3 * kCoutPad;
   constexpr uint32_t R = kStackSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
