@@ -54,12 +54,15 @@ struct IfConvArgs {
   const uint8_t* residual;  // kIfResPrelu: chunked FP16 like out
   uint8_t* out;             // chunked FP16 [n][h_out][out_chunks][w_out][16 B]
   int out_chunks;
+  int out_split;            // 1: each chunk row stored parity-split, even pixels then odd (the
+                            // layout a stride-2 conv reads); w_out even
   float* out_f32;  // kIfConvT: FP32 [n][2 h_out][2 w_out][8] (5 used: flow x0 y0 x1 y1, mask)
   int* err;
 };
 
 struct IfMaps {
-  CUtensorMap a;  // stride 1: 3-D {2 W u64, chunks, batch*H}; stride 2: 5-D {2, 2, W/2, chunks, batch*H}
+  CUtensorMap a;  // stride 1: 3-D {2 W u64, chunks, batch*H}; stride 2 (parity-split rows): 4-D
+                  // {W u64, 2 parities, chunks, batch*H}
 };
 
 constexpr uint32_t kIfSmemExtra = 1024 + 16 * 8 + 16 + 2 * kIfMaxN * 4;
@@ -169,8 +172,8 @@ __global__ void __launch_bounds__(kIfThreads, 1)
             if constexpr (kStride == 1) {
               tma_load_3d(dst, &maps.a, bar, p0 * 2, grp * a.g, row);
             } else {
-              tma_load_5d(dst, &maps.a, bar, 0, 0, p0, grp * a.g, row);  // even pixels
-              tma_load_5d(dst + a.g * kIfChunkBytes, &maps.a, bar, 0, 1, p0, grp * a.g, row);  // odd pixels
+              tma_load_4d(dst, &maps.a, bar, p0 * 2, 0, grp * a.g, row);  // even pixels
+              tma_load_4d(dst + a.g * kIfChunkBytes, &maps.a, bar, p0 * 2, 1, grp * a.g, row);  // odd pixels
             }
             const uint8_t* src = a.wpack + static_cast<size_t>(dy * a.n_groups + grp) * a.b_bytes;
             for (uint32_t off = 0; off < a.b_bytes; off += 32768u) {
@@ -272,6 +275,7 @@ __global__ void __launch_bounds__(kIfThreads, 1)
       const int m = quad * 32 + lane;
       const int x = strip * kIfStrip + m;
       const bool store = m < kIfStrip && x < a.w_out;
+      const int xs = a.out_split ? (x & 1) * (a.w_out >> 1) + (x >> 1) : x;  // stored column
 #pragma unroll 1
       for (int q = 0; q < IfShape<kN>::groups_per_warp; ++q) {
         const int cg = half * IfShape<kN>::groups_per_warp + q;  // 8-column group = output chunk
@@ -288,7 +292,7 @@ __global__ void __launch_bounds__(kIfThreads, 1)
           *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
           *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], 0.0f, 0.0f, 0.0f);
         } else {
-          const size_t pix = ((static_cast<size_t>(n) * a.h_out + oy) * a.out_chunks + cg) * a.w_out + x;
+          const size_t pix = ((static_cast<size_t>(n) * a.h_out + oy) * a.out_chunks + cg) * a.w_out + xs;
           if constexpr (kEpi == kIfResPrelu) {
             const uint4 r = __ldg(reinterpret_cast<const uint4*>(a.residual + pix * 16));
             const uint32_t rw[4] = {r.x, r.y, r.z, r.w};

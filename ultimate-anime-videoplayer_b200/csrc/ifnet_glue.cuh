@@ -248,8 +248,10 @@ constexpr int glue_run() {
   return kGlueRunRows / if_scale(K) > 0 ? kGlueRunRows / if_scale(K) : 1;
 }
 
-// Stores the 16 planes of one output pixel as two FP16 chunks.
+// Stores the 16 planes of one output pixel as two FP16 chunks. Each chunk row is parity-split,
+// the even pixels then the odd ones (wo even), which is the layout conv0a's stride-2 loads read.
 __device__ __forceinline__ void store_chunks(uint8_t* row, int wo, int ox, const float v[16]) {
+  const int xs = (ox & 1) * (wo >> 1) + (ox >> 1);
 #pragma unroll
   for (int ch = 0; ch < 2; ++ch) {
     uint4 o;
@@ -261,11 +263,12 @@ __device__ __forceinline__ void store_chunks(uint8_t* row, int wo, int ox, const
     o.y = *reinterpret_cast<uint32_t*>(&h1);
     o.z = *reinterpret_cast<uint32_t*>(&h2);
     o.w = *reinterpret_cast<uint32_t*>(&h3);
-    *reinterpret_cast<uint4*>(row + (static_cast<size_t>(ch) * wo + ox) * 16) = o;
+    *reinterpret_cast<uint4*>(row + (static_cast<size_t>(ch) * wo + xs) * 16) = o;
   }
 }
 
-// Input of block K as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used):
+// Input of block K as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used;
+// each chunk row parity-split):
 // the block's planes resized to 1/s (not for s = 1), the flow planes then divided by s. One
 // instantiation per block, so that every plane array stays in registers; 64 registers a thread
 // (4 blocks of 256 per SM: measured 19-27 % faster than 80-88 registers at 2-3 blocks, no spills).

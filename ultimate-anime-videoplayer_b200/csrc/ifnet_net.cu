@@ -155,6 +155,7 @@ struct IfLayer {
     a.stage_bytes = (a.a_bytes + a.b_bytes + 1023u) & ~1023u;
     a.out = out;
     a.out_chunks = out_chunks;
+    a.out_split = 0;
     a.out_f32 = out_f32;
     a.residual = epi == kIfResPrelu ? in : nullptr;
     a.err = err;
@@ -205,11 +206,13 @@ struct IfLayer {
       r = fn(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, in, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
+      // parity-split rows: a chunk row is its W/2 even pixels then its W/2 odd pixels, so each
+      // parity box is one contiguous 2 KB run per chunk
       if (w_in % 2 != 0) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet: stride-2 input of odd width");
-      const cuuint64_t dims[5] = {2, 2, static_cast<cuuint64_t>(w_in / 2), static_cast<cuuint64_t>(in_chunks), rows};
-      const cuuint64_t strides[4] = {16, 32, row, row * in_chunks};
-      const cuuint32_t box[5] = {2, 1, 128, static_cast<cuuint32_t>(g), 1};
-      r = fn(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, in, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      const cuuint64_t dims[4] = {static_cast<cuuint64_t>(w_in), 2, static_cast<cuuint64_t>(in_chunks), rows};
+      const cuuint64_t strides[3] = {static_cast<cuuint64_t>(w_in / 2) * 16, row, row * in_chunks};
+      const cuuint32_t box[4] = {256, 1, static_cast<cuuint32_t>(g), 1};
+      r = fn(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, in, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     if (r != CUDA_SUCCESS)
@@ -318,6 +321,7 @@ Status IfnetNet::create(const std::vector<float>& params, int max_batch, int H, 
     auto la = std::make_unique<IfLayer>();
     KB2_TRY(la->build(c / 2, 2, kIfPrelu, conv_w(wa, cin0), c / 2, cin0, ba, sa, x->ptr, max_batch_, h0, w0, 2, h1,
                       w1, a0->ptr, c / 16, nullptr, err));
+    la->args.out_split = 1;  // conv0b reads a0 with stride 2
     la->kind = k_c0a;
     layers_.push_back(std::move(la));
     // conv0b
