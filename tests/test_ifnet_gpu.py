@@ -129,6 +129,25 @@ def test_batch_is_independent_per_pair(params):
         np.testing.assert_array_equal(together[i:i + 1], alone)
 
 
+def test_stream_pairs_as_overlapping_views(params):
+    """Consecutive pairs of one frame sequence, (f_i, f_i+1), given as two views one frame apart
+    into the same device buffer (how a player streams a video; the bench's e2e leg does this),
+    give the same frames as the pairs copied into separate tensors."""
+    import torch
+    from synth import shifted_pair
+    seq = f16(np.stack([shifted_pair(64, 96, seed=70 + i)[0] for i in range(4)]))
+    separate = run_ifnet(seq[:3], seq[1:], 0.5, params)
+    eng = kb.Engine(kb.MODEL_IFNET, kb.make_blob(kb.MODEL_IFNET, nets.ifnet_flat(params)), 64, 96, max_batch=3)
+    eng.set_timestep(0.5)
+    d = torch.from_numpy(np.ascontiguousarray(seq, np.float16)).cuda()
+    out = torch.full((3, 3, 64, 96), float("nan"), dtype=torch.float16, device="cuda")
+    eng.enqueue([d[:3], d[1:]], [out])
+    eng.check_device()
+    eng.close()
+    np.testing.assert_array_equal(out.float().cpu().numpy(), separate)
+    np.testing.assert_array_equal(d.float().cpu().numpy(), seq)  # the inputs are only read
+
+
 def test_ifnet_refusals(params):
     import torch
     blob = kb.make_blob(kb.MODEL_IFNET, nets.ifnet_flat(params))
