@@ -60,6 +60,30 @@ typedef enum kb2_precision { KB2_PREC_FP16 = 1, KB2_PREC_FP8_E4M3 = 2 } kb2_prec
 
 typedef struct kb2_engine kb2_engine;
 
+/* Weight blob v1 (KB2_MODEL_SPAN_X2 and KB2_MODEL_IFNET): a 32-byte header, then the network's
+ * float32 parameters back to back, little-endian, in the order below. Conv weights are OIHW
+ * ([out][in][ky][kx]), transposed-conv weights [in][out][ky][kx] (ONNX ConvTranspose), each
+ * followed by its bias and, where the layer has one, its PReLU slopes (one per output channel).
+ *
+ * KB2_MODEL_SPAN_X2, canonical SPAN x2 (48 channels, 6 blocks; 389,916 floats):
+ *   conv_1      W [48][3][3][3],   b [48]
+ *   block b = 0..5, conv k = 1..3 (c1, c2 with SiLU after them; c3 into the SPAB gate):
+ *               W [48][48][3][3],  b [48]
+ *   conv_cat    W [48][192][1][1], b [48]   input channels: [conv_1 out, block 5 out, block 0 out,
+ *                                           block 5's c1 activation], 48 each
+ *   upsampler   W [12][48][3][3],  b [12]   then PixelShuffle(2), channel c*4 + dy*2 + dx
+ *
+ * KB2_MODEL_IFNET, classic IFNet (4 blocks at 1/8, 1/4, 1/2, 1/1 with C = 192, 128, 96, 64 channels;
+ * 5,160,980 floats). Block k's input has cin = 7 channels for k = 0 (frame A rgb, frame B rgb,
+ * timestep) and 12 after (warped A rgb, warped B rgb, timestep, mask, flow 4 / scale), then per block:
+ *   conv0a      W [C/2][cin][3][3], b [C/2], slope [C/2]   (stride 2)
+ *   conv0b      W [C][C/2][3][3],   b [C],   slope [C]     (stride 2)
+ *   res j=0..7  W [C][C][3][3],     b [C],   slope [C]     (PReLU(conv(x) + x))
+ *   last        W [C][5][4][4],     b [5]                  (transposed, stride 2, pad 1: 4 flow + mask)
+ */
+#define KB2_SPAN_X2_PARAMS 389916
+#define KB2_IFNET_PARAMS 5160980
+
 /* Engine creation parameters (the reference's Artifact + shape set, backend.h:446). */
 typedef struct kb2_engine_desc {
   int32_t model;        /* kb2_model */
@@ -139,9 +163,12 @@ int kb2_span_calibrate(kb2_engine* engine, void* stream, const kb2_tensor* frame
  *   - Limit: one x2 output frame (24 * H * W bytes) plus 256 bytes must fit in 64 MiB, i.e.
  *     H * W <= 2,796,192 pixels (1920x1080 fits, 2560x1440 does not); larger engines are refused
  *     with KB2_SHAPE_INVALID. Frames run min(max_batch, what fits) at a time.
- *   - The engine's device must be the current device. The first call on a device looks up the
- *     array (cudaGetSymbolAddress), which makes the driver load and reserve it there: make that
- *     first call before any stream capture begins. The call is synchronous on `stream`.
+ *   - The engine's device must be the current device. Every call looks up the array's address in
+ *     the current context (cudaGetSymbolAddress); the first call in a context makes the driver load
+ *     and reserve it there: make that first call before any stream capture begins. Under lazy
+ *     module loading (CUDA's default) only that first call reserves the 64 MiB; with
+ *     CUDA_MODULE_LOADING=EAGER every context that loads this library reserves it on each device it
+ *     uses, whether or not this entry point is called. The call is synchronous on `stream`.
  *   - Profiling must be off (its timing events would be created on demand).
  *   - Overlapping calls on one device race on the shared array: serialise them. */
 int kb2_span_calibrate_static(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks,

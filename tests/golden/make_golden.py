@@ -1,6 +1,6 @@
 """Generates tests/golden/*.npz from the reference's own FP32 CPU interpreter.
 
-    make -C oracle                      # builds oracle/_ref/libkirari_ref.so from the reference sources
+    make -C oracle REF=<reference checkout>     # builds oracle/_ref/libkirari_ref.so from the reference sources
     python tests/golden/make_golden.py
 
 The fixtures pin the numpy restatement (oracle/nets.py) and, through it, the CUDA path. Weights are

@@ -2,7 +2,7 @@
 (src/kernels/spec/ring_pack.h, color.h unorm16), built into oracle/_ref/libkirari_ref.so by
 oracle/Makefile (without multiply-add contraction, as the reference compiles it).
 
-    make -C oracle
+    make -C oracle REF=<reference checkout>
     python tests/golden/make_pack_golden.py
 
 The frame holds FP16 values (the engines' output format): a ramp over [-0.1, 1.1], the code

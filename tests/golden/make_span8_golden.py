@@ -2,7 +2,7 @@
 the unshuffle SPAN (src/gpu/span_fp8/package.cpp:143, forward.cpp:144), built into
 oracle/_ref/libkirari_ref.so by oracle/Makefile.
 
-    make -C oracle
+    make -C oracle REF=<reference checkout>
     python tests/golden/make_span8_golden.py
 
 The packages are regenerated from their seeds by oracle/nets.py (span8_init, span8_package); each

@@ -1,7 +1,7 @@
 """Generates tests/golden/warp_*.npz from the reference's own CPU warp_blend_at, warp_blend_poses and
 flow_max (src/kernels/ref/warp.cpp:261, :270, :290), built into oracle/_ref/libkirari_ref.so by oracle/Makefile.
 
-    make -C oracle
+    make -C oracle REF=<reference checkout>
     python tests/golden/make_warp_golden.py
 
 Frames are rounded to FP16 first (the library's frame format), so the GPU path reads the same values.

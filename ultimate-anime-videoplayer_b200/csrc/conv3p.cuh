@@ -1,9 +1,10 @@
-// Paired stacked 3x3 convolution: the stacked-kernel-row scheme of conv3s.cuh with every MMA shared
-// by the two SMs of a cluster (sm_100a, tcgen05 cta_group::2, M = 256).
+// Paired stacked 3x3 convolution: the stacked-kernel-row scheme (stack_common.cuh) with every MMA
+// shared by the two SMs of a cluster (sm_100a, tcgen05 cta_group::2, M = 256).
 //
-// Why: the single issuing thread limits conv3s. Measured on B200, a tcgen05.mma of M = 128 costs its
-// issuing thread ~60 cycles whatever else runs, and each instruction between MMAs costs more, so a
-// row of 9 MMAs plus its bookkeeping took ~1,400-1,800 cycles against ~820 cycles of tensor work. An
+// Why: the single issuing thread limits a one-SM stacked conv. Measured on B200, a tcgen05.mma of
+// M = 128 costs its issuing thread ~60 cycles whatever else runs, and each instruction between MMAs
+// costs more, so a row of 9 MMAs plus its bookkeeping took ~1,400-1,800 cycles against ~820 cycles
+// of tensor work. An
 // M = 256 MMA (cta_group::2) runs at the same ~72 cycles per instruction (N = 144, measured) but
 // feeds both SMs of the pair: the issue cost per output pixel halves.
 //
@@ -14,7 +15,7 @@
 //    0 .. N/2 - 1, block 1 rows N/2 .. N - 1, each as [K step][K half][N/2 rows][16 bytes], so one
 //    descriptor addresses both halves and D column c is B row c;
 //  * D: each block's TMEM holds its own 128 pixels x all N columns (the 6-slot, 8-block dual-location
-//    window of conv3s.cuh, unchanged).
+//    window of stack_common.cuh).
 // Block 0's thread issues every MMA; its barriers gather the pair: the input row is "full" when both
 // blocks' copies landed (the copies of block 1 complete on block 0's barrier), and an accumulator
 // slot is free when both blocks' epilogues read it (block 1 arrives remotely). Commits multicast to
@@ -32,7 +33,7 @@
 
 #include <utility>
 
-#include "conv3s.cuh"
+#include "stack_common.cuh"
 
 namespace kb2 {
 

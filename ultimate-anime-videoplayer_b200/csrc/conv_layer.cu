@@ -51,20 +51,14 @@ void launch_impl(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, cons
   conv_tc_kernel<F8, N, E, O><<<grid, ConvShape<N>::threads, smem, s>>>(m, a);
 }
 template <bool F8, int N, int E, int O>
-void launch_stacked(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
-  conv3s_kernel<F8, N, E, O><<<grid, StackShape<N>::threads, smem, s>>>(m, a);
-}
-template <bool F8, int N, int E, int O>
 void launch_paired(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
   conv3p_kernel<F8, N, E, O><<<grid, PairShape<N, E>::threads, smem, s>>>(m, a);  // clusters of 2 (__cluster_dims__)
 }
 
-constexpr int kKindGeneric = 0, kKindStacked = 1, kKindPaired = 2;
-// 3x3 layers whose rows are 2, 3, 5 or 9 K steps run on the pair kernel (conv3p.cuh)
-constexpr bool kPairedStack = true;
+constexpr int kKindGeneric = 0, kKindPaired = 2;
 
 struct KernelEntry {
-  int kind;  // kKindGeneric: conv_tc.cuh; kKindStacked: conv3s.cuh; kKindPaired: conv3p.cuh
+  int kind;  // kKindGeneric: conv_tc.cuh; kKindPaired: conv3p.cuh
   bool fp8;
   int n, epi, out;
   LaunchFn launch;
@@ -77,30 +71,16 @@ struct KernelEntry {
     kKindGeneric, F8, N, E, O, &launch_impl<F8, N, E, O>,                                                \
         reinterpret_cast<const void*>(&conv_tc_kernel<F8, N, E, O>), ConvShape<N>::threads               \
   }
-#define KB2_STACKED(F8, N, E, O)                                                                         \
-  KernelEntry {                                                                                          \
-    kKindStacked, F8, N, E, O, &launch_stacked<F8, N, E, O>,                                             \
-        reinterpret_cast<const void*>(&conv3s_kernel<F8, N, E, O>), StackShape<N>::threads               \
-  }
 #define KB2_PAIRED(F8, N, E, O)                                                                          \
   KernelEntry {                                                                                          \
     kKindPaired, F8, N, E, O, &launch_paired<F8, N, E, O>,                                               \
         reinterpret_cast<const void*>(&conv3p_kernel<F8, N, E, O>), PairShape<N, E>::threads             \
   }
 
-// The instantiations the SPAN engines use: 3x3 layers on the stacked kernel, the 1x1 conv_cat on
-// the generic one.
+// The instantiations the engines use: 3x3 layers on the pair kernel, the 1x1 convs (conv_cat, the
+// unshuffle SPAN's attention) on the generic one.
 const KernelEntry kKernels[] = {
     KB2_KERNEL(false, 48, kEpiBias, kOutF16Chunk),
-    KB2_STACKED(false, 48, kEpiBias, kOutF16Chunk),
-    KB2_STACKED(false, 48, kEpiSilu, kOutF16Chunk),
-    KB2_STACKED(false, 48, kEpiSpanAttn, kOutF16Chunk),
-    KB2_STACKED(false, 16, kEpiBias, kOutPixShuf2),
-    KB2_STACKED(false, 48, kEpiSpanAttn, kOutF16E4m3),
-    KB2_STACKED(true, 48, kEpiSilu, kOutE4m3Chunk),
-    KB2_STACKED(true, 48, kEpiSilu, kOutF16E4m3),
-    KB2_STACKED(true, 48, kEpiSpanAttn, kOutE4m3Chunk),
-    KB2_STACKED(true, 48, kEpiSpanAttn, kOutF16Chunk),
     KB2_PAIRED(false, 48, kEpiBias, kOutF16Chunk),
     KB2_PAIRED(false, 48, kEpiSilu, kOutF16Chunk),
     KB2_PAIRED(false, 48, kEpiSpanAttn, kOutF16Chunk),
@@ -179,10 +159,11 @@ int num_sms() {
 Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const float* prelu_slope,
                         const float* act_scales, const ChunkedTensor* const* inputs, int* err_word) {
   spec = s;
-  kind = wants_stacked(s) ? kKindStacked : kKindGeneric;
-  const KernelEntry* k = find_kernel(s, kind);  // stacked shapes may have a pair kernel only (below)
-  if (k == nullptr && (kind != kKindStacked || find_kernel(s, kKindPaired) == nullptr))
-    return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this layer shape");
+  // 3x3 layers run stacked on the pair kernel (conv3p.cuh), the rest on the generic one
+  const bool stacked = wants_stacked(s);
+  kind = stacked ? kKindPaired : kKindGeneric;
+  const KernelEntry* k = find_kernel(s, kind);
+  if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this layer shape");
   const ChunkedTensor& in0 = *inputs[0];
   for (int i = 0; i < s.n_sources; ++i) {
     const ChunkedTensor& t = *inputs[i];
@@ -194,7 +175,6 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   const int halo = s.taps == 9 ? 1 : 0;
   if (chunks * epc < s.cin) return refuse(KB2_INPUT_MISMATCH, "input tensor narrower than the conv");
 
-  const bool stacked = kind != kKindGeneric;
   auto steps = make_ksteps(s, chunks);
   if (stacked) {
     // one input row per instruction group: the dy = 0 steps (every dy uses the same pixel shifts
@@ -203,14 +183,9 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     for (const auto& st : steps)
       if (st[0].dy == 0) row_steps.push_back(st);
     steps = row_steps;
-    // rows of 2, 3, 5, 9 (or 12 at 64 channels) K steps run on the pair kernel (one MMA for two SMs)
-    const int nk = static_cast<int>(steps.size());
-    const KernelEntry* kp = find_kernel(s, kKindPaired);
-    if ((kPairedStack || k == nullptr) && kp != nullptr && pair_admits(s, nk)) {
-      kind = kKindPaired;
-      k = kp;
-    }
-    if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this row shape");
+    // the pair kernel (one MMA for two SMs) runs rows of the K-step counts it admits
+    if (!pair_admits(s, static_cast<int>(steps.size())))
+      return refuse(KB2_FORMAT_UNSUPPORTED, "no tensor-core kernel for this row shape");
   }
   const bool paired = kind == kKindPaired;
   if (static_cast<int>(steps.size()) > kMaxKSteps) return refuse(KB2_FORMAT_UNSUPPORTED, "too many K steps");
@@ -278,7 +253,7 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     a.n_tiles = 0;
     for (int i = 0; i < 3; ++i) a.idesc_n[i] = make_idesc(kTileM, (i + 1) * s.n_pad);
     a.acc_slots = static_cast<int>(kStackSlots);
-    if (static_cast<int>(steps.size()) > (paired ? kPairMaxK : kRowMaxK))
+    if (static_cast<int>(steps.size()) > kPairMaxK)
       return refuse(KB2_FORMAT_UNSUPPORTED, "stacked: too many K steps per row");
   }
   const int n_rows_b = stacked ? 3 * s.n_pad : s.n_pad;  // rows of B per K step

@@ -29,7 +29,7 @@ struct ConvLayer {
   DeviceBuffer wpack, bias, scale, slope;
   size_t smem = 0;
   int grid = 0;
-  int kind = 0;  // kernel family: 0 conv_tc.cuh, 1 conv3s.cuh, 2 conv3p.cuh (paired)
+  int kind = 0;  // kernel family: 0 conv_tc.cuh, 2 conv3p.cuh (paired stacked 3x3)
 
   // W: [n_real][n_sources * cin][k][k] (OIHW), b: [n_real]. act_scales: per-source E4M3 scale of
   // the input tensors (FP8 only; folded into the per-output-channel weight scales).

@@ -9,7 +9,7 @@
 
 namespace kb2 {
 
-constexpr size_t kIfnetParams = 5160980;  // oracle/nets.py ifnet_param_shapes
+constexpr size_t kIfnetParams = KB2_IFNET_PARAMS;  // the blob order of include/kirari_b200.h
 // Padded frame: multiples of 32, what the network needs (its coarsest level is 1/32 of the frame).
 // The reference pads to 64 for its RIFE 4.x models (src/kernels/spec/rife.h:33); for 1920x1080 both
 // give 1920x1088.

@@ -26,12 +26,6 @@
 
 namespace kb2 {
 
-// Fused E4M3 SPAN blocks (spab8.cuh, bit-identical to the three separate launches) are off: its
-// three 3-slot accumulator rings wrap on two rows in three, and a wrapped row is issued as two MMA
-// groups. Measured on 8 x 1080p one fused block took 3.71 ms against 0.94 + 0.94 + 1.07 ms for the
-// three stacked launches; a conv row's issue took ~1,000 cycles unwrapped and ~1,700 wrapped.
-constexpr bool kFuseSpab = false;
-
 namespace {
 
 // NCHW half [n][3][H][W] -> [n][H][2][W][8] half (16 channels, 3 real).
@@ -135,7 +129,7 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
     KB2_TRY(tensor(6, false, &xb));
   }
 
-  // parameter offsets (oracle/nets.py span_param_shapes order)
+  // parameter offsets (the blob order of include/kirari_b200.h)
   const int c = 48;
   const float* w1 = params.data();
   const float* b1 = w1 + c * 3 * 9;
@@ -195,7 +189,6 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
   for (int b = 0; b < kSpanBlocks; ++b) {
     const bool q = block_fp8(b);
     const bool last = b == kSpanBlocks - 1;
-    const ChunkedTensor* blk_in = x_in;
     const float* wk[3];
     for (int k = 0; k < 3; ++k) wk[k] = blk + (static_cast<size_t>(b) * 3 + k) * conv48;
     auto bias = [&](int k) { return wk[k] + static_cast<size_t>(c) * c * 9; };
@@ -233,28 +226,6 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
     } else {
       KB2_TRY(add(spec(9, true, c, kEpiSpanAttn, kOutF16Chunk), wk[2], bias(2), &sc_a2, {t2},
                   Step{nullptr, x6, nullptr, x_in, 1.0f, res_scale, -1}));
-    }
-    if (q && kFuseSpab) {
-      // E4M3 block: its three launches become one fused kernel (spab8.cuh); the three layers stay
-      // as the holders of the packed weights and scales
-      const Step s3 = steps_.back();
-      steps_.pop_back();
-      const Step s2 = steps_.back();
-      steps_.pop_back();
-      const Step s1 = steps_.back();
-      steps_.pop_back();
-      spabs_.push_back(std::make_unique<SpabLayer>());
-      SpabLayer* f = spabs_.back().get();
-      KB2_TRY(f->build(*s1.layer, *s2.layer, *s3.layer, *blk_in, s1.out_inv_scale, s2.out_inv_scale, s3.out_inv_scale,
-                       s3.res_scale, last, err));
-      Step fs = s3;
-      fs.layer = nullptr;
-      fs.spab = f;
-      fs.t1_copy = last ? s1.out : nullptr;
-      fs.flops_px = s1.flops_px + s2.flops_px + s3.flops_px;
-      fs.bytes_px = blk_in->chunks * 16.0 + s3.out->chunks * 16.0 + (last ? s1.out->chunks * 16.0 : 0.0);
-      fs.kind = kind_index("span.spab.fp8");
-      steps_.push_back(fs);
     }
   }
   {  // conv_cat: FP16 1x1 over four FP16 sources
@@ -297,13 +268,9 @@ Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, b
   for (const Step& s : steps_) {
     void* dst = s.out != nullptr ? static_cast<void*>(s.out->ptr) : out;
     if (profiling_) KB2_TRY(timed(s.kind, 0.0, 0.0, stream, true));
-    if (s.spab != nullptr) {
-      KB2_TRY(s.spab->launch(stream, batch, dst, s.t1_copy != nullptr ? s.t1_copy->ptr : nullptr));
-    } else {
-      KB2_TRY(s.layer->launch(stream, batch, dst, s.residual != nullptr ? s.residual->ptr : nullptr, s.out_inv_scale,
-                              s.res_scale, s.out2 != nullptr ? s.out2->ptr : nullptr,
-                              s.residual != nullptr ? s.residual->chunks : 0));
-    }
+    KB2_TRY(s.layer->launch(stream, batch, dst, s.residual != nullptr ? s.residual->ptr : nullptr, s.out_inv_scale,
+                            s.res_scale, s.out2 != nullptr ? s.out2->ptr : nullptr,
+                            s.residual != nullptr ? s.residual->chunks : 0));
     if (profiling_) KB2_TRY(timed(s.kind, s.flops_px * pixels, s.bytes_px * pixels, stream, false));
     if (capture_peaks && s.peak >= 0) {
       const size_t n2 = static_cast<size_t>(batch) * H_ * s.out->chunks * W_ * 4;  // 4 half2 per chunk

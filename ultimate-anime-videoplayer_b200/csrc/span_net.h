@@ -6,11 +6,10 @@
 #include <vector>
 
 #include "conv_layer.h"
-#include "spab_layer.h"
 
 namespace kb2 {
 
-constexpr size_t kSpanParams = 389916;  // oracle/nets.py span_param_shapes
+constexpr size_t kSpanParams = KB2_SPAN_X2_PARAMS;  // the blob order of include/kirari_b200.h
 constexpr int kSpanScales = 19;         // 1 + 3 * 6 E4M3 activation scales
 constexpr int kSpanBlocks = 6;
 
@@ -62,8 +61,6 @@ class SpanNet {
     int peak;  // calibration index of `out`, -1 none
     int kind;  // profile record
     double flops_px, bytes_px;  // algorithmic work per output pixel
-    SpabLayer* spab;              // a fused E4M3 block (then `layer` is unused), else null
-    const ChunkedTensor* t1_copy;  // fused last block: FP16 copy of its first activation
   };
   int kind_index(const char* name);
   Status timed(int kind, double flops, double bytes, cudaStream_t stream, bool begin);
@@ -75,7 +72,6 @@ class SpanNet {
   DeviceBuffer err_, peaks_;
   std::vector<std::unique_ptr<Tensor>> tensors_;
   std::vector<std::unique_ptr<ConvLayer>> layers_;
-  std::vector<std::unique_ptr<SpabLayer>> spabs_;
   std::vector<Step> steps_;
   const ChunkedTensor* img_ = nullptr;
   bool profiling_ = false;

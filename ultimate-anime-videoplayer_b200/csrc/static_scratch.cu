@@ -9,39 +9,32 @@
 // calibration itself allocates nothing.
 //
 // The array is kStaticScratchBytes (64 MiB) of __device__ memory. The driver reserves it on a
-// device when it loads this file's module there. That happens on the first static_scratch() call
-// made with that device current: cudaGetSymbolAddress loads the module. The memory stays reserved
-// until the context ends. Nothing else in the library touches this module, so engines that never
-// use the static path never pay for the array.
+// device when it loads this file's module there. With lazy module loading (CUDA's default,
+// CUDA_MODULE_LOADING=LAZY) that happens on the first static_scratch() call made with that device
+// current, so engines that never use the static path never pay for the array. With
+// CUDA_MODULE_LOADING=EAGER every context that loads the library reserves the 64 MiB on each device
+// it uses, whether or not the static path ever runs. The memory stays reserved until the context
+// ends.
 //
 // One array per device, shared by every engine on it: overlapping calls on the same device race
 // on it.
-#include <mutex>
-
 #include "static_scratch.h"
 
 namespace kb2 {
 
 namespace {
 __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
-
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void* g_addr[kMaxDevices] = {};  // g_static_scratch's address on each device, once looked up
 }  // namespace
 
 Status static_scratch(void** ptr) {
-  int dev = -1;
-  KB2_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices) return refuse(KB2_FORMAT_UNSUPPORTED, "static scratch: device ordinal >= 64");
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (g_addr[dev] == nullptr) {
-    void* p = nullptr;
-    KB2_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));  // with `dev` current: loads the module there
-    if (p == nullptr) return refuse(KB2_VENDOR_CALL_FAILED, "static scratch: null symbol address");
-    g_addr[dev] = p;
-  }
-  *ptr = g_addr[dev];
+  // Looked up on every call, not cached: the address belongs to the module as loaded in the
+  // current context, and a context that is destroyed and made again (cudaDeviceReset, or another
+  // driver-API context made current) may load the module at another address. Once the module is
+  // loaded the lookup is cheap.
+  void* p = nullptr;
+  KB2_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+  if (p == nullptr) return refuse(KB2_VENDOR_CALL_FAILED, "static scratch: null symbol address");
+  *ptr = p;
   return Status::Ok();
 }
 

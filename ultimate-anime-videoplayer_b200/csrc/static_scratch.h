@@ -7,9 +7,9 @@ namespace kb2 {
 
 constexpr size_t kStaticScratchBytes = static_cast<size_t>(64) << 20;  // 64 MiB per device
 
-// Device address of the static scratch on the current device. The first call on a device looks it
-// up with cudaGetSymbolAddress, which loads the array's module on that device (the one-time setup);
-// later calls only read a cached address.
+// Device address of the static scratch in the current device's current context, looked up with
+// cudaGetSymbolAddress on every call. The first call in a context loads the array's module there
+// (the one-time setup, under lazy module loading); later calls are a cheap lookup.
 Status static_scratch(void** ptr);
 
 }  // namespace kb2
