@@ -126,10 +126,32 @@ int kb2_workspace_bytes(const kb2_engine* engine, uint64_t* bytes);
  * (src/gpu/cuda/backend/tensorrt_backend.cpp:527-548).
  *   SPAN:  inputs[0] = F16 [n,3,H,W];              outputs[0] = F16 [n,3,2H,2W]
  *   IFNet: inputs[0] = F16 [n,3,H,W] (frame A), inputs[1] = F16 [n,3,H,W] (frame B);
- *          outputs[0] = F16 [n,3,H,W] (the frame at the engine's timestep)
+ *          outputs[0] = F16 [n,3,H,W] (the frame at the engine's timestep), or, the motion
+ *          variant (the reference's run_motion, src/app/play/upscale_motion.cpp:71-84, whose finish
+ *          writes "flow and mask", src/gpu/cuda/backend/rife_finish.cuh:40-55): two outputs
+ *          outputs[0] = flow [n,4,Hp,Wp] (f0x, f0y, f1x, f1y: displacements to frames A and B in
+ *          pixels) and outputs[1] = mask [n,1,Hp,Wp] (sigmoid of the mask: the weight of frame A),
+ *          both F32 or both F16, over the padded plane of kb2_rife_geometry. F32 outputs feed
+ *          kb2_motion (kb2_warp_blend_at, kb2_flow_max) directly.
  * n <= max_batch, H and W the engine's. Device pointers must be 16-byte aligned. */
 int kb2_enqueue(kb2_engine* engine, void* stream, const kb2_tensor* inputs, int32_t n_inputs,
                 const kb2_tensor* outputs, int32_t n_outputs);
+
+/* SPAN x2: what the following enqueues write. 0 (the default): F16 frames [n,3,2H,2W]. A
+ * kb2_display_format: the display pixels the reference's ring store writes from its last layer's
+ * epilogue (store_pixel, src/gpu/cuda/backend/span_native16_kernels.cuh:325; pixel codes of
+ * src/kernels/spec/ring_pack.h), written here by the upsampler's epilogue, with no F16 frame in
+ * between: outputs[0] is then U8 [n, B, 2H, 2W] with B = 8 (RGBA16) or 4 (RGB10A2 forms) bytes a
+ * pixel, the pixels packed row by row (row pitch 2W * B bytes; the C dimension is the pixel's bytes,
+ * interleaved). Each pixel equals kb2_pack_display of the F16 frame the engine would have written.
+ * KB2_FORMAT_UNSUPPORTED for other engines. */
+int kb2_set_output_format(kb2_engine* engine, int32_t format);
+
+/* IFNet: the padded plane the network runs on (multiples of 32) and the frame's window in it, as the
+ * reference's rife_geometry (src/kernels/spec/rife.h:47-63; left / top = half the padding, rounded
+ * down to even): the motion outputs are plane_h x plane_w, the frame at (window_x, window_y). */
+int kb2_rife_geometry(const kb2_engine* engine, int32_t* plane_h, int32_t* plane_w, int32_t* window_x,
+                      int32_t* window_y);
 
 /* IFNet: timestep of the following enqueues, in (0, 1) (the time planes of the reference's
  * 11-plane input, src/kernels/spec/rife.h:60; Engine::next_times_only, backend.h:391). */

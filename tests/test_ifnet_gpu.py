@@ -174,3 +174,120 @@ def test_ifnet_refusals(params):
         assert e.value.status == kb.KB2_SHAPE_INVALID
     finally:
         eng.close()
+
+
+# ------------------------------------------------------------------------------------------------
+# the motion variant: flow and mask in place of the frame (the reference's run_motion,
+# src/app/play/upscale_motion.cpp:71-84; finish src/gpu/cuda/backend/rife_finish.cuh:40-55)
+# ------------------------------------------------------------------------------------------------
+# Flow is in pixels; the FP16 network's flow error that keeps the blended frame within 2/255 at a
+# sharp edge (an image gradient of ~1 a pixel) is about 0.01 px, and the measured error is below it.
+MOTION_FLOW_MAX_ABS = 0.02
+MOTION_MASK_MAX_ABS = 2.0 / 255.0
+
+
+def padded_motion_oracle(a, b, t, p):
+    """The oracle's final flow [n,4,Hp,Wp] and sigmoid(mask) [n,1,Hp,Wp] on the engine's padded plane,
+    with the window (x, y, w, h) of the frames in it."""
+    n, c, h, w = a.shape
+    hp, wp = -(-h // 32) * 32, -(-w // 32) * 32
+    top, left = ((hp - h) // 2) & ~1, ((wp - w) // 2) & ~1
+
+    def pad(x):
+        z = np.zeros((n, c, hp, wp), np.float32)
+        z[:, :, top:top + h, left:left + w] = x
+        return z
+
+    _, flow, mask = nets.ifnet_forward(pad(a), pad(b), t, p, return_flow=True)
+    return flow, nets.sigmoid(mask), (left, top, w, h)
+
+
+def run_motion(a, b, t, p, dtype="float32"):
+    import torch
+    n, _, h, w = a.shape
+    eng = kb.Engine(kb.MODEL_IFNET, kb.make_blob(kb.MODEL_IFNET, nets.ifnet_flat(p)), h, w, max_batch=n)
+    try:
+        eng.set_timestep(t)
+        ta = torch.from_numpy(np.ascontiguousarray(a, np.float16)).cuda()
+        tb = torch.from_numpy(np.ascontiguousarray(b, np.float16)).cuda()
+        flow, mask, win = eng.motion(ta, tb, dtype=getattr(torch, dtype))
+        eng.check_device()
+    finally:
+        eng.close()
+    return flow, mask, win
+
+
+@pytest.mark.parametrize("shape,t", [((1, 72, 100), 0.5), ((2, 64, 96), 0.5), ((1, 130, 66), 0.3)])
+def test_motion_matches_oracle(shape, t, params):
+    from synth import shifted_pair
+    n, h, w = shape
+    pairs = [shifted_pair(h, w, seed=90 + i) for i in range(n)]
+    a = f16(np.stack([q[0] for q in pairs]))
+    b = f16(np.stack([q[1] for q in pairs]))
+    flow, mask, win = run_motion(a, b, t, params)
+    rflow, rmask, rwin = padded_motion_oracle(a, b, t, params)
+    assert win == rwin
+    flow, mask = flow.cpu().numpy(), mask.cpu().numpy()
+    assert flow.shape == rflow.shape and mask.shape == rmask.shape
+    assert np.isfinite(flow).all() and np.isfinite(mask).all()
+    ferr = float(np.max(np.abs(flow - rflow)))
+    merr = float(np.max(np.abs(mask - rmask)))
+    print(f"motion {shape} t={t}: flow max-abs {ferr:.5f} px (|flow| up to {np.abs(rflow).max():.2f}), "
+          f"mask max-abs {merr * 255:.3f}/255")
+    assert ferr <= MOTION_FLOW_MAX_ABS, f"flow max-abs {ferr:.5f} px"
+    assert merr <= MOTION_MASK_MAX_ABS, f"mask max-abs {merr * 255:.3f}/255"
+
+
+def test_motion_f16_is_the_f32_motion_rounded(params):
+    from synth import shifted_pair
+    a, b = (f16(x[None]) for x in shifted_pair(64, 96, seed=95))
+    flow32, mask32, _ = run_motion(a, b, 0.5, params)
+    flow16, mask16, _ = run_motion(a, b, 0.5, params, dtype="float16")
+    np.testing.assert_array_equal(flow16.cpu().numpy(), flow32.half().cpu().numpy())
+    np.testing.assert_array_equal(mask16.cpu().numpy(), mask32.half().cpu().numpy())
+
+
+@pytest.mark.parametrize("t", [1.0 / 3.0, 0.5])
+def test_motion_feeds_warp_blend_at(t, params):
+    """The library's interpolator feeding its own warp: IFNet motion at the middle of the pair, then
+    kb2_warp_blend_at at t, against the oracle's motion through the reference's CPU warp_blend_at
+    (src/kernels/ref/warp.cpp:261; the numpy restatement where the reference build is absent)."""
+    import torch
+    from oracle import ref_lib
+    from synth import shifted_pair
+    a, b = (f16(x[None]) for x in shifted_pair(72, 100, seed=97))
+    flow, mask, win = run_motion(a, b, 0.5, params)
+    ta = torch.from_numpy(a.astype(np.float16)).cuda()
+    tb = torch.from_numpy(b.astype(np.float16)).cuda()
+    got = kb.warp_blend_at(ta, tb, flow, mask, win, t)
+    torch.cuda.synchronize()
+    got = got.float().cpu().numpy()[0]
+    rflow, rmask, rwin = padded_motion_oracle(a, b, 0.5, params)
+    warp = ref_lib.warp_blend_at if ref_lib.available() else nets.warp_blend_at
+    ref = warp(a[0], b[0], rflow[0], rmask[0, 0], rwin, t)
+    err = nets.max_abs_clamped(got, ref)
+    print(f"motion -> warp_blend_at t={t:.3f}: max-abs {err * 255:.3f}/255")
+    assert err <= FP16_MAX_ABS, f"t={t}: max-abs {err * 255:.3f}/255"
+    if t == 0.5:  # at the middle the warp of the mid-pair motion is the network's own frame
+        frame = run_ifnet(a, b, 0.5, params)[0]
+        assert nets.max_abs_clamped(got, frame) <= FP16_MAX_ABS
+
+
+def test_motion_refusals(params):
+    import torch
+    blob = kb.make_blob(kb.MODEL_IFNET, nets.ifnet_flat(params))
+    eng = kb.Engine(kb.MODEL_IFNET, blob, 72, 100, max_batch=1)
+    try:
+        assert eng.rife_geometry() == (96, 128, 14, 12)
+        x = torch.zeros((1, 3, 72, 100), dtype=torch.float16, device="cuda")
+        flow = torch.zeros((1, 4, 96, 128), dtype=torch.float32, device="cuda")
+        mask = torch.zeros((1, 1, 96, 128), dtype=torch.float32, device="cuda")
+        for bad in ([flow, mask.half()],  # types differ
+                    [torch.zeros((1, 4, 72, 100), device="cuda"), mask],  # the window, not the plane
+                    [flow, torch.zeros((1, 2, 96, 128), device="cuda")],
+                    [flow.to(torch.uint8), mask.to(torch.uint8)]):
+            with pytest.raises(kb.KB2Error) as e:
+                eng.enqueue([x, x], bad)
+            assert e.value.status == kb.KB2_INPUT_MISMATCH
+    finally:
+        eng.close()

@@ -39,15 +39,39 @@ kb2::Status tensor_ptr(const kb2_tensor& t, int type, const int64_t (&dims)[4], 
 
 namespace kb2 {
 Status Engine::frame_io(const kb2_tensor* inputs, int n_in, const kb2_tensor* outputs, int n_out, int n_frames_in,
-                        int out_scale, void** in_ptrs, void** out_ptr, int* batch) const {
+                        int out_scale, void** in_ptrs, void** out_ptr, int* batch, int display_bytes) const {
   if (inputs == nullptr || outputs == nullptr || n_in != n_frames_in || n_out != 1)
     return refuse(KB2_INPUT_MISMATCH, "wrong number of input / output tensors");
   const int64_t n = inputs[0].dims[0];
   if (n < 1 || n > max_batch()) return refuse(KB2_SHAPE_INVALID, "batch out of contract");
   const int64_t din[4] = {n, 3, height(), width()};
   for (int i = 0; i < n_in; ++i) KB2_TRY(tensor_ptr(inputs[i], KB2_F16, din, &in_ptrs[i]));
-  const int64_t dout[4] = {n, 3, height() * out_scale, width() * out_scale};
-  KB2_TRY(tensor_ptr(outputs[0], KB2_F16, dout, out_ptr));
+  if (display_bytes > 0) {
+    const int64_t dpix[4] = {n, display_bytes, height() * out_scale, width() * out_scale};
+    KB2_TRY(tensor_ptr(outputs[0], KB2_U8, dpix, out_ptr));
+  } else {
+    const int64_t dout[4] = {n, 3, height() * out_scale, width() * out_scale};
+    KB2_TRY(tensor_ptr(outputs[0], KB2_F16, dout, out_ptr));
+  }
+  *batch = static_cast<int>(n);
+  return Status::Ok();
+}
+
+Status Engine::motion_io(const kb2_tensor* inputs, int n_in, const kb2_tensor* outputs, int n_out, int ph, int pw,
+                         void** in_ptrs, void** flow, void** mask, bool* f16, int* batch) const {
+  if (inputs == nullptr || outputs == nullptr || n_in != 2 || n_out != 2)
+    return refuse(KB2_INPUT_MISMATCH, "motion: two frames in, flow and mask out");
+  const int64_t n = inputs[0].dims[0];
+  if (n < 1 || n > max_batch()) return refuse(KB2_SHAPE_INVALID, "batch out of contract");
+  const int64_t din[4] = {n, 3, height(), width()};
+  for (int i = 0; i < n_in; ++i) KB2_TRY(tensor_ptr(inputs[i], KB2_F16, din, &in_ptrs[i]));
+  const int type = outputs[0].type;
+  if (type != KB2_F32 && type != KB2_F16) return refuse(KB2_INPUT_MISMATCH, "motion outputs: F32 or F16");
+  const int64_t dflow[4] = {n, 4, ph, pw};
+  const int64_t dmask[4] = {n, 1, ph, pw};
+  KB2_TRY(tensor_ptr(outputs[0], type, dflow, flow));
+  KB2_TRY(tensor_ptr(outputs[1], type, dmask, mask));
+  *f16 = type == KB2_F16;
   *batch = static_cast<int>(n);
   return Status::Ok();
 }
@@ -115,6 +139,15 @@ int kb2_enqueue(kb2_engine* engine, void* stream, const kb2_tensor* inputs, int3
   try {
     return set_error(engine, engine->impl->enqueue(static_cast<cudaStream_t>(stream), inputs, n_inputs, outputs,
                                                    n_outputs));
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
+int kb2_set_output_format(kb2_engine* engine, int32_t format) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    return set_error(engine, engine->impl->set_output_format(format));
   } catch (const std::exception& ex) {
     return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
   }
@@ -219,6 +252,17 @@ int kb2_read_profile(kb2_engine* engine, kb2_layer_profile* records, int32_t cap
     return rc;
   } catch (const std::exception& ex) {
     return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
+int kb2_rife_geometry(const kb2_engine* engine, int32_t* plane_h, int32_t* plane_w, int32_t* window_x,
+                      int32_t* window_y) {
+  if (engine == nullptr || plane_h == nullptr || plane_w == nullptr || window_x == nullptr || window_y == nullptr)
+    return KB2_INVALID_ARGUMENT;
+  try {
+    return engine->impl->geometry(plane_h, plane_w, window_x, window_y).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
   }
 }
 

@@ -85,6 +85,7 @@ const KernelEntry kKernels[] = {
     KB2_PAIRED(false, 48, kEpiSilu, kOutF16Chunk),
     KB2_PAIRED(false, 48, kEpiSpanAttn, kOutF16Chunk),
     KB2_PAIRED(false, 16, kEpiBias, kOutPixShuf2),
+    KB2_PAIRED(false, 16, kEpiBias, kOutPixShuf2Display),
     KB2_PAIRED(false, 48, kEpiSpanAttn, kOutF16E4m3),
     KB2_PAIRED(true, 48, kEpiSilu, kOutE4m3Chunk),
     KB2_PAIRED(true, 48, kEpiSilu, kOutF16E4m3),
@@ -411,7 +412,8 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
 }
 
 Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
-                         float res_scale, void* out2, int res_chunks, const void* residual2) const {
+                         float res_scale, void* out2, int res_chunks, const void* residual2, long long out_pitch,
+                         int display_format) const {
   const KernelEntry* k = find_kernel(spec, kind);
   if (k == nullptr) return refuse(KB2_FORMAT_UNSUPPORTED, "no kernel");
   const bool paired = kind == kKindPaired;
@@ -426,6 +428,8 @@ Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* 
   a.res_chunks = res_chunks;
   a.out_inv_scale = out_inv_scale;
   a.res_scale = res_scale;
+  a.out_pitch = out_pitch;
+  a.display_format = display_format;
   int g = a.items < grid ? a.items : grid;
   if (paired) {
     // pair kernel: contiguous row ranges, one per cluster (conv3p.cuh PairSpan)

@@ -37,8 +37,10 @@ struct ConvLayer {
                const float* act_scales, const ChunkedTensor* const* inputs, int* err_word);
   // residual / out: device pointers for this launch (residual may be null); residual2: the second
   // addend of kEpiTanhGate.
+  // display: kOutPixShuf2Display's row pitch and kb2_display_format.
   Status launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,
-                float res_scale, void* out2 = nullptr, int res_chunks = 0, const void* residual2 = nullptr) const;
+                float res_scale, void* out2 = nullptr, int res_chunks = 0, const void* residual2 = nullptr,
+                long long out_pitch = 0, int display_format = 0) const;
 };
 
 int num_sms();

@@ -28,6 +28,7 @@
 //  * Persistent CTAs walk work items (image, band of rows, 128-pixel strip).
 #pragma once
 
+#include "display_pixel.cuh"
 #include "tc_common.cuh"
 
 namespace kb2 {
@@ -61,6 +62,10 @@ enum OutFmt : int {
   kOutPixShuf2 = 2,   // NCHW half [n][3][2H][2W], DepthToSpace(2, CRD) of 12 channels
   kOutF16E4m3 = 3,    // both: half chunks to `out`, E4M3 chunks (value * out_inv_scale) to `out2`
   kOutPixShuf4 = 4,   // NCHW half [n][3][4H][4W], DepthToSpace(4, CRD) of 48 channels
+  // DepthToSpace(2, CRD) of 12 channels as display pixels (display_pixel.cuh, format a.display_format),
+  // rows of 2W pixels at a.out + (n * 2H + row) * a.out_pitch: each value rounded to FP16 first, so the
+  // pixels are those the packing pass makes of the FP16 frame
+  kOutPixShuf2Display = 5,
 };
 
 struct KStep {
@@ -101,6 +106,8 @@ struct ConvArgs {
   int out_chunks;  // chunks per output pixel (chunked formats)
   uint8_t* out2;   // kOutF16E4m3: the E4M3 copy
   int out2_chunks;
+  long long out_pitch;  // kOutPixShuf2Display: bytes per output row
+  int display_format;   // kOutPixShuf2Display: kb2_display_format
   int* err;
 };
 
@@ -266,6 +273,33 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
         const size_t at = ((static_cast<size_t>(n) * 3 + plane) * H4 + 4 * static_cast<size_t>(y) + i) * W4 + 4 * x;
         *reinterpret_cast<uint2*>(a.out + at * 2) =
             make_uint2(pack_half2(v[4 * q], v[4 * q + 1]), pack_half2(v[4 * q + 2], v[4 * q + 3]));
+      }
+    }
+  }
+  if constexpr (kOut == kOutPixShuf2Display) {
+    // channel 4p + 2i + j -> display pixel (2y + i, 2x + j), p = r, g, b: the thread holds all 12
+    // channels of its input pixel (col0 = 0), so each output row gets its two pixels in one store
+    static_assert(kCols >= 12, "the display epilogue needs the pixel's 12 channels");
+    const int fmt = a.display_format;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t oy = 2u * static_cast<uint32_t>(y) + static_cast<uint32_t>(i);
+      uint8_t* row = a.out + (static_cast<size_t>(n) * 2 * a.H + oy) * static_cast<size_t>(a.out_pitch);
+      float c[2][3];
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int p = 0; p < 3; ++p) c[j][p] = __half2float(__float2half_rn(v[4 * p + 2 * i + j]));
+      const uint32_t ox = 2u * static_cast<uint32_t>(x);
+      if (fmt == KB2_DISPLAY_RGBA16) {
+        const uint2 p0 = rgba16(c[0][0], c[0][1], c[0][2]);
+        const uint2 p1 = rgba16(c[1][0], c[1][1], c[1][2]);
+        *reinterpret_cast<uint4*>(row + static_cast<size_t>(ox) * 8) = make_uint4(p0.x, p0.y, p1.x, p1.y);
+      } else {
+        const bool dither = fmt == KB2_DISPLAY_RGB10A2_DITHER;
+        *reinterpret_cast<uint2*>(row + static_cast<size_t>(ox) * 4) =
+            make_uint2(rgb10a2(c[0][0], c[0][1], c[0][2], dither, ox, oy),
+                       rgb10a2(c[1][0], c[1][1], c[1][2], dither, ox + 1u, oy));
       }
     }
   }

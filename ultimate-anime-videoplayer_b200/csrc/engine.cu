@@ -40,9 +40,11 @@ class SpanEngine final : public Engine {
     void* in = nullptr;
     void* out = nullptr;
     int batch = 0;
-    KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 1, 2, &in, &out, &batch));
+    KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 1, 2, &in, &out, &batch,
+                     net_.output_format() != 0 ? net_.display_bytes() : 0));
     return net_.run(stream, in, out, batch);
   }
+  Status set_output_format(int format) override { return net_.set_output_format(format); }
   Status calibrate(cudaStream_t stream, const kb2_tensor& frames, float* peaks, int n_peaks) override {
     if (n_peaks != kSpanScales) return refuse(KB2_INPUT_MISMATCH, "SPAN calibration returns 19 peaks");
     if (frames.type != KB2_F16 || frames.dims[1] != 3 || frames.dims[2] != height() || frames.dims[3] != width() ||
@@ -106,7 +108,7 @@ class IfnetEngine final : public Engine {
     return net_.create(params, d.max_batch, d.height, d.width);
   }
   std::vector<std::string> input_names() const override { return {"img0", "img1"}; }
-  std::vector<std::string> output_names() const override { return {"output"}; }
+  std::vector<std::string> output_names() const override { return {"output"}; }  // motion: {"flow", "mask"}
   int max_batch() const override { return net_.max_batch(); }
   int height() const override { return net_.height(); }
   int width() const override { return net_.width(); }
@@ -114,11 +116,26 @@ class IfnetEngine final : public Engine {
   Status enqueue(cudaStream_t stream, const kb2_tensor* inputs, int n_inputs, const kb2_tensor* outputs,
                  int n_outputs) override {
     void* in[2] = {nullptr, nullptr};
-    void* out = nullptr;
     int batch = 0;
+    if (n_outputs == 2) {  // the motion variant: flow and mask (upscale_motion.cpp:71-84)
+      void *flow = nullptr, *mask = nullptr;
+      bool f16 = false;
+      KB2_TRY(motion_io(inputs, n_inputs, outputs, n_outputs, net_.plane_height(), net_.plane_width(), in, &flow,
+                        &mask, &f16, &batch));
+      if (inputs[1].dims[0] != inputs[0].dims[0]) return refuse(KB2_INPUT_MISMATCH, "IFNet: frame counts differ");
+      return net_.run_motion(stream, in[0], in[1], flow, mask, f16, batch);
+    }
+    void* out = nullptr;
     KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 2, 1, in, &out, &batch));
     if (inputs[1].dims[0] != inputs[0].dims[0]) return refuse(KB2_INPUT_MISMATCH, "IFNet: frame counts differ");
     return net_.run(stream, in[0], in[1], out, batch);
+  }
+  Status geometry(int32_t* ph, int32_t* pw, int32_t* x, int32_t* y) const override {
+    *ph = net_.plane_height();
+    *pw = net_.plane_width();
+    *x = net_.window_x();
+    *y = net_.window_y();
+    return Status::Ok();
   }
   Status set_timestep(float t) override { return net_.set_timestep(t); }
   Status set_profiling(bool on) override {

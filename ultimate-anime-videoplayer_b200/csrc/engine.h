@@ -30,18 +30,29 @@ class Engine {
     return refuse(KB2_FORMAT_UNSUPPORTED, "this engine does not calibrate");
   }
   Status check_device(cudaStream_t stream, int32_t* code);
+  // kb2_set_output_format: 0 = F16 frames, else a kb2_display_format (SPAN x2 only)
+  virtual Status set_output_format(int) { return refuse(KB2_FORMAT_UNSUPPORTED, "this engine writes F16 frames only"); }
   virtual Status set_profiling(bool) { return refuse(KB2_FORMAT_UNSUPPORTED, "no profiling"); }
   virtual Status read_profile(kb2_layer_profile*, int, int* count) {
     *count = 0;
     return refuse(KB2_FORMAT_UNSUPPORTED, "no profiling");
   }
   virtual int launches_per_enqueue() const = 0;
+  // IFNet: the padded plane of the motion outputs and the frame's window in it (kb2_rife_geometry)
+  virtual Status geometry(int32_t*, int32_t*, int32_t*, int32_t*) const {
+    return refuse(KB2_FORMAT_UNSUPPORTED, "this engine has no motion plane");
+  }
 
  protected:
   // Validates the frame tensors of an enqueue: n_frames_in inputs F16 [n,3,H,W], one output
-  // F16 [n,3,H*out_scale,W*out_scale], n <= max_batch, 16-byte aligned.
+  // F16 [n,3,H*out_scale,W*out_scale] (display_bytes > 0: display pixels, U8
+  // [n,display_bytes,H*out_scale,W*out_scale]), n <= max_batch, 16-byte aligned.
   Status frame_io(const kb2_tensor* inputs, int n_in, const kb2_tensor* outputs, int n_out, int n_frames_in,
-                  int out_scale, void** in_ptrs, void** out_ptr, int* batch) const;
+                  int out_scale, void** in_ptrs, void** out_ptr, int* batch, int display_bytes = 0) const;
+  // Validates the IFNet motion variant's tensors: two F16 frames [n,3,H,W] in; out flow [n,4,ph,pw]
+  // and mask [n,1,ph,pw], both F32 or both F16 (*f16).
+  Status motion_io(const kb2_tensor* inputs, int n_in, const kb2_tensor* outputs, int n_out, int ph, int pw,
+                   void** in_ptrs, void** flow, void** mask, bool* f16, int* batch) const;
   virtual int* err_word() const = 0;
 };
 

@@ -392,6 +392,44 @@ __global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, i
   }
 }
 
+// The motion variant's outputs in place of the blend (the reference's motion finish,
+// src/gpu/cuda/backend/rife_finish.cuh:40-55, called from fused_finish, rife_fused_kernels.cu:208):
+// over the whole padded plane, the final flow (FP32 planes of blocks 0-2 plus block 3's part, in
+// the network's order) into flow [n][4][Hp][Wp] and sigmoid(mask), the weight of frame A, into
+// mask [n][1][Hp][Wp]; T = float, or __half as the reference's engine writes them. One thread per
+// column walking kGlueRunRows rows, with block 3's flow resize cached along the column; each plane
+// row is one coalesced run of stores.
+__device__ __forceinline__ void store_motion(float* p, float v) { *p = v; }
+__device__ __forceinline__ void store_motion(__half* p, float v) { *p = __float2half_rn(v); }
+
+template <typename T>
+__global__ void ifnet_motion_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, T* __restrict__ flow,
+                                    T* __restrict__ mask) {
+  const int X = blockIdx.x * blockDim.x + threadIdx.x;
+  if (X >= F.Wp) return;
+  LevelCol col;
+  level_col_init(L, kIfBlocks - 1, X, col);
+  const int runs = (F.Hp + kGlueRunRows - 1) / kGlueRunRows;
+  const size_t pl = FF.plane();
+  for (int r = blockIdx.y; r < batch * runs; r += gridDim.y) {
+    const int n = r / runs;
+    const int y0 = (r - n * runs) * kGlueRunRows;
+    col.lo = -1;
+    for (int Y = y0; Y < y0 + kGlueRunRows && Y < F.Hp; ++Y) {
+      const float* p = FF.pixel(n, Y, X);
+      float f[4], m;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) f[c] = __ldg(p + c * pl);
+      m = __ldg(p + 4 * pl);
+      flow_step_col(L, kIfBlocks - 1, n, Y, col, f, &m);
+      const size_t at = static_cast<size_t>(Y) * F.Wp + X;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) store_motion(flow + (static_cast<size_t>(n) * 4 + c) * pl + at, f[c]);
+      store_motion(mask + static_cast<size_t>(n) * pl + at, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-m))));
+    }
+  }
+}
+
 // Warp taps of a flow field [n][2][h][w] (FP32): x0, x1, y0, y1 as int32 planes [n][4][h][w] and
 // the weights wx, wy as FP32 planes [n][2][h][w] (kb2_warp_taps).
 __global__ void warp_taps_kernel(const float* __restrict__ flow, int batch, int h, int w, int32_t* __restrict__ taps,

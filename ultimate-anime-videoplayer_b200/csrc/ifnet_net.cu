@@ -287,6 +287,7 @@ Status IfnetNet::create(const std::vector<float>& params, int max_batch, int H, 
   const int k_c0a = timer_.kind("ifnet.conv0a"), k_c0b = timer_.kind("ifnet.conv0b");
   const int k_res = timer_.kind("ifnet.res"), k_ct = timer_.kind("ifnet.convt");
   k_blend_ = timer_.kind("ifnet.blend");
+  k_motion_ = timer_.kind("ifnet.motion");
   KB2_TRY(flow_full_.alloc(static_cast<size_t>(max_batch_) * 5 * Hp_ * Wp_ * sizeof(float)));
   KB2_CUDA(cudaMemset(flow_full_.ptr, 0, flow_full_.bytes));
   KB2_TRY(pad_.alloc(static_cast<size_t>(max_batch_) * 2 * Hp_ * Wp_ * sizeof(uint2)));
@@ -409,6 +410,15 @@ size_t IfnetNet::device_bytes() const {
 }
 
 Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, void* out, int batch) {
+  return run_impl(stream, img0, img1, Finish{out, nullptr, nullptr, false}, batch);
+}
+
+Status IfnetNet::run_motion(cudaStream_t stream, const void* img0, const void* img1, void* flow, void* mask, bool f16,
+                            int batch) {
+  return run_impl(stream, img0, img1, Finish{nullptr, flow, mask, f16}, batch);
+}
+
+Status IfnetNet::run_impl(cudaStream_t stream, const void* img0, const void* img1, const Finish& finish, int batch) {
   if (batch < 1 || batch > max_batch_) return refuse(KB2_SHAPE_INVALID, "IFNet: batch out of contract");
   uint2* pad0 = pad_.as<uint2>();
   IfFrames F{static_cast<const __half*>(img0), static_cast<const __half*>(img1), H_, W_, Hp_, Wp_, top_, left_, pad0,
@@ -462,10 +472,25 @@ Status IfnetNet::run(cudaStream_t stream, const void* img0, const void* img1, vo
       KB2_TRY(timer_.end(l.kind, l.flops_px * opx, l.bytes_px * opx, stream));
     }
   }
+  if (finish.image == nullptr) {
+    // motion: read the FP32 flow field (20 B/px), write 4 flow planes and the mask
+    const long long px = static_cast<long long>(batch) * Hp_ * Wp_;
+    const dim3 g = row_grid(Wp_, batch * ((Hp_ + kGlueRunRows - 1) / kGlueRunRows));
+    KB2_TRY(timer_.begin(stream));
+    if (finish.f16)
+      ifnet_motion_kernel<__half><<<g, kGlueThreads, 0, stream>>>(F, L, FF, batch, static_cast<__half*>(finish.flow),
+                                                                   static_cast<__half*>(finish.mask));
+    else
+      ifnet_motion_kernel<float><<<g, kGlueThreads, 0, stream>>>(F, L, FF, batch, static_cast<float*>(finish.flow),
+                                                                  static_cast<float*>(finish.mask));
+    KB2_CUDA(cudaGetLastError());
+    KB2_TRY(timer_.end(k_motion_, 0.0, px * (20.0 + 5.0 * (finish.f16 ? 2.0 : 4.0)), stream));
+    return Status::Ok();
+  }
   const long long px = static_cast<long long>(batch) * H_ * W_;
   KB2_TRY(timer_.begin(stream));
   ifnet_blend_kernel<<<row_grid(W_, batch * ((H_ + kGlueRunRows - 1) / kGlueRunRows)), kGlueThreads, 0, stream>>>(
-      F, L, FF, batch, static_cast<__half*>(out));
+      F, L, FF, batch, static_cast<__half*>(finish.image));
   KB2_CUDA(cudaGetLastError());
   KB2_TRY(timer_.end(k_blend_, 0.0, px * (20.0 + 12.0 + 6.0), stream));
   return Status::Ok();

@@ -24,6 +24,15 @@ class IfnetNet {
   Status create(const std::vector<float>& params, int max_batch, int H, int W);
   // img0 / img1: NCHW F16 [batch][3][H][W]; out: NCHW F16 [batch][3][H][W] (device pointers).
   Status run(cudaStream_t stream, const void* img0, const void* img1, void* out, int batch);
+  // The motion variant: the same network with the final flow [batch][4][Hp][Wp] and sigmoid(mask)
+  // [batch][1][Hp][Wp] over the padded plane (FP32, or FP16 when `f16`) in place of the frame.
+  Status run_motion(cudaStream_t stream, const void* img0, const void* img1, void* flow, void* mask, bool f16,
+                    int batch);
+  // The padded plane and the frame's window in it (the reference's rife_geometry).
+  int plane_height() const { return Hp_; }
+  int plane_width() const { return Wp_; }
+  int window_x() const { return left_; }
+  int window_y() const { return top_; }
   Status set_timestep(float t);
   size_t device_bytes() const;
   int* err_word() const { return err_.as<int>(); }
@@ -40,6 +49,14 @@ class IfnetNet {
     DeviceBuffer buf;
   };
   Status tensor(std::unique_ptr<Tensor>& t, int H, int W, int chunks);
+  // What the last kernel writes: the blended frame (image), or the motion (flow and mask).
+  struct Finish {
+    void* image;
+    void* flow;
+    void* mask;
+    bool f16;
+  };
+  Status run_impl(cudaStream_t stream, const void* img0, const void* img1, const Finish& finish, int batch);
 
   int max_batch_ = 0, H_ = 0, W_ = 0, Hp_ = 0, Wp_ = 0, top_ = 0, left_ = 0;
   float timestep_ = 0.5f;
@@ -51,7 +68,7 @@ class IfnetNet {
   DeviceBuffer flow_full_;                        // flow / mask after blocks 0-2, FP32 [n][5][Hp][Wp]
   DeviceBuffer pad_;                              // both frames, padded RGBx FP16 pixels [2][n][Hp][Wp]
   LayerTimer timer_;
-  int k_glue_[4] = {}, k_blend_ = 0, k_pad_ = 0;
+  int k_glue_[4] = {}, k_blend_ = 0, k_pad_ = 0, k_motion_ = 0;
 };
 
 // Bilinear backward-warp taps of a flow field [n][2][h][w] (FP32, device): x0, x1, y0, y1 as int32

@@ -238,7 +238,22 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
     s.n_real = 12;
     s.n_pad = 16;
     KB2_TRY(add(s, wup, bup, nullptr, {cat}, Step{nullptr, nullptr, nullptr, nullptr, 1.0f, 1.0f, -1}));
+    // the same layer writing display pixels (set_output_format)
+    s.out = kOutPixShuf2Display;
+    layers_.push_back(std::make_unique<ConvLayer>());
+    up_display_ = layers_.back().get();
+    const ChunkedTensor* in_cat[1] = {cat};
+    KB2_TRY(up_display_->build(s, wup, bup, nullptr, nullptr, in_cat, err));
+    k_display_ = kind_index("span.upsampler.display");
   }
+  return Status::Ok();
+}
+
+Status SpanNet::set_output_format(int format) {
+  if (format != 0 && format != KB2_DISPLAY_RGBA16 && format != KB2_DISPLAY_RGB10A2 &&
+      format != KB2_DISPLAY_RGB10A2_DITHER)
+    return refuse(KB2_FORMAT_UNSUPPORTED, "SPAN: unknown output format");
+  out_format_ = format;
   return Status::Ok();
 }
 
@@ -267,11 +282,19 @@ Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, b
   unsigned int* peaks = peaks_dst != nullptr ? peaks_dst : peaks_.as<unsigned int>();
   for (const Step& s : steps_) {
     void* dst = s.out != nullptr ? static_cast<void*>(s.out->ptr) : out;
-    if (profiling_) KB2_TRY(timed(s.kind, 0.0, 0.0, stream, true));
-    KB2_TRY(s.layer->launch(stream, batch, dst, s.residual != nullptr ? s.residual->ptr : nullptr, s.out_inv_scale,
-                            s.res_scale, s.out2 != nullptr ? s.out2->ptr : nullptr,
-                            s.residual != nullptr ? s.residual->chunks : 0));
-    if (profiling_) KB2_TRY(timed(s.kind, s.flops_px * pixels, s.bytes_px * pixels, stream, false));
+    // the frame-writing layer: NCHW F16, or display pixels from the same layer's display twin
+    // (calibration passes, which capture peaks, always write F16 frames into their scratch)
+    const bool display = s.out == nullptr && out_format_ != 0 && !capture_peaks;
+    const ConvLayer* layer = display ? up_display_ : s.layer;
+    const int kind = display ? k_display_ : s.kind;
+    double bytes_px = s.bytes_px;
+    if (display) bytes_px += 4.0 * display_bytes() - s.layer->spec.n_real * 2.0;  // 4 pixels instead of 12 halves
+    if (profiling_) KB2_TRY(timed(kind, 0.0, 0.0, stream, true));
+    KB2_TRY(layer->launch(stream, batch, dst, s.residual != nullptr ? s.residual->ptr : nullptr, s.out_inv_scale,
+                          s.res_scale, s.out2 != nullptr ? s.out2->ptr : nullptr,
+                          s.residual != nullptr ? s.residual->chunks : 0, nullptr,
+                          display ? 2LL * W_ * display_bytes() : 0LL, out_format_));
+    if (profiling_) KB2_TRY(timed(kind, s.flops_px * pixels, bytes_px * pixels, stream, false));
     if (capture_peaks && s.peak >= 0) {
       const size_t n2 = static_cast<size_t>(batch) * H_ * s.out->chunks * W_ * 4;  // 4 half2 per chunk
       absmax_f16_kernel<<<4 * num_sms(), 256, 0, stream>>>(reinterpret_cast<const __half2*>(s.out->ptr), n2,

@@ -22,6 +22,11 @@ class SpanNet {
   Status run(cudaStream_t stream, const void* in, void* out, int batch, bool capture_peaks = false,
              unsigned int* peaks_dst = nullptr);
   Status calibrate(cudaStream_t stream, const void* frames, int n, float* peaks_out);
+  // 0: run() writes NCHW F16 frames; a kb2_display_format: packed display pixels from the
+  // upsampler's epilogue, rows of 2W pixels (display_bytes() each) at out + row * 2W * bytes.
+  Status set_output_format(int format);
+  int output_format() const { return out_format_; }
+  int display_bytes() const { return out_format_ == KB2_DISPLAY_RGBA16 ? 8 : 4; }
   // calibrate() with the caller's device scratch in place of its per-call allocation: the peak
   // words at the start of `scratch`, the discarded x2 frames after them (kb2_span_calibrate_static).
   Status calibrate_in(cudaStream_t stream, const void* frames, int n, float* peaks_out, uint8_t* scratch,
@@ -74,6 +79,9 @@ class SpanNet {
   std::vector<std::unique_ptr<ConvLayer>> layers_;
   std::vector<Step> steps_;
   const ChunkedTensor* img_ = nullptr;
+  ConvLayer* up_display_ = nullptr;  // the upsampler with the display epilogue (same weights)
+  int k_display_ = 0;
+  int out_format_ = 0;
   bool profiling_ = false;
   std::vector<Profile> kinds_;
   struct Pending {

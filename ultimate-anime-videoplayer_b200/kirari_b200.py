@@ -40,7 +40,7 @@ EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
            "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max",
-           "kb2_warp_blend_poses", "kb2_pack_display")
+           "kb2_warp_blend_poses", "kb2_pack_display", "kb2_rife_geometry", "kb2_set_output_format")
 
 
 class KB2Error(RuntimeError):
@@ -116,6 +116,8 @@ def lib():
         L.kb2_read_profile.argtypes = [ctypes.c_void_p, ctypes.POINTER(LayerProfile), ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_int32)]
         L.kb2_launches_per_enqueue.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
+        L.kb2_rife_geometry.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int32)] * 4
+        L.kb2_set_output_format.argtypes = [ctypes.c_void_p, ctypes.c_int32]
         _lib = L
     return _lib
 
@@ -179,6 +181,28 @@ class Engine:
     def enqueue_raw(self, ins, outs, stream_handle):
         """Pre-built kb2_tensor arrays (no per-call marshalling), for timing loops."""
         self._check(lib().kb2_enqueue(self.h, stream_handle, ins, len(ins), outs, len(outs)))
+
+    def set_output_format(self, fmt):
+        """SPAN x2: 0 = F16 frames, or a DISPLAY_* format (outputs U8 [n, 8 or 4, 2H, 2W], packed pixels)."""
+        self._check(lib().kb2_set_output_format(self.h, int(fmt)))
+
+    def rife_geometry(self):
+        """IFNet: (plane_h, plane_w, window_x, window_y) of the motion outputs."""
+        v = [ctypes.c_int32(0) for _ in range(4)]
+        self._check(lib().kb2_rife_geometry(self.h, *[ctypes.byref(x) for x in v]))
+        return tuple(x.value for x in v)
+
+    def motion(self, a, b, dtype=None, stream=None):
+        """IFNet motion variant on torch device frames a, b F16 [n,3,H,W]: returns (flow [n,4,Hp,Wp],
+        mask [n,1,Hp,Wp], window (x, y, W, H)) as torch tensors of `dtype` (float32 by default)."""
+        import torch
+        dtype = dtype or torch.float32
+        ph, pw, x, y = self.rife_geometry()
+        n = int(a.shape[0])
+        flow = torch.full((n, 4, ph, pw), float("nan"), dtype=dtype, device=a.device)
+        mask = torch.full((n, 1, ph, pw), float("nan"), dtype=dtype, device=a.device)
+        self.enqueue([a, b], [flow, mask], stream)
+        return flow, mask, (x, y, self.width, self.height)
 
     def set_timestep(self, t):
         self._check(lib().kb2_set_timestep(self.h, float(t)))
