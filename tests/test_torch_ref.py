@@ -32,3 +32,20 @@ def test_torch_span_reference_matches_config0_golden():
     ref = g["out"].astype(np.float32)
     # the fixture's FP16 rounding: half an FP16 ulp of the value
     assert float(np.max(np.abs(got - ref) - np.abs(ref) * 2.0 ** -11)) < 1e-4
+
+
+def test_torch_ifnet_reference_matches_the_oracle():
+    from synth import shifted_pair
+    p = nets.ifnet_init(2)
+    a, b = shifted_pair(64, 96, seed=8)
+    got, flow, mask = torch_ref.ifnet_forward(a[None], b[None], 0.3, p, device="cpu", return_flow=True)
+    ref, rflow, rmask = nets.ifnet_forward(a[None], b[None], 0.3, p, return_flow=True)
+    assert float(np.max(np.abs(got - ref))) < 1e-4
+    assert float(np.max(np.abs(flow - rflow))) < 1e-3
+    assert float(np.max(np.abs(mask - rmask))) < 1e-4
+
+
+def test_torch_ifnet_reference_matches_reference_golden():
+    g = golden("ifnet_64x96_t05.npz")
+    got = torch_ref.ifnet_forward(g["a"], g["b"], float(g["t"]), nets.ifnet_init(2), device="cpu")
+    assert float(np.max(np.abs(got - g["out"]))) < 1e-4
