@@ -147,6 +147,18 @@ int kb2_enqueue(kb2_engine* engine, void* stream, const kb2_tensor* inputs, int3
  * KB2_FORMAT_UNSUPPORTED for other engines. */
 int kb2_set_output_format(kb2_engine* engine, int32_t format);
 
+/* SPAN x2: process every frame of the following enqueues as `tiles` row tiles (configs[2] of the
+ * contract: 8 tiles with an 8-pixel halo), the way a player that runs SPAN on bands of rows does.
+ * Tile t owns the core rows [t * C, min(H, (t + 1) * C)), C = ceil(H / tiles), and is computed from
+ * C + 2 * halo input rows around them (the window moved inside the frame at its top and bottom),
+ * as one frame of zero-padded SPAN; the tiles' core output rows are stitched into outputs[0]. The
+ * network's receptive radius is 20 input rows (conv_1, three 3x3 convs a block, the upsampler), so
+ * a halo of 20 or more gives the whole-frame result (up to the order of FP32 sums), a smaller one
+ * changes the rows near the seams (the reference's exact_side, src/gpu/span_fp8/forward.cpp:169,
+ * states the same bound). tiles <= 1: whole frames (the default). Builds a second network of the
+ * tile's height (device memory); 1 <= tiles <= H / 2, 0 <= halo <= 64, else KB2_SHAPE_INVALID. */
+int kb2_set_row_tiles(kb2_engine* engine, int32_t tiles, int32_t halo);
+
 /* IFNet: the padded plane the network runs on (multiples of 32) and the frame's window in it, as the
  * reference's rife_geometry (src/kernels/spec/rife.h:47-63; left / top = half the padding, rounded
  * down to even): the motion outputs are plane_h x plane_w, the frame at (window_x, window_y). */

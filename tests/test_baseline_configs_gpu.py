@@ -143,7 +143,7 @@ def test_config3_ifnet_full_width(h, w):
     from synth import shifted_pair
     p = nets.ifnet_init(2)
     fa, fb = shifted_pair(h, w, seed=31)
-    a, b = f16(fa[None]), f16(fb[None])
+    a, b = np.ascontiguousarray(f16(fa[None])), np.ascontiguousarray(f16(fb[None]))
     eng = kb.Engine(kb.MODEL_IFNET, kb.make_blob(kb.MODEL_IFNET, nets.ifnet_flat(p)), h, w, max_batch=1)
     try:
         eng.set_timestep(0.5)

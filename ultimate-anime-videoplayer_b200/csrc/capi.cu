@@ -153,6 +153,15 @@ int kb2_set_output_format(kb2_engine* engine, int32_t format) {
   }
 }
 
+int kb2_set_row_tiles(kb2_engine* engine, int32_t tiles, int32_t halo) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    return set_error(engine, engine->impl->set_row_tiles(tiles, halo));
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
 int kb2_set_timestep(kb2_engine* engine, float timestep) {
   if (engine == nullptr) return KB2_INVALID_ARGUMENT;
   return set_error(engine, engine->impl->set_timestep(timestep));

@@ -1,5 +1,6 @@
 // Engine implementations: SPAN x2 (FP16 / FP8), IFNet, the unshuffle SPAN of a .span8 package, and
 // the factory.
+#include <algorithm>
 #include <cstring>
 
 #include "engine.h"
@@ -27,7 +28,42 @@ namespace {
 class SpanEngine final : public Engine {
  public:
   Status init(const kb2_engine_desc& d, const std::vector<float>& params) {
+    params_ = params;
+    precision_ = d.precision;
+    if (d.act_scales != nullptr && d.act_scale_count > 0)
+      scales_.assign(d.act_scales, d.act_scales + d.act_scale_count);
     return net_.create(params, d.precision, d.max_batch, d.height, d.width, d.act_scales, d.act_scale_count);
+  }
+  // kb2_set_row_tiles: every frame of the following enqueues runs as `tiles` row tiles, each read
+  // with `halo` rows of context above and below (fewer at the frame's top and bottom, where the
+  // window stays inside the frame), on a second network of the tile's height; the tiles' core rows
+  // are stitched into the output. tiles = 1 (or 0): whole frames.
+  Status set_row_tiles(int tiles, int halo) override {
+    const int H = net_.height();
+    if (tiles < 0 || halo < 0 || halo > 64 || tiles > H / 2)
+      return refuse(KB2_SHAPE_INVALID, "row tiles: 1 <= tiles <= H / 2 and 0 <= halo <= 64");
+    tile_net_.reset();
+    tile_in_.reset();
+    tiles_ = tiles <= 1 ? 0 : tiles;
+    halo_ = halo;
+    if (tiles_ == 0) return Status::Ok();
+    core_ = (H + tiles_ - 1) / tiles_;
+    tile_h_ = std::min(H, core_ + 2 * halo_);
+    auto net = std::make_unique<SpanNet>();
+    KB2_TRY(net->create(params_, precision_, net_.max_batch() * tiles_, tile_h_, net_.width(),
+                        scales_.empty() ? nullptr : scales_.data(), static_cast<int>(scales_.size()),
+                        net_.err_word()));
+    KB2_TRY(net->set_output_format(net_.output_format()));
+    net->set_profiling(profiling_);
+    auto in = std::make_unique<DeviceBuffer>();
+    KB2_TRY(in->alloc(static_cast<size_t>(net_.max_batch()) * tiles_ * 3 * tile_h_ * net_.width() * 2));
+    tile_out_bytes_ = static_cast<size_t>(net_.max_batch()) * tiles_ * 4 * tile_h_ * net_.width() * 8;
+    auto out = std::make_unique<DeviceBuffer>();
+    KB2_TRY(out->alloc(tile_out_bytes_));  // room for F16 frames (6 B / px) or RGBA16 pixels (8 B / px)
+    tile_net_ = std::move(net);
+    tile_in_ = std::move(in);
+    tile_out_ = std::move(out);
+    return Status::Ok();
   }
   std::vector<std::string> input_names() const override { return {"input"}; }
   std::vector<std::string> output_names() const override { return {"output"}; }
@@ -42,9 +78,14 @@ class SpanEngine final : public Engine {
     int batch = 0;
     KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 1, 2, &in, &out, &batch,
                      net_.output_format() != 0 ? net_.display_bytes() : 0));
+    if (tiles_ > 0) return run_tiled(stream, in, out, batch);
     return net_.run(stream, in, out, batch);
   }
-  Status set_output_format(int format) override { return net_.set_output_format(format); }
+  Status set_output_format(int format) override {
+    KB2_TRY(net_.set_output_format(format));
+    if (tile_net_ != nullptr) KB2_TRY(tile_net_->set_output_format(format));
+    return Status::Ok();
+  }
   Status calibrate(cudaStream_t stream, const kb2_tensor& frames, float* peaks, int n_peaks) override {
     if (n_peaks != kSpanScales) return refuse(KB2_INPUT_MISMATCH, "SPAN calibration returns 19 peaks");
     if (frames.type != KB2_F16 || frames.dims[1] != 3 || frames.dims[2] != height() || frames.dims[3] != width() ||
@@ -74,12 +115,14 @@ class SpanEngine final : public Engine {
                              static_cast<uint8_t*>(scratch), kStaticScratchBytes);
   }
   Status set_profiling(bool on) override {
+    profiling_ = on;
     net_.set_profiling(on);
+    if (tile_net_ != nullptr) tile_net_->set_profiling(on);
     return Status::Ok();
   }
   Status read_profile(kb2_layer_profile* records, int capacity, int* count) override {
     std::vector<SpanNet::Profile> kinds;
-    KB2_TRY(net_.read_profile(kinds));
+    KB2_TRY((tile_net_ != nullptr ? *tile_net_ : net_).read_profile(kinds));
     *count = static_cast<int>(kinds.size());
     for (int i = 0; i < *count && i < capacity; ++i) {
       kb2_layer_profile& r = records[i];
@@ -92,13 +135,58 @@ class SpanEngine final : public Engine {
     }
     return Status::Ok();
   }
-  int launches_per_enqueue() const override { return net_.launches_per_run(); }
+  int launches_per_enqueue() const override {
+    return tile_net_ != nullptr ? tile_net_->launches_per_run() : net_.launches_per_run();
+  }
 
  protected:
-  int* err_word() const override { return net_.err_word(); }
+  int* err_word() const override { return net_.err_word(); }  // the tile network reports into it too
 
  private:
+  // Tile t of a frame: core rows [t * core, min(H, (t + 1) * core)), read from the window of tile_h
+  // rows starting at core start - halo, moved inside the frame at its top and bottom.
+  int tile_window(int t) const { return std::clamp(t * core_ - halo_, 0, net_.height() - tile_h_); }
+
+  Status run_tiled(cudaStream_t stream, const void* in, void* out, int batch) {
+    const int H = net_.height(), W = net_.width();
+    const size_t plane = static_cast<size_t>(H) * W * 2;          // one input channel, bytes
+    const size_t tile_plane = static_cast<size_t>(tile_h_) * W * 2;
+    // cut: frame f, tile t -> tile frame f * tiles + t (3 channels of tile_h contiguous rows each)
+    for (int f = 0; f < batch; ++f)
+      for (int t = 0; t < tiles_; ++t) {
+        const uint8_t* src = static_cast<const uint8_t*>(in) + f * 3 * plane + static_cast<size_t>(tile_window(t)) * W * 2;
+        uint8_t* dst = tile_in_->as<uint8_t>() + (static_cast<size_t>(f) * tiles_ + t) * 3 * tile_plane;
+        KB2_CUDA(cudaMemcpy2DAsync(dst, tile_plane, src, plane, tile_plane, 3, cudaMemcpyDeviceToDevice, stream));
+      }
+    KB2_TRY(tile_net_->run(stream, tile_in_->ptr, tile_out_->ptr, batch * tiles_));
+    // stitch the core rows: F16 frames plane by plane, display pixels row by row
+    const bool display = net_.output_format() != 0;
+    const size_t row_bytes = display ? static_cast<size_t>(2 * W) * net_.display_bytes() : static_cast<size_t>(2 * W) * 2;
+    const int planes = display ? 1 : 3;
+    const size_t out_plane = row_bytes * 2 * H, tile_out_plane = row_bytes * 2 * tile_h_;
+    for (int f = 0; f < batch; ++f)
+      for (int t = 0; t < tiles_; ++t) {
+        const int c0 = t * core_, c1 = std::min(H, c0 + core_);
+        if (c1 <= c0) continue;
+        const int ys = tile_window(t);
+        const uint8_t* src = tile_out_->as<uint8_t>() + (static_cast<size_t>(f) * tiles_ + t) * planes * tile_out_plane +
+                             static_cast<size_t>(2 * (c0 - ys)) * row_bytes;
+        uint8_t* dst = static_cast<uint8_t*>(out) + static_cast<size_t>(f) * planes * out_plane +
+                       static_cast<size_t>(2 * c0) * row_bytes;
+        KB2_CUDA(cudaMemcpy2DAsync(dst, out_plane, src, tile_out_plane, static_cast<size_t>(2 * (c1 - c0)) * row_bytes,
+                                   planes, cudaMemcpyDeviceToDevice, stream));
+      }
+    return Status::Ok();
+  }
+
   SpanNet net_;
+  std::vector<float> params_, scales_;
+  int precision_ = KB2_PREC_FP16;
+  bool profiling_ = false;
+  int tiles_ = 0, halo_ = 0, core_ = 0, tile_h_ = 0;
+  size_t tile_out_bytes_ = 0;
+  std::unique_ptr<SpanNet> tile_net_;
+  std::unique_ptr<DeviceBuffer> tile_in_, tile_out_;
 };
 
 class IfnetEngine final : public Engine {

@@ -30,6 +30,8 @@ class Engine {
     return refuse(KB2_FORMAT_UNSUPPORTED, "this engine does not calibrate");
   }
   Status check_device(cudaStream_t stream, int32_t* code);
+  // kb2_set_row_tiles (SPAN x2 only)
+  virtual Status set_row_tiles(int, int) { return refuse(KB2_FORMAT_UNSUPPORTED, "this engine runs whole frames"); }
   // kb2_set_output_format: 0 = F16 frames, else a kb2_display_format (SPAN x2 only)
   virtual Status set_output_format(int) { return refuse(KB2_FORMAT_UNSUPPORTED, "this engine writes F16 frames only"); }
   virtual Status set_profiling(bool) { return refuse(KB2_FORMAT_UNSUPPORTED, "no profiling"); }

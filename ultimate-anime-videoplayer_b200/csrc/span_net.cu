@@ -77,7 +77,7 @@ Status SpanNet::make_tensor(std::unique_ptr<Tensor>& t, int chunks, bool fp8) {
 }
 
 Status SpanNet::create(const std::vector<float>& params, int precision, int max_batch, int H, int W,
-                       const float* act_scales, int n_scales) {
+                       const float* act_scales, int n_scales, int* shared_err) {
   if (params.size() != kSpanParams) return refuse(KB2_WEIGHTS_INVALID, "SPAN: parameter count mismatch");
   if (max_batch < 1 || H < 1 || W < 1 || H > 8192 || W > 8192)
     return refuse(KB2_SHAPE_INVALID, "SPAN: frame size out of contract");
@@ -96,8 +96,13 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
   max_batch_ = max_batch;
   H_ = H;
   W_ = W;
-  KB2_TRY(err_.alloc(sizeof(int)));
-  KB2_CUDA(cudaMemset(err_.ptr, 0, sizeof(int)));
+  if (shared_err != nullptr) {
+    err_ptr_ = shared_err;
+  } else {
+    KB2_TRY(err_.alloc(sizeof(int)));
+    KB2_CUDA(cudaMemset(err_.ptr, 0, sizeof(int)));
+    err_ptr_ = err_.as<int>();
+  }
   KB2_TRY(peaks_.alloc(kSpanScales * sizeof(unsigned int)));
 
   auto tensor = [&](int chunks, bool fp8, const ChunkedTensor** out) -> Status {
@@ -140,7 +145,7 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
   const float* wup = bcat + c;
   const float* bup = wup + 12 * c * 9;
 
-  int* err = err_.as<int>();
+  int* err = err_ptr_;
   auto add = [&](const ConvSpec& s, const float* w, const float* b, const float* in_scales,
                  std::vector<const ChunkedTensor*> inputs, Step step) -> Status {
     layers_.push_back(std::make_unique<ConvLayer>());

@@ -15,8 +15,9 @@ constexpr int kSpanBlocks = 6;
 
 class SpanNet {
  public:
+  // shared_err: another network's device error word to report into (null: its own).
   Status create(const std::vector<float>& params, int precision, int max_batch, int H, int W,
-                const float* act_scales, int n_scales);
+                const float* act_scales, int n_scales, int* shared_err = nullptr);
   // in: NCHW F16 [batch][3][H][W]; out: NCHW F16 [batch][3][2H][2W] (device pointers).
   // peaks_dst: where capture_peaks collects the 19 peak words (null: the engine's own words).
   Status run(cudaStream_t stream, const void* in, void* out, int batch, bool capture_peaks = false,
@@ -32,7 +33,7 @@ class SpanNet {
   Status calibrate_in(cudaStream_t stream, const void* frames, int n, float* peaks_out, uint8_t* scratch,
                       size_t scratch_bytes);
   size_t device_bytes() const;
-  int* err_word() const { return err_.as<int>(); }
+  int* err_word() const { return err_ptr_; }
   int height() const { return H_; }
   int width() const { return W_; }
   int max_batch() const { return max_batch_; }
@@ -75,6 +76,7 @@ class SpanNet {
   int max_batch_ = 0, H_ = 0, W_ = 0;
   std::vector<float> scales_;
   DeviceBuffer err_, peaks_;
+  int* err_ptr_ = nullptr;
   std::vector<std::unique_ptr<Tensor>> tensors_;
   std::vector<std::unique_ptr<ConvLayer>> layers_;
   std::vector<Step> steps_;

@@ -40,7 +40,8 @@ EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "
            "kb2_workspace_bytes", "kb2_enqueue", "kb2_set_timestep", "kb2_check_device", "kb2_span_calibrate",
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
            "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max",
-           "kb2_warp_blend_poses", "kb2_pack_display", "kb2_rife_geometry", "kb2_set_output_format")
+           "kb2_warp_blend_poses", "kb2_pack_display", "kb2_rife_geometry", "kb2_set_output_format",
+           "kb2_set_row_tiles")
 
 
 class KB2Error(RuntimeError):
@@ -118,6 +119,7 @@ def lib():
         L.kb2_launches_per_enqueue.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
         L.kb2_rife_geometry.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int32)] * 4
         L.kb2_set_output_format.argtypes = [ctypes.c_void_p, ctypes.c_int32]
+        L.kb2_set_row_tiles.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32]
         _lib = L
     return _lib
 
@@ -185,6 +187,10 @@ class Engine:
     def set_output_format(self, fmt):
         """SPAN x2: 0 = F16 frames, or a DISPLAY_* format (outputs U8 [n, 8 or 4, 2H, 2W], packed pixels)."""
         self._check(lib().kb2_set_output_format(self.h, int(fmt)))
+
+    def set_row_tiles(self, tiles, halo):
+        """SPAN x2: run frames as `tiles` row tiles with `halo` rows of context, stitched (1: whole frames)."""
+        self._check(lib().kb2_set_row_tiles(self.h, int(tiles), int(halo)))
 
     def rife_geometry(self):
         """IFNet: (plane_h, plane_w, window_x, window_y) of the motion outputs."""
