@@ -13,7 +13,8 @@ Workloads (the contract's configs):
             t = 0.2, 0.4, 0.6, 0.8 on every pair, 48-frame chunks dealt round-robin over the ranks,
             every output frame gathered to the host in order (a step = one chunk);
   janai / janai8  the AnimeJaNai unshuffle SPAN b8f64 of a seeded .span8 package (FP16 / E4M3 blocks);
-  warp      frames at t = 1/3 from one mid-pair motion (kb2_warp_blend_at), 8 pairs of 1080p.
+  warp      frames at t = 1/3 from one mid-pair motion (kb2_warp_blend_at), 8 pairs of 1080p;
+  kernels   one small pass of every kernel kind (--family to pick one), for the ncu summaries.
 
 `value` is whole-job frames/s with the inputs resident in HBM, timed with CUDA events on the enqueue
 stream (max over ranks). `e2e` is the same through the public C ABI with pinned host frames: the
@@ -45,7 +46,7 @@ for _p in (ROOT, PKG):
 FRAME_H, FRAME_W = 1080, 1920
 FLOP_PER_PX = 777888.0  # canonical SPAN x2: 388,944 MACs per input pixel
 CHAIN_TIMES = (0.2, 0.4, 0.6, 0.8)
-WORKLOADS = ("default", "span16", "span8", "rife", "rife4k", "chain", "janai", "janai8", "warp")
+WORKLOADS = ("default", "span16", "span8", "rife", "rife4k", "chain", "janai", "janai8", "warp", "kernels")
 
 
 def parse():
@@ -62,7 +63,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
+    ap.add_argument("--family", default="all", help="--workload kernels: all or one of " + ", ".join(
+        ("span16", "span8", "rife", "warp", "janai", "janai8")))
     a = ap.parse_args()
+    if a.workload == "kernels" and "--batch" not in sys.argv:
+        a.batch = 1
     if a.workload == "rife4k":
         a.height, a.width = a.height or 2160, a.width or 3840
     a.height, a.width = a.height or FRAME_H, a.width or FRAME_W
@@ -209,19 +214,24 @@ def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, tim
     return sum(done) * ch * cw / float(fh * fw), dt
 
 
-def janai_package(fp8, H, W):
-    """The seeded b8f64 .span8 package of the janai workloads; FP8: activation scales calibrated on
-    four 64x128 crops of seeded frames (the reference derives them offline, derive.h:42-62), by the
-    CPU restatement."""
+def janai_package(fp8, H, W, device=0):
+    """The seeded b8f64 .span8 package of the janai workloads; FP8: the same contents with activation
+    scales derived from the peaks the FP16 engine of the package measures on four seeded frames
+    (kb2_span_calibrate; the reference derives them offline the same way, derive.h:42-62)."""
     import numpy as np
+    import torch
+    import kirari_b200 as kb
     import seeded
     from synth import anime_frames
     p = seeded.span8_init(8, 64, seed=3)
-    if fp8:
-        from oracle import nets
-        crops = anime_frames(4, min(H, 64), min(W, 128), seed=900).astype(np.float16).astype(np.float32)
-        p = nets.span8_fp8_package(p, crops)
-    return seeded.span8_package(p)
+    pkg = seeded.span8_package(p)
+    if not fp8:
+        return pkg
+    e16 = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, pkg, H, W, max_batch=4, device=device)
+    frames = torch.from_numpy(anime_frames(4, H, W, seed=900).astype(np.float16)).cuda()
+    peaks = e16.calibrate(frames, n_peaks=1 + 3 * p["blocks"])
+    e16.close()
+    return seeded.span8_package(seeded.span8_fp8_from_peaks(p, peaks))
 
 
 def config0_one_thread():
@@ -312,8 +322,9 @@ def run_reference(args):
         frame, frame_b = np.ascontiguousarray(fa, np.float32), np.ascontiguousarray(fb, np.float32)
         flat = seeded.ifnet_flat(seeded.ifnet_init(2))
     elif workload in ("janai", "janai8"):
+        # the reference's FP32 forward reads the package's FP16 weights; the E4M3 scales do not enter it
         frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
-        flat = janai_package(workload == "janai8", args.height, args.width)
+        flat = janai_package(False, args.height, args.width)
     else:
         frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
         flat = seeded.span_flat(seeded.span_init(1))
@@ -398,7 +409,7 @@ def setup_leg(workload, B, H, W, timestep, D):
            "janai": workload in ("janai", "janai8"), "fp8": workload == "span8"}
     if leg["janai"]:
         q = workload == "janai8"
-        leg["flat"] = janai_package(q, H, W)
+        leg["flat"] = janai_package(q, H, W, D.local_rank)
         leg["frames"] = anime_frames(B, H, W, seed=shard.frame_seed(10, D.rank, 0)).astype(np.float16)
         leg["eng"] = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, leg["flat"], H, W, max_batch=B,
                                precision=kb.PREC_FP8 if q else kb.PREC_FP16, device=D.local_rank)
@@ -1070,6 +1081,100 @@ def run_warp_reference(args):
                       "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
+# ------------------------------------------------------------------------------------------------
+# one small pass of every kernel kind, for the per-kernel ncu summaries under profiles/
+# ------------------------------------------------------------------------------------------------
+KERNEL_FAMILIES = ("span16", "span8", "rife", "warp", "janai", "janai8")
+
+
+def run_kernels(args):
+    """Each family runs once, batch `--batch` (1 by default here) at 1920x1080, so that every
+    tensor of the SPAN and IFNet paths is larger than L2 while the process holds a few GB: span16
+    (the FP16 engine, F16 frames then display pixels), span8 (the E4M3 engine, after one FP16
+    calibration pass), rife (IFNet image and motion variants), warp (kb2_warp_blend_at bilinear,
+    Catmull-Rom and pan-locked, kb2_warp_blend_poses, kb2_flow_max, kb2_pack_display), janai /
+    janai8 (the unshuffle SPAN b8f64). Prints one JSON line with each family's kernel launches and
+    device time; not a benchmark line."""
+    import numpy as np
+    import torch
+    import kirari_b200 as kb
+    import seeded
+    from synth import anime_frames, shifted_pair
+
+    D = Dist()
+    B, H, W = args.batch, args.height, args.width
+    fams = KERNEL_FAMILIES if args.family == "all" else (args.family,)
+    stream = torch.cuda.Stream()
+    sh = kb.ctypes.c_void_p(stream.cuda_stream)
+    report = {}
+
+    def timed(name, fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            launches = fn()
+            e1.record(stream)
+        e1.synchronize()
+        report[name] = {"launches": launches, "ms": e0.elapsed_time(e1)}
+
+    x = torch.from_numpy(anime_frames(B, H, W, seed=7).astype(np.float16)).cuda()
+    for fam in fams:
+        if fam in ("span16", "span8"):
+            blob = kb.make_blob(kb.MODEL_SPAN_X2, seeded.span_flat(seeded.span_init(1)))
+            scales = None
+            if fam == "span8":
+                e16 = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B)
+                scales = seeded.scales_from_peaks(e16.calibrate(x, stream), floor=2.0 ** -14)
+                e16.close()
+            eng = kb.Engine(kb.MODEL_SPAN_X2, blob, H, W, max_batch=B, act_scales=scales,
+                            precision=kb.PREC_FP8 if fam == "span8" else kb.PREC_FP16)
+            out = torch.empty((B, 3, 2 * H, 2 * W), dtype=torch.float16, device="cuda")
+            timed(fam, lambda: (eng.enqueue([x], [out], stream), eng.launches_per_enqueue())[1])
+            if fam == "span16":
+                pix = torch.empty((B, 4, 2 * H, 2 * W), dtype=torch.uint8, device="cuda")
+                eng.set_output_format(kb.DISPLAY_RGB10A2)
+                timed("span16.display", lambda: (eng.enqueue([x], [pix], stream), eng.launches_per_enqueue())[1])
+                del pix
+            eng.check_device(stream)
+            eng.close()
+            del out
+        elif fam == "rife":
+            fa, fb = shifted_pair(H, W, seed=3)
+            a = torch.from_numpy(np.ascontiguousarray(np.repeat(fa[None], B, 0), np.float16)).cuda()
+            b = torch.from_numpy(np.ascontiguousarray(np.repeat(fb[None], B, 0), np.float16)).cuda()
+            eng = kb.Engine(kb.MODEL_IFNET, kb.make_blob(kb.MODEL_IFNET, seeded.ifnet_flat(seeded.ifnet_init(2))), H, W,
+                            max_batch=B)
+            out = torch.empty((B, 3, H, W), dtype=torch.float16, device="cuda")
+            timed("rife", lambda: (eng.enqueue([a, b], [out], stream), eng.launches_per_enqueue())[1])
+            timed("rife.motion", lambda: (eng.motion(a, b, stream=stream), eng.launches_per_enqueue())[1])
+            eng.check_device(stream)
+            eng.close()
+        elif fam == "warp":
+            a, b, flow, mask, win = warp_inputs(B, H, W, 11)
+            ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+            tf, tm = torch.from_numpy(flow).cuda(), torch.from_numpy(mask).cuda()
+            timed("warp.bilinear", lambda: (kb.warp_blend_at(ta, tb, tf, tm, win, WARP_T, stream=stream), 1)[1])
+            timed("warp.catmull_rom", lambda: (kb.warp_blend_at(ta, tb, tf, tm, win, WARP_T, stream=stream, warp=1), 1)[1])
+            timed("warp.pan_lock", lambda: (kb.warp_blend_at(ta, tb, tf, tm, win, WARP_T, stream=stream, pan_lock=1), 2)[1])
+            timed("warp.poses", lambda: (kb.warp_blend_poses(ta, tb, tf, tm, tf, tm, win, WARP_T, stream=stream), 1)[1])
+            timed("flow_max", lambda: (kb.flow_max(tf, tm, win, stream=stream), 1)[1])
+            frames = torch.empty((B, 3, 2 * H, 2 * W), dtype=torch.float16, device="cuda").uniform_()
+            timed("pack_display", lambda: (kb.pack_display(frames, kb.DISPLAY_RGB10A2_DITHER, stream=stream), 1)[1])
+        elif fam in ("janai", "janai8"):
+            q = fam == "janai8"
+            eng = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, janai_package(q, H, W), H, W, max_batch=B,
+                            precision=kb.PREC_FP8 if q else kb.PREC_FP16)
+            out = torch.empty((B, 3, 2 * H, 2 * W), dtype=torch.float16, device="cuda")
+            timed(fam, lambda: (eng.enqueue([x], [out], stream), eng.launches_per_enqueue())[1])
+            eng.check_device(stream)
+            eng.close()
+        torch.cuda.empty_cache()
+    if D.rank == 0:
+        print(json.dumps({"kernels": report, "batch": B, "frame": f"{W}x{H}",
+                          "note": "one pass of each kernel kind (profiling aid), not a benchmark line"}))
+    D.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1078,6 +1183,8 @@ def main():
         run_warp(args)
     elif args.workload == "chain":
         run_chain(args)
+    elif args.workload == "kernels":
+        run_kernels(args)
     else:
         run_ours(args)
 

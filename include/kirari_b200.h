@@ -181,10 +181,13 @@ int kb2_check_device(kb2_engine* engine, void* stream, int32_t* code);
  * calling thread for that time; allocates 16 bytes of device memory. */
 int kb2_selftest_bounded_wait(int32_t device, int32_t* code, double* waited_seconds);
 
-/* SPAN FP16 engine only: runs the frames through the FP16 network and returns, per quantised tensor,
- * the maximum |value| seen (19 peaks: [3b] block b input, [3b+1] / [3b+2] its two activations,
- * [18] last block output), the calibration of span_fp8::derive (src/gpu/span_fp8/derive.h:42-46).
- * Synchronous on `stream`. Scales are then peak * 1.25 / 448. */
+/* SPAN FP16 engines only: runs the frames through the FP16 network and returns, per quantised tensor,
+ * the maximum |value| seen, the calibration of span_fp8::derive (src/gpu/span_fp8/derive.h:42-46).
+ * KB2_MODEL_SPAN_X2: 19 peaks ([3b] block b input, [3b+1] / [3b+2] its two activations, [18] last
+ * block output). KB2_MODEL_SPAN_UNSHUFFLE: 1 + 3 * blocks peaks in the package's scale order
+ * (package.h:15-17: conv_1's output, then per block its two ReLU outputs and its output), so that a
+ * player derives an FP8 package from an FP16 one on the device. Synchronous on `stream`. Scales are
+ * then peak * 1.25 / 448. */
 int kb2_span_calibrate(kb2_engine* engine, void* stream, const kb2_tensor* frames, float* peaks,
                        int32_t n_peaks);
 

@@ -115,3 +115,41 @@ def test_span8_fp8_refuses_fp16_packages():
     with pytest.raises(kb.KB2Error) as e:
         kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, pkg, 32, 64, precision=kb.PREC_FP8)
     assert e.value.status == kb.KB2_FORMAT_UNSUPPORTED
+
+
+@pytest.mark.parametrize("blocks,real", [(2, 48), (3, 64)])
+def test_span8_calibration_peaks_track_the_oracle(blocks, real):
+    """kb2_span_calibrate on an unshuffle-SPAN engine: the package's 1 + 3 * blocks peaks (conv_1's
+    output, per block its two ReLU outputs and its output) from the FP16 engine, against the FP32
+    oracle's peaks of the same tensors (span8_forward); an FP8 package made from them runs."""
+    import torch
+    from synth import anime_frames
+    p = nets.span8_init(blocks, real, seed=5)
+    pkg = nets.span8_package(p)
+    x = f16(anime_frames(3, 40, 72, seed=8))
+    eng = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, pkg, 40, 72, max_batch=2)  # 3 frames: batches of 2 and 1
+    try:
+        got = eng.calibrate(torch.from_numpy(x.astype(np.float16)).cuda(), n_peaks=1 + 3 * blocks)
+        with pytest.raises(kb.KB2Error) as e:
+            eng.calibrate(torch.from_numpy(x.astype(np.float16)).cuda(), n_peaks=19 if blocks != 6 else 16)
+        assert e.value.status == kb.KB2_INPUT_MISMATCH
+    finally:
+        eng.close()
+    ref = []
+    for i in range(3):
+        pk = []
+        nets.span8_forward(x[i:i + 1], p, peaks=pk)
+        ref.append(pk)
+    ref = np.max(np.asarray(ref, np.float32), axis=0)
+    np.testing.assert_allclose(got, ref, rtol=1e-2)
+    import seeded
+    q = seeded.span8_fp8_from_peaks(p, got)
+    e8 = kb.Engine(kb.MODEL_SPAN_UNSHUFFLE, seeded.span8_package(q), 40, 72, max_batch=1, precision=kb.PREC_FP8)
+    try:
+        out8 = torch.full((1, 3, 80, 144), float("nan"), dtype=torch.float16, device="cuda")
+        e8.enqueue([torch.from_numpy(x[:1].astype(np.float16)).cuda()], [out8])
+        e8.check_device()
+        out8 = out8.float().cpu().numpy()
+    finally:
+        e8.close()
+    assert nets.psnr(out8, nets.span8_forward(x[:1], q)) >= 45.0

@@ -280,6 +280,16 @@ class Span8Engine final : public Engine {
     KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 1, 2, &in, &out, &batch));
     return net_.run(stream, in, out, batch);
   }
+  Status calibrate(cudaStream_t stream, const kb2_tensor& frames, float* peaks, int n_peaks) override {
+    if (n_peaks != net_.scale_count())
+      return refuse(KB2_INPUT_MISMATCH, "unshuffle SPAN calibration returns 1 + 3 * blocks peaks");
+    if (frames.type != KB2_F16 || frames.dims[1] != 3 || frames.dims[2] != height() || frames.dims[3] != width() ||
+        frames.dims[0] < 1)
+      return refuse(KB2_INPUT_MISMATCH, "calibration frames: F16 [n,3,H,W] expected");
+    const uint64_t addr = frames.handle + frames.offset;
+    if (addr == 0 || (addr & 15u) != 0) return refuse(KB2_INPUT_MISMATCH, "calibration frames misaligned");
+    return net_.calibrate(stream, reinterpret_cast<const void*>(addr), static_cast<int>(frames.dims[0]), peaks);
+  }
   Status set_profiling(bool on) override {
     net_.timer().enable(on);
     return Status::Ok();

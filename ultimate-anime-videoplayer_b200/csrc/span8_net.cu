@@ -26,6 +26,7 @@
 #include <cstring>
 
 #include "span8_net.h"
+#include "span_net.h"
 
 namespace kb2 {
 
@@ -195,6 +196,8 @@ Status Span8Net::create(const Span8Package& pkg, bool fp8, int max_batch, int H,
   w_ = W / 2;
   ch_ = pkg.real;
   fp8_ = fp8;
+  blocks_ = pkg.blocks;
+  KB2_TRY(peaks_.alloc(static_cast<size_t>(1 + 3 * blocks_) * sizeof(unsigned int)));
   const int C = ch_, cc = C / 8, cq = C / 16;  // FP16 and E4M3 chunks of a C-channel tensor
   KB2_TRY(err_.alloc(sizeof(int)));
   KB2_CUDA(cudaMemset(err_.ptr, 0, sizeof(int)));
@@ -238,10 +241,11 @@ Status Span8Net::create(const Span8Package& pkg, bool fp8, int max_batch, int H,
 
   auto add = [&](const ConvSpec& sp, const std::vector<float>& w, const std::vector<float>& b, const float* act_scale,
                  const ChunkedTensor* const* inputs, const ChunkedTensor* out, const ChunkedTensor* out2, float out_scale,
-                 const ChunkedTensor* res, const ChunkedTensor* res2, int kind) -> Status {
+                 const ChunkedTensor* res, const ChunkedTensor* res2, int kind, int peak = -1) -> Status {
     auto l = std::make_unique<ConvLayer>();
     KB2_TRY(l->build(sp, w.data(), b.data(), nullptr, act_scale, inputs, err));
-    steps_.push_back(Step{l.get(), out, out2, out2 != nullptr ? 1.0f / out_scale : 1.0f, res, res2, kind});
+    steps_.push_back(Step{l.get(), out, out2, out2 != nullptr ? 1.0f / out_scale : 1.0f, res, res2, kind,
+                          fp8 ? -1 : peak});
     layers_.push_back(std::move(l));
     return Status::Ok();
   };
@@ -263,7 +267,7 @@ Status Span8Net::create(const Span8Package& pkg, bool fp8, int max_batch, int H,
   {
     const ChunkedTensor* in[1] = {&u->t};
     KB2_TRY(add(spec(9, false, 12, C, kEpiBias, fp8 ? kOutF16E4m3 : kOutF16Chunk), oihw(pkg.first, C, 3, 1, kFirstIn, 12),
-                bias(pkg.first, C), nullptr, in, &s0->t, q_of(&s0->t), sc[0], nullptr, nullptr, k_first));
+                bias(pkg.first, C), nullptr, in, &s0->t, q_of(&s0->t), sc[0], nullptr, nullptr, k_first, 0));
   }
   const ChunkedTensor* x = &s0->t;
   for (int b = 0; b < pkg.blocks; ++b) {
@@ -281,7 +285,7 @@ Status Span8Net::create(const Span8Package& pkg, bool fp8, int max_batch, int H,
                     &s_in, in_x, nullptr, &r1->t, sc[1 + 3 * b], nullptr, nullptr, k_relu));
     } else {
       KB2_TRY(add(spec(9, false, C, C, kEpiPrelu, kOutF16Chunk), oihw(blk.c[0], C, 3, 1, kStored, C), bias(blk.c[0], C),
-                  nullptr, in_x, last ? &r1_last->t : &r1->t, nullptr, 1.0f, nullptr, nullptr, k_relu));
+                  nullptr, in_x, last ? &r1_last->t : &r1->t, nullptr, 1.0f, nullptr, nullptr, k_relu, 1 + 3 * b));
     }
     // c2 reads the E4M3 ReLU output (FP16: the last block's own copy)
     const ChunkedTensor* in_1[1] = {fp8 || !last ? &r1->t : &r1_last->t};
@@ -291,7 +295,7 @@ Status Span8Net::create(const Span8Package& pkg, bool fp8, int max_batch, int H,
                   &s1, in_1, nullptr, &r2->t, s2, nullptr, nullptr, k_relu));
     else
       KB2_TRY(add(spec(9, false, C, C, kEpiPrelu, kOutF16Chunk), oihw(blk.c[1], C, 3, 1, kStored, C), bias(blk.c[1], C),
-                  nullptr, in_1, &r2->t, nullptr, 1.0f, nullptr, nullptr, k_relu));
+                  nullptr, in_1, &r2->t, nullptr, 1.0f, nullptr, nullptr, k_relu, 2 + 3 * b));
     const ChunkedTensor* in_2[1] = {&r2->t};
     KB2_TRY(add(spec(9, fp8, C, C, kEpiBias, kOutF16Chunk), oihw(blk.c[2], C, 3, 1, kStored, C), bias(blk.c[2], C),
                 fp8 ? &s2 : nullptr, in_2, &c3->t, nullptr, 1.0f, nullptr, nullptr, k_c3));
@@ -299,7 +303,7 @@ Status Span8Net::create(const Span8Package& pkg, bool fp8, int max_batch, int H,
     const ChunkedTensor* xo = b == 0 ? &x1->t : (x == &xa->t ? &xb->t : &xa->t);
     const ChunkedTensor* in_3[1] = {&c3->t};
     KB2_TRY(add(spec(1, false, C, C, kEpiTanhGate, fp8 ? kOutF16E4m3 : kOutF16Chunk), oihw(blk.att, C, 1, 1, kStored, C),
-                bias(blk.att, C), nullptr, in_3, xo, q_of(xo), sc[3 + 3 * b], x, &c3->t, k_gate));
+                bias(blk.att, C), nullptr, in_3, xo, q_of(xo), sc[3 + 3 * b], x, &c3->t, k_gate, 3 + 3 * b));
     x = xo;
   }
   {
@@ -326,7 +330,31 @@ size_t Span8Net::device_bytes() const {
   return total;
 }
 
-Status Span8Net::run(cudaStream_t stream, const void* in, void* out, int batch) {
+Status Span8Net::calibrate(cudaStream_t stream, const void* frames, int n, float* peaks_out) {
+  if (fp8_) return refuse(KB2_FORMAT_UNSUPPORTED, "unshuffle SPAN: calibration runs on the FP16 engine");
+  const int ns = scale_count();
+  std::vector<float> best(static_cast<size_t>(ns), 0.0f);
+  DeviceBuffer scratch;  // the discarded x2 frames
+  KB2_TRY(scratch.alloc(static_cast<size_t>(max_batch_) * 3 * 4 * H_ * W_ * 2));
+  std::vector<unsigned int> bits(static_cast<size_t>(ns));
+  for (int i = 0; i < n; i += max_batch_) {
+    const int batch = n - i < max_batch_ ? n - i : max_batch_;
+    KB2_CUDA(cudaMemsetAsync(peaks_.ptr, 0, peaks_.bytes, stream));
+    const uint8_t* src = static_cast<const uint8_t*>(frames) + static_cast<size_t>(i) * 3 * H_ * W_ * 2;
+    KB2_TRY(run(stream, src, scratch.ptr, batch, peaks_.as<unsigned int>()));
+    KB2_CUDA(cudaMemcpyAsync(bits.data(), peaks_.ptr, peaks_.bytes, cudaMemcpyDeviceToHost, stream));
+    KB2_CUDA(cudaStreamSynchronize(stream));
+    for (int k = 0; k < ns; ++k) {
+      float f;
+      std::memcpy(&f, &bits[static_cast<size_t>(k)], 4);
+      best[static_cast<size_t>(k)] = std::fmax(best[static_cast<size_t>(k)], f);
+    }
+  }
+  std::memcpy(peaks_out, best.data(), best.size() * sizeof(float));
+  return Status::Ok();
+}
+
+Status Span8Net::run(cudaStream_t stream, const void* in, void* out, int batch, unsigned int* peaks) {
   if (batch < 1 || batch > max_batch_) return refuse(KB2_SHAPE_INVALID, "unshuffle SPAN: batch out of contract");
   {
     const int by = std::max(1, std::min(batch * h_, 65535));
@@ -354,6 +382,10 @@ Status Span8Net::run(cudaStream_t stream, const void* in, void* out, int batch) 
                             s.residual != nullptr ? s.residual->chunks : 0,
                             s.residual2 != nullptr ? s.residual2->ptr : nullptr));
     KB2_TRY(timer_.end(s.kind, flops, bytes, stream));
+    if (peaks != nullptr && s.peak >= 0 && o != nullptr) {
+      const size_t n2 = static_cast<size_t>(batch) * h_ * o->chunks * w_ * 4;  // 4 half2 per chunk
+      KB2_TRY(launch_absmax(stream, o->ptr, n2, peaks + s.peak));
+    }
   }
   return Status::Ok();
 }

@@ -40,7 +40,13 @@ class Span8Net {
   // otherwise every layer in FP16.
   Status create(const Span8Package& pkg, bool fp8, int max_batch, int H, int W);
   // in: NCHW F16 [batch][3][H][W]; out: NCHW F16 [batch][3][2H][2W] (device pointers).
-  Status run(cudaStream_t stream, const void* in, void* out, int batch);
+  // peaks: raise the package's 1 + 3 * blocks activation peaks there (FP16 engine only).
+  Status run(cudaStream_t stream, const void* in, void* out, int batch, unsigned int* peaks = nullptr);
+  // The FP16 engine over n frames: max |v| of each tensor the package scales (package.h:15-17:
+  // [0] conv_1's output, per block b [1 + 3b] and [2 + 3b] its two ReLU outputs, [3 + 3b] its output),
+  // the peaks the reference's span_fp8::derive collects (derive.h:42-46). Synchronous on `stream`.
+  Status calibrate(cudaStream_t stream, const void* frames, int n, float* peaks_out);
+  int scale_count() const { return 1 + 3 * blocks_; }
   size_t device_bytes() const;
   int* err_word() const { return err_.as<int>(); }
   int height() const { return H_; }
@@ -62,12 +68,14 @@ class Span8Net {
     const ChunkedTensor* residual;
     const ChunkedTensor* residual2;
     int kind;
+    int peak;  // index of `out` among the package's scaled tensors, -1 none
   };
   Status make_tensor(std::unique_ptr<Tensor>& t, int chunks, bool fp8 = false);
 
   int max_batch_ = 0, H_ = 0, W_ = 0, h_ = 0, w_ = 0, ch_ = 0;
   bool fp8_ = false;
-  DeviceBuffer err_;
+  int blocks_ = 0;
+  DeviceBuffer err_, peaks_;
   std::vector<std::unique_ptr<Tensor>> tensors_;
   std::vector<std::unique_ptr<ConvLayer>> layers_;
   std::vector<Step> steps_;

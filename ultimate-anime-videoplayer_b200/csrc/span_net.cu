@@ -63,6 +63,11 @@ __global__ void absmax_f16_kernel(const __half2* __restrict__ v, size_t n2, unsi
 
 }  // namespace
 
+Status launch_absmax(cudaStream_t stream, const void* f16, size_t n_half2, unsigned int* dst) {
+  absmax_f16_kernel<<<4 * num_sms(), 256, 0, stream>>>(static_cast<const __half2*>(f16), n_half2, dst);
+  return cuda_status(cudaGetLastError(), "absmax launch");
+}
+
 Status SpanNet::make_tensor(std::unique_ptr<Tensor>& t, int chunks, bool fp8) {
   t = std::make_unique<Tensor>();
   t->t.batch = max_batch_;
@@ -302,9 +307,7 @@ Status SpanNet::run(cudaStream_t stream, const void* in, void* out, int batch, b
     if (profiling_) KB2_TRY(timed(kind, s.flops_px * pixels, bytes_px * pixels, stream, false));
     if (capture_peaks && s.peak >= 0) {
       const size_t n2 = static_cast<size_t>(batch) * H_ * s.out->chunks * W_ * 4;  // 4 half2 per chunk
-      absmax_f16_kernel<<<4 * num_sms(), 256, 0, stream>>>(reinterpret_cast<const __half2*>(s.out->ptr), n2,
-                                                          peaks + s.peak);
-      KB2_CUDA(cudaGetLastError());
+      KB2_TRY(launch_absmax(stream, s.out->ptr, n2, peaks + s.peak));
     }
   }
   return Status::Ok();

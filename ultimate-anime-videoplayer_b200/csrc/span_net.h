@@ -13,6 +13,9 @@ constexpr size_t kSpanParams = KB2_SPAN_X2_PARAMS;  // the blob order of include
 constexpr int kSpanScales = 19;         // 1 + 3 * 6 E4M3 activation scales
 constexpr int kSpanBlocks = 6;
 
+// max |v| over n_half2 FP16 pairs raised into *dst (atomicMax on the float bits; *dst starts at 0).
+Status launch_absmax(cudaStream_t stream, const void* f16, size_t n_half2, unsigned int* dst);
+
 class SpanNet {
  public:
   // shared_err: another network's device error word to report into (null: its own).

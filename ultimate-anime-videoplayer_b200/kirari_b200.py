@@ -224,10 +224,11 @@ class Engine:
         self._check(lib().kb2_workspace_bytes(self.h, ctypes.byref(v)))
         return v.value
 
-    def calibrate(self, frames, stream=None):
-        peaks = (ctypes.c_float * 19)()
+    def calibrate(self, frames, stream=None, n_peaks=19):
+        """kb2_span_calibrate: 19 peaks (canonical SPAN) or 1 + 3 * blocks (a .span8 package's engine)."""
+        peaks = (ctypes.c_float * n_peaks)()
         t = to_kb2_tensor(frames)
-        self._check(lib().kb2_span_calibrate(self.h, _stream_handle(stream), ctypes.byref(t), peaks, 19))
+        self._check(lib().kb2_span_calibrate(self.h, _stream_handle(stream), ctypes.byref(t), peaks, n_peaks))
         return np.array(peaks[:], np.float32)
 
     def calibrate_static(self, frames, stream=None):

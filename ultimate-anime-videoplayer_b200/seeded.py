@@ -189,3 +189,13 @@ def scales_from_peaks(peaks, floor=None):
     if not np.all(np.isfinite(peaks)) or np.any(peaks <= 0):
         raise ValueError("unusable calibration peak")
     return (peaks * SCALE_HEADROOM / E4M3_MAX).astype(np.float32)
+
+
+def span8_fp8_from_peaks(p, peaks, floor=2.0 ** -14):
+    """An FP8 package (no FP16 flag) of contents `p` with activation scales derived from calibration
+    peaks in the package's order (conv_1's output, per block its two ReLU outputs and its output):
+    scale = max(peak, floor) * 1.25 / 448, as the reference's derive writes them (derive.h:42-62)."""
+    q = dict(p)
+    q["flags"] = 0
+    q["scales"] = scales_from_peaks(peaks, floor)
+    return q
