@@ -159,6 +159,36 @@ int kb2_set_output_format(kb2_engine* engine, int32_t format);
  * tile's height (device memory); 1 <= tiles <= H / 2, 0 <= halo <= 64, else KB2_SHAPE_INVALID. */
 int kb2_set_row_tiles(kb2_engine* engine, int32_t tiles, int32_t halo);
 
+/* Moving tiles of SPAN x2 (the reference's kernels/spec/span_tiles.h, Engine::span_tile_grid and
+ * Engine::next_span_tiles, src/gpu/backend.h:401-412): only the tiles that changed are recomputed,
+ * the rest of the output keeps the previous frame's. The grid is in input pixels: tile_w x tile_h
+ * tiles from (0, 0), row by row, the last row and column cut by the frame; reach_* is the network's
+ * receptive radius (20 input pixels) rounded up to tiles: the caller marks as core every tile whose
+ * output can change, i.e. within reach of a changed input pixel (kernels::dilate_span_tiles). */
+typedef struct kb2_tile_grid {
+  int32_t tile_w, tile_h; /* input pixels */
+  int32_t cols, rows;     /* tiles across and down */
+  int32_t reach_cols, reach_rows;
+  int32_t shift_step;     /* a pan must be a multiple of this many input pixels */
+  int32_t scale;          /* output pixels per input pixel (2) */
+} kb2_tile_grid;
+int kb2_span_tile_grid(const kb2_engine* engine, kb2_tile_grid* grid);
+
+/* The next kb2_enqueue of this SPAN x2 engine (one call only) computes only what the tiles marked
+ * non-zero in `core` (cols x rows bytes, row by row) need, and writes outputs[0] only there. Before
+ * that, if `previous` is not null and is not the call's output, outputs[0] receives `previous` (the
+ * previous call's output, same type and shape) moved by (shift_x, shift_y) input pixels (x scale
+ * output pixels), its pixels whose source falls outside the frame left as they are (their tiles must
+ * be core); `previous` null: outputs[0] already holds the previous output, and there is no shift. A
+ * shift onto the same buffer makes the next call compute and write the whole frame. The engine
+ * computes each dirty row of tiles from a window of its rows plus the reach above and below, or the
+ * whole frame when that costs less; the core tiles' values equal the whole frame's up to the order of
+ * FP32 sums. KB2_OK: the next call will do it; KB2_FORMAT_UNSUPPORTED (an empty core, which cancels a
+ * pending request; a shift without `previous`; row tiles on; another model): the next call computes
+ * the whole frame. The first request allocates the window network (device memory). */
+int kb2_next_span_tiles(kb2_engine* engine, const uint8_t* core, int32_t count, int32_t shift_x, int32_t shift_y,
+                        const kb2_tensor* previous);
+
 /* IFNet: the padded plane the network runs on (multiples of 32) and the frame's window in it, as the
  * reference's rife_geometry (src/kernels/spec/rife.h:47-63; left / top = half the padding, rounded
  * down to even): the motion outputs are plane_h x plane_w, the frame at (window_x, window_y). */

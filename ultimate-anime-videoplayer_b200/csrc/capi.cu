@@ -153,6 +153,26 @@ int kb2_set_output_format(kb2_engine* engine, int32_t format) {
   }
 }
 
+int kb2_span_tile_grid(const kb2_engine* engine, kb2_tile_grid* grid) {
+  if (engine == nullptr || grid == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    *grid = kb2_tile_grid{};
+    return engine->impl->tile_grid(grid).code;
+  } catch (...) {
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
+
+int kb2_next_span_tiles(kb2_engine* engine, const uint8_t* core, int32_t count, int32_t shift_x, int32_t shift_y,
+                        const kb2_tensor* previous) {
+  if (engine == nullptr) return KB2_INVALID_ARGUMENT;
+  try {
+    return set_error(engine, engine->impl->next_tiles(core, count, shift_x, shift_y, previous));
+  } catch (const std::exception& ex) {
+    return set_error(engine, kb2::refuse(KB2_VENDOR_CALL_FAILED, ex.what()));
+  }
+}
+
 int kb2_set_row_tiles(kb2_engine* engine, int32_t tiles, int32_t halo) {
   if (engine == nullptr) return KB2_INVALID_ARGUMENT;
   try {

@@ -987,8 +987,7 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
 }
 
 template <bool kFp8, int kCoutPad, int kEpi, int kOut>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, kEpi>::threads, 1)
-    conv3p_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
+__device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs& a) {
   static_assert(kCoutPad == 16 || kCoutPad == 48 || kCoutPad == 64, "paired kernel: 16, 48 or 64 output channels");
   static_assert(kStackBlocks * kCoutPad <= kStackTmemCols, "TMEM blocks");
   constexpr int kGroupWarps = PairShape<kCoutPad, kEpi>::group_warps;
@@ -1120,6 +1119,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
     constexpr int kSteps = kCols / 16;
     constexpr uint32_t kG = static_cast<uint32_t>(PairShape<kCoutPad, kEpi>::groups);
     constexpr bool kResidual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
+    // slots 0 and 1 add their second TMEM block 16 columns at a time on the gated and residual shapes
+    // (there a whole second block of live registers beside v and the residual words spilled: ptxas -v;
+    // measured 3-9 % faster), and all at once elsewhere (one TMEM wait; 1-2 % faster there)
+    constexpr bool kPieceAdd = kResidual;
     const int ew = warp - 2;
     const uint32_t grp = static_cast<uint32_t>(ew / kGroupWarps);
     const int quad = warp & 3;
@@ -1127,11 +1130,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
     const uint32_t free0 = cluster_addr(smem_u32(slot_free), 0);  // block 0's slot_free[0]
-    // FP16 layers: this warp's biases in registers and no channel scale (re-reading both from shared
-    // memory on every row measured 5-15 % slower); E4M3 layers and the 64-channel residual shape
-    // (96 registers a thread at 576 threads) read bias and scale from shared memory (in registers
-    // they spill)
-    constexpr bool kRegBias = !kFp8 && kCoutPad != 64;
+    // FP16 layers without a residual: this warp's biases in registers and no channel scale (re-reading
+    // both from shared memory on every row measured 5-15 % slower); E4M3 layers, the gated layers (72
+    // registers a thread at 832 threads: register biases spilled 64 bytes, and reading them from shared
+    // memory measured 0.5 % faster) and the 64-channel residual shape read bias and scale from shared
+    // memory
+    constexpr bool kRegBias = !kFp8 && kCoutPad != 64 && !kResidual;
     float r_bias[kCols], r_scale[kCols];
 #pragma unroll
     for (int j = 0; j < kCols; ++j) {
@@ -1160,7 +1164,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
         const uint32_t s = acc.idx;
         uint32_t res[kCols / 2];
         if constexpr (kResidual) {
-          if (store) load_residual_words<kCols>(a, n, y, x, col0, res);
+          if (store) load_residual_words<kCols, kFp8>(a, n, y, x, col0, res);
         }
         const bool got = wait_bar(&done[in.idx], in.phase, a.err, kErrWaitEpilogue);
         if (!__all_sync(0xffffffffu, got)) {
@@ -1171,7 +1175,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
         float v[kCols];
 #pragma unroll
         for (int k = 0; k < kSteps; ++k) tmem_ld16(my_cols + s * kCoutPad + 16u * k, v + 16 * k);
-        if (s < 2) {  // slots 0 and 1: the part of the sum that landed in block 6 or 7
+        if (s < 2 && kPieceAdd) {  // slots 0 and 1: the part of the sum that landed in block 6 or 7
+#pragma unroll
+          for (int k = 0; k < kSteps; ++k) {
+            float w[16];
+            tmem_ld16(my_cols + (s + 6) * kCoutPad + 16u * k, w);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[16 * k + j] += w[j];
+          }
+        } else if (s < 2) {
           float w[kCols];
 #pragma unroll
           for (int k = 0; k < kSteps; ++k) tmem_ld16(my_cols + (s + 6) * kCoutPad + 16u * k, w + 16 * k);
@@ -1217,6 +1230,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, 
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kStackTmemCols);
   }
+}
+
+// The kernel: one block of a cluster pair per SM, its register budget set by its thread count.
+template <bool kFp8, int kCoutPad, int kEpi, int kOut>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, kEpi>::threads, 1)
+    conv3p_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
+  conv3p_body<kFp8, kCoutPad, kEpi, kOut>(maps, a);
 }
 
 }  // namespace kb2

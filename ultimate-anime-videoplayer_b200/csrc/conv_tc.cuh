@@ -130,14 +130,28 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // The residual words of kCols channels [col0, col0 + kCols) of one pixel (same pixel and channels as
 // the output, in the block input's format): 4 words per 8 channels for FP16, 2 for E4M3. Loaded
 // ahead of the accumulator wait by the paired kernel, so the load latency hides behind the wait.
-template <int kCols>
+// kResFp8: the residual is E4M3 (the E4M3 layers' block inputs), else FP16.
+template <int kCols, bool kResFp8>
 __device__ __forceinline__ void load_residual_words(const ConvArgs& a, int n, int y, int x, int col0,
                                                     uint32_t (&w)[kCols / 2]) {
   const size_t pix_row = static_cast<size_t>(n) * a.H + y;
+  if (kCols % 16 == 0 && kResFp8 && (col0 & 15) == 0) {
+    // whole 16-channel E4M3 chunks: one 16-byte load each (groups 2 g2 and 2 g2 + 1)
+#pragma unroll
+    for (int g2 = 0; g2 < kCols / 16; ++g2) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(
+          a.residual + ((pix_row * a.res_chunks + (col0 + 16 * g2) / 16) * a.W + x) * 16));
+      w[8 * g2] = q.x;
+      w[8 * g2 + 1] = q.y;
+      w[8 * g2 + 4] = q.z;
+      w[8 * g2 + 5] = q.w;
+    }
+    return;
+  }
 #pragma unroll
   for (int g = 0; g < kCols / 8; ++g) {
     const int c = col0 + 8 * g;
-    if (a.res_fp8) {
+    if (kResFp8) {
       const uint2 q = __ldg(reinterpret_cast<const uint2*>(
           a.residual + ((pix_row * a.res_chunks + c / 16) * a.W + x) * 16 + (c % 16)));
       w[4 * g] = q.x;
@@ -249,16 +263,28 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
     uint8_t* dst = kOut == kOutE4m3Chunk ? a.out : a.out2;
     const int dst_chunks = kOut == kOutE4m3Chunk ? a.out_chunks : a.out2_chunks;
     const float is = a.out_inv_scale;
-#pragma unroll
-    for (int g = 0; g < kCols / 8; ++g) {
-      const float* f = v + 8 * g;
-      const int c = col0 + 8 * g;
+    auto e4m3x8 = [&](const float* f) {
       uint2 q;
       q.x = static_cast<uint32_t>(pack_e4m3x2(f[0] * is, f[1] * is)) |
             (static_cast<uint32_t>(pack_e4m3x2(f[2] * is, f[3] * is)) << 16);
       q.y = static_cast<uint32_t>(pack_e4m3x2(f[4] * is, f[5] * is)) |
             (static_cast<uint32_t>(pack_e4m3x2(f[6] * is, f[7] * is)) << 16);
-      *reinterpret_cast<uint2*>(dst + ((pix_row * dst_chunks + c / 16) * a.W + x) * 16 + (c % 16)) = q;
+      return q;
+    };
+    if (kCols % 16 == 0 && (col0 & 15) == 0) {
+      // whole 16-channel chunks: one 16-byte store each
+#pragma unroll
+      for (int g = 0; g < kCols / 16; ++g) {
+        const uint2 lo = e4m3x8(v + 16 * g), hi = e4m3x8(v + 16 * g + 8);
+        *reinterpret_cast<uint4*>(dst + ((pix_row * dst_chunks + (col0 + 16 * g) / 16) * a.W + x) * 16) =
+            make_uint4(lo.x, lo.y, hi.x, hi.y);
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < kCols / 8; ++g) {
+        const int c = col0 + 8 * g;
+        *reinterpret_cast<uint2*>(dst + ((pix_row * dst_chunks + c / 16) * a.W + x) * 16 + (c % 16)) = e4m3x8(v + 8 * g);
+      }
     }
   }
   if constexpr (kOut == kOutPixShuf4) {

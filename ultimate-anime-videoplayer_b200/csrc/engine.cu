@@ -1,12 +1,14 @@
 // Engine implementations: SPAN x2 (FP16 / FP8), IFNet, the unshuffle SPAN of a .span8 package, and
 // the factory.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "engine.h"
 #include "ifnet_net.h"
 #include "span8_net.h"
 #include "span_net.h"
+#include "span_tiles.h"
 #include "static_scratch.h"
 
 namespace kb2 {
@@ -78,8 +80,49 @@ class SpanEngine final : public Engine {
     int batch = 0;
     KB2_TRY(frame_io(inputs, n_inputs, outputs, n_outputs, 1, 2, &in, &out, &batch,
                      net_.output_format() != 0 ? net_.display_bytes() : 0));
+    if (moving_.has) {  // one enqueue only, as the reference's next_span_tiles
+      MovingJob job = std::move(moving_);
+      moving_ = MovingJob{};
+      if (tiles_ == 0) return run_moving(stream, in, out, batch, outputs[0], job);
+    }
     if (tiles_ > 0) return run_tiled(stream, in, out, batch);
     return net_.run(stream, in, out, batch);
+  }
+  Status tile_grid(kb2_tile_grid* g) const override {
+    g->tile_w = kMoveTile;
+    g->tile_h = kMoveTile;
+    g->cols = (net_.width() + kMoveTile - 1) / kMoveTile;
+    g->rows = (net_.height() + kMoveTile - 1) / kMoveTile;
+    g->reach_cols = (kSpanReach + kMoveTile - 1) / kMoveTile;
+    g->reach_rows = g->reach_cols;
+    g->shift_step = 1;
+    g->scale = 2;
+    return Status::Ok();
+  }
+  // kb2_next_span_tiles: the next enqueue computes only what the core tiles need, and writes only them
+  // (after copying `previous`, moved by (sx, sy) input pixels, into its output).
+  Status next_tiles(const uint8_t* core, int count, int sx, int sy, const kb2_tensor* previous) override {
+    moving_ = MovingJob{};
+    kb2_tile_grid g{};
+    KB2_TRY(tile_grid(&g));
+    if (core == nullptr || count != g.cols * g.rows)
+      return refuse(KB2_INPUT_MISMATCH, "moving tiles: core must hold cols x rows bytes");
+    if (tiles_ != 0) return refuse(KB2_FORMAT_UNSUPPORTED, "moving tiles: not with row tiles");
+    if ((sx != 0 || sy != 0) && previous == nullptr)
+      return refuse(KB2_FORMAT_UNSUPPORTED, "moving tiles: a shift needs the previous output");
+    if (std::abs(sx) >= net_.width() || std::abs(sy) >= net_.height())
+      return refuse(KB2_SHAPE_INVALID, "moving tiles: shift beyond the frame");
+    bool any = false;
+    for (int i = 0; i < count; ++i) any = any || core[i] != 0;
+    if (!any) return refuse(KB2_FORMAT_UNSUPPORTED, "moving tiles: empty core (the request is cancelled)");
+    KB2_TRY(ensure_moving());
+    moving_.core.assign(core, core + count);
+    moving_.sx = sx;
+    moving_.sy = sy;
+    moving_.has_prev = previous != nullptr;
+    if (previous != nullptr) moving_.prev = *previous;
+    moving_.has = true;
+    return Status::Ok();
   }
   Status set_output_format(int format) override {
     KB2_TRY(net_.set_output_format(format));
@@ -179,6 +222,146 @@ class SpanEngine final : public Engine {
     return Status::Ok();
   }
 
+  // ---- moving tiles
+  static constexpr int kMoveTile = 64;  // tile side, input pixels
+  static constexpr int kSpanReach = 20;  // receptive radius of the network, input pixels
+  struct MovingJob {
+    bool has = false, has_prev = false;
+    std::vector<uint8_t> core;
+    int sx = 0, sy = 0;
+    kb2_tensor prev{};
+  };
+  int move_rows() const { return std::min(net_.height(), kMoveTile + 2 * kSpanReach); }  // a window's rows
+  int move_windows() const { return net_.max_batch() * std::max(1, (net_.height() - 1) / move_rows()); }
+
+  // The window network, its buffers and the tile list's staging, made once (at the first request).
+  Status ensure_moving() {
+    if (win_net_ != nullptr) return Status::Ok();
+    const int H = net_.height(), W = net_.width(), hw = move_rows();
+    auto net = std::make_unique<SpanNet>();
+    KB2_TRY(net->create(params_, precision_, move_windows(), hw, W, scales_.empty() ? nullptr : scales_.data(),
+                        static_cast<int>(scales_.size()), net_.err_word()));
+    auto win_in = std::make_unique<DeviceBuffer>();
+    KB2_TRY(win_in->alloc(static_cast<size_t>(move_windows()) * 3 * hw * W * 2));
+    auto win_out = std::make_unique<DeviceBuffer>();  // F16 frames (24 B / input px) or RGBA16 (32)
+    KB2_TRY(win_out->alloc(static_cast<size_t>(move_windows()) * 32 * hw * W));
+    auto full_out = std::make_unique<DeviceBuffer>();
+    KB2_TRY(full_out->alloc(static_cast<size_t>(net_.max_batch()) * 32 * H * W));
+    const int cols = (W + kMoveTile - 1) / kMoveTile, rows = (H + kMoveTile - 1) / kMoveTile;
+    const size_t list = static_cast<size_t>(net_.max_batch()) * cols * rows;
+    auto tiles = std::make_unique<DeviceBuffer>();
+    KB2_TRY(tiles->alloc(list * sizeof(TileCopy)));
+    TileCopy* host = nullptr;
+    KB2_CUDA(cudaMallocHost(reinterpret_cast<void**>(&host), list * sizeof(TileCopy)));
+    cudaEvent_t ev = nullptr;
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+      cudaFreeHost(host);
+      return refuse(KB2_VENDOR_CALL_FAILED, "moving tiles: cudaEventCreate");
+    }
+    win_net_ = std::move(net);
+    win_in_ = std::move(win_in);
+    win_out_ = std::move(win_out);
+    full_out_ = std::move(full_out);
+    tile_list_ = std::move(tiles);
+    tile_host_ = host;
+    tile_sent_ = ev;
+    return Status::Ok();
+  }
+
+  Status run_moving(cudaStream_t stream, const void* in, void* out, int batch, const kb2_tensor& out_t,
+                    const MovingJob& job) {
+    const int H = net_.height(), W = net_.width(), hw = move_rows();
+    const bool display = net_.output_format() != 0;
+    const int planes = display ? 1 : 3, pxb = display ? net_.display_bytes() : 2;
+    const size_t row_bytes = static_cast<size_t>(2 * W) * pxb;
+    const size_t frame_bytes = row_bytes * 2 * H * planes;
+    KB2_TRY(win_net_->set_output_format(net_.output_format()));
+    // the previous output into this one, moved by the pan
+    if (job.has_prev) {
+      const kb2_tensor& p = job.prev;
+      for (int i = 0; i < 4; ++i)
+        if (p.dims[i] != out_t.dims[i] || p.type != out_t.type)
+          return refuse(KB2_INPUT_MISMATCH, "moving tiles: previous output of another shape");
+      const void* prev = reinterpret_cast<const void*>(p.handle + p.offset);
+      if (prev == out && (job.sx != 0 || job.sy != 0)) return net_.run(stream, in, out, batch);  // no shift in place
+      if (prev != out) {
+        if (job.sx == 0 && job.sy == 0)
+          KB2_CUDA(cudaMemcpyAsync(out, prev, frame_bytes * batch, cudaMemcpyDeviceToDevice, stream));
+        else
+          KB2_TRY(shift_frames(stream, prev, out, batch, planes, 2 * H, static_cast<int>(row_bytes), pxb, 2 * job.sx,
+                               2 * job.sy));
+      }
+    }
+    const int cols = (W + kMoveTile - 1) / kMoveTile, rows = (H + kMoveTile - 1) / kMoveTile;
+    std::vector<int> dirty;
+    for (int r = 0; r < rows; ++r) {
+      bool d = false;
+      for (int c = 0; c < cols; ++c) d = d || job.core[static_cast<size_t>(r) * cols + c] != 0;
+      if (d) dirty.push_back(r);
+    }
+    const int nd = static_cast<int>(dirty.size());
+    // windows of the dirty tile rows, or the whole frames when that costs less
+    const bool whole = static_cast<long long>(nd) * hw >= H || nd * batch > move_windows();
+    const void* win = nullptr;
+    int win_rows = 0;
+    std::vector<int> ys(static_cast<size_t>(nd));
+    if (whole) {
+      KB2_TRY(net_.run(stream, in, full_out_->ptr, batch));
+      win = full_out_->ptr;
+      win_rows = 2 * H;
+    } else {
+      const size_t plane = static_cast<size_t>(H) * W * 2, wplane = static_cast<size_t>(hw) * W * 2;
+      for (int k = 0; k < nd; ++k) ys[k] = std::clamp(dirty[k] * kMoveTile - kSpanReach, 0, H - hw);
+      for (int f = 0; f < batch; ++f)
+        for (int k = 0; k < nd; ++k) {
+          const uint8_t* src = static_cast<const uint8_t*>(in) + f * 3 * plane + static_cast<size_t>(ys[k]) * W * 2;
+          uint8_t* dst = win_in_->as<uint8_t>() + (static_cast<size_t>(f) * nd + k) * 3 * wplane;
+          KB2_CUDA(cudaMemcpy2DAsync(dst, wplane, src, plane, wplane, 3, cudaMemcpyDeviceToDevice, stream));
+        }
+      KB2_TRY(win_net_->run(stream, win_in_->ptr, win_out_->ptr, batch * nd));
+      win = win_out_->ptr;
+      win_rows = 2 * hw;
+    }
+    // the core tiles, from their windows into the output
+    KB2_CUDA(cudaEventSynchronize(tile_sent_));  // the staging's previous list has been copied
+    const int unit = display ? 1 : 2;               // output pixels a unit of the copy's columns
+    int n = 0;
+    for (int f = 0; f < batch; ++f)
+      for (int k = 0; k < nd; ++k) {
+        const int r = dirty[k];
+        const int y0 = r * kMoveTile, y1 = std::min(H, y0 + kMoveTile);
+        for (int c = 0; c < cols; ++c) {
+          if (job.core[static_cast<size_t>(r) * cols + c] == 0) continue;
+          const int x0 = c * kMoveTile, x1 = std::min(W, x0 + kMoveTile);
+          TileCopy& t = tile_host_[n++];
+          t.frame = f;
+          t.window = whole ? f : f * nd + k;
+          t.out_y = 2 * y0;
+          t.win_y = whole ? 2 * y0 : 2 * (y0 - ys[k]);
+          t.x = 2 * x0 / unit;
+          t.cols = 2 * (x1 - x0) / unit;
+          t.rows = 2 * (y1 - y0);
+        }
+      }
+    KB2_CUDA(cudaMemcpyAsync(tile_list_->ptr, tile_host_, n * sizeof(TileCopy), cudaMemcpyHostToDevice, stream));
+    KB2_CUDA(cudaEventRecord(tile_sent_, stream));
+    return copy_tiles(stream, tile_list_->as<TileCopy>(), n, planes, win, out, static_cast<int>(row_bytes), 2 * H,
+                      win_rows, pxb);
+  }
+
+  MovingJob moving_;
+  std::unique_ptr<SpanNet> win_net_;
+  std::unique_ptr<DeviceBuffer> win_in_, win_out_, full_out_, tile_list_;
+  TileCopy* tile_host_ = nullptr;
+  cudaEvent_t tile_sent_ = nullptr;
+
+ public:
+  ~SpanEngine() override {
+    if (tile_sent_ != nullptr) cudaEventDestroy(tile_sent_);
+    if (tile_host_ != nullptr) cudaFreeHost(tile_host_);
+  }
+
+ private:
   SpanNet net_;
   std::vector<float> params_, scales_;
   int precision_ = KB2_PREC_FP16;

@@ -30,6 +30,13 @@ class Engine {
     return refuse(KB2_FORMAT_UNSUPPORTED, "this engine does not calibrate");
   }
   Status check_device(cudaStream_t stream, int32_t* code);
+  // kb2_span_tile_grid / kb2_next_span_tiles: moving tiles (SPAN x2 only)
+  virtual Status tile_grid(kb2_tile_grid*) const {
+    return refuse(KB2_FORMAT_UNSUPPORTED, "this engine computes whole frames only");
+  }
+  virtual Status next_tiles(const uint8_t*, int, int, int, const kb2_tensor*) {
+    return refuse(KB2_FORMAT_UNSUPPORTED, "this engine computes whole frames only");
+  }
   // kb2_set_row_tiles (SPAN x2 only)
   virtual Status set_row_tiles(int, int) { return refuse(KB2_FORMAT_UNSUPPORTED, "this engine runs whole frames"); }
   // kb2_set_output_format: 0 = F16 frames, else a kb2_display_format (SPAN x2 only)

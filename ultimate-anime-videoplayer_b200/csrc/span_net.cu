@@ -49,13 +49,20 @@ __global__ void pack_frame_kernel(const __half* __restrict__ in, uint8_t* __rest
 }
 
 // max |v| over an F16 chunked tensor -> atomicMax on the float bits (non-negative floats order as
-// unsigned integers).
+// unsigned integers). 16-byte loads (8 halves); n2 % 4 == 0 (4 half2 in every 16-byte chunk).
 __global__ void absmax_f16_kernel(const __half2* __restrict__ v, size_t n2, unsigned int* out) {
   float m = 0.0f;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n2;
+  const uint4* v4 = reinterpret_cast<const uint4*>(v);
+  const size_t n4 = n2 / 4;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const float2 f = __half22float2(v[i]);
-    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+    const uint4 q = __ldg(v4 + i);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
   }
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
@@ -64,6 +71,8 @@ __global__ void absmax_f16_kernel(const __half2* __restrict__ v, size_t n2, unsi
 }  // namespace
 
 Status launch_absmax(cudaStream_t stream, const void* f16, size_t n_half2, unsigned int* dst) {
+  if (n_half2 % 4 != 0 || (reinterpret_cast<uintptr_t>(f16) & 15u) != 0)
+    return refuse(KB2_FORMAT_UNSUPPORTED, "absmax: whole 16-byte chunks expected");
   absmax_f16_kernel<<<4 * num_sms(), 256, 0, stream>>>(static_cast<const __half2*>(f16), n_half2, dst);
   return cuda_status(cudaGetLastError(), "absmax launch");
 }

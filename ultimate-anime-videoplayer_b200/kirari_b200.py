@@ -41,7 +41,7 @@ EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
            "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max",
            "kb2_warp_blend_poses", "kb2_pack_display", "kb2_rife_geometry", "kb2_set_output_format",
-           "kb2_set_row_tiles")
+           "kb2_set_row_tiles", "kb2_span_tile_grid", "kb2_next_span_tiles")
 
 
 class KB2Error(RuntimeError):
@@ -68,6 +68,11 @@ class Motion(ctypes.Structure):
                 ("plane_w", ctypes.c_int32), ("x", ctypes.c_int32), ("y", ctypes.c_int32),
                 ("width", ctypes.c_int32), ("height", ctypes.c_int32), ("warp", ctypes.c_int32),
                 ("pan_lock", ctypes.c_int32), ("at_instant", ctypes.c_int32)]
+
+
+class SpanTileGrid(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("tile_w", "tile_h", "cols", "rows", "reach_cols", "reach_rows",
+                                             "shift_step", "scale")]
 
 
 class LayerProfile(ctypes.Structure):
@@ -120,6 +125,9 @@ def lib():
         L.kb2_rife_geometry.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int32)] * 4
         L.kb2_set_output_format.argtypes = [ctypes.c_void_p, ctypes.c_int32]
         L.kb2_set_row_tiles.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32]
+        L.kb2_span_tile_grid.argtypes = [ctypes.c_void_p, ctypes.POINTER(SpanTileGrid)]
+        L.kb2_next_span_tiles.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.POINTER(Tensor)]
         _lib = L
     return _lib
 
@@ -191,6 +199,21 @@ class Engine:
     def set_row_tiles(self, tiles, halo):
         """SPAN x2: run frames as `tiles` row tiles with `halo` rows of context, stitched (1: whole frames)."""
         self._check(lib().kb2_set_row_tiles(self.h, int(tiles), int(halo)))
+
+    def span_tile_grid(self):
+        """SPAN x2 moving tiles: dict(tile_w, tile_h, cols, rows, reach_cols, reach_rows, shift_step, scale)."""
+        g = SpanTileGrid()
+        self._check(lib().kb2_span_tile_grid(self.h, ctypes.byref(g)))
+        return {n: getattr(g, n) for n, _ in SpanTileGrid._fields_}
+
+    def next_span_tiles(self, core, shift_x=0, shift_y=0, previous=None):
+        """Requests that the next enqueue recompute only the core tiles (uint8 [rows, cols]); raises
+        KB2Error (KB2_FORMAT_UNSUPPORTED: the next call computes the whole frame) when refused."""
+        c = np.ascontiguousarray(core, np.uint8)
+        self._core_keep = c
+        prev = None if previous is None else to_kb2_tensor(previous)
+        self._check(lib().kb2_next_span_tiles(self.h, c.ctypes.data_as(ctypes.c_void_p), int(c.size), int(shift_x),
+                                              int(shift_y), None if prev is None else ctypes.byref(prev)))
 
     def rife_geometry(self):
         """IFNet: (plane_h, plane_w, window_x, window_y) of the motion outputs."""
