@@ -1004,7 +1004,8 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
   uint64_t* wpeer = wbar + 1;               // block 0: block 1's weights landed
   uint64_t* drain = wpeer + 1;              // both blocks: every MMA completed
   uint64_t* s_k = bars + 128;               // per K step of a row: (a_off >> 4) | (lbo >> 4) << 16
-  float* s_bias = reinterpret_cast<float*>(s_k + kMaxKSteps + 1);
+  // per-channel constants, 16-byte aligned (the epilogue reads them four at a time)
+  float* s_bias = reinterpret_cast<float*>(s_k + kMaxKSteps + 2);
   float* s_scale = s_bias + kMaxN;
   float* s_slope = s_scale + kMaxN;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_slope + kMaxN);
@@ -1198,7 +1199,8 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
         __syncwarp();
         if (lane == 0) mbar_arrive_remote_relaxed(free0 + s * 8u);
         if (store)
-          epilogue_cols<kEpi, kOut, kCols>(a, e_bias, e_scale, s_slope + col0, v, 0, n, y, x, col0,
+          epilogue_cols<kEpi, kOut, kCols, kRegBias ? kConstsAny : (kFp8 ? kConstsVec4 : kConstsVec4Bias)>(
+              a, e_bias, e_scale, s_slope + col0, v, 0, n, y, x, col0,
                                            kResidual ? res : nullptr);
       }
       if (!ok) break;

@@ -167,20 +167,62 @@ __device__ __forceinline__ void load_residual_words(const ConvArgs& a, int n, in
   }
 }
 
-template <int kEpi, int kOut, int kCols>
+// How the per-channel constants are read: kConstsAny through the pointers as given (registers or
+// shared memory), one value at a time; kConstsVec4 from 16-byte aligned shared memory, four at a
+// time (a quarter of the load instructions); kConstsVec4Bias the same with the scale 1 (FP16 layers).
+enum ConstsMode : int { kConstsAny = 0, kConstsVec4 = 1, kConstsVec4Bias = 2 };
+
+template <int kEpi, int kOut, int kCols, int kConsts = kConstsAny>
 __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_bias, const float* s_scale,
                                               const float* s_slope, float* v, int kc0, int n, int y, int x,
                                               int col0_override = -1, const uint32_t* res_pre = nullptr) {
   const int col0 = col0_override >= 0 ? col0_override : kc0;
   const size_t pix_row = static_cast<size_t>(n) * a.H + y;
+  if constexpr (kConsts == kConstsAny) {
 #pragma unroll
-  for (int j = 0; j < kCols; ++j) v[j] = fmaf(v[j], s_scale[kc0 + j], s_bias[kc0 + j]);
+    for (int j = 0; j < kCols; ++j) v[j] = fmaf(v[j], s_scale[kc0 + j], s_bias[kc0 + j]);
+  } else {
+    static_assert(kCols % 4 == 0, "vector constants: four channels at a time");
+#pragma unroll
+    for (int j = 0; j < kCols; j += 4) {
+      const float4 b = *reinterpret_cast<const float4*>(s_bias + kc0 + j);
+      if constexpr (kConsts == kConstsVec4) {
+        const float4 sc = *reinterpret_cast<const float4*>(s_scale + kc0 + j);
+        v[j] = fmaf(v[j], sc.x, b.x);
+        v[j + 1] = fmaf(v[j + 1], sc.y, b.y);
+        v[j + 2] = fmaf(v[j + 2], sc.z, b.z);
+        v[j + 3] = fmaf(v[j + 3], sc.w, b.w);
+      } else {
+        v[j] += b.x;
+        v[j + 1] += b.y;
+        v[j + 2] += b.z;
+        v[j + 3] += b.w;
+      }
+    }
+  }
+  // PReLU slopes of this pixel's channels (from shared memory four at a time where it is aligned)
+  auto slope = [&](int j) -> float { return s_slope[kc0 + j]; };
+  float slope_v[kEpi == kEpiPrelu || kEpi == kEpiResPrelu ? kCols : 1];
+  if constexpr ((kEpi == kEpiPrelu || kEpi == kEpiResPrelu) && kConsts != kConstsAny) {
+#pragma unroll
+    for (int j = 0; j < kCols; j += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(s_slope + kc0 + j);
+      slope_v[j] = q.x;
+      slope_v[j + 1] = q.y;
+      slope_v[j + 2] = q.z;
+      slope_v[j + 3] = q.w;
+    }
+  }
+  auto slope_at = [&](int j) -> float {
+    if constexpr ((kEpi == kEpiPrelu || kEpi == kEpiResPrelu) && kConsts != kConstsAny) return slope_v[j];
+    else return slope(j);
+  };
   if constexpr (kEpi == kEpiSilu) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j) v[j] = v[j] * sigmoidf_fast(v[j]);
   } else if constexpr (kEpi == kEpiPrelu) {
 #pragma unroll
-    for (int j = 0; j < kCols; ++j) v[j] = v[j] >= 0.0f ? v[j] : v[j] * s_slope[kc0 + j];
+    for (int j = 0; j < kCols; ++j) v[j] = v[j] >= 0.0f ? v[j] : v[j] * slope_at(j);
   } else if constexpr (kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu) {
     // residual: same pixel and channels, in the block input's format
 #pragma unroll
@@ -222,7 +264,7 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
           t = (t + r[k]) * sigmoid_centered(t);
         } else {
           const float u = t + r[k];
-          t = u >= 0.0f ? u : u * s_slope[kc0 + 8 * g + k];
+          t = u >= 0.0f ? u : u * slope_at(8 * g + k);
         }
       }
     }

@@ -34,6 +34,7 @@ constexpr uint32_t kStackBlocks = 8;  // TMEM blocks: one per slot, plus 6 and 7
 constexpr uint32_t kStackZeroOff = 2176;
 constexpr uint32_t kStackZeroBytes = 48 * 32;
 constexpr uint32_t kStackSmemExtra = 1024 + kStackZeroOff + kStackZeroBytes + 64;
-static_assert(128 * 8 + (kMaxKSteps + 1) * 8 + 3 * kMaxN * 4 + 4 <= kStackZeroOff, "shared layout");
+static_assert(128 * 8 + (kMaxKSteps + 2) * 8 + 3 * kMaxN * 4 + 4 <= kStackZeroOff, "shared layout");
+static_assert(((128 + kMaxKSteps + 2) * 8) % 16 == 0, "per-channel constants 16-byte aligned");
 
 }  // namespace kb2
