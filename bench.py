@@ -9,6 +9,7 @@ Workloads (the contract's configs):
             configs[3] at 3840x2160 (IFNet FP16, 8 frame pairs a step, key "rife_4k") timed in the
             same process, each with its own value, roofline, e2e, clocks and output check;
   span16 / span8 / rife (1080p; --height 2160 --width 3840 for 4K) / rife4k: one of those alone;
+  rife425   RIFE 4.25 (the fused RIFE 4.2x plan, KB2_MODEL_RIFE_FUSED, seeded) at 3840x2160;
   chain     configs[4], the full chain: SPAN x2 FP8 on a 1080p stream, then IFNet at 3840x2160 for
             t = 0.2, 0.4, 0.6, 0.8 on every pair, 48-frame chunks dealt round-robin over the ranks,
             every output frame gathered to the host in order (a step = one chunk);
@@ -46,7 +47,7 @@ for _p in (ROOT, PKG):
 FRAME_H, FRAME_W = 1080, 1920
 FLOP_PER_PX = 777888.0  # canonical SPAN x2: 388,944 MACs per input pixel
 CHAIN_TIMES = (0.2, 0.4, 0.6, 0.8)
-WORKLOADS = ("default", "span16", "span8", "rife", "rife4k", "chain", "janai", "janai8", "warp", "kernels")
+WORKLOADS = ("default", "span16", "span8", "rife", "rife4k", "rife425", "chain", "janai", "janai8", "warp", "kernels")
 
 
 def parse():
@@ -68,7 +69,7 @@ def parse():
     a = ap.parse_args()
     if a.workload == "kernels" and "--batch" not in sys.argv:
         a.batch = 1
-    if a.workload == "rife4k":
+    if a.workload in ("rife4k", "rife425"):
         a.height, a.width = a.height or 2160, a.width or 3840
     a.height, a.width = a.height or FRAME_H, a.width or FRAME_W
     return a
@@ -168,18 +169,19 @@ def cpu_model():
 # ------------------------------------------------------------------------------------------------
 CROP_H, CROP_W = 24, 48
 RIFE_CROP_H, RIFE_CROP_W = 64, 96  # IFNet needs multiples of 32
+RIFE42_CROP_H, RIFE42_CROP_W = 64, 128  # RIFE 4.25: multiples of 4 x 8
 
 
-def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, timestep=0.5, full=None):
+def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, timestep=0.5, full=None, rife42=False):
     """Each host thread runs the reference's FP32 network on its own crop of the frame (the
     interpreter is single-threaded per call); returns (frames processed, seconds). SPAN when
-    frame_b is None, else IFNet on the crop pair; `flat` given as bytes is a .span8 package, run by
-    the reference's unshuffle-SPAN forward (src/gpu/span_fp8/forward.cpp:144)."""
+    frame_b is None, else IFNet (RIFE 4.2x with rife42) on the crop pair; `flat` given as bytes is a
+    .span8 package, run by the reference's unshuffle-SPAN forward (src/gpu/span_fp8/forward.cpp:144)."""
     from oracle import ref_lib
     import numpy as np
 
     rife = frame_b is not None
-    ch, cw = (RIFE_CROP_H, RIFE_CROP_W) if rife else (CROP_H, CROP_W)
+    ch, cw = crop_of(rife, rife42)
     H, W = frame.shape[1:]
     rng = np.random.default_rng(0)
     jobs = []
@@ -195,7 +197,9 @@ def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, tim
     def work(t):
         for tt, a, b in jobs:
             if tt == t:
-                if rife:
+                if rife42:
+                    ref_lib.rife42_forward(a, b, timestep, flat)
+                elif rife:
                     ref_lib.ifnet_forward(a, b, timestep, flat)
                 elif isinstance(flat, bytes):
                     ref_lib.span8_forward(flat, a)
@@ -212,6 +216,13 @@ def reference_sample(threads, frame, flat, crops_per_thread=1, frame_b=None, tim
     dt = time.perf_counter() - t0
     fh, fw = full if full is not None else (FRAME_H, FRAME_W)
     return sum(done) * ch * cw / float(fh * fw), dt
+
+
+def crop_of(rife, rife42=False):
+    """The crop each reference thread runs: SPAN, IFNet or RIFE 4.25."""
+    if rife42:
+        return RIFE42_CROP_H, RIFE42_CROP_W
+    return (RIFE_CROP_H, RIFE_CROP_W) if rife else (CROP_H, CROP_W)
 
 
 def janai_package(fp8, H, W, device=0):
@@ -246,19 +257,21 @@ def config0_one_thread():
     return time.perf_counter() - t0
 
 
-def cpu_baseline(frame, flat, budget_s=12.0, frame_b=None, timestep=0.5, full=None, with_config0=False):
+def cpu_baseline(frame, flat, budget_s=12.0, frame_b=None, timestep=0.5, full=None, with_config0=False,
+                 rife42=False):
     from oracle import ref_lib
     if not ref_lib.available():
         return None
     cores = host_cores()
-    kw = dict(frame_b=frame_b, timestep=timestep, full=full)
+    kw = dict(frame_b=frame_b, timestep=timestep, full=full, rife42=rife42)
     frames, dt = reference_sample(cores, frame, flat, **kw)
     reps = max(1, int(budget_s / max(dt, 1e-3)))
     if reps > 1:
         frames, dt = reference_sample(cores, frame, flat, crops_per_thread=reps, **kw)
-    ch, cw = (RIFE_CROP_H, RIFE_CROP_W) if frame_b is not None else (CROP_H, CROP_W)
+    ch, cw = crop_of(frame_b is not None, rife42)
     fh, fw = full if full is not None else (FRAME_H, FRAME_W)
-    net = "IFNet pairs" if frame_b is not None else ("unshuffle SPAN b8f64" if isinstance(flat, bytes) else "SPAN")
+    net = ("RIFE 4.25 pairs" if rife42 else "IFNet pairs" if frame_b is not None else
+           "unshuffle SPAN b8f64" if isinstance(flat, bytes) else "SPAN")
     out = {"value": frames / dt, "unit": "frames/s", "cores": cores, "kind": "reference", "cpu": cpu_model(),
            "sample": f"{cores} threads x {reps} {net} crops of {ch}x{cw} px of synthetic {fw}x{fh} frames, "
                      f"reference FP32 IR interpreter (oracle/_ref), scaled by pixels to {fw}x{fh} frames"}
@@ -272,6 +285,14 @@ def cpu_baseline(frame, flat, budget_s=12.0, frame_b=None, timestep=0.5, full=No
 
 def workload_desc(workload, B, H, W, timestep, steps, world=1):
     """metric, dtype, config of an engine workload (shared by both arms)."""
+    if workload == "rife425":
+        metric = f"RIFE 4.25 {W}x{H} interpolated frames/s"
+        config = {"workload": f"RIFE 4.25 (fused RIFE 4.2x plan, seeded weights) FP16, {B} frame pairs per step, "
+                              f"{W}x{H}, t={timestep}",
+                  "global_batch": B * world, "frames_per_gpu": B * steps,
+                  "parallelism": f"pair-sharded x{world}, no collective",
+                  "l2": f"working set > L2: {B} pairs of {W}x{H} FP16 frames and their activations"}
+        return metric, "f16", config
     if workload in ("rife", "rife4k"):
         metric = f"RIFE IFNet {W}x{H} interpolated frames/s"
         config = {"workload": f"configs[3] IFNet FP16, {B} frame pairs per step, {W}x{H}, t={timestep}",
@@ -316,11 +337,12 @@ def run_reference(args):
     if not ref_lib.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
         return
-    rife = workload in ("rife", "rife4k")
+    rife = workload in ("rife", "rife4k", "rife425")
+    rife42 = workload == "rife425"
     if rife:
         fa, fb = shifted_pair(args.height, args.width, 0)
         frame, frame_b = np.ascontiguousarray(fa, np.float32), np.ascontiguousarray(fb, np.float32)
-        flat = seeded.ifnet_flat(seeded.ifnet_init(2))
+        flat = rife42_flat() if rife42 else seeded.ifnet_flat(seeded.ifnet_init(2))
     elif workload in ("janai", "janai8"):
         # the reference's FP32 forward reads the package's FP16 weights; the E4M3 scales do not enter it
         frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
@@ -328,7 +350,7 @@ def run_reference(args):
     else:
         frame, frame_b = anime_frame(args.height, args.width, 0).astype(np.float32), None
         flat = seeded.span_flat(seeded.span_init(1))
-    kw = dict(frame_b=frame_b, timestep=args.timestep, full=(args.height, args.width))
+    kw = dict(frame_b=frame_b, timestep=args.timestep, full=(args.height, args.width), rife42=rife42)
     cores = host_cores()
     for _ in range(args.warmup):
         reference_sample(cores, frame, flat, **kw)
@@ -338,7 +360,7 @@ def run_reference(args):
         total_frames += f
         total_s += dt
     value = total_frames / total_s
-    ch, cw = (RIFE_CROP_H, RIFE_CROP_W) if rife else (CROP_H, CROP_W)
+    ch, cw = crop_of(rife, rife42)
     line = {"metric": metric, "value": value, "unit": "frames/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -381,6 +403,13 @@ class Dist:
             dist.destroy_process_group()
 
 
+def rife42_flat():
+    """The seeded RIFE 4.25 parameter array of the rife425 workload (12 plan floats first)."""
+    import seeded
+    plan = seeded.RIFE_PLANS["4.25"]
+    return seeded.rife_flat(seeded.rife_init(plan), plan)
+
+
 def calibrated_scales(blob, H, W, B, device):
     """configs[2]'s activation scales: the FP16 engine's peaks over 16 seeded frames (not the timed
     ones), scale = max(peak, 2^-14) * 1.25 / 448 (the reference's derive, derive.h:42-62)."""
@@ -405,7 +434,8 @@ def setup_leg(workload, B, H, W, timestep, D):
     import shard
     from synth import anime_frames, shifted_pair
 
-    leg = {"workload": workload, "B": B, "H": H, "W": W, "timestep": timestep, "rife": workload in ("rife", "rife4k"),
+    leg = {"workload": workload, "B": B, "H": H, "W": W, "timestep": timestep,
+           "rife": workload in ("rife", "rife4k", "rife425"), "r42": workload == "rife425",
            "janai": workload in ("janai", "janai8"), "fp8": workload == "span8"}
     if leg["janai"]:
         q = workload == "janai8"
@@ -416,17 +446,19 @@ def setup_leg(workload, B, H, W, timestep, D):
         leg["host_in"] = [leg["frames"]]
         leg["out_shape"] = (B, 3, 2 * H, 2 * W)
     elif leg["rife"]:
-        p = seeded.ifnet_init(2)
-        leg["params"] = p
-        leg["flat"] = seeded.ifnet_flat(p)
+        if leg["r42"]:
+            leg["flat"] = rife42_flat()
+        else:
+            leg["params"] = seeded.ifnet_init(2)
+            leg["flat"] = seeded.ifnet_flat(leg["params"])
         # 4 distinct seeded pairs, each used twice in the step's 8 (generating 4K frames is slow on
         # the host); the step's inputs are still 8 x 2 x 49.8 MB at 4K, far above the 126 MB L2
         uniq = min(B, 4)
         pairs = [shifted_pair(H, W, seed=shard.frame_seed(10, D.rank, i)) for i in range(uniq)]
         leg["frames"] = np.ascontiguousarray(np.stack([pairs[i % uniq][0] for i in range(B)]), np.float16)
         leg["frames_b"] = np.ascontiguousarray(np.stack([pairs[i % uniq][1] for i in range(B)]), np.float16)
-        leg["eng"] = kb.Engine(kb.MODEL_IFNET, kb.make_blob(kb.MODEL_IFNET, leg["flat"]), H, W, max_batch=B,
-                               device=D.local_rank)
+        model = kb.MODEL_RIFE_FUSED if leg["r42"] else kb.MODEL_IFNET
+        leg["eng"] = kb.Engine(model, kb.make_blob(model, leg["flat"]), H, W, max_batch=B, device=D.local_rank)
         leg["eng"].set_timestep(timestep)
         leg["host_in"] = [leg["frames"], leg["frames_b"]]
         leg["out_shape"] = (B, 3, H, W)
@@ -465,17 +497,22 @@ def verify_leg(leg, d_in, d_out):
     if leg["rife"]:
         a = d_in[0][0:1].float().cpu().numpy()
         b = d_in[1][0:1].float().cpu().numpy()
-        hp, wp = -(-H // 32) * 32, -(-W // 32) * 32
+        al = 64 if leg["r42"] else 32
+        hp, wp = -(-H // al) * al, -(-W // al) * al
         top, left = ((hp - H) // 2) & ~1, ((wp - W) // 2) & ~1
         pa = np.zeros((1, 3, hp, wp), np.float32)
         pb = np.zeros((1, 3, hp, wp), np.float32)
         pa[:, :, top:top + H, left:left + W] = a
         pb[:, :, top:top + H, left:left + W] = b
-        ref = torch_ref.ifnet_forward(pa, pb, leg["timestep"], leg["params"])[:, :, top:top + H, left:left + W]
+        if leg["r42"]:
+            ref = torch_ref.rife42_forward(pa, pb, leg["timestep"], leg["flat"])[0][:, :, top:top + H, left:left + W]
+        else:
+            ref = torch_ref.ifnet_forward(pa, pb, leg["timestep"], leg["params"])[:, :, top:top + H, left:left + W]
         got = d_out[0:1].float().cpu().numpy()
         err = float(np.max(np.abs(clamp01(got) - clamp01(ref))))
         torch.cuda.empty_cache()
-        return {"frame": 0, "region": f"whole {W}x{H} frame", "reference": "torch FP32 IFNet (tests/torch_ref.py)",
+        return {"frame": 0, "region": f"whole {W}x{H} frame",
+                "reference": f"torch FP32 {'RIFE 4.25' if leg['r42'] else 'IFNet'} (tests/torch_ref.py)",
                 "max_abs_255": err * 255.0, "ok": bool(err <= 2.0 / 255.0)}
     ch, cw, halo = 64, 128, 24
     y0, x0 = max(0, H // 2 - ch // 2), max(0, W // 2 - cw // 2)
@@ -688,6 +725,7 @@ def run_leg(workload, args, D, B, H, W, steps, headline):
     if D.rank == 0 and D.world == 1 and not args.no_cpu_baseline and cpu_budget(headline, leg):
         fr = leg["frames"][0].astype(np.float32)
         cpu = cpu_baseline(fr, leg["flat"], frame_b=leg["frames_b"][0].astype(np.float32) if leg["rife"] else None,
+                           rife42=leg["r42"],
                            timestep=args.timestep, full=(H, W), with_config0=headline)
     eng.close()
     del d_in, d_out

@@ -55,13 +55,22 @@ typedef struct kb2_tensor {
  * span_fp8::parse does, package.cpp:143); `weights` / `weights_bytes` are then the package file's
  * bytes. KB2_PREC_FP16 runs any package in FP16; KB2_PREC_FP8_E4M3 runs an FP8 package's blocks in
  * E4M3 with its own activation scales. Same frames as KB2_MODEL_SPAN_X2 (even H and W). */
-typedef enum kb2_model { KB2_MODEL_SPAN_X2 = 1, KB2_MODEL_IFNET = 2, KB2_MODEL_SPAN_UNSHUFFLE = 3 } kb2_model;
+/* KB2_MODEL_RIFE_FUSED: RIFE 4.2x (4.25, 4.26, 4.25 lite, 4.22 lite), the reference's fused RIFE
+ * (RifeFusedEngine, src/gpu/cuda/backend/rife_fused_engine.h:41; plan src/kernels/spec/rife_fused.h:
+ * 7-19) on its native block kernels (src/prepare/rife_native.h). Same enqueue contract as
+ * KB2_MODEL_IFNET (image, or the motion variant); weight blob v1 below. */
+typedef enum kb2_model {
+  KB2_MODEL_SPAN_X2 = 1,
+  KB2_MODEL_IFNET = 2,
+  KB2_MODEL_SPAN_UNSHUFFLE = 3,
+  KB2_MODEL_RIFE_FUSED = 4
+} kb2_model;
 typedef enum kb2_precision { KB2_PREC_FP16 = 1, KB2_PREC_FP8_E4M3 = 2 } kb2_precision;
 
 typedef struct kb2_engine kb2_engine;
 
-/* Weight blob v1 (KB2_MODEL_SPAN_X2 and KB2_MODEL_IFNET): a 32-byte header, then the network's
- * float32 parameters back to back, little-endian, in the order below. Conv weights are OIHW
+/* Weight blob v1 (KB2_MODEL_SPAN_X2, KB2_MODEL_IFNET and KB2_MODEL_RIFE_FUSED): a 32-byte header,
+ * then the network's float32 parameters back to back, little-endian, in the order below. Conv weights are OIHW
  * ([out][in][ky][kx]), transposed-conv weights [in][out][ky][kx] (ONNX ConvTranspose), each
  * followed by its bias and, where the layer has one, its PReLU slopes (one per output channel).
  *
@@ -80,6 +89,23 @@ typedef struct kb2_engine kb2_engine;
  *   conv0b      W [C][C/2][3][3],   b [C],   slope [C]     (stride 2)
  *   res j=0..7  W [C][C][3][3],     b [C],   slope [C]     (PReLU(conv(x) + x))
  *   last        W [C][5][4][4],     b [5]                  (transposed, stride 2, pad 1: 4 flow + mask)
+ *
+ * KB2_MODEL_RIFE_FUSED, RIFE 4.2x: 12 plan floats first (exact small integers): blocks B (2..5),
+ * the input reduction d_0..d_4 of each block (powers of two up to 32, d_0 >= 2, d_(B-1) = 1; 0 past
+ * the last block), the block widths C_0..C_4 (32, 64, 96, 128 or 192; 0 past the last block), 16
+ * (the encoder width). RIFE 4.25: 5, 8 8 4 2 1, 192 128 96 64 32. Then, with LeakyReLU written
+ * as per-channel slopes (0.2 each for the published models):
+ *   encoder cnn0 W [16][3][3][3],  b [16], slope [16]   (stride 2)
+ *           cnn1 W [16][16][3][3], b [16], slope [16]
+ *           cnn2 W [16][16][3][3], b [16], slope [16]
+ *           cnn3 W [16][4][4][4],  b [4]                 (transposed, stride 2, pad 1)
+ *   block k: cin = 15 for k = 0 (A rgb, B rgb, encodings of A and B, timestep), 28 after (warped A
+ *   rgb, warped B rgb, warped encodings of A and B, timestep, mask, 8 attributes, flow 4 / d_k):
+ *     conv0a  W [C/2][cin][3][3], b [C/2], slope [C/2]  (stride 2)
+ *     conv0b  W [C][C/2][3][3],   b [C],   slope [C]    (stride 2)
+ *     res j=0..7 W [C][C][3][3],  b [C],   beta [C], slope [C]   (act(beta (conv(x) + b) + x))
+ *     last    W [C][52][4][4],    b [52]                (transposed, stride 2, pad 1; then
+ *                                                         DepthToSpace(2, CRD): flow 4, mask, 8)
  */
 #define KB2_SPAN_X2_PARAMS 389916
 #define KB2_IFNET_PARAMS 5160980

@@ -35,10 +35,10 @@ import numpy as np
 _PKG = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "ultimate-anime-videoplayer_b200")
 if _PKG not in sys.path:
     sys.path.insert(0, _PKG)
-from seeded import (E4M3_MAX, IFNET_CHANNELS, IFNET_RES, IFNET_SCALES, SCALE_HEADROOM, SPAN8_HEADER,  # noqa: E402,F401
-                    SPAN8_IN, SPAN8_PIXEL, SPAN8_STORED, SPAN_BLOCKS, SPAN_C, _crc32, _flat, ifnet_flat,
-                    ifnet_init, ifnet_param_shapes, kaiming, span8_init, span8_package, span_flat, span_init,
-                    span_param_shapes, unflatten)
+from seeded import (E4M3_MAX, IFNET_CHANNELS, IFNET_RES, IFNET_SCALES, RIFE_PLANS, SCALE_HEADROOM,  # noqa: E402,F401
+                    SPAN8_HEADER, SPAN8_IN, SPAN8_PIXEL, SPAN8_STORED, SPAN_BLOCKS, SPAN_C, _crc32, _flat,
+                    ifnet_flat, ifnet_init, ifnet_param_shapes, kaiming, rife_flat, rife_init, rife_param_shapes,
+                    span8_init, span8_package, span_flat, span_init, span_param_shapes, unflatten)
 
 
 # --------------------------------------------------------------------------------------------

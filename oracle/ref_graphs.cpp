@@ -10,11 +10,15 @@
 //    (op_elementwise.cpp), Concat, DepthToSpace CRD (op_pixel.cpp:78);
 //  * classic IFNet 4.x: Conv stride 2, PRelu, ConvTranspose (op_window.cpp:309), Resize linear
 //    half-pixel (op_sample.cpp:139), Slice, GridSample bilinear/border/align-corners
-//    (op_sample.cpp:200).
+//    (op_sample.cpp:200);
+//  * RIFE 4.2x (4.25, 4.26, 4.25 lite, 4.22 lite): the same operators plus DepthToSpace CRD, with the
+//    encoder (cnn0..cnn3) and the IFBlocks of 52-channel Y as the reference's fused RIFE describes them
+//    (src/kernels/spec/rife_fused.h:1-19, src/kernels/ref/rife_fused.cpp).
 //
 // Only tests/, the package's smoke check and bench.py's CPU-baseline leg call it, as the checker or
-// as the timed reference CPU implementation. The parameter order is the one of
-// oracle/nets.py (span_param_shapes / ifnet_param_shapes).
+// as the timed reference CPU implementation. The parameter order is the weight blob's, as the
+// product's C header defines it (include/kirari_b200.h).
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -24,6 +28,7 @@
 #include "gpu/ir/graph.h"
 #include "gpu/ir/interpreter.h"
 #include "gpu/ir/ir.h"
+#include "kernels/ref/rife_fused.h"
 
 namespace ir = kirari::gpu::ir;
 
@@ -177,6 +182,138 @@ int finish(Builder& b, ir::TensorId out, const std::vector<ir::NamedValue>& inpu
   return 0;
 }
 
+
+// The RIFE 4.2x graph and the tensors the checks read.
+struct Rife42Graph {
+  Builder b;
+  int blocks = 0;
+  int reduce[5] = {};
+  int channels[5] = {};
+  ir::TensorId f0 = ir::kNoTensor, f1 = ir::kNoTensor;  // encodings [n,4,h,w]
+  ir::TensorId x[5] = {};                               // block inputs X_k [n,15|28,h/d,w/d]
+  ir::TensorId y[5] = {};                               // block outputs Y_k [n,52,h/2d,w/2d]
+  ir::TensorId image = ir::kNoTensor, flow = ir::kNoTensor, mask = ir::kNoTensor;
+};
+
+bool build_rife42(Rife42Graph& r, int n, int h, int w, float timestep, const float* params, long n_params) {
+  if (n_params < 12) {
+    g_error = "no plan";
+    return false;
+  }
+  r.blocks = static_cast<int>(params[0]);
+  if (r.blocks < 2 || r.blocks > 5 || params[11] != 16.0F) {
+    g_error = "plan";
+    return false;
+  }
+  for (int k = 0; k < r.blocks; ++k) {
+    r.reduce[k] = static_cast<int>(params[1 + k]);
+    r.channels[k] = static_cast<int>(params[6 + k]);
+  }
+  Builder& b = r.b;
+  Params pr{params + 12, n_params - 12};
+  const ir::TensorId i0 = b.input("img0", {n, 3, h, w});
+  const ir::TensorId i1 = b.input("img1", {n, 3, h, w});
+  const ir::TensorId tplane =
+      b.constant({n, 1, h, w}, std::vector<float>(static_cast<std::size_t>(n) * h * w, timestep));
+  ir::AxisAttrs cat_axis;
+  cat_axis.axis = 1;
+  // the encoder (cnn0..cnn3) of both frames: its weights are read once, applied to each frame
+  const long enc_count[4] = {16L * 3 * 9 + 32, 16L * 16 * 9 + 32, 16L * 16 * 9 + 32, 16L * 4 * 16 + 4};
+  std::vector<float> enc_params;
+  for (long c : enc_count) {
+    const std::vector<float> v = pr.take(c);
+    enc_params.insert(enc_params.end(), v.begin(), v.end());
+  }
+  auto encode = [&](ir::TensorId img) {
+    Params ep{enc_params.data(), static_cast<long>(enc_params.size())};
+    ir::TensorId e = prelu(b, ep, conv(b, ep, img, 3, 16, 3, 2, 1), 16);
+    e = prelu(b, ep, conv(b, ep, e, 16, 16, 3, 1, 1), 16);
+    e = prelu(b, ep, conv(b, ep, e, 16, 16, 3, 1, 1), 16);
+    ir::ConvTransposeAttrs ta;
+    ta.strides = {2, 2};
+    ta.pads = {1, 1, 1, 1};
+    const ir::TensorId tw = b.constant({16, 4, 4, 4}, ep.take(16L * 4 * 16));
+    const ir::TensorId tb = b.constant({4}, ep.take(4));
+    return b.node(ir::OpKind::ConvTranspose, {e, tw, tb}, ta);
+  };
+  r.f0 = encode(i0);
+  r.f1 = encode(i1);
+  ir::TensorId flow = ir::kNoTensor;
+  ir::TensorId mask = ir::kNoTensor;
+  ir::TensorId feat = ir::kNoTensor;
+  ir::TensorId w0 = i0;
+  ir::TensorId w1 = i1;
+  ir::TensorId wf0 = r.f0;
+  ir::TensorId wf1 = r.f1;
+  for (int k = 0; k < r.blocks; ++k) {
+    const int c = r.channels[k];
+    const auto d = static_cast<float>(r.reduce[k]);
+    // X_k: 0-2 A, 3-5 B, 6-9 encoding of A, 10-13 of B, 14 timestep (k = 0: unwarped, 15 channels);
+    // k >= 1 warped, then 15 mask, 16-23 attributes of block k-1, 24-27 flow / d
+    ir::TensorId xin = k == 0 ? b.node(ir::OpKind::Concat, {i0, i1, r.f0, r.f1, tplane}, cat_axis)
+                              : b.node(ir::OpKind::Concat, {w0, w1, wf0, wf1, tplane, mask, feat}, cat_axis);
+    const int in_ch = k == 0 ? 15 : 28;
+    if (d != 1.0F) xin = resize(b, xin, 1.0F / d);
+    if (k > 0) {
+      ir::TensorId f = flow;
+      if (d != 1.0F) f = resize(b, f, 1.0F / d);
+      f = b.node(ir::OpKind::Mul, {f, b.scalar(1.0F / d)});
+      xin = b.node(ir::OpKind::Concat, {xin, f}, cat_axis);
+    }
+    r.x[k] = xin;
+    ir::TensorId hdn = prelu(b, pr, conv(b, pr, xin, in_ch, c / 2, 3, 2, 1), c / 2);
+    hdn = prelu(b, pr, conv(b, pr, hdn, c / 2, c, 3, 2, 1), c);
+    for (int j = 0; j < 8; ++j) {  // ResConv: act(conv(x) * beta + x)
+      const ir::TensorId rc = conv(b, pr, hdn, c, c, 3, 1, 1);
+      const ir::TensorId beta = b.constant({1, c, 1, 1}, pr.take(c));
+      hdn = prelu(b, pr, b.node(ir::OpKind::Add, {b.node(ir::OpKind::Mul, {rc, beta}), hdn}), c);
+    }
+    ir::ConvTransposeAttrs ta;
+    ta.strides = {2, 2};
+    ta.pads = {1, 1, 1, 1};
+    const ir::TensorId tw = b.constant({c, 52, 4, 4}, pr.take(static_cast<long>(c) * 52 * 16));
+    const ir::TensorId tb = b.constant({52}, pr.take(52));
+    r.y[k] = b.node(ir::OpKind::ConvTranspose, {hdn, tw, tb}, ta);
+    ir::BlockAttrs d2s;
+    d2s.blocksize = 2;
+    d2s.mode = ir::BlockMode::Crd;
+    ir::TensorId tmp = b.node(ir::OpKind::DepthToSpace, {r.y[k]}, d2s);
+    if (d != 1.0F) tmp = resize(b, tmp, d);
+    const ir::TensorId fd = b.node(ir::OpKind::Mul, {slice_channels(b, tmp, 0, 4), b.scalar(d)});
+    mask = slice_channels(b, tmp, 4, 5);
+    feat = slice_channels(b, tmp, 5, 13);
+    flow = k == 0 ? fd : b.node(ir::OpKind::Add, {flow, fd});
+    const ir::TensorId fa = slice_channels(b, flow, 0, 2);
+    const ir::TensorId fb = slice_channels(b, flow, 2, 4);
+    w0 = warp(b, i0, fa, n, h, w);
+    w1 = warp(b, i1, fb, n, h, w);
+    if (k + 1 < r.blocks) {
+      wf0 = warp(b, r.f0, fa, n, h, w);
+      wf1 = warp(b, r.f1, fb, n, h, w);
+    }
+  }
+  r.mask = b.node(ir::OpKind::Sigmoid, {mask});
+  const ir::TensorId one_minus = b.node(ir::OpKind::Sub, {b.scalar(1.0F), r.mask});
+  r.image = b.node(ir::OpKind::Add, {b.node(ir::OpKind::Mul, {w0, r.mask}),
+                                     b.node(ir::OpKind::Mul, {w1, one_minus})});
+  r.flow = flow;
+  if (!pr.ok || pr.left != 0) {
+    g_error = "parameter count mismatch";
+    return false;
+  }
+  return true;
+}
+
+std::vector<ir::NamedValue> rife42_inputs(const float* img0, const float* img1, int n, int h, int w) {
+  const std::size_t count = static_cast<std::size_t>(n) * 3 * h * w;
+  std::vector<ir::NamedValue> inputs;
+  inputs.push_back(
+      {"img0", ir::Value{.type = ir::DataType::F32, .dims = {n, 3, h, w}, .f = {img0, img0 + count}}});
+  inputs.push_back(
+      {"img1", ir::Value{.type = ir::DataType::F32, .dims = {n, 3, h, w}, .f = {img1, img1 + count}}});
+  return inputs;
+}
+
 }  // namespace
 
 extern "C" {
@@ -312,6 +449,96 @@ int kref_ifnet_forward(const float* img0, const float* img1, int n, int h, int w
     inputs.push_back(
         {"img1", ir::Value{.type = ir::DataType::F32, .dims = {n, 3, h, w}, .f = {img1, img1 + count}}});
     return finish(b, y, inputs, out, count);
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 4;
+  }
+}
+
+// RIFE 4.2x: the plan (blocks, input reduction d_k and width C_k of each block) is the parameter
+// array's first 12 floats [blocks, d_0..d_4, C_0..C_4, 16], then the encoder and the blocks in the
+// order of include/kirari_b200.h (KB2_MODEL_RIFE_FUSED). img0, img1 [n,3,h,w] with h and w multiples
+// of 4 * max d -> out [n,3,h,w]; flow_out [n,4,h,w] and mask_out [n,1,h,w] (after the sigmoid) when
+// not null.
+int kref_rife42_forward(const float* img0, const float* img1, int n, int h, int w, float timestep,
+                        const float* params, long n_params, float* out, float* flow_out, float* mask_out) {
+  try {
+    Rife42Graph r;
+    if (!build_rife42(r, n, h, w, timestep, params, n_params)) return 1;
+    r.b.g.outputs = {r.image, r.flow, r.mask};
+    auto result = ir::run(r.b.g, rife42_inputs(img0, img1, n, h, w));
+    if (!result) {
+      g_error = result.error().detail;
+      return 2;
+    }
+    const std::size_t plane = static_cast<std::size_t>(n) * h * w;
+    const std::size_t sizes[3] = {3 * plane, 4 * plane, plane};
+    float* dst[3] = {out, flow_out, mask_out};
+    for (int i = 0; i < 3; ++i) {
+      const ir::Value& v = (*result)[static_cast<std::size_t>(i)].value;
+      if (v.f.size() != sizes[i]) {
+        g_error = "unexpected output size";
+        return 3;
+      }
+      if (dst[i] != nullptr) std::memcpy(dst[i], v.f.data(), sizes[i] * sizeof(float));
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 4;
+  }
+}
+
+// Pins the graph above against the reference's own double-precision statement of the fused RIFE
+// glue (src/kernels/ref/rife_fused.cpp: rife_fused_block_input, rife_fused_finish): one frame pair
+// runs through the graph, its encodings and Y_k are handed to the reference's glue, and
+// err[k] (k < blocks) = max |X_k graph - X_k reference|, err[blocks .. blocks + 2] = the same for the
+// final image, flow and mask.
+int kref_rife42_glue_check(const float* img0, const float* img1, int h, int w, float timestep, const float* params,
+                           long n_params, double* err) {
+  try {
+    Rife42Graph r;
+    if (!build_rife42(r, 1, h, w, timestep, params, n_params)) return 1;
+    const int blocks = r.blocks;
+    r.b.g.outputs = {r.f0, r.f1, r.image, r.flow, r.mask};
+    for (int k = 0; k < blocks; ++k) r.b.g.outputs.push_back(r.y[k]);
+    for (int k = 0; k < blocks; ++k) r.b.g.outputs.push_back(r.x[k]);
+    auto result = ir::run(r.b.g, rife42_inputs(img0, img1, 1, h, w));
+    if (!result) {
+      g_error = result.error().detail;
+      return 2;
+    }
+    auto value = [&](std::size_t i) -> const std::vector<float>& { return (*result)[i].value.f; };
+    namespace kr = kirari::kernels::ref;
+    kr::RifeFusedState st;
+    st.plan.blocks = blocks;
+    for (int k = 0; k < blocks; ++k) st.plan.reduce[static_cast<std::size_t>(k)] = r.reduce[k];
+    st.height = h;
+    st.width = w;
+    const std::size_t area = static_cast<std::size_t>(h) * w;
+    st.input.assign(11 * area, 0.0);
+    for (std::size_t i = 0; i < 3 * area; ++i) {
+      st.input[i] = img0[i];
+      st.input[3 * area + i] = img1[i];
+    }
+    for (std::size_t i = 0; i < area; ++i) st.input[6 * area + i] = timestep;
+    st.encode.assign(value(0).begin(), value(0).end());
+    st.encode.insert(st.encode.end(), value(1).begin(), value(1).end());
+    for (int k = 0; k < blocks; ++k)
+      st.y.emplace_back(value(5 + static_cast<std::size_t>(k)).begin(), value(5 + static_cast<std::size_t>(k)).end());
+    auto max_diff = [](const std::vector<double>& a, const std::vector<float>& b) {
+      if (a.size() != b.size()) return 1e30;
+      double m = 0.0;
+      for (std::size_t i = 0; i < a.size(); ++i) m = std::max(m, std::fabs(a[i] - static_cast<double>(b[i])));
+      return m;
+    };
+    for (int k = 0; k < blocks; ++k)
+      err[k] = max_diff(kr::rife_fused_block_input(st, k), value(5 + static_cast<std::size_t>(blocks + k)));
+    const kr::RifeFusedResult fin = kr::rife_fused_finish(st);
+    err[blocks] = max_diff(fin.image, value(2));
+    err[blocks + 1] = max_diff(fin.flow, value(3));
+    err[blocks + 2] = max_diff(fin.mask, value(4));
+    return 0;
   } catch (const std::exception& e) {
     g_error = e.what();
     return 4;

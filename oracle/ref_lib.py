@@ -70,6 +70,50 @@ def ifnet_forward(img0, img1, timestep, flat_params):
     return out
 
 
+def _rife42_bind(L):
+    if not hasattr(L, "_rife42"):
+        i = ctypes.c_int
+        L.kref_rife42_forward.argtypes = [_fp, _fp, i, i, i, ctypes.c_float, _fp, ctypes.c_long, _fp, _fp, _fp]
+        L.kref_rife42_glue_check.argtypes = [_fp, _fp, i, i, ctypes.c_float, _fp, ctypes.c_long,
+                                             ctypes.POINTER(ctypes.c_double)]
+        L._rife42 = True
+    return L
+
+
+def rife42_forward(img0, img1, timestep, flat_params):
+    """RIFE 4.2x through the reference's interpreter: (image [n,3,h,w], flow [n,4,h,w], sigmoid(mask)
+    [n,1,h,w]); flat_params starts with the 12 plan floats."""
+    L = _rife42_bind(lib())
+    a = np.ascontiguousarray(img0, np.float32)
+    b = np.ascontiguousarray(img1, np.float32)
+    p = np.ascontiguousarray(flat_params, np.float32)
+    n, _, h, w = a.shape
+    out = np.empty((n, 3, h, w), np.float32)
+    flow = np.empty((n, 4, h, w), np.float32)
+    mask = np.empty((n, 1, h, w), np.float32)
+    rc = L.kref_rife42_forward(_ptr(a), _ptr(b), n, h, w, timestep, _ptr(p), p.size, _ptr(out), _ptr(flow),
+                               _ptr(mask))
+    if rc != 0:
+        raise RuntimeError(f"kref_rife42_forward: {rc} {L.kref_last_error().decode()}")
+    return out, flow, mask
+
+
+def rife42_glue_check(img0, img1, timestep, flat_params):
+    """Max differences between the graph's X_k / image / flow / mask and the reference's own
+    double-precision fused-RIFE glue (src/kernels/ref/rife_fused.cpp), on the first frame pair."""
+    L = _rife42_bind(lib())
+    a = np.ascontiguousarray(img0[0], np.float32)
+    b = np.ascontiguousarray(img1[0], np.float32)
+    p = np.ascontiguousarray(flat_params, np.float32)
+    _, h, w = a.shape
+    blocks = int(p[0])
+    err = (ctypes.c_double * (blocks + 3))()
+    rc = L.kref_rife42_glue_check(_ptr(a), _ptr(b), h, w, timestep, _ptr(p), p.size, err)
+    if rc != 0:
+        raise RuntimeError(f"kref_rife42_glue_check: {rc} {L.kref_last_error().decode()}")
+    return list(err)
+
+
 def _span8_bind(L):
     if getattr(L, "_span8_bound", False):
         return L

@@ -1,9 +1,10 @@
 """Pins the torch FP32 SPAN reference (tests/torch_ref.py, used by the full-size GPU tests) to the
 numpy oracle and to the reference interpreter's fixtures, on the CPU."""
 import numpy as np
+import pytest
 
 import torch_ref
-from oracle import nets
+from oracle import nets, ref_lib
 from util import golden
 
 
@@ -49,3 +50,17 @@ def test_torch_ifnet_reference_matches_reference_golden():
     g = golden("ifnet_64x96_t05.npz")
     got = torch_ref.ifnet_forward(g["a"], g["b"], float(g["t"]), nets.ifnet_init(2), device="cpu")
     assert float(np.max(np.abs(got - g["out"]))) < 1e-4
+
+
+@pytest.mark.skipif(not ref_lib.available(), reason="oracle/_ref not built (needs the reference sources)")
+@pytest.mark.parametrize("name", ["4.25", "4.22lite"])
+def test_torch_rife42_reference_matches_the_interpreter(name):
+    from synth import shifted_pair
+    plan = nets.RIFE_PLANS[name]
+    flat = nets.rife_flat(nets.rife_init(plan), plan)
+    a, b = shifted_pair(64, 128, seed=9)
+    got, flow, mask = torch_ref.rife42_forward(a[None], b[None], 0.4, flat, device="cpu")
+    ref, rflow, rmask = ref_lib.rife42_forward(a[None], b[None], 0.4, flat)
+    assert float(np.max(np.abs(got - ref))) < 1e-4
+    assert float(np.max(np.abs(flow - rflow))) < 1e-3
+    assert float(np.max(np.abs(mask - rmask))) < 1e-4

@@ -1,4 +1,4 @@
-"""FP32 PyTorch references of canonical SPAN x2 and classic IFNet, for parity at full frame sizes
+"""FP32 PyTorch references of canonical SPAN x2, classic IFNet and RIFE 4.2x, for parity at full frame sizes
 (test aid only: the tests and bench.py's output check use them, the product never does).
 
 The numpy oracle (oracle/nets.py, pinned to the reference's interpreter) needs minutes for one
@@ -122,3 +122,69 @@ def ifnet_forward(img0, img1, timestep, p, device="cuda", return_flow=False):
     if return_flow:
         return out.cpu().numpy(), flow.cpu().numpy(), mask.cpu().numpy()
     return out.cpu().numpy()
+
+
+def rife42_forward(img0, img1, timestep, flat, device="cuda"):
+    """RIFE 4.2x (oracle/ref_graphs.cpp kref_rife42_forward) in torch FP32 on one pair img0, img1
+    [1,3,h,w] (h, w multiples of 4 * max d): (image [1,3,h,w], flow [1,4,h,w], sigmoid(mask)
+    [1,1,h,w]) as numpy. flat: the C ABI's parameter array (12 plan floats first)."""
+    import torch
+    import torch.nn.functional as F
+    _fp32_mode()
+    flat = np.asarray(flat, np.float32)
+    blocks = int(flat[0])
+    plan = (blocks, tuple(int(v) for v in flat[1:1 + blocks]), tuple(int(v) for v in flat[6:6 + blocks]))
+    p = seeded.unflatten(flat[seeded.RIFE_PLAN_FLOATS:], seeded.rife_param_shapes(plan))
+    w = {k: torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device) for k, v in p.items()}
+    a = torch.as_tensor(np.asarray(img0, np.float32)).to(device)
+    b = torch.as_tensor(np.asarray(img1, np.float32)).to(device)
+    _, _, h, wd = a.shape
+    t = torch.full((1, 1, h, wd), float(timestep), device=device)
+
+    def resize(x, hh, ww):
+        return F.interpolate(x, size=(hh, ww), mode="bilinear", align_corners=False)
+
+    def act(x, name):
+        return F.prelu(x, w[name + ".slope"])
+
+    def encode(x):
+        e = act(F.conv2d(x, w["enc.cnn0.w"], w["enc.cnn0.b"], stride=2, padding=1), "enc.cnn0")
+        e = act(F.conv2d(e, w["enc.cnn1.w"], w["enc.cnn1.b"], padding=1), "enc.cnn1")
+        e = act(F.conv2d(e, w["enc.cnn2.w"], w["enc.cnn2.b"], padding=1), "enc.cnn2")
+        return F.conv_transpose2d(e, w["enc.cnn3.w"], w["enc.cnn3.b"], stride=2, padding=1)
+
+    def block(x, flow, d, k):
+        if d != 1:
+            x = resize(x, h // d, wd // d)
+        if flow is not None:
+            f = resize(flow, h // d, wd // d) if d != 1 else flow
+            x = torch.cat([x, f * (1.0 / d)], 1)
+        y = act(F.conv2d(x, w[f"b{k}.conv0a.w"], w[f"b{k}.conv0a.b"], stride=2, padding=1), f"b{k}.conv0a")
+        y = act(F.conv2d(y, w[f"b{k}.conv0b.w"], w[f"b{k}.conv0b.b"], stride=2, padding=1), f"b{k}.conv0b")
+        for j in range(seeded.IFNET_RES):
+            r = F.conv2d(y, w[f"b{k}.res{j}.w"], w[f"b{k}.res{j}.b"], padding=1)
+            y = act(r * w[f"b{k}.res{j}.beta"][None, :, None, None] + y, f"b{k}.res{j}")
+        tmp = F.pixel_shuffle(F.conv_transpose2d(y, w[f"b{k}.last.w"], w[f"b{k}.last.b"], stride=2, padding=1), 2)
+        if d != 1:
+            tmp = resize(tmp, h, wd)
+        return tmp[:, :4] * float(d), tmp[:, 4:5], tmp[:, 5:13]
+
+    with torch.no_grad():
+        fa, fb = encode(a), encode(b)
+        flow = mask = feat = None
+        w0, w1, wf0, wf1 = a, b, fa, fb
+        for k in range(blocks):
+            d = plan[1][k]
+            if k == 0:
+                flow, mask, feat = block(torch.cat([a, b, fa, fb, t], 1), None, d, k)
+            else:
+                fd, mask, feat = block(torch.cat([w0, w1, wf0, wf1, t, mask, feat], 1), flow, d, k)
+                flow = flow + fd
+            w0 = _warp(a, flow[0, 0], flow[0, 1])
+            w1 = _warp(b, flow[0, 2], flow[0, 3])
+            if k + 1 < blocks:
+                wf0 = _warp(fa, flow[0, 0], flow[0, 1])
+                wf1 = _warp(fb, flow[0, 2], flow[0, 3])
+        m = torch.sigmoid(mask)
+        out = w0 * m + w1 * (1 - m)
+    return out.cpu().numpy(), flow.cpu().numpy(), m.cpu().numpy()

@@ -6,6 +6,7 @@
 
 #include "engine.h"
 #include "ifnet_net.h"
+#include "rife_net.h"
 #include "span8_net.h"
 #include "span_net.h"
 #include "span_tiles.h"
@@ -372,10 +373,12 @@ class SpanEngine final : public Engine {
   std::unique_ptr<DeviceBuffer> tile_in_, tile_out_;
 };
 
-class IfnetEngine final : public Engine {
+// The interpolators: classic IFNet (IfnetNet) and RIFE 4.2x (RifeNet), the same enqueue contract.
+template <class Net>
+class InterpEngine final : public Engine {
  public:
   Status init(const kb2_engine_desc& d, const std::vector<float>& params) {
-    if (d.precision != KB2_PREC_FP16) return refuse(KB2_FORMAT_UNSUPPORTED, "IFNet runs in FP16 only");
+    if (d.precision != KB2_PREC_FP16) return refuse(KB2_FORMAT_UNSUPPORTED, "the interpolators run in FP16 only");
     return net_.create(params, d.max_batch, d.height, d.width);
   }
   std::vector<std::string> input_names() const override { return {"img0", "img1"}; }
@@ -434,7 +437,7 @@ class IfnetEngine final : public Engine {
   int* err_word() const override { return net_.err_word(); }
 
  private:
-  IfnetNet net_;
+  Net net_;
 };
 
 // The unshuffle SPAN of a .span8 package (KB2_MODEL_SPAN_UNSHUFFLE): FP16, or E4M3 blocks for an FP8
@@ -505,7 +508,8 @@ class Span8Engine final : public Engine {
 
 Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
   // Everything that needs no device is checked first: the blob and the shapes.
-  if (d.model != KB2_MODEL_SPAN_X2 && d.model != KB2_MODEL_IFNET && d.model != KB2_MODEL_SPAN_UNSHUFFLE)
+  if (d.model != KB2_MODEL_SPAN_X2 && d.model != KB2_MODEL_IFNET && d.model != KB2_MODEL_SPAN_UNSHUFFLE &&
+      d.model != KB2_MODEL_RIFE_FUSED)
     return refuse(KB2_FORMAT_UNSUPPORTED, "unknown model");
   std::vector<float> params;
   Span8Package pkg;
@@ -513,6 +517,10 @@ Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
     KB2_TRY(parse_span8(d.weights, d.weights_bytes, pkg));
   else
     KB2_TRY(parse_blob(d.weights, d.weights_bytes, d.model, params));
+  if (d.model == KB2_MODEL_RIFE_FUSED) {
+    RifePlan plan;
+    KB2_TRY(rife_read_plan(params, plan));
+  }
   if (d.max_batch < 1 || d.height < 1 || d.width < 1 || d.height > 8192 || d.width > 8192)
     return refuse(KB2_SHAPE_INVALID, "frame size or batch out of contract");
   int count = 0;
@@ -537,7 +545,13 @@ Status make_engine(const kb2_engine_desc& d, std::unique_ptr<Engine>& out) {
     return Status::Ok();
   }
   if (d.model == KB2_MODEL_IFNET) {
-    auto e = std::make_unique<IfnetEngine>();
+    auto e = std::make_unique<InterpEngine<IfnetNet>>();
+    KB2_TRY(e->init(d, params));
+    out = std::move(e);
+    return Status::Ok();
+  }
+  if (d.model == KB2_MODEL_RIFE_FUSED) {
+    auto e = std::make_unique<InterpEngine<RifeNet>>();
     KB2_TRY(e->init(d, params));
     out = std::move(e);
     return Status::Ok();

@@ -19,7 +19,9 @@
 //  * Warp 0: producer. Warp 1: TMEM owner + MMA issuer. Warps 2..9: epilogue, two per TMEM lane
 //    quadrant, each half of the columns. The accumulator is double-buffered in TMEM. Fused
 //    epilogues: bias + PReLU; bias + residual + PReLU; transposed-conv phases scattered as FP32
-//    pixels of 8 floats (+ bias; 5 used).
+//    pixels of 8 floats (+ bias; 5 used); for RIFE 4.2x, the encoder's transposed conv as FP16
+//    pixels of 4 channels, and the blocks' transposed conv with the DepthToSpace(2) after it folded
+//    into the store (Z pixels of 16 FP16 channels, 13 used).
 #pragma once
 
 #include "tc_common.cuh"
@@ -30,13 +32,21 @@ enum IfEpi : int {
   kIfPrelu = 0,     // PReLU(acc + bias)
   kIfResPrelu = 1,  // PReLU(acc + bias + residual), residual = the conv input (same shape)
   kIfConvT = 2,     // 4 phases x 8 columns (5 used): out[co][2y+py][2x+px] = acc + bias, FP32 planes
+  // RIFE 4.2x encoder cnn3: 4 phases x 8 columns (4 used): acc + bias as one 8-byte FP16 pixel of 4
+  // channels at (2y + py, 2x + px) of an image [n][2 h_out][2 w_out] (`out`)
+  kIfConvTEnc = 3,
+  // RIFE 4.2x block transposed conv to Y (52 channels) and DepthToSpace(2, CRD) to Z (13 channels):
+  // column n = 64 phase + 16 (2 qy + qx) + c holds Y channel 4 c + 2 qy + qx of ConvT output phase
+  // (py, px) = (phase / 2, phase % 2), i.e. Z channel c of Z pixel (4y + 2py + qy, 4x + 2px + qx);
+  // acc + bias stored as Z pixels of 16 FP16 (32 bytes, c < 13 used) [n][4 h_out][4 w_out] (`out`)
+  kIfConvTZ = 4,
 };
 
 constexpr int kIfEpiWarps = 8;
 constexpr int kIfThreads = 64 + 32 * kIfEpiWarps;
 constexpr int kIfMaxStages = 4;
 constexpr int kIfStrip = 126;  // output pixels per item: the shifted A tiles stay in a 128-pixel box
-constexpr int kIfMaxN = 192;
+constexpr int kIfMaxN = 256;
 constexpr uint32_t kIfChunkBytes = 128 * 16;  // one chunk of a 128-pixel box
 
 struct IfConvArgs {
@@ -57,6 +67,7 @@ struct IfConvArgs {
   int out_split;            // 1: each chunk row stored parity-split, even pixels then odd (the
                             // layout a stride-2 conv reads); w_out even
   float* out_f32;  // kIfConvT: FP32 [n][2 h_out][2 w_out][8] (5 used: flow x0 y0 x1 y1, mask)
+                   // (kIfConvTEnc / kIfConvTZ store through `out`, their layouts above)
   int* err;
 };
 
@@ -65,11 +76,15 @@ struct IfMaps {
                   // {W u64, 2 parities, chunks, batch*H}
 };
 
-constexpr uint32_t kIfSmemExtra = 1024 + 16 * 8 + 16 + 2 * kIfMaxN * 4;
+// Dynamic shared memory of a launch besides its ring: alignment slack, barriers, the TMEM holder,
+// bias and slopes of N columns (at least 192 columns' room, the budget of the classic layers).
+__host__ __device__ constexpr uint32_t if_smem_extra(int n) {
+  return 1024 + 16 * 8 + 16 + 2 * static_cast<uint32_t>(n > 192 ? n : 192) * 4;
+}
 
 template <int kN>
 struct IfShape {
-  static_assert(kN % 16 == 0 && kN >= 32 && kN <= kIfMaxN, "N");
+  static_assert(kN % 16 == 0 && kN >= 16 && kN <= kIfMaxN, "N");
   static constexpr uint32_t tmem_cols = 2 * kN <= 64 ? 64 : (2 * kN <= 128 ? 128 : (2 * kN <= 256 ? 256 : 512));
   static constexpr int groups_per_warp = kN / 16;  // 8-column groups per epilogue warp (half of N)
 };
@@ -115,7 +130,7 @@ __global__ void __launch_bounds__(kIfThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   float* s_bias = reinterpret_cast<float*>(tmem_holder + 4);
-  float* s_slope = s_bias + kIfMaxN;
+  float* s_slope = s_bias + kN;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -291,6 +306,21 @@ __global__ void __launch_bounds__(kIfThreads, 1)
           float* dst = a.out_f32 + ((static_cast<size_t>(n) * (2 * a.h_out) + 2 * oy + py) * (2 * a.w_out) + (2 * x + px)) * 8;
           *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
           *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], 0.0f, 0.0f, 0.0f);
+        } else if constexpr (kEpi == kIfConvTEnc) {
+          const int py = cg >> 1, px = cg & 1;
+          const size_t pix = (static_cast<size_t>(n) * (2 * a.h_out) + 2 * oy + py) * (2 * a.w_out) + (2 * x + px);
+          *reinterpret_cast<uint2*>(a.out + pix * 8) = make_uint2(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]));
+        } else if constexpr (kEpi == kIfConvTZ) {
+          const int phase = cg >> 3, par = (cg >> 1) & 3, part = cg & 1;
+          const int zy = 4 * oy + 2 * (phase >> 1) + (par >> 1);
+          const int zx = 4 * x + 2 * (phase & 1) + (par & 1);
+          const size_t pix = (static_cast<size_t>(n) * (4 * a.h_out) + zy) * (4 * a.w_out) + zx;
+          uint4 o;
+          o.x = pack_half2(v[0], v[1]);
+          o.y = pack_half2(v[2], v[3]);
+          o.z = pack_half2(v[4], v[5]);
+          o.w = pack_half2(v[6], v[7]);
+          *reinterpret_cast<uint4*>(a.out + pix * 32 + part * 16) = o;
         } else {
           const size_t pix = ((static_cast<size_t>(n) * a.h_out + oy) * a.out_chunks + cg) * a.w_out + xs;
           if constexpr (kEpi == kIfResPrelu) {

@@ -31,6 +31,7 @@ KB2_F32, KB2_F16, KB2_U8, KB2_I8 = 0, 1, 2, 3
 MODEL_SPAN_X2 = 1
 MODEL_IFNET = 2
 MODEL_SPAN_UNSHUFFLE = 3  # weights: the bytes of a .span8 package
+MODEL_RIFE_FUSED = 4  # RIFE 4.2x: 12 plan floats, then the parameters
 DISPLAY_RGBA16, DISPLAY_RGB10A2, DISPLAY_RGB10A2_DITHER = 1, 2, 3
 PREC_FP16 = 1
 PREC_FP8 = 2

@@ -18,6 +18,18 @@ SPAN_BLOCKS = 6
 IFNET_CHANNELS = (192, 128, 96, 64)
 IFNET_SCALES = (8, 4, 2, 1)
 IFNET_RES = 8
+# RIFE 4.2x plans (the reference's fused RIFE, src/kernels/spec/rife_fused.h:7-12): blocks, the input
+# reduction d_k of each block and its width C_k. The widths are the models' own (4.25: 192 .. 32);
+# the lite models' widths are read from their weights by the importer, these are stand-ins.
+RIFE_PLANS = {
+    "4.25": (5, (8, 8, 4, 2, 1), (192, 128, 96, 64, 32)),
+    "4.26": (5, (16, 8, 4, 2, 1), (192, 128, 96, 64, 32)),
+    "4.25lite": (5, (32, 16, 8, 4, 1), (128, 96, 64, 32, 32)),
+    "4.22lite": (4, (8, 4, 2, 1), (128, 96, 64, 32)),
+}
+RIFE_ENC = 16        # encoder width (cnn0..cnn2), 4 planes out per frame
+RIFE_Y = 52          # Y_k channels (13 after DepthToSpace(2): flow 4, mask 1, attributes 8)
+RIFE_PLAN_FLOATS = 12
 E4M3_MAX = 448.0
 SCALE_HEADROOM = 1.25
 
@@ -61,6 +73,70 @@ def ifnet_param_shapes():
                     (f"b{k}.res{j}.slope", (c,))]
         out += [(f"b{k}.last.w", (c, 5, 4, 4)), (f"b{k}.last.b", (5,))]
     return out
+
+
+def rife_plan_floats(plan):
+    """The 12 leading floats of a RIFE 4.2x parameter array: blocks, d_0..d_4, C_0..C_4, 16."""
+    blocks, reduce, channels = plan
+    v = np.zeros(RIFE_PLAN_FLOATS, np.float32)
+    v[0] = blocks
+    v[1:1 + blocks] = reduce
+    v[6:6 + blocks] = channels
+    v[11] = RIFE_ENC
+    return v
+
+
+def rife_param_shapes(plan):
+    """[(name, shape)] of RIFE 4.2x after its plan floats: the encoder cnn0..cnn2 (3x3, + slopes) and
+    cnn3 (4x4 stride-2 transposed, [Cin, Cout, kh, kw]); per block conv0a / conv0b (3x3 stride 2, +
+    slopes), 8 ResConv (W, b, beta, slopes: act(beta * (conv + b) + x)) and the transposed conv to
+    52 channels."""
+    blocks, reduce, channels = plan
+    e = RIFE_ENC
+    out = [("enc.cnn0.w", (e, 3, 3, 3)), ("enc.cnn0.b", (e,)), ("enc.cnn0.slope", (e,))]
+    for j in (1, 2):
+        out += [(f"enc.cnn{j}.w", (e, e, 3, 3)), (f"enc.cnn{j}.b", (e,)), (f"enc.cnn{j}.slope", (e,))]
+    out += [("enc.cnn3.w", (e, 4, 4, 4)), ("enc.cnn3.b", (4,))]
+    for k in range(blocks):
+        c = channels[k]
+        cin = 15 if k == 0 else 28
+        out += [(f"b{k}.conv0a.w", (c // 2, cin, 3, 3)), (f"b{k}.conv0a.b", (c // 2,)),
+                (f"b{k}.conv0a.slope", (c // 2,))]
+        out += [(f"b{k}.conv0b.w", (c, c // 2, 3, 3)), (f"b{k}.conv0b.b", (c,)), (f"b{k}.conv0b.slope", (c,))]
+        for j in range(IFNET_RES):
+            out += [(f"b{k}.res{j}.w", (c, c, 3, 3)), (f"b{k}.res{j}.b", (c,)), (f"b{k}.res{j}.beta", (c,)),
+                    (f"b{k}.res{j}.slope", (c,))]
+        out += [(f"b{k}.last.w", (c, RIFE_Y, 4, 4)), (f"b{k}.last.b", (RIFE_Y,))]
+    return out
+
+
+def rife_flat(params, plan):
+    """The C ABI's parameter array of KB2_MODEL_RIFE_FUSED: plan floats, then the parameters."""
+    return np.concatenate([rife_plan_floats(plan), _flat(params, rife_param_shapes(plan))])
+
+
+def rife_init(plan, seed=3, res_gain=1.0, last_gain=0.3, bias_std=0.02):
+    """Seeded RIFE 4.2x weights: Kaiming-normal convs, LeakyReLU slopes 0.2 (the models'
+    activation), ResConv betas drawn in [0.1, 0.3] (so the residual stack neither vanishes nor
+    explodes), a small gain on the transposed convs (flows of a few pixels), small biases."""
+    rng = np.random.default_rng(seed)
+    p = {}
+    for name, shape in rife_param_shapes(plan):
+        if name.endswith(".slope"):
+            p[name] = np.full(shape, 0.2, np.float32)
+        elif name.endswith(".beta"):
+            p[name] = rng.uniform(0.1, 0.3, shape).astype(np.float32)
+        elif name.endswith(".b"):
+            p[name] = (rng.standard_normal(shape) * bias_std).astype(np.float32)
+        elif ".last." in name:
+            p[name] = kaiming(rng, shape, shape[0] * 4, gain=last_gain)
+        elif name == "enc.cnn3.w":
+            p[name] = kaiming(rng, shape, shape[0] * 4, gain=1.0)
+        elif ".res" in name:
+            p[name] = kaiming(rng, shape, int(np.prod(shape[1:])), gain=res_gain)
+        else:
+            p[name] = kaiming(rng, shape, int(np.prod(shape[1:])))
+    return p
 
 
 def _flat(params, shapes):
