@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--family", default="all", help="--workload kernels: all or one of " + ", ".join(
-        ("span16", "span8", "rife", "warp", "janai", "janai8")))
+        ("span16", "span8", "rife", "rife425", "warp", "janai", "janai8")))
     a = ap.parse_args()
     if a.workload == "kernels" and "--batch" not in sys.argv:
         a.batch = 1
@@ -1134,14 +1134,15 @@ def run_warp_reference(args):
 # ------------------------------------------------------------------------------------------------
 # one small pass of every kernel kind, for the per-kernel ncu summaries under profiles/
 # ------------------------------------------------------------------------------------------------
-KERNEL_FAMILIES = ("span16", "span8", "rife", "warp", "janai", "janai8")
+KERNEL_FAMILIES = ("span16", "span8", "rife", "rife425", "warp", "janai", "janai8")
 
 
 def run_kernels(args):
     """Each family runs once, batch `--batch` (1 by default here) at 1920x1080, so that every
     tensor of the SPAN and IFNet paths is larger than L2 while the process holds a few GB: span16
     (the FP16 engine, F16 frames then display pixels), span8 (the E4M3 engine, after one FP16
-    calibration pass), rife (IFNet image and motion variants), warp (kb2_warp_blend_at bilinear,
+    calibration pass), rife (IFNet image and motion variants), rife425 (RIFE 4.25 image and motion
+    variants), warp (kb2_warp_blend_at bilinear,
     Catmull-Rom and pan-locked, kb2_warp_blend_poses, kb2_flow_max, kb2_pack_display), janai /
     janai8 (the unshuffle SPAN b8f64). Prints one JSON line with each family's kernel launches and
     device time; not a benchmark line."""
@@ -1197,6 +1198,16 @@ def run_kernels(args):
             out = torch.empty((B, 3, H, W), dtype=torch.float16, device="cuda")
             timed("rife", lambda: (eng.enqueue([a, b], [out], stream), eng.launches_per_enqueue())[1])
             timed("rife.motion", lambda: (eng.motion(a, b, stream=stream), eng.launches_per_enqueue())[1])
+            eng.check_device(stream)
+            eng.close()
+        elif fam == "rife425":
+            fa, fb = shifted_pair(H, W, seed=3)
+            a = torch.from_numpy(np.ascontiguousarray(np.repeat(fa[None], B, 0), np.float16)).cuda()
+            b = torch.from_numpy(np.ascontiguousarray(np.repeat(fb[None], B, 0), np.float16)).cuda()
+            eng = kb.Engine(kb.MODEL_RIFE_FUSED, kb.make_blob(kb.MODEL_RIFE_FUSED, rife42_flat()), H, W, max_batch=B)
+            out = torch.empty((B, 3, H, W), dtype=torch.float16, device="cuda")
+            timed("rife425", lambda: (eng.enqueue([a, b], [out], stream), eng.launches_per_enqueue())[1])
+            timed("rife425.motion", lambda: (eng.motion(a, b, stream=stream), eng.launches_per_enqueue())[1])
             eng.check_device(stream)
             eng.close()
         elif fam == "warp":

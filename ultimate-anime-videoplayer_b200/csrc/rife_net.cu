@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <string>
 
 #include "if_layer.h"
 #include "rife_glue.cuh"
@@ -31,6 +32,21 @@ constexpr int kRifeRes = 8;
 constexpr int kRifeEnc = 16;
 constexpr int kRifeY = 52;
 constexpr size_t kRifePlanFloats = 12;
+
+// The motion kernel of a plan whose last block is `last`.
+template <typename T, class Finish>
+Status launch_motion(dim3 g, cudaStream_t stream, const IfFrames& F, const RifeZ& Z, int last, int batch,
+                     const Finish& f) {
+  T* flow = static_cast<T*>(f.flow);
+  T* mask = static_cast<T*>(f.mask);
+  switch (last) {
+    case 1: rife_motion_kernel<1, T><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, flow, mask); break;
+    case 2: rife_motion_kernel<2, T><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, flow, mask); break;
+    case 3: rife_motion_kernel<3, T><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, flow, mask); break;
+    default: rife_motion_kernel<4, T><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, flow, mask); break;
+  }
+  return cuda_status(cudaGetLastError(), "RIFE motion launch");
+}
 
 bool block_width_ok(int c) { return c == 32 || c == 64 || c == 96 || c == 128 || c == 192; }
 
@@ -111,8 +127,9 @@ Status RifeNet::create(const std::vector<float>& params, int max_batch, int H, i
   KB2_CUDA(cudaMemset(err_.ptr, 0, sizeof(int)));
   int* err = err_.as<int>();
   k_pad_ = timer_.kind("rife.pad");
-  k_enc_ = timer_.kind("rife.encoder");
-  k_glue_ = timer_.kind("rife.glue");
+  const int k_enc0 = timer_.kind("rife.enc.cnn0"), k_enc12 = timer_.kind("rife.enc.cnn12"),
+            k_enc3 = timer_.kind("rife.enc.cnn3");
+  for (int k = 0; k < plan_.blocks; ++k) k_glue_[k] = timer_.kind(("rife.glue.b" + std::to_string(k)).c_str());
   k_c0a_ = timer_.kind("rife.conv0a");
   k_c0b_ = timer_.kind("rife.conv0b");
   k_res_ = timer_.kind("rife.res");
@@ -253,7 +270,8 @@ Status RifeNet::create(const std::vector<float>& params, int max_batch, int H, i
     lt->kind = k_ct_;
     L.push_back(std::move(lt));
   }
-  for (auto& l : enc_layers_) l->kind = k_enc_;
+  for (size_t i = 0; i < enc_layers_.size(); ++i)
+    enc_layers_[i]->kind = i == 0 ? k_enc0 : i + 1 == enc_layers_.size() ? k_enc3 : k_enc12;
   if (static_cast<size_t>(p - params.data()) != params.size())
     return refuse(KB2_WEIGHTS_INVALID, "RIFE 4.2x: parameter layout mismatch");
   return Status::Ok();
@@ -326,39 +344,45 @@ Status RifeNet::run_impl(cudaStream_t stream, const void* img0, const void* img1
   KB2_CUDA(cudaGetLastError());
   KB2_TRY(timer_.end(k_pad_, 0.0, full_px * (12.0 + 2 * 8.0 + 2 * 16.0), stream));
   for (auto& l : enc_layers_) KB2_TRY(timed(*l, 2 * batch));
+  auto runs = [](int rows) { return (rows + kRifeRunRows - 1) / kRifeRunRows; };
   for (int k = 0; k < plan_.blocks; ++k) {
     const int d = plan_.reduce[k];
     const int ho = Hp_ / d, wo = Wp_ / d;
-    const dim3 g = row_grid(d >= 2 ? 4 * wo : wo, batch * ho);
+    const dim3 g = row_grid(d >= 2 ? 4 * wo : wo, batch * runs(ho));
     const double px = static_cast<double>(batch) * ho * wo;
+    const float t = timestep_;
     KB2_TRY(timer_.begin(stream));
-    if (k == 0)
-      rife_block_input_kernel<15><<<g, kGlueThreads, 0, stream>>>(F, E, Z, 0, d, batch, timestep_, x_[k]);
-    else
-      rife_block_input_kernel<28><<<g, kGlueThreads, 0, stream>>>(F, E, Z, k, d, batch, timestep_, x_[k]);
+    switch (k) {
+      case 0: rife_first_input_kernel<<<g, kGlueThreads, 0, stream>>>(F, E, d, batch, t, x_[k]); break;
+      case 1: rife_block_input_kernel<1><<<g, kGlueThreads, 0, stream>>>(F, E, Z, d, batch, t, x_[k]); break;
+      case 2: rife_block_input_kernel<2><<<g, kGlueThreads, 0, stream>>>(F, E, Z, d, batch, t, x_[k]); break;
+      case 3: rife_block_input_kernel<3><<<g, kGlueThreads, 0, stream>>>(F, E, Z, d, batch, t, x_[k]); break;
+      default: rife_block_input_kernel<4><<<g, kGlueThreads, 0, stream>>>(F, E, Z, d, batch, t, x_[k]); break;
+    }
     KB2_CUDA(cudaGetLastError());
     // X written, frames and encodings read at the sample points (4 per pixel when d >= 2)
-    KB2_TRY(timer_.end(k_glue_, 0.0, px * ((k == 0 ? 2 : 4) * 16.0 + (d >= 2 ? 4.0 : 1.0) * 32.0), stream));
+    KB2_TRY(timer_.end(k_glue_[k], 0.0, px * ((k == 0 ? 2 : 4) * 16.0 + (d >= 2 ? 4.0 : 1.0) * 32.0), stream));
     for (auto& l : layers_[k]) KB2_TRY(timed(*l, batch));
   }
   const int last = plan_.blocks - 1;
   if (finish.image == nullptr) {
-    const dim3 g = row_grid(Wp_, batch * Hp_);
+    const dim3 g = row_grid(Wp_, batch * runs(Hp_));
     KB2_TRY(timer_.begin(stream));
-    if (finish.f16)
-      rife_motion_kernel<__half><<<g, kGlueThreads, 0, stream>>>(F, Z, last, batch, static_cast<__half*>(finish.flow),
-                                                                  static_cast<__half*>(finish.mask));
-    else
-      rife_motion_kernel<float><<<g, kGlueThreads, 0, stream>>>(F, Z, last, batch, static_cast<float*>(finish.flow),
-                                                                 static_cast<float*>(finish.mask));
-    KB2_CUDA(cudaGetLastError());
+    KB2_TRY(finish.f16 ? launch_motion<__half>(g, stream, F, Z, last, batch, finish)
+                       : launch_motion<float>(g, stream, F, Z, last, batch, finish));
     KB2_TRY(timer_.end(k_motion_, 0.0, full_px * (kRifeZBytes + 5.0 * (finish.f16 ? 2.0 : 4.0)), stream));
     return Status::Ok();
   }
   const double px = static_cast<double>(batch) * H_ * W_;
+  const dim3 g = row_grid(W_, batch * runs(H_));
+  __half* out = static_cast<__half*>(finish.image);
   KB2_TRY(timer_.begin(stream));
-  rife_finish_kernel<<<row_grid(W_, batch * H_), kGlueThreads, 0, stream>>>(F, Z, last, batch,
-                                                                            static_cast<__half*>(finish.image));
+  switch (last) {
+    case 1: rife_finish_kernel<1><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, out); break;
+    case 2: rife_finish_kernel<2><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, out); break;
+    case 3: rife_finish_kernel<3><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, out); break;
+    default: rife_finish_kernel<4><<<g, kGlueThreads, 0, stream>>>(F, Z, batch, out); break;
+  }
   KB2_CUDA(cudaGetLastError());
   KB2_TRY(timer_.end(k_finish_, 0.0, px * (kRifeZBytes + 16.0 + 6.0), stream));
   return Status::Ok();

@@ -73,8 +73,7 @@ class RifeNet {
   uint8_t* enc_ = nullptr;                                 // encodings, [2 n][Hp][Wp] 4 x FP16
   DeviceBuffer pad_;                                       // both frames, padded RGBx [2][n][Hp][Wp]
   LayerTimer timer_;
-  int k_pad_ = 0, k_enc_ = 0, k_glue_ = 0, k_c0a_ = 0, k_c0b_ = 0, k_res_ = 0, k_ct_ = 0, k_finish_ = 0,
-      k_motion_ = 0;
+  int k_pad_ = 0, k_glue_[5] = {}, k_c0a_ = 0, k_c0b_ = 0, k_res_ = 0, k_ct_ = 0, k_finish_ = 0, k_motion_ = 0;
 };
 
 }  // namespace kb2
