@@ -110,6 +110,22 @@ typedef struct kb2_engine kb2_engine;
 #define KB2_SPAN_X2_PARAMS 389916
 #define KB2_IFNET_PARAMS 5160980
 
+/* The weight blob v1 of KB2_MODEL_RIFE_FUSED from ONNX: the pieces of a split RIFE 4.2x model as the
+ * reference's native RIFE path reads them (src/prepare/rife_native.h:39 rife_native_layers, after
+ * src/prepare/rife_split.h cut the model): pieces[0] the encoder (cnn0..cnn3), pieces[1 + k] block k,
+ * each a ModelProto's bytes whose single input runs through a chain of Conv 3x3 (pad 1, stride 1 or 2)
+ * with LeakyRelu / PRelu / Relu, ResConv (Conv, Mul by a per-channel beta, Add of the conv's input,
+ * activation) and a last ConvTranspose 4x4 stride 2; Cast and Identity pass through; a 1x1 Conv that
+ * follows a conv is folded into it, a depthwise 3x3 stored as a diagonal one (the reference's reader).
+ * Initializers and Constant values: FLOAT, FLOAT16, FLOAT8E4M3FN or INT8, raw or typed, inline.
+ * reduce[k]: block k's input reduction (the plan; the widths come from the weights), 2 to 5 blocks.
+ * blob = NULL: *blob_bytes receives the size; else *blob_bytes is the buffer's capacity on entry and
+ * the blob's size on return. Refusals: KB2_WEIGHTS_INVALID (unreadable, or not this topology),
+ * KB2_FORMAT_UNSUPPORTED (weights outside the file, segments, sparse initializers, other element
+ * types), KB2_INVALID_ARGUMENT; kb2_create_error() says why. Host only: no device is touched. */
+int kb2_rife_blob_from_onnx(const void* const* pieces, const uint64_t* piece_bytes, int32_t blocks,
+                            const int32_t* reduce, void* blob, uint64_t* blob_bytes);
+
 /* Engine creation parameters (the reference's Artifact + shape set, backend.h:446). */
 typedef struct kb2_engine_desc {
   int32_t model;        /* kb2_model */

@@ -251,3 +251,47 @@ def pan_estimate(a, b):
     out = np.zeros(3, np.float32)
     L.kref_pan_estimate(_ptr(a), _ptr(b), h, w, _ptr(out))
     return float(out[0]), float(out[1]), bool(out[2] != 0)
+
+
+class RefRefusal(RuntimeError):
+    """The reference's reader refused a piece; the message is its refusal detail."""
+
+
+def rife_native_layers(piece: bytes):
+    """The reference's reader of one RIFE ONNX piece (src/prepare/rife_native.cpp
+    rife_native_layers): a list of layers, each a dict with transposed, cin, cout, kernel, stride and
+    the float arrays w (OIHW for a conv, [cin][cout][4][4] for the transposed conv: the ONNX and
+    weight-blob layouts, rearranged from the reference's [cout][k^2][cin]), b, slope and scale
+    (empty when absent). Raises RefRefusal when the reference refuses the piece."""
+    L = lib()
+    if not getattr(L, "_onnx_bound", False):
+        L.kref_rife_native_layers.argtypes = [ctypes.c_char_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_int32),
+                                              ctypes.c_int, _fp, ctypes.c_uint64, ctypes.c_char_p, ctypes.c_int]
+        L.kref_rife_native_layers.restype = ctypes.c_int
+        L._onnx_bound = True
+    max_layers = 64
+    meta = np.zeros((max_layers, 9), np.int32)
+    vals = np.zeros(len(piece) + 4096, np.float32)  # a piece holds at least a byte per value
+    err = ctypes.create_string_buffer(512)
+    n = L.kref_rife_native_layers(piece, len(piece), meta.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                  max_layers, _ptr(vals), vals.size, err, 512)
+    if n == -1:
+        raise RefRefusal(err.value.decode(errors="replace"))
+    if n < 0:
+        raise RuntimeError("kref_rife_native_layers: buffer too small")
+    out, at = [], 0
+    for m in meta[:n]:
+        tr, cin, cout, k, stride, nw, nb, ns, nsc = (int(v) for v in m)
+        w = vals[at:at + nw].reshape(cout, k * k, cin)
+        at += nw
+        if tr:
+            w = w.transpose(2, 0, 1).reshape(cin, cout, k, k)
+        else:
+            w = w.transpose(0, 2, 1).reshape(cout, cin, k, k)
+        layer = {"transposed": bool(tr), "cin": cin, "cout": cout, "kernel": k, "stride": stride,
+                 "w": np.ascontiguousarray(w)}
+        for key, cnt in (("b", nb), ("slope", ns), ("scale", nsc)):
+            layer[key] = vals[at:at + cnt].copy()
+            at += cnt
+        out.append(layer)
+    return out

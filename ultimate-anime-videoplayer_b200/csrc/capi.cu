@@ -1,13 +1,16 @@
 // The C ABI of include/kirari_b200.h over the C++ engines. Every entry point catches everything:
 // nothing throws across the boundary (the reference's rule for its module entry points,
 // src/gpu/backend.h:575-587).
+#include <cstring>
 #include <memory>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "kirari_b200.h"
 #include "engine.h"
 #include "ifnet_net.h"
+#include "onnx_import.h"
 
 namespace {
 thread_local std::string g_create_error;
@@ -82,6 +85,41 @@ extern "C" {
 int kb2_abi_version(void) { return KB2_ABI_VERSION; }
 
 const char* kb2_create_error(void) { return g_create_error.c_str(); }
+
+int kb2_rife_blob_from_onnx(const void* const* pieces, const uint64_t* piece_bytes, int32_t blocks,
+                            const int32_t* reduce, void* blob, uint64_t* blob_bytes) {
+  try {
+    g_create_error.clear();
+    if (pieces == nullptr || piece_bytes == nullptr || reduce == nullptr || blob_bytes == nullptr || blocks < 0 ||
+        blocks > 5) {
+      g_create_error = "null or out-of-range argument";
+      return KB2_INVALID_ARGUMENT;
+    }
+    std::vector<const uint8_t*> p(static_cast<size_t>(blocks) + 1);
+    for (size_t i = 0; i < p.size(); ++i) p[i] = static_cast<const uint8_t*>(pieces[i]);
+    std::vector<uint8_t> out;
+    const kb2::Status st = kb2::rife_blob_from_onnx(p.data(), piece_bytes, blocks, reduce, out);
+    if (!st.ok()) {
+      g_create_error = st.detail;
+      return st.code;
+    }
+    const uint64_t capacity = *blob_bytes;
+    *blob_bytes = out.size();
+    if (blob == nullptr) return KB2_OK;
+    if (capacity < out.size()) {
+      g_create_error = "blob buffer too small";
+      return KB2_INVALID_ARGUMENT;
+    }
+    std::memcpy(blob, out.data(), out.size());
+    return KB2_OK;
+  } catch (const std::exception& ex) {
+    g_create_error = ex.what();
+    return KB2_VENDOR_CALL_FAILED;
+  } catch (...) {
+    g_create_error = "unknown failure";
+    return KB2_VENDOR_CALL_FAILED;
+  }
+}
 
 int kb2_create(const kb2_engine_desc* desc, kb2_engine** out) {
   try {

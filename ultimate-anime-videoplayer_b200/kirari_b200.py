@@ -42,7 +42,7 @@ EXPORTS = ("kb2_abi_version", "kb2_create", "kb2_create_error", "kb2_destroy", "
            "kb2_set_profiling", "kb2_read_profile", "kb2_launches_per_enqueue", "kb2_span_calibrate_static",
            "kb2_warp_taps", "kb2_selftest_bounded_wait", "kb2_warp_blend_at", "kb2_flow_max",
            "kb2_warp_blend_poses", "kb2_pack_display", "kb2_rife_geometry", "kb2_set_output_format",
-           "kb2_set_row_tiles", "kb2_span_tile_grid", "kb2_next_span_tiles")
+           "kb2_set_row_tiles", "kb2_span_tile_grid", "kb2_next_span_tiles", "kb2_rife_blob_from_onnx")
 
 
 class KB2Error(RuntimeError):
@@ -94,6 +94,9 @@ def lib():
         L.kb2_abi_version.restype = ctypes.c_int
         L.kb2_create.argtypes = [ctypes.POINTER(EngineDesc), ctypes.POINTER(ctypes.c_void_p)]
         L.kb2_create_error.restype = ctypes.c_char_p
+        L.kb2_rife_blob_from_onnx.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_uint64),
+                                              ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p,
+                                              ctypes.POINTER(ctypes.c_uint64)]
         L.kb2_destroy.argtypes = [ctypes.c_void_p]
         L.kb2_last_error.argtypes = [ctypes.c_void_p]
         L.kb2_last_error.restype = ctypes.c_char_p
@@ -155,6 +158,26 @@ def _stream_handle(stream):
     if stream is None:
         stream = torch.cuda.current_stream()
     return ctypes.c_void_p(stream.cuda_stream)
+
+
+def rife_blob_from_onnx(pieces, reduce) -> bytes:
+    """kb2_rife_blob_from_onnx: the KB2_MODEL_RIFE_FUSED weight blob from ONNX pieces (bytes: the
+    encoder, then one per block) and the plan's input reductions."""
+    n = len(pieces)
+    bufs = [ctypes.create_string_buffer(bytes(p), len(p)) for p in pieces]
+    ptrs = (ctypes.c_void_p * n)(*[ctypes.cast(b, ctypes.c_void_p) for b in bufs])
+    sizes = (ctypes.c_uint64 * n)(*[len(p) for p in pieces])
+    red = (ctypes.c_int32 * max(1, len(reduce)))(*reduce)
+    size = ctypes.c_uint64(0)
+    L = lib()
+    rc = L.kb2_rife_blob_from_onnx(ptrs, sizes, n - 1, red, None, ctypes.byref(size))
+    if rc != KB2_OK:
+        raise KB2Error(rc, L.kb2_create_error().decode(errors="replace"))
+    out = ctypes.create_string_buffer(size.value)
+    rc = L.kb2_rife_blob_from_onnx(ptrs, sizes, n - 1, red, out, ctypes.byref(size))
+    if rc != KB2_OK:
+        raise KB2Error(rc, L.kb2_create_error().decode(errors="replace"))
+    return out.raw[:size.value]
 
 
 class Engine:
