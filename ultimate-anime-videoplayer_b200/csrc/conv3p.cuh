@@ -1029,8 +1029,9 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     fence_mbar_init();
   }
   for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
-    s_bias[j] = j < kCoutPad ? a.bias[j] : 0.0f;
-    s_scale[j] = (a.chan_scale != nullptr && j < kCoutPad) ? a.chan_scale[j] : 1.0f;
+    constexpr float kHalf = epi_halved<kEpi>() ? 0.5f : 1.0f;  // SiLU and gate layers: constants halved (exact)
+    s_bias[j] = j < kCoutPad ? kHalf * a.bias[j] : 0.0f;
+    s_scale[j] = kHalf * ((a.chan_scale != nullptr && j < kCoutPad) ? a.chan_scale[j] : 1.0f);
     s_slope[j] = (a.slope != nullptr && j < kCoutPad) ? a.slope[j] : 0.0f;
   }
   for (int j = threadIdx.x; j <= kMaxKSteps; j += blockDim.x)
@@ -1141,7 +1142,7 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
 #pragma unroll
     for (int j = 0; j < kCols; ++j) {
       r_bias[j] = kRegBias ? s_bias[col0 + j] : 0.0f;
-      r_scale[j] = 1.0f;
+      r_scale[j] = epi_halved<kEpi>() ? 0.5f : 1.0f;
     }
     const float* e_bias = kRegBias ? r_bias : s_bias + col0;
     const float* e_scale = kRegBias ? r_scale : s_scale + col0;
@@ -1199,7 +1200,7 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
         __syncwarp();
         if (lane == 0) mbar_arrive_remote_relaxed(free0 + s * 8u);
         if (store)
-          epilogue_cols<kEpi, kOut, kCols, kRegBias ? kConstsAny : (kFp8 ? kConstsVec4 : kConstsVec4Bias)>(
+          epilogue_cols<kEpi, kOut, kCols, (kRegBias || kEpi == kEpiPrelu || kEpi == kEpiResPrelu) ? kConstsAny : (kFp8 ? kConstsVec4 : kConstsVec4Bias)>(
               a, e_bias, e_scale, s_slope + col0, v, 0, n, y, x, col0,
                                            kResidual ? res : nullptr);
       }

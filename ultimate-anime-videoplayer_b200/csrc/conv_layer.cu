@@ -403,6 +403,9 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   int band = static_cast<int>(rows_total / (16LL * slots));
   const int band_min = stacked ? 8 : 4;
   band = band < band_min ? band_min : (band > 64 ? 64 : band);
+  // 1x1 layers (no halo rows, so short bands cost nothing): bands of 8 rows keep the blocks that
+  // run at once on neighbouring rows of the same frames (conv_cat 2 % faster on 8 x 1080p)
+  if (!stacked && a.in_rows == 1) band = std::min(band, 8);
   a.band_rows = band;
   a.bands = (a.H + band - 1) / band;
   a.items = a.batch * a.bands * units;

@@ -167,6 +167,14 @@ __device__ __forceinline__ void load_residual_words(const ConvArgs& a, int n, in
   }
 }
 
+// SiLU and the SPAN gate work on h = v / 2, the argument of their tanh: the kernels store those
+// layers' bias and channel scale halved (exact), so the constant step yields h, and
+//   SiLU(v) = v sigmoid(v) = h tanh(h) + h,
+//   (v + x)(sigmoid(v) - 1/2) = (h + x / 2) tanh(h),
+// two multiplies fewer per value than from v.
+template <int kEpi>
+__host__ __device__ constexpr bool epi_halved() { return kEpi == kEpiSilu || kEpi == kEpiSpanAttn; }
+
 // How the per-channel constants are read: kConstsAny through the pointers as given (registers or
 // shared memory), one value at a time; kConstsVec4 from 16-byte aligned shared memory, four at a
 // time (a quarter of the load instructions); kConstsVec4Bias the same with the scale 1 (FP16 layers).
@@ -192,6 +200,11 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
         v[j + 1] = fmaf(v[j + 1], sc.y, b.y);
         v[j + 2] = fmaf(v[j + 2], sc.z, b.z);
         v[j + 3] = fmaf(v[j + 3], sc.w, b.w);
+      } else if constexpr (epi_halved<kEpi>()) {
+        v[j] = fmaf(v[j], 0.5f, b.x);
+        v[j + 1] = fmaf(v[j + 1], 0.5f, b.y);
+        v[j + 2] = fmaf(v[j + 2], 0.5f, b.z);
+        v[j + 3] = fmaf(v[j + 3], 0.5f, b.w);
       } else {
         v[j] += b.x;
         v[j + 1] += b.y;
@@ -200,31 +213,20 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
       }
     }
   }
-  // PReLU slopes of this pixel's channels (from shared memory four at a time where it is aligned)
-  auto slope = [&](int j) -> float { return s_slope[kc0 + j]; };
-  float slope_v[kEpi == kEpiPrelu || kEpi == kEpiResPrelu ? kCols : 1];
-  if constexpr ((kEpi == kEpiPrelu || kEpi == kEpiResPrelu) && kConsts != kConstsAny) {
-#pragma unroll
-    for (int j = 0; j < kCols; j += 4) {
-      const float4 q = *reinterpret_cast<const float4*>(s_slope + kc0 + j);
-      slope_v[j] = q.x;
-      slope_v[j + 1] = q.y;
-      slope_v[j + 2] = q.z;
-      slope_v[j + 3] = q.w;
-    }
-  }
-  auto slope_at = [&](int j) -> float {
-    if constexpr ((kEpi == kEpiPrelu || kEpi == kEpiResPrelu) && kConsts != kConstsAny) return slope_v[j];
-    else return slope(j);
-  };
+  // PReLU slopes of this pixel's channels, read from shared memory where they are used (held in
+  // registers for the whole residual loop they made the 64-channel residual conv spill)
+  auto slope_at = [&](int j) -> float { return s_slope[kc0 + j]; };
   if constexpr (kEpi == kEpiSilu) {
 #pragma unroll
-    for (int j = 0; j < kCols; ++j) v[j] = v[j] * sigmoidf_fast(v[j]);
+    for (int j = 0; j < kCols; ++j) v[j] = fmaf(v[j], tanh_approx(v[j]), v[j]);  // v holds h = v / 2
   } else if constexpr (kEpi == kEpiPrelu) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j) v[j] = v[j] >= 0.0f ? v[j] : v[j] * slope_at(j);
   } else if constexpr (kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu) {
     // residual: same pixel and channels, in the block input's format
+    // r holds the residual's stored values (E4M3 codes decoded, or FP16); its factor in the sum:
+    // the dequantisation scale (E4M3), halved for the gate, which adds x / 2 to h
+    const float rc = (a.res_fp8 ? a.res_scale : 1.0f) * (kEpi == kEpiSpanAttn ? 0.5f : 1.0f);
 #pragma unroll
     for (int g = 0; g < kCols / 8; ++g) {
       const int c = col0 + 8 * g;
@@ -239,10 +241,10 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
         for (int k = 0; k < 2; ++k) {
           const float2 lo = unpack_e4m3x2(static_cast<uint16_t>(w2[k] & 0xFFFFu));
           const float2 hi = unpack_e4m3x2(static_cast<uint16_t>(w2[k] >> 16));
-          r[4 * k + 0] = lo.x * a.res_scale;
-          r[4 * k + 1] = lo.y * a.res_scale;
-          r[4 * k + 2] = hi.x * a.res_scale;
-          r[4 * k + 3] = hi.y * a.res_scale;
+          r[4 * k + 0] = lo.x;
+          r[4 * k + 1] = lo.y;
+          r[4 * k + 2] = hi.x;
+          r[4 * k + 3] = hi.y;
         }
       } else {
         const uint4 q = res_pre != nullptr
@@ -261,9 +263,9 @@ __device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_
       for (int k = 0; k < 8; ++k) {
         float& t = v[8 * g + k];
         if constexpr (kEpi == kEpiSpanAttn) {
-          t = (t + r[k]) * sigmoid_centered(t);
+          t = fmaf(rc, r[k], t) * tanh_approx(t);  // t holds h = v / 2
         } else {
-          const float u = t + r[k];
+          const float u = fmaf(rc, r[k], t);
           t = u >= 0.0f ? u : u * slope_at(8 * g + k);
         }
       }
@@ -434,8 +436,9 @@ __global__ void __launch_bounds__(ConvShape<kN>::threads, 1)
     fence_mbar_init();
   }
   for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
-    s_bias[j] = j < kN ? a.bias[j] : 0.0f;
-    s_scale[j] = (a.chan_scale != nullptr && j < kN) ? a.chan_scale[j] : 1.0f;
+    constexpr float kHalf = epi_halved<kEpi>() ? 0.5f : 1.0f;  // exact
+    s_bias[j] = j < kN ? kHalf * a.bias[j] : 0.0f;
+    s_scale[j] = kHalf * ((a.chan_scale != nullptr && j < kN) ? a.chan_scale[j] : 1.0f);
     s_slope[j] = (a.slope != nullptr && j < kN) ? a.slope[j] : 0.0f;
   }
   for (int j = threadIdx.x; j <= kMaxKSteps; j += blockDim.x) {
