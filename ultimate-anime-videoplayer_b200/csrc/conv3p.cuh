@@ -31,6 +31,8 @@
 // the MMA issuer, warps 2.. = epilogue of the block's own pixels (conv_tc.cuh epilogues).
 #pragma once
 
+#include <type_traits>
+
 #include <utility>
 
 #include "stack_common.cuh"
@@ -1005,9 +1007,8 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
   uint64_t* drain = wpeer + 1;              // both blocks: every MMA completed
   uint64_t* s_k = bars + 128;               // per K step of a row: (a_off >> 4) | (lbo >> 4) << 16
   // per-channel constants, 16-byte aligned (the epilogue reads them four at a time)
-  float* s_bias = reinterpret_cast<float*>(s_k + kMaxKSteps + 2);
-  float* s_scale = s_bias + kMaxN;
-  float* s_slope = s_scale + kMaxN;
+  // PReLU slopes (bias and scale are read from the parameter space, ConvArgs::cbias / cscale)
+  float* s_slope = reinterpret_cast<float*>(s_k + kMaxKSteps + 2) + 2 * kMaxN;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_slope + kMaxN);
   uint8_t* zero_b = reinterpret_cast<uint8_t*>(bars) + kStackZeroOff;
 
@@ -1029,9 +1030,6 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     fence_mbar_init();
   }
   for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
-    constexpr float kHalf = epi_halved<kEpi>() ? 0.5f : 1.0f;  // SiLU and gate layers: constants halved (exact)
-    s_bias[j] = j < kCoutPad ? kHalf * a.bias[j] : 0.0f;
-    s_scale[j] = kHalf * ((a.chan_scale != nullptr && j < kCoutPad) ? a.chan_scale[j] : 1.0f);
     s_slope[j] = (a.slope != nullptr && j < kCoutPad) ? a.slope[j] : 0.0f;
   }
   for (int j = threadIdx.x; j <= kMaxKSteps; j += blockDim.x)
@@ -1132,20 +1130,6 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
     const uint32_t free0 = cluster_addr(smem_u32(slot_free), 0);  // block 0's slot_free[0]
-    // FP16 layers without a residual: this warp's biases in registers and no channel scale (re-reading
-    // both from shared memory on every row measured 5-15 % slower); E4M3 layers, the gated layers (72
-    // registers a thread at 832 threads: register biases spilled 64 bytes, and reading them from shared
-    // memory measured 0.5 % faster) and the 64-channel residual shape read bias and scale from shared
-    // memory
-    constexpr bool kRegBias = !kFp8 && kCoutPad != 64 && !kResidual;
-    float r_bias[kCols], r_scale[kCols];
-#pragma unroll
-    for (int j = 0; j < kCols; ++j) {
-      r_bias[j] = kRegBias ? s_bias[col0 + j] : 0.0f;
-      r_scale[j] = epi_halved<kEpi>() ? 0.5f : 1.0f;
-    }
-    const float* e_bias = kRegBias ? r_bias : s_bias + col0;
-    const float* e_scale = kRegBias ? r_scale : s_scale + col0;
     // the group's slots start free (phase 0 of slot_free)
     if (lane == 0)
       for (uint32_t s = grp; s < R; s += kG) mbar_arrive_remote_relaxed(free0 + s * 8u);
@@ -1199,10 +1183,36 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote_relaxed(free0 + s * 8u);
-        if (store)
-          epilogue_cols<kEpi, kOut, kCols, (kRegBias || kEpi == kEpiPrelu || kEpi == kEpiResPrelu) ? kConstsAny : (kFp8 ? kConstsVec4 : kConstsVec4Bias)>(
-              a, e_bias, e_scale, s_slope + col0, v, 0, n, y, x, col0,
-                                           kResidual ? res : nullptr);
+        if (store) {
+          // Bias and scale come from the parameter space (ConvArgs::cbias / cscale) at the warp's
+          // first channel. Where a warp covers every channel that offset is 0; the FP16 48-channel
+          // gates (three column groups) dispatch it as a compile-time offset too, so the constants
+          // are operands of the epilogue's FMAs, with no loads and no registers held across rows
+          // (the other multi-group shapes spill with three copies of the epilogue, and index them).
+          // FP16 48- and 16-channel layers use the bias alone (their scale is the constant 1 or 1/2;
+          // the 64-channel shapes keep both, which holds their spills to 8 bytes).
+          constexpr int kGroups = kCoutPad / kCols;
+          constexpr int kConsts = (kFp8 || kCoutPad == 64) ? kConstsAny : kConstsBias;
+          auto epi = [&](auto first) {
+            constexpr int c0 = decltype(first)::value;
+            const int at = c0 < 0 ? col0 : c0;
+            epilogue_cols<kEpi, kOut, kCols, kConsts>(a, a.cbias + at, a.cscale + at, s_slope + col0, v, 0, n, y, x,
+                                                      col0, kResidual ? res : nullptr);
+          };
+          static_assert(kGroups >= 1 && kGroups <= 3, "one to three column groups a row");
+          if constexpr (kGroups == 1) {
+            epi(std::integral_constant<int, 0>{});
+          } else if constexpr (kGroups == 3 && !kFp8) {
+            if (col0 == 0)
+              epi(std::integral_constant<int, 0>{});
+            else if (col0 == kCols)
+              epi(std::integral_constant<int, kCols>{});
+            else
+              epi(std::integral_constant<int, 2 * kCols>{});
+          } else {
+            epi(std::integral_constant<int, -1>{});  // runtime offset
+          }
+        }
       }
       if (!ok) break;
       // the segment's 2 + pad virtual entries (cleared by its input rows rows .. rows + 1 + pad):

@@ -335,6 +335,14 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   a.bias = bias.as<float>();
   a.slope = slope.as<float>();
   a.chan_scale = s.fp8 ? scale.as<float>() : nullptr;
+  {
+    // SiLU and gate layers hold their constants halved (exact): their epilogue works on v / 2
+    const float half = (s.epi == kEpiSilu || s.epi == kEpiSpanAttn) ? 0.5f : 1.0f;
+    for (int co = 0; co < kMaxN; ++co) {
+      a.cbias[co] = co < s.n_pad ? half * bias_h[co] : 0.0f;
+      a.cscale[co] = half * ((s.fp8 && co < static_cast<int>(wscale.size())) ? wscale[co] : 1.0f);
+    }
+  }
   a.out_chunks = s.out_chunks;
   a.out2_chunks = s.out2_chunks;
   a.err = err_word;

@@ -96,6 +96,11 @@ struct ConvArgs {
   const float* bias;        // N entries (zero padded)
   const float* chan_scale;  // N entries or null
   const float* slope;       // N entries (PReLU) or null
+  // The epilogue's per-channel bias and scale (1 where the layer has none), in the parameter space:
+  // every warp reads the same values, which the constant cache serves without the shared-memory
+  // pipe the MMAs' operands use. SiLU and gate layers hold them halved (epi_halved).
+  float cbias[kMaxN];
+  float cscale[kMaxN];
   float out_inv_scale;      // E4M3 output: 1 / scale
   float res_scale;          // E4M3 residual dequantisation scale
   const uint8_t* residual;  // same pixels and channels as the output, chunked
@@ -167,51 +172,33 @@ __device__ __forceinline__ void load_residual_words(const ConvArgs& a, int n, in
   }
 }
 
-// SiLU and the SPAN gate work on h = v / 2, the argument of their tanh: the kernels store those
-// layers' bias and channel scale halved (exact), so the constant step yields h, and
+// SiLU and the SPAN gate work on h = v / 2, the argument of their tanh: the host stores those
+// layers' bias and channel scale halved (exact, ConvArgs::cbias / cscale), so the constant step
+// yields h, and
 //   SiLU(v) = v sigmoid(v) = h tanh(h) + h,
 //   (v + x)(sigmoid(v) - 1/2) = (h + x / 2) tanh(h),
 // two multiplies fewer per value than from v.
 template <int kEpi>
 __host__ __device__ constexpr bool epi_halved() { return kEpi == kEpiSilu || kEpi == kEpiSpanAttn; }
 
-// How the per-channel constants are read: kConstsAny through the pointers as given (registers or
-// shared memory), one value at a time; kConstsVec4 from 16-byte aligned shared memory, four at a
-// time (a quarter of the load instructions); kConstsVec4Bias the same with the scale 1 (FP16 layers).
-enum ConstsMode : int { kConstsAny = 0, kConstsVec4 = 1, kConstsVec4Bias = 2 };
+// How the per-channel constants are applied: kConstsAny, v * scale + bias from both arrays;
+// kConstsBias, the bias array alone with the layer's constant scale (1, or 1/2 for the halved
+// epilogues): FP16 layers, whose scale array holds only that constant.
+enum ConstsMode : int { kConstsAny = 0, kConstsBias = 1 };
 
 template <int kEpi, int kOut, int kCols, int kConsts = kConstsAny>
-__device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* s_bias, const float* s_scale,
+__device__ __forceinline__ void epilogue_cols(const ConvArgs& a, const float* bias, const float* scale,
                                               const float* s_slope, float* v, int kc0, int n, int y, int x,
                                               int col0_override = -1, const uint32_t* res_pre = nullptr) {
   const int col0 = col0_override >= 0 ? col0_override : kc0;
   const size_t pix_row = static_cast<size_t>(n) * a.H + y;
   if constexpr (kConsts == kConstsAny) {
 #pragma unroll
-    for (int j = 0; j < kCols; ++j) v[j] = fmaf(v[j], s_scale[kc0 + j], s_bias[kc0 + j]);
+    for (int j = 0; j < kCols; ++j) v[j] = fmaf(v[j], scale[kc0 + j], bias[kc0 + j]);
   } else {
-    static_assert(kCols % 4 == 0, "vector constants: four channels at a time");
+    constexpr float kScale = epi_halved<kEpi>() ? 0.5f : 1.0f;
 #pragma unroll
-    for (int j = 0; j < kCols; j += 4) {
-      const float4 b = *reinterpret_cast<const float4*>(s_bias + kc0 + j);
-      if constexpr (kConsts == kConstsVec4) {
-        const float4 sc = *reinterpret_cast<const float4*>(s_scale + kc0 + j);
-        v[j] = fmaf(v[j], sc.x, b.x);
-        v[j + 1] = fmaf(v[j + 1], sc.y, b.y);
-        v[j + 2] = fmaf(v[j + 2], sc.z, b.z);
-        v[j + 3] = fmaf(v[j + 3], sc.w, b.w);
-      } else if constexpr (epi_halved<kEpi>()) {
-        v[j] = fmaf(v[j], 0.5f, b.x);
-        v[j + 1] = fmaf(v[j + 1], 0.5f, b.y);
-        v[j + 2] = fmaf(v[j + 2], 0.5f, b.z);
-        v[j + 3] = fmaf(v[j + 3], 0.5f, b.w);
-      } else {
-        v[j] += b.x;
-        v[j + 1] += b.y;
-        v[j + 2] += b.z;
-        v[j + 3] += b.w;
-      }
-    }
+    for (int j = 0; j < kCols; ++j) v[j] = fmaf(v[j], kScale, bias[kc0 + j]);
   }
   // PReLU slopes of this pixel's channels, read from shared memory where they are used (held in
   // registers for the whole residual loop they made the 64-channel residual conv spill)
@@ -413,9 +400,8 @@ __global__ void __launch_bounds__(ConvShape<kN>::threads, 1)
   // of the descriptor fields the delta is added to, and are masked off before use)
   uint64_t* s_kstep = bars + 64;
   uint64_t* s_tile = s_kstep + kMaxKSteps + 1;  // per A tile: (off >> 4) | (lbo >> 4) << 16
-  float* s_bias = reinterpret_cast<float*>(s_tile + kMaxTiles);
-  float* s_scale = s_bias + kMaxN;
-  float* s_slope = s_scale + kMaxN;
+  // PReLU slopes (bias and scale are read from the parameter space, ConvArgs::cbias / cscale)
+  float* s_slope = reinterpret_cast<float*>(s_tile + kMaxTiles) + 2 * kMaxN;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_slope + kMaxN);
 
   const int warp = threadIdx.x >> 5;
@@ -436,9 +422,6 @@ __global__ void __launch_bounds__(ConvShape<kN>::threads, 1)
     fence_mbar_init();
   }
   for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
-    constexpr float kHalf = epi_halved<kEpi>() ? 0.5f : 1.0f;  // exact
-    s_bias[j] = j < kN ? kHalf * a.bias[j] : 0.0f;
-    s_scale[j] = kHalf * ((a.chan_scale != nullptr && j < kN) ? a.chan_scale[j] : 1.0f);
     s_slope[j] = (a.slope != nullptr && j < kN) ? a.slope[j] : 0.0f;
   }
   for (int j = threadIdx.x; j <= kMaxKSteps; j += blockDim.x) {
@@ -632,7 +615,7 @@ __global__ void __launch_bounds__(ConvShape<kN>::threads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        if (store) epilogue_cols<kEpi, kOut, 16>(a, s_bias, s_scale, s_slope, v, col0, n, y, x);
+        if (store) epilogue_cols<kEpi, kOut, 16>(a, a.cbias, a.cscale, s_slope, v, col0, n, y, x);
         ++acc_cnt;
       }
     }
