@@ -280,7 +280,8 @@ __global__ void __launch_bounds__(kGlueThreads, 4)
   }
 }
 
-// The interpolated frame: warp both frames by the final flow, blend with sigmoid(mask), crop the
+// The interpolated frame: warp both frames by the final flow, blend with sigmoid(mask) (as
+// 1 / (1 + __expf(-mask)), the reference's fused finish, rife_finish.cuh:46), crop the
 // window: out = w0 * m + w1 * (1 - m), NCHW FP16 [n][3][H][W]. One thread per column walking
 // kGlueRunRows rows, with block 3's flow resize cached along the column.
 __global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, int batch, __half* __restrict__ out) {
@@ -307,7 +308,7 @@ __global__ void ifnet_blend_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, i
       float w0[3], w1[3];
       warp3(F.pad0 + frame, F, Y, X, f[0], f[1], w0);
       warp3(F.pad1 + frame, F, Y, X, f[2], f[3], w1);
-      const float m = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-mask)));
+      const float m = __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-mask)));
       const float m1 = __fsub_rn(1.0f, m);
       __half* o = out + (static_cast<size_t>(n) * 3 * F.H + y) * F.W + x;
 #pragma unroll
@@ -348,7 +349,7 @@ __global__ void ifnet_motion_kernel(IfFrames F, IfFlowLevels L, IfFlowField FF, 
       const size_t at = static_cast<size_t>(Y) * F.Wp + X;
 #pragma unroll
       for (int c = 0; c < 4; ++c) store_motion(flow + (static_cast<size_t>(n) * 4 + c) * pl + at, f[c]);
-      store_motion(mask + static_cast<size_t>(n) * pl + at, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-m))));
+      store_motion(mask + static_cast<size_t>(n) * pl + at, __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-m))));
     }
   }
 }

@@ -401,7 +401,7 @@ __global__ void __launch_bounds__(kGlueThreads) rife_finish_kernel(IfFrames F, R
       float w0[3], w1[3];
       warp3(F.pad0 + frame, F, Y, X, f[0], f[1], w0);
       warp3(F.pad1 + frame, F, Y, X, f[2], f[3], w1);
-      const float m = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-mask)));
+      const float m = __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-mask)));
       const float m1 = __fsub_rn(1.0f, m);
       __half* o = out + (static_cast<size_t>(n) * 3 * F.H + y) * F.W + x;
 #pragma unroll
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(kGlueThreads) rife_motion_kernel(IfFrames F, R
       const size_t at = static_cast<size_t>(Y) * F.Wp + X;
 #pragma unroll
       for (int c = 0; c < 4; ++c) store_motion(flow + (static_cast<size_t>(n) * 4 + c) * pl + at, f[c]);
-      store_motion(mask + static_cast<size_t>(n) * pl + at, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-m))));
+      store_motion(mask + static_cast<size_t>(n) * pl + at, __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-m))));
     }
   }
 }
