@@ -527,8 +527,14 @@ def verify_leg(leg, d_in, d_out):
     mse = float(np.mean(diff.astype(np.float64) ** 2))
     db = float("inf") if mse == 0 else float(10.0 * np.log10(1.0 / mse))
     ok = bool(db >= 45.0) if leg["fp8"] else bool(err <= 2.0 / 255.0)
-    return {"frame": 0, "region": f"{cw}x{ch} input px at ({x0}, {y0}) with a {halo}-px halo",
-            "reference": "torch FP32 SPAN (tests/torch_ref.py)", "max_abs_255": err * 255.0, "psnr_db": db, "ok": ok}
+    out = {"frame": 0, "region": f"{cw}x{ch} input px at ({x0}, {y0}) with a {halo}-px halo",
+           "reference": "torch FP32 SPAN (tests/torch_ref.py)", "max_abs_255": err * 255.0, "psnr_db": db, "ok": ok}
+    if leg["fp8"]:
+        out["note"] = ("with the configs' Kaiming-seeded weights the activations of blocks 1-5 (the E4M3 ones) "
+                       "decay below 1e-5, so the output is carried by conv_1 and block 0 (FP16) and matches the "
+                       "FP16 leg's here; E4M3 on a network whose every block carries signal is checked by "
+                       "tests/test_span_gpu.py::test_fp8_live_blocks_psnr")
+    return out
 
 
 def e2e_leg(leg, D, eng, sh, stream, d_in, steps, warmup, display):
