@@ -46,14 +46,17 @@ constexpr int kPairMaxK = 12;      // K steps per input row: 2, 3 (conv_1), 5, 6
 // (entry e goes to group e % groups, so a group owns the slots s with s % groups = g and that many
 // rows are in the epilogue at once); a warp covers 32 pixels x warp_cols channels. Measured on
 // 8 x 1080p (in-process A/B): without a residual, 3 groups of 4 warps x 48 channels beat 2 groups of
-// 12 warps x 16 channels by 5-18 % (fewer epilogue warps disturb the MMA issuer less); the SPAB gate
-// layers, which also hold the residual words, are 20-30 % slower that way and keep 2 x 12 x 16.
-template <int kCoutPad, int kEpi>
+// 12 warps x 16 channels by 5-18 % (fewer epilogue warps disturb the MMA issuer less); the FP16 SPAB
+// gate layers, which also hold 24 residual words a thread, are 20-30 % slower that way and keep
+// 2 x 12 x 16. The E4M3 gates hold half those words and take 3 x 4 x 48 (128 registers, no spills):
+// 10 % faster than 2 x 12 x 16, their instruction stream being the bound (`wide`).
+template <int kCoutPad, int kEpi, bool kFp8 = false>
 struct PairShape {
   static constexpr bool residual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
-  static constexpr int groups = residual ? 2 : 3;
+  static constexpr bool wide = residual && kFp8 && kCoutPad == 48;
+  static constexpr int groups = residual && !wide ? 2 : 3;
   // 64 channels (the IFNet residual convs): 32 columns a warp, 2 x 8 warps (576 threads)
-  static constexpr int cols = residual ? (kCoutPad % 32 == 0 ? 32 : 16) : (kCoutPad % 48 == 0 ? 48 : 32);
+  static constexpr int cols = wide ? 48 : residual ? (kCoutPad % 32 == 0 ? 32 : 16) : (kCoutPad % 48 == 0 ? 48 : 32);
   static_assert(kStackSlots % groups == 0, "groups divide the accumulator slots");
   static constexpr int warp_cols = kCoutPad < cols ? kCoutPad : cols;
   static_assert(warp_cols % 16 == 0 && kCoutPad % warp_cols == 0, "16-column TMEM loads per warp");
@@ -992,7 +995,7 @@ template <bool kFp8, int kCoutPad, int kEpi, int kOut>
 __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs& a) {
   static_assert(kCoutPad == 16 || kCoutPad == 48 || kCoutPad == 64, "paired kernel: 16, 48 or 64 output channels");
   static_assert(kStackBlocks * kCoutPad <= kStackTmemCols, "TMEM blocks");
-  constexpr int kGroupWarps = PairShape<kCoutPad, kEpi>::group_warps;
+  constexpr int kGroupWarps = PairShape<kCoutPad, kEpi, kFp8>::group_warps;
   constexpr uint32_t R = kStackSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -1115,9 +1118,9 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     // The groups of warps take the accumulator entries in turn (PairShape), so that many
     // rows are in the epilogue at once. A warp covers 32 lanes (pixels) x kCols columns of its
     // group's entries in 16-column steps; its residual words are loaded before it waits.
-    constexpr int kCols = PairShape<kCoutPad, kEpi>::warp_cols;
+    constexpr int kCols = PairShape<kCoutPad, kEpi, kFp8>::warp_cols;
     constexpr int kSteps = kCols / 16;
-    constexpr uint32_t kG = static_cast<uint32_t>(PairShape<kCoutPad, kEpi>::groups);
+    constexpr uint32_t kG = static_cast<uint32_t>(PairShape<kCoutPad, kEpi, kFp8>::groups);
     constexpr bool kResidual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
     // slots 0 and 1 add their second TMEM block 16 columns at a time on the gated and residual shapes
     // (there a whole second block of live registers beside v and the residual words spilled: ptxas -v;
@@ -1247,7 +1250,7 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
 
 // The kernel: one block of a cluster pair per SM, its register budget set by its thread count.
 template <bool kFp8, int kCoutPad, int kEpi, int kOut>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, kEpi>::threads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<kCoutPad, kEpi, kFp8>::threads, 1)
     conv3p_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ ConvArgs a) {
   conv3p_body<kFp8, kCoutPad, kEpi, kOut>(maps, a);
 }

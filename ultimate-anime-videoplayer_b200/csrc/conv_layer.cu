@@ -52,7 +52,7 @@ void launch_impl(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, cons
 }
 template <bool F8, int N, int E, int O>
 void launch_paired(dim3 grid, size_t smem, cudaStream_t s, const ConvMaps& m, const ConvArgs& a) {
-  conv3p_kernel<F8, N, E, O><<<grid, PairShape<N, E>::threads, smem, s>>>(m, a);  // clusters of 2 (__cluster_dims__)
+  conv3p_kernel<F8, N, E, O><<<grid, PairShape<N, E, F8>::threads, smem, s>>>(m, a);  // clusters of 2 (__cluster_dims__)
 }
 
 constexpr int kKindGeneric = 0, kKindPaired = 2;
@@ -74,7 +74,7 @@ struct KernelEntry {
 #define KB2_PAIRED(F8, N, E, O)                                                                          \
   KernelEntry {                                                                                          \
     kKindPaired, F8, N, E, O, &launch_paired<F8, N, E, O>,                                               \
-        reinterpret_cast<const void*>(&conv3p_kernel<F8, N, E, O>), PairShape<N, E>::threads             \
+        reinterpret_cast<const void*>(&conv3p_kernel<F8, N, E, O>), PairShape<N, E, F8>::threads             \
   }
 
 // The instantiations the engines use: 3x3 layers on the pair kernel, the 1x1 convs (conv_cat, the
