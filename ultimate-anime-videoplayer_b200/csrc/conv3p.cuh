@@ -46,14 +46,15 @@ constexpr int kPairMaxK = 12;      // K steps per input row: 2, 3 (conv_1), 5, 6
 // (entry e goes to group e % groups, so a group owns the slots s with s % groups = g and that many
 // rows are in the epilogue at once); a warp covers 32 pixels x warp_cols channels. Measured on
 // 8 x 1080p (in-process A/B): without a residual, 3 groups of 4 warps x 48 channels beat 2 groups of
-// 12 warps x 16 channels by 5-18 % (fewer epilogue warps disturb the MMA issuer less); the FP16 SPAB
-// gate layers, which also hold 24 residual words a thread, are 20-30 % slower that way and keep
-// 2 x 12 x 16. The E4M3 gates hold half those words and take 3 x 4 x 48 (128 registers, no spills):
-// 10 % faster than 2 x 12 x 16, their instruction stream being the bound (`wide`).
+// 12 warps x 16 channels by 5-18 % (fewer epilogue warps disturb the MMA issuer less). The 48-channel
+// SPAB gates, which also hold the residual words, take 3 x 4 x 48 too (`wide`, 128 registers): the
+// E4M3 gates 10 % and the FP16 gates 2 % faster than on 2 x 12 x 16 with the epilogue's constants in
+// the parameter space (before that move, with per-warp register biases, the FP16 gates spilled on
+// 3 x 4 x 48 and ran 20-30 % slower). The 64-channel residual shape keeps 2 groups x 8 x 32.
 template <int kCoutPad, int kEpi, bool kFp8 = false>
 struct PairShape {
   static constexpr bool residual = kEpi == kEpiSpanAttn || kEpi == kEpiResPrelu;
-  static constexpr bool wide = residual && kFp8 && kCoutPad == 48;
+  static constexpr bool wide = residual && kCoutPad == 48;
   static constexpr int groups = residual && !wide ? 2 : 3;
   // 64 channels (the IFNet residual convs): 32 columns a warp, 2 x 8 warps (576 threads)
   static constexpr int cols = wide ? 48 : residual ? (kCoutPad % 32 == 0 ? 32 : 16) : (kCoutPad % 48 == 0 ? 48 : 32);
