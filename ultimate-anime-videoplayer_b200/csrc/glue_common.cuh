@@ -68,25 +68,38 @@ __device__ __forceinline__ void frame_rgb(const uint2* fr, int Wp, int Y, int X,
   c[2] = __low2float(*reinterpret_cast<const __half2*>(&q.y));
 }
 
+// The bilinear mix of the four 8-byte FP16 pixels (4 channels) around a warp position, in packed
+// FP16 pairs: lerp(lerp(a, b, wx), lerp(d, e, wx), wy), each lerp as p + w (q - p). The positions
+// (tap indices and weights, warp_tap) are computed in FP32 as the reference states them; only the
+// mixing of the pixel values, which are FP16 like the results' consumers, runs on pairs.
+__device__ __forceinline__ void bilerp_h2(const uint2* fr, int Wp, const AxisTap& tx, const AxisTap& ty, __half2& c01,
+                                          __half2& c23) {
+  const __half2 wx = __float2half2_rn(tx.t), wy = __float2half2_rn(ty.t);
+  const uint2 qa = __ldg(fr + (ty.lo * Wp + tx.lo));
+  const uint2 qb = __ldg(fr + (ty.lo * Wp + tx.hi));
+  const uint2 qd = __ldg(fr + (ty.hi * Wp + tx.lo));
+  const uint2 qe = __ldg(fr + (ty.hi * Wp + tx.hi));
+  auto h = [](uint32_t u) { return *reinterpret_cast<const __half2*>(&u); };
+  const __half2 t0 = __hfma2(wx, __hsub2(h(qb.x), h(qa.x)), h(qa.x));
+  const __half2 t1 = __hfma2(wx, __hsub2(h(qb.y), h(qa.y)), h(qa.y));
+  const __half2 b0 = __hfma2(wx, __hsub2(h(qe.x), h(qd.x)), h(qd.x));
+  const __half2 b1 = __hfma2(wx, __hsub2(h(qe.y), h(qd.y)), h(qd.y));
+  c01 = __hfma2(wy, __hsub2(b0, t0), t0);
+  c23 = __hfma2(wy, __hsub2(b1, t1), t1);
+}
+
 // Backward warp of the 3 channels of a padded frame (`fr`: its first pixel) at pixel (Y, X) by
 // flow (fx, fy).
 __device__ __forceinline__ void warp3(const uint2* fr, const IfFrames& F, int Y, int X, float fx, float fy,
                                       float out[3]) {
   const AxisTap tx = warp_tap(X, fx, F.Wp);
   const AxisTap ty = warp_tap(Y, fy, F.Hp);
-  const float wx1 = __fsub_rn(1.0f, tx.t), wy1 = __fsub_rn(1.0f, ty.t);
-  float a[3], b[3], d[3], e[3];
-  frame_rgb(fr, F.Wp, ty.lo, tx.lo, a);
-  frame_rgb(fr, F.Wp, ty.lo, tx.hi, b);
-  frame_rgb(fr, F.Wp, ty.hi, tx.lo, d);
-  frame_rgb(fr, F.Wp, ty.hi, tx.hi, e);
-#pragma unroll
-  for (int c = 0; c < 3; ++c) {
-    // (a (1 - wx) + b wx) (1 - wy) + (d (1 - wx) + e wx) wy
-    const float top = __fadd_rn(__fmul_rn(a[c], wx1), __fmul_rn(b[c], tx.t));
-    const float bot = __fadd_rn(__fmul_rn(d[c], wx1), __fmul_rn(e[c], tx.t));
-    out[c] = __fadd_rn(__fmul_rn(top, wy1), __fmul_rn(bot, ty.t));
-  }
+  __half2 c01, c23;
+  bilerp_h2(fr, F.Wp, tx, ty, c01, c23);
+  const float2 rg = __half22float2(c01);
+  out[0] = rg.x;
+  out[1] = rg.y;
+  out[2] = __low2float(c23);
 }
 
 __device__ __forceinline__ void store_motion(float* p, float v) { *p = v; }

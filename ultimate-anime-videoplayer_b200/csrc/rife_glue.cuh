@@ -59,18 +59,14 @@ __device__ __forceinline__ void half4(uint2 q, float c[4]) {
 __device__ __forceinline__ void warp4(const uint2* fr, int Hp, int Wp, int Y, int X, float fx, float fy, float out[4]) {
   const AxisTap tx = warp_tap(X, fx, Wp);
   const AxisTap ty = warp_tap(Y, fy, Hp);
-  const float wx1 = __fsub_rn(1.0f, tx.t), wy1 = __fsub_rn(1.0f, ty.t);
-  float a[4], b[4], d[4], e[4];
-  half4(__ldg(fr + (static_cast<size_t>(ty.lo) * Wp + tx.lo)), a);
-  half4(__ldg(fr + (static_cast<size_t>(ty.lo) * Wp + tx.hi)), b);
-  half4(__ldg(fr + (static_cast<size_t>(ty.hi) * Wp + tx.lo)), d);
-  half4(__ldg(fr + (static_cast<size_t>(ty.hi) * Wp + tx.hi)), e);
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const float top = __fadd_rn(__fmul_rn(a[c], wx1), __fmul_rn(b[c], tx.t));
-    const float bot = __fadd_rn(__fmul_rn(d[c], wx1), __fmul_rn(e[c], tx.t));
-    out[c] = __fadd_rn(__fmul_rn(top, wy1), __fmul_rn(bot, ty.t));
-  }
+  __half2 c01, c23;
+  bilerp_h2(fr, Wp, tx, ty, c01, c23);
+  const float2 a = __half22float2(c01);
+  const float2 b = __half22float2(c23);
+  out[0] = a.x;
+  out[1] = a.y;
+  out[2] = b.x;
+  out[3] = b.y;
 }
 
 // Rows a glue thread walks down its column: its column's resize taps and source caches are set
