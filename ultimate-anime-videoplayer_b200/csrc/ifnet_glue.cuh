@@ -192,6 +192,16 @@ __device__ __forceinline__ void store_chunks(uint8_t* row, int wo, int ox, const
   }
 }
 
+// store_chunks of 16 planes already paired as FP16.
+__device__ __forceinline__ void store_chunks_h2(uint8_t* row, int wo, int ox, const __half2 v[8]) {
+  const int xs = (ox & 1) * (wo >> 1) + (ox >> 1);
+  const uint32_t* u = reinterpret_cast<const uint32_t*>(v);
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch)
+    *reinterpret_cast<uint4*>(row + (static_cast<size_t>(ch) * wo + xs) * 16) =
+        make_uint4(u[4 * ch], u[4 * ch + 1], u[4 * ch + 2], u[4 * ch + 3]);
+}
+
 // Input of block K as row-chunked FP16 [n][Hp/s][2][Wp/s][8 halves] (16 channels, 12 or 7 used;
 // each chunk row parity-split):
 // the block's planes resized to 1/s (not for s = 1), the flow planes then divided by s. One
@@ -248,7 +258,11 @@ __global__ void __launch_bounds__(kGlueThreads, 4)
       for (int j = 0; j < K; ++j) cols[j].lo = -1;
       for (int oy = y0; oy < y0 + R && oy < ho; ++oy) {
         const AxisTap ty = resize_tap(oy, static_cast<float>(s), F.Hp);
-        float h[2][12];
+        // the planes' resize (x by the pair's shuffle, then y) as packed FP16 pairs: the block
+        // input is stored in FP16, and no tap position depends on it
+        constexpr int np = (nc + 1) / 2;
+        const __half2 wx = __float2half2_rn(tx.t), wy = __float2half2_rn(ty.t);
+        __half2 h[2][np];
 #pragma unroll
         for (int yy = 0; yy < 2; ++yy) {
           const int Y = yy ? ty.hi : ty.lo;
@@ -258,23 +272,30 @@ __global__ void __launch_bounds__(kGlueThreads, 4)
             frame_rgb(F.pad0 + frame, F.Wp, Y, X, q);
             frame_rgb(F.pad1 + frame, F.Wp, Y, X, q + 3);
             q[6] = timestep;
+            q[7] = 0.0f;
           } else {
             block_planes<K>(F, L, FF, n, Y, X, cols, timestep, q);
           }
 #pragma unroll
-          for (int c = 0; c < nc; ++c) {
-            const float p = __shfl_xor_sync(0xffffffffu, q[c], 1);
-            h[yy][c] = side ? lerp_rn(p, q[c], tx.t) : lerp_rn(q[c], p, tx.t);
+          for (int i = 0; i < np; ++i) {
+            const __half2 mine = __floats2half2_rn(q[2 * i], q[2 * i + 1]);
+            const uint32_t mu = *reinterpret_cast<const uint32_t*>(&mine);
+            const uint32_t pu = __shfl_xor_sync(0xffffffffu, mu, 1);
+            const __half2 other = *reinterpret_cast<const __half2*>(&pu);
+            const __half2 lo = side ? other : mine, hi = side ? mine : other;
+            h[yy][i] = __hfma2(wx, __hsub2(hi, lo), lo);
           }
         }
-        float v[16];
+        __half2 v2[8];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) v[c] = c < nc ? lerp_rn(h[0][c], h[1][c], ty.t) : 0.0f;
-        if constexpr (K > 0) {
-#pragma unroll
-          for (int c = 8; c < 12; ++c) v[c] = __fmul_rn(v[c], inv);
+        for (int i = 0; i < 8; ++i)
+          v2[i] = i < np ? __hfma2(wy, __hsub2(h[1][i], h[0][i]), h[0][i]) : __floats2half2_rn(0.0f, 0.0f);
+        if constexpr (K > 0) {  // the flow planes 8-11 divided by s (a power of two: exact)
+          const __half2 inv2 = __float2half2_rn(inv);
+          v2[4] = __hmul2(v2[4], inv2);
+          v2[5] = __hmul2(v2[5], inv2);
         }
-        if (live && side == 0) store_chunks(out + (static_cast<size_t>(n) * ho + oy) * 2 * wo * 16, wo, ox, v);
+        if (live && side == 0) store_chunks_h2(out + (static_cast<size_t>(n) * ho + oy) * 2 * wo * 16, wo, ox, v2);
       }
     }
   }
