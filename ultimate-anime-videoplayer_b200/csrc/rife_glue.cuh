@@ -373,9 +373,10 @@ __device__ __forceinline__ void final_flow(const RifeZ& Z, int n, int Y, int X, 
 
 // The interpolated frame in the window: out = warp(A) m + warp(B) (1 - m), m = sigmoid(mask),
 // NCHW FP16 [n][3][H][W]; L = the last block's index. One thread per column walking kRifeRunRows
-// rows with the column caches of Z_0 .. Z_(L-1).
+// rows with the column caches of Z_0 .. Z_(L-1). Four blocks an SM (64 registers, no spills): the
+// gathers' latency wants the warps; at the compiler's own 128 registers the kernel ran 35 % slower.
 template <int L>
-__global__ void __launch_bounds__(kGlueThreads) rife_finish_kernel(IfFrames F, RifeZ Z, int batch,
+__global__ void __launch_bounds__(kGlueThreads, 4) rife_finish_kernel(IfFrames F, RifeZ Z, int batch,
                                                                    __half* __restrict__ out) {
   const int x = blockIdx.x * blockDim.x + threadIdx.x;
   if (x >= F.W) return;
@@ -410,7 +411,7 @@ __global__ void __launch_bounds__(kGlueThreads) rife_finish_kernel(IfFrames F, R
 // The motion variant over the padded plane: the final flow [n][4][Hp][Wp] and sigmoid(mask)
 // [n][1][Hp][Wp], T = float or __half; the walk of rife_finish_kernel.
 template <int L, typename T>
-__global__ void __launch_bounds__(kGlueThreads) rife_motion_kernel(IfFrames F, RifeZ Z, int batch,
+__global__ void __launch_bounds__(kGlueThreads, 4) rife_motion_kernel(IfFrames F, RifeZ Z, int batch,
                                                                    T* __restrict__ flow, T* __restrict__ mask) {
   const int X = blockIdx.x * blockDim.x + threadIdx.x;
   if (X >= F.Wp) return;
