@@ -218,6 +218,10 @@ def test_refuses_bad_arguments(pieces):
     with pytest.raises(kb.KB2Error) as e:
         kb.rife_blob_from_onnx(pieces[:1], [])
     assert e.value.status == kb.KB2_INVALID_ARGUMENT
+    for bad in ([8, 3], [0, 8], [64, 8]):
+        with pytest.raises(kb.KB2Error) as e:
+            kb.rife_blob_from_onnx(pieces[:3], bad)
+        assert e.value.status == kb.KB2_INVALID_ARGUMENT and "reductions" in e.value.message
 
 
 def test_blob_creates_an_engine_shape_check(pieces):

@@ -652,6 +652,9 @@ Status rife_blob_from_onnx(const uint8_t* const* pieces, const uint64_t* sizes, 
                            std::vector<uint8_t>& blob) {
   if (pieces == nullptr || sizes == nullptr || reduce == nullptr) return refuse(KB2_INVALID_ARGUMENT, "null argument");
   if (blocks < 2 || blocks > 5) return refuse(KB2_INVALID_ARGUMENT, "RIFE 4.2x: 2 to 5 blocks");
+  for (int k = 0; k < blocks; ++k)
+    if (reduce[k] < 1 || reduce[k] > 32 || (reduce[k] & (reduce[k] - 1)) != 0)
+      return refuse(KB2_INVALID_ARGUMENT, "RIFE 4.2x: block input reductions are powers of two, 1 to 32");
   std::vector<float> plan(12, 0.0f), params;
   plan[0] = static_cast<float>(blocks);
   plan[11] = 16.0f;
