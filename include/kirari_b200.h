@@ -118,7 +118,8 @@ typedef struct kb2_engine kb2_engine;
  * activation) and a last ConvTranspose 4x4 stride 2; Cast and Identity pass through; a 1x1 Conv that
  * follows a conv is folded into it, a depthwise 3x3 stored as a diagonal one (the reference's reader).
  * Initializers and Constant values: FLOAT, FLOAT16, FLOAT8E4M3FN or INT8, raw or typed, inline.
- * reduce[k]: block k's input reduction (the plan; the widths come from the weights), 2 to 5 blocks.
+ * reduce[k]: block k's input reduction (the plan: a power of two, 1 to 32; the widths come from the
+ * weights), 2 to 5 blocks.
  * blob = NULL: *blob_bytes receives the size; else *blob_bytes is the buffer's capacity on entry and
  * the blob's size on return. Refusals: KB2_WEIGHTS_INVALID (unreadable, or not this topology),
  * KB2_FORMAT_UNSUPPORTED (weights outside the file, segments, sparse initializers, other element
