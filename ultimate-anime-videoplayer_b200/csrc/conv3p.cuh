@@ -870,18 +870,25 @@ constexpr uint32_t pair_ring() {
 // With 12 input slots the input phase is one bit per period (`ph`); with 6 it is 0 for rows 0-5 and
 // 1 for rows 6-11 of every period (`ph` stays 0). The issuing thread then executes little besides
 // its two asm blocks.
-template <bool kFp8, int kCoutPad, int kNK, int kK>
+// Input-phase flips over a 12-row period of a ring of kRing slots: the period's rows wrap the ring
+// 12 / kRing times, so the phase of slot 0 flips between periods when that count is odd.
+template <uint32_t kRing>
+constexpr uint32_t pair_period_flip() {
+  static_assert(12u % kRing == 0u, "the ring divides the 12-row period");
+  return (12u / kRing) & 1u;
+}
+
+template <bool kFp8, int kCoutPad, int kNK, uint32_t kRing, int kK>
 __device__ __forceinline__ bool pair_row_k(const PairRowCtx<kNK>& c, uint32_t ph, uint32_t& pre) {
-  constexpr uint32_t kRing = pair_ring<kNK>();
   constexpr uint32_t kIn = kK % kRing;
-  constexpr uint32_t kInPh = kRing == 6u && kK >= 6 ? 1u : 0u;
+  constexpr uint32_t kInPh = (static_cast<uint32_t>(kK) / kRing) & 1u;
   constexpr uint32_t kSlot = kK % 6;
   constexpr uint32_t kAccPh = kK >= 6 ? 1u : 0u;
   constexpr uint32_t kStart = kSlot >= 2 ? kSlot - 2 : kSlot + 4;
   constexpr uint32_t kNext = (kK + 1) % 12;
   constexpr uint32_t kNextIn = kNext % kRing;
   // the next row's input phase: row 0 of the next period when k = 11
-  constexpr uint32_t kNextInPh = kK == 11 ? (kRing == 12u ? 1u : 0u) : (kRing == 6u && kNext >= 6 ? 1u : 0u);
+  constexpr uint32_t kNextInPh = kK == 11 ? pair_period_flip<kRing>() : (kNext / kRing) & 1u;
   constexpr uint32_t kNextSlot = kNext % 6;
   constexpr uint32_t kNextAccPh = kNext >= 6 ? 1u : 0u;
   constexpr uint32_t kIdClear = make_idesc(256, kCoutPad);
@@ -907,15 +914,16 @@ __device__ __forceinline__ bool pair_row_k(const PairRowCtx<kNK>& c, uint32_t ph
   return true;
 }
 
-template <bool kFp8, int kCoutPad, int kNK, int... kKs>
+template <bool kFp8, int kCoutPad, int kNK, uint32_t kRing, int... kKs>
 __device__ __forceinline__ bool pair_period(const PairRowCtx<kNK>& c, uint32_t ph, uint32_t& pre,
                                             std::integer_sequence<int, kKs...>) {
-  return (pair_row_k<kFp8, kCoutPad, kNK, kKs>(c, ph, pre) && ...);
+  return (pair_row_k<kFp8, kCoutPad, kNK, kRing, kKs>(c, ph, pre) && ...);
 }
 
 // The MMA issuer of the pair (block 0, one thread), for rows of kNK K steps. Every input row is
-// alike (uniform rows), so the issuer only needs the number of input rows of its items.
-template <bool kFp8, int kCoutPad, int kNK>
+// alike (uniform rows), so the issuer only needs the number of input rows of its items. kRing: the
+// input ring's slot count (pair_ring, or kColsRing for the four-source kEpiColsBias layers).
+template <bool kFp8, int kCoutPad, int kNK, uint32_t kRing = pair_ring<kNK>()>
 __device__ __forceinline__ void pair_issue(const PairIssue& is) {
   static_assert(kStackSlots == 6, "the 12-row period assumes 6 accumulator slots");
   const ConvArgs& a = is.a;
@@ -950,13 +958,12 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
     int n, pair, y0, y1;
     while (sp.next(a, n, pair, y0, y1)) total += static_cast<uint32_t>(y1 - y0 + 2 + pair_pad(y1 - y0));
   }
-  constexpr uint32_t kRing = pair_ring<kNK>();
-  if (a.ring != kRing) return;  // the host sizes the ring by pair_ring
-  uint32_t ph = 0;   // input ring phase of the current period (12 slots; 6 slots: always 0)
+  if (a.ring != kRing) return;  // the host sizes the ring by pair_ring / kColsRing
+  uint32_t ph = 0;   // input ring phase of slot 0 in the current period
   uint32_t pre = 0;  // next row's barriers found complete by the previous row: 1 = input, 2 = slot
   uint32_t g = 0;
-  for (; g + 12u <= total; g += 12u, ph ^= (kRing == 12u ? 1u : 0u))
-    if (!pair_period<kFp8, kCoutPad, kNK>(c, ph, pre, std::make_integer_sequence<int, 12>{})) return;
+  for (; g + 12u <= total; g += 12u, ph ^= pair_period_flip<kRing>())
+    if (!pair_period<kFp8, kCoutPad, kNK, kRing>(c, ph, pre, std::make_integer_sequence<int, 12>{})) return;
   // the last rows (fewer than a period), with run-time positions
   RingPos in{0, ph};
   RingPos acc{0, 0};
@@ -995,6 +1002,8 @@ __device__ __forceinline__ void pair_issue(const PairIssue& is) {
 template <bool kFp8, int kCoutPad, int kEpi, int kOut>
 __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs& a) {
   static_assert(kCoutPad == 16 || kCoutPad == 48 || kCoutPad == 64, "paired kernel: 16, 48 or 64 output channels");
+  static_assert(kEpi != kEpiColsBias || (kCoutPad == 48 && !kFp8 && (kOut == kOutPixShuf2 || kOut == kOutPixShuf2Display)),
+                "columns in N: FP16, 3 kernel columns x 16 channels, a pixel-shuffled output");
   static_assert(kStackBlocks * kCoutPad <= kStackTmemCols, "TMEM blocks");
   constexpr int kGroupWarps = PairShape<kCoutPad, kEpi, kFp8>::group_warps;
   constexpr uint32_t R = kStackSlots;
@@ -1031,6 +1040,8 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     mbar_init(wbar, 1);
     mbar_init(wpeer, 1);
     mbar_init(drain, 1);
+    if constexpr (kEpi == kEpiColsBias)
+      for (uint32_t i = 0; i < 6; ++i) mbar_init(&bars[kStackXchgBar + i], 4);  // the 4 warps of a group
     fence_mbar_init();
   }
   for (int j = threadIdx.x; j < kMaxN; j += blockDim.x) {
@@ -1040,7 +1051,11 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     s_k[j] = j < a.n_ksteps
                  ? (static_cast<uint64_t>(a.ks[j].a_off >> 4) | (static_cast<uint64_t>(a.ks[j].lbo >> 4) << 16))
                  : 0;
-  if (warp == 0 && lane == 0) prefetch_tmap(&maps.m[0]);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&maps.m[0]);
+    if constexpr (kEpi == kEpiColsBias)
+      for (int src = 1; src < 4; ++src) prefetch_tmap(&maps.m[src]);
+  }
   if (warp == 1) {
     tmem_alloc_pair(tmem_holder, kStackTmemCols);
     tmem_relinquish_pair();
@@ -1075,8 +1090,15 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
             break;
           }
           if (rank == 0) mbar_arrive_expect_tx(&full[in.idx], 2u * a.slot_bytes);
-          // one box: 128 pixels from x0 - 1 (zero fill outside the image), all chunks
-          tma_load_4d_pair(ring + in.idx * a.slot_bytes, &maps.m[0], full0 + in.idx * 8u, (x0 - 1) * 2, 0, r, n);
+          // one box a source: 128 pixels from x0 - 1 (zero fill outside the image), all chunks
+          if constexpr (kEpi == kEpiColsBias) {
+#pragma unroll
+            for (int src = 0; src < 4; ++src)
+              tma_load_4d_pair(ring + in.idx * a.slot_bytes + src * a.src_bytes, &maps.m[src], full0 + in.idx * 8u,
+                               (x0 - 1) * 2, 0, r, n);
+          } else {
+            tma_load_4d_pair(ring + in.idx * a.slot_bytes, &maps.m[0], full0 + in.idx * 8u, (x0 - 1) * 2, 0, r, n);
+          }
           in.advance(a.ring);
         }
       }
@@ -1091,7 +1113,9 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
           const PairIssue is{a, smem_u32(ring), smem_u32(sw), smem_u32(zero_b), tmem_base, s_k, full, done, slot_free};
           // rows of K steps as the host admits them (conv_layer.cu pair_admits): 64 output channels
           // 12 or 3 in FP16, 6 in E4M3 (64 input channels); 48: 12 (FP16), 9, 5, 3 or 2
-          if constexpr (kCoutPad == 64 && kFp8) {
+          if constexpr (kEpi == kEpiColsBias) {
+            pair_issue<kFp8, kCoutPad, 12, kColsRing>(is);  // 4 sources x 3 channel pairs
+          } else if constexpr (kCoutPad == 64 && kFp8) {
             pair_issue<kFp8, kCoutPad, 6>(is);
           } else if constexpr (kCoutPad == 64) {
             if (a.n_ksteps == 12) pair_issue<kFp8, kCoutPad, 12>(is);
@@ -1126,7 +1150,7 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     // slots 0 and 1 add their second TMEM block 16 columns at a time on the gated and residual shapes
     // (there a whole second block of live registers beside v and the residual words spilled: ptxas -v;
     // measured 3-9 % faster), and all at once elsewhere (one TMEM wait; 1-2 % faster there)
-    constexpr bool kPieceAdd = kResidual;
+    constexpr bool kPieceAdd = kResidual || kEpi == kEpiColsBias;  // the column sum holds 48 values too
     const int ew = warp - 2;
     const uint32_t grp = static_cast<uint32_t>(ew / kGroupWarps);
     const int quad = warp & 3;
@@ -1134,22 +1158,52 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t my_cols = tmem_base + lane_addr + static_cast<uint32_t>(col0);
     const uint32_t free0 = cluster_addr(smem_u32(slot_free), 0);  // block 0's slot_free[0]
-    // the group's slots start free (phase 0 of slot_free)
+    // the group's slots start free (phase 0 of slot_free); with the kernel columns in N, slot 4's
+    // first phase is group 2's (below)
     if (lane == 0)
-      for (uint32_t s = grp; s < R; s += kG) mbar_arrive_remote_relaxed(free0 + s * 8u);
+      for (uint32_t s = grp; s < R; s += kG)
+        if (kEpi != kEpiColsBias || s != 4u) mbar_arrive_remote_relaxed(free0 + s * 8u);
     RingPos acc{0, 0};  // slot of the current entry
     RingPos in{0, 0};   // input ring position of the row that completes output row y (y + 2 of the band)
     uint32_t eg = 0;     // entry index modulo the group count
     bool ok = true;
+    // kEpiColsBias: the group's exchange buffer in use (0 / 1) and the phase bit of each one's barrier
+    uint32_t xbuf = 0, xph = 0;
+    float* xchg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kStackXchgOff) + grp * (2u * 4u * 32u);
+    // kEpiColsBias: the cluster's input rows (= entries, one each) and the current entry's index.
+    // With a ring of 4 input slots a parity wait can pass falsely: waiting for the k-th completion
+    // of a slot's `done` succeeds while completion k - 1 is still pending (same parity as "k done").
+    // Entry e waits for input row e + 2; every group's previous wait (entry e - 3, row e - 1) has
+    // already seen row e - 2, the slot's previous use, complete, except for a group's first entry:
+    // group 2 starts at entry 2 (row 4, the second use of slot 0), so it first waits for row 0. That
+    // wait could alias too if row 4 had completed as well, so row 4 is held back until it is done:
+    // slot 4's first phase (entry 4, issued with row 4) is released by group 2 after the wait.
+    uint32_t total_rows = 0, ent = 0;
+    if constexpr (kEpi == kEpiColsBias) {
+      PairSpan sp0(a, cluster_id_x(), cluster_count_x());
+      int n0, p0, r0, r1;
+      while (sp0.next(a, n0, p0, r0, r1)) total_rows += static_cast<uint32_t>(r1 - r0 + 2 + pair_pad(r1 - r0));
+      static_assert(kColsRing == 4 && kStackSlots == 6, "the start-up order below covers 4 input and 6 accumulator slots");
+      if (grp == 2u) {
+        if (total_rows > 4u) {
+          const bool got0 = wait_bar(&done[0], 0u, a.err, kErrWaitEpilogue);
+          if (!__all_sync(0xffffffffu, got0)) ok = false;
+        }
+        if (lane == 0) mbar_arrive_remote_relaxed(free0 + 4u * 8u);
+      }
+    }
     PairSpan sp(a, cluster_id_x(), cluster_count_x());
     int n, pair, y0, y1;
     while (ok && sp.next(a, n, pair, y0, y1)) {
       const int m = quad * 32 + lane;
-      const int x = (2 * pair + static_cast<int>(rank)) * a.strip_w + m;
-      const bool store = m < a.strip_w && x < a.W;
+      // the strip column this lane writes: its own pixel, or with the kernel columns in N the pixel
+      // of slot position m, one right of the slot's first (x0 - 1): lanes 0 and 127 write nothing
+      const int xc = kEpi == kEpiColsBias ? m - 1 : m;
+      const int x = (2 * pair + static_cast<int>(rank)) * a.strip_w + xc;
+      const bool store = xc >= 0 && xc < a.strip_w && x < a.W;
       in.advance(a.ring);  // the band's input rows y0 - 1 and y0 complete no output row
       in.advance(a.ring);
-      for (int y = y0; y < y1; ++y, acc.advance(R), in.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1) {
+      for (int y = y0; y < y1; ++y, acc.advance(R), in.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1, ++ent) {
         if (eg != grp) continue;
         const uint32_t s = acc.idx;
         uint32_t res[kCols / 2];
@@ -1187,7 +1241,56 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote_relaxed(free0 + s * 8u);
-        if (store) {
+        if constexpr (kEpi == kEpiColsBias) {
+          // out[c] = D[m - 1][c] + D[m][16 + c] + D[m + 1][32 + c]: neighbours within the warp by
+          // shuffles; lanes 0 and 31 take theirs from the warps of the adjacent lane quadrants, which
+          // process the same entry, through a shared buffer (two of them alternate, so a buffer is
+          // rewritten only after all four warps passed the barrier of the other one)
+          float* xb = xchg + xbuf * (4u * 32u);
+          if (lane == 31) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xb[quad * 32 + j] = v[j];
+          }
+          if (lane == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xb[quad * 32 + 16 + j] = v[32 + j];
+          }
+          __syncwarp();
+          uint64_t* xbar = bars + kStackXchgBar + grp * 2u + xbuf;
+          if (lane == 0) mbar_arrive(xbar);
+          const bool xok = wait_bar(xbar, (xph >> xbuf) & 1u, a.err, kErrWaitEpilogue);
+          if (!__all_sync(0xffffffffu, xok)) {
+            ok = false;
+            break;
+          }
+          xph ^= 1u << xbuf;
+          xbuf ^= 1u;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float l = __shfl_up_sync(0xffffffffu, v[j], 1);
+            float r = __shfl_down_sync(0xffffffffu, v[32 + j], 1);
+            if (lane == 0) l = quad > 0 ? xb[(quad - 1) * 32 + j] : 0.0f;
+            if (lane == 31) r = quad < 3 ? xb[(quad + 1) * 32 + 16 + j] : 0.0f;
+            v[16 + j] += l + r;
+          }
+          if (store) {
+            float* o = v + 16;
+            if (y == 0 || y == a.H - 1 || x == 0 || x == a.W - 1) {
+              // taps outside the image read zeros in the layer this conv stands for: drop their bias terms
+#pragma unroll
+              for (int t = 0; t < 9; ++t) {
+                const int ky = t / 3, kx = t % 3;
+                const bool outside =
+                    (ky == 0 && y == 0) || (ky == 2 && y == a.H - 1) || (kx == 0 && x == 0) || (kx == 2 && x == a.W - 1);
+                if (outside) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) o[j] -= a.tap_bias[t][j];
+                }
+              }
+            }
+            epilogue_cols<kEpiBias, kOut, 16, kConstsBias>(a, a.cbias, a.cscale, s_slope, o, 0, n, y, x, 0, nullptr);
+          }
+        } else if (store) {
           // Bias and scale come from the parameter space (ConvArgs::cbias / cscale) at the warp's
           // first channel. Where a warp covers every channel that offset is 0; the FP16 48-channel
           // gates (three column groups) dispatch it as a compile-time offset too, so the constants
@@ -1228,9 +1331,19 @@ __device__ __forceinline__ void conv3p_body(const ConvMaps& maps, const ConvArgs
       vin.retreat(a.ring);
       vin.retreat(a.ring);
       for (int k = 0; k < virt - 2; ++k) in.advance(a.ring);  // past the padding rows as well
-      for (int k = 0; k < virt; ++k, acc.advance(R), vin.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1) {
+      for (int k = 0; k < virt; ++k, acc.advance(R), vin.advance(a.ring), eg = eg + 1 == kG ? 0 : eg + 1, ++ent) {
         if (eg != grp) continue;
-        const bool got = wait_bar(&done[vin.idx], vin.phase, a.err, kErrWaitEpilogue);
+        bool got;
+        if constexpr (kEpi == kEpiColsBias) {
+          // With 4 input slots, row e + 4 reuses row e's slot as soon as entry e - 2 (another group)
+          // is released, so `done` of row e may have completed twice by now and its parity would
+          // alias. Row e + 2 (or the cluster's last row) is safe: its slot is next used by row e + 6,
+          // which needs this entry's own slot, released only below.
+          const uint32_t r = ent + 2u < total_rows ? ent + 2u : total_rows - 1u;
+          got = wait_bar(&done[r % kColsRing], (r / kColsRing) & 1u, a.err, kErrWaitEpilogue);
+        } else {
+          got = wait_bar(&done[vin.idx], vin.phase, a.err, kErrWaitEpilogue);
+        }
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;

@@ -20,6 +20,12 @@ struct Half {
 
 std::vector<std::array<Half, 2>> make_ksteps(const ConvSpec& s, int chunks) {
   std::vector<std::array<Half, 2>> steps;
+  if (s.epi == kEpiColsBias) {
+    // kernel columns in N: every step reads the slot unshifted (dx = -1: slot pixel m for MMA row m)
+    for (int src = 0; src < s.n_sources; ++src)
+      for (int c = 0; c + 1 < chunks; c += 2) steps.push_back({Half{src, 0, -1, c, false}, Half{src, 0, -1, c + 1, false}});
+    return steps;
+  }
   if (s.taps == 1) {
     std::vector<Half> seq;
     for (int src = 0; src < s.n_sources; ++src)
@@ -84,8 +90,9 @@ const KernelEntry kKernels[] = {
     KB2_PAIRED(false, 48, kEpiBias, kOutF16Chunk),
     KB2_PAIRED(false, 48, kEpiSilu, kOutF16Chunk),
     KB2_PAIRED(false, 48, kEpiSpanAttn, kOutF16Chunk),
-    KB2_PAIRED(false, 16, kEpiBias, kOutPixShuf2),
-    KB2_PAIRED(false, 16, kEpiBias, kOutPixShuf2Display),
+    // SPAN's conv_cat folded into its upsampler: one 3x3 conv over the four sources, kernel columns in N
+    KB2_PAIRED(false, 48, kEpiColsBias, kOutPixShuf2),
+    KB2_PAIRED(false, 48, kEpiColsBias, kOutPixShuf2Display),
     KB2_PAIRED(false, 48, kEpiSpanAttn, kOutF16E4m3),
     KB2_PAIRED(true, 48, kEpiSilu, kOutE4m3Chunk),
     KB2_PAIRED(true, 48, kEpiSilu, kOutF16E4m3),
@@ -117,6 +124,7 @@ const KernelEntry kKernels[] = {
 };
 
 bool wants_stacked(const ConvSpec& s) {
+  if (s.epi == kEpiColsBias) return s.taps == 9 && s.n_sources == 4 && s.n_pad == 48 && !s.fp8;
   return s.taps == 9 && s.n_sources == 1 && (s.n_pad == 48 || s.n_pad == 16 || s.n_pad == 64);
 }
 
@@ -197,7 +205,11 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   for (const auto& st : steps)
     for (const Half& h : st) reach = std::max(reach, h.dx + halo);
   const int px = kRowBoxPx;
-  const int strip_w = px - reach;
+  // kernel columns in N: MMA row m is slot pixel m, and output m - 1 needs rows m - 1 .. m + 1
+  const bool cols = s.epi == kEpiColsBias;
+  if (cols && (s.n_real > 16 || s.cin % 16 != 0 || chunks * epc != s.cin))
+    return refuse(KB2_FORMAT_UNSUPPORTED, "columns in N: up to 16 outputs from whole 16-channel input pairs");
+  const int strip_w = cols ? px - 2 : px - reach;
   if (strip_w < 64) return refuse(KB2_FORMAT_UNSUPPORTED, "row slot too narrow for the taps");
   const uint32_t src_bytes = static_cast<uint32_t>(chunks) * px * 16;
   const uint32_t slot_bytes = src_bytes * static_cast<uint32_t>(s.n_sources);
@@ -287,14 +299,16 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
       const Half& hf = steps[j][h];
       for (int row = 0; row < n_rows_b; ++row) {
         const int blk = row / s.n_pad;
-        const int co = row % s.n_pad;
+        // with the kernel columns in N, row 16 kx + c of a kernel-row block is column kx, channel c
+        const int col_kx = cols ? (row % s.n_pad) / 16 : 0;
+        const int co = cols ? row % 16 : row % s.n_pad;
         if (co >= s.n_real) continue;
         for (int e = 0; e < epc; ++e) {
           const int ci = hf.chunk * epc + e;
           float v = 0.0f;
           if (!hf.zero && ci < s.cin) {
             const int ky = stacked ? 2 - blk : (s.taps == 9 ? hf.dy + 1 : 0);
-            const int kx = s.taps == 9 ? hf.dx + 1 : 0;
+            const int kx = cols ? col_kx : (s.taps == 9 ? hf.dx + 1 : 0);
             v = w_at(co, hf.src * s.cin + ci, ky, kx);
           }
           // paired kernel: block r of the pair holds B rows [r N/2, (r + 1) N/2) of every step
@@ -367,10 +381,11 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
     if (!one_per_sm && !stacked && ring < min_ring + 2) ring = fit(227u * 1024u);  // wide slots: one block per SM
     ring = std::min(ring, 12);
     // the pair issuer's ring is fixed by its 12-row periods (checked against shared memory below)
-    if (paired) ring = static_cast<int>(steps.size() == 12 ? pair_ring<12>() : pair_ring<9>());
+    if (paired) ring = static_cast<int>(cols ? kColsRing : steps.size() == 12 ? pair_ring<12>() : pair_ring<9>());
     a.ring = static_cast<uint32_t>(std::max(ring, min_ring));
   }
-  smem = a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (stacked ? kStackSmemExtra : kConvSmemExtra);
+  smem = a.w_smem + static_cast<size_t>(a.ring) * slot_bytes + (stacked ? kStackSmemExtra : kConvSmemExtra) +
+         (cols ? kStackXchgBytes : 0u);
   // a block that allocates all 512 TMEM columns asks for more than half the SM's shared memory, so
   // two of them are never co-resident (the second would only wait in tcgen05.alloc)
   if (one_per_sm) smem = std::max<size_t>(smem, 120u * 1024u);
@@ -420,6 +435,11 @@ Status ConvLayer::build(const ConvSpec& s, const float* W, const float* b, const
   grid = a.items < slots ? a.items : slots;
   if (paired) grid = 2 * slots;  // two blocks per cluster; the launch trims it to the rows
   return Status::Ok();
+}
+
+void ConvLayer::set_tap_bias(const float* tb) {
+  for (int t = 0; t < 9; ++t)
+    for (int c = 0; c < 16; ++c) args.tap_bias[t][c] = c < spec.n_real ? tb[t * spec.n_real + c] : 0.0f;
 }
 
 Status ConvLayer::launch(cudaStream_t stream, int batch, void* out, const void* residual, float out_inv_scale,

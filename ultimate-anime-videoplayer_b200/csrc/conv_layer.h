@@ -12,7 +12,7 @@ namespace kb2 {
 struct ConvSpec {
   int taps = 9;           // 9: 3x3 pad 1; 1: 1x1
   bool fp8 = false;       // E4M3 operands (else FP16)
-  int n_sources = 1;      // 1, or 4 for the concat-free 1x1 (conv_cat)
+  int n_sources = 1;      // 1, or 4: the concat-free 1x1 (conv_cat), or kEpiColsBias (conv_cat + upsampler)
   int cin = 48;           // real input channels per source
   int n_real = 48;        // real output channels
   int n_pad = 48;         // N of the MMA (multiple of 16, <= 64)
@@ -35,6 +35,9 @@ struct ConvLayer {
   // the input tensors (FP8 only; folded into the per-output-channel weight scales).
   Status build(const ConvSpec& s, const float* W, const float* b, const float* prelu_slope,
                const float* act_scales, const ChunkedTensor* const* inputs, int* err_word);
+  // kEpiColsBias: the bias term of each tap, [9][n_real] (tap ky * 3 + kx), dropped where that tap
+  // falls outside the image (ConvArgs::tap_bias)
+  void set_tap_bias(const float* tb);
   // residual / out: device pointers for this launch (residual may be null); residual2: the second
   // addend of kEpiTanhGate.
   // display: kOutPixShuf2Display's row pitch and kb2_display_format.

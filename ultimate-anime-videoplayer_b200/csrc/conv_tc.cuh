@@ -54,6 +54,11 @@ enum Epi : int {
   kEpiPrelu = 3,     // PReLU(v)
   kEpiResPrelu = 4,  // PReLU(v + residual)
   kEpiTanhGate = 5,  // (residual + residual2) * tanh(v): the unshuffle SPAN's block end (x + c3) * tanh(att)
+  // 3x3 conv with its kernel columns in N (pair kernel only, conv3p.cuh): accumulator column
+  // 16 kx + c of MMA row m holds kernel column kx of output channel c applied at slot pixel m; the
+  // epilogue sums D[m - 1][c] + D[m][16 + c] + D[m + 1][32 + c] across neighbouring lanes, then adds
+  // the bias and the border terms of ConvArgs::tap_bias
+  kEpiColsBias = 6,
 };
 
 enum OutFmt : int {
@@ -101,6 +106,10 @@ struct ConvArgs {
   // pipe the MMAs' operands use. SiLU and gate layers hold them halved (epi_halved).
   float cbias[kMaxN];
   float cscale[kMaxN];
+  // kEpiColsBias: the part of cbias that tap (ky, kx) = (t / 3, t % 3) contributes, per output
+  // channel. cbias holds the interior sum; an output pixel whose tap falls outside the image
+  // subtracts that tap's term (the layer this conv replaces zero-pads its input, bias included).
+  float tap_bias[9][16];
   float out_inv_scale;      // E4M3 output: 1 / scale
   float res_scale;          // E4M3 residual dequantisation scale
   const uint8_t* residual;  // same pixels and channels as the output, chunked

@@ -7,9 +7,14 @@
 //   conv_1    3x3 3->48                                                     -> S0
 //   block b   c1 3x3 + SiLU -> T1; c2 3x3 + SiLU -> T2;
 //             c3 3x3 then (c3 + x)(sigmoid(c3) - 0.5), x the block input    -> X(b+1)
-//   conv_cat  1x1 over the four sources [S0, X6, X1, T1 of the last block], no concat buffer
+//   conv_cat  1x1 over the four sources [S0, X6, X1, T1 of the last block]
 //   upsampler 3x3 48->12 + PixelShuffle(2) in the epilogue                  -> NCHW F16 [n][3][2H][2W]
 // The concat order is the reference's span_fp8::forward (src/gpu/span_fp8/forward.cpp:158-160).
+// conv_cat and the upsampler run as ONE layer: both are linear, so the upsampler of conv_cat's
+// output is a 3x3 conv of the four sources with the composed weights Wup . Wcat (192 -> 12), the
+// kernel columns in N (conv3p.cuh kEpiColsBias). conv_cat's bias reaches the output through the
+// upsampler's taps, except where a tap falls outside the image (the upsampler pads its input with
+// zeros): those terms are dropped at the border. The 48-channel concat output is never stored.
 //
 // Precision. FP16 engine: FP16 operands and activations, FP32 accumulation. FP8 engine: blocks 1..5
 // run E4M3 x E4M3 -> FP32 (per-tensor activation scales, per-output-channel weight scales); conv_1,
@@ -70,6 +75,35 @@ __global__ void absmax_f16_kernel(const __half2* __restrict__ v, size_t n2, unsi
 
 }  // namespace
 
+// The upsampler (3x3, 48 -> 12, zero padding) of conv_cat (1x1, 4c -> c) as one 3x3 conv of the 4c
+// source channels: Wc[o][i][ky][kx] = sum_m Wup[o][m][ky][kx] Wcat[m][i]. Bias: bup[o] plus, per tap,
+// tb[ky * 3 + kx][o] = sum_m Wup[o][m][ky][kx] bcat[m], which holds only where the tap reads inside
+// the image; bc is the interior sum and the kernel subtracts the taps that fall outside. Sums in
+// double, rounded once.
+void compose_cat_upsampler(const float* wcat, const float* bcat, const float* wup, const float* bup, int c,
+                           std::vector<float>& wc, std::vector<float>& bc, std::vector<float>& tb) {
+  const int ci_n = 4 * c, co_n = 12;
+  wc.assign(static_cast<size_t>(co_n) * ci_n * 9, 0.0f);
+  bc.assign(co_n, 0.0f);
+  tb.assign(static_cast<size_t>(9) * co_n, 0.0f);
+  for (int o = 0; o < co_n; ++o) {
+    double interior = bup[o];
+    for (int t = 0; t < 9; ++t) {
+      double bt = 0.0;
+      for (int m = 0; m < c; ++m) bt += static_cast<double>(wup[(static_cast<size_t>(o) * c + m) * 9 + t]) * bcat[m];
+      tb[static_cast<size_t>(t) * co_n + o] = static_cast<float>(bt);
+      interior += bt;
+      for (int i = 0; i < ci_n; ++i) {
+        double w = 0.0;
+        for (int m = 0; m < c; ++m)
+          w += static_cast<double>(wup[(static_cast<size_t>(o) * c + m) * 9 + t]) * wcat[static_cast<size_t>(m) * ci_n + i];
+        wc[(static_cast<size_t>(o) * ci_n + i) * 9 + t] = static_cast<float>(w);
+      }
+    }
+    bc[o] = static_cast<float>(interior);
+  }
+}
+
 Status launch_absmax(cudaStream_t stream, const void* f16, size_t n_half2, unsigned int* dst) {
   if (n_half2 % 4 != 0 || (reinterpret_cast<uintptr_t>(f16) & 15u) != 0)
     return refuse(KB2_FORMAT_UNSUPPORTED, "absmax: whole 16-byte chunks expected");
@@ -127,14 +161,13 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
     return Status::Ok();
   };
   const ChunkedTensor *s0, *t1h, *t2h, *x1, *x1q = nullptr, *t1q = nullptr, *t2q = nullptr, *xa, *xb;
-  const ChunkedTensor *t1l, *t1lq = nullptr, *x6 = nullptr, *cat;
+  const ChunkedTensor *t1l, *t1lq = nullptr, *x6 = nullptr;
   KB2_TRY(tensor(2, false, &img_));
   KB2_TRY(tensor(6, false, &s0));
   KB2_TRY(tensor(6, false, &t1h));
   KB2_TRY(tensor(6, false, &t2h));
   KB2_TRY(tensor(6, false, &x1));
   KB2_TRY(tensor(6, false, &t1l));
-  KB2_TRY(tensor(6, false, &cat));
   if (fp8_) {
     KB2_TRY(tensor(3, true, &x1q));
     KB2_TRY(tensor(3, true, &t1q));
@@ -175,8 +208,7 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
     step.bytes_px = bytes;
     const char* precision = s.fp8 ? "fp8" : "fp16";
     std::string name;
-    if (s.n_sources == 4) name = "span.conv_cat.fp16";
-    else if (s.out == kOutPixShuf2) name = "span.upsampler.fp16";
+    if (s.epi == kEpiColsBias) name = "span.cat_upsampler.fp16";
     else if (s.cin == 3) name = "span.conv_1.fp16";
     else if (s.epi == kEpiSpanAttn) name = std::string("span.block_gate.") + precision;
     else name = std::string("span.block_conv.") + precision;
@@ -247,23 +279,25 @@ Status SpanNet::create(const std::vector<float>& params, int precision, int max_
                   Step{nullptr, x6, nullptr, x_in, 1.0f, res_scale, -1}));
     }
   }
-  {  // conv_cat: FP16 1x1 over four FP16 sources
-    ConvSpec s = spec(1, false, c, kEpiBias, kOutF16Chunk);
+  {  // conv_cat + upsampler + PixelShuffle(2): one 3x3 conv over the four FP16 sources
+    std::vector<float> wc, bc, tb;
+    compose_cat_upsampler(wcat, bcat, wup, bup, c, wc, bc, tb);
+    ConvSpec s = spec(9, false, c, kEpiColsBias, kOutPixShuf2);
     s.n_sources = 4;
-    KB2_TRY(add(s, wcat, bcat, nullptr, {s0, x6, x1, t1l}, Step{nullptr, cat, nullptr, nullptr, 1.0f, 1.0f, -1}));
-  }
-  {  // upsampler + PixelShuffle(2)
-    ConvSpec s = spec(9, false, c, kEpiBias, kOutPixShuf2);
     s.n_real = 12;
-    s.n_pad = 16;
-    KB2_TRY(add(s, wup, bup, nullptr, {cat}, Step{nullptr, nullptr, nullptr, nullptr, 1.0f, 1.0f, -1}));
+    s.n_pad = 48;  // MMA columns of a kernel row: 3 kernel columns x 16 channels
+    const std::vector<const ChunkedTensor*> srcs = {s0, x6, x1, t1l};
+    KB2_TRY(add(s, wc.data(), bc.data(), nullptr, srcs, Step{nullptr, nullptr, nullptr, nullptr, 1.0f, 1.0f, -1}));
+    layers_.back()->set_tap_bias(tb.data());
+    // the network's own work: conv_cat's 1x1 and the upsampler's 3x3, not the composed conv's
+    steps_.back().flops_px = 2.0 * (4 * c) * c + 2.0 * c * 12 * 9;
     // the same layer writing display pixels (set_output_format)
     s.out = kOutPixShuf2Display;
     layers_.push_back(std::make_unique<ConvLayer>());
     up_display_ = layers_.back().get();
-    const ChunkedTensor* in_cat[1] = {cat};
-    KB2_TRY(up_display_->build(s, wup, bup, nullptr, nullptr, in_cat, err));
-    k_display_ = kind_index("span.upsampler.display");
+    KB2_TRY(up_display_->build(s, wc.data(), bc.data(), nullptr, nullptr, srcs.data(), err));
+    up_display_->set_tap_bias(tb.data());
+    k_display_ = kind_index("span.cat_upsampler.display");
   }
   return Status::Ok();
 }

@@ -35,6 +35,15 @@ constexpr uint32_t kStackZeroOff = 2176;
 constexpr uint32_t kStackZeroBytes = 48 * 32;
 constexpr uint32_t kStackSmemExtra = 1024 + kStackZeroOff + kStackZeroBytes + 64;
 static_assert(128 * 8 + (kMaxKSteps + 2) * 8 + 3 * kMaxN * 4 + 4 <= kStackZeroOff, "shared layout");
+// kEpiColsBias layers only, after the zero tile: the edge-pixel exchange of the epilogue warps,
+// [3 groups][2 buffers][4 lane quadrants][32 floats], and its barriers at bars[kStackXchgBar ..)
+constexpr uint32_t kStackXchgOff = kStackZeroOff + kStackZeroBytes;
+constexpr uint32_t kStackXchgBytes = 3 * 2 * 4 * 32 * 4;
+constexpr uint32_t kStackXchgBar = 64;  // 6 barriers, beyond the ring's 2 x 12 + 9
+static_assert(kStackXchgOff % 16 == 0, "exchange rows 16-byte aligned");
+// the input ring of kEpiColsBias layers: four 48 KB row slots (four 48-channel sources) beside
+// the weights; 4 divides the issuer's 12-row period
+constexpr uint32_t kColsRing = 4;
 static_assert(((128 + kMaxKSteps + 2) * 8) % 16 == 0, "per-channel constants 16-byte aligned");
 
 }  // namespace kb2
