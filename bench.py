@@ -15,7 +15,9 @@ Workloads (the contract's configs):
             every output frame gathered to the host in order (a step = one chunk);
   janai / janai8  the AnimeJaNai unshuffle SPAN b8f64 of a seeded .span8 package (FP16 / E4M3 blocks);
   warp      frames at t = 1/3 from one mid-pair motion (kb2_warp_blend_at), 8 pairs of 1080p;
-  kernels   one small pass of every kernel kind (--family to pick one), for the ncu summaries.
+  kernels   one small pass of every kernel kind (--family to pick one), for the ncu summaries;
+  hostcopy  the host traffic of the SPAN x2 e2e leg alone (its pinned uploads and display-pixel
+            reads, no compute): the frames/s ceiling the host side sets at this many ranks.
 
 `value` is whole-job frames/s with the inputs resident in HBM, timed with CUDA events on the enqueue
 stream (max over ranks). `e2e` is the same through the public C ABI with pinned host frames: the
@@ -48,6 +50,7 @@ FRAME_H, FRAME_W = 1080, 1920
 FLOP_PER_PX = 777888.0  # canonical SPAN x2: 388,944 MACs per input pixel
 CHAIN_TIMES = (0.2, 0.4, 0.6, 0.8)
 WORKLOADS = ("default", "span16", "span8", "rife", "rife4k", "rife425", "chain", "janai", "janai8", "warp", "kernels",
+             "hostcopy",
              "tiles")
 
 
@@ -1315,6 +1318,60 @@ def run_tiles(args):
     D.close()
 
 
+def run_hostcopy(args):
+    """The e2e leg of configs[1] without the engine: per step, on every rank, the H2D copy of B
+    1080p F16 NCHW frames from pinned memory and the D2H read of B 3840x2160 RGB10A2 frames into
+    pinned memory, on two streams, double-buffered as e2e_leg does; then the D2H reads alone. Wall
+    clock between barriers, max over ranks. `value` is the frames/s at which the host side alone
+    would carry that leg at this many ranks; an e2e rate near it is bound by host copies, not by
+    the GPUs. Not a benchmark of the frame path."""
+    import torch
+    import shard
+    D = Dist()
+    B, H, W = args.batch, FRAME_H, FRAME_W
+    h_in = torch.empty((B, 3, H, W), dtype=torch.float16).pin_memory()
+    d_in = [torch.empty((B, 3, H, W), dtype=torch.float16, device="cuda") for _ in range(2)]
+    d_out = [torch.zeros((B, 4, 2 * H, 2 * W), dtype=torch.uint8, device="cuda") for _ in range(2)]
+    h_out = [torch.empty((B, 4, 2 * H, 2 * W), dtype=torch.uint8).pin_memory() for _ in range(2)]
+    s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    in_b = h_in.numel() * 2
+    out_b = h_out[0].numel()
+
+    def run(n, with_h2d):
+        for i in range(n):
+            k = i % 2
+            if with_h2d:
+                with torch.cuda.stream(s_h2d):
+                    d_in[k].copy_(h_in, non_blocking=True)
+            with torch.cuda.stream(s_d2h):
+                h_out[k].copy_(d_out[k], non_blocking=True)
+        torch.cuda.synchronize()
+
+    def timed(with_h2d):
+        run(max(args.warmup, 3), with_h2d)
+        D.barrier()
+        t0 = time.perf_counter()
+        run(args.steps, with_h2d)
+        D.barrier()
+        return D.max(time.perf_counter() - t0)
+
+    both = timed(True)
+    d2h = timed(False)
+    n = D.world
+    line = {"metric": "host-copy ceiling of the configs[1] e2e leg (SPAN x2, 1080p in, 4K RGB10A2 out)",
+            "value": shard.whole_job_rate(B * args.steps, n, both), "unit": "frames/s", "n_gpus": n,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
+            "h2d_bytes_per_step": in_b, "d2h_bytes_per_step": out_b,
+            "both_gbs_total": n * (in_b + out_b) * args.steps / both / 1e9,
+            "d2h_only_gbs_total": n * out_b * args.steps / d2h / 1e9,
+            "d2h_only_frames_per_s": shard.whole_job_rate(B * args.steps, n, d2h),
+            "note": "copies only (no compute): pinned H2D of the step's F16 frames and D2H of its display "
+                    "pixels on two streams per rank, the e2e leg's buffers and order; not a benchmark line"}
+    if D.rank == 0:
+        print(json.dumps(line))
+    D.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1327,6 +1384,8 @@ def main():
         run_kernels(args)
     elif args.workload == "tiles":
         run_tiles(args)
+    elif args.workload == "hostcopy":
+        run_hostcopy(args)
     else:
         run_ours(args)
 
