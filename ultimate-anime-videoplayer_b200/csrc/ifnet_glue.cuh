@@ -66,6 +66,27 @@ __global__ void ifnet_pad_frames_kernel(IfFrames F, int batch) {
   }
 }
 
+// The video-stream form of the padding: pair n is frames n and n + 1 of one buffer (img1 = img0 one
+// frame on), so each of the `frames` = batch + 1 frames is padded once, into consecutive planes of
+// pad0, and pad1 = pad0 one plane on. Same pixels as ifnet_pad_frames_kernel, half the traffic.
+__global__ void ifnet_pad_stream_kernel(IfFrames F, int frames) {
+  const size_t plane = static_cast<size_t>(F.H) * F.W;
+  const int X = blockIdx.x * blockDim.x + threadIdx.x;
+  if (X >= F.Wp) return;
+  for (int r = blockIdx.y; r < frames * F.Hp; r += gridDim.y) {
+    const int n = r / F.Hp;
+    const int Y = r - n * F.Hp;
+    const int y = Y - F.top, x = X - F.left;
+    uint2 p = make_uint2(0, 0);
+    if (y >= 0 && y < F.H && x >= 0 && x < F.W) {
+      const size_t at = static_cast<size_t>(n) * 3 * plane + static_cast<size_t>(y) * F.W + x;
+      const __half2 c01 = __halves2half2(F.img0[at], F.img0[at + plane]);
+      const __half2 c2 = __halves2half2(F.img0[at + 2 * plane], __float2half_rn(0.0f));
+      p = make_uint2(*reinterpret_cast<const uint32_t*>(&c01), *reinterpret_cast<const uint32_t*>(&c2));
+    }
+    F.pad0[static_cast<size_t>(r) * F.Wp + X] = p;
+  }
+}
 
 // The x half of block j's flow resize at one full-resolution column, cached along a column: the
 // column's x tap (fixed), and for the source row pair last used (lo, hi) both rows' 5 channels

@@ -184,8 +184,14 @@ Status IfnetNet::run_motion(cudaStream_t stream, const void* img0, const void* i
 Status IfnetNet::run_impl(cudaStream_t stream, const void* img0, const void* img1, const Finish& finish, int batch) {
   if (batch < 1 || batch > max_batch_) return refuse(KB2_SHAPE_INVALID, "IFNet: batch out of contract");
   uint2* pad0 = pad_.as<uint2>();
+  const size_t pad_plane = static_cast<size_t>(Hp_) * Wp_;
+  // A video stream passes pair n as frames n and n + 1 of one buffer (img1 = img0 one frame on): its
+  // batch + 1 frames are then padded once each, and pad1 is pad0 one plane on (pad_ holds 2 x
+  // max_batch planes, at least batch + 1).
+  const bool stream_pairs =
+      static_cast<const __half*>(img1) == static_cast<const __half*>(img0) + static_cast<size_t>(3) * H_ * W_;
   IfFrames F{static_cast<const __half*>(img0), static_cast<const __half*>(img1), H_, W_, Hp_, Wp_, top_, left_, pad0,
-             pad0 + static_cast<size_t>(max_batch_) * Hp_ * Wp_};
+             pad0 + (stream_pairs ? pad_plane : static_cast<size_t>(max_batch_) * pad_plane)};
   // a grid of row runs for the glue kernels (ifnet_glue.cuh): about 16 blocks per SM, each walking runs
   const int sms = num_sms();
   auto row_grid = [sms](int width, int rows) {
@@ -196,9 +202,15 @@ Status IfnetNet::run_impl(cudaStream_t stream, const void* img0, const void* img
   {
     const long long px = static_cast<long long>(batch) * Hp_ * Wp_;
     KB2_TRY(timer_.begin(stream));
-    ifnet_pad_frames_kernel<<<row_grid(Wp_, batch * Hp_), kGlueThreads, 0, stream>>>(F, batch);
-    KB2_CUDA(cudaGetLastError());
-    KB2_TRY(timer_.end(k_pad_, 0.0, px * (12.0 + 16.0), stream));
+    if (stream_pairs) {
+      ifnet_pad_stream_kernel<<<row_grid(Wp_, (batch + 1) * Hp_), kGlueThreads, 0, stream>>>(F, batch + 1);
+      KB2_CUDA(cudaGetLastError());
+      KB2_TRY(timer_.end(k_pad_, 0.0, static_cast<double>(px + static_cast<long long>(pad_plane)) * (6.0 + 8.0), stream));
+    } else {
+      ifnet_pad_frames_kernel<<<row_grid(Wp_, batch * Hp_), kGlueThreads, 0, stream>>>(F, batch);
+      KB2_CUDA(cudaGetLastError());
+      KB2_TRY(timer_.end(k_pad_, 0.0, px * (12.0 + 16.0), stream));
+    }
   }
   IfFlowLevels L{};
   for (int k = 0; k < kIfBlocks; ++k) {
