@@ -54,6 +54,34 @@ def test_nearest_x2_package_is_exact():
     np.testing.assert_array_equal(out, np.repeat(np.repeat(x, 2, axis=2), 2, axis=3))
 
 
+def test_cat_upsampler_composition():
+    """SPAN's conv_cat (1x1, 192 -> 48, bias) followed by its upsampler (3x3, 48 -> 12, zero padding)
+    equals one 3x3 conv of the four sources with the composed weights, whose bias is the
+    upsampler's plus, for each tap that reads inside the image, that tap's share of conv_cat's
+    bias. This is the algebra the library's fused conv_cat + upsampler layer computes (the weights
+    composed on the host, the border terms dropped in the epilogue); checked here with the oracle's
+    FP32 conv on frames whose every pixel is a border pixel in some direction."""
+    rng = np.random.default_rng(3)
+    c = 48
+    wcat = rng.standard_normal((c, 4 * c, 1, 1)) * 0.1
+    bcat = rng.standard_normal(c)
+    wup = rng.standard_normal((12, c, 3, 3)) * 0.1
+    bup = rng.standard_normal(12)
+    wc = np.einsum("omyx,mi->oiyx", wup, wcat[:, :, 0, 0])
+    tap = np.einsum("omyx,m->yxo", wup, bcat)  # [ky][kx][o]
+    for h, w in ((1, 1), (2, 3), (3, 2), (5, 7)):
+        src = rng.standard_normal((1, 4 * c, h, w))
+        ref = nets.conv2d(nets.conv2d(src, wcat, bcat, pad=0), wup, bup)
+        out = nets.conv2d(src, wc, bup + tap.sum(axis=(0, 1)))
+        for y in range(h):
+            for x in range(w):
+                for ky in range(3):
+                    for kx in range(3):
+                        if not (0 <= y + ky - 1 < h and 0 <= x + kx - 1 < w):
+                            out[0, :, y, x] -= tap[ky, kx]
+        np.testing.assert_allclose(out, ref, rtol=0, atol=2e-5 * max(1.0, float(np.abs(ref).max())))
+
+
 def nearest_params():
     p = {k: np.zeros(s, np.float32) for k, s in nets.span_param_shapes()}
     for c in range(3):
